@@ -1,0 +1,51 @@
+"""Loader for the in-tree sm_100a extension ``resihp/_C.so``.
+
+The CUDA path has no fallback: on a machine with a GPU, a missing or unloadable
+extension is an error (``require()`` raises), never a silent switch to torch kernels.
+CPU tensors take the plain-torch FP32 path of each op, which is what the CPU test tier
+and the reference-semantics runs use.
+"""
+
+from __future__ import annotations
+
+import importlib.util
+import os
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+_LIB = os.path.join(_PKG, "_C.so")
+_module = None
+_error: Exception | None = None
+
+
+def _load():
+    global _module, _error
+    if _module is not None or _error is not None:
+        return _module
+    try:
+        import torch  # noqa: F401  (libtorch must be loaded before the extension)
+
+        spec = importlib.util.spec_from_file_location("resihp._C", _LIB)
+        if spec is None or not os.path.exists(_LIB):
+            raise ImportError(f"extension not built: {_LIB} (run python -m resihp.ops.build)")
+        module = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(module)
+        _module = module
+    except Exception as exc:  # kept and re-raised by require()
+        _error = exc
+    return _module
+
+
+def available() -> bool:
+    return _load() is not None
+
+
+def require():
+    """The loaded extension module; raises if it cannot be loaded."""
+    module = _load()
+    if module is None:
+        raise RuntimeError(f"resihp CUDA extension unavailable: {_error}")
+    return module
+
+
+def library_path() -> str:
+    return _LIB
