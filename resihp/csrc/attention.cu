@@ -1,0 +1,781 @@
+// Causal flash attention (forward and backward) on the sm_100a tensor cores.
+//
+// Q, K and V are read in place from the fused projection qkv[T, (Hq + 2*Hkv) * D]
+// (row t = batch b, position t % S), GQA maps q head h to kv head h / (Hq / Hkv).
+// One TMA tensor map (box 64 columns x 128 rows, 128-byte swizzle) serves every tile:
+// a 64-column slab of 128 rows is a K-major operand when its columns are the reduction
+// dimension (Q, K in S = Q K^T) and an MN-major operand when its rows are (V in P V).
+//
+// Forward, one CTA per (q block of 128 rows, q head, batch):
+//   warp 0      TMA: Q once, then K_j / V_j into a 2-deep ring
+//   warp 1      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers,
+//               O += P_j V_j into the TMEM O accumulator (S_{j+1} is issued before
+//               PV_j so the tensor core works while softmax runs)
+//   warps 2-5   softmax, one thread per query row: row max over the S row in TMEM,
+//               P = exp2(S * scale*log2e - m), P written as bf16 into a 128B-swizzled
+//               smem tile (the A operand of PV), O rescaled in TMEM when the max grows,
+//               finally O / l stored as bf16 and the log-sum-exp kept for backward.
+// Backward (deterministic, no atomics):
+//   attn_bwd_dkdv  one CTA per (kv block, kv head, batch), looping over every q head of
+//                  the group and every causal q block: S^T = K Q^T, dP^T = V dO^T,
+//                  P^T = exp(S^T - lse), dS^T = P^T (dP^T - Delta), then
+//                  dV += P^T dO and dK += dS^T Q accumulated in TMEM.
+//   attn_bwd_dq    one CTA per (q block, q head, batch): S, dP recomputed, dQ += dS K.
+//   The same smem tile of dS^T serves as K-major A (for dK) -- and the dQ kernel writes
+//   its own dS tile K-major for dQ += dS K.
+// All waits are bounded (common.cuh) and report into the error word.
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace resihp {
+
+namespace {
+
+constexpr int kBlk = 128;          // q rows and kv rows per tile
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  __nv_bfloat16* out;      // [T, Hq*D] (forward) or dqkv [T, W] (backward)
+  float* lse;              // [B, Hq, S] natural-log log-sum-exp
+  const __nv_bfloat16* dout;  // backward: dO [T, Hq*D]
+  const float* delta;      // backward: rowsum(dO * O) [B, Hq, S]
+  int seq, hq, hkv, d;
+  int64_t out_ld;
+  int64_t dout_ld;
+  float scale;             // 1/sqrt(D)
+  int* err;
+};
+
+// Byte offset of bf16 element (r, c) in a K-major 128B-swizzled tile made of 64-column
+// chunks of `rows` rows each.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c, int rows) {
+  const int chunk = c >> 6;
+  const int cc = c & 63;
+  const int unit = (cc >> 3) ^ (r & 7);
+  return uint32_t(chunk * rows * 128 + r * 128 + unit * 16 + (cc & 7) * 2);
+}
+
+// Write 32 consecutive columns (c0 .. c0+31, c0 % 32 == 0) of row r, given as 16 packed
+// bf16 pairs, into a swizzled K-major tile.
+__device__ __forceinline__ void store_row32(uint8_t* tile, int r, int c0, const uint32_t (&pk)[16], int rows) {
+  #pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint4 v = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    *reinterpret_cast<uint4*>(tile + sw128_offset(r, c0 + 8 * u, rows)) = v;
+  }
+}
+
+template <int D>
+struct FwdSmem {
+  static constexpr int kQ = kBlk * D * 2;
+  static constexpr int kKV = kBlk * D * 2;
+  static constexpr int kStages = 2;
+  static constexpr int kP = kBlk * kBlk * 2;
+  static constexpr int kBytes = kQ + 2 * kStages * kKV + kP + 1024 + 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  using L = FwdSmem<D>;
+  constexpr int ST = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + L::kQ;                 // ST stages of K
+  uint8_t* sv = sk + ST * L::kKV;           // ST stages of V
+  uint8_t* sp = sv + ST * L::kKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + L::kP);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + ST;
+  uint64_t* kv_empty = v_full + ST;
+  uint64_t* s_full = kv_empty + ST;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+
+  const int qblk = (a.seq / kBlk) - 1 - blockIdx.x;   // heaviest causal rows first
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / (a.hq / a.hkv);
+  const int nblk = qblk + 1;
+  const int row0 = b * a.seq + qblk * kBlk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch(&tm);
+      mbar_expect_tx(q_full, L::kQ);
+      #pragma unroll
+      for (int c = 0; c < D / 64; ++c) tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0);
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j % ST;
+        const uint32_t n = j / ST;
+        if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, a.err, kErrTmaWait)) break;
+        const int kv_row = b * a.seq + j * kBlk;
+        mbar_expect_tx(&k_full[st], L::kKV);
+        #pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(sk + st * L::kKV + c * kBlk * 128, &tm, &k_full[st], (a.hq + kvh) * D + 64 * c, kv_row);
+        mbar_expect_tx(&v_full[st], L::kKV);
+        #pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(sv + st * L::kKV + c * kBlk * 128, &tm, &v_full[st], (a.hq + a.hkv + kvh) * D + 64 * c,
+                      kv_row);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
+      constexpr uint32_t id_o = idesc_bf16_f32(kBlk, D, 0, 1);
+      const uint32_t q_addr = smem_u32(sq);
+      const uint32_t p_addr = smem_u32(sp);
+      bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % ST;
+        if (!mbar_wait(p_full, j & 1, a.err, kErrMmaWait)) return false;
+        if (!mbar_wait(&v_full[st], (j / ST) & 1, a.err, kErrMmaWait)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sv + st * L::kKV);
+        #pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk) {
+          const uint64_t da = smem_desc_sw128(p_addr + (kk >> 2) * kBlk * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, kBlk * 128, 1024);
+          umma_bf16(t_o, da, db, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int st = j % ST;
+        const int sb = j & 1;
+        if (!mbar_wait(&k_full[st], (j / ST) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sk + st * L::kKV);
+        #pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+          umma_bf16(tmem + sb * kBlk, smem_desc_sw128(q_addr + off, 16, 1024),
+                    smem_desc_sw128(k_addr + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) issue_pv(nblk - 1);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;           // query row within the tile
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = j == qblk;
+      const uint32_t t_s = tmem + sb * kBlk + lane_off;
+      // pass 1: row max (raw scores)
+      float mx = m;
+      #pragma unroll 1
+      for (int c = 0; c < kBlk; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(t_s + c, v);
+        tmem_wait_ld();
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float s = __uint_as_float(v[e]);
+          if (!diag || c + e <= r) mx = fmaxf(mx, s);
+        }
+      }
+      const float alpha = exp2f((m - mx) * sl2);   // 0 on the first block (m = -inf)
+      const float neg = mx * sl2;
+      // P smem is still being read by PV_{j-1}: wait for it before overwriting
+      if (j > 0) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+        tc_fence_after();
+      }
+      float rowsum = 0.f;
+      #pragma unroll 1
+      for (int c = 0; c < kBlk; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(t_s + c, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+        #pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = exp2f(__uint_as_float(v[e]) * sl2 - neg);
+          float p1 = exp2f(__uint_as_float(v[e + 1]) * sl2 - neg);
+          if (diag && c + e > r) p0 = 0.f;
+          if (diag && c + e + 1 > r) p1 = 0.f;
+          __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+          const float2 pr = __bfloat1622float2(pb);   // sum what the MMA will see
+          rowsum += pr.x + pr.y;
+          pk[e / 2] = *reinterpret_cast<uint32_t*>(&pb);
+        }
+        store_row32(sp, r, c, pk, kBlk);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);
+      l = l * alpha + rowsum;
+      m = mx;
+      // rescale the running O when this warp saw the max grow
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        #pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(t_o + lane_off + c, v);
+          tmem_wait_ld();
+          #pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st16(t_o + lane_off + c, v);
+        }
+        tmem_wait_st();
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(pv_done, (nblk - 1) & 1, a.err, kErrEpiWait)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* dst = a.out + int64_t(row0 + r) * a.out_ld + int64_t(h) * D;
+      #pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(t_o + lane_off + c, v);
+        tmem_wait_ld();
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(v[8 * u + 0]) * inv, __uint_as_float(v[8 * u + 1]) * inv);
+          o.y = pack_bf16(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv);
+          o.z = pack_bf16(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv);
+          o.w = pack_bf16(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+        }
+      }
+      a.lse[(int64_t(b) * a.hq + h) * a.seq + qblk * kBlk + r] = m * a.scale + logf(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Delta[b, h, s] = sum_d dO * O  (fp32)
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_ld, const __nv_bfloat16* __restrict__ dout,
+                                  int64_t do_ld, float* __restrict__ delta, int rows, int seq, int hq, int d) {
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= rows * hq) return;
+  const int t = warp_global / hq, h = warp_global % hq;
+  const __nv_bfloat16* po = o + int64_t(t) * o_ld + int64_t(h) * d;
+  const __nv_bfloat16* pd = dout + int64_t(t) * do_ld + int64_t(h) * d;
+  float acc = 0.f;
+  for (int c = lane * 2; c < d; c += 64) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + c));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + c));
+    acc += x.x * y.x + x.y * y.y;
+  }
+  #pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int b = t / seq, s = t % seq;
+    delta[(int64_t(b) * hq + h) * seq + s] = acc;
+  }
+}
+
+// ---- backward: dK, dV ----------------------------------------------------------------
+
+template <int D>
+struct DkdvSmem {
+  static constexpr int kT = kBlk * D * 2;   // one 128 x D bf16 tile
+  static constexpr int kP = kBlk * kBlk * 2;
+  static constexpr int kBytes = 4 * kT + 2 * kP + 2 * kBlk * 4 + 1024 + 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
+                         AttnArgs a) {
+  using L = DkdvSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint8_t* sk = smem;
+  uint8_t* sv = sk + L::kT;
+  uint8_t* sq = sv + L::kT;
+  uint8_t* sdo = sq + L::kT;
+  uint8_t* spt = sdo + L::kT;   // P^T  [kv, q] K-major
+  uint8_t* sdst = spt + L::kP;  // dS^T [kv, q] K-major
+  float* s_lse = reinterpret_cast<float*>(sdst + L::kP);   // per q row: lse * log2e
+  float* s_delta = s_lse + kBlk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + kBlk);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;     // Q_i, dO_i (and lse/delta) landed
+  uint64_t* qd_empty = bars + 2;    // the MMAs reading Q_i, dO_i are done
+  uint64_t* sp_full = bars + 3;     // S^T and dP^T ready in TMEM
+  uint64_t* sp_empty = bars + 4;    // softmax finished reading S^T / dP^T
+  uint64_t* ds_full = bars + 5;     // P^T and dS^T written to smem
+  uint64_t* acc_done = bars + 6;    // dV/dK MMAs of this step done (smem P^T/dS^T free)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+
+  const int kvblk = blockIdx.x;
+  const int g = blockIdx.y;
+  const int b = blockIdx.z;
+  const int group = a.hq / a.hkv;
+  const int nq = a.seq / kBlk - kvblk;          // causal: q blocks kvblk .. end
+  const int steps = nq * group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kv_row0 = b * a.seq + kvblk * kBlk;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qd_full, 1);
+    mbar_init(qd_empty, 1);
+    mbar_init(sp_full, 1);
+    mbar_init(sp_empty, 4);
+    mbar_init(ds_full, 4);
+    mbar_init(acc_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_st = tmem, t_dpt = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, 2 * L::kT);
+      #pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sk + c * kBlk * 128, &tm, kv_full, (a.hq + g) * D + 64 * c, kv_row0);
+        tma_load_2d(sv + c * kBlk * 128, &tm, kv_full, (a.hq + a.hkv + g) * D + 64 * c, kv_row0);
+      }
+      for (int it = 0; it < steps; ++it) {
+        const int h = g * group + it / nq;
+        const int qb = kvblk + it % nq;
+        if (!mbar_wait(qd_empty, (it & 1) ^ 1, a.err, kErrTmaWait)) break;
+        const int q_row0 = b * a.seq + qb * kBlk;
+        mbar_expect_tx(qd_full, 2 * L::kT);
+        #pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_2d(sq + c * kBlk * 128, &tm, qd_full, h * D + 64 * c, q_row0);
+          tma_load_2d(sdo + c * kBlk * 128, &tm_do, qd_full, h * D + 64 * c, q_row0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
+      constexpr uint32_t id_acc = idesc_bf16_f32(kBlk, D, 0, 1);
+      const uint32_t k_addr = smem_u32(sk), v_addr = smem_u32(sv), q_addr = smem_u32(sq), do_addr = smem_u32(sdo);
+      const uint32_t pt_addr = smem_u32(spt), dst_addr = smem_u32(sdst);
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
+      for (int it = 0; it < steps && ok; ++it) {
+        if (!mbar_wait(qd_full, it & 1, a.err, kErrMmaWait)) { ok = false; break; }
+        if (!mbar_wait(sp_empty, (it & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        #pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+          umma_bf16(t_st, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024), id_s,
+                    kk > 0);
+          umma_bf16(t_dpt, smem_desc_sw128(v_addr + off, 16, 1024), smem_desc_sw128(do_addr + off, 16, 1024), id_s,
+                    kk > 0);
+        }
+        umma_commit(sp_full);
+        if (!mbar_wait(ds_full, it & 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        #pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+          umma_bf16(t_dv, smem_desc_sw128(pt_addr + aoff, 16, 1024), smem_desc_sw128(do_addr + kk * 2048, kBlk * 128, 1024),
+                    id_acc, (it > 0 || kk > 0));
+          umma_bf16(t_dk, smem_desc_sw128(dst_addr + aoff, 16, 1024), smem_desc_sw128(q_addr + kk * 2048, kBlk * 128, 1024),
+                    id_acc, (it > 0 || kk > 0));
+        }
+        umma_commit(qd_empty);
+        umma_commit(acc_done);
+      }
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int c_row = q4 * 32 + lane;      // kv row within the tile
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    const int et = threadIdx.x - 64;       // 0..127
+    bool ok = true;
+    for (int it = 0; it < steps; ++it) {
+      const int h = g * group + it / nq;
+      const int qb = kvblk + it % nq;
+      const bool diag = qb == kvblk;
+      // lse / delta of this q block into smem (read by every kv row)
+      {
+        const int64_t base = (int64_t(b) * a.hq + h) * a.seq + qb * kBlk;
+        // previous step's readers are done once ds_full of that step was arrived; the
+        // named barrier below orders the overwrite after all 128 threads passed it.
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        s_lse[et] = a.lse[base + et] * kLog2e;
+        s_delta[et] = a.delta[base + et];
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      if (!mbar_wait(sp_full, it & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      if (it > 0) {
+        // smem P^T / dS^T of the previous step are read by its dV/dK MMAs
+        if (!mbar_wait(acc_done, (it - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      }
+      #pragma unroll 1
+      for (int c = 0; c < kBlk; c += 32) {
+        uint32_t sv32[32], dv32[32];
+        tmem_ld32(t_st + lane_off + c, sv32);
+        tmem_ld32(t_dpt + lane_off + c, dv32);
+        tmem_wait_ld();
+        uint32_t pk[16], dk[16];
+        #pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p[2], ds[2];
+          #pragma unroll
+          for (int z = 0; z < 2; ++z) {
+            const int qr = c + e + z;      // q row within the q tile
+            float pv = exp2f(__uint_as_float(sv32[e + z]) * sl2 - s_lse[qr]);
+            if (diag && qr < c_row) pv = 0.f;
+            p[z] = pv;
+            ds[z] = pv * (__uint_as_float(dv32[e + z]) - s_delta[qr]);
+          }
+          pk[e / 2] = pack_bf16(p[0], p[1]);
+          dk[e / 2] = pack_bf16(ds[0], ds[1]);
+        }
+        store_row32(spt, c_row, c, pk, kBlk);
+        store_row32(sdst, c_row, c, dk, kBlk);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sp_empty);
+        mbar_arrive(ds_full);
+      }
+    }
+    if (ok && steps > 0 && mbar_wait(acc_done, (steps - 1) & 1, a.err, kErrEpiWait)) {
+      tc_fence_after();
+      __nv_bfloat16* dk_dst = a.out + int64_t(kv_row0 + c_row) * a.out_ld + int64_t(a.hq + g) * D;
+      __nv_bfloat16* dv_dst = a.out + int64_t(kv_row0 + c_row) * a.out_ld + int64_t(a.hq + a.hkv + g) * D;
+      #pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t v1[32], v2[32];
+        tmem_ld32(t_dv + lane_off + c, v1);
+        tmem_ld32(t_dk + lane_off + c, v2);
+        tmem_wait_ld();
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 o1, o2;
+          o1.x = pack_bf16(__uint_as_float(v1[8 * u + 0]), __uint_as_float(v1[8 * u + 1]));
+          o1.y = pack_bf16(__uint_as_float(v1[8 * u + 2]), __uint_as_float(v1[8 * u + 3]));
+          o1.z = pack_bf16(__uint_as_float(v1[8 * u + 4]), __uint_as_float(v1[8 * u + 5]));
+          o1.w = pack_bf16(__uint_as_float(v1[8 * u + 6]), __uint_as_float(v1[8 * u + 7]));
+          o2.x = pack_bf16(__uint_as_float(v2[8 * u + 0]) * a.scale, __uint_as_float(v2[8 * u + 1]) * a.scale);
+          o2.y = pack_bf16(__uint_as_float(v2[8 * u + 2]) * a.scale, __uint_as_float(v2[8 * u + 3]) * a.scale);
+          o2.z = pack_bf16(__uint_as_float(v2[8 * u + 4]) * a.scale, __uint_as_float(v2[8 * u + 5]) * a.scale);
+          o2.w = pack_bf16(__uint_as_float(v2[8 * u + 6]) * a.scale, __uint_as_float(v2[8 * u + 7]) * a.scale);
+          *reinterpret_cast<uint4*>(dv_dst + c + 8 * u) = o1;
+          *reinterpret_cast<uint4*>(dk_dst + c + 8 * u) = o2;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---- backward: dQ --------------------------------------------------------------------
+
+template <int D>
+struct DqSmem {
+  static constexpr int kT = kBlk * D * 2;
+  static constexpr int kStages = 2;
+  static constexpr int kP = kBlk * kBlk * 2;
+  static constexpr int kBytes = 2 * kT + 2 * kStages * kT + kP + 1024 + 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
+  using L = DqSmem<D>;
+  constexpr int ST = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+  uint8_t* sq = smem;
+  uint8_t* sdo = sq + L::kT;
+  uint8_t* sk = sdo + L::kT;           // ST stages
+  uint8_t* sv = sk + ST * L::kT;       // ST stages
+  uint8_t* sds = sv + ST * L::kT;      // dS [q, kv] K-major
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + L::kP);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;        // ST
+  uint64_t* kv_empty = kv_full + ST;   // ST
+  uint64_t* sp_full = kv_empty + ST;
+  uint64_t* sp_empty = sp_full + 1;
+  uint64_t* ds_full = sp_empty + 1;
+  uint64_t* dq_done = ds_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_done + 1);
+
+  const int qblk = (a.seq / kBlk) - 1 - blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / (a.hq / a.hkv);
+  const int nblk = qblk + 1;
+  const int row0 = b * a.seq + qblk * kBlk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(sp_empty, 4);
+    mbar_init(ds_full, 4);
+    mbar_init(dq_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(q_full, 2 * L::kT);
+      #pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0);
+        tma_load_2d(sdo + c * kBlk * 128, &tm_do, q_full, h * D + 64 * c, row0);
+      }
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_empty[st], ((j / ST) & 1) ^ 1, a.err, kErrTmaWait)) break;
+        const int kv_row = b * a.seq + j * kBlk;
+        mbar_expect_tx(&kv_full[st], 2 * L::kT);
+        #pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_2d(sk + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + kvh) * D + 64 * c, kv_row);
+          tma_load_2d(sv + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + a.hkv + kvh) * D + 64 * c, kv_row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
+      constexpr uint32_t id_dq = idesc_bf16_f32(kBlk, D, 0, 1);
+      const uint32_t q_addr = smem_u32(sq), do_addr = smem_u32(sdo), ds_addr = smem_u32(sds);
+      bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_full[st], (j / ST) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+        if (!mbar_wait(sp_empty, (j & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sk + st * L::kT), v_addr = smem_u32(sv + st * L::kT);
+        #pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+          umma_bf16(t_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024), id_s,
+                    kk > 0);
+          umma_bf16(t_dp, smem_desc_sw128(do_addr + off, 16, 1024), smem_desc_sw128(v_addr + off, 16, 1024), id_s,
+                    kk > 0);
+        }
+        umma_commit(sp_full);
+        if (!mbar_wait(ds_full, j & 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        #pragma unroll
+        for (int kk = 0; kk < kBlk / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+          umma_bf16(t_dq, smem_desc_sw128(ds_addr + aoff, 16, 1024), smem_desc_sw128(k_addr + kk * 2048, kBlk * 128, 1024),
+                    id_dq, (j > 0 || kk > 0));
+        }
+        umma_commit(&kv_empty[st]);
+        umma_commit(dq_done);
+      }
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const float sl2 = a.scale * kLog2e;
+    const int64_t stat = (int64_t(b) * a.hq + h) * a.seq + qblk * kBlk + r;
+    const float lse2 = a.lse[stat] * kLog2e;
+    const float dlt = a.delta[stat];
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const bool diag = j == qblk;
+      if (!mbar_wait(sp_full, j & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      if (j > 0 && !mbar_wait(dq_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      #pragma unroll 1
+      for (int c = 0; c < kBlk; c += 32) {
+        uint32_t s32[32], p32[32];
+        tmem_ld32(t_s + lane_off + c, s32);
+        tmem_ld32(t_dp + lane_off + c, p32);
+        tmem_wait_ld();
+        uint32_t pk[16];
+        #pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float ds[2];
+          #pragma unroll
+          for (int z = 0; z < 2; ++z) {
+            float pv = exp2f(__uint_as_float(s32[e + z]) * sl2 - lse2);
+            if (diag && c + e + z > r) pv = 0.f;
+            ds[z] = pv * (__uint_as_float(p32[e + z]) - dlt);
+          }
+          pk[e / 2] = pack_bf16(ds[0], ds[1]);
+        }
+        store_row32(sds, r, c, pk, kBlk);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sp_empty);
+        mbar_arrive(ds_full);
+      }
+    }
+    if (ok && mbar_wait(dq_done, (nblk - 1) & 1, a.err, kErrEpiWait)) {
+      tc_fence_after();
+      __nv_bfloat16* dst = a.out + int64_t(row0 + r) * a.out_ld + int64_t(h) * D;
+      #pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(t_dq + lane_off + c, v);
+        tmem_wait_ld();
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(v[8 * u + 0]) * a.scale, __uint_as_float(v[8 * u + 1]) * a.scale);
+          o.y = pack_bf16(__uint_as_float(v[8 * u + 2]) * a.scale, __uint_as_float(v[8 * u + 3]) * a.scale);
+          o.z = pack_bf16(__uint_as_float(v[8 * u + 4]) * a.scale, __uint_as_float(v[8 * u + 5]) * a.scale);
+          o.w = pack_bf16(__uint_as_float(v[8 * u + 6]) * a.scale, __uint_as_float(v[8 * u + 7]) * a.scale);
+          *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <class K>
+void set_smem(K kernel, int bytes) {
+  RESIHP_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+void check_shapes(int rows, int seq, int hq, int hkv, int d) {
+  RESIHP_CHECK(d == 64 || d == 128, "attention head_dim must be 64 or 128, got ", d);
+  RESIHP_CHECK(seq % kBlk == 0 && rows % seq == 0, "attention needs seq % 128 == 0 and rows % seq == 0");
+  RESIHP_CHECK(hkv > 0 && hq % hkv == 0, "query heads must be a multiple of kv heads");
+}
+
+}  // namespace
+
+void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float* lse, int rows, int seq, int hq,
+              int hkv, int d, float scale, int* err, cudaStream_t st) {
+  check_shapes(rows, seq, hq, hkv, d);
+  const CUtensorMap tm = make_tma_2d_bf16(qkv, rows, int64_t(hq + 2 * hkv) * d, qkv_ld, 64, kBlk);
+  AttnArgs a{static_cast<__nv_bfloat16*>(out), lse, nullptr, nullptr, seq, hq, hkv, d, out_ld, 0, scale, err};
+  dim3 grid(seq / kBlk, hq, rows / seq);
+  if (d == 128) {
+    set_smem(attn_fwd_kernel<128>, FwdSmem<128>::kBytes);
+    attn_fwd_kernel<128><<<grid, 192, FwdSmem<128>::kBytes, st>>>(tm, a);
+  } else {
+    set_smem(attn_fwd_kernel<64>, FwdSmem<64>::kBytes);
+    attn_fwd_kernel<64><<<grid, 192, FwdSmem<64>::kBytes, st>>>(tm, a);
+  }
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, const void* dout, int64_t dout_ld,
+              const float* lse, float* delta, void* dqkv, int64_t dqkv_ld, int rows, int seq, int hq, int hkv, int d,
+              float scale, int* err, cudaStream_t st) {
+  check_shapes(rows, seq, hq, hkv, d);
+  RESIHP_CHECK(dqkv_ld == int64_t(hq + 2 * hkv) * d, "dqkv must be dense");
+  {
+    const int warps = rows * hq;
+    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(out), out_ld,
+                                                                static_cast<const __nv_bfloat16*>(dout), dout_ld,
+                                                                delta, rows, seq, hq, d);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+  }
+  const CUtensorMap tm = make_tma_2d_bf16(qkv, rows, int64_t(hq + 2 * hkv) * d, qkv_ld, 64, kBlk);
+  const CUtensorMap tm_do = make_tma_2d_bf16(dout, rows, int64_t(hq) * d, dout_ld, 64, kBlk);
+  AttnArgs a{static_cast<__nv_bfloat16*>(dqkv), const_cast<float*>(lse), static_cast<const __nv_bfloat16*>(dout),
+             delta, seq, hq, hkv, d, dqkv_ld, dout_ld, scale, err};
+  dim3 grid_kv(seq / kBlk, hkv, rows / seq);
+  dim3 grid_q(seq / kBlk, hq, rows / seq);
+  if (d == 128) {
+    set_smem(attn_bwd_dkdv_kernel<128>, DkdvSmem<128>::kBytes);
+    attn_bwd_dkdv_kernel<128><<<grid_kv, 192, DkdvSmem<128>::kBytes, st>>>(tm, tm_do, a);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    set_smem(attn_bwd_dq_kernel<128>, DqSmem<128>::kBytes);
+    attn_bwd_dq_kernel<128><<<grid_q, 192, DqSmem<128>::kBytes, st>>>(tm, tm_do, a);
+  } else {
+    set_smem(attn_bwd_dkdv_kernel<64>, DkdvSmem<64>::kBytes);
+    attn_bwd_dkdv_kernel<64><<<grid_kv, 192, DkdvSmem<64>::kBytes, st>>>(tm, tm_do, a);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    set_smem(attn_bwd_dq_kernel<64>, DqSmem<64>::kBytes);
+    attn_bwd_dq_kernel<64><<<grid_q, 192, DqSmem<64>::kBytes, st>>>(tm, tm_do, a);
+  }
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace resihp

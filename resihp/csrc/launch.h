@@ -42,3 +42,35 @@ void gemm_raw(const void* a, int64_t lda, bool a_mn, const void* b, int64_t ldb,
               int max_ctas, int force_bn);
 
 }  // namespace resihp
+
+namespace resihp {
+
+int rmsnorm_partial_rows(int rows, int d, int num_sms);
+void rmsnorm_fwd(const void* x, const void* r, const void* w, void* y, void* s_out, float* rstd, int rows, int d,
+                 float eps, int num_sms, cudaStream_t st);
+void rmsnorm_bwd(const void* dy, const void* s, const void* w, const float* rstd, const void* dres, void* ds,
+                 float* partial, float* dw, int accumulate, int rows, int d, int num_sms, cudaStream_t st);
+
+void rope(void* qkv, const float* cs, int rows, int seq, int heads_qk, int hd, int64_t row_stride, int pos_offset,
+          bool inverse, int num_sms, cudaStream_t st);
+void swiglu_fwd(const void* gu, void* h, int rows, int f, int num_sms, cudaStream_t st);
+void swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, int num_sms, cudaStream_t st);
+void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, float lr, float b1, float b2,
+           float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st);
+void embedding_fwd(const int64_t* ids, const void* w, void* out, int rows, int d, int64_t start, int64_t count,
+                   cudaStream_t st);
+void embedding_bwd(const int64_t* sorted_ids, const int64_t* order, const void* dy, float* dw, int rows, int d,
+                   int64_t start, int64_t count, cudaStream_t st);
+
+void xent_stats(const void* logits, int64_t ld, const int64_t* labels, float* stats, int rows, int v, int64_t start,
+                cudaStream_t st);
+void xent_grad(void* logits, int64_t ld, const int64_t* labels, const float* lse, const float* scale, int rows, int v,
+               int64_t start, cudaStream_t st);
+
+void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float* lse, int rows, int seq, int hq,
+              int hkv, int d, float scale, int* err, cudaStream_t st);
+void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, const void* dout, int64_t dout_ld,
+              const float* lse, float* delta, void* dqkv, int64_t dqkv_ld, int rows, int seq, int hq, int hkv, int d,
+              float scale, int* err, cudaStream_t st);
+
+}  // namespace resihp

@@ -1,0 +1,196 @@
+// Memory-bound kernels of the Llama block and the optimizer:
+//   * RoPE (rotate-half / GPT-NeoX pairing) applied in place to the Q and K heads of
+//     the fused QKV activation, forward and backward (backward rotates by -theta);
+//   * SwiGLU  h = silu(g) * u  over the fused [g | u] projection, forward and backward;
+//   * AdamW over flat fp32 buffers, writing the bf16 working copy in the same pass;
+//   * vocab-parallel embedding lookup, and its deterministic backward (runs of equal
+//     token ids, pre-sorted, are summed in order by one block each).
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace resihp {
+
+namespace {
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+
+// qkv: [rows, (hq + 2*hkv) * hd] bf16; row t has sequence position t % seq.
+// cs: [seq, hd/2, 2] fp32 = (cos, sin) of position * inv_freq[i].
+// Each thread rotates one (i, i + hd/2) pair of one Q or K head.
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs, int rows, int seq,
+                            int heads_qk, int hd, int64_t row_stride, int pos_offset, float sign) {
+  const int half = hd / 2;
+  const int64_t total = int64_t(rows) * heads_qk * half;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int p = int(i % half);
+    const int64_t rh = i / half;
+    const int h = int(rh % heads_qk);
+    const int64_t row = rh / heads_qk;
+    const int pos = int((row + pos_offset) % seq);
+    const float2 c = cs[int64_t(pos) * half + p];
+    __nv_bfloat16* base = qkv + row * row_stride + int64_t(h) * hd;
+    const float x1 = bf(base[p]);
+    const float x2 = bf(base[p + half]);
+    const float sn = sign * c.y;
+    base[p] = __float2bfloat16(x1 * c.x - x2 * sn);
+    base[p + half] = __float2bfloat16(x2 * c.x + x1 * sn);
+  }
+}
+
+__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// gu: [rows, 2F] = [g | u];  h: [rows, F]
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int rows,
+                                  int f) {
+  const int64_t total = int64_t(rows) * f / 2;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row = (2 * i) / f;
+    const int col = int((2 * i) % f);
+    const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * f + col);
+    const __nv_bfloat162 u = *reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * f + f + col);
+    const float2 gf = __bfloat1622float2(g), uf = __bfloat1622float2(u);
+    const float a = gf.x * sigmoid(gf.x) * uf.x;
+    const float b = gf.y * sigmoid(gf.y) * uf.y;
+    *reinterpret_cast<uint32_t*>(h + row * f + col) = pack_bf16(a, b);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
+                                  __nv_bfloat16* __restrict__ dgu, int rows, int f) {
+  const int64_t total = int64_t(rows) * f / 2;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row = (2 * i) / f;
+    const int col = int((2 * i) % f);
+    const float2 gf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * f + col));
+    const float2 uf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * f + f + col));
+    const float2 d = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dh + row * f + col));
+    float dg[2], du[2];
+    const float g2[2] = {gf.x, gf.y}, u2[2] = {uf.x, uf.y}, d2[2] = {d.x, d.y};
+    #pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float s = sigmoid(g2[j]);
+      const float silu = g2[j] * s;
+      du[j] = d2[j] * silu;
+      dg[j] = d2[j] * u2[j] * s * (1.f + g2[j] * (1.f - s));
+    }
+    *reinterpret_cast<uint32_t*>(dgu + row * 2 * f + col) = pack_bf16(dg[0], dg[1]);
+    *reinterpret_cast<uint32_t*>(dgu + row * 2 * f + f + col) = pack_bf16(du[0], du[1]);
+  }
+}
+
+// AdamW step over flat fp32 buffers, the torch.optim.AdamW formulation:
+//   p *= 1 - lr*wd;  m = m + (1-b1)(g-m);  v = b2 v + (1-b2) g^2
+//   p -= (lr / bc1) * m / (sqrt(v) / sqrt(bc2) + eps)
+// and the bf16 working copy of p is refreshed in the same pass.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, int64_t n, float lr, float b1,
+                             float b2, float eps, float wd, float step_size, float bc2_sqrt, float grad_scale) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const float gi = g[i] * grad_scale;
+    float pi = p[i] * (1.f - lr * wd);
+    float mi = m[i];
+    mi = mi + (1.f - b1) * (gi - mi);
+    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    const float denom = sqrtf(vi) / bc2_sqrt + eps;
+    pi = pi - step_size * (mi / denom);
+    p[i] = pi;
+    m[i] = mi;
+    v[i] = vi;
+    if (p_bf16 != nullptr) p_bf16[i] = __float2bfloat16(pi);
+  }
+}
+
+// out[t, :] = W[id_t - start, :] if the id falls in this rank's vocab shard, else 0.
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
+                                     __nv_bfloat16* __restrict__ out, int rows, int d, int64_t start, int64_t count) {
+  const int t = blockIdx.x;
+  if (t >= rows) return;
+  const int64_t id = ids[t] - start;
+  const bool mine = id >= 0 && id < count;
+  uint4* dst = reinterpret_cast<uint4*>(out + int64_t(t) * d);
+  const uint4* src = reinterpret_cast<const uint4*>(w + (mine ? id : 0) * d);
+  for (int c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = mine ? src[c] : make_uint4(0, 0, 0, 0);
+}
+
+// One block per run of equal ids in ``order`` (token indices sorted by id, stable):
+// dW[id - start] += sum of dy rows of the run, in sorted (= token) order.
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ order,
+                                     const __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int rows, int d,
+                                     int64_t start, int64_t count) {
+  const int head = blockIdx.x;
+  if (head >= rows) return;
+  const int64_t id = sorted_ids[head];
+  if (head > 0 && sorted_ids[head - 1] == id) return;  // not the first of its run
+  const int64_t local = id - start;
+  if (local < 0 || local >= count) return;
+  int end = head + 1;
+  while (end < rows && sorted_ids[end] == id) ++end;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = head; j < end; ++j) acc += bf(dy[order[j] * d + c]);
+    dw[local * d + c] += acc;
+  }
+}
+
+int grid_for(int64_t work, int block, int num_sms) {
+  int64_t g = (work + block - 1) / block;
+  return int(std::max<int64_t>(1, std::min<int64_t>(g, int64_t(num_sms) * 16)));
+}
+
+}  // namespace
+
+void rope(void* qkv, const float* cs, int rows, int seq, int heads_qk, int hd, int64_t row_stride, int pos_offset,
+          bool inverse, int num_sms, cudaStream_t st) {
+  RESIHP_CHECK(hd % 2 == 0, "rope head_dim must be even");
+  const int64_t work = int64_t(rows) * heads_qk * (hd / 2);
+  rope_kernel<<<grid_for(work, 256, num_sms), 256, 0, st>>>(static_cast<__nv_bfloat16*>(qkv),
+                                                             reinterpret_cast<const float2*>(cs), rows, seq, heads_qk,
+                                                             hd, row_stride, pos_offset, inverse ? -1.f : 1.f);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void swiglu_fwd(const void* gu, void* h, int rows, int f, int num_sms, cudaStream_t st) {
+  RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
+  swiglu_fwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(h), rows, f);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, int num_sms, cudaStream_t st) {
+  RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
+  swiglu_bwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
+      rows, f);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, float lr, float b1, float b2,
+           float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st) {
+  RESIHP_CHECK(step >= 1, "AdamW step must be >= 1");
+  const double bc1 = 1.0 - std::pow(double(b1), double(step));
+  const double bc2 = 1.0 - std::pow(double(b2), double(step));
+  const float step_size = float(double(lr) / bc1);
+  const float bc2_sqrt = float(std::sqrt(bc2));
+  adamw_kernel<<<grid_for(n, 256, num_sms), 256, 0, st>>>(p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, lr, b1,
+                                                         b2, eps, wd, step_size, bc2_sqrt, grad_scale);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_fwd(const int64_t* ids, const void* w, void* out, int rows, int d, int64_t start, int64_t count,
+                   cudaStream_t st) {
+  RESIHP_CHECK(d % 8 == 0, "embedding width must be a multiple of 8");
+  embedding_fwd_kernel<<<rows, 128, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(w),
+                                             static_cast<__nv_bfloat16*>(out), rows, d, start, count);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_bwd(const int64_t* sorted_ids, const int64_t* order, const void* dy, float* dw, int rows, int d,
+                   int64_t start, int64_t count, cudaStream_t st) {
+  embedding_bwd_kernel<<<rows, 256, 0, st>>>(sorted_ids, order, static_cast<const __nv_bfloat16*>(dy), dw, rows, d,
+                                             start, count);
+  RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace resihp

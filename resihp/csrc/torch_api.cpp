@@ -87,6 +87,189 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
            int(force_bn));
 }
 
+
+static int sms(const torch::Tensor& t) {
+  static int counts[64] = {0};
+  const int dev = t.device().index();
+  if (counts[dev] == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev));
+  return counts[dev];
+}
+
+static void check_rows(const torch::Tensor& t, int64_t cols, const char* name) {
+  check_cuda_bf16(t, name);
+  TORCH_CHECK(t.dim() == 2 && t.size(1) == cols && t.is_contiguous(), name, " must be contiguous [rows, ", cols, "]");
+}
+
+// ---- RMSNorm --------------------------------------------------------------------------
+
+std::vector<torch::Tensor> rmsnorm_fwd_t(torch::Tensor x, c10::optional<torch::Tensor> r, torch::Tensor w, double eps) {
+  const int64_t d = w.numel();
+  check_rows(x, d, "x");
+  check_cuda_bf16(w, "w");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({x.size(0)}, x.options().dtype(torch::kFloat));
+  torch::Tensor s = x;
+  const void* rp = nullptr;
+  if (r.has_value()) {
+    check_rows(*r, d, "residual");
+    s = torch::empty_like(x);
+    rp = r->data_ptr();
+  }
+  rmsnorm_fwd(x.data_ptr(), rp, w.data_ptr(), y.data_ptr(), rp ? s.data_ptr() : nullptr, rstd.data_ptr<float>(),
+              int(x.size(0)), int(d), float(eps), sms(x), cur_stream());
+  return {y, s, rstd};
+}
+
+torch::Tensor rmsnorm_bwd_t(torch::Tensor dy, torch::Tensor s, torch::Tensor w, torch::Tensor rstd,
+                            c10::optional<torch::Tensor> dres, torch::Tensor dw, bool accumulate) {
+  const int64_t d = w.numel();
+  check_rows(dy, d, "dy");
+  check_rows(s, d, "s");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat && dw.numel() == d && dw.is_contiguous(), "dw must be fp32 [d]");
+  c10::cuda::CUDAGuard guard(dy.device());
+  const int rows = int(dy.size(0));
+  auto partial = torch::empty({rmsnorm_partial_rows(rows, int(d), sms(dy)), d}, dy.options().dtype(torch::kFloat));
+  auto ds = torch::empty_like(dy);
+  const void* dr = nullptr;
+  if (dres.has_value()) {
+    check_rows(*dres, d, "dres");
+    dr = dres->data_ptr();
+  }
+  rmsnorm_bwd(dy.data_ptr(), s.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dr, ds.data_ptr(),
+              partial.data_ptr<float>(), dw.data_ptr<float>(), accumulate ? 1 : 0, rows, int(d), sms(dy), cur_stream());
+  return ds;
+}
+
+// ---- RoPE / SwiGLU --------------------------------------------------------------------
+
+void rope_t(torch::Tensor qkv, torch::Tensor cs, int64_t seq, int64_t heads_qk, int64_t hd, int64_t pos_offset,
+            bool inverse) {
+  check_cuda_bf16(qkv, "qkv");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D with unit inner stride");
+  TORCH_CHECK(cs.scalar_type() == torch::kFloat && cs.is_contiguous() && cs.numel() == seq * hd, "cs must be fp32 [seq, hd/2, 2]");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  rope(qkv.data_ptr(), cs.data_ptr<float>(), int(qkv.size(0)), int(seq), int(heads_qk), int(hd), qkv.stride(0),
+       int(pos_offset), inverse, sms(qkv), cur_stream());
+}
+
+torch::Tensor swiglu_fwd_t(torch::Tensor gu) {
+  check_cuda_bf16(gu, "gu");
+  TORCH_CHECK(gu.dim() == 2 && gu.is_contiguous(), "gu must be contiguous [rows, 2F]");
+  c10::cuda::CUDAGuard guard(gu.device());
+  const int64_t f = gu.size(1) / 2;
+  auto h = torch::empty({gu.size(0), f}, gu.options());
+  swiglu_fwd(gu.data_ptr(), h.data_ptr(), int(gu.size(0)), int(f), sms(gu), cur_stream());
+  return h;
+}
+
+torch::Tensor swiglu_bwd_t(torch::Tensor gu, torch::Tensor dh) {
+  check_cuda_bf16(gu, "gu");
+  const int64_t f = gu.size(1) / 2;
+  check_rows(dh, f, "dh");
+  c10::cuda::CUDAGuard guard(gu.device());
+  auto dgu = torch::empty_like(gu);
+  swiglu_bwd(gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), int(gu.size(0)), int(f), sms(gu), cur_stream());
+  return dgu;
+}
+
+// ---- AdamW ----------------------------------------------------------------------------
+
+void adamw_t(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p_bf16,
+             double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale) {
+  for (auto* t : {&p, &g, &m, &v})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat && t->is_contiguous() && t->numel() == p.numel(),
+                "AdamW buffers must be contiguous fp32 of equal size");
+  void* pb = nullptr;
+  if (p_bf16.has_value()) {
+    TORCH_CHECK(p_bf16->scalar_type() == torch::kBFloat16 && p_bf16->numel() == p.numel() && p_bf16->is_contiguous(),
+                "bf16 copy must match");
+    pb = p_bf16->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(p.device());
+  adamw(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), pb, p.numel(), float(lr),
+        float(b1), float(b2), float(eps), float(wd), step, float(grad_scale), sms(p), cur_stream());
+}
+
+// ---- embedding ------------------------------------------------------------------------
+
+torch::Tensor embedding_fwd_t(torch::Tensor ids, torch::Tensor w, int64_t start) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kLong && ids.is_contiguous(), "ids must be int64 CUDA");
+  check_cuda_bf16(w, "w");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "embedding table must be contiguous");
+  c10::cuda::CUDAGuard guard(w.device());
+  auto out = torch::empty({ids.numel(), w.size(1)}, w.options());
+  embedding_fwd(ids.data_ptr<int64_t>(), w.data_ptr(), out.data_ptr(), int(ids.numel()), int(w.size(1)), start,
+                w.size(0), cur_stream());
+  return out;
+}
+
+void embedding_bwd_t(torch::Tensor ids, torch::Tensor dy, torch::Tensor dw, int64_t start) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kLong, "ids must be int64 CUDA");
+  check_cuda_bf16(dy, "dy");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat && dw.dim() == 2 && dw.is_contiguous(), "dw must be fp32 [V, d]");
+  c10::cuda::CUDAGuard guard(dy.device());
+  auto flat = ids.reshape({-1});
+  auto sorted = std::get<0>(torch::sort(flat, /*stable=*/true, /*dim=*/0, /*descending=*/false));
+  auto order = std::get<1>(torch::sort(flat, true, 0, false)).contiguous();
+  auto dy2 = dy.reshape({flat.numel(), dw.size(1)}).contiguous();
+  embedding_bwd(sorted.contiguous().data_ptr<int64_t>(), order.data_ptr<int64_t>(), dy2.data_ptr(),
+                dw.data_ptr<float>(), int(flat.numel()), int(dw.size(1)), start, dw.size(0), cur_stream());
+}
+
+// ---- cross-entropy --------------------------------------------------------------------
+
+torch::Tensor xent_stats_t(torch::Tensor logits, torch::Tensor labels, int64_t start) {
+  check_cuda_bf16(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D");
+  TORCH_CHECK(labels.scalar_type() == torch::kLong && labels.numel() == logits.size(0) && labels.is_contiguous(),
+              "labels must be int64 [rows]");
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto stats = torch::empty({logits.size(0), 3}, logits.options().dtype(torch::kFloat));
+  xent_stats(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), stats.data_ptr<float>(),
+             int(logits.size(0)), int(logits.size(1)), start, cur_stream());
+  return stats;
+}
+
+void xent_grad_t(torch::Tensor logits, torch::Tensor labels, torch::Tensor lse, torch::Tensor scale, int64_t start) {
+  check_cuda_bf16(logits, "logits");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat && lse.numel() == logits.size(0) && lse.is_contiguous(), "lse");
+  TORCH_CHECK(scale.scalar_type() == torch::kFloat && scale.numel() == 1 && scale.is_cuda(), "scale must be a CUDA fp32 scalar");
+  c10::cuda::CUDAGuard guard(logits.device());
+  xent_grad(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), lse.data_ptr<float>(),
+            scale.data_ptr<float>(), int(logits.size(0)), int(logits.size(1)), start, cur_stream());
+}
+
+// ---- attention ------------------------------------------------------------------------
+
+std::vector<torch::Tensor> attn_fwd_t(torch::Tensor qkv, int64_t seq, int64_t hq, int64_t hkv, int64_t d, double scale) {
+  check_cuda_bf16(qkv, "qkv");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (hq + 2 * hkv) * d, "qkv must be [T, (hq+2hkv)*d]");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int64_t rows = qkv.size(0);
+  auto out = torch::empty({rows, hq * d}, qkv.options());
+  auto lse = torch::empty({rows / seq, hq, seq}, qkv.options().dtype(torch::kFloat));
+  attn_fwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr<float>(), int(rows), int(seq),
+           int(hq), int(hkv), int(d), float(scale), error_word(qkv.device()), cur_stream());
+  return {out, lse};
+}
+
+torch::Tensor attn_bwd_t(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, int64_t seq,
+                         int64_t hq, int64_t hkv, int64_t d, double scale) {
+  check_cuda_bf16(qkv, "qkv");
+  check_cuda_bf16(out, "out");
+  check_cuda_bf16(dout, "dout");
+  TORCH_CHECK(dout.stride(1) == 1 && out.stride(1) == 1, "attention tensors need unit inner stride");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int64_t rows = qkv.size(0);
+  auto dqkv = torch::empty({rows, (hq + 2 * hkv) * d}, qkv.options());
+  auto delta = torch::empty_like(lse);
+  attn_bwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), dout.data_ptr(), dout.stride(0),
+           lse.data_ptr<float>(), delta.data_ptr<float>(), dqkv.data_ptr(), dqkv.stride(0), int(rows), int(seq),
+           int(hq), int(hkv), int(d), float(scale), error_word(qkv.device()), cur_stream());
+  return dqkv;
+}
+
 }  // namespace resihp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -95,4 +278,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &resihp::gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c"), py::arg("epi"), py::arg("alpha") = 1.0, py::arg("residual") = py::none(),
         py::arg("max_ctas") = 0, py::arg("force_bn") = 0);
+  m.def("rmsnorm_fwd", &resihp::rmsnorm_fwd_t);
+  m.def("rmsnorm_bwd", &resihp::rmsnorm_bwd_t);
+  m.def("rope", &resihp::rope_t);
+  m.def("swiglu_fwd", &resihp::swiglu_fwd_t);
+  m.def("swiglu_bwd", &resihp::swiglu_bwd_t);
+  m.def("adamw", &resihp::adamw_t);
+  m.def("embedding_fwd", &resihp::embedding_fwd_t);
+  m.def("embedding_bwd", &resihp::embedding_bwd_t);
+  m.def("xent_stats", &resihp::xent_stats_t);
+  m.def("xent_grad", &resihp::xent_grad_t);
+  m.def("attn_fwd", &resihp::attn_fwd_t);
+  m.def("attn_bwd", &resihp::attn_bwd_t);
 }
