@@ -1,0 +1,210 @@
+"""The atomic, topology-free logical checkpoint.
+
+Format (identical keys and digest to the reference, ``resihp/checkpoint.py:64-108``, so
+either implementation reads the other's files)::
+
+    {"format_version": 1, "completed_steps": int, "plan_version": int,
+     "identity": {...shape- and data-defining config fields...},
+     "params": {name: full FP32 tensor},
+     "optim":  {name: {"exp_avg", "exp_avg_sq", "step"}},
+     "cpu_rng_state": ByteTensor, "cuda_rng_state": [ByteTensor] | None,
+     "digest": sha256 over the scalar fields and every tensor's dtype, shape and bytes}
+
+``identity`` holds the reference's fields for GPT-2 blocks and adds the Llama shape
+fields otherwise; topology (TP/PP/DP, micro-batch size) is deliberately absent.
+Writes go to ``<path>.tmp``, are read back and digest-checked, then ``os.replace``-d
+over the single canonical path; any failure removes the temp file and leaves the last
+valid checkpoint untouched. Every problem a load can find is reported as its own
+:class:`CheckpointError` (missing file, unreadable payload, format, identity, names,
+shapes, cursor/step consistency, digest -- digest last).
+"""
+
+from __future__ import annotations
+
+from hashlib import sha256
+import json
+import os
+from pathlib import Path
+
+import torch
+
+from .config import TrainConfig
+
+FORMAT_VERSION = 1
+OPTIM_STATES = ("exp_avg", "exp_avg_sq", "step")
+
+
+class CheckpointError(RuntimeError):
+    """A checkpoint is missing, unreadable, inconsistent or corrupted."""
+
+
+def identity(config: TrainConfig) -> dict:
+    out = {
+        "model_dim": config.model_dim,
+        "num_layers": config.num_layers,
+        "num_heads": config.num_heads,
+        "batch_size": config.batch_size,
+        "seed": config.seed,
+        "vocab_size": config.vocab_size,
+        "sequence_length": config.seq_len,
+    }
+    if config.arch != "gpt2":
+        out.update(
+            arch=config.arch, ffn_dim=config.ffn, num_kv_heads=config.kv_heads,
+            tied_embeddings=config.tied_embeddings,
+        )
+    return out
+
+
+def payload_digest(payload: dict) -> str:
+    h = sha256()
+    scalars = {k: payload[k] for k in ("format_version", "completed_steps", "plan_version", "identity")}
+    h.update(json.dumps(scalars, sort_keys=True).encode("utf-8"))
+
+    def add(t):
+        arr = t.detach().cpu().contiguous().numpy()
+        h.update(repr(arr.dtype).encode("utf-8"))
+        h.update(repr(arr.shape).encode("utf-8"))
+        h.update(arr.tobytes())
+
+    for name in sorted(payload["params"]):
+        h.update(name.encode("utf-8"))
+        add(payload["params"][name])
+    for name in sorted(payload["optim"]):
+        for key in OPTIM_STATES:
+            value = payload["optim"][name][key]
+            h.update(f"{name}:{key}".encode("utf-8"))
+            add(value if torch.is_tensor(value) else torch.tensor(value))
+    add(payload["cpu_rng_state"])
+    cuda = payload["cuda_rng_state"]
+    h.update(b"cuda:none" if cuda is None else b"cuda")
+    for t in cuda or ():
+        add(t)
+    return h.hexdigest()
+
+
+def build_payload(config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int) -> dict:
+    """Payload from a full logical state ``{name: {param[, exp_avg, exp_avg_sq, step]}}``."""
+    params = {n: f["param"].detach().to("cpu", torch.float32).clone() for n, f in full.items()}
+    optim = {}
+    for n, f in full.items():
+        if "exp_avg" in f:
+            optim[n] = {
+                "exp_avg": f["exp_avg"].detach().to("cpu", torch.float32).clone(),
+                "exp_avg_sq": f["exp_avg_sq"].detach().to("cpu", torch.float32).clone(),
+                "step": (f["step"].detach().cpu().clone() if torch.is_tensor(f["step"]) else torch.tensor(float(f["step"]))),
+            }
+    return {
+        "format_version": FORMAT_VERSION,
+        "completed_steps": int(completed_steps),
+        "plan_version": int(plan_version),
+        "identity": identity(config),
+        "params": params,
+        "optim": optim,
+        "cpu_rng_state": torch.get_rng_state(),
+        "cuda_rng_state": torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None,
+    }
+
+
+def _torch_load(path: Path, mmap: bool = False) -> dict:
+    return torch.load(path, weights_only=False, mmap=mmap)
+
+
+def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int = 0) -> Path:
+    """Atomically write the logical checkpoint; returns the canonical path."""
+    if type(plan_version) is not int or plan_version < 0:
+        raise CheckpointError("plan_version must be a non-negative integer")
+    payload = build_payload(config, full, completed_steps=completed_steps, plan_version=plan_version)
+    payload["digest"] = payload_digest(payload)
+    path = Path(path)
+    tmp = path.with_name(path.name + ".tmp")
+    try:
+        torch.save(payload, tmp)
+        if payload_digest(_torch_load(tmp)) != payload["digest"]:
+            raise CheckpointError("checkpoint write verification failed: temp file differs from memory")
+        os.replace(tmp, path)
+    except BaseException:
+        if tmp.exists():
+            tmp.unlink()
+        raise
+    return path
+
+
+def read_payload(path, *, mmap: bool = False) -> dict:
+    path = Path(path)
+    if not path.exists():
+        raise CheckpointError(f"checkpoint missing: {path}")
+    try:
+        return _torch_load(path, mmap=mmap)
+    except Exception as error:
+        raise CheckpointError(f"checkpoint unreadable {path}: {error}") from error
+
+
+def verify_digest(payload: dict) -> None:
+    stored = payload.get("digest")
+    if stored is None:
+        raise CheckpointError("checkpoint has no content digest")
+    if payload_digest(payload) != stored:
+        raise CheckpointError("checkpoint digest mismatch: content is corrupted")
+
+
+def validate(payload: dict, config: TrainConfig, expected_shapes: dict[str, tuple]) -> None:
+    """Every structural check, each as its own root cause; the digest is checked last."""
+    if payload.get("format_version") != FORMAT_VERSION:
+        raise CheckpointError(f"unsupported checkpoint format version: {payload.get('format_version')}")
+    if payload["identity"] != identity(config):
+        raise CheckpointError(f"checkpoint identity differs from the run: {payload['identity']} != {identity(config)}")
+    saved = payload["params"]
+    missing = set(expected_shapes) - set(saved)
+    if missing:
+        raise CheckpointError(f"checkpoint is missing parameters: {sorted(missing)}")
+    extra = set(saved) - set(expected_shapes)
+    if extra:
+        raise CheckpointError(f"checkpoint has unknown parameters: {sorted(extra)}")
+    for name, shape in expected_shapes.items():
+        if tuple(saved[name].shape) != tuple(shape):
+            raise CheckpointError(f"checkpoint parameter shape mismatch {name}: {tuple(saved[name].shape)} != {tuple(shape)}")
+    completed = payload["completed_steps"]
+    optim = payload["optim"]
+    if completed == 0:
+        if optim:
+            raise CheckpointError("cursor inconsistency: completed_steps is 0 but optimizer state is present")
+    else:
+        if set(optim) != set(saved):
+            raise CheckpointError(
+                f"cursor inconsistency: optimizer state does not match parameters "
+                f"missing={sorted(set(saved) - set(optim))} extra={sorted(set(optim) - set(saved))}"
+            )
+        for name, state in optim.items():
+            step = int(state["step"].item()) if torch.is_tensor(state["step"]) else int(state["step"])
+            if step != completed:
+                raise CheckpointError(f"cursor inconsistency: completed_steps={completed} but {name}.step={step}")
+    verify_digest(payload)
+
+
+def load_anchor(path, *, verify: bool = True) -> tuple[dict[str, dict[str, torch.Tensor]], int]:
+    """``({name: {param[, exp_avg, exp_avg_sq, step]}}, completed_steps)`` from a checkpoint."""
+    payload = read_payload(path)
+    if verify:
+        verify_digest(payload)
+    anchor = {}
+    for name, param in payload["params"].items():
+        entry = {"param": param}
+        state = payload["optim"].get(name)
+        if state is not None:
+            entry.update({k: state[k] for k in OPTIM_STATES})
+        anchor[name] = entry
+    return anchor, payload["completed_steps"]
+
+
+def load_checkpoint(path, config: TrainConfig) -> tuple[dict, int, int]:
+    """Validated ``(anchor, completed_steps, plan_version)``; restores the CPU/CUDA RNG."""
+    from .models.layout import model_specs
+
+    payload = read_payload(path)
+    validate(payload, config, {s.name: s.shape for s in model_specs(config)})
+    torch.set_rng_state(payload["cpu_rng_state"])
+    if payload["cuda_rng_state"] is not None and torch.cuda.is_available():
+        torch.cuda.set_rng_state_all(payload["cuda_rng_state"])
+    anchor, completed = load_anchor(path, verify=False)
+    return anchor, completed, payload["plan_version"]

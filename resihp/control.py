@@ -1,0 +1,278 @@
+"""Control plane: fail-stop detection, world re-formation, consistent stop.
+
+Semantics of the reference (``resihp/control.py:55-485``):
+
+* A fail-stop is a real ``SIGKILL``. Detection is out of band: :meth:`ControlPlane.observe`
+  rendezvouses at each iteration boundary on the launcher's store and reads the
+  membership the supervisor published from its process table.
+* A rank has a stable **plan rank** (its launch identity, the only rank the planner,
+  plan and checkpoint speak) and a **torch rank** (its index in the current membership,
+  re-assigned every time the world is re-formed); this class owns the translation.
+* The **world group** is a Gloo group over the current membership, re-formed under a
+  fresh store prefix after every fail-stop; control collectives ride it. The
+  **training groups** come from the current plan (NCCL on GPU, Gloo on CPU), built in
+  one plan-derived order by every rank: one TP group per stage, one union group per
+  pipeline hop, the executor group over every placed rank, the gradient-reduction groups
+  (DP position groups and tied-embedding pairs) and the live group over every surviving
+  rank, which the recovery transfers ride.
+* Six consistent-stop codes; :meth:`agree` raises the *same* :class:`ConsistentStop` on
+  every rank, derived from the gathered reports rather than the local view.
+* :meth:`safe_point` runs steps 4-9: mark failed, replan, dissolve and re-form the world,
+  agree on the plan, build the new groups, recover along the single path, agree on plan
+  and state digests. A stop leaves no training group behind.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from datetime import timedelta
+import os
+import time
+
+from . import membership
+from .config import TrainConfig
+from .parallel.dp import reduction_topology
+from .plan import ExecutionPlan, InfeasiblePlan, boundary_hops, build_plan
+from .recovery import TrainingGroups
+
+STOP_CODES = (
+    "no_feasible_tp",
+    "no_executable_pp",
+    "no_feasible_dp_target",
+    "checkpoint_unusable",
+    "plan_disagreement",
+    "state_mismatch",
+)
+_DIGEST_STOP = {"plan": "plan_disagreement", "state": "state_mismatch"}
+GROUP_TIMEOUT = timedelta(seconds=int(os.environ.get("RESIHP_GROUP_TIMEOUT", "300")))
+
+
+@dataclass(frozen=True)
+class StopReason:
+    code: str
+    message: str
+
+
+class ConsistentStop(RuntimeError):
+    def __init__(self, reason: StopReason):
+        super().__init__(f"{reason.code}: {reason.message}")
+        self.reason = reason
+
+
+class ControlPlane:
+    """This rank's place in the world; rebuilds it after a real fail-stop."""
+
+    def __init__(self, rank, members, store, training_backend, *, memory_budget=None):
+        self.rank = int(rank)
+        self.members = tuple(sorted(members))
+        self.store = store
+        self.training_backend = training_backend
+        self.epoch = 0
+        self.boundary = 0
+        self.world_group = None
+        self.groups = TrainingGroups()
+        self.memory_budget = memory_budget
+        self.training_run = None
+        self.checkpoint_path = None
+        self.device = None
+        self.state_digest = ""
+        self.pin = False
+        self.last_recovery: dict = {}
+
+    @classmethod
+    def initialize(cls, *, training_backend=None, memory_budget=None) -> "ControlPlane":
+        import torch
+
+        rank = int(os.environ["RANK"])
+        world = int(os.environ["WORLD_SIZE"])
+        store = membership.connect(os.environ[membership.HOST_ENV], os.environ[membership.PORT_ENV])
+        if training_backend is None:
+            training_backend = "nccl" if torch.cuda.is_available() else "gloo"
+        cp = cls(rank, range(world), store, training_backend, memory_budget=memory_budget)
+        cp.form_world(cp.members, epoch=0)
+        return cp
+
+    # --- ranks ---------------------------------------------------------------------
+
+    @property
+    def world_size(self) -> int:
+        return len(self.members)
+
+    def torch_rank(self, plan_rank: int) -> int:
+        return self.members.index(plan_rank)
+
+    # --- detection / world ---------------------------------------------------------
+
+    def observe(self) -> tuple[int, ...]:
+        """Safe-point steps 3-4: arrive at the next boundary; the ranks that did not."""
+        self.boundary += 1
+        published = membership.boundary(self.store, self.boundary, timeout=GROUP_TIMEOUT)
+        return tuple(r for r in self.members if r not in published)
+
+    def form_world(self, members, *, epoch: int) -> None:
+        import torch.distributed as dist
+
+        self.members = tuple(sorted(members))
+        self.epoch = int(epoch)
+        dist.init_process_group(
+            backend="gloo",
+            store=dist.PrefixStore(membership.PG_PREFIX.format(epoch=self.epoch), self.store),
+            rank=self.torch_rank(self.rank),
+            world_size=self.world_size,
+            timeout=GROUP_TIMEOUT,
+        )
+        self.world_group = dist.group.WORLD
+        self.groups.world = self.world_group
+
+    def dissolve_world(self) -> None:
+        import torch.distributed as dist
+
+        self.destroy_training_groups()
+        dist.destroy_process_group()
+        self.world_group = None
+        self.groups.world = None
+
+    # --- training groups -----------------------------------------------------------
+
+    def attach_run(self, run, *, checkpoint_path, device=None, pin=False) -> None:
+        self.training_run = run
+        self.checkpoint_path = checkpoint_path
+        self.device = device
+        self.pin = pin
+
+    def is_training_rank(self, plan: ExecutionPlan) -> bool:
+        return self.rank in set(plan.active_ranks)
+
+    def _new_group(self, plan_ranks):
+        import torch.distributed as dist
+
+        return dist.new_group(
+            ranks=[self.torch_rank(r) for r in plan_ranks], backend=self.training_backend, timeout=GROUP_TIMEOUT
+        )
+
+    def build_training_groups(self, plan: ExecutionPlan) -> TrainingGroups:
+        """Safe-point step 6c: every rank creates every group in the same plan order."""
+        g = TrainingGroups(world=self.world_group)
+        for stage in sorted(plan.stages, key=lambda s: (s.replica_id, s.stage_id)):
+            handle = self._new_group(stage.tp_members)
+            if self.rank in stage.tp_members:
+                g.tp = handle
+        for hop in boundary_hops(plan):
+            handle = self._new_group(hop)
+            if self.rank in hop:
+                g.hops[hop] = handle
+        executors = self._new_group(plan.active_ranks)
+        g.executor = executors if self.is_training_rank(plan) else None
+        topo = reduction_topology(plan)
+        for members in topo.tied_groups + topo.dp_groups:
+            handle = self._new_group(members)
+            if self.rank in members:
+                g.reduce[members] = handle
+        g.live = self._new_group(self.members)
+        self.groups = g
+        return g
+
+    def destroy_training_groups(self) -> None:
+        import torch.distributed as dist
+
+        g = self.groups
+        handles = [g.tp, *g.hops.values(), g.executor, *g.reduce.values(), g.live]
+        seen = set()
+        for h in handles:
+            if h is not None and id(h) not in seen:
+                seen.add(id(h))
+                dist.destroy_process_group(h)
+        self.groups = TrainingGroups(world=self.world_group)
+
+    # --- the iteration -------------------------------------------------------------
+
+    def training_step(self):
+        if self.training_run is None:
+            return None
+        return self.training_run.step()
+
+    def commit_checkpoint(self, plan: ExecutionPlan, *, cursor: int) -> None:
+        from .recovery import commit_checkpoint
+
+        if not self.is_training_rank(plan):
+            return
+        commit_checkpoint(
+            self.training_run, self.checkpoint_path, plan=plan, groups=self.groups,
+            writer=self.rank == plan.active_ranks[0], cursor=cursor, device=self.device,
+        )
+
+    def _recover_state(self, plan, previous, cursor) -> None:
+        from .recovery import recover
+
+        self.training_run, self.state_digest = recover(
+            self.training_run, plan=plan, previous=previous, rank=self.rank, cursor=cursor,
+            checkpoint_path=self.checkpoint_path, groups=self.groups, device=self.device, pin=self.pin,
+        )
+
+    def agree(self, reason: StopReason | None = None, **digests: str) -> None:
+        """Unanimous decision over the world group (same ConsistentStop everywhere)."""
+        import torch.distributed as dist
+
+        local = (None if reason is None else (reason.code, reason.message), tuple(sorted(digests.items())))
+        gathered: list = [None] * self.world_size
+        dist.all_gather_object(gathered, local, group=self.world_group)
+        for index, (reported, _) in enumerate(gathered):
+            if reported is not None:
+                raise ConsistentStop(StopReason(reported[0], f"rank {self.members[index]}: {reported[1]}"))
+        for label in sorted(digests):
+            values = {dict(entry)[label] for _, entry in gathered}
+            if len(values) > 1:
+                raise ConsistentStop(StopReason(_DIGEST_STOP[label], f"ranks disagree on the {label} digest: {sorted(values)}"))
+
+    def safe_point(self, config: TrainConfig, plan: ExecutionPlan, failed_ranks, lost, *, next_step: int):
+        """Steps 4-9 of the fail-stop safe point; returns ``(new plan, failed ranks)``."""
+        t0 = time.perf_counter()
+        phases = {}
+        failed = tuple(sorted(set(failed_ranks) | set(lost)))
+        survivors = tuple(r for r in self.members if r not in set(lost))
+        new_plan, reason = None, None
+        try:
+            new_plan = build_plan(
+                config, step=next_step, version=plan.version + 1, failed_ranks=failed, previous=plan,
+                memory_budget=self.memory_budget, vocab_size=config.vocab_size, sequence_length=config.seq_len,
+            )
+        except InfeasiblePlan as error:
+            reason = StopReason(error.reason.code, error.reason.message)
+        phases["replan_s"] = time.perf_counter() - t0
+        t = time.perf_counter()
+        self.dissolve_world()
+        self.form_world(survivors, epoch=self.epoch + 1)
+        phases["reform_world_s"] = time.perf_counter() - t
+        self.agree(reason, plan="" if new_plan is None else new_plan.digest)
+        try:
+            t = time.perf_counter()
+            self.build_training_groups(new_plan)
+            phases["build_groups_s"] = time.perf_counter() - t
+            t = time.perf_counter()
+            reason = None
+            try:
+                self._recover_state(new_plan, plan, next_step)
+            except Exception as error:  # classified below; anything else is a bug
+                from .recovery import recovery_stop_code
+
+                code = recovery_stop_code(error)
+                if code is None:
+                    raise
+                reason = StopReason(code, str(error))
+            phases["recover_state_s"] = time.perf_counter() - t
+            self.agree(reason)
+            self.agree(plan=new_plan.digest, state=self.state_digest)
+        except ConsistentStop:
+            self.destroy_training_groups()
+            raise
+        phases["total_s"] = time.perf_counter() - t0
+        self.last_recovery = phases
+        return new_plan, failed
+
+    def shutdown(self) -> None:
+        import torch.distributed as dist
+
+        self.destroy_training_groups()
+        dist.barrier(group=self.world_group)
+        dist.destroy_process_group()
+        self.world_group = None

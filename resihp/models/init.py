@@ -1,0 +1,80 @@
+"""Deterministic initial weights for a configuration.
+
+* GPT-2 blocks: the reference's module construction order and torch defaults
+  (``resihp/model.py:100-116``: embeddings ``normal(0, 1)``, ``nn.Linear``
+  Kaiming-uniform, LayerNorm ones/zeros), driven by ``torch.manual_seed(seed)``, so the
+  full logical state is bit-identical to the reference model built with the same seed.
+* Llama blocks: every matrix ``normal(0, init_std)`` (default 0.02), norm weights 1.
+  Each logical tensor has its own generator seeded from ``(seed, name)``, so a rank
+  materialises only the tensors its stage owns -- on the device it trains on -- and
+  still agrees bit for bit with every other rank and with a single-process run on the
+  same device type.
+"""
+
+from __future__ import annotations
+
+import zlib
+
+import torch
+
+from ..config import TrainConfig
+from .layout import TensorSpec, model_specs, stage_specs
+
+
+def _gpt2_reference_state(config: TrainConfig) -> dict[str, torch.Tensor]:
+    from torch import nn
+
+    d = config.model_dim
+    torch.manual_seed(config.seed)
+    state: dict[str, torch.Tensor] = {}
+    state["token_embedding.weight"] = nn.Embedding(config.vocab_size, d).weight.detach()
+    state["position_embedding.weight"] = nn.Embedding(config.seq_len, d).weight.detach()
+    for gid in range(config.num_layers):
+        p = f"layers.{gid}."
+        state[p + "attn_norm.weight"] = nn.LayerNorm(d).weight.detach()
+        state[p + "attn_norm.bias"] = torch.zeros(d)
+        for name in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            state[p + f"attn.{name}.weight"] = nn.Linear(d, d, bias=False).weight.detach()
+        state[p + "mlp_norm.weight"] = nn.LayerNorm(d).weight.detach()
+        state[p + "mlp_norm.bias"] = torch.zeros(d)
+        state[p + "mlp.fc1.weight"] = nn.Linear(d, config.ffn, bias=False).weight.detach()
+        state[p + "mlp.fc2.weight"] = nn.Linear(config.ffn, d, bias=False).weight.detach()
+    state["final_norm.weight"] = nn.LayerNorm(d).weight.detach()
+    state["final_norm.bias"] = torch.zeros(d)
+    head = nn.Linear(d, config.vocab_size, bias=False).weight.detach()
+    if config.tied_embeddings:
+        pass  # the head reuses token_embedding.weight
+    else:
+        state["lm_head.weight"] = head
+    return state
+
+
+def _seed_for(config: TrainConfig, name: str) -> int:
+    return (config.seed * 1_000_003 + zlib.crc32(name.encode("utf-8"))) & 0x7FFF_FFFF_FFFF
+
+
+def init_tensor(config: TrainConfig, spec: TensorSpec, device) -> torch.Tensor:
+    """One Llama-block logical tensor, full shape, FP32, on ``device``."""
+    if spec.init == "ones":
+        return torch.ones(spec.shape, dtype=torch.float32, device=device)
+    if spec.init == "zeros":
+        return torch.zeros(spec.shape, dtype=torch.float32, device=device)
+    gen = torch.Generator(device=device).manual_seed(_seed_for(config, spec.name))
+    std = 0.02 if config.init_std is None else config.init_std
+    return torch.randn(spec.shape, generator=gen, dtype=torch.float32, device=device) * std
+
+
+def initial_state(config: TrainConfig, *, names=None, device="cpu") -> dict[str, torch.Tensor]:
+    """Full logical FP32 tensors for ``names`` (default: the whole model)."""
+    if config.arch == "gpt2":
+        full = _gpt2_reference_state(config)
+        keep = full if names is None else {n: full[n] for n in names}
+        return {n: t.to(device) for n, t in keep.items()}
+    specs = {s.name: s for s in model_specs(config)}
+    wanted = list(specs) if names is None else list(names)
+    return {n: init_tensor(config, specs[n], device) for n in wanted}
+
+
+def initial_stage_state(config: TrainConfig, layer_ids, is_first, is_last, device="cpu") -> dict[str, torch.Tensor]:
+    names = [s.name for s in stage_specs(config, layer_ids, is_first, is_last)]
+    return initial_state(config, names=names, device=device)

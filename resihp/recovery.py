@@ -1,0 +1,432 @@
+"""The single fail-stop recovery path, and a rank's training state under one plan.
+
+Orchestration only: the planner's :class:`~resihp.plan.StateRoute` entries decide what
+moves from which donor under which layout; :func:`recover` executes them (reference:
+``resihp/recovery.py:373-468``). What is recovered is ``param``, ``exp_avg``,
+``exp_avg_sq`` and ``step`` plus the data cursor; gradients are never persistent.
+
+Transfers. A peer route (``prev_owner`` / ``peer_replica``) is one collective over the
+group of all live ranks: the donors place their shards (one copy of every element: every
+TP shard of the donor stage, a replicated tensor from its first member only) into a
+full-size buffer of the route's tensors, the buffer is summed, and each target keeps
+its slice under the *new* degree -- the re-partition happens in the same pass. A
+``checkpoint`` route is sliced straight from the anchor. The reference moves the same
+state through a CPU object gather of the whole model per donor degree.
+
+Verification (principle A1): once installed, each rank's new shards are compared with
+``torch.equal`` against the same slices of the checkpoint anchor; the agreed state
+digest is the checkpoint's own content digest, identical on every rank. When the
+checkpoint is older than the live state (``checkpoint_every > 1``) a plan that needs a
+``checkpoint`` route rolls every rank back to the anchor; otherwise the live state is
+kept and the digest is agreed over the ranks' local shard digests.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from hashlib import sha256
+
+import torch
+import torch.distributed as dist
+
+from .checkpoint import CheckpointError, read_payload, save_checkpoint, verify_digest
+from .models.init import initial_stage_state
+from .models.layout import group_specs, model_specs, stage_specs
+from .parallel.dp import GradientReducer
+from .parallel.pp import PipelineRuntime
+from .parallel.tp import TensorParallelStage, local_slice
+from .planner.dp import DPAssignment
+from .reference import digest_tensors, token_stream
+
+FIELDS = ("param", "exp_avg", "exp_avg_sq")
+
+
+class ReshardError(RuntimeError):
+    """State could not be recovered intact (stop code ``state_mismatch``)."""
+
+
+@dataclass
+class TrainingGroups:
+    """The process groups one rank holds under one plan (``None`` = not a member)."""
+
+    world: object = None
+    tp: object = None
+    hops: dict = field(default_factory=dict)
+    executor: object = None
+    reduce: dict = field(default_factory=dict)
+    live: object = None
+
+
+# --- reading the plan -----------------------------------------------------------------
+
+
+def stage_of(plan, rank):
+    for s in plan.stages:
+        if rank in s.tp_members:
+            return s
+    return None
+
+
+def replica_stages(plan, replica):
+    return sorted((s for s in plan.stages if s.replica_id == replica), key=lambda s: s.stage_id)
+
+
+def stage_ends(plan, stage) -> tuple[bool, bool]:
+    ends = replica_stages(plan, stage.replica_id)
+    return stage.stage_id == ends[0].stage_id, stage.stage_id == ends[-1].stage_id
+
+
+def stage_layout(plan, stage) -> dict[str, int | None]:
+    first, last = stage_ends(plan, stage)
+    return {s.name: s.shard_dim for s in stage_specs(plan.config, range(*stage.layer_range), first, last)}
+
+
+def route_names(config, route) -> dict[str, int | None]:
+    return {s.name: s.shard_dim for s in group_specs(config, route.layer, route.boundary)}
+
+
+def routes_for(plan, rank) -> tuple:
+    return tuple(r for r in plan.state_routes if rank in r.target_ranks)
+
+
+def acquire_layout(plan, rank) -> dict[str, int | None]:
+    out: dict[str, int | None] = {}
+    for r in routes_for(plan, rank):
+        out.update(route_names(plan.config, r))
+    return out
+
+
+def dp_assignment(plan) -> DPAssignment:
+    return DPAssignment(step=plan.step, failure_signature=plan.failed_ranks, placements=plan.placements)
+
+
+def _shape_of(config) -> dict[str, tuple]:
+    return {s.name: s.shape for s in model_specs(config)}
+
+
+# --- a rank's state under one plan -------------------------------------------------------
+
+
+class PlannedRun:
+    """This rank's stage and 1F1B runtime under ``plan``; ``cursor`` = completed steps."""
+
+    def __init__(self, plan, *, rank, local_state, moments, groups: TrainingGroups, device, cursor, pin=False):
+        sp = stage_of(plan, rank)
+        first, last = stage_ends(plan, sp)
+        self.plan = plan
+        self.rank = rank
+        self.device = torch.device("cpu") if device is None else torch.device(device)
+        self.stage = TensorParallelStage(
+            plan.config, layer_ids=range(*sp.layer_range), is_first=first, is_last=last,
+            local_state=local_state, group=groups.tp, device=self.device, moments=moments,
+        )
+        reducer = GradientReducer(plan, rank, groups=groups.reduce, executor_group=groups.executor, replica_id=sp.replica_id)
+        needs_reduce = bool(reducer.topology.dp_groups or reducer.topology.tied_groups or not reducer.topology.homogeneous
+                            or self.stage.sp)
+        self.runtime = PipelineRuntime(
+            self.stage, rank=rank, replica_id=sp.replica_id, assignment=dp_assignment(plan),
+            boundary_groups=groups.hops, reducer=reducer if needs_reduce else None,
+        )
+        self.batches = token_stream(plan.config, pin=pin and self.device.type == "cuda")
+        self.cursor = cursor
+
+    def step(self):
+        loss = self.runtime.train_step(self.batches[self.cursor])
+        self.cursor += 1
+        return loss
+
+    def local_state(self) -> dict:
+        """``{name: {shard_index, shard_count, param, exp_avg, exp_avg_sq, step}}``."""
+        st = self.stage
+        step = torch.tensor(float(st.flat.step))
+        out = {}
+        for name, (view, _d) in st.local_shards().items():
+            entry = {"shard_index": st.tp_rank, "shard_count": st.tp_size, "param": view}
+            if st.flat.step > 0:
+                entry.update(st.moment_views(name))
+                entry["step"] = step
+            out[name] = entry
+        return out
+
+
+def initial_run(plan, *, rank, groups: TrainingGroups, device=None, pin=False):
+    """The run a rank starts with: the seeded initial weights cut to its stage and shard."""
+    sp = stage_of(plan, rank)
+    if sp is None:
+        return None
+    first, last = stage_ends(plan, sp)
+    full = initial_stage_state(plan.config, range(*sp.layer_range), first, last, device=device or "cpu")
+    idx = sp.tp_members.index(rank)
+    local = {
+        s.name: local_slice(full[s.name], s.shard_dim, idx, sp.tp_degree)
+        for s in stage_specs(plan.config, range(*sp.layer_range), first, last)
+    }
+    return PlannedRun(plan, rank=rank, local_state=local, moments={}, groups=groups, device=device, cursor=0, pin=pin)
+
+
+# --- gathering the full logical state ---------------------------------------------------
+
+
+def _canonical_holders(plan) -> dict[str, object]:
+    """For each logical name, the one stage whose shards form its canonical copy."""
+    out: dict[str, object] = {}
+    for s in plan.stages:
+        for name in stage_layout(plan, s):
+            out.setdefault(name, s)
+    return out
+
+
+def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems: int = 32 * 1024 * 1024):
+    """Assemble ``{name: {param, exp_avg, exp_avg_sq, step}}`` on plan rank ``dst``.
+
+    Every rank of ``group`` (the executor group) calls this; each element is contributed
+    by exactly one rank of the name's canonical holder stage and summed, so the result is
+    exact. ``dst=None`` makes every rank receive it. Returns ``None`` elsewhere.
+    """
+    config = plan.config
+    holders = _canonical_holders(plan)
+    shapes = _shape_of(config)
+    local = {} if run is None else run.local_state()
+    step = 0 if run is None else run.stage.flat.step
+    me = None if run is None else run.rank
+    names = [s.name for s in model_specs(config)]
+    out: dict[str, dict] = {n: {} for n in names}
+    dst_group_rank = None if dst is None else plan.active_ranks.index(dst)
+    want = dst is None or me == dst
+
+    def numel(shape):
+        n = 1
+        for x in shape:
+            n *= x
+        return n
+
+    buckets, cur, size = [], [], 0
+    for n in names:
+        cur.append(n)
+        size += numel(shapes[n]) * len(FIELDS)
+        if size >= bucket_elems:
+            buckets.append(cur)
+            cur, size = [], 0
+    if cur:
+        buckets.append(cur)
+
+    for bucket in buckets:
+        total = sum(numel(shapes[n]) for n in bucket) * len(FIELDS)
+        buf = torch.zeros(total, dtype=torch.float32, device=device)
+        off = 0
+        for n in bucket:
+            k = numel(shapes[n])
+            holder = holders[n]
+            entry = local.get(n)
+            for f in FIELDS:
+                if entry is not None and me in holder.tp_members and f in entry:
+                    idx = holder.tp_members.index(me)
+                    full = buf[off: off + k].view(shapes[n])
+                    dim = dict(stage_layout(plan, holder))[n]
+                    if dim is None:
+                        if idx == 0:
+                            full.copy_(entry[f])
+                    else:
+                        torch.chunk(full, holder.tp_degree, dim=dim)[idx].copy_(entry[f])
+                off += k
+        if dst is None:
+            dist.all_reduce(buf, group=group)
+        else:
+            dist.reduce(buf, dst=dist.get_global_rank(group, dst_group_rank), group=group)
+        if want:
+            off = 0
+            for n in bucket:
+                k = numel(shapes[n])
+                for f in FIELDS:
+                    out[n][f] = buf[off: off + k].view(shapes[n]).cpu()
+                    off += k
+    if not want:
+        return None
+    step_t = torch.tensor(float(step))
+    full_state = {}
+    for n in names:
+        entry = {"param": out[n]["param"]}
+        if step > 0:
+            entry.update(exp_avg=out[n]["exp_avg"], exp_avg_sq=out[n]["exp_avg_sq"], step=step_t.clone())
+        full_state[n] = entry
+    return full_state
+
+
+def commit_checkpoint(run, path, *, plan, groups: TrainingGroups, writer: bool, cursor: int, device=None):
+    """Safe-point step 2: gather every shard and atomically write the one checkpoint."""
+    if groups.executor is None:
+        return
+    dst = plan.active_ranks[0]
+    full = gather_full_state(run, plan, group=groups.executor, dst=dst, device=device or "cpu")
+    if writer:
+        save_checkpoint(path, plan.config, full, completed_steps=cursor, plan_version=plan.version)
+
+
+def logical_digest(full) -> str:
+    return digest_tensors(sorted((f"{n}.{k}", t) for n, fs in full.items() for k, t in fs.items()))
+
+
+# --- the single recovery path ------------------------------------------------------------
+
+
+def _route_transfer(config, route, local, rank, *, group, device):
+    """Execute one peer route; returns this rank's new shards if it is a target."""
+    specs = group_specs(config, route.layer, route.boundary)
+    sizes = []
+    for s in specs:
+        n = 1
+        for x in s.shape:
+            n *= x
+        sizes.append(n)
+    per_field = sum(sizes)
+    buf = torch.zeros(per_field * len(FIELDS) + 1, dtype=torch.float32, device=device)
+    if rank in route.donor_ranks:
+        idx = route.donor_ranks.index(rank)
+        for fi, f in enumerate(FIELDS):
+            off = fi * per_field
+            for s, k in zip(specs, sizes):
+                entry = local.get(s.name)
+                if entry is None or f not in entry:
+                    raise ReshardError(f"donor rank {rank} does not hold {s.name}.{f}")
+                full = buf[off: off + k].view(s.shape)
+                if s.shard_dim is None:
+                    if idx == 0:
+                        full.copy_(entry[f])
+                else:
+                    torch.chunk(full, route.donor_degree, dim=s.shard_dim)[idx].copy_(entry[f])
+                off += k
+        if idx == 0:
+            buf[-1] = float(local[specs[0].name]["step"])
+    dist.all_reduce(buf, group=group)
+    if rank not in route.target_ranks:
+        return {}
+    t = route.target_ranks.index(rank)
+    out = {}
+    step = buf[-1].detach().cpu().clone()
+    for s, k in zip(specs, sizes):
+        out[s.name] = {}
+    for fi, f in enumerate(FIELDS):
+        off = fi * per_field
+        for s, k in zip(specs, sizes):
+            full = buf[off: off + k].view(s.shape)
+            out[s.name][f] = local_slice(full, s.shard_dim, t, route.target_degree)
+            off += k
+    for s in specs:
+        out[s.name]["step"] = step.clone()
+    return out
+
+
+def _anchor_slices(config, route, anchor, rank):
+    t = route.target_ranks.index(rank)
+    out = {}
+    for s in group_specs(config, route.layer, route.boundary):
+        entry = anchor.get(s.name)
+        if entry is None:
+            raise ReshardError(f"logical tensor {s.name} unavailable from peers and checkpoint")
+        out[s.name] = {f: local_slice(entry[f], s.shard_dim, t, route.target_degree) for f in FIELDS if f in entry}
+        if "step" in entry:
+            out[s.name]["step"] = entry["step"].clone()
+    return out
+
+
+def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: TrainingGroups, device=None, pin=False):
+    """Safe-point step 7: execute ``plan``'s state routes; returns ``(run, state digest)``.
+
+    Every surviving rank calls this (the idle ones too: their shards may be donors).
+    """
+    config = plan.config
+    payload = read_payload(checkpoint_path)
+    verify_digest(payload)
+    completed = payload["completed_steps"]
+    anchor = {}
+    for name, param in payload["params"].items():
+        entry = {"param": param}
+        if name in payload["optim"]:
+            entry.update(payload["optim"][name])
+        anchor[name] = entry
+    stage = stage_of(plan, rank)
+    local = {} if run is None else run.local_state()
+    needs_checkpoint = any(r.donor_kind == "checkpoint" for r in plan.state_routes)
+    rollback = completed != cursor and needs_checkpoint
+    tdev = torch.device("cpu") if device is None else torch.device(device)
+
+    acquired: dict[str, dict] = {}
+    if rollback:
+        local = {}
+    for route in plan.state_routes:
+        if route.donor_kind == "checkpoint" or rollback:
+            if rank in route.target_ranks:
+                acquired.update(_anchor_slices(config, route, anchor, rank))
+            continue
+        acquired.update(_route_transfer(config, route, local, rank, group=groups.live, device=tdev))
+
+    new_run = None
+    if stage is not None:
+        owned = stage_layout(plan, stage)
+        idx = stage.tp_members.index(rank)
+        state: dict[str, dict] = {}
+        for name, dim in owned.items():
+            if name in acquired:
+                state[name] = acquired[name]
+            elif rollback:
+                e = anchor[name]
+                state[name] = {f: local_slice(e[f], dim, idx, stage.tp_degree) for f in FIELDS if f in e}
+                if "step" in e:
+                    state[name]["step"] = e["step"]
+            elif name in local:
+                state[name] = local[name]
+            else:
+                raise ReshardError(f"no state route covers {name} for rank {rank}")
+        new_run = PlannedRun(
+            plan, rank=rank, local_state={n: f["param"] for n, f in state.items()},
+            moments={n: f for n, f in state.items() if "exp_avg" in f}, groups=groups, device=device,
+            cursor=completed if (rollback or completed == cursor) else cursor, pin=pin,
+        )
+
+    if completed == cursor or rollback:
+        if new_run is not None:
+            problems = checkpoint_mismatches(new_run, plan=plan, rank=rank, anchor=anchor)
+            if problems:
+                raise ReshardError(f"rank {rank} state differs from the checkpoint: {problems[:5]}")
+        return new_run, payload["digest"]
+    mine = "" if new_run is None else digest_tensors(sorted(
+        (f"{n}.{k}", v) for n, e in new_run.local_state().items() for k, v in e.items() if torch.is_tensor(v)
+    ))
+    gathered = [None] * dist.get_world_size(groups.world)
+    dist.all_gather_object(gathered, (rank, mine), group=groups.world)
+    return new_run, sha256(repr(sorted(gathered)).encode("utf-8")).hexdigest()
+
+
+def checkpoint_mismatches(run, *, plan, rank, anchor) -> list[str]:
+    """Principle A1: every way this rank's state differs from the anchor's slices."""
+    stage = stage_of(plan, rank)
+    if stage is None:
+        return [] if run is None else [f"rank {rank} is placed nowhere but still holds a run"]
+    layout = stage_layout(plan, stage)
+    shards = run.stage.local_shards()
+    if set(shards) != set(layout):
+        return [f"stage holds the wrong names: extra={sorted(set(shards) - set(layout))} "
+                f"missing={sorted(set(layout) - set(shards))}"]
+    idx = stage.tp_members.index(rank)
+    problems = []
+    for name, dim in layout.items():
+        want = anchor[name]
+        if not torch.equal(shards[name][0].detach().cpu(), local_slice(want["param"], dim, idx, stage.tp_degree)):
+            problems.append(f"{name}.param")
+        if "exp_avg" not in want:
+            continue
+        mv = run.stage.moment_views(name)
+        for f in ("exp_avg", "exp_avg_sq"):
+            if not torch.equal(mv[f].detach().cpu(), local_slice(want[f], dim, idx, stage.tp_degree)):
+                problems.append(f"{name}.{f}")
+        if float(run.stage.flat.step) != float(want["step"]):
+            problems.append(f"{name}.step")
+    return problems
+
+
+def recovery_stop_code(error: Exception) -> str | None:
+    if isinstance(error, CheckpointError):
+        return "checkpoint_unusable"
+    if isinstance(error, ReshardError):
+        return "state_mismatch"
+    return None

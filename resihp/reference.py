@@ -1,0 +1,128 @@
+"""Single-process deterministic training run: the numerics oracle.
+
+The token stream is the reference's exactly (``resihp/reference.py:97-103``): one
+``torch.Generator`` seeded with ``config.seed`` draws ``randint(0, V, (B, S))`` per
+iteration, so every rank of a distributed run and this oracle see the same batches. It
+is generated lazily (a 1.3B-parameter run does not keep a thousand batches around).
+
+:class:`ReferenceRun` trains the whole model as one stage at TP degree 1 on one device
+with FP32 master weights -- the same :class:`~resihp.parallel.tp.TensorParallelStage`
+code the distributed runtime uses -- on the full batch in one pass, and records the
+loss plus SHA-256 digests of the parameters and AdamW state after every step.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from hashlib import sha256
+
+import torch
+
+from .config import TrainConfig
+from .models.init import initial_state
+from .parallel.tp import TensorParallelStage
+
+
+class TokenStream:
+    """Batch ``i`` of the fixed, seeded data order (``randint(0, V, (B, S))`` per step)."""
+
+    def __init__(self, vocab_size: int, sequence_length: int, batch_size: int, seed: int, *, pin: bool = False):
+        self.shape = (batch_size, sequence_length)
+        self.vocab_size = vocab_size
+        self.seed = seed
+        self.pin = pin
+        self._gen = torch.Generator().manual_seed(seed)
+        self._next = 0
+        self._cache: dict[int, torch.Tensor] = {}
+
+    def __getitem__(self, index: int) -> torch.Tensor:
+        if index in self._cache:
+            return self._cache[index]
+        if index < self._next:
+            self._gen = torch.Generator().manual_seed(self.seed)
+            self._next = 0
+        batch = None
+        while self._next <= index:
+            batch = torch.randint(0, self.vocab_size, self.shape, generator=self._gen)
+            self._next += 1
+        if self.pin and torch.cuda.is_available():
+            batch = batch.pin_memory()
+        self._cache = {index: batch}
+        return batch
+
+
+def token_stream(config: TrainConfig, *, pin: bool = False) -> TokenStream:
+    return TokenStream(config.vocab_size, config.seq_len, config.batch_size, config.seed, pin=pin)
+
+
+def digest_tensors(items) -> str:
+    """SHA-256 over ``(name, tensor)`` pairs by their exact FP32 bytes."""
+    h = sha256()
+    for name, tensor in items:
+        arr = tensor.detach().cpu().to(torch.float32).contiguous().numpy()
+        h.update(name.encode("utf-8"))
+        h.update(repr(arr.shape).encode("utf-8"))
+        h.update(arr.tobytes())
+    return h.hexdigest()
+
+
+@dataclass(frozen=True)
+class StepRecord:
+    step: int
+    loss: float
+    param_digest: str
+    optim_digest: str
+
+
+class ReferenceRun:
+    """The whole model in one process (see the module docstring)."""
+
+    def __init__(self, config: TrainConfig, *, device="cpu", full_state=None, moments=None, cursor: int = 0):
+        if config.seq_len < 2:
+            raise ValueError("sequence_length must be at least 2 for next-token loss")
+        self.config = config
+        self.device = torch.device(device)
+        state = initial_state(config, device=self.device) if full_state is None else full_state
+        self.stage = TensorParallelStage(
+            config, layer_ids=range(config.num_layers), is_first=True, is_last=True,
+            local_state=state, group=None, device=self.device, moments=moments,
+        )
+        self.batches = token_stream(config)
+        self.cursor = cursor
+
+    def step(self) -> StepRecord:
+        tokens = self.batches[self.cursor].to(self.device)
+        stage = self.stage
+        stage.zero_grad()
+        b, s = tokens.shape
+        loss = stage.forward(tokens=tokens, loss_scale=1.0 / (b * (s - 1)))
+        loss.backward()
+        stage.optimizer_step()
+        record = StepRecord(
+            step=self.cursor,
+            loss=float(loss.detach()),
+            param_digest=digest_tensors(sorted(stage.logical_state_dict().items())),
+            optim_digest=digest_tensors(sorted(
+                (f"{n}.{k}", v) for n in stage.logical_state_dict() for k, v in stage.moment_views(n).items()
+            )),
+        )
+        self.cursor += 1
+        return record
+
+    def full_state(self) -> dict[str, dict[str, torch.Tensor]]:
+        """``{name: {param, exp_avg, exp_avg_sq, step}}`` (the checkpoint's logical form)."""
+        out = {}
+        step = torch.tensor(float(self.stage.flat.step))
+        for name, (view, _d) in self.stage.local_shards().items():
+            entry = {"param": view.detach().clone()}
+            if self.stage.flat.step > 0:
+                mv = self.stage.moment_views(name)
+                entry.update({k: v.detach().clone() for k, v in mv.items()})
+                entry["step"] = step.clone()
+            out[name] = entry
+        return out
+
+
+def run_reference(config: TrainConfig, *, device="cpu") -> list[StepRecord]:
+    run = ReferenceRun(config, device=device)
+    return [run.step() for _ in range(config.iterations)]

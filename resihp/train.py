@@ -1,0 +1,129 @@
+"""One rank's training process: the fail-stop control loop, or a config echo.
+
+``python -m resihp.train --config train.json --failures failures.json`` is what the
+launcher spawns per rank (reference ``resihp/train.py:75-188``). Without ``RANK`` in
+the environment it only echoes the two files as JSON.
+
+Each iteration: train (1F1B over the plan), commit the logical checkpoint (every
+``checkpoint_every`` iterations; every iteration by default, as the reference), then
+-- if the schedule names this rank -- ``SIGKILL`` itself, then rendezvous at the
+boundary; a boundary that comes back short triggers exactly one safe point. The JSON
+lines on stdout are the reference's ``{"acceptance": ...}`` / ``{"stopped": ...}``
+plus ``{"step": ...}`` per trained iteration on a last-stage rank and
+``{"recovery": ...}`` per fail-stop.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import time
+from pathlib import Path
+
+from .config import load_config
+
+CHECKPOINT_PATH = Path(os.environ.get("RESIHP_CHECKPOINT", "checkpoint.pt"))
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description="resihp training worker")
+    p.add_argument("--config", required=True, type=Path)
+    p.add_argument("--failures", required=True, type=Path)
+    return p.parse_args(argv)
+
+
+def select_device():
+    import torch
+
+    if not torch.cuda.is_available():
+        return torch.device("cpu")
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def fail_stop(schedule, rank: int, iteration: int) -> None:
+    """``SIGKILL`` this process if the schedule fails ``rank`` after ``iteration``."""
+    import signal
+
+    if schedule.get(iteration) == rank:
+        os.kill(os.getpid(), signal.SIGKILL)
+
+
+def _emit(obj) -> None:
+    print(json.dumps(obj, ensure_ascii=False), flush=True)
+
+
+def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
+    import torch
+
+    from .control import ConsistentStop, ControlPlane
+    from .plan import build_plan
+    from .recovery import initial_run
+
+    config = loaded.train
+    schedule = {e.after_iteration: e.failed_rank for e in loaded.failures}
+    device = select_device()
+    control = ControlPlane.initialize(memory_budget=config.memory_budget_bytes)
+    plan = build_plan(
+        config, step=0, version=0, memory_budget=config.memory_budget_bytes,
+        vocab_size=config.vocab_size, sequence_length=config.seq_len,
+    )
+    groups = control.build_training_groups(plan)
+    control.attach_run(initial_run(plan, rank=control.rank, groups=groups, device=device),
+                       checkpoint_path=checkpoint_path, device=device)
+    failed: tuple[int, ...] = ()
+    trained: list[int] = []
+    versions = [plan.version]
+    digests = [plan.digest]
+    tokens_per_step = config.batch_size * config.seq_len
+    try:
+        for step in range(config.iterations):
+            iteration = step + 1
+            if control.training_run is not None:
+                trained.append(iteration)
+            t0 = time.perf_counter()
+            loss = control.training_step()
+            if device.type == "cuda":
+                torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            if loss is not None:
+                _emit({"step": iteration, "rank": control.rank, "loss": loss, "plan_version": plan.version,
+                       "step_s": dt, "tokens_per_s": tokens_per_step / dt if dt > 0 else None})
+            if iteration % config.checkpoint_every == 0:
+                control.commit_checkpoint(plan, cursor=iteration)
+            fail_stop(schedule, control.rank, iteration)
+            t_fail = time.perf_counter()
+            lost = control.observe()
+            if lost:
+                plan, failed = control.safe_point(config, plan, failed, lost, next_step=iteration)
+                versions.append(plan.version)
+                digests.append(plan.digest)
+                _emit({"recovery": {"rank": control.rank, "event": len(versions) - 1, "lost": list(lost),
+                                    "plan_version": plan.version, "seconds": time.perf_counter() - t_fail,
+                                    "phases": control.last_recovery}})
+    except ConsistentStop as stop:
+        _emit({"stopped": stop.reason.code, "reason": stop.reason.message})
+        control.shutdown()
+        return None
+    _emit({"acceptance": {
+        "rank": control.rank, "device": device.type, "training_backend": control.training_backend,
+        "trained_iterations": trained, "plan_versions": versions, "plan_digests": digests,
+        "failed_ranks": list(failed), "world_members": list(control.members),
+    }})
+    control.shutdown()
+    return plan
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if "RANK" in os.environ:
+        run_distributed(load_config(args.config, args.failures))
+        return
+    config = json.loads(args.config.read_text(encoding="utf-8"))
+    failures = json.loads(args.failures.read_text(encoding="utf-8"))
+    print(json.dumps({"config": config, "failures": failures}, ensure_ascii=False, sort_keys=True))
+
+
+if __name__ == "__main__":
+    main()
