@@ -1,0 +1,308 @@
+#!/usr/bin/env python
+"""Headline benchmark: training tokens/s of the BASELINE config-2 model on N B200s.
+
+Model: Llama-style 1.3B (24 layers, hidden 2048, 16 heads MHA, SwiGLU 5504, vocab 32000),
+bf16 compute with FP32 master weights and AdamW; sequence 2048, micro-batch 2, global
+batch 64 sequences of synthetic seeded tokens, random normal(0, 0.02) init. Layout per
+N (sub-layouts of config 2's TP2 x PP2 x DP2; total work fixed, so scaling is strong):
+1 -> TP1, 2 -> TP2, 4 -> TP2 x PP2, 8 -> TP2 x PP2 x DP2 (sequence parallel when TP > 1).
+
+``value`` is device-timed: CUDA events around exactly K steps, barrier + synchronize on
+both sides, max over ranks. ``e2e`` is the same K steps through the public API
+(``PlannedRun.step``: per micro-batch host-to-device copies of the tokens from pinned
+memory, the loss read back to the host) timed on the host clock, max over ranks.
+Every input (weights, activations, logits) is far larger than the 126 MB L2.
+
+``--impl reference`` runs the unmodified reference from ``baseline/_ref`` through its
+own public API (ControlPlane groups, ``initial_run``, ``PlannedRun.step``) at the
+closest shape it can express (GPT-2 blocks, FFN 4d, FP32), printing the same line.
+
+    python bench.py --gpus N --steps K --warmup W [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import socket
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; fail-stop recovery seconds"
+MODEL = dict(model_dim=2048, num_layers=24, num_heads=16, ffn_dim=5504, vocab_size=32000, seq_len=2048)
+GLOBAL_BATCH = 64
+MICRO_BATCH = 2
+LAYOUTS = {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 2, 2)}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["resihp", "reference"], default="resihp")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+        threading.Thread(target=self._read, daemon=True).start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 9:
+                self.rows.append(parts)
+
+    def stop(self, visible):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        rows = [r for r in self.rows if visible is None or r[0] in visible]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def _env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def _store(rank, world):
+    from torch.distributed import TCPStore
+
+    if world == 1 and "MASTER_ADDR" not in os.environ:
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        return TCPStore("127.0.0.1", port, is_master=True, wait_for_workers=False)
+    host = os.environ.get("MASTER_ADDR", "127.0.0.1")
+    port = int(os.environ.get("MASTER_PORT", "29500")) + 17
+    return TCPStore(host, port, world_size=world, is_master=rank == 0, wait_for_workers=False)
+
+
+def _visible(local, world):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = vis.split(",")
+        return set(ids[:world]) if world > 1 else {ids[local] if local < len(ids) else ids[0]}
+    return {str(i) for i in range(world)} if world > 1 else {str(local)}
+
+
+def _timed(run_step, warmup, steps, barrier, reduce_max, local, world):
+    import torch
+
+    for _ in range(warmup):
+        run_step()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler()
+    if local == 0:
+        sampler.start()
+        time.sleep(0.5)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run_step()
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop(_visible(local, world)) if local == 0 else None
+    device_s = start.elapsed_time(end) / 1000.0
+    return reduce_max(device_s), reduce_max(wall), clocks
+
+
+def run_ours(args):
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.ops import _ext, check_device_errors
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run
+
+    rank, world, local = _env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    tp, pp, dp = LAYOUTS[world]
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    config = TrainConfig(
+        **MODEL, num_kv_heads=None, batch_size=GLOBAL_BATCH, micro_batch_size=MICRO_BATCH, seed=1,
+        tp=tp, pp=pp, dp=dp, iterations=args.warmup + args.steps, arch="llama", dtype="bf16",
+        sequence_parallel=tp > 1, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95, weight_decay=0.1,
+    )
+    cp = ControlPlane(rank, range(world), _store(rank, world), "nccl")
+    cp.form_world(range(world), epoch=0)
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    run = initial_run(plan, rank=rank, groups=groups, device=device, pin=True)
+    h2d_bytes = 0
+    d2h_bytes = 0
+    if run is not None:
+        mbs = len(run.runtime.micro_batches)
+        if run.stage.is_first or run.stage.is_last:
+            h2d_bytes = mbs * MICRO_BATCH * config.seq_len * 8
+        d2h_bytes = 4 if run.stage.is_last else 0
+
+    def step():
+        return run.step() if run is not None else None
+
+    def barrier():
+        dist.barrier(group=cp.world_group)
+
+    def reduce_max(x):
+        t = torch.tensor([float(x)])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cp.world_group)
+        return float(t.item())
+
+    counter = _ext.launch_counter()
+    for _ in range(args.warmup):
+        step()
+    counter.launches = 0
+    counter.enabled = True
+    device_s, wall_s, clocks = _timed(step, 0, args.steps, barrier, reduce_max, local, world)
+    counter.enabled = False
+    launches = int(reduce_max(counter.launches))
+    check_device_errors(local)
+    bytes_in = torch.tensor([float(h2d_bytes), float(d2h_bytes)])
+    dist.all_reduce(bytes_in, group=cp.world_group)
+    tokens = args.steps * GLOBAL_BATCH * config.seq_len
+    value = tokens / device_s
+    e2e = tokens / wall_s
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * device_s / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded uniform tokens), random-init weights",
+            "config": {"model": "llama-1.3b (24L, d2048, 16H MHA, SwiGLU 5504, V32000)", "global_batch": GLOBAL_BATCH,
+                       "micro_batch": MICRO_BATCH, "seq_len": config.seq_len,
+                       "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if tp > 1 else ""),
+                       "l2": "inputs larger than L2 (weights/activations >> 126 MB)"},
+            "clocks": clocks,
+            "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(bytes_in[0]),
+                    "d2h_bytes_per_step": int(bytes_in[1])},
+            "gpu_launches": launches,
+            "impl": "resihp",
+        }
+        print(json.dumps(line), flush=True)
+    del run
+    cp.destroy_training_groups()
+    dist.barrier(group=cp.world_group)
+    dist.destroy_process_group()
+
+
+def run_reference(args):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "resihp")):
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}))
+        return
+    sys.path = [ref] + [p for p in sys.path if os.path.abspath(p or ".") != ROOT]
+    import torch
+    import torch.distributed as dist
+
+    import resihp
+    assert os.path.abspath(resihp.__file__).startswith(ref), resihp.__file__
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run
+
+    rank, world, local = _env()
+    tp, pp, dp = LAYOUTS[world]
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    config = TrainConfig(model_dim=MODEL["model_dim"], num_layers=MODEL["num_layers"], num_heads=MODEL["num_heads"],
+                         batch_size=GLOBAL_BATCH, micro_batch_size=MICRO_BATCH, seed=1, tp=tp, pp=pp, dp=dp,
+                         iterations=args.warmup + args.steps)
+    cp = ControlPlane(rank, range(world), _store(rank, world), "nccl", vocab_size=MODEL["vocab_size"],
+                      sequence_length=MODEL["seq_len"])
+    cp.form_world(range(world), epoch=0)
+    plan = build_plan(config, step=0, version=0, vocab_size=MODEL["vocab_size"], sequence_length=MODEL["seq_len"])
+    cp.build_training_groups(plan)
+    run = initial_run(plan, rank=rank, vocab_size=MODEL["vocab_size"], sequence_length=MODEL["seq_len"],
+                      tp_group=cp.tp_group, executor_group=cp.executor_group, boundary_groups=cp.boundary_groups,
+                      device=device)
+
+    def step():
+        return run.step() if run is not None else None
+
+    def barrier():
+        dist.barrier(group=cp.world_group)
+
+    def reduce_max(x):
+        t = torch.tensor([float(x)])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cp.world_group)
+        return float(t.item())
+
+    device_s, wall_s, clocks = _timed(step, args.warmup, args.steps, barrier, reduce_max, local, world)
+    tokens = args.steps * GLOBAL_BATCH * MODEL["seq_len"]
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(tokens / device_s, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * device_s / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded uniform tokens), random-init weights",
+            "config": {"model": "gpt2-arch 1.3b (24L, d2048, 16H, FFN 4d, V32000): closest reference shape",
+                       "global_batch": GLOBAL_BATCH, "micro_batch": MICRO_BATCH, "seq_len": MODEL["seq_len"],
+                       "parallelism": f"tp{tp}-pp{pp}-dp{dp}", "l2": "inputs larger than L2"},
+            "clocks": clocks,
+            "e2e": {"value": round(tokens / wall_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": None,
+                    "d2h_bytes_per_step": None},
+            "impl": "reference",
+        }), flush=True)
+    cp.shutdown()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

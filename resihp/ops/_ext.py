@@ -35,16 +35,58 @@ def _load():
     return _module
 
 
+# Kernels each extension entry point launches (for the benchmark's launch count).
+KERNELS_PER_CALL = {
+    "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "rope": 1, "swiglu_fwd": 1, "swiglu_bwd": 1,
+    "adamw": 1, "embedding_fwd": 1, "embedding_bwd": 1, "xent_stats": 1, "xent_grad": 1,
+    "attn_fwd": 1, "attn_bwd": 3,
+}
+
+
+class _Counting:
+    """Proxy over the extension module that counts kernel launches per entry point."""
+
+    def __init__(self, module):
+        self._module = module
+        self.launches = 0
+        self.enabled = False
+
+    def __getattr__(self, name):
+        fn = getattr(self._module, name)
+        per = KERNELS_PER_CALL.get(name)
+        if per is None:
+            return fn
+
+        def counted(*args, **kwargs):
+            if self.enabled:
+                self.launches += per
+            return fn(*args, **kwargs)
+
+        return counted
+
+
+_counting = None
+
+
+def launch_counter() -> "_Counting":
+    """The counting proxy; set ``.enabled`` and read ``.launches``."""
+    require()
+    return _counting
+
+
 def available() -> bool:
     return _load() is not None
 
 
 def require():
     """The loaded extension module; raises if it cannot be loaded."""
+    global _counting
     module = _load()
     if module is None:
         raise RuntimeError(f"resihp CUDA extension unavailable: {_error}")
-    return module
+    if _counting is None:
+        _counting = _Counting(module)
+    return _counting
 
 
 def library_path() -> str:
