@@ -214,3 +214,83 @@ void rmsnorm_bwd(const void* dy, const void* s, const void* w, const float* rstd
 }
 
 }  // namespace resihp
+
+// ---- allocation-free entry point (declared in no_alloc.h) ------------------------------
+#include <mutex>
+
+#include "no_alloc.h"
+
+// Scratch of the allocation-free entry point: the per-(block, row slot) fp32 partial
+// sums of the weight gradient, one array per device that loads this library.
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[RESIHP_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::mutex g_scratch_mutex;
+
+// Device address of the scratch array on the current device, looked up once per device
+// with that device current (host code only sees a stand-in for the symbol).
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_rmsnorm_bwd_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+bool width_supported(int d) {
+  if (d <= 0 || d % 8 != 0 || d / 8 > 1024) return false;
+  const int lanes = d / 8;
+  return lanes >= 32 ? lanes % 32 == 0 : 32 % lanes == 0;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int resihp_rmsnorm_bwd_noalloc(
+    const void* dy, const void* s, const void* w, const float* rstd, const void* dres, void* ds, float* dw,
+    int accumulate, int rows, int d, cudaStream_t stream) {
+  using namespace resihp;
+  if (dy == nullptr || s == nullptr || w == nullptr || rstd == nullptr || ds == nullptr || dw == nullptr || rows < 1 ||
+      !width_supported(d))
+    return RESIHP_NOALLOC_BAD_ARGUMENT;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  // Same launch shape as the allocating entry point (rmsnorm_bwd), so results agree.
+  const int block = norm_block(d);
+  const int rows_per_block = block / (d / 8);
+  const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * sms);
+  const long long need = static_cast<long long>(grid) * rows_per_block * d;
+  if (need > RESIHP_NOALLOC_SCRATCH_FLOATS) return RESIHP_NOALLOC_TOO_LARGE;
+  float* partial = nullptr;
+  if (noalloc_scratch(&partial) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  rmsnorm_bwd_kernel<<<grid, block, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
+      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
+      static_cast<__nv_bfloat16*>(ds), partial, rows, d);
+  if (cudaGetLastError() != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  column_sum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(partial, grid * rows_per_block, d, dw, accumulate);
+  if (cudaGetLastError() != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  return RESIHP_NOALLOC_OK;
+}
+
+extern "C" __attribute__((visibility("default"))) const char* resihp_noalloc_strerror(int code) {
+  switch (code) {
+    case RESIHP_NOALLOC_OK: return "ok";
+    case RESIHP_NOALLOC_BAD_ARGUMENT: return "bad argument: null pointer, rows < 1, or unsupported width d";
+    case RESIHP_NOALLOC_TOO_LARGE:
+      return "scratch need exceeds the built-in 16 MiB (RESIHP_NOALLOC_SCRATCH_FLOATS) scratch array";
+    case RESIHP_NOALLOC_CUDA_ERROR: return "a CUDA runtime call or kernel launch failed";
+    default: return "unknown error code";
+  }
+}
