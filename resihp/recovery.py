@@ -430,3 +430,27 @@ def recovery_stop_code(error: Exception) -> str | None:
     if isinstance(error, ReshardError):
         return "state_mismatch"
     return None
+
+
+def run_from_anchor(plan, *, rank, anchor, completed, groups: TrainingGroups, device=None, pin=False):
+    """A fresh run of ``plan`` whose state is the checkpoint ``anchor`` (cursor ``completed``).
+
+    The uninterrupted re-run that a recovered run is compared against: the same plan, the
+    same state, the same data cursor, started from scratch.
+    """
+    stage = stage_of(plan, rank)
+    if stage is None:
+        return None
+    idx = stage.tp_members.index(rank)
+    params, moments = {}, {}
+    for name, dim in stage_layout(plan, stage).items():
+        e = anchor[name]
+        params[name] = local_slice(e["param"], dim, idx, stage.tp_degree)
+        if "exp_avg" in e:
+            moments[name] = {
+                "exp_avg": local_slice(e["exp_avg"], dim, idx, stage.tp_degree),
+                "exp_avg_sq": local_slice(e["exp_avg_sq"], dim, idx, stage.tp_degree),
+                "step": e["step"],
+            }
+    return PlannedRun(plan, rank=rank, local_state=params, moments=moments, groups=groups, device=device,
+                      cursor=completed, pin=pin)

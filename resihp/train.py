@@ -51,7 +51,11 @@ def fail_stop(schedule, rank: int, iteration: int) -> None:
 
 
 def _emit(obj) -> None:
-    print(json.dumps(obj, ensure_ascii=False), flush=True)
+    """One JSON line in a single write, so lines of concurrent ranks never interleave."""
+    import sys
+
+    sys.stdout.write(json.dumps(obj, ensure_ascii=False) + "\n")
+    sys.stdout.flush()
 
 
 def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):

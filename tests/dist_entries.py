@@ -1,0 +1,128 @@
+"""Process entry points of the distributed CPU/Gloo gates (importable by spawned children)."""
+
+import json
+import os
+import sys
+from pathlib import Path
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def _setup(env):
+    os.environ.update(env)
+    import torch
+
+    torch.set_num_threads(1)
+
+
+def train_entry(rank, env, config_dict, steps, out_dir, dump_state):
+    """Train ``steps`` iterations of one plan; write losses (+ final shards) per rank."""
+    _setup(env)
+    import torch
+
+    from harness import write_result
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run
+
+    config = TrainConfig(**config_dict)
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    run = initial_run(plan, rank=rank, groups=groups)
+    losses = []
+    for _ in range(steps):
+        losses.append(run.step() if run is not None else None)
+    result = {"rank": rank, "losses": losses, "schedule": None if run is None else run.runtime.schedule}
+    if dump_state and run is not None:
+        shards = {n: t.detach().tolist() for n, (t, _d) in run.stage.local_shards().items()}
+        result.update(shards=shards, tp_rank=run.stage.tp_rank, tp_size=run.stage.tp_size)
+    write_result(out_dir, rank, result)
+    cp.shutdown()
+
+
+def failstop_entry(rank, env, config_dict, failures, out_dir):
+    """The worker loop with a failure schedule; records per-iteration losses and plans."""
+    _setup(env)
+    import torch
+
+    from harness import write_result
+    from resihp.config import TrainConfig
+    from resihp.control import ConsistentStop, ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run
+    from resihp.train import fail_stop
+
+    config = TrainConfig(**config_dict)
+    schedule = {int(k): v for k, v in failures.items()}
+    os.chdir(out_dir)
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=Path(out_dir, "checkpoint.pt"))
+    record = {"rank": rank, "losses": {}, "plans": [plan.digest], "stopped": None, "recoveries": []}
+    failed = ()
+    try:
+        for step in range(config.iterations):
+            it = step + 1
+            loss = cp.training_step()
+            if loss is not None:
+                record["losses"][str(it)] = loss
+            cp.commit_checkpoint(plan, cursor=it)
+            write_result(out_dir, rank, record)
+            fail_stop(schedule, rank, it)
+            lost = cp.observe()
+            if lost:
+                import shutil
+
+                # the lowest survivor keeps the checkpoint this failure resumes from
+                if rank == min(r for r in cp.members if r not in lost):
+                    shutil.copy(Path(out_dir, "checkpoint.pt"), Path(out_dir, f"anchor_{it}.pt"))
+                plan, failed = cp.safe_point(config, plan, failed, lost, next_step=it)
+                record["plans"].append(plan.digest)
+                record["recoveries"].append({"after": it, "lost": list(lost), "phases": cp.last_recovery})
+    except ConsistentStop as stop:
+        record["stopped"] = stop.reason.code
+        write_result(out_dir, rank, record)
+        cp.shutdown()
+        return
+    write_result(out_dir, rank, record)
+    cp.shutdown()
+
+
+def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir):
+    """Uninterrupted re-run of the post-failure plan from the anchor the failure resumed from."""
+    _setup(env)
+    from harness import write_result
+    from resihp.checkpoint import load_anchor
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import run_from_anchor
+
+    config = TrainConfig(**config_dict)
+    survivors = [r for r in range(config.world_size) if r not in failed]
+    plan_rank = survivors[rank]
+    v0 = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    plan = build_plan(config, step=after, version=1, failed_ranks=failed, previous=v0,
+                      vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    import torch.distributed as dist
+
+    from resihp import membership
+
+    store = membership.connect(os.environ[membership.HOST_ENV], os.environ[membership.PORT_ENV])
+    cp = ControlPlane(plan_rank, survivors, store, "gloo")
+    cp.form_world(survivors, epoch=0)
+    groups = cp.build_training_groups(plan)
+    anchor, completed = load_anchor(anchor_path)
+    run = run_from_anchor(plan, rank=plan_rank, anchor=anchor, completed=completed, groups=groups)
+    losses = {}
+    for it in range(after + 1, config.iterations + 1):
+        loss = run.step() if run is not None else None
+        if loss is not None:
+            losses[str(it)] = loss
+    write_result(out_dir, rank, {"rank": plan_rank, "losses": losses, "plan": plan.digest})
+    cp.shutdown()

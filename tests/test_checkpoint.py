@@ -1,0 +1,82 @@
+"""Checkpoint atomicity, validation and cross-compatibility with the reference."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from resihp.checkpoint import CheckpointError, load_anchor, load_checkpoint, save_checkpoint
+from resihp.config import TrainConfig
+from resihp.reference import ReferenceRun
+
+C = TrainConfig(model_dim=16, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=3, tp=1, pp=1, dp=1,
+                iterations=2, vocab_size=32, seq_len=8)
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _saved(tmp_path, steps=1):
+    run = ReferenceRun(C)
+    for _ in range(steps):
+        run.step()
+    path = tmp_path / "ck.pt"
+    save_checkpoint(path, C, run.full_state(), completed_steps=run.cursor, plan_version=2)
+    return path, run
+
+
+def test_roundtrip_and_validation(tmp_path):
+    path, run = _saved(tmp_path)
+    anchor, completed, version = load_checkpoint(path, C)
+    assert completed == 1 and version == 2
+    for name, (view, _d) in run.stage.local_shards().items():
+        assert torch.equal(anchor[name]["param"], view)
+
+
+def test_failed_replace_keeps_previous(tmp_path, monkeypatch):
+    path, run = _saved(tmp_path)
+    before = path.read_bytes()
+
+    def boom(*a, **k):
+        raise OSError("disk full")
+
+    monkeypatch.setattr(os, "replace", boom)
+    with pytest.raises(OSError):
+        save_checkpoint(path, C, run.full_state(), completed_steps=5, plan_version=3)
+    assert path.read_bytes() == before
+    assert not (tmp_path / "ck.pt.tmp").exists()
+
+
+def test_each_corruption_is_its_own_root_cause(tmp_path):
+    path, _ = _saved(tmp_path)
+    payload = torch.load(path, weights_only=False)
+    cases = {
+        "format": dict(payload, format_version=9),
+        "identity": dict(payload, identity=dict(payload["identity"], seed=4)),
+        "missing": dict(payload, params={k: v for k, v in list(payload["params"].items())[1:]}),
+        "cursor": dict(payload, completed_steps=7),
+        "digest": dict(payload, params={**payload["params"], "final_norm.weight": payload["params"]["final_norm.weight"] + 1}),
+    }
+    messages = {"format": "format", "identity": "identity", "missing": "missing", "cursor": "cursor", "digest": "digest"}
+    for key, bad in cases.items():
+        torch.save(bad, path)
+        with pytest.raises(CheckpointError, match=messages[key]):
+            load_checkpoint(path, C)
+    os.remove(path)
+    with pytest.raises(CheckpointError, match="missing"):
+        load_anchor(path)
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+def test_reference_reads_our_checkpoint(tmp_path):
+    path, run = _saved(tmp_path, steps=2)
+    code = (
+        "import sys, json; sys.path.insert(0, sys.argv[1])\n"
+        "from resihp.checkpoint import load_anchor\n"
+        "a, c = load_anchor(sys.argv[2]); print(json.dumps([c, sorted(a)]))\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code, REF, str(path)], capture_output=True, text=True, check=True, cwd="/")
+    completed, names = json.loads(out.stdout)
+    assert completed == 2 and names == sorted(run.stage.logical_state_dict())
