@@ -262,6 +262,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 CUtensorMap make_tma_2d_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
   RESIHP_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
   RESIHP_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  // The driver call needs this thread's context current; a thread whose first CUDA work
+  // is this encode (e.g. an autograd worker served from the allocator cache) may not
+  // have one yet, so make the current device's primary context current explicitly.
+  int dev = 0;
+  RESIHP_CUDA_CHECK(cudaGetDevice(&dev));
+  RESIHP_CUDA_CHECK(cudaSetDevice(dev));
   CUtensorMap map;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};

@@ -3,18 +3,22 @@
 // wrappers in torch_api.cpp translate tensors into these calls.
 #pragma once
 #include <cstdint>
-#include <sstream>
 #include <stdexcept>
+#include <string>
+#include <type_traits>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace resihp {
 
+// Error messages are assembled with std::string / std::to_string only (no iostreams):
+// they must be safe to build on any thread, including autograd worker threads.
 namespace detail {
-inline void append(std::ostringstream&) {}
+inline void append(std::string&) {}
 template <class T, class... R>
-inline void append(std::ostringstream& o, const T& v, const R&... r) {
-  o << v;
+inline void append(std::string& o, const T& v, const R&... r) {
+  if constexpr (std::is_arithmetic_v<T>) o += std::to_string(v);
+  else o += v;
   append(o, r...);
 }
 }  // namespace detail
@@ -22,9 +26,9 @@ inline void append(std::ostringstream& o, const T& v, const R&... r) {
 #define RESIHP_CHECK(cond, ...)                                                        \
   do {                                                                                 \
     if (!(cond)) {                                                                     \
-      std::ostringstream _o;                                                           \
+      std::string _o;                                                                  \
       ::resihp::detail::append(_o, "resihp: ", __VA_ARGS__);                           \
-      throw std::runtime_error(_o.str());                                              \
+      throw std::runtime_error(_o);                                                    \
     }                                                                                  \
   } while (0)
 
@@ -72,5 +76,25 @@ void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float*
 void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, const void* dout, int64_t dout_ld,
               const float* lse, float* delta, void* dqkv, int64_t dqkv_ld, int rows, int seq, int hq, int hkv, int d,
               float scale, int* err, cudaStream_t st);
+
+}  // namespace resihp
+
+namespace resihp {
+
+int fused_grid(int m, int n, int tp);
+void ag_publish(const void* x, void* slot, int64_t bytes, int rank, int tp, unsigned epoch, unsigned* sig_ag,
+                unsigned* const* peer_sig_ag, unsigned* done, unsigned done_base, int grid, int* err,
+                cudaStream_t st);
+void ag_gemm(const void* x_local, const void* xg, const void* const* peer_x, const void* w, int64_t ldw, bool w_mn,
+             void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp, unsigned epoch, unsigned* sig_ag,
+             unsigned* ready, unsigned ready_base, int grid, int* err, cudaStream_t st);
+void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
+             int k, int rank, int tp, unsigned epoch, void* const* peer_recv, unsigned* const* peer_arrive,
+             unsigned* const* peer_sig_rs, unsigned* arrive, unsigned* sig_rs, unsigned arrive_base,
+             const void* recv_local, int grid, int* err, cudaStream_t st);
+void* symm_alloc(int64_t bytes, void* handle_out);
+void* symm_open(const void* handle);
+void symm_close(void* p);
+void symm_free(void* p);
 
 }  // namespace resihp

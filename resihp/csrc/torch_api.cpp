@@ -6,6 +6,9 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <mutex>
+#include <csignal>
+#include <execinfo.h>
+#include <unistd.h>
 
 #include "launch.h"
 
@@ -270,6 +273,100 @@ torch::Tensor attn_bwd_t(torch::Tensor qkv, torch::Tensor out, torch::Tensor dou
   return dqkv;
 }
 
+
+// ---- debugging aid: native backtrace on SIGSEGV ---------------------------------------
+
+static void crash_handler(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "\n[resihp] native backtrace:\n";
+  (void)!write(2, msg, sizeof(msg) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
+void install_crash_handler() { signal(SIGSEGV, crash_handler); }
+
+// ---- symmetric workspace + fused TP collectives ---------------------------------------
+
+template <class T>
+static T* as_ptr(int64_t v) { return reinterpret_cast<T*>(static_cast<uintptr_t>(v)); }
+
+py::tuple symm_alloc_t(int64_t bytes) {
+  cudaIpcMemHandle_t h;
+  void* p = symm_alloc(bytes, &h);
+  return py::make_tuple(reinterpret_cast<int64_t>(p), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t symm_open_t(py::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  return reinterpret_cast<int64_t>(symm_open(s.data()));
+}
+
+void symm_close_t(int64_t p) { symm_close(as_ptr<void>(p)); }
+void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
+
+int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
+
+void ag_publish_t(torch::Tensor x, int64_t slot, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
+                  std::vector<int64_t> peer_sig_ag, int64_t done, int64_t done_base, int64_t grid) {
+  check_cuda_bf16(x, "x");
+  TORCH_CHECK(x.is_contiguous(), "published chunk must be contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  std::vector<unsigned*> peers;
+  for (auto v : peer_sig_ag) peers.push_back(as_ptr<unsigned>(v));
+  ag_publish(x.data_ptr(), as_ptr<void>(slot), x.numel() * 2, int(rank), int(tp), unsigned(epoch),
+             as_ptr<unsigned>(sig_ag), peers.data(), as_ptr<unsigned>(done), unsigned(done_base), int(grid),
+             error_word(x.device()), cur_stream());
+}
+
+void ag_gemm_t(torch::Tensor x_local, torch::Tensor xg, std::vector<int64_t> peer_x, torch::Tensor w, bool w_mn,
+               torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag, int64_t ready,
+               int64_t ready_base, int64_t grid) {
+  check_cuda_bf16(x_local, "x_local");
+  check_cuda_bf16(xg, "xg");
+  check_cuda_bf16(w, "w");
+  check_cuda_bf16(y, "y");
+  TORCH_CHECK(x_local.is_contiguous() && xg.is_contiguous() && y.is_contiguous() && w.stride(1) == 1,
+              "fused AG-GEMM tensors must be contiguous");
+  const int64_t k = x_local.size(1);
+  const int64_t t = xg.size(0);
+  const int64_t n = y.size(1);
+  TORCH_CHECK(xg.size(1) == k && y.size(0) == t && x_local.size(0) * tp == t, "fused AG-GEMM shapes");
+  TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused AG-GEMM weight");
+  c10::cuda::CUDAGuard guard(x_local.device());
+  std::vector<const void*> peers;
+  for (auto v : peer_x) peers.push_back(as_ptr<const void>(v));
+  ag_gemm(x_local.data_ptr(), xg.data_ptr(), peers.data(), w.data_ptr(), w.stride(0), w_mn, y.data_ptr(), y.stride(0),
+          int(t), int(n), int(k), int(rank), int(tp), unsigned(epoch), as_ptr<unsigned>(sig_ag),
+          as_ptr<unsigned>(ready), unsigned(ready_base), int(grid), error_word(x_local.device()), cur_stream());
+}
+
+void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_local, int64_t rank, int64_t tp,
+               int64_t epoch, std::vector<int64_t> peer_recv, std::vector<int64_t> peer_arrive,
+               std::vector<int64_t> peer_sig_rs, int64_t arrive, int64_t sig_rs, int64_t arrive_base,
+               int64_t recv_local, int64_t grid) {
+  check_cuda_bf16(h, "h");
+  check_cuda_bf16(w, "w");
+  check_cuda_bf16(y_local, "y_local");
+  TORCH_CHECK(h.is_contiguous() && y_local.is_contiguous() && w.stride(1) == 1, "fused GEMM-RS tensors must be contiguous");
+  const int64_t t = h.size(0), k = h.size(1), n = y_local.size(1);
+  TORCH_CHECK(y_local.size(0) * tp == t, "fused GEMM-RS shapes");
+  TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused GEMM-RS weight");
+  c10::cuda::CUDAGuard guard(h.device());
+  std::vector<void*> recv;
+  std::vector<unsigned*> arr, sig;
+  for (auto v : peer_recv) recv.push_back(as_ptr<void>(v));
+  for (auto v : peer_arrive) arr.push_back(as_ptr<unsigned>(v));
+  for (auto v : peer_sig_rs) sig.push_back(as_ptr<unsigned>(v));
+  gemm_rs(h.data_ptr(), w.data_ptr(), w.stride(0), w_mn, y_local.data_ptr(), y_local.stride(0), int(t), int(n), int(k),
+          int(rank), int(tp), unsigned(epoch), recv.data(), arr.data(), sig.data(), as_ptr<unsigned>(arrive),
+          as_ptr<unsigned>(sig_rs), unsigned(arrive_base), as_ptr<const void>(recv_local), int(grid),
+          error_word(h.device()), cur_stream());
+}
+
 }  // namespace resihp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -290,4 +387,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("xent_grad", &resihp::xent_grad_t);
   m.def("attn_fwd", &resihp::attn_fwd_t);
   m.def("attn_bwd", &resihp::attn_bwd_t);
+  m.def("install_crash_handler", &resihp::install_crash_handler);
+  m.def("symm_alloc", &resihp::symm_alloc_t);
+  m.def("symm_open", &resihp::symm_open_t);
+  m.def("symm_close", &resihp::symm_close_t);
+  m.def("symm_free", &resihp::symm_free_t);
+  m.def("fused_grid", &resihp::fused_grid_t);
+  m.def("ag_publish", &resihp::ag_publish_t);
+  m.def("ag_gemm", &resihp::ag_gemm_t);
+  m.def("gemm_rs", &resihp::gemm_rs_t);
 }

@@ -1,0 +1,97 @@
+"""Fused AG->GEMM and GEMM->RS kernels against NCCL + FP32 torch, on 2+ GPUs.
+
+Spawns one process per GPU (up to 8); each compares the fused forward and backward
+against all-gather / reduce-scatter on NCCL followed by an FP32 torch product.
+Skipped with fewer than two GPUs.
+"""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, out):
+    import faulthandler
+    import sys
+
+    faulthandler.enable()
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    from resihp.ops import check_device_errors
+    from resihp.parallel.fused import SymmetricWorkspace, ag_linear, linear_rs
+
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    d, n, t = 512, 768, 256 * world
+    tl = t // world
+    ws = SymmetricWorkspace(dist.group.WORLD, tl, d, torch.device("cuda", rank))
+    errs = {}
+    for it in range(3):  # several epochs: slot parity and counters advance
+        x_full = torch.randn(t, d, device="cuda", generator=g).bfloat16()
+        # this rank's column shard of the weight and of the output gradient
+        gr = torch.Generator(device="cuda").manual_seed(4321 + 17 * rank + it)
+        w1 = (torch.randn(n, d, device="cuda", generator=gr) / d**0.5).bfloat16()
+        w2 = (torch.randn(d, n, device="cuda", generator=g) / n**0.5).bfloat16()
+        dy_full = torch.randn(t, n, device="cuda", generator=gr).bfloat16()
+        x_local = x_full[rank * tl:(rank + 1) * tl].contiguous().requires_grad_()
+        mg1 = torch.zeros(n, d, device="cuda")
+        y = ag_linear(x_local, w1.requires_grad_(), mg1, ws)
+        ref = x_full.float() @ w1.float().t()
+        errs[f"ag_fwd{it}"] = ((y.float() - ref).norm() / ref.norm()).item()
+        y.backward(dy_full)
+        part = (dy_full.float() @ w1.float()).contiguous()
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        ref_dx = sum(parts)[rank * tl:(rank + 1) * tl]
+        errs[f"ag_dx{it}"] = ((x_local.grad.float() - ref_dx).norm() / ref_dx.norm()).item()
+        ref_dw = dy_full.float().t() @ x_full.float()
+        errs[f"ag_dw{it}"] = ((mg1 - ref_dw).norm() / ref_dw.norm()).item()
+        # row-parallel: every rank holds h_r = x_full @ shard-ish weight; use a rank-specific h
+        h = torch.randn(t, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(99 + rank + 7 * it)).bfloat16().requires_grad_()
+        mg2 = torch.zeros(d, n, device="cuda")
+        yr = linear_rs(h, w2.requires_grad_(), mg2, ws)
+        partial = (h.detach().float() @ w2.float().t()).contiguous()
+        allp = [torch.empty_like(partial) for _ in range(world)]
+        dist.all_gather(allp, partial)
+        ref_y = sum(allp)[rank * tl:(rank + 1) * tl]
+        errs[f"rs_fwd{it}"] = ((yr.float() - ref_y).norm() / ref_y.norm()).item()
+        dyl = torch.randn(tl, d, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5 + rank + it)).bfloat16()
+        yr.backward(dyl)
+        dyg = [torch.empty_like(dyl) for _ in range(world)]
+        dist.all_gather(dyg, dyl)
+        dyg = torch.cat(dyg).float()
+        ref_dh = dyg @ w2.float()
+        errs[f"rs_dh{it}"] = ((h.grad.float() - ref_dh).norm() / ref_dh.norm()).item()
+        ref_dw2 = dyg.t() @ h.detach().float()
+        errs[f"rs_dw{it}"] = ((mg2 - ref_dw2).norm() / ref_dw2.norm()).item()
+    torch.cuda.synchronize()
+    check_device_errors(rank)
+    ws.close()
+    torch.save(errs, os.path.join(out, f"errs_{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_fused_ag_gemm_and_gemm_rs(tmp_path):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        errs = torch.load(tmp_path / f"errs_{r}.pt")
+        for k, v in errs.items():
+            limit = 1e-3 if "dw" in k else 1.5e-2
+            assert v < limit, (r, k, v, errs)
