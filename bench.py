@@ -220,6 +220,7 @@ def run_ours(args):
             "config": {"model": "llama-1.3b (24L, d2048, 16H MHA, SwiGLU 5504, V32000)", "global_batch": GLOBAL_BATCH,
                        "micro_batch": MICRO_BATCH, "seq_len": config.seq_len,
                        "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if tp > 1 else ""),
+                       "tp_comm": "fused-nvlink" if (tp > 1 and os.environ.get("RESIHP_FUSED_TP", "1") != "0") else ("nccl" if tp > 1 else "none"),
                        "l2": "inputs larger than L2 (weights/activations >> 126 MB)"},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(bytes_in[0]),
@@ -228,6 +229,8 @@ def run_ours(args):
             "impl": "resihp",
         }
         print(json.dumps(line), flush=True)
+    if run is not None:
+        run.stage.close_comm()
     del run
     cp.destroy_training_groups()
     dist.barrier(group=cp.world_group)

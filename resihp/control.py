@@ -127,6 +127,9 @@ class ControlPlane:
     def dissolve_world(self) -> None:
         import torch.distributed as dist
 
+        # No kernel is in flight at a safe point; a dead peer cannot join a barrier.
+        if self.training_run is not None:
+            self.training_run.stage.close_comm(barrier=False)
         self.destroy_training_groups()
         dist.destroy_process_group()
         self.world_group = None
@@ -272,6 +275,8 @@ class ControlPlane:
     def shutdown(self) -> None:
         import torch.distributed as dist
 
+        if self.training_run is not None:
+            self.training_run.stage.close_comm(barrier=True)
         self.destroy_training_groups()
         dist.barrier(group=self.world_group)
         dist.destroy_process_group()

@@ -1,37 +1,38 @@
 // Tensor-parallel GEMMs fused with their sequence-parallel collective over NVLink peer
-// memory (CUDA IPC mappings of each rank's symmetric workspace; plain P2P loads,
-// stores and atomics -- no multicast of any kind).
+// memory (CUDA IPC mappings of each rank's symmetric workspace; plain P2P loads and
+// stores plus flag words -- no multicast of any kind).
 //
-//   AG->GEMM   y[T, N]  = all_gather_tokens(x_r[T/tp, K]) * W[N, K]^T
-//   GEMM->RS   y_r[T/tp, N] = reduce_scatter_tokens(h[T, K] * W[N, K]^T)
+//   AG->GEMM   y[T, N]      = all_gather_tokens(x_r[T/tp, K]) * op(W)
+//   GEMM->RS   y_r[T/tp, N] = reduce_scatter_tokens(h[T, K] * op(W))
 //
 // Both are the persistent tcgen05 GEMM of gemm.cu (TMA producer warp, one MMA-issuing
-// thread, four epilogue warps, two TMEM accumulators) with the collective woven in:
+// thread, four epilogue warps, two TMEM accumulators) plus four *copy warps* per CTA that
+// move the collective's data with coalesced 16-byte loads and stores while the tensor
+// cores work; every remote byte crosses NVLink exactly once.
 //
-// AG: tiles run chunk by chunk, this rank's own token chunk first (read in place through
-// its own tensor map). Two extra copy warps per CTA pull this CTA's share of every peer's
-// chunk over NVLink -- each remote byte crosses the link once -- into the local gather
-// buffer, then bump that chunk's ready counter; the producer waits for a chunk's counter
-// before its first TMA load from the gather buffer. The gather buffer ends up holding
-// the whole gathered input, which the backward pass reuses for the weight gradient.
-// A rank's chunk is published (copied into its symmetric slot, then flagged to every
-// peer) by ag_publish_kernel; slots alternate by epoch parity, and a rank only
-// overwrites a slot once every peer has published the next epoch, i.e. has finished
-// reading the previous one.
+// AG: the copy warps first publish this rank's chunk -- one pass writes it into the
+// rank's symmetric slot (epoch parity) and into the local gather buffer -- and the last
+// copy warp to finish flags the epoch to every peer. They then pull their CTA's share of
+// each peer's slot into the gather buffer and bump that chunk's ready counter. Tiles run
+// own chunk first (read in place through this rank's tensor map), then the peers' chunks
+// once their counters are complete. The gather buffer ends up holding the whole gathered
+// input, reused by the backward pass for the weight gradient.
 //
-// RS: tiles of the peers' token chunks run first; their epilogue stores the bf16
-// partial tile straight into the owner's receive slot (this rank's row of it) and bumps
-// the owner's arrival counter for this source. The own chunk runs last: its epilogue
-// waits for every source's tiles, then sums the partials in rank order (fp32) and writes
-// the reduced rows -- deterministic, and the reduction costs no extra pass.
+// RS: tiles of the peers' token chunks run first; their epilogue writes the partial tile
+// to this rank's own partial buffer (epoch parity) and bumps that tile's flag. Each CTA's
+// copy warps pull, for every own-chunk tile that CTA will finish, the peers' partial tiles
+// once flagged, into a local receive buffer; the own tile's epilogue then sums all ranks'
+// partials in rank order (fp32, deterministic) and writes the reduced rows.
 //
-// Every wait (peer flags, counters, mbarriers) is bounded by the global timer and
-// reports into the error word. Both kernels rely on all their CTAs being resident at once
-// (grid <= SM count, one CTA per SM); if that ever fails, the bounded waits turn it into
-// an error instead of a hang.
+// Buffer reuse needs no extra handshake: a rank reaches epoch e only after its epoch e-1
+// kernel consumed every peer's epoch e-1 data, which those peers produced only after
+// finishing their epoch e-2 kernels -- the last readers of this parity's buffers.
+//
+// Every wait (peer flags, counters, mbarriers) is bounded by the global timer and reports
+// into the error word. All CTAs must be resident together (grid <= SM count, one CTA
+// per SM); if that ever failed, the bounded waits would turn it into an error, not a hang.
 #include <algorithm>
 #include <cstring>
-#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -40,30 +41,35 @@
 namespace resihp {
 
 constexpr int kMaxTp = 8;
+constexpr int kCopyWarps = 4;
+constexpr int kFusedThreads = 192 + 32 * kCopyWarps;
 
 struct CommArgs {
   int rank, tp, rows_per_rank;
   unsigned epoch;
   // AG
-  const __nv_bfloat16* peer_x[kMaxTp];  // each rank's published slot for this call
-  __nv_bfloat16* xg;                     // local gather buffer [T, K]
-  const __nv_bfloat16* x_local;          // this rank's chunk [T/tp, K]
+  const __nv_bfloat16* peer_slot[kMaxTp];  // each rank's slot for this epoch
+  __nv_bfloat16* own_slot;                 // this rank's slot for this epoch
+  __nv_bfloat16* xg;                       // local gather buffer [T, K]
+  const __nv_bfloat16* x_local;            // this rank's chunk [T/tp, K]
   int64_t ldx;
-  unsigned* sig_ag;                      // local: sig_ag[s] = last epoch rank s published
-  unsigned* ready;                       // local per-chunk ready counters [tp]
+  unsigned* sig_ag;                        // local: sig_ag[s] = last epoch rank s published
+  unsigned* peer_sig_ag[kMaxTp];           // each rank's sig_ag array
+  unsigned* pub;                           // local publish counter
+  unsigned pub_target;
+  unsigned* ready;                         // local per-chunk ready counters [tp]
   unsigned ready_target;
   // RS
-  __nv_bfloat16* peer_recv[kMaxTp];      // each rank's receive slot base for this call
-  unsigned* peer_arrive[kMaxTp];         // each rank's arrival counters [tp]
-  unsigned* peer_sig_rs[kMaxTp];         // each rank's sig_rs array [tp]
-  unsigned* arrive;                      // local arrival counters [tp]
-  unsigned* sig_rs;                      // local sig_rs array [tp]
-  unsigned arrive_target;
-  __nv_bfloat16* recv_local;             // local receive slot base for this call
+  __nv_bfloat16* part_local;               // this rank's partial buffer [T, N] for this epoch
+  const __nv_bfloat16* peer_part[kMaxTp];  // each rank's partial buffer for this epoch
+  unsigned* flag_local;                    // this rank's per-tile flags
+  const unsigned* peer_flag[kMaxTp];       // each rank's per-tile flags
+  unsigned flag_target;
+  __nv_bfloat16* recv;                     // local receive buffer [tp][T/tp, N]
 };
 
 struct FusedArgs {
-  void* c;          // AG: y [T, N]; RS: y_r [T/tp, N]
+  void* c;  // AG: y [T, N]; RS: y_r [T/tp, N]
   int64_t ldc;
   int m, n, k;
   int* err;
@@ -99,10 +105,39 @@ __device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int
   return true;
 }
 
+// One lane waits, the whole warp learns the outcome.
+__device__ __forceinline__ bool warp_wait_geq(const unsigned* p, unsigned target, int* err, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = wait_geq(p, target, err, kErrPeerWait) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
+}
+
+// Copy `rows` rows of `cols16` 16-byte vectors (row strides in vectors) with the copy-warp
+// threads, eight loads in flight per thread.
+__device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* src, int64_t sld, int rows,
+                                          int cols16, int ct) {
+  const int64_t total = int64_t(rows) * cols16;
+  constexpr int kU = 8;
+  constexpr int kT = 32 * kCopyWarps;
+  for (int64_t base = ct; base < total; base += int64_t(kT) * kU) {
+    uint4 r[kU];
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + int64_t(u) * kT;
+      if (i < total) r[u] = ld_cg_v4(src + (i / cols16) * sld + (i % cols16));
+    }
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + int64_t(u) * kT;
+      if (i < total) dst[(i / cols16) * dld + (i % cols16)] = r[u];
+    }
+  }
 }
 
 // ---- tile order ------------------------------------------------------------------------
@@ -116,10 +151,10 @@ struct FusedShape {
   static constexpr int kABytes = kFBM * kFBK * 2;
   static constexpr int kBBytes = BN * kFBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
 };
 
-// Tile t -> (chunk, m0, n0). Chunks are visited starting at (rank + first) % tp; inside a
+// Tile t -> (chunk, m0, tn). Chunks are visited starting at (rank + first) % tp; inside a
 // chunk, tiles are grouped along M for L2 reuse.
 __device__ __forceinline__ void fused_tile(int t, int tiles_m_chunk, int tiles_n, const CommArgs& c, int first,
                                            int& chunk, int& m0, int& tn_out) {
@@ -133,18 +168,17 @@ __device__ __forceinline__ void fused_tile(int t, int tiles_m_chunk, int tiles_n
   const int g0 = group * kGroup;
   const int size = min(tiles_m_chunk - g0, kGroup);
   const int in_group = local % per_group;
-  const int tm = g0 + in_group % size;
-  const int tn = in_group / size;
-  m0 = chunk * c.rows_per_rank + tm * kFBM;
-  tn_out = tn;
+  m0 = chunk * c.rows_per_rank + (g0 + in_group % size) * kFBM;
+  tn_out = in_group / size;
 }
 
 template <int BN, bool B_MN, int MODE>
-__global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
+__global__ void __launch_bounds__(kFusedThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_a2,
                       const __grid_constant__ CUtensorMap tma_b, FusedArgs g) {
   using S = FusedShape<BN>;
   constexpr int kStages = S::kStages;
+  constexpr int kPullSlots = 4;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
@@ -152,7 +186,8 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* pulled = acc_empty + 2;  // RS: own tile j's peer partials are in `recv`
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pulled + kPullSlots);
 
   const CommArgs& cm = g.comm;
   const int warp = threadIdx.x >> 5;
@@ -172,12 +207,8 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    for (int j = 0; j < kPullSlots; ++j) mbar_init(&pulled[j], kCopyWarps);
     fence_barrier_init();
-    if (MODE == 2 && blockIdx.x == 0) {
-      // "I started RS epoch e": every slot of epoch e-1 has been read here.
-      for (int p = 0; p < cm.tp; ++p)
-        if (p != cm.rank) st_release_sys(cm.peer_sig_rs[p] + cm.rank, cm.epoch);
-    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
@@ -186,6 +217,7 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch(&tma_a);
       tma_prefetch(&tma_b);
@@ -224,6 +256,7 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(kFBM, BN, 0, B_MN ? 1 : 0);
       int s = 0;
@@ -254,12 +287,10 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
       }
     }
   } else if (warp < 6) {
+    // ---------------- epilogue ----------------
     const int q = warp & 3;
     int i = 0;
-    bool remote_ok[kMaxTp];
-    #pragma unroll
-    for (int p = 0; p < kMaxTp; ++p) remote_ok[p] = false;
-    bool own_ready = false;
+    int j_own = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
       int chunk, m0, tn;
@@ -268,37 +299,18 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
       const uint32_t accph = (i >> 1) & 1;
       if (!mbar_wait(&acc_full[a], accph, g.err, kErrEpiWait)) break;
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;             // global row in [0, T)
-      const int lrow = row - chunk * cm.rows_per_rank;  // row inside its chunk
+      const int row = m0 + q * 32 + lane;
+      const int lrow = row - chunk * cm.rows_per_rank;
+      const bool reduce_here = MODE == 2 && chunk == cm.rank;
       __nv_bfloat16* dst;
-      int64_t ld;
-      if (MODE == 1) {
-        dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
-        ld = g.ldc;
-      } else if (chunk != cm.rank) {
-        // wait once per owner: its slot of this parity is free again
-        if (!remote_ok[chunk]) {
-          if (cm.epoch > 1 && lane == 0 &&
-              !wait_geq(cm.sig_rs + chunk, cm.epoch - 1, g.err, kErrPeerWait))
-            ok = false;
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          remote_ok[chunk] = true;
-        }
-        dst = cm.peer_recv[chunk] + (int64_t(cm.rank) * cm.rows_per_rank + lrow) * g.n;
-        ld = g.n;
-      } else {
-        if (!own_ready) {
-          if (lane == 0) {
-            for (int p = 0; p < cm.tp && ok; ++p)
-              if (p != cm.rank && !wait_geq(cm.arrive + p, cm.arrive_target, g.err, kErrPeerWait)) ok = false;
-          }
-          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-          own_ready = true;
-        }
-        dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(lrow) * g.ldc;
-        ld = g.ldc;
+      if (MODE == 1) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
+      else if (!reduce_here) dst = cm.part_local + int64_t(row) * g.n;
+      else dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(lrow) * g.ldc;
+      if (reduce_here) {
+        const int slot = j_own % kPullSlots;
+        if (!mbar_wait(&pulled[slot], (j_own / kPullSlots) & 1, g.err, kErrEpiWait)) ok = false;
+        ++j_own;
       }
-      (void)ld;
       #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t v[32];
@@ -309,8 +321,8 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
         float f[32];
         #pragma unroll
         for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
-        if (MODE == 2 && chunk == cm.rank) {
-          // rank-ordered sum of every source's partial (own partial in fp32)
+        if (reduce_here) {
+          // every rank's partial, summed in rank order (this rank's own in fp32)
           float tot[32];
           #pragma unroll
           for (int e = 0; e < 32; ++e) tot[e] = 0.f;
@@ -318,18 +330,18 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
             if (src == cm.rank) {
               #pragma unroll
               for (int e = 0; e < 32; ++e) tot[e] += f[e];
-            } else {
-              const __nv_bfloat16* p = cm.recv_local + (int64_t(src) * cm.rows_per_rank + lrow) * g.n + col0;
+              continue;
+            }
+            const __nv_bfloat16* p = cm.recv + (int64_t(src) * cm.rows_per_rank + lrow) * g.n + col0;
+            #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 raw4 = *reinterpret_cast<const uint4*>(p + 8 * u);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw4);
               #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                uint4 raw4 = *reinterpret_cast<const uint4*>(p + 8 * u);
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw4);
-                #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 x = __bfloat1622float2(h[e]);
-                  tot[8 * u + 2 * e] += x.x;
-                  tot[8 * u + 2 * e + 1] += x.y;
-                }
+              for (int e = 0; e < 4; ++e) {
+                const float2 x = __bfloat1622float2(h[e]);
+                tot[8 * u + 2 * e] += x.x;
+                tot[8 * u + 2 * e + 1] += x.y;
               }
             }
           }
@@ -346,51 +358,82 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
           *reinterpret_cast<uint4*>(dst + col0 + 8 * u) = o;
         }
       }
-      if (MODE == 2 && chunk != cm.rank) {
-        // publish this warp's 32 rows of the tile: fence the stores system-wide, then
-        // one lane bumps the owner's counter (four arrivals per tile, one per warp)
+      if (MODE == 2 && !reduce_here) {
+        // flag this warp's 32 rows of the partial tile (four flags per tile, one per warp)
         __threadfence_system();
         __syncwarp();
-        if (lane == 0) atomicAdd_system(cm.peer_arrive[chunk] + cm.rank, 1u);
+        if (lane == 0) atomicAdd(cm.flag_local + (m0 / kFBM) * tiles_n + tn, 1u);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
-  } else if (MODE == 1) {
-    // copy warps: this CTA's share of every peer chunk, then of the own chunk
-    const int ct = threadIdx.x - 192;  // 0..63
-    const int64_t vec_per_row = cm.ldx / 8;
-    const int lo = int(int64_t(cm.rows_per_rank) * blockIdx.x / gridDim.x);
-    const int hi = int(int64_t(cm.rows_per_rank) * (blockIdx.x + 1) / gridDim.x);
+  } else {
+    // ---------------- copy warps ----------------
+    const int ct = threadIdx.x - 192;  // 0 .. 32*kCopyWarps-1
     bool ok = true;
-    for (int p = 1; p <= cm.tp && ok; ++p) {
-      const int chunk = (cm.rank + p) % cm.tp;
-      const bool own = chunk == cm.rank;
-      if (!own) {
-        if (lane == 0 && !wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, kErrPeerWait)) ok = false;
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (MODE == 1) {
+      const int cols16 = int(cm.ldx / 8);
+      const int lo = int(int64_t(cm.rows_per_rank) * blockIdx.x / gridDim.x);
+      const int hi = int(int64_t(cm.rows_per_rank) * (blockIdx.x + 1) / gridDim.x);
+      // publish: this CTA's rows of the own chunk -> own slot and gather buffer
+      {
+        const uint4* src = reinterpret_cast<const uint4*>(cm.x_local + int64_t(lo) * cm.ldx);
+        uint4* slot = reinterpret_cast<uint4*>(cm.own_slot + int64_t(lo) * cm.ldx);
+        uint4* xg = reinterpret_cast<uint4*>(cm.xg + (int64_t(cm.rank) * cm.rows_per_rank + lo) * cm.ldx);
+        const int64_t total = int64_t(hi - lo) * cols16;
+        for (int64_t v = ct; v < total; v += 32 * kCopyWarps) {
+          const uint4 x = src[v];
+          slot[v] = x;
+          xg[v] = x;
+        }
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+          const unsigned prev = atomicAdd(cm.pub, 1u);
+          if (prev + 1 == cm.pub_target) {
+            // the last copy warp of the grid announces the epoch to every peer
+            __threadfence_system();
+            for (int p = 0; p < cm.tp; ++p)
+              if (p != cm.rank) st_release_sys(cm.peer_sig_ag[p] + cm.rank, cm.epoch);
+          }
+        }
+      }
+      // pull: this CTA's rows of every peer chunk
+      for (int p = 1; p < cm.tp && ok; ++p) {
+        const int chunk = (cm.rank + p) % cm.tp;
+        ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
         if (!ok) break;
+        copy_rows(reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx), cols16,
+                  reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(lo) * cm.ldx), cols16, hi - lo,
+                  cols16, ct);
+        fence_proxy_async_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(cm.ready + chunk, 1u);
       }
-      const uint4* src = reinterpret_cast<const uint4*>((own ? cm.x_local : cm.peer_x[chunk]) + int64_t(lo) * cm.ldx);
-      uint4* dst = reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx);
-      const int64_t nvec = int64_t(hi - lo) * vec_per_row;
-      constexpr int kUnroll = 8;
-      for (int64_t base = ct; base < nvec; base += 64 * kUnroll) {
-        uint4 r[kUnroll];
-        #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (base + u * 64 < nvec) r[u] = ld_cg_v4(src + base + u * 64);
-        #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (base + u * 64 < nvec) dst[base + u * 64] = r[u];
+    } else {
+      // for each own-chunk tile this CTA will reduce: pull the peers' partial tiles
+      int j = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int chunk, m0, tn;
+        fused_tile(t, tiles_m_chunk, tiles_n, cm, first, chunk, m0, tn);
+        if (chunk != cm.rank) continue;
+        const int lrow0 = m0 - chunk * cm.rows_per_rank;
+        const int ncols16 = min(BN, g.n - tn * BN) / 8;
+        for (int src = 0; src < cm.tp && ok; ++src) {
+          if (src == cm.rank) continue;
+          ok = warp_wait_geq(cm.peer_flag[src] + (m0 / kFBM) * tiles_n + tn, cm.flag_target, g.err, lane);
+          if (!ok) break;
+          const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[src] + int64_t(m0) * g.n + tn * BN);
+          uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(src) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
+          copy_rows(to, g.n / 8, from, g.n / 8, kFBM, ncols16, ct);
+        }
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pulled[j % kPullSlots]);
+        ++j;
       }
-      // make this warp's stores visible to the TMA (async proxy) readers, then arrive
-      // (two arrivals per CTA per chunk, one per copy warp)
-      fence_proxy_async_global();
-      __threadfence();
-      __syncwarp();
-      if (lane == 0 && !own) atomicAdd(cm.ready + chunk, 1u);
     }
   }
 
@@ -399,46 +442,6 @@ __global__ void __launch_bounds__(MODE == 1 ? 256 : 192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
-  }
-}
-
-// Publish this rank's chunk for AG epoch `epoch`: wait until every peer has published
-// epoch-1 (so it finished reading this parity's slot at epoch-2), copy the chunk into the
-// slot, and -- from the last block to finish -- flag the epoch to every peer.
-struct PublishArgs {
-  const uint4* x;
-  uint4* slot;
-  int64_t nvec;
-  int rank, tp;
-  unsigned epoch;
-  unsigned* sig_ag;                 // local
-  unsigned* peer_sig_ag[kMaxTp];    // each rank's sig_ag array
-  unsigned* done;                   // local block-completion counter
-  unsigned done_target;
-  int* err;
-};
-
-__global__ void ag_publish_kernel(PublishArgs a) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) {
-    ok = 1;
-    if (a.epoch > 1)
-      for (int p = 0; p < a.tp; ++p)
-        if (p != a.rank && !wait_geq(a.sig_ag + p, a.epoch - 1, a.err, kErrPeerWait)) ok = 0;
-  }
-  __syncthreads();
-  if (!ok) return;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < a.nvec; i += int64_t(gridDim.x) * blockDim.x)
-    a.slot[i] = a.x[i];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(a.done, 1u);
-    if (prev + 1 == a.done_target) {
-      __threadfence_system();
-      for (int p = 0; p < a.tp; ++p)
-        if (p != a.rank) st_release_sys(a.peer_sig_ag[p] + a.rank, a.epoch);
-    }
   }
 }
 
@@ -463,49 +466,29 @@ void launch_fused(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorM
   RESIHP_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem));
   // The grid never exceeds the SM count and one CTA fills an SM, so on a GPU this process
   // owns every CTA is resident at once.
-  kernel<<<grid, MODE == 1 ? 256 : 192, S::kSmem, st>>>(ta, ta2, tb, g);
+  kernel<<<grid, kFusedThreads, S::kSmem, st>>>(ta, ta2, tb, g);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace
 
 int fused_grid(int m, int n, int tp) {
-  const int tiles = (m / kFBM) * ((n + 255) / 256);
   (void)tp;
+  const int tiles = (m / kFBM) * ((n + 255) / 256);
   return std::min(tiles, sm_count());
 }
 
-void ag_publish(const void* x, void* slot, int64_t bytes, int rank, int tp, unsigned epoch, unsigned* sig_ag,
-                unsigned* const* peer_sig_ag, unsigned* done, unsigned done_base, int grid, int* err,
-                cudaStream_t st) {
-  RESIHP_CHECK(bytes % 16 == 0 && tp <= kMaxTp, "ag_publish: bad size or tp");
-  PublishArgs a{};
-  a.x = static_cast<const uint4*>(x);
-  a.slot = static_cast<uint4*>(slot);
-  a.nvec = bytes / 16;
-  a.rank = rank;
-  a.tp = tp;
-  a.epoch = epoch;
-  a.sig_ag = sig_ag;
-  for (int p = 0; p < tp; ++p) a.peer_sig_ag[p] = peer_sig_ag[p];
-  a.done = done;
-  a.done_target = done_base + unsigned(grid);
-  a.err = err;
-  ag_publish_kernel<<<grid, 256, 0, st>>>(a);
-  RESIHP_CUDA_CHECK(cudaGetLastError());
-}
-
-void ag_gemm(const void* x_local, const void* xg, const void* const* peer_x, const void* w, int64_t ldw, bool w_mn,
-             void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp, unsigned epoch, unsigned* sig_ag,
+void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
+             int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
+             unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,
              unsigned* ready, unsigned ready_base, int grid, int* err, cudaStream_t st) {
   RESIHP_CHECK(tp >= 2 && tp <= kMaxTp && t_rows % tp == 0 && (t_rows / tp) % kFBM == 0,
                "ag_gemm: rows per rank must be a multiple of 128");
   RESIHP_CHECK(n % 8 == 0 && k % 8 == 0, "ag_gemm: N and K must be multiples of 8");
   const int tl = t_rows / tp;
-  const int bn = 256;
   CUtensorMap ta = make_tma_2d_bf16(x_local, tl, k, k, 64, kFBM);
   CUtensorMap ta2 = make_tma_2d_bf16(xg, t_rows, k, k, 64, kFBM);
-  CUtensorMap tb = w_mn ? make_tma_2d_bf16(w, k, n, ldw, 64, 64) : make_tma_2d_bf16(w, n, k, ldw, 64, bn);
+  CUtensorMap tb = w_mn ? make_tma_2d_bf16(w, k, n, ldw, 64, 64) : make_tma_2d_bf16(w, n, k, ldw, 64, 256);
   FusedArgs g{};
   g.c = y;
   g.ldc = ldy;
@@ -518,28 +501,33 @@ void ag_gemm(const void* x_local, const void* xg, const void* const* peer_x, con
   c.tp = tp;
   c.rows_per_rank = tl;
   c.epoch = epoch;
-  for (int p = 0; p < tp; ++p) c.peer_x[p] = static_cast<const __nv_bfloat16*>(peer_x[p]);
-  c.xg = static_cast<__nv_bfloat16*>(const_cast<void*>(xg));
+  for (int p = 0; p < tp; ++p) {
+    c.peer_slot[p] = static_cast<const __nv_bfloat16*>(peer_slot[p]);
+    c.peer_sig_ag[p] = peer_sig_ag[p];
+  }
+  c.own_slot = static_cast<__nv_bfloat16*>(own_slot);
+  c.xg = static_cast<__nv_bfloat16*>(xg);
   c.x_local = static_cast<const __nv_bfloat16*>(x_local);
   c.ldx = k;
   c.sig_ag = sig_ag;
+  c.pub = pub;
+  c.pub_target = pub_base + unsigned(kCopyWarps * grid);
   c.ready = ready;
-  c.ready_target = ready_base + 2u * unsigned(grid);
+  c.ready_target = ready_base + unsigned(kCopyWarps * grid);
   if (w_mn) launch_fused<256, true, 1>(ta, ta2, tb, g, grid, st);
   else launch_fused<256, false, 1>(ta, ta2, tb, g, grid, st);
 }
 
 void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
-             int k, int rank, int tp, unsigned epoch, void* const* peer_recv, unsigned* const* peer_arrive,
-             unsigned* const* peer_sig_rs, unsigned* arrive, unsigned* sig_rs, unsigned arrive_base,
-             const void* recv_local, int grid, int* err, cudaStream_t st) {
+             int k, int rank, int tp, unsigned epoch, void* part_local, const void* const* peer_part,
+             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int grid, int* err,
+             cudaStream_t st) {
   RESIHP_CHECK(tp >= 2 && tp <= kMaxTp && t_rows % tp == 0 && (t_rows / tp) % kFBM == 0,
                "gemm_rs: rows per rank must be a multiple of 128");
   RESIHP_CHECK(n % 32 == 0 && k % 8 == 0, "gemm_rs: N must be a multiple of 32 and K of 8");
   const int tl = t_rows / tp;
-  const int bn = 256;
   CUtensorMap ta = make_tma_2d_bf16(h, t_rows, k, k, 64, kFBM);
-  CUtensorMap tb = w_mn ? make_tma_2d_bf16(w, k, n, ldw, 64, 64) : make_tma_2d_bf16(w, n, k, ldw, 64, bn);
+  CUtensorMap tb = w_mn ? make_tma_2d_bf16(w, k, n, ldw, 64, 64) : make_tma_2d_bf16(w, n, k, ldw, 64, 256);
   FusedArgs g{};
   g.c = y_local;
   g.ldc = ldy;
@@ -552,16 +540,14 @@ void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local
   c.tp = tp;
   c.rows_per_rank = tl;
   c.epoch = epoch;
+  c.part_local = static_cast<__nv_bfloat16*>(part_local);
   for (int p = 0; p < tp; ++p) {
-    c.peer_recv[p] = static_cast<__nv_bfloat16*>(peer_recv[p]);
-    c.peer_arrive[p] = peer_arrive[p];
-    c.peer_sig_rs[p] = peer_sig_rs[p];
+    c.peer_part[p] = static_cast<const __nv_bfloat16*>(peer_part[p]);
+    c.peer_flag[p] = peer_flag[p];
   }
-  c.arrive = arrive;
-  c.sig_rs = sig_rs;
-  c.recv_local = static_cast<__nv_bfloat16*>(const_cast<void*>(recv_local));
-  const int tiles_per_chunk = (tl / kFBM) * ((n + bn - 1) / bn);
-  c.arrive_target = arrive_base + 4u * unsigned(tiles_per_chunk);
+  c.flag_local = flag_local;
+  c.flag_target = 4u * epoch;  // four warp flags per tile per call
+  c.recv = static_cast<__nv_bfloat16*>(recv);
   if (w_mn) launch_fused<256, true, 2>(ta, ta, tb, g, grid, st);
   else launch_fused<256, false, 2>(ta, ta, tb, g, grid, st);
 }

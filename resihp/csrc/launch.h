@@ -82,16 +82,14 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
 namespace resihp {
 
 int fused_grid(int m, int n, int tp);
-void ag_publish(const void* x, void* slot, int64_t bytes, int rank, int tp, unsigned epoch, unsigned* sig_ag,
-                unsigned* const* peer_sig_ag, unsigned* done, unsigned done_base, int grid, int* err,
-                cudaStream_t st);
-void ag_gemm(const void* x_local, const void* xg, const void* const* peer_x, const void* w, int64_t ldw, bool w_mn,
-             void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp, unsigned epoch, unsigned* sig_ag,
+void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
+             int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
+             unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,
              unsigned* ready, unsigned ready_base, int grid, int* err, cudaStream_t st);
 void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
-             int k, int rank, int tp, unsigned epoch, void* const* peer_recv, unsigned* const* peer_arrive,
-             unsigned* const* peer_sig_rs, unsigned* arrive, unsigned* sig_rs, unsigned arrive_base,
-             const void* recv_local, int grid, int* err, cudaStream_t st);
+             int k, int rank, int tp, unsigned epoch, void* part_local, const void* const* peer_part,
+             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int grid, int* err,
+             cudaStream_t st);
 void* symm_alloc(int64_t bytes, void* handle_out);
 void* symm_open(const void* handle);
 void symm_close(void* p);

@@ -310,61 +310,52 @@ void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
 
 int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
 
-void ag_publish_t(torch::Tensor x, int64_t slot, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
-                  std::vector<int64_t> peer_sig_ag, int64_t done, int64_t done_base, int64_t grid) {
-  check_cuda_bf16(x, "x");
-  TORCH_CHECK(x.is_contiguous(), "published chunk must be contiguous");
-  c10::cuda::CUDAGuard guard(x.device());
-  std::vector<unsigned*> peers;
-  for (auto v : peer_sig_ag) peers.push_back(as_ptr<unsigned>(v));
-  ag_publish(x.data_ptr(), as_ptr<void>(slot), x.numel() * 2, int(rank), int(tp), unsigned(epoch),
-             as_ptr<unsigned>(sig_ag), peers.data(), as_ptr<unsigned>(done), unsigned(done_base), int(grid),
-             error_word(x.device()), cur_stream());
-}
-
-void ag_gemm_t(torch::Tensor x_local, torch::Tensor xg, std::vector<int64_t> peer_x, torch::Tensor w, bool w_mn,
-               torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag, int64_t ready,
-               int64_t ready_base, int64_t grid) {
+void ag_gemm_t(torch::Tensor x_local, int64_t own_slot, std::vector<int64_t> peer_slot, torch::Tensor xg,
+               torch::Tensor w, bool w_mn, torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
+               std::vector<int64_t> peer_sig_ag, int64_t pub, int64_t pub_base, int64_t ready, int64_t ready_base,
+               int64_t grid) {
   check_cuda_bf16(x_local, "x_local");
   check_cuda_bf16(xg, "xg");
   check_cuda_bf16(w, "w");
   check_cuda_bf16(y, "y");
   TORCH_CHECK(x_local.is_contiguous() && xg.is_contiguous() && y.is_contiguous() && w.stride(1) == 1,
               "fused AG-GEMM tensors must be contiguous");
+  TORCH_CHECK(int64_t(peer_slot.size()) == tp && int64_t(peer_sig_ag.size()) == tp, "one entry per rank");
   const int64_t k = x_local.size(1);
   const int64_t t = xg.size(0);
   const int64_t n = y.size(1);
   TORCH_CHECK(xg.size(1) == k && y.size(0) == t && x_local.size(0) * tp == t, "fused AG-GEMM shapes");
   TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused AG-GEMM weight");
   c10::cuda::CUDAGuard guard(x_local.device());
-  std::vector<const void*> peers;
-  for (auto v : peer_x) peers.push_back(as_ptr<const void>(v));
-  ag_gemm(x_local.data_ptr(), xg.data_ptr(), peers.data(), w.data_ptr(), w.stride(0), w_mn, y.data_ptr(), y.stride(0),
-          int(t), int(n), int(k), int(rank), int(tp), unsigned(epoch), as_ptr<unsigned>(sig_ag),
-          as_ptr<unsigned>(ready), unsigned(ready_base), int(grid), error_word(x_local.device()), cur_stream());
+  std::vector<const void*> slots;
+  std::vector<unsigned*> sigs;
+  for (auto v : peer_slot) slots.push_back(as_ptr<const void>(v));
+  for (auto v : peer_sig_ag) sigs.push_back(as_ptr<unsigned>(v));
+  ag_gemm(x_local.data_ptr(), as_ptr<void>(own_slot), slots.data(), xg.data_ptr(), w.data_ptr(), w.stride(0), w_mn,
+          y.data_ptr(), y.stride(0), int(t), int(n), int(k), int(rank), int(tp), unsigned(epoch),
+          as_ptr<unsigned>(sig_ag), sigs.data(), as_ptr<unsigned>(pub), unsigned(pub_base), as_ptr<unsigned>(ready),
+          unsigned(ready_base), int(grid), error_word(x_local.device()), cur_stream());
 }
 
 void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_local, int64_t rank, int64_t tp,
-               int64_t epoch, std::vector<int64_t> peer_recv, std::vector<int64_t> peer_arrive,
-               std::vector<int64_t> peer_sig_rs, int64_t arrive, int64_t sig_rs, int64_t arrive_base,
-               int64_t recv_local, int64_t grid) {
+               int64_t epoch, int64_t part_local, std::vector<int64_t> peer_part, int64_t flag_local,
+               std::vector<int64_t> peer_flag, int64_t recv, int64_t grid) {
   check_cuda_bf16(h, "h");
   check_cuda_bf16(w, "w");
   check_cuda_bf16(y_local, "y_local");
   TORCH_CHECK(h.is_contiguous() && y_local.is_contiguous() && w.stride(1) == 1, "fused GEMM-RS tensors must be contiguous");
+  TORCH_CHECK(int64_t(peer_part.size()) == tp && int64_t(peer_flag.size()) == tp, "one entry per rank");
   const int64_t t = h.size(0), k = h.size(1), n = y_local.size(1);
   TORCH_CHECK(y_local.size(0) * tp == t, "fused GEMM-RS shapes");
   TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused GEMM-RS weight");
   c10::cuda::CUDAGuard guard(h.device());
-  std::vector<void*> recv;
-  std::vector<unsigned*> arr, sig;
-  for (auto v : peer_recv) recv.push_back(as_ptr<void>(v));
-  for (auto v : peer_arrive) arr.push_back(as_ptr<unsigned>(v));
-  for (auto v : peer_sig_rs) sig.push_back(as_ptr<unsigned>(v));
+  std::vector<const void*> parts;
+  std::vector<const unsigned*> flags;
+  for (auto v : peer_part) parts.push_back(as_ptr<const void>(v));
+  for (auto v : peer_flag) flags.push_back(as_ptr<const unsigned>(v));
   gemm_rs(h.data_ptr(), w.data_ptr(), w.stride(0), w_mn, y_local.data_ptr(), y_local.stride(0), int(t), int(n), int(k),
-          int(rank), int(tp), unsigned(epoch), recv.data(), arr.data(), sig.data(), as_ptr<unsigned>(arrive),
-          as_ptr<unsigned>(sig_rs), unsigned(arrive_base), as_ptr<const void>(recv_local), int(grid),
-          error_word(h.device()), cur_stream());
+          int(rank), int(tp), unsigned(epoch), as_ptr<void>(part_local), parts.data(), as_ptr<unsigned>(flag_local),
+          flags.data(), as_ptr<void>(recv), int(grid), error_word(h.device()), cur_stream());
 }
 
 }  // namespace resihp
@@ -393,7 +384,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &resihp::symm_close_t);
   m.def("symm_free", &resihp::symm_free_t);
   m.def("fused_grid", &resihp::fused_grid_t);
-  m.def("ag_publish", &resihp::ag_publish_t);
   m.def("ag_gemm", &resihp::ag_gemm_t);
   m.def("gemm_rs", &resihp::gemm_rs_t);
 }

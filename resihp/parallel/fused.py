@@ -10,8 +10,10 @@
 Both replace the NCCL pair ``gather_tokens`` / ``scatter_tokens`` of
 :mod:`resihp.parallel.collectives` (the baseline). They exchange data through a
 :class:`SymmetricWorkspace` per TP group: one CUDA-IPC-shared region per rank holding
-the cross-GPU flags and counters, two publish slots for the AG input and two receive
-slots per source for the RS partials. Nothing in the workspace is multicast.
+the cross-GPU flag words, two publish slots for the AG input and two partial buffers
+for the RS (alternating by call parity), plus a local receive buffer. Peers only ever
+read each other's regions (P2P loads) and write each other's flag words; nothing in the
+workspace is multicast.
 
 All ranks of a TP group issue their fused calls in the same order (they follow the same
 model code), which is what the epoch counters rely on.
@@ -44,11 +46,20 @@ def _debug_check(what: str, device) -> None:
     sys.stderr.flush()
     if code:
         raise RuntimeError(f"fused {what} reported error code {code}")
-_FLAG_BYTES = 256  # sig_ag[8] | sig_rs[8] | arrive[8] | ready[8] | done | pad
+
+
+_MAX_TILES = 8192             # per-tile flags of the RS partial buffer
+_FLAG_BYTES = 4096 + 4 * _MAX_TILES
 
 
 class SymmetricWorkspace:
-    """This rank's IPC-shared region and its mappings of every peer's region."""
+    """This rank's IPC-shared region and its mappings of every peer's region.
+
+    Layout (bytes): flag words | two AG publish slots ``[T/tp, width]`` | two RS partial
+    buffers ``[T, width]`` | one RS receive buffer ``[tp, T/tp, width]``. The AG input and
+    the RS output of every fused call have the model width, so one region serves all four
+    projections of a layer and their backward passes.
+    """
 
     def __init__(self, group, rows_per_rank: int, width: int, device):
         k = _ext.require()
@@ -57,13 +68,18 @@ class SymmetricWorkspace:
         self.rank = dist.get_rank(group)
         if self.tp > 8:
             raise ValueError("fused TP collectives support up to 8 ranks")
+        t = rows_per_rank * self.tp
+        if (t // 128) * ((width + 255) // 256) > _MAX_TILES:
+            raise ValueError("fused TP workspace: too many output tiles")
         self.rows_per_rank = rows_per_rank
         self.width = width
         self.device = torch.device(device)
         self.slot_bytes = rows_per_rank * width * 2
-        self.x_off = _FLAG_BYTES
-        self.recv_off = self.x_off + 2 * self.slot_bytes
-        self.total = self.recv_off + 2 * self.tp * self.slot_bytes
+        self.part_bytes = t * width * 2
+        self.slot_off = _FLAG_BYTES
+        self.part_off = self.slot_off + 2 * self.slot_bytes
+        self.recv_off = self.part_off + 2 * self.part_bytes
+        self.total = self.recv_off + self.tp * self.slot_bytes
         with torch.cuda.device(self.device):
             self.base, handle = k.symm_alloc(self.total)
             torch.cuda.synchronize()
@@ -76,32 +92,28 @@ class SymmetricWorkspace:
         dist.barrier(group=group)
         self.ag_epoch = 0
         self.rs_epoch = 0
+        self.pub_base = 0
         self.ready_base = 0
-        self.done_base = 0
-        self.arrive_base = 0
         self.closed = False
 
     # flag words (u32) inside a region
     def _sig_ag(self, base):
         return base
 
-    def _sig_rs(self, base):
-        return base + 32
-
-    def _arrive(self, base):
+    def _pub(self, base):
         return base + 64
 
     def _ready(self, base):
-        return base + 96
-
-    def _done(self, base):
         return base + 128
 
-    def x_slot(self, base, epoch):
-        return base + self.x_off + (epoch % 2) * self.slot_bytes
+    def _tile_flags(self, base):
+        return base + 4096
 
-    def recv_slot(self, base, epoch):
-        return base + self.recv_off + (epoch % 2) * self.tp * self.slot_bytes
+    def _slot(self, base, epoch):
+        return base + self.slot_off + (epoch % 2) * self.slot_bytes
+
+    def _part(self, base, epoch):
+        return base + self.part_off + (epoch % 2) * self.part_bytes
 
     def fits(self, rows: int, width: int) -> bool:
         return rows == self.rows_per_rank * self.tp and width == self.width
@@ -114,18 +126,15 @@ class SymmetricWorkspace:
         self.ag_epoch += 1
         e = self.ag_epoch
         x_local = x_local.contiguous()
-        grid = min(148, max(1, x_local.numel() * 2 // (1 << 20)))
-        k.ag_publish(x_local, self.x_slot(self.base, e), self.rank, self.tp, e, self._sig_ag(self.base),
-                     [self._sig_ag(p) for p in self.peers], self._done(self.base), self.done_base, grid)
-        self.done_base += grid
-        _debug_check(f"ag_publish epoch {e}", x_local.device)
         t = x_local.shape[0] * self.tp
         xg = torch.empty((t, x_local.shape[1]), dtype=x_local.dtype, device=x_local.device)
         y = torch.empty((t, n), dtype=x_local.dtype, device=x_local.device)
-        ggrid = k.fused_grid(t, n, self.tp)
-        k.ag_gemm(x_local, xg, [self.x_slot(p, e) for p in self.peers], w, w_mn, y, self.rank, self.tp, e,
-                  self._sig_ag(self.base), self._ready(self.base), self.ready_base, ggrid)
-        self.ready_base += 2 * ggrid
+        grid = k.fused_grid(t, n, self.tp)
+        k.ag_gemm(x_local, self._slot(self.base, e), [self._slot(p, e) for p in self.peers], xg, w, w_mn, y,
+                  self.rank, self.tp, e, self._sig_ag(self.base), [self._sig_ag(p) for p in self.peers],
+                  self._pub(self.base), self.pub_base, self._ready(self.base), self.ready_base, grid)
+        self.pub_base += 4 * grid
+        self.ready_base += 4 * grid
         _debug_check(f"ag_gemm epoch {e}", x_local.device)
         return y, xg
 
@@ -138,12 +147,9 @@ class SymmetricWorkspace:
         t = h.shape[0]
         y = torch.empty((t // self.tp, n), dtype=h.dtype, device=h.device)
         grid = k.fused_grid(t, n, self.tp)
-        k.gemm_rs(h, w, w_mn, y, self.rank, self.tp, e, [self.recv_slot(p, e) for p in self.peers],
-                  [self._arrive(p) for p in self.peers], [self._sig_rs(p) for p in self.peers],
-                  self._arrive(self.base), self._sig_rs(self.base), self.arrive_base,
-                  self.recv_slot(self.base, e), grid)
-        tiles_per_chunk = (self.rows_per_rank // 128) * ((n + 255) // 256)
-        self.arrive_base += 4 * tiles_per_chunk
+        k.gemm_rs(h, w, w_mn, y, self.rank, self.tp, e, self._part(self.base, e),
+                  [self._part(p, e) for p in self.peers], self._tile_flags(self.base),
+                  [self._tile_flags(p) for p in self.peers], self.base + self.recv_off, grid)
         _debug_check(f"gemm_rs epoch {e}", h.device)
         return y
 
@@ -151,9 +157,9 @@ class SymmetricWorkspace:
         """Unmap the peers' regions and free this one.
 
         Every rank of the group must have finished its fused kernels first -- a peer may
-        still be reading this rank's slots -- so by default the group synchronises before
-        anything is unmapped. At a fail-stop safe point (``barrier=False``) no kernel is
-        in flight anywhere and the dead peer cannot take part in a barrier.
+        still be reading this rank's buffers -- so by default the group synchronises
+        before anything is unmapped. At a fail-stop safe point (``barrier=False``) no
+        kernel is in flight anywhere and the dead peer cannot take part in a barrier.
         """
         if self.closed:
             return

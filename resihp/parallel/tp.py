@@ -38,6 +38,7 @@ from ..config import TrainConfig
 from ..models.layout import TensorSpec, local_shape, stage_specs
 from ..ops import functional as fn
 from . import collectives as cc
+from . import fused
 
 _ALIGN = 64  # elements: keeps every tensor 256-byte aligned for TMA
 
@@ -149,6 +150,11 @@ class TensorParallelStage:
             self.install_moments(moments)
         self.flat.refresh_work()
         self._bind_compute_tensors()
+        self.ws = None
+        rows = config.micro_batch_size * config.seq_len
+        if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= 8
+                and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0):
+            self.ws = fused.SymmetricWorkspace(group, rows // self.tp_size, self.dim, self.device)
         self.rope = None
         if config.arch == "llama":
             self.rope = fn.rope_table(config.seq_len, config.head_dim, config.rope_theta, device=self.device)
@@ -234,6 +240,24 @@ class TensorParallelStage:
         tokens = micro_batch_size * self.sequence_length
         return (tokens // self.tp_size if self.sp else tokens, self.dim)
 
+    def close_comm(self, *, barrier: bool = True) -> None:
+        """Release the peer-memory workspace (at a safe point, with nothing in flight)."""
+        if self.ws is not None:
+            self.ws.close(barrier=barrier)
+            self.ws = None
+
+    def _col_linear(self, h, w, g):
+        """Column-parallel linear; under SP the token all-gather is fused into the GEMM."""
+        if self.ws is not None:
+            return fused.ag_linear(h, w, g, self.ws)
+        return fn.linear(self._col_input(h), w, g)
+
+    def _row_linear(self, x, w, g):
+        """Row-parallel linear; under SP the token reduce-scatter is fused into the GEMM."""
+        if self.ws is not None:
+            return fused.linear_rs(x, w, g, self.ws)
+        return self._row_output(fn.linear(x, w, g))
+
     def _col_input(self, h):
         return cc.gather_tokens(h, self.group) if self.sp else cc.copy_to_tp(h, self.group)
 
@@ -256,14 +280,13 @@ class TensorParallelStage:
         hq, hkv = c.num_heads // self.tp_size, c.kv_heads // self.tp_size
         h, _ = fn.rmsnorm(x, self.w[p + "attn_norm.weight"], c.norm_eps, self.g[p + "attn_norm.weight"])
         wqkv, gqkv = self.fused_w[p + "qkv"]
-        qkv = fn.linear(self._col_input(h), wqkv, gqkv)
+        qkv = self._col_linear(h, wqkv, gqkv)
         o = fn.rope_attention(qkv, self.rope, c.seq_len, hq, hkv, c.head_dim)
-        a = self._row_output(fn.linear(o, self.w[p + "attn.o_proj.weight"], self.g[p + "attn.o_proj.weight"]))
+        a = self._row_linear(o, self.w[p + "attn.o_proj.weight"], self.g[p + "attn.o_proj.weight"])
         h, x = fn.rmsnorm(a, self.w[p + "mlp_norm.weight"], c.norm_eps, self.g[p + "mlp_norm.weight"], residual=x)
         wgu, ggu = self.fused_w[p + "gate_up"]
-        gu = fn.linear(self._col_input(h), wgu, ggu)
-        m = fn.linear(fn.swiglu(gu), self.w[p + "mlp.down.weight"], self.g[p + "mlp.down.weight"])
-        return x + self._row_output(m)
+        gu = self._col_linear(h, wgu, ggu)
+        return x + self._row_linear(fn.swiglu(gu), self.w[p + "mlp.down.weight"], self.g[p + "mlp.down.weight"])
 
     def _gpt2_layer(self, x, gid):
         p = f"layers.{gid}."
@@ -288,9 +311,11 @@ class TensorParallelStage:
             h = fn.layernorm(x, self.w["final_norm.weight"], self.w["final_norm.bias"])
         else:
             h, _ = fn.rmsnorm(x, self.w["final_norm.weight"], c.norm_eps, self.g["final_norm.weight"])
-        h = self._col_input(h) if c.arch == "llama" else cc.copy_to_tp(h, self.group)
         head = "token_embedding.weight" if c.tied_embeddings else "lm_head.weight"
-        logits = fn.linear(h, self.w[head], self.g[head])
+        if c.arch == "llama":
+            logits = self._col_linear(h, self.w[head], self.g[head])
+        else:
+            logits = fn.linear(cc.copy_to_tp(h, self.group), self.w[head], self.g[head])
         labels = torch.full_like(tokens, -1)
         labels[:, :-1] = tokens[:, 1:]
         return fn.vocab_parallel_cross_entropy(
