@@ -1,0 +1,122 @@
+#!/usr/bin/env python
+"""Fail-stop recovery benchmark: recovery seconds and tokens/s around kills.
+
+Runs the real launcher (``python -m resihp.launch``) on the config-2 model -- Llama-style
+1.3B, bf16 with FP32 master weights and AdamW, TP2 x PP2 x DP2 on 8 GPUs, sequence 2048,
+micro-batch 2, global batch 64, synthetic seeded tokens -- with a failure schedule that
+SIGKILLs GPU 5 after step 30 and GPU 2 after step 60. Each fail-stop is detected through
+the launcher's store, replanned by the memory-aware planner (180 GB budget per GPU),
+and the parameters plus AdamW state move to their new owners peer to peer; no checkpoint
+is needed because every lost shard survives on a peer replica. (Without a peer replica,
+DP = 1, the checkpoint is committed every step, as the reference does.)
+
+Prints one JSON line: per event the recovery time (failure -> end of the first resumed
+step, max over surviving ranks) with its phases, and tokens/s of the steps before and
+after each event.
+
+    python bench_recovery.py [--gpus 8] [--kills 30:5,60:2] [--iterations 70]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+MODEL = dict(model_dim=2048, num_layers=24, num_heads=16, ffn_dim=5504, vocab_size=32000, seq_len=2048)
+LAYOUTS = {2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 2, 2)}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=8)
+    p.add_argument("--kills", default="30:5,60:2", help="after_iteration:rank,...")
+    p.add_argument("--iterations", type=int, default=70)
+    p.add_argument("--timeout", type=float, default=1500)
+    p.add_argument("--small", action="store_true", help="a 4-layer model (quick check)")
+    p.add_argument("--checkpoint-every", type=int, default=None,
+                   help="commit the logical checkpoint every N steps (default: every step without a peer "
+                        "replica, never with one)")
+    return p.parse_args()
+
+
+def main():
+    args = parse()
+    tp, pp, dp = LAYOUTS[args.gpus]
+    model = dict(MODEL)
+    if args.small:
+        model.update(num_layers=4, model_dim=1024, num_heads=8, ffn_dim=2752, seq_len=1024)
+    config = dict(
+        **model, batch_size=64, micro_batch_size=2, seed=1, tp=tp, pp=pp, dp=dp, iterations=args.iterations,
+        arch="llama", dtype="bf16", sequence_parallel=True, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95,
+        weight_decay=0.1, memory_budget_bytes=180 * 10**9,
+        checkpoint_every=args.checkpoint_every or (1 if dp == 1 else 1_000_000),
+    )
+    kills = [tuple(int(x) for x in k.split(":")) for k in args.kills.split(",") if k]
+    failures = {"events": [{"after_iteration": a, "failed_rank": r} for a, r in kills]}
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg_path = os.path.join(tmp, "train.json")
+        fail_path = os.path.join(tmp, "failures.json")
+        with open(cfg_path, "w") as f:
+            json.dump(config, f)
+        with open(fail_path, "w") as f:
+            json.dump(failures, f)
+        env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", RESIHP_CHECKPOINT=os.path.join(tmp, "ck.pt"))
+        env.setdefault("RESIHP_GROUP_TIMEOUT", "120")
+        out = subprocess.run(
+            [sys.executable, "-m", "resihp.launch", "--config", cfg_path, "--failures", fail_path,
+             "--timeout", str(args.timeout)],
+            cwd=tmp, env=env, capture_output=True, text=True, timeout=args.timeout + 120,
+        )
+    lines = []
+    for line in out.stdout.splitlines():
+        if line.startswith("{"):
+            try:
+                lines.append(json.loads(line))
+            except json.JSONDecodeError:
+                pass
+    launch = next((l["launch"] for l in lines if "launch" in l), None)
+    steps: dict[int, list] = {}
+    for l in lines:
+        if "step" in l:
+            steps.setdefault(l["step"], []).append(l["step_s"])
+    tokens = config["batch_size"] * config["seq_len"]
+    step_rate = {it: tokens / max(v) for it, v in steps.items()}
+    events = []
+    for a, r in kills:
+        rec = [l["recovery"] for l in lines if "recovery" in l and l["recovery"]["after_iteration"] == a]
+        if not rec:
+            events.append({"after_iteration": a, "failed_rank": r, "recovered": False})
+            continue
+        worst = max(rec, key=lambda x: x["seconds"])
+        before = [step_rate[i] for i in range(max(2, a - 5), a + 1) if i in step_rate]
+        after = [step_rate[i] for i in range(a + 2, a + 8) if i in step_rate]
+        events.append({
+            "after_iteration": a, "failed_rank": r, "recovered": True,
+            "recovery_s": round(worst["seconds"], 3), "safe_point_s": round(worst["safe_point_s"], 3),
+            "first_resumed_step_s": round(worst.get("first_step_s", 0.0), 3),
+            "phases_s": {k: round(v, 3) for k, v in worst["phases"].items()},
+            "plan_version": worst["plan_version"],
+            "tokens_per_s_before": round(statistics.median(before), 1) if before else None,
+            "tokens_per_s_after": round(statistics.median(after), 1) if after else None,
+        })
+    print(json.dumps({
+        "metric": "fail-stop recovery seconds (failure -> end of first resumed step, max over survivors)",
+        "n_gpus": args.gpus, "config": {"model": "llama-1.3b" if not args.small else "llama-small",
+                                        "parallelism": f"tp{tp}-pp{pp}-dp{dp}-sp", "dtype": "bf16",
+                                        "global_batch": 64, "seq_len": config["seq_len"]},
+        "events": events, "launch": launch, "launcher_rc": out.returncode,
+        "stopped": [l for l in lines if "stopped" in l],
+        "steps_seen": sorted(steps),
+        "recovery_lines": [l["recovery"] for l in lines if "recovery" in l][:4],
+        "stderr_tail": out.stderr[-1500:] if out.returncode else "",
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

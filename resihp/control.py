@@ -103,8 +103,24 @@ class ControlPlane:
 
     # --- detection / world ---------------------------------------------------------
 
+    def quiesce(self) -> None:
+        """Wait until this rank's GPU has finished everything it was given.
+
+        CUDA work -- NCCL collectives included -- is asynchronous, so a rank can reach the
+        end of an iteration on the host while its last collective is still queued on the
+        device. A fail-stop must find nothing in flight (a rank killed with a collective
+        half issued would leave its peers' streams waiting for it), so the iteration ends
+        here, on every rank, before the kill point and before the boundary rendezvous.
+        A completed collective on this rank implies every peer has joined it as well.
+        """
+        import torch
+
+        if self.device is not None and torch.device(self.device).type == "cuda":
+            torch.cuda.synchronize(self.device)
+
     def observe(self) -> tuple[int, ...]:
         """Safe-point steps 3-4: arrive at the next boundary; the ranks that did not."""
+        self.quiesce()
         self.boundary += 1
         published = membership.boundary(self.store, self.boundary, timeout=GROUP_TIMEOUT)
         return tuple(r for r in self.members if r not in published)

@@ -329,30 +329,56 @@ def _anchor_slices(config, route, anchor, rank):
     return out
 
 
-def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: TrainingGroups, device=None, pin=False):
-    """Safe-point step 7: execute ``plan``'s state routes; returns ``(run, state digest)``.
+def _load_anchor(checkpoint_path):
+    """``(anchor, completed_steps, digest)`` of a checkpoint, ``None`` if there is none."""
+    from pathlib import Path
 
-    Every surviving rank calls this (the idle ones too: their shards may be donors).
-    """
-    config = plan.config
+    if checkpoint_path is None or not Path(checkpoint_path).exists():
+        return None
     payload = read_payload(checkpoint_path)
     verify_digest(payload)
-    completed = payload["completed_steps"]
     anchor = {}
     for name, param in payload["params"].items():
         entry = {"param": param}
         if name in payload["optim"]:
             entry.update(payload["optim"][name])
         anchor[name] = entry
-    stage = stage_of(plan, rank)
-    local = {} if run is None else run.local_state()
+    return anchor, payload["completed_steps"], payload["digest"]
+
+
+def state_fingerprint(run) -> str:
+    """Cheap, deterministic fingerprint of one rank's shards (computed on its device)."""
+    if run is None:
+        return ""
+    st = run.stage
+    sums = []
+    for buf in (st.flat.master, st.flat.exp_avg, st.flat.exp_avg_sq):
+        b = buf.double()
+        sums += [float(b.sum()), float(b.abs().sum()), float((b * b).sum())]
+    return sha256(repr((st.flat.step, [f"{x:.17g}" for x in sums])).encode("utf-8")).hexdigest()
+
+
+def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: TrainingGroups, device=None, pin=False):
+    """Safe-point step 7: execute ``plan``'s state routes; returns ``(run, state digest)``.
+
+    Every surviving rank calls this (the idle ones too: their shards may be donors).
+    The checkpoint is read only when some route needs it or when it is current, in which
+    case it is also the A1 oracle; otherwise the agreed digest covers every rank's shard
+    fingerprint.
+    """
+    config = plan.config
     needs_checkpoint = any(r.donor_kind == "checkpoint" for r in plan.state_routes)
-    rollback = completed != cursor and needs_checkpoint
+    loaded = _load_anchor(checkpoint_path)
+    if loaded is None and needs_checkpoint:
+        raise CheckpointError(f"checkpoint missing: {checkpoint_path}")
+    anchor, completed, ck_digest = loaded if loaded is not None else ({}, None, None)
+    current = completed == cursor
+    rollback = needs_checkpoint and not current
+    stage = stage_of(plan, rank)
+    local = {} if run is None or rollback else run.local_state()
     tdev = torch.device("cpu") if device is None else torch.device(device)
 
     acquired: dict[str, dict] = {}
-    if rollback:
-        local = {}
     for route in plan.state_routes:
         if route.donor_kind == "checkpoint" or rollback:
             if rank in route.target_ranks:
@@ -380,20 +406,17 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
         new_run = PlannedRun(
             plan, rank=rank, local_state={n: f["param"] for n, f in state.items()},
             moments={n: f for n, f in state.items() if "exp_avg" in f}, groups=groups, device=device,
-            cursor=completed if (rollback or completed == cursor) else cursor, pin=pin,
+            cursor=completed if rollback else cursor, pin=pin,
         )
 
-    if completed == cursor or rollback:
+    if current or rollback:
         if new_run is not None:
             problems = checkpoint_mismatches(new_run, plan=plan, rank=rank, anchor=anchor)
             if problems:
                 raise ReshardError(f"rank {rank} state differs from the checkpoint: {problems[:5]}")
-        return new_run, payload["digest"]
-    mine = "" if new_run is None else digest_tensors(sorted(
-        (f"{n}.{k}", v) for n, e in new_run.local_state().items() for k, v in e.items() if torch.is_tensor(v)
-    ))
+        return new_run, ck_digest
     gathered = [None] * dist.get_world_size(groups.world)
-    dist.all_gather_object(gathered, (rank, mine), group=groups.world)
+    dist.all_gather_object(gathered, (rank, state_fingerprint(new_run)), group=groups.world)
     return new_run, sha256(repr(sorted(gathered)).encode("utf-8")).hexdigest()
 
 

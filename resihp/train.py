@@ -77,6 +77,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
     control.attach_run(initial_run(plan, rank=control.rank, groups=groups, device=device),
                        checkpoint_path=checkpoint_path, device=device)
     failed: tuple[int, ...] = ()
+    pending_recovery = None
     trained: list[int] = []
     versions = [plan.version]
     digests = [plan.digest]
@@ -94,8 +95,15 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
             if loss is not None:
                 _emit({"step": iteration, "rank": control.rank, "loss": loss, "plan_version": plan.version,
                        "step_s": dt, "tokens_per_s": tokens_per_step / dt if dt > 0 else None})
+            if pending_recovery is not None:
+                # failure -> end of the first resumed step, as seen by this rank
+                pending_recovery["seconds"] = time.perf_counter() - pending_recovery.pop("t_fail")
+                pending_recovery["first_step_s"] = dt
+                _emit({"recovery": pending_recovery})
+                pending_recovery = None
             if iteration % config.checkpoint_every == 0:
                 control.commit_checkpoint(plan, cursor=iteration)
+            control.quiesce()  # the iteration, its commit and all their GPU work are complete
             fail_stop(schedule, control.rank, iteration)
             t_fail = time.perf_counter()
             lost = control.observe()
@@ -103,9 +111,14 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
                 plan, failed = control.safe_point(config, plan, failed, lost, next_step=iteration)
                 versions.append(plan.version)
                 digests.append(plan.digest)
-                _emit({"recovery": {"rank": control.rank, "event": len(versions) - 1, "lost": list(lost),
-                                    "plan_version": plan.version, "seconds": time.perf_counter() - t_fail,
-                                    "phases": control.last_recovery}})
+                pending_recovery = {"rank": control.rank, "event": len(versions) - 1, "lost": list(lost),
+                                    "after_iteration": iteration, "plan_version": plan.version,
+                                    "safe_point_s": time.perf_counter() - t_fail,
+                                    "phases": control.last_recovery, "t_fail": t_fail}
+        if pending_recovery is not None:
+            pending_recovery.pop("t_fail")
+            pending_recovery["seconds"] = pending_recovery["safe_point_s"]
+            _emit({"recovery": pending_recovery})
     except ConsistentStop as stop:
         _emit({"stopped": stop.reason.code, "reason": stop.reason.message})
         control.shutdown()
