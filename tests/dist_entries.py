@@ -126,3 +126,28 @@ def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir):
             losses[str(it)] = loss
     write_result(out_dir, rank, {"rank": plan_rank, "losses": losses, "plan": plan.digest})
     cp.shutdown()
+
+
+def a2_entry(rank, env, config_dict, anchor_path, start, out_dir):
+    """Resume a TP run from an anchor, take one step, compare shards to the A2 oracle."""
+    _setup(env)
+    from harness import write_result
+    from resihp import verify
+    from resihp.checkpoint import load_anchor
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import run_from_anchor
+
+    config = TrainConfig(**config_dict)
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=start, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    anchor, completed = load_anchor(anchor_path)
+    run = run_from_anchor(plan, rank=rank, anchor=anchor, completed=completed, groups=groups)
+    a1 = verify.matches_checkpoint(run, plan=plan, rank=rank, checkpoint_path=anchor_path)
+    run.step()
+    record = verify.steps_from_anchor(config, anchor, start=completed, count=1)[0]
+    cmp = verify.compare_shards(run.stage, record, lr=config.lr)
+    write_result(out_dir, rank, {"rank": rank, "a1": a1, "cmp": cmp})
+    cp.shutdown()
