@@ -49,6 +49,14 @@ struct AttnArgs {
   int* err;
 };
 
+// 2^x with the hardware approximation (one MUFU instruction; relative error ~2^-22,
+// far below the bf16 rounding P and dS go through next).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Byte offset of bf16 element (r, c) in a K-major 128B-swizzled tile made of 64-column
 // chunks of `rows` rows each.
 __device__ __forceinline__ uint32_t sw128_offset(int r, int c, int rows) {
@@ -206,20 +214,21 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const bool diag = j == qblk;
       const uint32_t t_s = tmem + sb * kBlk + lane_off;
-      // pass 1: row max (raw scores)
+      // the whole S row in registers: four 32-column loads, one wait
+      uint32_t v[kBlk];
+      #pragma unroll
+      for (int c = 0; c < kBlk; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+      tmem_wait_ld();
       float mx = m;
-      #pragma unroll 1
-      for (int c = 0; c < kBlk; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_s + c, v);
-        tmem_wait_ld();
+      if (diag) {
         #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float s = __uint_as_float(v[e]);
-          if (!diag || c + e <= r) mx = fmaxf(mx, s);
-        }
+        for (int e = 0; e < kBlk; ++e)
+          if (e <= r) mx = fmaxf(mx, __uint_as_float(v[e]));
+      } else {
+        #pragma unroll
+        for (int e = 0; e < kBlk; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
       }
-      const float alpha = exp2f((m - mx) * sl2);   // 0 on the first block (m = -inf)
+      const float alpha = fast_exp2((m - mx) * sl2);   // 0 on the first block (m = -inf)
       const float neg = mx * sl2;
       // P smem is still being read by PV_{j-1}: wait for it before overwriting
       if (j > 0) {
@@ -227,22 +236,17 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
       }
       float rowsum = 0.f;
-      #pragma unroll 1
+      #pragma unroll
       for (int c = 0; c < kBlk; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_s + c, v);
-        tmem_wait_ld();
         uint32_t pk[16];
         #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = exp2f(__uint_as_float(v[e]) * sl2 - neg);
-          float p1 = exp2f(__uint_as_float(v[e + 1]) * sl2 - neg);
+          float p0 = fast_exp2(fmaf(__uint_as_float(v[c + e]), sl2, -neg));
+          float p1 = fast_exp2(fmaf(__uint_as_float(v[c + e + 1]), sl2, -neg));
           if (diag && c + e > r) p0 = 0.f;
           if (diag && c + e + 1 > r) p1 = 0.f;
-          __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-          const float2 pr = __bfloat1622float2(pb);   // sum what the MMA will see
-          rowsum += pr.x + pr.y;
-          pk[e / 2] = *reinterpret_cast<uint32_t*>(&pb);
+          rowsum += p0 + p1;
+          pk[e / 2] = pack_bf16(p0, p1);
         }
         store_row32(sp, r, c, pk, kBlk);
       }
@@ -478,7 +482,7 @@ __global__ void __launch_bounds__(192, 1)
           #pragma unroll
           for (int z = 0; z < 2; ++z) {
             const int qr = c + e + z;      // q row within the q tile
-            float pv = exp2f(__uint_as_float(sv32[e + z]) * sl2 - s_lse[qr]);
+            float pv = fast_exp2(fmaf(__uint_as_float(sv32[e + z]), sl2, -s_lse[qr]));
             if (diag && qr < c_row) pv = 0.f;
             p[z] = pv;
             ds[z] = pv * (__uint_as_float(dv32[e + z]) - s_delta[qr]);
@@ -671,7 +675,7 @@ __global__ void __launch_bounds__(192, 1)
           float ds[2];
           #pragma unroll
           for (int z = 0; z < 2; ++z) {
-            float pv = exp2f(__uint_as_float(s32[e + z]) * sl2 - lse2);
+            float pv = fast_exp2(fmaf(__uint_as_float(s32[e + z]), sl2, -lse2));
             if (diag && c + e + z > r) pv = 0.f;
             ds[z] = pv * (__uint_as_float(p32[e + z]) - dlt);
           }
