@@ -11,6 +11,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "launch.h"
+
 namespace resihp {
 
 // Wait budget for one barrier phase. Generous on purpose: a healthy wait is
@@ -229,6 +231,50 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- cross-GPU flag words (system scope) ---------------------------------------------
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait until *p >= target (wrap-safe); false + error code when the budget runs out.
+__device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int* err, int code) {
+  const uint64_t start = globaltimer();
+  #pragma unroll 1
+  while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
+    if (globaltimer() - start > kWaitBudgetNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- AdamW, one element (torch.optim.AdamW's formulation) -----------------------------
+// Shared by the stand-alone optimizer kernel and the fused DP-reduce + AdamW kernel, so
+// both paths round identically.
+__device__ __forceinline__ void adamw_elem(float& p, float& m, float& v, float g, const AdamWCoef& c) {
+  const float gi = g * c.grad_scale;
+  float pi = p * (1.f - c.lr * c.wd);
+  const float mi = m + (1.f - c.b1) * (gi - m);
+  const float vi = c.b2 * v + (1.f - c.b2) * gi * gi;
+  const float denom = sqrtf(vi) / c.bc2_sqrt + c.eps;
+  pi = pi - c.step_size * (mi / denom);
+  p = pi;
+  m = mi;
+  v = vi;
 }
 
 }  // namespace resihp

@@ -76,35 +76,6 @@ struct FusedArgs {
   CommArgs comm;
 };
 
-// ---- memory-model helpers ------------------------------------------------------------
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// Wait until *p >= target (wrap-safe); false + error code when the budget runs out.
-__device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int* err, int code) {
-  const uint64_t start = globaltimer();
-  #pragma unroll 1
-  while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
-    if (globaltimer() - start > kWaitBudgetNs) {
-      record_error(err, code);
-      return false;
-    }
-  }
-  return true;
-}
-
 // One lane waits, the whole warp learns the outcome.
 __device__ __forceinline__ bool warp_wait_geq(const unsigned* p, unsigned target, int* err, int lane) {
   int ok = 1;

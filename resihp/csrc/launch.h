@@ -38,6 +38,12 @@ inline void append(std::string& o, const T& v, const R&... r) {
     RESIHP_CHECK(_e == cudaSuccess, #expr, " failed: ", cudaGetErrorString(_e));        \
   } while (0)
 
+// AdamW coefficients of one step (bias corrections folded in on the host, in double).
+struct AdamWCoef {
+  float lr, b1, b2, eps, wd, step_size, bc2_sqrt, grad_scale;
+};
+AdamWCoef adamw_coef(float lr, float b1, float b2, float eps, float wd, int64_t step, float grad_scale);
+
 CUtensorMap make_tma_2d_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows);
 
 // C[m,n] (=, +=) alpha * A * B^T; see gemm.cu for operand conventions and epilogues.
@@ -94,5 +100,28 @@ void* symm_alloc(int64_t bytes, void* handle_out);
 void* symm_open(const void* handle);
 void symm_close(void* p);
 void symm_free(void* p);
+
+}  // namespace resihp
+
+namespace resihp {
+
+// Peer-memory kernels over a stage's flat training state (peer_state.cu).
+constexpr int kMaxDp = 8;
+int dp_grid(int64_t n, int num_sms);
+void dp_allreduce_adamw(const float* const* grads, int dp, int me, float* sum_out, float* p, float* m, float* v,
+                        void* p_bf16, int64_t n, const AdamWCoef& coef, unsigned* flags_local,
+                        unsigned* const* flags_peer, unsigned epoch, int grid, int* err, cudaStream_t st);
+
+// One strided block copy of the state move: rows x cols fp32 elements.
+struct CopyDesc {
+  const float* src;
+  float* dst;
+  void* dst_bf16;     // optional bf16 copy at the same element offsets (the compute weights)
+  int64_t src_ld, dst_ld;
+  int64_t rows, cols;
+  int64_t item_base;  // first work item (one item = one row) of this descriptor
+  int64_t vec4;       // 1: every address, stride and width is a multiple of 16 bytes
+};
+void reshard_gather(const CopyDesc* descs_device, int ndesc, int64_t items, int* err, int num_sms, cudaStream_t st);
 
 }  // namespace resihp

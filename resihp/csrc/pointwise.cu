@@ -85,16 +85,10 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __
 //   p -= (lr / bc1) * m / (sqrt(v) / sqrt(bc2) + eps)
 // and the bf16 working copy of p is refreshed in the same pass.
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, int64_t n, float lr, float b1,
-                             float b2, float eps, float wd, float step_size, float bc2_sqrt, float grad_scale) {
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, int64_t n, AdamWCoef c) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
-    const float gi = g[i] * grad_scale;
-    float pi = p[i] * (1.f - lr * wd);
-    float mi = m[i];
-    mi = mi + (1.f - b1) * (gi - mi);
-    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
-    const float denom = sqrtf(vi) / bc2_sqrt + eps;
-    pi = pi - step_size * (mi / denom);
+    float pi = p[i], mi = m[i], vi = v[i];
+    adamw_elem(pi, mi, vi, g[i], c);
     p[i] = pi;
     m[i] = mi;
     v[i] = vi;
@@ -166,15 +160,26 @@ void swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, int 
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
-void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, float lr, float b1, float b2,
-           float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st) {
+AdamWCoef adamw_coef(float lr, float b1, float b2, float eps, float wd, int64_t step, float grad_scale) {
   RESIHP_CHECK(step >= 1, "AdamW step must be >= 1");
   const double bc1 = 1.0 - std::pow(double(b1), double(step));
   const double bc2 = 1.0 - std::pow(double(b2), double(step));
-  const float step_size = float(double(lr) / bc1);
-  const float bc2_sqrt = float(std::sqrt(bc2));
-  adamw_kernel<<<grid_for(n, 256, num_sms), 256, 0, st>>>(p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, lr, b1,
-                                                         b2, eps, wd, step_size, bc2_sqrt, grad_scale);
+  AdamWCoef c;
+  c.lr = lr;
+  c.b1 = b1;
+  c.b2 = b2;
+  c.eps = eps;
+  c.wd = wd;
+  c.step_size = float(double(lr) / bc1);
+  c.bc2_sqrt = float(std::sqrt(bc2));
+  c.grad_scale = grad_scale;
+  return c;
+}
+
+void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, float lr, float b1, float b2,
+           float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st) {
+  const AdamWCoef c = adamw_coef(lr, b1, b2, eps, wd, step, grad_scale);
+  adamw_kernel<<<grid_for(n, 256, num_sms), 256, 0, st>>>(p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, c);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 

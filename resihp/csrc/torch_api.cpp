@@ -358,6 +358,72 @@ void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_loca
           flags.data(), as_ptr<void>(recv), int(grid), error_word(h.device()), cur_stream());
 }
 
+// ---- flat-state regions and the peer-state kernels ----------------------------------------
+
+// A zeroed, IPC-exported device allocation wrapped as a uint8 tensor. The memory is
+// released when the last tensor viewing it dies (the deleter frees it on its device).
+py::tuple symm_region_t(int64_t bytes, int64_t device) {
+  TORCH_CHECK(bytes > 0, "region size must be positive");
+  c10::cuda::CUDAGuard guard(c10::Device(c10::kCUDA, device));
+  cudaIpcMemHandle_t h;
+  void* p = symm_alloc(bytes, &h);
+  const int dev = int(device);
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  auto t = torch::from_blob(
+      p, {bytes},
+      [dev](void* q) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(dev);
+        cudaFree(q);
+        cudaSetDevice(prev);
+      },
+      opts);
+  return py::make_tuple(t, py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t dp_grid_t(int64_t n, int64_t device) {
+  return dp_grid(n, at::cuda::getDeviceProperties(device)->multiProcessorCount);
+}
+
+void dp_allreduce_adamw_t(std::vector<int64_t> grads, int64_t me, torch::Tensor sum_out, torch::Tensor p,
+                          torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p_bf16, double lr, double b1,
+                          double b2, double eps, double wd, int64_t step, double grad_scale, int64_t flags_local,
+                          std::vector<int64_t> flags_peer, int64_t epoch, int64_t grid) {
+  for (auto* t : {&sum_out, &p, &m, &v})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat && t->is_contiguous() && t->numel() == p.numel(),
+                "DP AdamW buffers must be contiguous fp32 of equal size");
+  const int64_t dp = int64_t(grads.size());
+  TORCH_CHECK(dp >= 1 && dp <= kMaxDp && int64_t(flags_peer.size()) == dp && me >= 0 && me < dp,
+              "one gradient buffer and one flag array per DP rank");
+  void* pb = nullptr;
+  if (p_bf16.has_value()) {
+    TORCH_CHECK(p_bf16->scalar_type() == torch::kBFloat16 && p_bf16->numel() == p.numel() && p_bf16->is_contiguous(),
+                "bf16 copy must match");
+    pb = p_bf16->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(p.device());
+  std::vector<const float*> g;
+  std::vector<unsigned*> f;
+  for (auto x : grads) g.push_back(as_ptr<const float>(x));
+  for (auto x : flags_peer) f.push_back(as_ptr<unsigned>(x));
+  const AdamWCoef c = adamw_coef(float(lr), float(b1), float(b2), float(eps), float(wd), step, float(grad_scale));
+  dp_allreduce_adamw(g.data(), int(dp), int(me), sum_out.data_ptr<float>(), p.data_ptr<float>(), m.data_ptr<float>(),
+                     v.data_ptr<float>(), pb, p.numel(), c, as_ptr<unsigned>(flags_local), f.data(), unsigned(epoch),
+                     int(grid), error_word(p.device()), cur_stream());
+}
+
+// descs: int64 [n, 9] on the device, one CopyDesc per row (see launch.h for the fields).
+void reshard_gather_t(torch::Tensor descs, int64_t items) {
+  static_assert(sizeof(CopyDesc) == 9 * sizeof(int64_t), "CopyDesc is nine 8-byte fields");
+  TORCH_CHECK(descs.is_cuda() && descs.scalar_type() == torch::kLong && descs.is_contiguous() && descs.dim() == 2 &&
+                  descs.size(1) == 9, "copy descriptors must be a contiguous int64 [n, 9] CUDA tensor");
+  c10::cuda::CUDAGuard guard(descs.device());
+  reshard_gather(reinterpret_cast<const CopyDesc*>(descs.data_ptr<int64_t>()), int(descs.size(0)), items,
+                 error_word(descs.device()), at::cuda::getDeviceProperties(descs.device().index())->multiProcessorCount,
+                 cur_stream());
+}
+
 }  // namespace resihp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -386,4 +452,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_grid", &resihp::fused_grid_t);
   m.def("ag_gemm", &resihp::ag_gemm_t);
   m.def("gemm_rs", &resihp::gemm_rs_t);
+  m.def("symm_region", &resihp::symm_region_t);
+  m.def("dp_grid", &resihp::dp_grid_t);
+  m.def("dp_allreduce_adamw", &resihp::dp_allreduce_adamw_t);
+  m.def("reshard_gather", &resihp::reshard_gather_t);
 }

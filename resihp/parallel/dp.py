@@ -146,6 +146,33 @@ class GradientReducer:
         self.executor_group = executor_group
         self.replica_id = replica_id
         self.bucket_elems = 64 * 1024 * 1024
+        self.fused_dp = None
+
+    def attach(self, stage) -> None:
+        """Set up the fused DP step (one NVLink kernel: all-reduce + AdamW) where it applies.
+
+        Collective over this rank's DP position group. Applies on the CUDA kernel path of
+        a homogeneous plan; every rank decides the same way (config, device kind and the
+        ``RESIHP_FUSED_DP`` switch are common to the job).
+        """
+        from . import peer
+
+        if not (peer.ENABLED and stage.kernel and stage.flat.shared and self.topology.homogeneous):
+            return
+        for members in self.topology.dp_groups:
+            if self.rank in members and 1 < len(members) <= peer.MAX_DP:
+                stage.dp = peer.DpPeers(stage, self.groups[members])
+                self.fused_dp = stage.dp
+
+    def reduce_and_step(self, stage) -> bool:
+        """Reduce; with the fused DP step also take the optimizer step. True if stepped."""
+        if self.fused_dp is None or self.fused_dp.closed:
+            self.reduce(stage)
+            return False
+        self._sp_partial_replicated(stage)
+        self._reduce_tied(stage)
+        self.fused_dp.step(stage)
+        return True
 
     def reduce(self, stage) -> None:
         if self.topology.homogeneous:
@@ -167,11 +194,14 @@ class GradientReducer:
             v.copy_(buf[off: off + v.numel()].view_as(v))
             off += v.numel()
 
-    def _reduce_fast(self, stage) -> None:
-        self._sp_partial_replicated(stage)
+    def _reduce_tied(self, stage) -> None:
         for members in self.topology.tied_groups:
             if self.rank in members:
                 dist.all_reduce(stage.g["token_embedding.weight"], group=self.groups[members])
+
+    def _reduce_fast(self, stage) -> None:
+        self._sp_partial_replicated(stage)
+        self._reduce_tied(stage)
         for members in self.topology.dp_groups:
             if self.rank in members:
                 grad = stage.flat.grad

@@ -250,9 +250,8 @@ class PipelineRuntime:
             self._send_backward(backward(self._recv_backward(shape)))
 
         self.schedule.append("W")
-        if self.reducer is not None:
-            self.reducer.reduce(stage)
-        stage.optimizer_step()
+        if self.reducer is None or not self.reducer.reduce_and_step(stage):
+            stage.optimizer_step()
         if not stage.is_last:
             return None
         return total if return_tensor else float(total)

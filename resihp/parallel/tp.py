@@ -57,10 +57,23 @@ def local_slice(full: torch.Tensor, dim: int | None, rank: int, size: int) -> to
     return torch.chunk(full, size, dim=dim)[rank].contiguous().clone()
 
 
-class FlatState:
-    """Flat FP32 master / grad / Adam buffers plus the compute copy, with named views."""
+REGION_FLAG_BYTES = 64 * 1024  # flag words at the head of a shared state region
 
-    def __init__(self, entries: list[tuple[TensorSpec, tuple[int, ...]]], device, compute_dtype):
+
+class FlatState:
+    """Flat FP32 master / grad / Adam buffers plus the compute copy, with named views.
+
+    ``shared=True`` (the CUDA kernel path) places every buffer in one CUDA-IPC-exported
+    region -- ``flags | master | exp_avg | exp_avg_sq | grad0 | grad1 | work`` -- so
+    data-parallel peers can read each other's gradients and a post-failure reshard can
+    pull state from its donors with P2P loads. The two gradient buffers alternate by
+    step parity: the fused DP reduction reads the accumulated one and writes the summed
+    gradient into the other, which becomes :attr:`grad` for the rest of the step.
+    """
+
+    FIELDS = ("master", "exp_avg", "exp_avg_sq", "grad0", "grad1")
+
+    def __init__(self, entries: list[tuple[TensorSpec, tuple[int, ...]]], device, compute_dtype, *, shared=False):
         self.entries = entries
         self.offsets: dict[str, tuple[int, tuple[int, ...]]] = {}
         cursor = 0
@@ -73,16 +86,59 @@ class FlatState:
             cursor += _numel(shape)
             prev_fuse = spec.fuse
         self.numel = max(1, (cursor + _ALIGN - 1) // _ALIGN * _ALIGN)
-        f32 = dict(dtype=torch.float32, device=device)
-        self.master = torch.zeros(self.numel, **f32)
-        self.grad = torch.zeros(self.numel, **f32)
-        self.exp_avg = torch.zeros(self.numel, **f32)
-        self.exp_avg_sq = torch.zeros(self.numel, **f32)
         self.step = 0
-        if compute_dtype == torch.float32:
-            self.work = self.master
+        self.shared = bool(shared)
+        self.region = None
+        self.handle = None
+        self.field_offsets: dict[str, int] = {}
+        if self.shared:
+            self._alloc_region(torch.device(device), compute_dtype)
         else:
-            self.work = torch.zeros(self.numel, dtype=compute_dtype, device=device)
+            f32 = dict(dtype=torch.float32, device=device)
+            self.master = torch.zeros(self.numel, **f32)
+            self.grads = (torch.zeros(self.numel, **f32),)
+            self.exp_avg = torch.zeros(self.numel, **f32)
+            self.exp_avg_sq = torch.zeros(self.numel, **f32)
+            if compute_dtype == torch.float32:
+                self.work = self.master
+            else:
+                self.work = torch.zeros(self.numel, dtype=compute_dtype, device=device)
+        self.parity = 0
+        self.grad = self.grads[0]
+
+    def _alloc_region(self, device, compute_dtype) -> None:
+        from ..ops import _ext
+
+        n = self.numel
+        work_bytes = n * torch.empty((), dtype=compute_dtype).element_size()
+        off = REGION_FLAG_BYTES
+        for name in self.FIELDS:
+            self.field_offsets[name] = off
+            off += 4 * n
+        self.field_offsets["work"] = off
+        total = off + work_bytes
+        self.region, self.handle = _ext.require().symm_region(total, device.index or 0)
+        self.region_ptr = self.region.data_ptr()
+
+        def field(name, dtype, count):
+            start = self.field_offsets[name]
+            return self.region[start: start + count * torch.empty((), dtype=dtype).element_size()].view(dtype)
+
+        self.flags = self.region[:REGION_FLAG_BYTES].view(torch.int32)
+        self.master = field("master", torch.float32, n)
+        self.exp_avg = field("exp_avg", torch.float32, n)
+        self.exp_avg_sq = field("exp_avg_sq", torch.float32, n)
+        self.grads = (field("grad0", torch.float32, n), field("grad1", torch.float32, n))
+        self.work = field("work", compute_dtype, n)
+
+    def set_parity(self, parity: int) -> None:
+        self.parity = parity
+        self.grad = self.grads[parity]
+
+    def export(self) -> dict:
+        """What a peer needs to read this state: IPC handle, field and tensor offsets, step."""
+        return {"handle": self.handle, "fields": dict(self.field_offsets), "numel": self.numel,
+                "offsets": {n: off for n, (off, _s) in self.offsets.items()}, "step": self.step}
 
     def view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
         off, shape = self.offsets[name]
@@ -142,15 +198,17 @@ class TensorParallelStage:
         self.specs = stage_specs(config, self.layer_ids, self.is_first, self.is_last)
         self.spec_by_name = {s.name: s for s in self.specs}
         entries = [(s, local_shape(s, self.tp_size)) for s in self.specs]
-        self.flat = FlatState(entries, self.device, compute)
-        with torch.no_grad():
-            for s in self.specs:
-                self.flat.view(self.flat.master, s.name).copy_(local_state[s.name].to(self.device, torch.float32))
-        if moments:
-            self.install_moments(moments)
-        self.flat.refresh_work()
+        self.flat = FlatState(entries, self.device, compute, shared=self.kernel)
+        if local_state is not None:
+            with torch.no_grad():
+                for s in self.specs:
+                    self.flat.view(self.flat.master, s.name).copy_(local_state[s.name].to(self.device, torch.float32))
+            if moments:
+                self.install_moments(moments)
+            self.flat.refresh_work()
         self._bind_compute_tensors()
         self.ws = None
+        self.dp = None  # peer mappings of the fused DP reduction (set by the gradient reducer)
         rows = config.micro_batch_size * config.seq_len
         if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= 8
                 and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0):
@@ -162,19 +220,15 @@ class TensorParallelStage:
     # --- parameters -----------------------------------------------------------------
 
     def _bind_compute_tensors(self) -> None:
-        """Compute weights (views of ``work``) and their gradient views."""
+        """Compute weights (views of ``work``) and the gradient views of each grad buffer."""
         self.w: dict[str, torch.Tensor] = {}
-        self.g: dict[str, torch.Tensor] = {}
+        fused_w: dict[str, torch.Tensor] = {}
         for s in self.specs:
-            self.g[s.name] = self.flat.view(self.flat.grad, s.name)
             if self.kernel:
                 self.w[s.name] = self.flat.view(self.flat.work, s.name).detach().requires_grad_(True)
             else:
-                p = nn.Parameter(self.flat.view(self.flat.master, s.name))
-                p.grad = self.g[s.name]
-                self.w[s.name] = p
-        # fused column-parallel weights (kernel path: one GEMM each)
-        self.fused_w: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+                self.w[s.name] = nn.Parameter(self.flat.view(self.flat.master, s.name))
+        spans = []
         if self.config.arch == "llama":
             d = self.dim
             for gid in self.layer_ids:
@@ -182,10 +236,24 @@ class TensorParallelStage:
                 for key, first, last in (("qkv", "attn.q_proj.weight", "attn.v_proj.weight"),
                                          ("gate_up", "mlp.gate.weight", "mlp.up.weight")):
                     w = self.flat.span(self.flat.work, p + first, p + last, d)
-                    g = self.flat.span(self.flat.grad, p + first, p + last, d)
                     if self.kernel:
                         w = w.detach().requires_grad_(True)
-                    self.fused_w[p + key] = (w, g)
+                    fused_w[p + key] = w
+                    spans.append((p + key, p + first, p + last))
+        self._grad_sets = []
+        for buf in self.flat.grads:
+            g = {s.name: self.flat.view(buf, s.name) for s in self.specs}
+            fw = {key: (fused_w[key], self.flat.span(buf, a, b, self.dim)) for key, a, b in spans}
+            self._grad_sets.append((g, fw))
+        self.use_grad(self.flat.parity)
+
+    def use_grad(self, parity: int) -> None:
+        """Make grad buffer ``parity`` the one the kernels accumulate into and ``g`` shows."""
+        self.flat.set_parity(parity)
+        self.g, self.fused_w = self._grad_sets[parity]
+        if not self.kernel:
+            for name, p in self.w.items():
+                p.grad = self.g[name]
 
     def parameters(self):
         return list(self.w.values())
@@ -241,10 +309,13 @@ class TensorParallelStage:
         return (tokens // self.tp_size if self.sp else tokens, self.dim)
 
     def close_comm(self, *, barrier: bool = True) -> None:
-        """Release the peer-memory workspace (at a safe point, with nothing in flight)."""
+        """Release the peer-memory mappings (at a safe point, with nothing in flight)."""
         if self.ws is not None:
             self.ws.close(barrier=barrier)
             self.ws = None
+        if self.dp is not None:
+            self.dp.close(barrier=barrier)
+            self.dp = None
 
     def _col_linear(self, h, w, g):
         """Column-parallel linear; under SP the token all-gather is fused into the GEMM."""

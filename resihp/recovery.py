@@ -31,6 +31,8 @@ import torch.distributed as dist
 
 from .checkpoint import CheckpointError, read_payload, save_checkpoint, verify_digest
 from .models.init import initial_stage_state
+from .ops import _ext
+from .parallel import peer
 from .models.layout import group_specs, model_specs, stage_specs
 from .parallel.dp import GradientReducer
 from .parallel.pp import PipelineRuntime
@@ -123,6 +125,8 @@ class PlannedRun:
         reducer = GradientReducer(plan, rank, groups=groups.reduce, executor_group=groups.executor, replica_id=sp.replica_id)
         needs_reduce = bool(reducer.topology.dp_groups or reducer.topology.tied_groups or not reducer.topology.homogeneous
                             or self.stage.sp)
+        if needs_reduce:
+            reducer.attach(self.stage)
         self.runtime = PipelineRuntime(
             self.stage, rank=rank, replica_id=sp.replica_id, assignment=dp_assignment(plan),
             boundary_groups=groups.hops, reducer=reducer if needs_reduce else None,
@@ -358,6 +362,140 @@ def state_fingerprint(run) -> str:
     return sha256(repr((st.flat.step, [f"{x:.17g}" for x in sums])).encode("utf-8")).hexdigest()
 
 
+def _collective_recover(run, local, *, plan, rank, anchor, rollback, completed, groups, device, tdev, cursor, pin):
+    """Peer routes as one collective each over the live group (CPU / FP32 path)."""
+    config = plan.config
+    stage = stage_of(plan, rank)
+    acquired: dict[str, dict] = {}
+    for route in plan.state_routes:
+        if route.donor_kind == "checkpoint" or rollback:
+            if rank in route.target_ranks:
+                acquired.update(_anchor_slices(config, route, anchor, rank))
+            continue
+        acquired.update(_route_transfer(config, route, local, rank, group=groups.live, device=tdev))
+    if stage is None:
+        return None
+    owned = stage_layout(plan, stage)
+    idx = stage.tp_members.index(rank)
+    state: dict[str, dict] = {}
+    for name, dim in owned.items():
+        if name in acquired:
+            state[name] = acquired[name]
+        elif rollback:
+            e = anchor[name]
+            state[name] = {f: local_slice(e[f], dim, idx, stage.tp_degree) for f in FIELDS if f in e}
+            if "step" in e:
+                state[name]["step"] = e["step"]
+        elif name in local:
+            state[name] = local[name]
+        else:
+            raise ReshardError(f"no state route covers {name} for rank {rank}")
+    return PlannedRun(
+        plan, rank=rank, local_state={n: f["param"] for n, f in state.items()},
+        moments={n: f for n, f in state.items() if "exp_avg" in f}, groups=groups, device=device,
+        cursor=completed if rollback else cursor, pin=pin,
+    )
+
+
+def _p2p_recover(run, *, plan, rank, anchor, groups, device, cursor, pin):
+    """The CUDA path: new owners pull their shards from the donors' regions over NVLink.
+
+    Every surviving rank publishes its flat-state region (IPC handle, field and tensor
+    offsets, AdamW step) over the world group; each rank of the new plan builds its stage
+    with an unfilled region and moves every owned tensor with one ``reshard_gather``
+    launch: pieces of peer routes from the donors' regions (re-chunked for the new TP
+    degree inside the copy descriptors), tensors it keeps from its own old region, and
+    ``checkpoint`` routes from the host anchor. A barrier over the world group then tells
+    the donors that nothing reads their regions any more.
+    """
+    from .ops import check_device_errors
+
+    config = plan.config
+    k = _ext.require()
+    mine = None if run is None else run.stage.flat.export()
+    gathered = [None] * dist.get_world_size(groups.world)
+    dist.all_gather_object(gathered, (rank, mine), group=groups.world)
+    regions = {r: m for r, m in gathered if m is not None}
+    stage = stage_of(plan, rank)
+    new_run = None
+    opened: dict[int, int] = {}
+    try:
+        if stage is not None:
+            new_run = PlannedRun(plan, rank=rank, local_state=None, moments=None, groups=groups, device=device,
+                                 cursor=cursor, pin=pin)
+            flat = new_run.stage.flat
+            shapes = _shape_of(config)
+            owned = stage_layout(plan, stage)
+            idx = stage.tp_members.index(rank)
+            by_name = {}
+            for route in routes_for(plan, rank):
+                for name in route_names(config, route):
+                    by_name[name] = route
+
+            def region_of(r):
+                if r == rank:
+                    if run is None:
+                        raise ReshardError(f"rank {rank} is named as a donor but holds no state")
+                    return run.stage.flat.region_ptr
+                if r not in regions:
+                    raise ReshardError(f"donor rank {r} published no state")
+                if r not in opened:
+                    opened[r] = k.symm_open(regions[r]["handle"])
+                return opened[r]
+
+            gp = peer.GatherPlan()
+            host: dict[str, dict] = {}
+            steps = set()
+            for name, dim in owned.items():
+                dst_off = flat.offsets[name][0]
+                route = by_name.get(name)
+                if route is not None and route.donor_kind == "checkpoint":
+                    host[name] = _anchor_slices(config, route, anchor, rank)[name]
+                    if "step" in host[name]:
+                        steps.add(int(float(host[name]["step"])))
+                    continue
+                if route is not None:
+                    pieces = peer.shard_pieces(shapes[name], dim, route.donor_degree, route.target_degree,
+                                               route.target_ranks.index(rank))
+                    donors = route.donor_ranks
+                else:
+                    if run is None or name not in run.stage.flat.offsets:
+                        raise ReshardError(f"no state route covers {name} for rank {rank}")
+                    n = run.stage.flat.offsets[name][1]
+                    count = 1
+                    for x in n:
+                        count *= int(x)
+                    pieces = [peer.Piece(0, 0, count, 0, count, 1, count)]
+                    donors = (rank,)
+                for piece in pieces:
+                    donor = donors[piece.donor]
+                    meta = regions.get(donor) if donor != rank else mine
+                    if meta is None or name not in meta["offsets"]:
+                        raise ReshardError(f"donor rank {donor} does not hold {name}")
+                    gp.add([piece], src_region=region_of(donor), src_fields=meta["fields"],
+                           src_tensor_off=meta["offsets"][name], dst_flat=flat, dst_tensor_off=dst_off)
+                    steps.add(int(meta["step"]))
+            gp.launch(flat.master.device)
+            with torch.no_grad():
+                for name, entry in host.items():
+                    for f, buf in (("param", flat.master), ("exp_avg", flat.exp_avg), ("exp_avg_sq", flat.exp_avg_sq)):
+                        if f in entry:
+                            flat.view(buf, name).copy_(entry[f].to(buf.device))
+                    if flat.work is not flat.master:
+                        flat.view(flat.work, name).copy_(flat.view(flat.master, name))
+            torch.cuda.synchronize(flat.master.device)
+            check_device_errors(flat.master.device.index or 0)
+            if len(steps) > 1:
+                raise ReshardError(f"donors disagree on the AdamW step: {sorted(steps)}")
+            flat.step = steps.pop() if steps else 0
+    finally:
+        # Everyone's gathers are done before any donor region may be released.
+        dist.barrier(group=groups.world)
+        for ptr in opened.values():
+            k.symm_close(ptr)
+    return new_run
+
+
 def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: TrainingGroups, device=None, pin=False):
     """Safe-point step 7: execute ``plan``'s state routes; returns ``(run, state digest)``.
 
@@ -374,40 +512,17 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
     anchor, completed, ck_digest = loaded if loaded is not None else ({}, None, None)
     current = completed == cursor
     rollback = needs_checkpoint and not current
-    stage = stage_of(plan, rank)
     local = {} if run is None or rollback else run.local_state()
     tdev = torch.device("cpu") if device is None else torch.device(device)
 
-    acquired: dict[str, dict] = {}
-    for route in plan.state_routes:
-        if route.donor_kind == "checkpoint" or rollback:
-            if rank in route.target_ranks:
-                acquired.update(_anchor_slices(config, route, anchor, rank))
-            continue
-        acquired.update(_route_transfer(config, route, local, rank, group=groups.live, device=tdev))
-
-    new_run = None
-    if stage is not None:
-        owned = stage_layout(plan, stage)
-        idx = stage.tp_members.index(rank)
-        state: dict[str, dict] = {}
-        for name, dim in owned.items():
-            if name in acquired:
-                state[name] = acquired[name]
-            elif rollback:
-                e = anchor[name]
-                state[name] = {f: local_slice(e[f], dim, idx, stage.tp_degree) for f in FIELDS if f in e}
-                if "step" in e:
-                    state[name]["step"] = e["step"]
-            elif name in local:
-                state[name] = local[name]
-            else:
-                raise ReshardError(f"no state route covers {name} for rank {rank}")
-        new_run = PlannedRun(
-            plan, rank=rank, local_state={n: f["param"] for n, f in state.items()},
-            moments={n: f for n, f in state.items() if "exp_avg" in f}, groups=groups, device=device,
-            cursor=completed if rollback else cursor, pin=pin,
-        )
+    p2p = (tdev.type == "cuda" and config.dtype == "bf16" and peer.ENABLED and not rollback)
+    if p2p:
+        new_run = _p2p_recover(run, plan=plan, rank=rank, anchor=anchor, groups=groups, device=tdev,
+                               cursor=cursor, pin=pin)
+    else:
+        new_run = _collective_recover(run, local, plan=plan, rank=rank, anchor=anchor, rollback=rollback,
+                                      completed=completed, groups=groups, device=device, tdev=tdev, cursor=cursor,
+                                      pin=pin)
 
     if current or rollback:
         if new_run is not None:

@@ -2,6 +2,8 @@
 
     python -m resihp.utils.kernel_probe gemm   # forward + wgrad GEMM, 4096 x 6144 x 2048
     python -m resihp.utils.kernel_probe attn   # causal attention fwd + bwd, B2 H16 S2048 D128
+    python -m resihp.utils.kernel_probe dp     # fused DP all-reduce + AdamW, 2 replicas emulated, 64M elements
+    python -m resihp.utils.kernel_probe reshard  # state move TP2 -> TP1 of one 1.3B layer group (3 fields)
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
 and launches every kernel a handful of times, so a capture of one or two launches ends
@@ -38,10 +40,61 @@ def attn() -> None:
         out.backward(torch.randn_like(out))
 
 
+def dp() -> None:
+    """One DP rank of two; the peer's region is a second local region (flags preset)."""
+    from resihp.models.layout import TensorSpec
+    from resihp.parallel.tp import FlatState
+
+    k = ops._ext.require()
+    n = 64 * 1024 * 1024
+    dev = torch.device("cuda", 0)
+    a, b = (FlatState([(TensorSpec("w", (n,), None, "normal"), (n,))], dev, torch.bfloat16, shared=True)
+            for _ in range(2))
+    for f in (a, b):
+        f.grads[0].normal_()
+    a.exp_avg_sq.fill_(1e-4)
+    grid = k.dp_grid(n, 0)
+    a.flags.view(-1, 8)[:grid, 1] = 1 << 20
+    for step in range(1, 4):
+        k.dp_allreduce_adamw([a.grads[0].data_ptr(), b.grads[0].data_ptr()], 0, a.grads[1], a.master, a.exp_avg,
+                             a.exp_avg_sq, a.work, 1e-4, 0.9, 0.95, 1e-8, 0.1, step, 1.0, a.region_ptr,
+                             [a.region_ptr, b.region_ptr], step, grid)
+
+
+def reshard() -> None:
+    """Two TP2 donors -> one TP1 target: q/k/v + gate/up (dim 0), o/down (dim 1), norms."""
+    from resihp.models.layout import TensorSpec
+    from resihp.parallel.peer import GatherPlan, shard_pieces
+    from resihp.parallel.tp import FlatState, local_slice
+
+    dev = torch.device("cuda", 0)
+    d, f = 2048, 5504
+    logical = [("qkv", (3 * d, d), 0), ("o", (d, d), 1), ("gate_up", (2 * f, d), 0), ("down", (d, f), 1),
+               ("norm", (d,), None)]
+
+    def flat(degree, idx):
+        entries = [(TensorSpec(n, s, dim, "normal"), tuple(local_slice(torch.empty(s), dim, idx, degree).shape))
+                   for n, s, dim in logical]
+        return FlatState(entries, dev, torch.bfloat16, shared=True)
+
+    donors = [flat(2, i) for i in range(2)]
+    for x in donors:
+        x.master.normal_()
+    target = flat(1, 0)
+    for _ in range(3):
+        gp = GatherPlan()
+        for name, s, dim in logical:
+            for piece in shard_pieces(s, dim, 2, 1, 0):
+                src = donors[piece.donor]
+                gp.add([piece], src_region=src.region_ptr, src_fields=src.field_offsets,
+                       src_tensor_off=src.offsets[name][0], dst_flat=target, dst_tensor_off=target.offsets[name][0])
+        gp.launch(dev)
+
+
 def main(argv=None) -> None:
     what = (argv or sys.argv[1:])[0]
     torch.manual_seed(0)
-    {"gemm": gemm, "attn": attn}[what]()
+    {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard}[what]()
     torch.cuda.synchronize()
     ops.check_device_errors()
     print("ok", what)
