@@ -39,6 +39,18 @@ GLOBAL_BATCH = 64
 MICRO_BATCH = 2
 LAYOUTS = {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 2, 2)}
 
+# BASELINE configs 3 and 5 (8 GPUs only; --config 3 / --config 5).
+CONFIGS = {
+    2: dict(model=MODEL, extra={}, global_batch=GLOBAL_BATCH, micro_batch=MICRO_BATCH, layouts=LAYOUTS,
+            name="llama-1.3b (24L, d2048, 16H MHA, SwiGLU 5504, V32000)"),
+    3: dict(model=dict(model_dim=4096, num_layers=32, num_heads=32, ffn_dim=14336, vocab_size=128256, seq_len=4096),
+            extra=dict(num_kv_heads=8, rope_theta=500000.0), global_batch=16, micro_batch=1, layouts={8: (4, 2, 1)},
+            name="llama-3-8b shape (32L, d4096, 32Q/8KV GQA, SwiGLU 14336, V128256, theta 5e5)"),
+    5: dict(model=dict(model_dim=5120, num_layers=40, num_heads=40, ffn_dim=13824, vocab_size=32000, seq_len=4096),
+            extra=dict(recompute=True), global_batch=8, micro_batch=1, layouts={8: (8, 1, 1)},
+            name="llama-2-13b shape (40L, d5120, 40H, SwiGLU 13824, V32000), activation recompute"),
+}
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -46,6 +58,8 @@ def parse():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["resihp", "reference"], default="resihp")
+    p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
+                   help="BASELINE config: 2 (default, 1/2/4/8 GPUs), 3 or 5 (8 GPUs)")
     return p.parse_args()
 
 
@@ -165,15 +179,22 @@ def run_ours(args):
     rank, world, local = _env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    tp, pp, dp = LAYOUTS[world]
+    spec = CONFIGS[args.config]
+    if world not in spec["layouts"]:
+        raise SystemExit(f"config {args.config} runs on {sorted(spec['layouts'])} GPUs, not {world}")
+    tp, pp, dp = spec["layouts"][world]
+    global_batch, micro_batch = spec["global_batch"], spec["micro_batch"]
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    extra = dict(num_kv_heads=None)
+    extra.update(spec["extra"])
     config = TrainConfig(
-        **MODEL, num_kv_heads=None, batch_size=GLOBAL_BATCH, micro_batch_size=MICRO_BATCH, seed=1,
+        **spec["model"], **extra, batch_size=global_batch, micro_batch_size=micro_batch, seed=1,
         tp=tp, pp=pp, dp=dp, iterations=args.warmup + args.steps, arch="llama", dtype="bf16",
         sequence_parallel=tp > 1, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95, weight_decay=0.1,
+        memory_budget_bytes=180 * 10**9,
     )
-    cp = ControlPlane(rank, range(world), _store(rank, world), "nccl")
+    cp = ControlPlane(rank, range(world), _store(rank, world), "nccl", device=device)
     cp.form_world(range(world), epoch=0)
     plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
     groups = cp.build_training_groups(plan)
@@ -183,7 +204,7 @@ def run_ours(args):
     if run is not None:
         mbs = len(run.runtime.micro_batches)
         if run.stage.is_first or run.stage.is_last:
-            h2d_bytes = mbs * MICRO_BATCH * config.seq_len * 8
+            h2d_bytes = mbs * micro_batch * config.seq_len * 8
         d2h_bytes = 4 if run.stage.is_last else 0
 
     def step():
@@ -208,7 +229,7 @@ def run_ours(args):
     check_device_errors(local)
     bytes_in = torch.tensor([float(h2d_bytes), float(d2h_bytes)])
     dist.all_reduce(bytes_in, group=cp.world_group)
-    tokens = args.steps * GLOBAL_BATCH * config.seq_len
+    tokens = args.steps * global_batch * config.seq_len
     value = tokens / device_s
     e2e = tokens / wall_s
     if rank == 0:
@@ -217,10 +238,11 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * device_s / args.steps, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded uniform tokens), random-init weights",
-            "config": {"model": "llama-1.3b (24L, d2048, 16H MHA, SwiGLU 5504, V32000)", "global_batch": GLOBAL_BATCH,
-                       "micro_batch": MICRO_BATCH, "seq_len": config.seq_len,
+            "config": {"model": spec["name"], "baseline_config": args.config, "global_batch": global_batch,
+                       "micro_batch": micro_batch, "seq_len": config.seq_len,
                        "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if tp > 1 else ""),
                        "tp_comm": "fused-nvlink" if (tp > 1 and os.environ.get("RESIHP_FUSED_TP", "1") != "0") else ("nccl" if tp > 1 else "none"),
+                       "dp_comm": ("fused-nvlink+adamw" if os.environ.get("RESIHP_FUSED_DP", "1") != "0" else "nccl") if dp > 1 else "none",
                        "l2": "inputs larger than L2 (weights/activations >> 126 MB)"},
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(bytes_in[0]),
@@ -238,6 +260,10 @@ def run_ours(args):
 
 
 def run_reference(args):
+    if args.config != 2:
+        print(json.dumps({"impl": "reference", "unavailable": f"config {args.config} needs GQA / sequence parallelism "
+                          "/ recompute / bf16, which the reference cannot express"}))
+        return
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "resihp")):
         print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}))

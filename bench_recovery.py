@@ -39,6 +39,7 @@ def parse():
     p.add_argument("--iterations", type=int, default=70)
     p.add_argument("--timeout", type=float, default=1500)
     p.add_argument("--small", action="store_true", help="a 4-layer model (quick check)")
+    p.add_argument("--layout", default=None, help="tp,pp,dp (default: config 4's layout for --gpus)")
     p.add_argument("--checkpoint-every", type=int, default=None,
                    help="commit the logical checkpoint every N steps (default: every step without a peer "
                         "replica, never with one)")
@@ -47,7 +48,9 @@ def parse():
 
 def main():
     args = parse()
-    tp, pp, dp = LAYOUTS[args.gpus]
+    tp, pp, dp = (tuple(int(x) for x in args.layout.split(",")) if args.layout else LAYOUTS[args.gpus])
+    if tp * pp * dp != args.gpus:
+        raise SystemExit(f"layout {tp}x{pp}x{dp} does not use {args.gpus} GPUs")
     model = dict(MODEL)
     if args.small:
         model.update(num_layers=4, model_dim=1024, num_heads=8, ffn_dim=2752, seq_len=1024)

@@ -45,6 +45,11 @@ STOP_CODES = (
 )
 _DIGEST_STOP = {"plan": "plan_disagreement", "state": "state_mismatch"}
 GROUP_TIMEOUT = timedelta(seconds=int(os.environ.get("RESIHP_GROUP_TIMEOUT", "300")))
+# On GPUs the world group also carries an NCCL communicator bound to this rank's device,
+# created eagerly when the world forms; every NCCL training group is then split from it
+# (ncclCommSplit) inside the safe point instead of being initialised from scratch on its
+# first collective.
+NCCL_SPLIT = os.environ.get("RESIHP_NCCL_SPLIT", "1") != "0"
 
 
 @dataclass(frozen=True)
@@ -62,7 +67,7 @@ class ConsistentStop(RuntimeError):
 class ControlPlane:
     """This rank's place in the world; rebuilds it after a real fail-stop."""
 
-    def __init__(self, rank, members, store, training_backend, *, memory_budget=None):
+    def __init__(self, rank, members, store, training_backend, *, memory_budget=None, device=None):
         self.rank = int(rank)
         self.members = tuple(sorted(members))
         self.store = store
@@ -74,13 +79,13 @@ class ControlPlane:
         self.memory_budget = memory_budget
         self.training_run = None
         self.checkpoint_path = None
-        self.device = None
+        self.device = device
         self.state_digest = ""
         self.pin = False
         self.last_recovery: dict = {}
 
     @classmethod
-    def initialize(cls, *, training_backend=None, memory_budget=None) -> "ControlPlane":
+    def initialize(cls, *, training_backend=None, memory_budget=None, device=None) -> "ControlPlane":
         import torch
 
         rank = int(os.environ["RANK"])
@@ -88,7 +93,7 @@ class ControlPlane:
         store = membership.connect(os.environ[membership.HOST_ENV], os.environ[membership.PORT_ENV])
         if training_backend is None:
             training_backend = "nccl" if torch.cuda.is_available() else "gloo"
-        cp = cls(rank, range(world), store, training_backend, memory_budget=memory_budget)
+        cp = cls(rank, range(world), store, training_backend, memory_budget=memory_budget, device=device)
         cp.form_world(cp.members, epoch=0)
         return cp
 
@@ -128,14 +133,21 @@ class ControlPlane:
     def form_world(self, members, *, epoch: int) -> None:
         import torch.distributed as dist
 
+        import torch
+
         self.members = tuple(sorted(members))
         self.epoch = int(epoch)
+        backend, bound = "gloo", None
+        if (NCCL_SPLIT and self.training_backend == "nccl" and self.device is not None
+                and torch.device(self.device).type == "cuda"):
+            backend, bound = "cpu:gloo,cuda:nccl", torch.device(self.device)
         dist.init_process_group(
-            backend="gloo",
+            backend=backend,
             store=dist.PrefixStore(membership.PG_PREFIX.format(epoch=self.epoch), self.store),
             rank=self.torch_rank(self.rank),
             world_size=self.world_size,
             timeout=GROUP_TIMEOUT,
+            device_id=bound,
         )
         self.world_group = dist.group.WORLD
         self.groups.world = self.world_group
@@ -156,7 +168,8 @@ class ControlPlane:
     def attach_run(self, run, *, checkpoint_path, device=None, pin=False) -> None:
         self.training_run = run
         self.checkpoint_path = checkpoint_path
-        self.device = device
+        if device is not None:
+            self.device = device
         self.pin = pin
 
     def is_training_rank(self, plan: ExecutionPlan) -> bool:

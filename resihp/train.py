@@ -68,7 +68,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
     config = loaded.train
     schedule = {e.after_iteration: e.failed_rank for e in loaded.failures}
     device = select_device()
-    control = ControlPlane.initialize(memory_budget=config.memory_budget_bytes)
+    control = ControlPlane.initialize(memory_budget=config.memory_budget_bytes, device=device)
     plan = build_plan(
         config, step=0, version=0, memory_budget=config.memory_budget_bytes,
         vocab_size=config.vocab_size, sequence_length=config.seq_len,

@@ -138,7 +138,7 @@ def _dp_worker(rank, world, port, out):
     config = TrainConfig(model_dim=256, num_layers=2, num_heads=4, batch_size=8, micro_batch_size=2, seed=3, tp=1,
                          pp=1, dp=world, iterations=4, arch="llama", vocab_size=1024, seq_len=128, ffn_dim=688,
                          dtype="bf16", lr=1e-3, beta1=0.9, beta2=0.95, weight_decay=0.1)
-    cp = ControlPlane(rank, range(world), store, "nccl")
+    cp = ControlPlane(rank, range(world), store, "nccl", device=device)  # NCCL groups split from the world
     cp.form_world(range(world), epoch=0)
     plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
     groups = cp.build_training_groups(plan)
