@@ -186,6 +186,8 @@ class ControlPlane:
         """Safe-point step 6c: every rank creates every group in the same plan order."""
         g = TrainingGroups(world=self.world_group)
         for stage in sorted(plan.stages, key=lambda s: (s.replica_id, s.stage_id)):
+            if len(stage.tp_members) == 1:
+                continue  # a TP degree of 1 needs no communicator (the stage treats None as size 1)
             handle = self._new_group(stage.tp_members)
             if self.rank in stage.tp_members:
                 g.tp = handle
@@ -200,9 +202,17 @@ class ControlPlane:
             handle = self._new_group(members)
             if self.rank in members:
                 g.reduce[members] = handle
-        g.live = self._new_group(self.members)
+        if self._needs_live_group(plan):
+            g.live = self._new_group(self.members)
         self.groups = g
         return g
+
+    def _needs_live_group(self, plan: ExecutionPlan) -> bool:
+        """The live group carries collective state moves; the CUDA bf16 path moves state
+        peer to peer instead (:func:`resihp.recovery.recover`) and does not need it."""
+        from .parallel import peer
+
+        return not (self.training_backend == "nccl" and plan.config.dtype == "bf16" and peer.ENABLED)
 
     def destroy_training_groups(self) -> None:
         import torch.distributed as dist
@@ -273,7 +283,10 @@ class ControlPlane:
         phases["replan_s"] = time.perf_counter() - t0
         t = time.perf_counter()
         self.dissolve_world()
+        phases["dissolve_world_s"] = time.perf_counter() - t
+        t1 = time.perf_counter()
         self.form_world(survivors, epoch=self.epoch + 1)
+        phases["form_world_s"] = time.perf_counter() - t1
         phases["reform_world_s"] = time.perf_counter() - t
         self.agree(reason, plan="" if new_plan is None else new_plan.digest)
         try:

@@ -1,54 +1,138 @@
-"""Fused AG->GEMM / GEMM->RS against NCCL + GEMM at the 1.3B model's layer shapes.
+"""Fused AG->GEMM / GEMM->RS against NCCL + GEMM, on 2-8 GPUs.
 
-    python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 \
-        --master-port 29581 -m resihp.utils.fused_probe
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port 29581 -m resihp.utils.fused_probe            # 1.3B layer shapes (T=4096, d=2048)
+    ... -m resihp.utils.fused_probe --sweep                         # BASELINE config-5 sweep
 
-CUDA-event timing (5 warm-up, 20 launches, max over ranks); rank 0 prints JSON.
+The sweep covers M = 4096..32768 tokens with K, N in {5120, 13824}: column-parallel
+AG->GEMM ``[M, 5120] x [5120, N/tp]`` (N = 5120, 13824) and row-parallel GEMM->RS
+``[M, K/tp] x [K/tp, 5120]`` (K = 5120, 13824), each against NCCL all-gather /
+reduce-scatter with cuBLAS (``torch.matmul``) and, for reference, with this
+package's GEMM. The roofline of a fused op is the slower of its FLOPs at the measured
+bf16 peak and the bytes that must cross NVLink at 770 GB/s per direction.
+
+CUDA-event timing (3 warm-up, 10 launches, max over ranks); rank 0 prints JSON.
 """
+
+from __future__ import annotations
 
 import json
 import os
+import sys
 
 import torch
 import torch.distributed as dist
 
-rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
-torch.cuda.set_device(rank)
-dist.init_process_group("nccl")
-from resihp.parallel.fused import SymmetricWorkspace
-from resihp import ops
-T, d = 4096, 2048
-tl = T // world
-ws = SymmetricWorkspace(dist.group.WORLD, tl, d, torch.device("cuda", rank))
-def t_ev(fn, it=20, warm=5):
-    for _ in range(warm): fn()
-    torch.cuda.synchronize(); dist.barrier()
-    s = torch.cuda.Event(enable_timing=True); e = torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(it): fn()
-    e.record(); torch.cuda.synchronize()
-    v = torch.tensor([s.elapsed_time(e) / it], device="cuda"); dist.all_reduce(v, op=dist.ReduceOp.MAX)
-    return v.item() * 1000
-res = {}
-x = torch.randn(tl, d, device="cuda").bfloat16()
-for name, n in (("qkv", 3 * d // world * 1), ("gate_up", 2 * 5504 // world)):
-    w = torch.randn(n, d, device="cuda").bfloat16()
-    def nccl():
-        xg = torch.empty(T, d, device="cuda", dtype=torch.bfloat16)
-        dist.all_gather_into_tensor(xg, x)
-        return ops.linear(xg, w)
-    def fused():
-        return ws.all_gather_gemm(x, w, False, n)
-    xg_full = torch.randn(T, d, device="cuda").bfloat16()
-    res[f"ag_{name}_n{n}_us"] = dict(nccl=t_ev(nccl), fused=t_ev(fused), gemm_only=t_ev(lambda: ops.linear(xg_full, w)),
-                                     ag_only=t_ev(lambda: dist.all_gather_into_tensor(torch.empty(T, d, device="cuda", dtype=torch.bfloat16), x)))
-for name, k in (("o", d // world), ("down", 5504 // world)):
-    h = torch.randn(T, k, device="cuda").bfloat16(); w = torch.randn(d, k, device="cuda").bfloat16()
-    def nccl():
-        y = ops.linear(h, w); out = torch.empty(tl, d, device="cuda", dtype=torch.bfloat16)
-        dist.reduce_scatter_tensor(out, y); return out
-    res[f"rs_{name}_k{k}_us"] = dict(nccl=t_ev(nccl), fused=t_ev(lambda: ws.gemm_reduce_scatter(h, w, False, d)),
-                                     gemm_only=t_ev(lambda: ops.linear(h, w)))
-ops.check_device_errors(rank)
-if rank == 0: print(json.dumps(res, indent=1))
-ws.close(); dist.destroy_process_group()
+LINK_GBS = 770.0
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f).get("bf16_tflops", 1590.0))
+    return 1590.0
+
+
+def main():
+    from resihp import ops
+    from resihp.parallel.fused import SymmetricWorkspace
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl")
+    dev = torch.device("cuda", rank)
+    sweep = "--sweep" in sys.argv
+    peak = _peaks()
+
+    def t_ev(fn, it=10, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(it):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        v = torch.tensor([s.elapsed_time(e) / it], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return v.item() * 1000
+
+    def roofline(flops, link_bytes):
+        return max(flops / (peak * 1e12), link_bytes / (LINK_GBS * 1e9)) * 1e6
+
+    if sweep:
+        width = 5120
+        ms = (4096, 8192, 16384, 32768)
+        ag_ns, rs_ks = (5120, 13824), (5120, 13824)
+    else:
+        width = 2048
+        ms = (4096,)
+        ag_ns, rs_ks = (3 * 2048, 2 * 5504), (2048, 5504)
+    out = []
+    for m in ms:
+        tl = m // world
+        ws = SymmetricWorkspace(dist.group.WORLD, tl, width, dev)
+        x = torch.randn(tl, width, device=dev).bfloat16()
+        for n_full in ag_ns:
+            n = n_full // world
+            w = (torch.randn(n, width, device=dev) / width**0.5).bfloat16()
+            xg_buf = torch.empty(m, width, device=dev, dtype=torch.bfloat16)
+
+            def nccl_cublas():
+                dist.all_gather_into_tensor(xg_buf, x)
+                return torch.matmul(xg_buf, w.t())
+
+            def nccl_ours():
+                dist.all_gather_into_tensor(xg_buf, x)
+                return ops.linear(xg_buf, w)
+
+            row = dict(op="ag_gemm", m=m, k=width, n=n_full, n_per_rank=n, tp=world,
+                       fused_us=t_ev(lambda: ws.all_gather_gemm(x, w, False, n)),
+                       nccl_cublas_us=t_ev(nccl_cublas), nccl_ours_us=t_ev(nccl_ours),
+                       gemm_only_us=t_ev(lambda: ops.linear(xg_buf, w)))
+            row["roofline_us"] = roofline(2.0 * m * width * n, (world - 1) / world * m * width * 2)
+            out.append(row)
+        for k_full in rs_ks:
+            k = k_full // world
+            h = torch.randn(m, k, device=dev).bfloat16()
+            w = (torch.randn(width, k, device=dev) / k**0.5).bfloat16()
+            y_buf = torch.empty(tl, width, device=dev, dtype=torch.bfloat16)
+
+            def nccl_cublas():
+                y = torch.matmul(h, w.t())
+                dist.reduce_scatter_tensor(y_buf, y)
+                return y_buf
+
+            def nccl_ours():
+                y = ops.linear(h, w)
+                dist.reduce_scatter_tensor(y_buf, y)
+                return y_buf
+
+            row = dict(op="gemm_rs", m=m, k=k_full, k_per_rank=k, n=width, tp=world,
+                       fused_us=t_ev(lambda: ws.gemm_reduce_scatter(h, w, False, width)),
+                       nccl_cublas_us=t_ev(nccl_cublas), nccl_ours_us=t_ev(nccl_ours),
+                       gemm_only_us=t_ev(lambda: ops.linear(h, w)))
+            row["roofline_us"] = roofline(2.0 * m * k * width, (world - 1) / world * m * width * 2)
+            out.append(row)
+        ws.close()
+        del x
+        torch.cuda.empty_cache()
+    ops.check_device_errors(rank)
+    if rank == 0:
+        for row in out:
+            for key in list(row):
+                if key.endswith("_us"):
+                    row[key] = round(row[key], 1)
+            row["fused_vs_nccl_cublas"] = round(row["nccl_cublas_us"] / row["fused_us"], 3)
+            row["fused_fraction_of_roofline"] = round(row["roofline_us"] / row["fused_us"], 3)
+            print(json.dumps(row), flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

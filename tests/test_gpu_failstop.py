@@ -31,3 +31,20 @@ def test_failstop_on_four_gpus():
     assert line["launch"]["killed_ranks"] == [3]
     ev = line["events"][0]
     assert ev["recovered"] and ev["plan_version"] == 1
+
+
+def test_failstop_peer_replica_on_four_gpus():
+    """TP1 x PP2 x DP2: the lost stage's state comes from the peer replica over NVLink."""
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs four GPUs")
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench_recovery.py"), "--gpus", "4", "--layout", "1,2,2", "--small",
+         "--kills", "3:3", "--iterations", "6", "--timeout", "400"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT,
+    )
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["launcher_rc"] == 0, line
+    assert line["launch"]["killed_ranks"] == [3]
+    ev = line["events"][0]
+    assert ev["recovered"] and ev["plan_version"] == 1
+    assert line["steps_seen"][-1] == 6
