@@ -165,6 +165,14 @@ def _timed(run_step, warmup, steps, barrier, reduce_max, local, world):
     return reduce_max(device_s), reduce_max(wall), clocks
 
 
+def _tp_comm(tp):
+    from resihp.parallel import fused
+
+    if tp == 1:
+        return "none"
+    return "fused-nvlink" if fused.ENABLED and tp <= fused.MAX_DEGREE else "nccl"
+
+
 def run_ours(args):
     sys.path.insert(0, ROOT)
     import torch
@@ -241,7 +249,7 @@ def run_ours(args):
             "config": {"model": spec["name"], "baseline_config": args.config, "global_batch": global_batch,
                        "micro_batch": micro_batch, "seq_len": config.seq_len,
                        "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if tp > 1 else ""),
-                       "tp_comm": "fused-nvlink" if (tp > 1 and os.environ.get("RESIHP_FUSED_TP", "1") != "0") else ("nccl" if tp > 1 else "none"),
+                       "tp_comm": _tp_comm(tp),
                        "dp_comm": ("fused-nvlink+adamw" if os.environ.get("RESIHP_FUSED_DP", "1") != "0" else "nccl") if dp > 1 else "none",
                        "l2": "inputs larger than L2 (weights/activations >> 126 MB)"},
             "clocks": clocks,

@@ -31,6 +31,11 @@ from ..ops import _ext
 from ..ops.gemm import linear_wgrad
 
 ENABLED = os.environ.get("RESIHP_FUSED_TP", "1") != "0"
+# Largest TP degree that takes the fused kernels. Above it the NCCL collectives + this
+# package's GEMM are used: in these kernels every CTA pulls a slice of every peer chunk
+# with register-staged loads, which keeps too few bytes in flight once the per-rank
+# chunk is small and the peers many (measured slower than NCCL at TP8).
+MAX_DEGREE = int(os.environ.get("RESIHP_FUSED_TP_MAX_DEGREE", "2"))
 DEBUG = os.environ.get("RESIHP_FUSED_DEBUG", "0") == "1"
 
 

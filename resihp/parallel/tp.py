@@ -210,7 +210,7 @@ class TensorParallelStage:
         self.ws = None
         self.dp = None  # peer mappings of the fused DP reduction (set by the gradient reducer)
         rows = config.micro_batch_size * config.seq_len
-        if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= 8
+        if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= min(8, fused.MAX_DEGREE)
                 and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0):
             self.ws = fused.SymmetricWorkspace(group, rows // self.tp_size, self.dim, self.device)
         self.rope = None

@@ -3,6 +3,7 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         --master-port 29581 -m resihp.utils.fused_probe            # 1.3B layer shapes (T=4096, d=2048)
     ... -m resihp.utils.fused_probe --sweep                         # BASELINE config-5 sweep
+    ... -m resihp.utils.fused_probe --config3                       # Llama-3-8B layer shapes
 
 The sweep covers M = 4096..32768 tokens with K, N in {5120, 13824}: column-parallel
 AG->GEMM ``[M, 5120] x [5120, N/tp]`` (N = 5120, 13824) and row-parallel GEMM->RS
@@ -45,6 +46,7 @@ def main():
     dist.init_process_group("nccl")
     dev = torch.device("cuda", rank)
     sweep = "--sweep" in sys.argv
+    config3 = "--config3" in sys.argv
     peak = _peaks()
 
     def t_ev(fn, it=10, warm=3):
@@ -69,6 +71,10 @@ def main():
         width = 5120
         ms = (4096, 8192, 16384, 32768)
         ag_ns, rs_ks = (5120, 13824), (5120, 13824)
+    elif config3:  # Llama-3-8B layer shapes: QKV with 8 KV heads, gate/up, O, down; one 4096-token micro-batch
+        width = 4096
+        ms = (4096,)
+        ag_ns, rs_ks = (4096 + 2 * 1024, 2 * 14336), (4096, 14336)
     else:
         width = 2048
         ms = (4096,)
