@@ -6,7 +6,7 @@
 //   GEMM->RS   y_r[T/tp, N] = reduce_scatter_tokens(h[T, K] * op(W))
 //
 // Both are the persistent tcgen05 GEMM of gemm.cu (TMA producer warp, one MMA-issuing
-// thread, four epilogue warps, two TMEM accumulators) plus six *copy warps* per CTA that
+// thread, four epilogue warps, two TMEM accumulators) plus four *copy warps* per CTA that
 // move the collective's data with coalesced 16-byte loads and stores while the tensor
 // cores work; every remote byte crosses NVLink exactly once.
 //
@@ -41,7 +41,7 @@
 namespace resihp {
 
 constexpr int kMaxTp = 8;
-constexpr int kCopyWarps = 6;
+constexpr int kCopyWarps = 4;
 constexpr int kFusedThreads = 192 + 32 * kCopyWarps;
 
 struct CommArgs {
@@ -90,12 +90,11 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 }
 
 // Copy `rows` rows of `cols16` 16-byte vectors (row strides in vectors) with the copy-warp
-// threads, sixteen loads in flight per thread (48 KB per CTA): enough to cover the NVLink
-// round trip when the peer reads are spread over many ranks.
+// threads, eight loads in flight per thread.
 __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* src, int64_t sld, int rows,
                                           int cols16, int ct) {
   const int64_t total = int64_t(rows) * cols16;
-  constexpr int kU = 16;
+  constexpr int kU = 8;
   constexpr int kT = 32 * kCopyWarps;
   for (int64_t base = ct; base < total; base += int64_t(kT) * kU) {
     uint4 r[kU];
@@ -443,6 +442,10 @@ void launch_fused(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorM
 }
 
 }  // namespace
+
+// Per launch, every copy warp of the grid bumps the AG publish counter once and each
+// chunk's ready counter once; the host advances its bases by this much per call.
+int fused_counter_step(int grid) { return kCopyWarps * grid; }
 
 int fused_grid(int m, int n, int tp) {
   (void)tp;

@@ -88,6 +88,7 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
 namespace resihp {
 
 int fused_grid(int m, int n, int tp);
+int fused_counter_step(int grid);
 void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
              int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
              unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,

@@ -309,6 +309,7 @@ void symm_close_t(int64_t p) { symm_close(as_ptr<void>(p)); }
 void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
 
 int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
+int64_t fused_counter_step_t(int64_t grid) { return fused_counter_step(int(grid)); }
 
 void ag_gemm_t(torch::Tensor x_local, int64_t own_slot, std::vector<int64_t> peer_slot, torch::Tensor xg,
                torch::Tensor w, bool w_mn, torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
@@ -450,6 +451,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &resihp::symm_close_t);
   m.def("symm_free", &resihp::symm_free_t);
   m.def("fused_grid", &resihp::fused_grid_t);
+  m.def("fused_counter_step", &resihp::fused_counter_step_t);
   m.def("ag_gemm", &resihp::ag_gemm_t);
   m.def("gemm_rs", &resihp::gemm_rs_t);
   m.def("symm_region", &resihp::symm_region_t);

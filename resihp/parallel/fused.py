@@ -138,8 +138,9 @@ class SymmetricWorkspace:
         k.ag_gemm(x_local, self._slot(self.base, e), [self._slot(p, e) for p in self.peers], xg, w, w_mn, y,
                   self.rank, self.tp, e, self._sig_ag(self.base), [self._sig_ag(p) for p in self.peers],
                   self._pub(self.base), self.pub_base, self._ready(self.base), self.ready_base, grid)
-        self.pub_base += 4 * grid
-        self.ready_base += 4 * grid
+        step = k.fused_counter_step(grid)  # the kernel's own per-launch counter increment
+        self.pub_base += step
+        self.ready_base += step
         _debug_check(f"ag_gemm epoch {e}", x_local.device)
         return y, xg
 
