@@ -59,8 +59,9 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
     config = TrainConfig(**config_dict)
     schedule = {int(k): v for k, v in failures.items()}
     os.chdir(out_dir)
-    cp = ControlPlane.initialize(training_backend="gloo")
-    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    cp = ControlPlane.initialize(training_backend="gloo", memory_budget=config.memory_budget_bytes)
+    plan = build_plan(config, step=0, version=0, memory_budget=config.memory_budget_bytes,
+                      vocab_size=config.vocab_size, sequence_length=config.seq_len)
     groups = cp.build_training_groups(plan)
     cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=Path(out_dir, "checkpoint.pt"))
     record = {"rank": rank, "losses": {}, "plans": [plan.digest], "stopped": None, "recoveries": []}
@@ -150,4 +151,46 @@ def a2_entry(rank, env, config_dict, anchor_path, start, out_dir):
     record = verify.steps_from_anchor(config, anchor, start=completed, count=1)[0]
     cmp = verify.compare_shards(run.stage, record, lr=config.lr)
     write_result(out_dir, rank, {"rank": rank, "a1": a1, "cmp": cmp})
+    cp.shutdown()
+
+
+def planned_entry(rank, env, config_dict, failed, steps, out_dir):
+    """Train the plan a failure sequence leads to, from the seeded initialisation.
+
+    ``rank`` indexes the survivors; no recovery happens -- this isolates the numerics of
+    a post-failure layout (heterogeneous TP boundaries, migrated layers, replicas with
+    different layouts reduced through the logical path).
+    """
+    _setup(env)
+    from harness import write_result
+    from resihp import membership
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run
+
+    config = TrainConfig(**config_dict)
+    survivors = [r for r in range(config.world_size) if r not in failed]
+    plan_rank = survivors[rank]
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    seen = []
+    for i, r in enumerate(failed):
+        seen.append(r)
+        plan = build_plan(config, step=i + 1, version=plan.version + 1, failed_ranks=tuple(seen), previous=plan,
+                          vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    store = membership.connect(os.environ[membership.HOST_ENV], os.environ[membership.PORT_ENV])
+    cp = ControlPlane(plan_rank, survivors, store, "gloo")
+    cp.form_world(survivors, epoch=0)
+    groups = cp.build_training_groups(plan)
+    run = initial_run(plan, rank=plan_rank, groups=groups)
+    losses = [run.step() if run is not None else None for _ in range(steps)]
+    from resihp.recovery import stage_of
+
+    stage = stage_of(plan, plan_rank)
+    result = {"rank": plan_rank, "losses": losses, "replica": None if stage is None else stage.replica_id}
+    if run is not None:
+        result.update(shards={n: t.detach().tolist() for n, (t, _d) in run.stage.local_shards().items()},
+                      tp_rank=run.stage.tp_rank, tp_size=run.stage.tp_size,
+                      dims={n: d for n, (_t, d) in run.stage.local_shards().items()})
+    write_result(out_dir, rank, result)
     cp.shutdown()

@@ -2,7 +2,10 @@
 
 * a checkpoint corrupted right after its commit -> every survivor raises
   ``checkpoint_unusable`` at the next safe point;
-* one rank planning differently -> every survivor raises ``plan_disagreement``.
+* one rank planning differently -> every survivor raises ``plan_disagreement``;
+* a live replicated weight tampered on a donor right after the commit -> the moved
+  state no longer equals the checkpoint (principle A1) -> ``state_mismatch``
+  (the reference's fault injector, ``tests/test_recovery.py:455-488``).
 Both leave no process group behind and exit cleanly.
 """
 
@@ -57,6 +60,12 @@ def _entry(rank, env, mode, out_dir):
                 payload = t.load(ck, weights_only=False)
                 payload["params"]["final_norm.weight"] = payload["params"]["final_norm.weight"] + 1
                 t.save(payload, ck)
+            if mode == "tamper" and it == 2 and rank == 0:
+                import torch as t
+
+                with t.no_grad():
+                    st = cp.training_run.stage
+                    st.flat.view(st.flat.master, "final_norm.weight").add_(1.0)
             fail_stop({2: 3}, rank, it)
             lost = cp.observe()
             if lost:
@@ -75,7 +84,8 @@ def _entry(rank, env, mode, out_dir):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("mode,code", [("corrupt", "checkpoint_unusable"), ("disagree", "plan_disagreement")])
+@pytest.mark.parametrize("mode,code", [("corrupt", "checkpoint_unusable"), ("disagree", "plan_disagreement"),
+                                       ("tamper", "state_mismatch")])
 def test_consistent_stop(mode, code, tmp_path):
     codes = run_ranks(_entry, 4, mode, str(tmp_path))
     assert_killed(codes, [3], mode)
