@@ -83,6 +83,7 @@ class ControlPlane:
         self.state_digest = ""
         self.pin = False
         self.last_recovery: dict = {}
+        self.resume_cursor = 0  # completed iterations training continues from after a safe point
 
     @classmethod
     def initialize(cls, *, training_backend=None, memory_budget=None, device=None) -> "ControlPlane":
@@ -246,7 +247,7 @@ class ControlPlane:
     def _recover_state(self, plan, previous, cursor) -> None:
         from .recovery import recover
 
-        self.training_run, self.state_digest = recover(
+        self.training_run, self.state_digest, self.resume_cursor = recover(
             self.training_run, plan=plan, previous=previous, rank=self.rank, cursor=cursor,
             checkpoint_path=self.checkpoint_path, groups=self.groups, device=self.device, pin=self.pin,
         )
@@ -267,7 +268,12 @@ class ControlPlane:
                 raise ConsistentStop(StopReason(_DIGEST_STOP[label], f"ranks disagree on the {label} digest: {sorted(values)}"))
 
     def safe_point(self, config: TrainConfig, plan: ExecutionPlan, failed_ranks, lost, *, next_step: int):
-        """Steps 4-9 of the fail-stop safe point; returns ``(new plan, failed ranks)``."""
+        """Steps 4-9 of the fail-stop safe point; returns ``(new plan, failed ranks)``.
+
+        Afterwards :attr:`resume_cursor` holds the completed-iteration count training
+        continues from (``next_step``, or an older checkpoint's count after a rollback),
+        the same on every rank.
+        """
         t0 = time.perf_counter()
         phases = {}
         failed = tuple(sorted(set(failed_ranks) | set(lost)))

@@ -497,7 +497,12 @@ def _p2p_recover(run, *, plan, rank, anchor, groups, device, cursor, pin):
 
 
 def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: TrainingGroups, device=None, pin=False):
-    """Safe-point step 7: execute ``plan``'s state routes; returns ``(run, state digest)``.
+    """Safe-point step 7: execute ``plan``'s state routes.
+
+    Returns ``(run, state digest, resume cursor)``: the cursor is the number of completed
+    iterations training continues from -- ``cursor`` itself, or the checkpoint's count
+    when the plan needs a checkpoint route and the checkpoint is older than the live
+    state (every rank then rolls back to it).
 
     Every surviving rank calls this (the idle ones too: their shards may be donors).
     The checkpoint is read only when some route needs it or when it is current, in which
@@ -529,10 +534,10 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
             problems = checkpoint_mismatches(new_run, plan=plan, rank=rank, anchor=anchor)
             if problems:
                 raise ReshardError(f"rank {rank} state differs from the checkpoint: {problems[:5]}")
-        return new_run, ck_digest
+        return new_run, ck_digest, completed if rollback else cursor
     gathered = [None] * dist.get_world_size(groups.world)
     dist.all_gather_object(gathered, (rank, state_fingerprint(new_run)), group=groups.world)
-    return new_run, sha256(repr(sorted(gathered)).encode("utf-8")).hexdigest()
+    return new_run, sha256(repr(sorted(gathered)).encode("utf-8")).hexdigest(), cursor
 
 
 def checkpoint_mismatches(run, *, plan, rank, anchor) -> list[str]:

@@ -83,8 +83,9 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
     digests = [plan.digest]
     tokens_per_step = config.batch_size * config.seq_len
     try:
-        for step in range(config.iterations):
-            iteration = step + 1
+        iteration = 0
+        while iteration < config.iterations:
+            iteration += 1
             if control.training_run is not None:
                 trained.append(iteration)
             t0 = time.perf_counter()
@@ -113,8 +114,11 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
                 digests.append(plan.digest)
                 pending_recovery = {"rank": control.rank, "event": len(versions) - 1, "lost": list(lost),
                                     "after_iteration": iteration, "plan_version": plan.version,
+                                    "resumed_from": control.resume_cursor,
                                     "safe_point_s": time.perf_counter() - t_fail,
                                     "phases": control.last_recovery, "t_fail": t_fail}
+                # a rollback to an older checkpoint re-runs the iterations after it
+                iteration = control.resume_cursor
         if pending_recovery is not None:
             pending_recovery.pop("t_fail")
             pending_recovery["seconds"] = pending_recovery["safe_point_s"]

@@ -67,12 +67,14 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
     record = {"rank": rank, "losses": {}, "plans": [plan.digest], "stopped": None, "recoveries": []}
     failed = ()
     try:
-        for step in range(config.iterations):
-            it = step + 1
+        it = 0
+        while it < config.iterations:
+            it += 1
             loss = cp.training_step()
             if loss is not None:
                 record["losses"][str(it)] = loss
-            cp.commit_checkpoint(plan, cursor=it)
+            if it % config.checkpoint_every == 0:
+                cp.commit_checkpoint(plan, cursor=it)
             write_result(out_dir, rank, record)
             fail_stop(schedule, rank, it)
             lost = cp.observe()
@@ -80,11 +82,14 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
                 import shutil
 
                 # the lowest survivor keeps the checkpoint this failure resumes from
-                if rank == min(r for r in cp.members if r not in lost):
-                    shutil.copy(Path(out_dir, "checkpoint.pt"), Path(out_dir, f"anchor_{it}.pt"))
+                ck = Path(out_dir, "checkpoint.pt")
+                if rank == min(r for r in cp.members if r not in lost) and ck.exists():
+                    shutil.copy(ck, Path(out_dir, f"anchor_{it}.pt"))
                 plan, failed = cp.safe_point(config, plan, failed, lost, next_step=it)
                 record["plans"].append(plan.digest)
-                record["recoveries"].append({"after": it, "lost": list(lost), "phases": cp.last_recovery})
+                record["recoveries"].append({"after": it, "lost": list(lost), "phases": cp.last_recovery,
+                                             "resumed_from": cp.resume_cursor})
+                it = cp.resume_cursor
     except ConsistentStop as stop:
         record["stopped"] = stop.reason.code
         write_result(out_dir, rank, record)
@@ -121,7 +126,7 @@ def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir):
     anchor, completed = load_anchor(anchor_path)
     run = run_from_anchor(plan, rank=plan_rank, anchor=anchor, completed=completed, groups=groups)
     losses = {}
-    for it in range(after + 1, config.iterations + 1):
+    for it in range(completed + 1, config.iterations + 1):
         loss = run.step() if run is not None else None
         if loss is not None:
             losses[str(it)] = loss

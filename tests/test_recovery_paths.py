@@ -1,0 +1,69 @@
+"""The two recovery paths around the checkpoint cadence (CPU/Gloo, real SIGKILLs).
+
+* **No checkpoint needed.** With a peer replica every lost shard survives on a live
+  rank, so a run that never writes a checkpoint recovers exactly like one that writes
+  one every iteration: after the fail-stop both continue with bit-identical losses.
+* **Rollback.** Without a peer replica (DP = 1) the dead rank's shards come from the
+  checkpoint. With ``checkpoint_every = 2`` a kill after iteration 3 finds a checkpoint of
+  iteration 2: every survivor rolls back to it, re-runs iteration 3 onwards under the new
+  plan, and matches, bit for bit, an uninterrupted run of the new plan from that
+  checkpoint.
+"""
+
+import os
+
+import pytest
+
+import dist_entries
+from harness import assert_killed, read_results, run_ranks
+
+BASE = dict(model_dim=32, num_layers=4, num_heads=4, batch_size=8, micro_batch_size=2, seed=4, iterations=6,
+            arch="llama", vocab_size=64, seq_len=8, ffn_dim=64, lr=1e-3, beta2=0.95)
+
+
+def _losses_after(results, first):
+    out = {}
+    for r in results.values():
+        for it, loss in r["losses"].items():
+            if int(it) >= first:
+                out.setdefault(int(it), set()).add(loss)
+    return {it: sorted(v) for it, v in sorted(out.items())}
+
+
+@pytest.mark.slow
+def test_peer_replica_recovery_needs_no_checkpoint(tmp_path):
+    runs = {}
+    for every in (1, 1000):
+        out = tmp_path / f"every{every}"
+        out.mkdir()
+        config = dict(BASE, tp=1, pp=2, dp=2, checkpoint_every=every)
+        codes = run_ranks(dist_entries.failstop_entry, 4, config, {"2": 3}, str(out))
+        assert_killed(codes, [3], f"checkpoint_every={every}")
+        results = read_results(out, [0, 1, 2])
+        assert all(r["stopped"] is None and r["recoveries"][0]["resumed_from"] == 2 for r in results.values())
+        assert os.path.exists(out / "checkpoint.pt") == (every == 1)
+        runs[every] = _losses_after(results, 3)
+    assert runs[1] == runs[1000] and sorted(runs[1]) == [3, 4, 5, 6]
+
+
+@pytest.mark.slow
+def test_rollback_to_an_older_checkpoint_matches_a_rerun(tmp_path):
+    config = dict(BASE, tp=2, pp=2, dp=1, checkpoint_every=2)
+    codes = run_ranks(dist_entries.failstop_entry, 4, config, {"3": 3}, str(tmp_path))
+    assert_killed(codes, [3], "rollback")
+    results = read_results(tmp_path, [0, 1, 2])
+    for r in results.values():
+        assert r["stopped"] is None, r
+        assert r["recoveries"][0]["after"] == 3 and r["recoveries"][0]["resumed_from"] == 2
+    anchor = tmp_path / "anchor_3.pt"
+    rerun_dir = tmp_path / "rerun"
+    rerun_dir.mkdir()
+    codes = run_ranks(dist_entries.rerun_entry, 3, config, [3], 3, str(anchor), str(rerun_dir))
+    assert set(codes.values()) == {0}
+    rerun = read_results(rerun_dir, [0, 1, 2])
+    got = _losses_after(results, 3)
+    want = {}
+    for r in rerun.values():
+        for it, loss in r["losses"].items():
+            want.setdefault(int(it), set()).add(loss)
+    assert got == {it: sorted(v) for it, v in sorted(want.items())} and sorted(got) == [3, 4, 5, 6]
