@@ -34,6 +34,7 @@ from .config import TrainConfig
 from .parallel.dp import reduction_topology
 from .plan import ExecutionPlan, InfeasiblePlan, boundary_hops, build_plan
 from .recovery import TrainingGroups
+from .utils.trace import nvtx_range
 
 STOP_CODES = (
     "no_feasible_tp",
@@ -239,10 +240,11 @@ class ControlPlane:
 
         if not self.is_training_rank(plan):
             return
-        commit_checkpoint(
-            self.training_run, self.checkpoint_path, plan=plan, groups=self.groups,
-            writer=self.rank == plan.active_ranks[0], cursor=cursor, device=self.device,
-        )
+        with nvtx_range("checkpoint_commit"):
+            commit_checkpoint(
+                self.training_run, self.checkpoint_path, plan=plan, groups=self.groups,
+                writer=self.rank == plan.active_ranks[0], cursor=cursor, device=self.device,
+            )
 
     def _recover_state(self, plan, previous, cursor) -> None:
         from .recovery import recover
@@ -288,21 +290,25 @@ class ControlPlane:
             reason = StopReason(error.reason.code, error.reason.message)
         phases["replan_s"] = time.perf_counter() - t0
         t = time.perf_counter()
-        self.dissolve_world()
+        with nvtx_range("dissolve_world"):
+            self.dissolve_world()
         phases["dissolve_world_s"] = time.perf_counter() - t
         t1 = time.perf_counter()
-        self.form_world(survivors, epoch=self.epoch + 1)
+        with nvtx_range("form_world"):
+            self.form_world(survivors, epoch=self.epoch + 1)
         phases["form_world_s"] = time.perf_counter() - t1
         phases["reform_world_s"] = time.perf_counter() - t
         self.agree(reason, plan="" if new_plan is None else new_plan.digest)
         try:
             t = time.perf_counter()
-            self.build_training_groups(new_plan)
+            with nvtx_range("build_groups"):
+                self.build_training_groups(new_plan)
             phases["build_groups_s"] = time.perf_counter() - t
             t = time.perf_counter()
             reason = None
             try:
-                self._recover_state(new_plan, plan, next_step)
+                with nvtx_range("recover_state"):
+                    self._recover_state(new_plan, plan, next_step)
             except Exception as error:  # classified below; anything else is a bug
                 from .recovery import recovery_stop_code
 

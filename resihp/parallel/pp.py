@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from ..planner.pp import pipeline_phases
+from ..utils.trace import nvtx_range
 from .dp import ActivationLog, executor_route, global_micro_count, stage_pipeline
 
 
@@ -142,8 +143,9 @@ class PipelineRuntime:
     def _exchange(ops):
         ops = list(ops)
         if ops:
-            for work in dist.batch_isend_irecv(ops):
-                work.wait()
+            with nvtx_range("p2p"):
+                for work in dist.batch_isend_irecv(ops):
+                    work.wait()
 
     def _recv_forward(self, shape):
         if self.upstream is None:
@@ -210,11 +212,12 @@ class PipelineRuntime:
             count += 1
             self.schedule.append(f"F{index}")
             data = chunks[index].to(device, non_blocking=True)
-            out = stage.forward(
-                tokens=data if (stage.is_first or stage.is_last) else None,
-                hidden=received,
-                loss_scale=loss_scale,
-            )
+            with nvtx_range(f"F{index}"):
+                out = stage.forward(
+                    tokens=data if (stage.is_first or stage.is_last) else None,
+                    hidden=received,
+                    loss_scale=loss_scale,
+                )
             if stage.is_last:
                 total.add_(out.detach())
             self.activation_log.retain(index)
@@ -228,10 +231,11 @@ class PipelineRuntime:
             self.schedule.append(f"B{index}")
             received = inputs.pop(0)
             out = outputs.pop(0)
-            if stage.is_last:
-                out.backward()
-            else:
-                out.backward(grad_output)
+            with nvtx_range(f"B{index}"):
+                if stage.is_last:
+                    out.backward()
+                else:
+                    out.backward(grad_output)
             self.activation_log.release(index)
             return None if stage.is_first else received.grad
 
@@ -250,8 +254,9 @@ class PipelineRuntime:
             self._send_backward(backward(self._recv_backward(shape)))
 
         self.schedule.append("W")
-        if self.reducer is None or not self.reducer.reduce_and_step(stage):
-            stage.optimizer_step()
+        with nvtx_range("W"):
+            if self.reducer is None or not self.reducer.reduce_and_step(stage):
+                stage.optimizer_step()
         if not stage.is_last:
             return None
         return total if return_tensor else float(total)

@@ -89,13 +89,19 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
             if control.training_run is not None:
                 trained.append(iteration)
             t0 = time.perf_counter()
-            loss = control.training_step()
+            events = None
             if device.type == "cuda":
+                events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                events[0].record()
+            loss = control.training_step()
+            if events is not None:
+                events[1].record()
                 torch.cuda.synchronize()
             dt = time.perf_counter() - t0
             if loss is not None:
                 _emit({"step": iteration, "rank": control.rank, "loss": loss, "plan_version": plan.version,
-                       "step_s": dt, "tokens_per_s": tokens_per_step / dt if dt > 0 else None})
+                       "step_s": dt, "tokens_per_s": tokens_per_step / dt if dt > 0 else None,
+                       "device_ms": None if events is None else events[0].elapsed_time(events[1])})
             if pending_recovery is not None:
                 # failure -> end of the first resumed step, as seen by this rank
                 pending_recovery["seconds"] = time.perf_counter() - pending_recovery.pop("t_fail")

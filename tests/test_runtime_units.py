@@ -117,3 +117,11 @@ def test_flat_state_views_and_parity_on_cpu():
     flat.set_parity(0)
     assert flat.grad is flat.grads[0]
     assert flat.export()["offsets"] == {"a": 0, "b": flat.offsets["b"][0]}
+
+
+def test_trace_ranges_are_free_when_off():
+    from resihp.utils import trace
+
+    with trace.nvtx_range("F0"):
+        pass
+    assert not trace._ON or torch.cuda.is_available()
