@@ -130,6 +130,48 @@ def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: i
     return path
 
 
+class CheckpointWriter:
+    """Writes checkpoints on a background thread, one at a time, in submission order.
+
+    The gather that assembles the logical state stays a collective on the training
+    ranks; only the writer rank's serialisation, read-back verification and atomic
+    rename move off the iteration's critical path. :meth:`flush` waits for the write in
+    flight and re-raises its error. Callers flush wherever the file must be current: at a
+    safe point before any rank reads it, before a scheduled self-kill (so a fail-stop
+    still happens after its iteration's commit, as in the reference), and at shutdown.
+    """
+
+    def __init__(self):
+        self._thread = None
+        self._error: BaseException | None = None
+
+    def submit(self, path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int) -> None:
+        import threading
+
+        self.flush()
+
+        def work():
+            try:
+                save_checkpoint(path, config, full, completed_steps=completed_steps, plan_version=plan_version)
+            except BaseException as error:  # re-raised by flush() on the training thread
+                self._error = error
+
+        self._thread = threading.Thread(target=work, name="resihp-checkpoint", daemon=True)
+        self._thread.start()
+
+    def flush(self) -> None:
+        if self._thread is not None:
+            self._thread.join()
+            self._thread = None
+        if self._error is not None:
+            error, self._error = self._error, None
+            raise error
+
+    @property
+    def pending(self) -> bool:
+        return self._thread is not None and self._thread.is_alive()
+
+
 def read_payload(path, *, mmap: bool = False) -> dict:
     path = Path(path)
     if not path.exists():

@@ -51,6 +51,8 @@ GROUP_TIMEOUT = timedelta(seconds=int(os.environ.get("RESIHP_GROUP_TIMEOUT", "30
 # (ncclCommSplit) inside the safe point instead of being initialised from scratch on its
 # first collective.
 NCCL_SPLIT = os.environ.get("RESIHP_NCCL_SPLIT", "1") != "0"
+# The checkpoint writer rank serialises and writes the file on a background thread.
+ASYNC_CHECKPOINT = os.environ.get("RESIHP_ASYNC_CHECKPOINT", "1") != "0"
 
 
 @dataclass(frozen=True)
@@ -85,6 +87,11 @@ class ControlPlane:
         self.pin = False
         self.last_recovery: dict = {}
         self.resume_cursor = 0  # completed iterations training continues from after a safe point
+        self.checkpoint_writer = None
+        if ASYNC_CHECKPOINT:
+            from .checkpoint import CheckpointWriter
+
+            self.checkpoint_writer = CheckpointWriter()
 
     @classmethod
     def initialize(cls, *, training_backend=None, memory_budget=None, device=None) -> "ControlPlane":
@@ -244,7 +251,13 @@ class ControlPlane:
             commit_checkpoint(
                 self.training_run, self.checkpoint_path, plan=plan, groups=self.groups,
                 writer=self.rank == plan.active_ranks[0], cursor=cursor, device=self.device,
+                background=self.checkpoint_writer,
             )
+
+    def flush_checkpoint(self) -> None:
+        """Wait for this rank's checkpoint write in flight (a no-op on non-writers)."""
+        if self.checkpoint_writer is not None:
+            self.checkpoint_writer.flush()
 
     def _recover_state(self, plan, previous, cursor) -> None:
         from .recovery import recover
@@ -278,6 +291,9 @@ class ControlPlane:
         """
         t0 = time.perf_counter()
         phases = {}
+        # the checkpoint file must be complete before the first agreement: every rank
+        # may read it during recovery
+        self.flush_checkpoint()
         failed = tuple(sorted(set(failed_ranks) | set(lost)))
         survivors = tuple(r for r in self.members if r not in set(lost))
         new_plan, reason = None, None
@@ -329,6 +345,7 @@ class ControlPlane:
     def shutdown(self) -> None:
         import torch.distributed as dist
 
+        self.flush_checkpoint()
         if self.training_run is not None:
             self.training_run.stage.close_comm(barrier=True)
         self.destroy_training_groups()

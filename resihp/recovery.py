@@ -256,13 +256,22 @@ def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems
     return full_state
 
 
-def commit_checkpoint(run, path, *, plan, groups: TrainingGroups, writer: bool, cursor: int, device=None):
-    """Safe-point step 2: gather every shard and atomically write the one checkpoint."""
+def commit_checkpoint(run, path, *, plan, groups: TrainingGroups, writer: bool, cursor: int, device=None,
+                      background=None):
+    """Safe-point step 2: gather every shard and atomically write the one checkpoint.
+
+    ``background`` (a :class:`~resihp.checkpoint.CheckpointWriter`) moves the writer's
+    file write to its thread; the gather itself is a collective and stays in line.
+    """
     if groups.executor is None:
         return
     dst = plan.active_ranks[0]
     full = gather_full_state(run, plan, group=groups.executor, dst=dst, device=device or "cpu")
-    if writer:
+    if not writer:
+        return
+    if background is not None:
+        background.submit(path, plan.config, full, completed_steps=cursor, plan_version=plan.version)
+    else:
         save_checkpoint(path, plan.config, full, completed_steps=cursor, plan_version=plan.version)
 
 

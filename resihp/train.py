@@ -42,11 +42,17 @@ def select_device():
     return torch.device("cuda", torch.cuda.current_device())
 
 
-def fail_stop(schedule, rank: int, iteration: int) -> None:
-    """``SIGKILL`` this process if the schedule fails ``rank`` after ``iteration``."""
+def fail_stop(schedule, rank: int, iteration: int, *, before=None) -> None:
+    """``SIGKILL`` this process if the schedule fails ``rank`` after ``iteration``.
+
+    ``before`` runs first (the worker passes its checkpoint flush, so a scheduled
+    fail-stop happens after its iteration's commit is on disk).
+    """
     import signal
 
     if schedule.get(iteration) == rank:
+        if before is not None:
+            before()
         os.kill(os.getpid(), signal.SIGKILL)
 
 
@@ -111,7 +117,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
             if iteration % config.checkpoint_every == 0:
                 control.commit_checkpoint(plan, cursor=iteration)
             control.quiesce()  # the iteration, its commit and all their GPU work are complete
-            fail_stop(schedule, control.rank, iteration)
+            fail_stop(schedule, control.rank, iteration, before=control.flush_checkpoint)
             t_fail = time.perf_counter()
             lost = control.observe()
             if lost:

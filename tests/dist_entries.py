@@ -76,16 +76,16 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
             if it % config.checkpoint_every == 0:
                 cp.commit_checkpoint(plan, cursor=it)
             write_result(out_dir, rank, record)
-            fail_stop(schedule, rank, it)
+            fail_stop(schedule, rank, it, before=cp.flush_checkpoint)
             lost = cp.observe()
             if lost:
                 import shutil
 
-                # the lowest survivor keeps the checkpoint this failure resumes from
-                ck = Path(out_dir, "checkpoint.pt")
-                if rank == min(r for r in cp.members if r not in lost) and ck.exists():
-                    shutil.copy(ck, Path(out_dir, f"anchor_{it}.pt"))
                 plan, failed = cp.safe_point(config, plan, failed, lost, next_step=it)
+                # the lowest survivor keeps the checkpoint this failure resumed from
+                ck = Path(out_dir, "checkpoint.pt")
+                if rank == min(cp.members) and ck.exists():
+                    shutil.copy(ck, Path(out_dir, f"anchor_{it}.pt"))
                 record["plans"].append(plan.digest)
                 record["recoveries"].append({"after": it, "lost": list(lost), "phases": cp.last_recovery,
                                              "resumed_from": cp.resume_cursor})

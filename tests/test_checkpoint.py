@@ -80,3 +80,25 @@ def test_reference_reads_our_checkpoint(tmp_path):
     out = subprocess.run([sys.executable, "-c", code, REF, str(path)], capture_output=True, text=True, check=True, cwd="/")
     completed, names = json.loads(out.stdout)
     assert completed == 2 and names == sorted(run.stage.logical_state_dict())
+
+
+def test_background_writer_orders_writes_and_surfaces_errors(tmp_path):
+    from resihp.checkpoint import CheckpointWriter
+
+    run = ReferenceRun(C)
+    writer = CheckpointWriter()
+    path = tmp_path / "ck.pt"
+    for step in range(1, 3):
+        run.step()
+        writer.submit(path, C, run.full_state(), completed_steps=step, plan_version=0)
+    writer.flush()
+    assert not writer.pending
+    anchor, completed = load_anchor(path)
+    assert completed == 2
+    for name, (view, _d) in run.stage.local_shards().items():
+        assert torch.equal(anchor[name]["param"], view)
+    writer.submit(path, C, run.full_state(), completed_steps=3, plan_version=-1)
+    with pytest.raises(CheckpointError, match="plan_version"):
+        writer.flush()
+    assert load_anchor(path)[1] == 2  # the failed write left the previous checkpoint in place
+    writer.flush()  # the error is reported once

@@ -57,6 +57,7 @@ def _entry(rank, env, mode, out_dir):
             if mode == "corrupt" and it == 2 and rank == 0:
                 import torch as t
 
+                cp.flush_checkpoint()  # the writer's background write must be on disk first
                 payload = t.load(ck, weights_only=False)
                 payload["params"]["final_norm.weight"] = payload["params"]["final_norm.weight"] + 1
                 t.save(payload, ck)
