@@ -4,6 +4,8 @@
     python -m resihp.utils.kernel_probe attn   # causal attention fwd + bwd, B2 H16 S2048 D128
     python -m resihp.utils.kernel_probe dp     # fused DP all-reduce + AdamW, 2 replicas emulated, 64M elements
     python -m resihp.utils.kernel_probe reshard  # state move TP2 -> TP1 of one 1.3B layer group (3 fields)
+    python -m resihp.utils.kernel_probe fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
+    python -m resihp.utils.kernel_probe fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
 and launches every kernel a handful of times, so a capture of one or two launches ends
@@ -91,10 +93,28 @@ def reshard() -> None:
         gp.launch(dev)
 
 
+def fused_ag(tp: int = 2) -> None:
+    from resihp.utils.fused_emulation import emulate_ag
+
+    for epoch in range(1, 4):
+        emulate_ag(4096, 2048, 3 * 2048 // tp, tp=tp, epoch=epoch)
+
+
+def fused_rs(tp: int = 2) -> None:
+    from resihp.utils.fused_emulation import emulate_rs
+
+    for epoch in range(1, 4):
+        emulate_rs(4096, 5504 // tp, 2048, tp=tp, epoch=epoch)
+
+
 def main(argv=None) -> None:
-    what = (argv or sys.argv[1:])[0]
+    args = argv or sys.argv[1:]
+    what = args[0]
     torch.manual_seed(0)
-    {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard}[what]()
+    if what in ("fused_ag", "fused_rs"):
+        {"fused_ag": fused_ag, "fused_rs": fused_rs}[what](int(args[1]) if len(args) > 1 else 2)
+    else:
+        {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard}[what]()
     torch.cuda.synchronize()
     ops.check_device_errors()
     print("ok", what)
