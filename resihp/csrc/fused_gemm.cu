@@ -41,8 +41,21 @@
 namespace resihp {
 
 constexpr int kMaxTp = 8;
-constexpr int kCopyWarps = 4;
-constexpr int kFusedThreads = 192 + 32 * kCopyWarps;
+
+// Copy-warp configuration per kernel variant.
+//   V = 0: four copy warps, eight 16-byte loads in flight per thread; the AG pull gives
+//          every CTA a slice of every peer chunk and a chunk's tiles start once all CTAs
+//          finished it (validated at TP2).
+//   V = 1: six copy warps, sixteen loads in flight per thread; the AG pull hands out
+//          (peer chunk, row block, row slice) units and a tile starts as soon as its own
+//          128-row block is complete; the RS pull gives each copy warp a fixed subset of
+//          the peers and takes whichever of them is ready first (for TP > 2).
+template <int V>
+struct CopyCfg {
+  static constexpr int kWarps = V == 0 ? 4 : 6;
+  static constexpr int kUnroll = V == 0 ? 8 : 16;
+  static constexpr int kThreads = 192 + 32 * kWarps;
+};
 
 struct CommArgs {
   int rank, tp, rows_per_rank;
@@ -57,8 +70,11 @@ struct CommArgs {
   unsigned* peer_sig_ag[kMaxTp];           // each rank's sig_ag array
   unsigned* pub;                           // local publish counter
   unsigned pub_target;
-  unsigned* ready;                         // local per-chunk ready counters [tp]
+  unsigned* ready;                         // local per-chunk ready counters [tp] (V = 0)
   unsigned ready_target;
+  unsigned* rb_ready;                      // local per-row-block ready counters [tp * T/tp/128] (V = 1)
+  unsigned rb_target;
+  int slices;                              // row slices per 128-row block in the V = 1 pull
   // RS
   __nv_bfloat16* part_local;               // this rank's partial buffer [T, N] for this epoch
   const __nv_bfloat16* peer_part[kMaxTp];  // each rank's partial buffer for this epoch
@@ -89,13 +105,12 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   return v;
 }
 
-// Copy `rows` rows of `cols16` 16-byte vectors (row strides in vectors) with the copy-warp
-// threads, eight loads in flight per thread.
+// Copy `rows` rows of `cols16` 16-byte vectors (row strides in vectors) with `kT` threads
+// (thread index `ct`), `kU` loads in flight per thread.
+template <int kT, int kU>
 __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* src, int64_t sld, int rows,
                                           int cols16, int ct) {
   const int64_t total = int64_t(rows) * cols16;
-  constexpr int kU = 8;
-  constexpr int kT = 32 * kCopyWarps;
   for (int64_t base = ct; base < total; base += int64_t(kT) * kU) {
     uint4 r[kU];
     #pragma unroll
@@ -143,11 +158,14 @@ __device__ __forceinline__ void fused_tile(int t, int tiles_m_chunk, int tiles_n
   tn_out = in_group / size;
 }
 
-template <int BN, bool B_MN, int MODE>
-__global__ void __launch_bounds__(kFusedThreads, 1)
+template <int BN, bool B_MN, int MODE, int V>
+__global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_a2,
                       const __grid_constant__ CUtensorMap tma_b, FusedArgs g) {
   using S = FusedShape<BN>;
+  constexpr int kCW = CopyCfg<V>::kWarps;
+  constexpr int kCT = 32 * kCW;
+  constexpr int kCU = CopyCfg<V>::kUnroll;
   constexpr int kStages = S::kStages;
   constexpr int kPullSlots = 4;
   extern __shared__ uint8_t smem_raw[];
@@ -178,7 +196,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
-    for (int j = 0; j < kPullSlots; ++j) mbar_init(&pulled[j], kCopyWarps);
+    for (int j = 0; j < kPullSlots; ++j) mbar_init(&pulled[j], kCW);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
@@ -196,16 +214,22 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      int ready_chunk = -1;
+      int ready_key = -1;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int chunk, m0, tn;
         fused_tile(t, tiles_m_chunk, tiles_n, cm, first, chunk, m0, tn);
         const int n0 = tn * BN;
         const bool own = chunk == cm.rank;
-        if (MODE == 1 && !own && ready_chunk != chunk) {
-          if (!wait_geq(cm.ready + chunk, cm.ready_target, g.err, kErrPeerWait)) { ok = false; break; }
-          fence_proxy_async_global();
-          ready_chunk = chunk;
+        if (MODE == 1 && !own) {
+          // V = 0: the whole peer chunk; V = 1: only this tile's 128-row block
+          const int key = V == 0 ? chunk : chunk * tiles_m_chunk + (m0 - chunk * cm.rows_per_rank) / kFBM;
+          if (key != ready_key) {
+            const bool arrived = V == 0 ? wait_geq(cm.ready + key, cm.ready_target, g.err, kErrPeerWait)
+                                        : wait_geq(cm.rb_ready + key, cm.rb_target, g.err, kErrPeerWait);
+            if (!arrived) { ok = false; break; }
+            fence_proxy_async_global();
+            ready_key = key;
+          }
         }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, g.err, kErrTmaWait)) { ok = false; break; }
@@ -341,7 +365,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
   } else {
     // ---------------- copy warps ----------------
-    const int ct = threadIdx.x - 192;  // 0 .. 32*kCopyWarps-1
+    const int ct = threadIdx.x - 192;  // 0 .. kCT-1
     bool ok = true;
     if (MODE == 1) {
       const int cols16 = int(cm.ldx / 8);
@@ -353,7 +377,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         uint4* slot = reinterpret_cast<uint4*>(cm.own_slot + int64_t(lo) * cm.ldx);
         uint4* xg = reinterpret_cast<uint4*>(cm.xg + (int64_t(cm.rank) * cm.rows_per_rank + lo) * cm.ldx);
         const int64_t total = int64_t(hi - lo) * cols16;
-        for (int64_t v = ct; v < total; v += 32 * kCopyWarps) {
+        for (int64_t v = ct; v < total; v += kCT) {
           const uint4 x = src[v];
           slot[v] = x;
           xg[v] = x;
@@ -370,18 +394,46 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           }
         }
       }
-      // pull: this CTA's rows of every peer chunk
-      for (int p = 1; p < cm.tp && ok; ++p) {
-        const int chunk = (cm.rank + p) % cm.tp;
-        ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
-        if (!ok) break;
-        copy_rows(reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx), cols16,
-                  reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(lo) * cm.ldx), cols16, hi - lo,
-                  cols16, ct);
-        fence_proxy_async_global();
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) atomicAdd(cm.ready + chunk, 1u);
+      if (V == 0) {
+        // pull: this CTA's rows of every peer chunk
+        for (int p = 1; p < cm.tp && ok; ++p) {
+          const int chunk = (cm.rank + p) % cm.tp;
+          ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
+          if (!ok) break;
+          copy_rows<kCT, kCU>(
+              reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx), cols16,
+              reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(lo) * cm.ldx), cols16, hi - lo, cols16,
+              ct);
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(cm.ready + chunk, 1u);
+        }
+      } else {
+        // pull: units (peer chunk, 128-row block, row slice) in the order the tiles need
+        // them; every copy warp bumps the block's counter after its share of a unit
+        const int blocks = tiles_m_chunk;
+        const int slices = cm.slices;
+        const int srows = kFBM / slices;
+        const int units = (cm.tp - 1) * blocks * slices;
+        int announced = -1;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+          const int chunk = (cm.rank + 1 + u / (blocks * slices)) % cm.tp;
+          const int rb = (u / slices) % blocks;
+          const int r0 = rb * kFBM + (u % slices) * srows;
+          if (chunk != announced) {
+            ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
+            if (!ok) break;
+            announced = chunk;
+          }
+          copy_rows<kCT, kCU>(
+              reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + r0) * cm.ldx), cols16,
+              reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(r0) * cm.ldx), cols16, srows, cols16, ct);
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(cm.rb_ready + chunk * blocks + rb, 1u);
+        }
       }
     } else {
       // for each own-chunk tile this CTA will reduce: pull the peers' partial tiles
@@ -392,13 +444,44 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         if (chunk != cm.rank) continue;
         const int lrow0 = m0 - chunk * cm.rows_per_rank;
         const int ncols16 = min(BN, g.n - tn * BN) / 8;
-        for (int src = 0; src < cm.tp && ok; ++src) {
-          if (src == cm.rank) continue;
-          ok = warp_wait_geq(cm.peer_flag[src] + (m0 / kFBM) * tiles_n + tn, cm.flag_target, g.err, lane);
-          if (!ok) break;
-          const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[src] + int64_t(m0) * g.n + tn * BN);
-          uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(src) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
-          copy_rows(to, g.n / 8, from, g.n / 8, kFBM, ncols16, ct);
+        const int flag = (m0 / kFBM) * tiles_n + tn;
+        if (V == 0) {
+          for (int src = 0; src < cm.tp && ok; ++src) {
+            if (src == cm.rank) continue;
+            ok = warp_wait_geq(cm.peer_flag[src] + flag, cm.flag_target, g.err, lane);
+            if (!ok) break;
+            const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[src] + int64_t(m0) * g.n + tn * BN);
+            uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(src) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
+            copy_rows<kCT, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, ct);
+          }
+        } else {
+          // this warp's peers (every kCW-th peer), copied in the order their tiles arrive
+          const int cw = ct >> 5;
+          unsigned pending = 0;
+          for (int src = 0, i = 0; src < cm.tp; ++src) {
+            if (src == cm.rank) continue;
+            if (i++ % kCW == cw) pending |= 1u << src;
+          }
+          const uint64_t start = globaltimer();
+          while (pending != 0 && ok) {
+            int got = -1;
+            if (lane == 0) {
+              for (int src = 0; src < cm.tp && got < 0; ++src)
+                if ((pending >> src & 1u) && static_cast<int>(ld_acquire_sys(cm.peer_flag[src] + flag) - cm.flag_target) >= 0)
+                  got = src;
+              if (got < 0 && globaltimer() - start > kWaitBudgetNs) {
+                record_error(g.err, kErrPeerWait);
+                got = -2;
+              }
+            }
+            got = __shfl_sync(0xffffffffu, got, 0);
+            if (got == -2) { ok = false; break; }
+            if (got < 0) continue;
+            const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[got] + int64_t(m0) * g.n + tn * BN);
+            uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(got) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
+            copy_rows<32, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, lane);
+            pending &= ~(1u << got);
+          }
         }
         __threadfence_block();
         __syncwarp();
@@ -429,23 +512,45 @@ int sm_count() {
   return n;
 }
 
-template <int BN, bool B_MN, int MODE>
-void launch_fused(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, FusedArgs g, int grid,
-                  cudaStream_t st) {
+template <int BN, bool B_MN, int MODE, int V>
+void launch_fused_v(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, FusedArgs g, int grid,
+                    cudaStream_t st) {
   using S = FusedShape<BN>;
-  auto kernel = fused_gemm_kernel<BN, B_MN, MODE>;
+  auto kernel = fused_gemm_kernel<BN, B_MN, MODE, V>;
   RESIHP_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem));
   // The grid never exceeds the SM count and one CTA fills an SM, so on a GPU this process
   // owns every CTA is resident at once.
-  kernel<<<grid, kFusedThreads, S::kSmem, st>>>(ta, ta2, tb, g);
+  kernel<<<grid, CopyCfg<V>::kThreads, S::kSmem, st>>>(ta, ta2, tb, g);
   RESIHP_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int BN, bool B_MN, int MODE>
+void launch_fused(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, FusedArgs g, int grid,
+                  int variant, cudaStream_t st) {
+  if (variant == 0) launch_fused_v<BN, B_MN, MODE, 0>(ta, ta2, tb, g, grid, st);
+  else launch_fused_v<BN, B_MN, MODE, 1>(ta, ta2, tb, g, grid, st);
+}
+
+int copy_warps(int variant) { return variant == 0 ? CopyCfg<0>::kWarps : CopyCfg<1>::kWarps; }
+
+// Row slices per 128-row block in the V = 1 AG pull: enough units for every CTA.
+int ag_slices(int rows_per_rank, int tp, int grid) {
+  const int units = (tp - 1) * (rows_per_rank / kFBM);
+  int s = 1;
+  while (s < 16 && units * s < grid) s *= 2;
+  return s;
 }
 
 }  // namespace
 
-// Per launch, every copy warp of the grid bumps the AG publish counter once and each
-// chunk's ready counter once; the host advances its bases by this much per call.
-int fused_counter_step(int grid) { return kCopyWarps * grid; }
+// Per launch, every copy warp of the grid bumps the AG publish counter once and (V = 0)
+// each chunk's ready counter once; the host advances its bases by this much per call.
+int fused_counter_step(int grid, int variant) { return copy_warps(variant) * grid; }
+
+// Per launch (V = 1), every peer 128-row block's ready counter grows by this much.
+int fused_block_step(int t_rows, int n, int tp, int grid) {
+  return ag_slices(t_rows / tp, tp, grid) * copy_warps(1);
+}
 
 int fused_grid(int m, int n, int tp) {
   (void)tp;
@@ -456,9 +561,11 @@ int fused_grid(int m, int n, int tp) {
 void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
              int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
              unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,
-             unsigned* ready, unsigned ready_base, int grid, int* err, cudaStream_t st) {
+             unsigned* ready, unsigned ready_base, unsigned* rb_ready, unsigned rb_base, int variant, int grid,
+             int* err, cudaStream_t st) {
   RESIHP_CHECK(tp >= 2 && tp <= kMaxTp && t_rows % tp == 0 && (t_rows / tp) % kFBM == 0,
                "ag_gemm: rows per rank must be a multiple of 128");
+  RESIHP_CHECK(variant == 0 || (variant == 1 && rb_ready != nullptr), "ag_gemm: unknown variant");
   RESIHP_CHECK(n % 8 == 0 && k % 8 == 0, "ag_gemm: N and K must be multiples of 8");
   const int tl = t_rows / tp;
   CUtensorMap ta = make_tma_2d_bf16(x_local, tl, k, k, 64, kFBM);
@@ -486,19 +593,23 @@ void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, 
   c.ldx = k;
   c.sig_ag = sig_ag;
   c.pub = pub;
-  c.pub_target = pub_base + unsigned(kCopyWarps * grid);
+  c.pub_target = pub_base + unsigned(fused_counter_step(grid, variant));
   c.ready = ready;
-  c.ready_target = ready_base + unsigned(kCopyWarps * grid);
-  if (w_mn) launch_fused<256, true, 1>(ta, ta2, tb, g, grid, st);
-  else launch_fused<256, false, 1>(ta, ta2, tb, g, grid, st);
+  c.ready_target = ready_base + unsigned(fused_counter_step(grid, variant));
+  c.rb_ready = rb_ready;
+  c.slices = ag_slices(tl, tp, grid);
+  c.rb_target = rb_base + unsigned(variant == 1 ? fused_block_step(t_rows, n, tp, grid) : 0);
+  if (w_mn) launch_fused<256, true, 1>(ta, ta2, tb, g, grid, variant, st);
+  else launch_fused<256, false, 1>(ta, ta2, tb, g, grid, variant, st);
 }
 
 void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
              int k, int rank, int tp, unsigned epoch, void* part_local, const void* const* peer_part,
-             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int grid, int* err,
+             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int variant, int grid, int* err,
              cudaStream_t st) {
   RESIHP_CHECK(tp >= 2 && tp <= kMaxTp && t_rows % tp == 0 && (t_rows / tp) % kFBM == 0,
                "gemm_rs: rows per rank must be a multiple of 128");
+  RESIHP_CHECK(variant == 0 || variant == 1, "gemm_rs: unknown variant");
   RESIHP_CHECK(n % 32 == 0 && k % 8 == 0, "gemm_rs: N must be a multiple of 32 and K of 8");
   const int tl = t_rows / tp;
   CUtensorMap ta = make_tma_2d_bf16(h, t_rows, k, k, 64, kFBM);
@@ -523,8 +634,8 @@ void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local
   c.flag_local = flag_local;
   c.flag_target = 4u * epoch;  // four warp flags per tile per call
   c.recv = static_cast<__nv_bfloat16*>(recv);
-  if (w_mn) launch_fused<256, true, 2>(ta, ta, tb, g, grid, st);
-  else launch_fused<256, false, 2>(ta, ta, tb, g, grid, st);
+  if (w_mn) launch_fused<256, true, 2>(ta, ta, tb, g, grid, variant, st);
+  else launch_fused<256, false, 2>(ta, ta, tb, g, grid, variant, st);
 }
 
 // ---- symmetric workspace: CUDA IPC -------------------------------------------------------

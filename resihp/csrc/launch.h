@@ -88,14 +88,16 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
 namespace resihp {
 
 int fused_grid(int m, int n, int tp);
-int fused_counter_step(int grid);
+int fused_counter_step(int grid, int variant);
+int fused_block_step(int t_rows, int n, int tp, int grid);
 void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
              int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
              unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,
-             unsigned* ready, unsigned ready_base, int grid, int* err, cudaStream_t st);
+             unsigned* ready, unsigned ready_base, unsigned* rb_ready, unsigned rb_base, int variant, int grid,
+             int* err, cudaStream_t st);
 void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
              int k, int rank, int tp, unsigned epoch, void* part_local, const void* const* peer_part,
-             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int grid, int* err,
+             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int variant, int grid, int* err,
              cudaStream_t st);
 void* symm_alloc(int64_t bytes, void* handle_out);
 void* symm_open(const void* handle);

@@ -309,12 +309,15 @@ void symm_close_t(int64_t p) { symm_close(as_ptr<void>(p)); }
 void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
 
 int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
-int64_t fused_counter_step_t(int64_t grid) { return fused_counter_step(int(grid)); }
+int64_t fused_counter_step_t(int64_t grid, int64_t variant) { return fused_counter_step(int(grid), int(variant)); }
+int64_t fused_block_step_t(int64_t t_rows, int64_t n, int64_t tp, int64_t grid) {
+  return fused_block_step(int(t_rows), int(n), int(tp), int(grid));
+}
 
 void ag_gemm_t(torch::Tensor x_local, int64_t own_slot, std::vector<int64_t> peer_slot, torch::Tensor xg,
                torch::Tensor w, bool w_mn, torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
                std::vector<int64_t> peer_sig_ag, int64_t pub, int64_t pub_base, int64_t ready, int64_t ready_base,
-               int64_t grid) {
+               int64_t grid, int64_t variant, int64_t rb_ready, int64_t rb_base) {
   check_cuda_bf16(x_local, "x_local");
   check_cuda_bf16(xg, "xg");
   check_cuda_bf16(w, "w");
@@ -335,12 +338,13 @@ void ag_gemm_t(torch::Tensor x_local, int64_t own_slot, std::vector<int64_t> pee
   ag_gemm(x_local.data_ptr(), as_ptr<void>(own_slot), slots.data(), xg.data_ptr(), w.data_ptr(), w.stride(0), w_mn,
           y.data_ptr(), y.stride(0), int(t), int(n), int(k), int(rank), int(tp), unsigned(epoch),
           as_ptr<unsigned>(sig_ag), sigs.data(), as_ptr<unsigned>(pub), unsigned(pub_base), as_ptr<unsigned>(ready),
-          unsigned(ready_base), int(grid), error_word(x_local.device()), cur_stream());
+          unsigned(ready_base), as_ptr<unsigned>(rb_ready), unsigned(rb_base), int(variant), int(grid),
+          error_word(x_local.device()), cur_stream());
 }
 
 void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_local, int64_t rank, int64_t tp,
                int64_t epoch, int64_t part_local, std::vector<int64_t> peer_part, int64_t flag_local,
-               std::vector<int64_t> peer_flag, int64_t recv, int64_t grid) {
+               std::vector<int64_t> peer_flag, int64_t recv, int64_t grid, int64_t variant) {
   check_cuda_bf16(h, "h");
   check_cuda_bf16(w, "w");
   check_cuda_bf16(y_local, "y_local");
@@ -356,7 +360,7 @@ void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_loca
   for (auto v : peer_flag) flags.push_back(as_ptr<const unsigned>(v));
   gemm_rs(h.data_ptr(), w.data_ptr(), w.stride(0), w_mn, y_local.data_ptr(), y_local.stride(0), int(t), int(n), int(k),
           int(rank), int(tp), unsigned(epoch), as_ptr<void>(part_local), parts.data(), as_ptr<unsigned>(flag_local),
-          flags.data(), as_ptr<void>(recv), int(grid), error_word(h.device()), cur_stream());
+          flags.data(), as_ptr<void>(recv), int(variant), int(grid), error_word(h.device()), cur_stream());
 }
 
 // ---- flat-state regions and the peer-state kernels ----------------------------------------
@@ -452,8 +456,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &resihp::symm_free_t);
   m.def("fused_grid", &resihp::fused_grid_t);
   m.def("fused_counter_step", &resihp::fused_counter_step_t);
-  m.def("ag_gemm", &resihp::ag_gemm_t);
-  m.def("gemm_rs", &resihp::gemm_rs_t);
+  m.def("fused_block_step", &resihp::fused_block_step_t);
+  m.def("ag_gemm", &resihp::ag_gemm_t, py::arg("x_local"), py::arg("own_slot"), py::arg("peer_slot"), py::arg("xg"),
+        py::arg("w"), py::arg("w_mn"), py::arg("y"), py::arg("rank"), py::arg("tp"), py::arg("epoch"),
+        py::arg("sig_ag"), py::arg("peer_sig_ag"), py::arg("pub"), py::arg("pub_base"), py::arg("ready"),
+        py::arg("ready_base"), py::arg("grid"), py::arg("variant") = 0, py::arg("rb_ready") = 0,
+        py::arg("rb_base") = 0);
+  m.def("gemm_rs", &resihp::gemm_rs_t, py::arg("h"), py::arg("w"), py::arg("w_mn"), py::arg("y_local"),
+        py::arg("rank"), py::arg("tp"), py::arg("epoch"), py::arg("part_local"), py::arg("peer_part"),
+        py::arg("flag_local"), py::arg("peer_flag"), py::arg("recv"), py::arg("grid"), py::arg("variant") = 0);
   m.def("symm_region", &resihp::symm_region_t);
   m.def("dp_grid", &resihp::dp_grid_t);
   m.def("dp_allreduce_adamw", &resihp::dp_allreduce_adamw_t);

@@ -36,6 +36,10 @@ ENABLED = os.environ.get("RESIHP_FUSED_TP", "1") != "0"
 # with register-staged loads, which keeps too few bytes in flight once the per-rank
 # chunk is small and the peers many (measured slower than NCCL at TP8).
 MAX_DEGREE = int(os.environ.get("RESIHP_FUSED_TP_MAX_DEGREE", "2"))
+# Kernel variant for TP > 2 (six copy warps with sixteen loads in flight each, per-row-block
+# readiness in the AG, first-ready peer order in the RS). Off until measured on GPUs.
+ROW_BLOCK_VARIANT = os.environ.get("RESIHP_FUSED_TP_V3", "0") == "1"
+_RB_READY = 256  # byte offset of the per-row-block ready counters in the flag area
 DEBUG = os.environ.get("RESIHP_FUSED_DEBUG", "0") == "1"
 
 
@@ -76,6 +80,9 @@ class SymmetricWorkspace:
         t = rows_per_rank * self.tp
         if (t // 128) * ((width + 255) // 256) > _MAX_TILES:
             raise ValueError("fused TP workspace: too many output tiles")
+        if _RB_READY + 4 * (t // 128) > 4096:
+            raise ValueError("fused TP workspace: too many row blocks for the flag area")
+        self.variant = 1 if (self.tp > 2 and ROW_BLOCK_VARIANT) else 0
         self.rows_per_rank = rows_per_rank
         self.width = width
         self.device = torch.device(device)
@@ -99,6 +106,7 @@ class SymmetricWorkspace:
         self.rs_epoch = 0
         self.pub_base = 0
         self.ready_base = 0
+        self.rb_base = 0
         self.closed = False
 
     # flag words (u32) inside a region
@@ -137,10 +145,14 @@ class SymmetricWorkspace:
         grid = k.fused_grid(t, n, self.tp)
         k.ag_gemm(x_local, self._slot(self.base, e), [self._slot(p, e) for p in self.peers], xg, w, w_mn, y,
                   self.rank, self.tp, e, self._sig_ag(self.base), [self._sig_ag(p) for p in self.peers],
-                  self._pub(self.base), self.pub_base, self._ready(self.base), self.ready_base, grid)
-        step = k.fused_counter_step(grid)  # the kernel's own per-launch counter increment
+                  self._pub(self.base), self.pub_base, self._ready(self.base), self.ready_base, grid,
+                  self.variant, self.base + _RB_READY, self.rb_base)
+        step = k.fused_counter_step(grid, self.variant)  # the kernel's own per-launch counter increments
         self.pub_base += step
-        self.ready_base += step
+        if self.variant == 0:
+            self.ready_base += step
+        else:
+            self.rb_base += k.fused_block_step(t, n, self.tp, grid)
         _debug_check(f"ag_gemm epoch {e}", x_local.device)
         return y, xg
 
@@ -155,7 +167,7 @@ class SymmetricWorkspace:
         grid = k.fused_grid(t, n, self.tp)
         k.gemm_rs(h, w, w_mn, y, self.rank, self.tp, e, self._part(self.base, e),
                   [self._part(p, e) for p in self.peers], self._tile_flags(self.base),
-                  [self._tile_flags(p) for p in self.peers], self.base + self.recv_off, grid)
+                  [self._tile_flags(p) for p in self.peers], self.base + self.recv_off, grid, self.variant)
         _debug_check(f"gemm_rs epoch {e}", h.device)
         return y
 

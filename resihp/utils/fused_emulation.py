@@ -23,7 +23,8 @@ def _u32(count, device, fill=0):
     return torch.full((count,), fill, dtype=torch.int32, device=device)
 
 
-def emulate_ag(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda"):
+def emulate_ag(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda",
+               variant: int = 0):
     """``(y, reference)`` of one emulated AG->GEMM launch of rank 0: ``y = gather(x) @ w.T``."""
     kx = _ext.require()
     dev = torch.device(device)
@@ -39,14 +40,17 @@ def emulate_ag(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed
     peer_sig = [_u32(8, dev) for _ in range(tp)]  # where this rank's announcement lands
     pub = _u32(1, dev)
     ready = _u32(tp, dev)
+    rb_ready = _u32(tokens // 128, dev)
     grid = kx.fused_grid(tokens, n, tp)
     kx.ag_gemm(chunks[0], slots[0].data_ptr(), [s.data_ptr() for s in slots], xg, w, False, y, 0, tp, epoch,
-               sig.data_ptr(), [p.data_ptr() for p in peer_sig], pub.data_ptr(), 0, ready.data_ptr(), 0, grid)
+               sig.data_ptr(), [p.data_ptr() for p in peer_sig], pub.data_ptr(), 0, ready.data_ptr(), 0, grid,
+               variant, rb_ready.data_ptr(), 0)
     ref = torch.cat(chunks).float() @ w.float().t()
     return y, ref, xg, torch.cat(chunks)
 
 
-def emulate_rs(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda"):
+def emulate_rs(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda",
+               variant: int = 0):
     """``(y_r, reference)`` of one emulated GEMM->RS launch of rank 0: rows ``[0, T/tp)`` of
     ``sum over ranks of h_rank @ w_rank.T``, the peers' partials preset in local buffers."""
     kx = _ext.require()
@@ -64,7 +68,7 @@ def emulate_rs(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed
     y = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
     grid = kx.fused_grid(tokens, n, tp)
     kx.gemm_rs(hs[0], ws[0], False, y, 0, tp, epoch, parts[0].data_ptr(), [p.data_ptr() for p in parts],
-               own_flags.data_ptr(), [f.data_ptr() for f in peer_flags], recv.data_ptr(), grid)
+               own_flags.data_ptr(), [f.data_ptr() for f in peer_flags], recv.data_ptr(), grid, variant)
     own = hs[0][:rows].float() @ ws[0].float().t()
     ref = own + sum(p[:rows].float() for p in partials[1:])
     return y, ref
