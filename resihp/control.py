@@ -9,12 +9,14 @@ Semantics of the reference (``resihp/control.py:55-485``):
   plan and checkpoint speak) and a **torch rank** (its index in the current membership,
   re-assigned every time the world is re-formed); this class owns the translation.
 * The **world group** is a Gloo group over the current membership, re-formed under a
-  fresh store prefix after every fail-stop; control collectives ride it. The
-  **training groups** come from the current plan (NCCL on GPU, Gloo on CPU), built in
-  one plan-derived order by every rank: one TP group per stage, one union group per
-  pipeline hop, the executor group over every placed rank, the gradient-reduction groups
-  (DP position groups and tied-embedding pairs) and the live group over every surviving
-  rank, which the recovery transfers ride.
+  fresh store prefix after every fail-stop; control collectives ride it. On GPUs it also
+  carries an NCCL communicator bound to the rank's device, created with the world. The
+  **training groups** come from the current plan (NCCL on GPU -- each an
+  ``ncclCommSplit`` of the world's communicator -- Gloo on CPU), built in one
+  plan-derived order by every rank: one TP group per stage of degree > 1, one union
+  group per pipeline hop, the executor group over every placed rank, the
+  gradient-reduction groups (DP position groups and tied-embedding pairs) and, where
+  state moves are collectives (CPU / FP32), the live group over every surviving rank.
 * Six consistent-stop codes; :meth:`agree` raises the *same* :class:`ConsistentStop` on
   every rank, derived from the gathered reports rather than the local view.
 * :meth:`safe_point` runs steps 4-9: mark failed, replan, dissolve and re-form the world,

@@ -5,13 +5,17 @@ moves from which donor under which layout; :func:`recover` executes them (refere
 ``resihp/recovery.py:373-468``). What is recovered is ``param``, ``exp_avg``,
 ``exp_avg_sq`` and ``step`` plus the data cursor; gradients are never persistent.
 
-Transfers. A peer route (``prev_owner`` / ``peer_replica``) is one collective over the
-group of all live ranks: the donors place their shards (one copy of every element: every
-TP shard of the donor stage, a replicated tensor from its first member only) into a
-full-size buffer of the route's tensors, the buffer is summed, and each target keeps
-its slice under the *new* degree -- the re-partition happens in the same pass. A
-``checkpoint`` route is sliced straight from the anchor. The reference moves the same
-state through a CPU object gather of the whole model per donor degree.
+Transfers. On the CUDA bf16 path a peer route (``prev_owner`` / ``peer_replica``) is a
+peer-to-peer pull: every rank publishes its flat-state region (a CUDA IPC handle plus
+offsets) over the world group and each new owner copies the pieces of its new shards
+straight from the donors' regions with one gather kernel, the re-partition to the new TP
+degree expressed in the copy descriptors (:mod:`resihp.parallel.peer`). On the CPU /
+FP32 path a peer route is one collective over the group of all live ranks: the donors
+place their shards (every TP shard of the donor stage, a replicated tensor from its
+first member only) into a full-size buffer, the buffer is summed, and each target keeps
+its slice under the new degree. A ``checkpoint`` route is sliced straight from the
+anchor. The reference moves the same state through a CPU object gather of the whole
+model per donor degree.
 
 Verification (principle A1): once installed, each rank's new shards are compared with
 ``torch.equal`` against the same slices of the checkpoint anchor; the agreed state
