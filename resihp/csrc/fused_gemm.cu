@@ -6,9 +6,9 @@
 //   GEMM->RS   y_r[T/tp, N] = reduce_scatter_tokens(h[T, K] * op(W))
 //
 // Both are the persistent tcgen05 GEMM of gemm.cu (TMA producer warp, one MMA-issuing
-// thread, four epilogue warps, two TMEM accumulators) plus four *copy warps* per CTA that
-// move the collective's data with coalesced 16-byte loads and stores while the tensor
-// cores work; every remote byte crosses NVLink exactly once.
+// thread, four epilogue warps, two TMEM accumulators) plus *copy warps* (four or six per
+// CTA, see CopyCfg) that move the collective's data with coalesced 16-byte loads and
+// stores while the tensor cores work; every remote byte crosses NVLink exactly once.
 //
 // AG: the copy warps first publish this rank's chunk -- one pass writes it into the
 // rank's symmetric slot (epoch parity) and into the local gather buffer -- and the last
