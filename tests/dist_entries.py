@@ -199,3 +199,73 @@ def planned_entry(rank, env, config_dict, failed, steps, out_dir):
                       dims={n: d for n, (_t, d) in run.stage.local_shards().items()})
     write_result(out_dir, rank, result)
     cp.shutdown()
+
+
+def e2e_entry(rank, env, config_dict, failures, out_dir):
+    """The worker loop with a per-iteration account for the end-to-end invariants.
+
+    Every iteration records the data cursor consumed, the plan version, the names this
+    rank owns and (on a stage's first TP rank) the (micro-batch, stage, replica) pairs it
+    executed; every recovery records whether the state equals the checkpoint before the
+    first resumed step (principle A1). The file is rewritten after each iteration, so a
+    killed rank leaves exactly the iterations it lived through.
+    """
+    _setup(env)
+    import torch.distributed as dist
+
+    from harness import write_result
+    from resihp import verify
+    from resihp.config import TrainConfig
+    from resihp.control import ConsistentStop, ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run, stage_of
+    from resihp.train import fail_stop
+
+    config = TrainConfig(**config_dict)
+    schedule = {int(k): v for k, v in failures.items()}
+    os.chdir(out_dir)
+    ck = Path(out_dir, "checkpoint.pt")
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=ck)
+    record = {"rank": rank, "iterations": [], "plans": [plan.digest], "recoveries": [], "stopped": None}
+    failed = ()
+    try:
+        it = 0
+        while it < config.iterations:
+            it += 1
+            run = cp.training_run
+            entry = {"iteration": it, "plan_version": plan.version, "trained": run is not None}
+            if run is not None:
+                stage = stage_of(plan, rank)
+                entry.update(cursor=run.cursor, owned=sorted(run.stage.local_shards()), replica=stage.replica_id,
+                             stage=stage.stage_id, leader=stage.tp_members[0] == rank)
+            loss = cp.training_step()
+            if run is not None:
+                entry["loss"] = loss
+                if entry["leader"]:
+                    entry["executed"] = [int(x[1:]) for x in run.runtime.schedule if x.startswith("F")]
+            record["iterations"].append(entry)
+            cp.commit_checkpoint(plan, cursor=it)
+            write_result(out_dir, rank, record)
+            fail_stop(schedule, rank, it, before=cp.flush_checkpoint)
+            lost = cp.observe()
+            if lost:
+                import shutil
+
+                plan, failed = cp.safe_point(config, plan, failed, lost, next_step=it)
+                if rank == min(cp.members):
+                    shutil.copy(ck, Path(out_dir, f"anchor_{it}.pt"))
+                a1 = None
+                if cp.training_run is not None:
+                    a1 = verify.matches_checkpoint(cp.training_run, plan=plan, rank=rank, checkpoint_path=ck)
+                record["plans"].append(plan.digest)
+                record["recoveries"].append({"after": it, "lost": list(lost), "a1": a1,
+                                             "resumed_from": cp.resume_cursor, "version": plan.version})
+                it = cp.resume_cursor
+    except ConsistentStop as stop:
+        record["stopped"] = stop.reason.code
+    cp.shutdown()
+    record["initialized"] = dist.is_initialized()
+    write_result(out_dir, rank, record)
