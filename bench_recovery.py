@@ -15,6 +15,7 @@ step, max over surviving ranks) with its phases, and tokens/s of the steps befor
 after each event.
 
     python bench_recovery.py [--gpus 8] [--kills 30:5,60:2] [--iterations 70]
+    python bench_recovery.py --config 1     # CPU/Gloo, 4 ranks, kill rank 3 after step 8
 """
 
 from __future__ import annotations
@@ -30,6 +31,12 @@ import tempfile
 ROOT = os.path.dirname(os.path.abspath(__file__))
 MODEL = dict(model_dim=2048, num_layers=24, num_heads=16, ffn_dim=5504, vocab_size=32000, seq_len=2048)
 LAYOUTS = {2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 2, 2)}
+# BASELINE config 1 (CPU/Gloo, FP32): Llama d256 L4 H4, SwiGLU 688, vocab 1024, tied embeddings,
+# seq 128, 4 micro-batches of 2, TP2 x PP2 x DP1, AdamW lr 1e-3 betas (0.9, 0.95) wd 0.1, seed 0.
+CONFIG1 = dict(model_dim=256, num_layers=4, num_heads=4, ffn_dim=688, vocab_size=1024, seq_len=128, batch_size=8,
+               micro_batch_size=2, seed=0, tp=2, pp=2, dp=1, iterations=20, arch="llama", dtype="fp32",
+               tied_embeddings=True, norm_eps=1e-5, rope_theta=10000.0, init_std=0.02, lr=1e-3, beta1=0.9,
+               beta2=0.95, weight_decay=0.1)
 
 
 def parse():
@@ -40,6 +47,8 @@ def parse():
     p.add_argument("--timeout", type=float, default=1500)
     p.add_argument("--small", action="store_true", help="a 4-layer model (quick check)")
     p.add_argument("--layout", default=None, help="tp,pp,dp (default: config 4's layout for --gpus)")
+    p.add_argument("--config", type=int, choices=(1, 4), default=4,
+                   help="4: the 1.3B GPU run (default); 1: the CPU/Gloo run of BASELINE config 1")
     p.add_argument("--checkpoint-every", type=int, default=None,
                    help="commit the logical checkpoint every N steps (default: every step without a peer "
                         "replica, never with one)")
@@ -48,18 +57,24 @@ def parse():
 
 def main():
     args = parse()
-    tp, pp, dp = (tuple(int(x) for x in args.layout.split(",")) if args.layout else LAYOUTS[args.gpus])
-    if tp * pp * dp != args.gpus:
-        raise SystemExit(f"layout {tp}x{pp}x{dp} does not use {args.gpus} GPUs")
-    model = dict(MODEL)
-    if args.small:
-        model.update(num_layers=4, model_dim=1024, num_heads=8, ffn_dim=2752, seq_len=1024)
-    config = dict(
-        **model, batch_size=64, micro_batch_size=2, seed=1, tp=tp, pp=pp, dp=dp, iterations=args.iterations,
-        arch="llama", dtype="bf16", sequence_parallel=True, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95,
-        weight_decay=0.1, memory_budget_bytes=180 * 10**9,
-        checkpoint_every=args.checkpoint_every or (1 if dp == 1 else 1_000_000),
-    )
+    if args.config == 1:
+        config = dict(CONFIG1)
+        tp, pp, dp = config["tp"], config["pp"], config["dp"]
+        args.gpus = tp * pp * dp
+        args.kills = "8:3"
+    else:
+        tp, pp, dp = (tuple(int(x) for x in args.layout.split(",")) if args.layout else LAYOUTS[args.gpus])
+        if tp * pp * dp != args.gpus:
+            raise SystemExit(f"layout {tp}x{pp}x{dp} does not use {args.gpus} GPUs")
+        model = dict(MODEL)
+        if args.small:
+            model.update(num_layers=4, model_dim=1024, num_heads=8, ffn_dim=2752, seq_len=1024)
+        config = dict(
+            **model, batch_size=64, micro_batch_size=2, seed=1, tp=tp, pp=pp, dp=dp, iterations=args.iterations,
+            arch="llama", dtype="bf16", sequence_parallel=True, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95,
+            weight_decay=0.1, memory_budget_bytes=180 * 10**9,
+            checkpoint_every=args.checkpoint_every or (1 if dp == 1 else 1_000_000),
+        )
     kills = [tuple(int(x) for x in k.split(":")) for k in args.kills.split(",") if k]
     failures = {"events": [{"after_iteration": a, "failed_rank": r} for a, r in kills]}
     with tempfile.TemporaryDirectory() as tmp:
@@ -70,6 +85,8 @@ def main():
         with open(fail_path, "w") as f:
             json.dump(failures, f)
         env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", RESIHP_CHECKPOINT=os.path.join(tmp, "ck.pt"))
+        if args.config == 1:
+            env.update(CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")  # config 1 is the CPU/Gloo run
         env.setdefault("RESIHP_GROUP_TIMEOUT", "120")
         out = subprocess.run(
             [sys.executable, "-m", "resihp.launch", "--config", cfg_path, "--failures", fail_path,
@@ -89,6 +106,7 @@ def main():
         if "step" in l:
             steps.setdefault(l["step"], []).append(l["step_s"])
     tokens = config["batch_size"] * config["seq_len"]
+    label = "llama-config1 (CPU/Gloo, FP32)" if args.config == 1 else ("llama-1.3b" if not args.small else "llama-small")
     step_rate = {it: tokens / max(v) for it, v in steps.items()}
     events = []
     for a, r in kills:
@@ -110,9 +128,10 @@ def main():
         })
     print(json.dumps({
         "metric": "fail-stop recovery seconds (failure -> end of first resumed step, max over survivors)",
-        "n_gpus": args.gpus, "config": {"model": "llama-1.3b" if not args.small else "llama-small",
-                                        "parallelism": f"tp{tp}-pp{pp}-dp{dp}-sp", "dtype": "bf16",
-                                        "global_batch": 64, "seq_len": config["seq_len"]},
+        "n_gpus": 0 if args.config == 1 else args.gpus, "ranks": args.gpus,
+        "config": {"model": label, "baseline_config": args.config,
+                   "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if config.get("sequence_parallel") else ""),
+                   "dtype": config["dtype"], "global_batch": config["batch_size"], "seq_len": config["seq_len"]},
         "events": events, "launch": launch, "launcher_rc": out.returncode,
         "stopped": [l for l in lines if "stopped" in l],
         "steps_seen": sorted(steps),
