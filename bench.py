@@ -173,6 +173,32 @@ def _tp_comm(tp):
     return "fused-nvlink" if fused.ENABLED and tp <= fused.MAX_DEGREE else "nccl"
 
 
+def _memory(run, plan, config, device):
+    """``(measured peak bytes, the planner's estimate)`` for this rank's stage."""
+    import torch
+
+    from resihp.memory import estimate_memory
+    from resihp.planner.pp import peak_in_flight
+    from resihp.recovery import stage_of
+
+    if run is None:
+        return 0.0, 0.0
+    st = run.stage
+    used = torch.cuda.max_memory_allocated(device)
+    if st.flat.region is not None:
+        used += st.flat.region.numel()
+    if st.ws is not None:
+        used += st.ws.total
+    sp = stage_of(plan, run.rank)
+    stages = sorted({s.stage_id for s in plan.stages if s.replica_id == sp.replica_id})
+    micro = len(run.runtime.micro_batches)
+    est = estimate_memory(config, tp_degree=sp.tp_degree, stage_layers=sp.stage_layers, micro_batches=micro,
+                          sequence_length=config.seq_len, vocab_size=config.vocab_size,
+                          in_flight_micro_batches=peak_in_flight(micro, stage_index=stages.index(sp.stage_id),
+                                                                 num_stages=len(stages)))
+    return float(used), float(est.total)
+
+
 def run_ours(args):
     sys.path.insert(0, ROOT)
     import torch
@@ -227,6 +253,7 @@ def run_ours(args):
         return float(t.item())
 
     counter = _ext.launch_counter()
+    torch.cuda.reset_peak_memory_stats(device)
     for _ in range(args.warmup):
         step()
     counter.launches = 0
@@ -235,6 +262,9 @@ def run_ours(args):
     counter.enabled = False
     launches = int(reduce_max(counter.launches))
     check_device_errors(local)
+    used, estimate = _memory(run, plan, config, device)
+    mem = torch.tensor([used, estimate])
+    dist.all_reduce(mem, op=dist.ReduceOp.MAX, group=cp.world_group)
     bytes_in = torch.tensor([float(h2d_bytes), float(d2h_bytes)])
     dist.all_reduce(bytes_in, group=cp.world_group)
     tokens = args.steps * global_batch * config.seq_len
@@ -256,6 +286,8 @@ def run_ours(args):
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(bytes_in[0]),
                     "d2h_bytes_per_step": int(bytes_in[1])},
             "gpu_launches": launches,
+            "memory": {"peak_gib": round(float(mem[0]) / 2**30, 2), "planner_estimate_gib": round(float(mem[1]) / 2**30, 2),
+                       "note": "max over ranks; peak = caching-allocator peak + flat-state region + TP workspace"},
             "impl": "resihp",
         }
         print(json.dumps(line), flush=True)

@@ -11,11 +11,13 @@ Two regimes share one entry point:
   the reference can express the configuration.
 * **B200 regime** (everything else, i.e. Llama blocks and/or bf16): weights in the
   compute dtype plus an FP32 master copy when that dtype is bf16, FP32 gradient
-  accumulation buffers and FP32 Adam moments, and a *per-layer* activation model that
+  accumulation buffers (two on the bf16 GPU path) and FP32 Adam moments, the fused TP
+  workspace under sequence parallelism, and a *per-layer* activation model that
   follows what the runtime actually keeps alive between a micro-batch's forward and its
   backward: the normalised inputs, Q/K/V after RoPE, the attention output and its
-  log-sum-exp, both MLP projections and the SwiGLU product. Replicated (``d``-wide)
-  terms shrink by TP under sequence parallelism; with recompute only each block's input
+  log-sum-exp, both MLP projections and the SwiGLU product. Under sequence parallelism
+  the block input and residual shrink by TP while the two column-parallel GEMM inputs
+  are kept gathered; with recompute only each block's input
   is kept, plus one block's full working set while it is being recomputed. The last
   stage adds one micro-batch of FP32 vocab-parallel logits.
 
@@ -107,12 +109,18 @@ def estimate_memory(
     boundary_params = 2 * vocab_size * d // tp_degree
     sharded = stage_params * weight_bytes
     boundary = boundary_params * weight_bytes
-    grads = (stage_params + boundary_params) * FP32
+    # bf16 runs on the GPU path, which keeps two FP32 gradient buffers (the fused DP step
+    # reads one and writes the reduced sum into the other)
+    grad_buffers = 2 if config.dtype == "bf16" else 1
+    grads = (stage_params + boundary_params) * FP32 * grad_buffers
     moments = (stage_params + boundary_params) * FP32
 
     kv = config.kv_heads * config.head_dim
     sp = tp_degree if config.sequence_parallel else 1
-    replicated_terms = 4 * d * act // sp  # block input, norm out, residual, mlp-norm out
+    # block input and residual stay token-sharded under SP; the inputs of the two
+    # column-parallel GEMMs (attention norm and MLP norm outputs) are kept gathered over
+    # the full sequence for their weight gradients
+    replicated_terms = 2 * d * act // sp + 2 * d * act
     sharded_terms = ((d + 2 * kv) + d + 3 * config.ffn) * act // tp_degree
     lse = (config.num_heads // tp_degree) * FP32
     full_block = replicated_terms + sharded_terms + lse
@@ -123,6 +131,10 @@ def estimate_memory(
     else:
         activation = tokens * stage_layers * full_block
     activation += mb_tokens * (vocab_size // tp_degree) * FP32
+    if config.dtype == "bf16" and config.sequence_parallel and tp_degree > 1:
+        # the fused TP kernels' peer-memory workspace: two publish slots, two partial
+        # buffers and one receive buffer of one micro-batch
+        activation += (2 * mb_tokens // tp_degree + 3 * mb_tokens) * d * BF16
     return MemoryBreakdown(sharded, boundary, grads, moments, moments, activation)
 
 

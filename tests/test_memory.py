@@ -38,9 +38,17 @@ def test_llama_regime_recompute_and_sp_reduce_activations():
     rc = estimate_memory(TrainConfig(**base, recompute=True), **kw)
     assert sp.activation < plain.activation and rc.activation < plain.activation
     assert plain.sharded_parameters == sp.sharded_parameters
-    # bf16 weights + fp32 master = 6 bytes per parameter, grads and moments 4 each
-    assert plain.gradients * 6 == plain.sharded_parameters * 4 + plain.boundary_parameters * 4 + (
-        plain.sharded_parameters + plain.boundary_parameters) * 0
+    # bf16 weights + fp32 master = 6 bytes per parameter; two fp32 gradient buffers (8 bytes)
+    # and 4 bytes per moment
+    params = (plain.sharded_parameters + plain.boundary_parameters) // 6
+    assert plain.gradients == 8 * params and plain.adam_exp_avg == 4 * params
+    # SP halves the block input and residual (d bf16 values per token and layer saved over
+    # 2 micro-batches x 2048 tokens x 12 layers) and adds the fused TP workspace of one
+    # micro-batch (two half-size publish slots, two partial buffers, one receive buffer)
+    mb_tokens = 2 * 2048
+    saved = 2 * mb_tokens * 12 * 2048 * 2
+    workspace = (2 * mb_tokens // 2 + 3 * mb_tokens) * 2048 * 2
+    assert sp.activation == plain.activation - saved + workspace
 
 
 def test_rejects_overcount():
