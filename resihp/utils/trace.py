@@ -4,7 +4,8 @@ The 1F1B runtime marks every micro-batch's forward ``F<i>`` and backward ``B<i>`
 pipeline exchange ``p2p`` and the gradient-reduction + optimizer step ``W`` (the same
 labels as :attr:`resihp.parallel.pp.PipelineRuntime.schedule`); the control plane marks
 the checkpoint commit and every safe-point phase. Disabled, :func:`nvtx_range` is a
-no-op context manager, so the hot path pays nothing.
+no-op context manager, so the hot path pays nothing. (The reference has no tracing; its
+only execution record is the schedule list of ``resihp/parallel/pp.py:127,369``.)
 """
 
 from __future__ import annotations
