@@ -102,3 +102,30 @@ def test_background_writer_orders_writes_and_surfaces_errors(tmp_path):
         writer.flush()
     assert load_anchor(path)[1] == 2  # the failed write left the previous checkpoint in place
     writer.flush()  # the error is reported once
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+def test_we_read_the_references_checkpoint(tmp_path):
+    """A checkpoint the reference wrote (after two of its own steps) loads and validates
+    here for the same configuration, names, step and values included."""
+    path = tmp_path / "ref.pt"
+    code = (
+        "import sys, json; sys.path.insert(0, sys.argv[1])\n"
+        "from resihp.config import TrainConfig\nfrom resihp.reference import ReferenceRun\n"
+        "from resihp.checkpoint import save_checkpoint\n"
+        "cfg = TrainConfig(model_dim=16, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=3,"
+        " tp=1, pp=1, dp=1, iterations=2)\n"
+        "run = ReferenceRun(cfg, vocab_size=32, sequence_length=8)\n"
+        "run.step(); run.step()\n"
+        "save_checkpoint(sys.argv[2], run, plan_version=1)\n"
+        "print(json.dumps({k: v.tolist() for k, v in run.model.logical_state_dict().items()}))\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code, REF, str(path)], capture_output=True, text=True, check=True,
+                         cwd="/")
+    theirs = json.loads(out.stdout)
+    anchor, completed, version = load_checkpoint(path, C)
+    assert completed == 2 and version == 1
+    assert sorted(anchor) == sorted(theirs)
+    for name, values in theirs.items():
+        assert torch.equal(anchor[name]["param"], torch.tensor(values)), name
+        assert int(anchor[name]["step"]) == 2
