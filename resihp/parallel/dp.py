@@ -220,8 +220,10 @@ class GradientReducer:
             s = held.get(spec.name)
             if s is not None:
                 if spec.shard_dim is None:
-                    contribute = stage.sp or stage.tp_rank == 0
-                    if contribute:
+                    # one copy per holder stage: without SP every TP member computed the
+                    # same gradient, with SP the partial sums were just all-reduced over
+                    # the TP group, so either way each member holds the stage's total
+                    if stage.tp_rank == 0:
                         full += stage.g[spec.name]
                 else:
                     torch.chunk(full, stage.tp_size, dim=spec.shard_dim)[stage.tp_rank].copy_(stage.g[spec.name])

@@ -24,6 +24,7 @@ CASES = [
     (dict(tp=1, pp=2, dp=2), (3,)),                        # replica 1 collapses to one 4-layer stage
     (dict(tp=2, pp=1, dp=2), (1,)),                        # replicas at TP1 and TP2
     (dict(tp=2, pp=2, dp=2, tied_embeddings=True), (5, 2)),  # two failures, tied pairs at mixed degrees
+    (dict(tp=2, pp=1, dp=2, sequence_parallel=True), (1,)),  # SP replica (TP2) next to a TP1 replica
 ]
 
 
