@@ -49,9 +49,11 @@ def _plans(config):
 
 
 @pytest.mark.slow
-def test_three_d_run_with_two_kills(tmp_path):
-    config = TrainConfig(**CONFIG)
-    codes = run_ranks(dist_entries.e2e_entry, 8, CONFIG, KILLS, str(tmp_path))
+@pytest.mark.parametrize("sp", [False, True], ids=["tp", "tp-sp"])
+def test_three_d_run_with_two_kills(tmp_path, sp):
+    run_config = dict(CONFIG, sequence_parallel=sp)
+    config = TrainConfig(**run_config)
+    codes = run_ranks(dist_entries.e2e_entry, 8, run_config, KILLS, str(tmp_path))
     assert_killed(codes, [1, 5], "end-to-end")
     results = read_results(tmp_path, range(8))
     survivors = [r for r in range(8) if r not in (1, 5)]
@@ -115,7 +117,7 @@ def test_three_d_run_with_two_kills(tmp_path):
                     per_replica.setdefault(e["replica"], e["loss"])
         return sum(per_replica.values())
 
-    oracle = ReferenceRun(TrainConfig(**dict(CONFIG, tp=1, pp=1, dp=1)))
+    oracle = ReferenceRun(TrainConfig(**dict(CONFIG, tp=1, pp=1, dp=1)))  # SP changes no math
     want = {1: oracle.step().loss, 2: oracle.step().loss}
     for after in (2, 4):
         anchor, completed = load_anchor(os.path.join(tmp_path, f"anchor_{after}.pt"))
