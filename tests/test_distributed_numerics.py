@@ -50,6 +50,7 @@ LAYOUTS = [
     dict(tp=1, pp=1, dp=2),
     dict(tp=2, pp=2, dp=1, sequence_parallel=True, tied_embeddings=True),
     dict(tp=2, pp=2, dp=2),
+    dict(tp=2, pp=2, dp=1, sequence_parallel=True, recompute=True),
 ]
 
 
