@@ -144,14 +144,36 @@ class CheckpointWriter:
     def __init__(self):
         self._thread = None
         self._error: BaseException | None = None
+        self._pinned: dict[int, torch.Tensor] = {}
+        self._stream = None
 
-    def submit(self, path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int) -> None:
+    def pinned(self, index: int, numel: int) -> torch.Tensor:
+        """Page-locked FP32 staging buffer ``index`` of at least ``numel`` elements, reused
+        across commits (callers flush before refilling it)."""
+        buf = self._pinned.get(index)
+        if buf is None or buf.numel() < numel:
+            buf = torch.empty(numel, dtype=torch.float32, pin_memory=True)
+            self._pinned[index] = buf
+        return buf[:numel]
+
+    def copy_stream(self, device):
+        """The side stream the device-to-host copies of a commit run on."""
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(device)
+        return self._stream
+
+    def submit(self, path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int,
+               ready=None) -> None:
+        """Write ``full`` in the background; ``ready`` (a CUDA event) marks when its
+        host tensors -- views of the pinned staging buffers -- hold their values."""
         import threading
 
         self.flush()
 
         def work():
             try:
+                if ready is not None:
+                    ready.synchronize()
                 save_checkpoint(path, config, full, completed_steps=completed_steps, plan_version=plan_version)
             except BaseException as error:  # re-raised by flush() on the training thread
                 self._error = error

@@ -184,12 +184,18 @@ def _canonical_holders(plan) -> dict[str, object]:
     return out
 
 
-def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems: int = 32 * 1024 * 1024):
+def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems: int = 32 * 1024 * 1024,
+                      staging=None):
     """Assemble ``{name: {param, exp_avg, exp_avg_sq, step}}`` on plan rank ``dst``.
 
     Every rank of ``group`` (the executor group) calls this; each element is contributed
     by exactly one rank of the name's canonical holder stage and summed, so the result is
     exact. ``dst=None`` makes every rank receive it. Returns ``None`` elsewhere.
+
+    ``staging`` (a :class:`~resihp.checkpoint.CheckpointWriter`, CUDA only) makes the
+    receiving rank copy each bucket into a reused page-locked buffer on a side stream
+    instead of a synchronous ``.cpu()``; it then returns ``(state, event)`` with the event
+    recorded after the last copy.
     """
     config = plan.config
     holders = _canonical_holders(plan)
@@ -218,7 +224,9 @@ def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems
     if cur:
         buckets.append(cur)
 
-    for bucket in buckets:
+    deferred = staging is not None and want and torch.device(device).type == "cuda"
+    side = staging.copy_stream(device) if deferred else None
+    for index, bucket in enumerate(buckets):
         total = sum(numel(shapes[n]) for n in bucket) * len(FIELDS)
         buf = torch.zeros(total, dtype=torch.float32, device=device)
         off = 0
@@ -242,11 +250,19 @@ def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems
         else:
             dist.reduce(buf, dst=dist.get_global_rank(group, dst_group_rank), group=group)
         if want:
+            host = None
+            if deferred:
+                host = staging.pinned(index, total)
+                side.wait_stream(torch.cuda.current_stream(device))
+                with torch.cuda.stream(side):
+                    host.copy_(buf, non_blocking=True)
+                buf.record_stream(side)  # the allocator keeps buf until the copy is done
             off = 0
             for n in bucket:
                 k = numel(shapes[n])
                 for f in FIELDS:
-                    out[n][f] = buf[off: off + k].view(shapes[n]).cpu()
+                    view = buf[off: off + k].view(shapes[n])
+                    out[n][f] = host[off: off + k].view(shapes[n]) if deferred else view.cpu()
                     off += k
     if not want:
         return None
@@ -257,6 +273,10 @@ def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems
         if step > 0:
             entry.update(exp_avg=out[n]["exp_avg"], exp_avg_sq=out[n]["exp_avg_sq"], step=step_t.clone())
         full_state[n] = entry
+    if deferred:
+        ready = torch.cuda.Event()
+        ready.record(side)
+        return full_state, ready
     return full_state
 
 
@@ -270,11 +290,18 @@ def commit_checkpoint(run, path, *, plan, groups: TrainingGroups, writer: bool, 
     if groups.executor is None:
         return
     dst = plan.active_ranks[0]
-    full = gather_full_state(run, plan, group=groups.executor, dst=dst, device=device or "cpu")
+    if writer and background is not None:
+        background.flush()  # the previous write may still read the staging buffers
+    staged = writer and background is not None and device is not None and torch.device(device).type == "cuda"
+    full = gather_full_state(run, plan, group=groups.executor, dst=dst, device=device or "cpu",
+                             staging=background if staged else None)
     if not writer:
         return
+    ready = None
+    if staged:
+        full, ready = full
     if background is not None:
-        background.submit(path, plan.config, full, completed_steps=cursor, plan_version=plan.version)
+        background.submit(path, plan.config, full, completed_steps=cursor, plan_version=plan.version, ready=ready)
     else:
         save_checkpoint(path, plan.config, full, completed_steps=cursor, plan_version=plan.version)
 
