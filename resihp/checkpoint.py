@@ -83,8 +83,18 @@ def payload_digest(payload: dict) -> str:
     return h.hexdigest()
 
 
-def build_payload(config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int) -> dict:
-    """Payload from a full logical state ``{name: {param[, exp_avg, exp_avg_sq, step]}}``."""
+def rng_states() -> tuple:
+    """``(cpu, cuda or None)`` generator states, as the payload stores them."""
+    return torch.get_rng_state(), (torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None)
+
+
+def build_payload(config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int,
+                  rng: tuple | None = None) -> dict:
+    """Payload from a full logical state ``{name: {param[, exp_avg, exp_avg_sq, step]}}``.
+
+    ``rng`` are the generator states to record (default: the current ones).
+    """
+    cpu_rng, cuda_rng = rng if rng is not None else rng_states()
     params = {n: f["param"].detach().to("cpu", torch.float32).clone() for n, f in full.items()}
     optim = {}
     for n, f in full.items():
@@ -101,8 +111,8 @@ def build_payload(config: TrainConfig, full: dict, *, completed_steps: int, plan
         "identity": identity(config),
         "params": params,
         "optim": optim,
-        "cpu_rng_state": torch.get_rng_state(),
-        "cuda_rng_state": torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None,
+        "cpu_rng_state": cpu_rng,
+        "cuda_rng_state": cuda_rng,
     }
 
 
@@ -110,11 +120,12 @@ def _torch_load(path: Path, mmap: bool = False) -> dict:
     return torch.load(path, weights_only=False, mmap=mmap)
 
 
-def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int = 0) -> Path:
+def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int = 0,
+                    rng: tuple | None = None) -> Path:
     """Atomically write the logical checkpoint; returns the canonical path."""
     if type(plan_version) is not int or plan_version < 0:
         raise CheckpointError("plan_version must be a non-negative integer")
-    payload = build_payload(config, full, completed_steps=completed_steps, plan_version=plan_version)
+    payload = build_payload(config, full, completed_steps=completed_steps, plan_version=plan_version, rng=rng)
     payload["digest"] = payload_digest(payload)
     path = Path(path)
     tmp = path.with_name(path.name + ".tmp")
@@ -169,12 +180,14 @@ class CheckpointWriter:
         import threading
 
         self.flush()
+        rng = rng_states()  # as of the commit, not of the write
 
         def work():
             try:
                 if ready is not None:
                     ready.synchronize()
-                save_checkpoint(path, config, full, completed_steps=completed_steps, plan_version=plan_version)
+                save_checkpoint(path, config, full, completed_steps=completed_steps, plan_version=plan_version,
+                                rng=rng)
             except BaseException as error:  # re-raised by flush() on the training thread
                 self._error = error
 
