@@ -306,6 +306,17 @@ int64_t symm_open_t(py::bytes handle) {
 }
 
 void symm_close_t(int64_t p) { symm_close(as_ptr<void>(p)); }
+
+// Debug helpers for guard bytes around workspace buffers (synchronous, any device memory).
+void debug_fill_bytes_t(int64_t p, int64_t bytes, int64_t value) {
+  C10_CUDA_CHECK(cudaMemset(as_ptr<void>(p), int(value & 0xff), size_t(bytes)));
+}
+
+py::bytes debug_read_bytes_t(int64_t p, int64_t bytes) {
+  std::string out(size_t(bytes), '\0');
+  C10_CUDA_CHECK(cudaMemcpy(out.data(), as_ptr<const void>(p), size_t(bytes), cudaMemcpyDeviceToHost));
+  return py::bytes(out);
+}
 void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
 
 int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
@@ -454,6 +465,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &resihp::symm_open_t);
   m.def("symm_close", &resihp::symm_close_t);
   m.def("symm_free", &resihp::symm_free_t);
+  m.def("debug_fill_bytes", &resihp::debug_fill_bytes_t);
+  m.def("debug_read_bytes", &resihp::debug_read_bytes_t);
   m.def("fused_grid", &resihp::fused_grid_t);
   m.def("fused_counter_step", &resihp::fused_counter_step_t);
   m.def("fused_block_step", &resihp::fused_block_step_t);

@@ -59,6 +59,8 @@ def _debug_check(what: str, device) -> None:
 
 _MAX_TILES = 8192             # per-tile flags of the RS partial buffer
 _FLAG_BYTES = 4096 + 4 * _MAX_TILES
+_GUARD_BYTES = 256            # debug layout: guard bytes after every buffer
+_GUARD_VALUE = 0xA5
 
 
 class SymmetricWorkspace:
@@ -88,12 +90,21 @@ class SymmetricWorkspace:
         self.device = torch.device(device)
         self.slot_bytes = rows_per_rank * width * 2
         self.part_bytes = t * width * 2
-        self.slot_off = _FLAG_BYTES
-        self.part_off = self.slot_off + 2 * self.slot_bytes
-        self.recv_off = self.part_off + 2 * self.part_bytes
-        self.total = self.recv_off + self.tp * self.slot_bytes
+        # debug builds of the layout put a guard after every buffer (none otherwise, so
+        # the production layout is unchanged)
+        g = _GUARD_BYTES if DEBUG else 0
+        self.slot_off = _FLAG_BYTES + g
+        self.slot_stride = self.slot_bytes + g
+        self.part_off = self.slot_off + 2 * self.slot_stride
+        self.part_stride = self.part_bytes + g
+        self.recv_off = self.part_off + 2 * self.part_stride
+        self.total = self.recv_off + self.tp * self.slot_bytes + g
+        self.guards = [_FLAG_BYTES] + [self.slot_off + i * self.slot_stride + self.slot_bytes for i in range(2)] + [
+            self.part_off + i * self.part_stride + self.part_bytes for i in range(2)] + [self.total - g] if g else []
         with torch.cuda.device(self.device):
             self.base, handle = k.symm_alloc(self.total)
+            for off in self.guards:
+                k.debug_fill_bytes(self.base + off, _GUARD_BYTES, _GUARD_VALUE)
             torch.cuda.synchronize()
         handles = [None] * self.tp
         dist.all_gather_object(handles, handle, group=group)
@@ -123,10 +134,18 @@ class SymmetricWorkspace:
         return base + 4096
 
     def _slot(self, base, epoch):
-        return base + self.slot_off + (epoch % 2) * self.slot_bytes
+        return base + self.slot_off + (epoch % 2) * self.slot_stride
 
     def _part(self, base, epoch):
-        return base + self.part_off + (epoch % 2) * self.part_bytes
+        return base + self.part_off + (epoch % 2) * self.part_stride
+
+    def check_guards(self, what: str) -> None:
+        """Debug layout: raise if a kernel wrote past any buffer of this region."""
+        k = _ext.require()
+        for off in self.guards:
+            data = k.debug_read_bytes(self.base + off, _GUARD_BYTES)
+            if data != bytes([_GUARD_VALUE]) * _GUARD_BYTES:
+                raise RuntimeError(f"fused {what}: workspace guard at byte {off} was overwritten")
 
     def fits(self, rows: int, width: int) -> bool:
         return rows == self.rows_per_rank * self.tp and width == self.width
@@ -154,6 +173,8 @@ class SymmetricWorkspace:
         else:
             self.rb_base += k.fused_block_step(t, n, self.tp, grid)
         _debug_check(f"ag_gemm epoch {e}", x_local.device)
+        if DEBUG:
+            self.check_guards(f"ag_gemm epoch {e}")
         return y, xg
 
     def gemm_reduce_scatter(self, h, w, w_mn: bool, n: int):
@@ -169,6 +190,8 @@ class SymmetricWorkspace:
                   [self._part(p, e) for p in self.peers], self._tile_flags(self.base),
                   [self._tile_flags(p) for p in self.peers], self.base + self.recv_off, grid, self.variant)
         _debug_check(f"gemm_rs epoch {e}", h.device)
+        if DEBUG:
+            self.check_guards(f"gemm_rs epoch {e}")
         return y
 
     def close(self, *, barrier: bool = True):
