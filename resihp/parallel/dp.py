@@ -147,6 +147,7 @@ class GradientReducer:
         self.replica_id = replica_id
         self.bucket_elems = 64 * 1024 * 1024
         self.fused_dp = None
+        self.hetero = None
 
     def attach(self, stage) -> None:
         """Set up the fused DP step (one NVLink kernel: all-reduce + AdamW) where it applies.
@@ -157,6 +158,11 @@ class GradientReducer:
         """
         from . import peer
 
+        if (not self.topology.homogeneous and peer.HETERO_ENABLED and stage.kernel and stage.flat.shared
+                and self.executor_group is not None):
+            stage.hetero = peer.HeteroPeers(stage, self.plan, self.rank, self.executor_group)
+            self.hetero = stage.hetero
+            return
         if not (peer.ENABLED and stage.kernel and stage.flat.shared and self.topology.homogeneous):
             return
         for members in self.topology.dp_groups:
@@ -177,6 +183,9 @@ class GradientReducer:
     def reduce(self, stage) -> None:
         if self.topology.homogeneous:
             self._reduce_fast(stage)
+        elif self.hetero is not None and not self.hetero.closed:
+            self._sp_partial_replicated(stage)
+            self.hetero.reduce(stage)
         else:
             self._reduce_logical(stage)
 

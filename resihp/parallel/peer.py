@@ -14,6 +14,9 @@ regions of other ranks and read them with P2P loads inside their own kernels:
   re-partition (shard dim 0 or 1, any old and new TP degree) expressed as strided copy
   descriptors, one ``reshard_gather`` launch per rank (reference: the all-gather-object
   reshard of ``resihp/parallel/reshard.py:187-243``).
+* :class:`HeteroPeers` -- the logical gradient sum for replicas with different layouts
+  (reference: ``resihp/parallel/dp.py:140-151``) as P2P pulls of the other holders'
+  pieces plus an ordered sum; off unless ``RESIHP_P2P_HETERO=1``.
 
 Mappings are opened after a fail-stop's world re-formation and closed at the next safe
 point, when no kernel is in flight; a dead rank's region is never mapped again.
@@ -223,9 +226,171 @@ class GatherPlan:
                     self.rows.append([src, dst, bf16, p.src_ld, p.dst_ld, p.rows, p.cols, self.items, vec4])
                     self.items += p.rows
 
+    def add_field(self, pieces, *, src_base: int, dst_base: int) -> None:
+        """Queue ``pieces`` of one FP32 field: ``src_base`` / ``dst_base`` are the byte
+        addresses of element 0 of the donor's and of the target's tensor."""
+        for piece in pieces:
+            for p in split_rows(piece):
+                src = src_base + 4 * p.src_off
+                dst = dst_base + 4 * p.dst_off
+                vec4 = int(src % 16 == 0 and dst % 16 == 0 and p.src_ld % 4 == 0 and p.dst_ld % 4 == 0
+                           and p.cols % 4 == 0)
+                self.rows.append([src, dst, 0, p.src_ld, p.dst_ld, p.rows, p.cols, self.items, vec4])
+                self.items += p.rows
+
     def launch(self, device) -> None:
         if not self.rows:
             return
         table = torch.tensor(self.rows, dtype=torch.int64).to(device)
         _ext.require().reshard_gather(table, self.items)
         self._keep = table  # alive until the launch has run (the caller synchronises)
+
+
+# ---------------------------------------------------------------------------------------
+# heterogeneous replicas: the logical gradient sum by P2P pulls
+# ---------------------------------------------------------------------------------------
+
+HETERO_ENABLED = os.environ.get("RESIHP_P2P_HETERO", "0") == "1"
+
+
+@dataclass(frozen=True)
+class StageMeta:
+    """What every executor publishes about its stage for the heterogeneous reduction."""
+
+    rank: int
+    replica: int
+    stage: int
+    tp_members: tuple[int, ...]
+    layout: dict          # {name: shard dim or None}
+    export: dict          # FlatState.export(): handle, field offsets, tensor offsets
+
+
+def hetero_terms(metas: dict, rank: int, shapes: dict) -> list[tuple[str, int, list]]:
+    """For each tensor ``rank`` owns: ``(name, own position, [(position, donor rank, Piece)])``.
+
+    The logical gradient of a tensor is the sum over every *holder stage* (each replica's
+    stage that holds it, twice per replica for tied embeddings) of that stage's full
+    gradient. Holders are ordered by (replica, stage); a rank's shard of the sum is the
+    same positions of every holder's contribution, cut from the holder's TP shards by
+    :func:`shard_pieces` (a replicated tensor from the holder's first TP rank).
+    """
+    me = metas[rank]
+    stages = {}
+    for m in metas.values():
+        stages.setdefault((m.replica, m.stage), m)
+    ordered = [stages[k] for k in sorted(stages)]
+    my_index = me.tp_members.index(rank)
+    out = []
+    for name, dim in sorted(me.layout.items()):
+        holders = [s for s in ordered if name in s.layout]
+        own = next(i for i, s in enumerate(holders) if (s.replica, s.stage) == (me.replica, me.stage))
+        terms = []
+        for pos, h in enumerate(holders):
+            if pos == own:
+                continue
+            for piece in shard_pieces(shapes[name], dim, len(h.tp_members), len(me.tp_members), my_index):
+                terms.append((pos, h.tp_members[piece.donor], piece))
+        out.append((name, own, terms))
+    return out
+
+
+def hetero_gather(terms, metas: dict, rank: int, flat, region_of, scratch) -> tuple[GatherPlan, list[dict]]:
+    """Copy descriptors pulling every other holder's pieces of this rank's shards into
+    ``scratch`` rows (one row per holder position, laid out like this rank's flat state);
+    ``region_of(rank)`` is the address of a rank's region here. Returns the descriptors
+    and, per term list, ``{holder position: scratch row}``."""
+    plan = GatherPlan()
+    slots = []
+    for name, _own, pieces in terms:
+        slot = {p: i for i, p in enumerate(sorted({p for p, _d, _q in pieces}))}
+        slots.append(slot)
+        dst_off = flat.offsets[name][0]
+        for pos, donor, piece in pieces:
+            m = metas[donor]
+            src = region_of(donor) + m.export["fields"]["grad0"] + 4 * m.export["offsets"][name]
+            plan.add_field([piece], src_base=src, dst_base=scratch[slot[pos]].data_ptr() + 4 * dst_off)
+    return plan, slots
+
+
+def hetero_sum(terms, slots, scratch, flat, grad) -> None:
+    """Overwrite each shard in ``grad`` (this rank's gradient buffer) with the sum of the
+    holders' contributions, added in holder order."""
+    with torch.no_grad():
+        for (name, own, pieces), slot in zip(terms, slots):
+            if not pieces:
+                continue
+            g = flat.view(grad, name)
+            off, shape = flat.offsets[name]
+            parts = [g if pos == own else scratch[slot[pos]][off: off + g.numel()].view(shape)
+                     for pos in range(len(slot) + 1)]
+            acc = parts[0].clone()
+            for t in parts[1:]:
+                acc.add_(t)
+            g.copy_(acc)
+
+
+class HeteroPeers:
+    """P2P logical gradient sum for replicas with different layouts (after fail-stops).
+
+    Each executor maps every other executor's flat-state region. Per step: every rank
+    synchronises and meets the others at a barrier (all gradients final), pulls the
+    pieces of the other holders' gradients of its own shards into a scratch buffer with
+    one gather launch, meets them again (all pulls done), and sums the holders'
+    contributions in (replica, stage) order into its gradient -- the same order on every
+    rank that holds an element, so the sums agree bit for bit. Replaces the per-tensor
+    full-size all-reduce of the collective path.
+    """
+
+    def __init__(self, stage, plan, rank, group):
+        from ..models.layout import model_specs
+        from ..recovery import stage_layout, stage_of
+
+        k = _ext.require()
+        flat = stage.flat
+        if not flat.shared:
+            raise ValueError("the P2P heterogeneous reduction needs the shared flat-state region")
+        sp = stage_of(plan, rank)
+        mine = StageMeta(rank, sp.replica_id, sp.stage_id, tuple(sp.tp_members), stage_layout(plan, sp), flat.export())
+        gathered = [None] * dist.get_world_size(group)
+        dist.all_gather_object(gathered, mine, group=group)
+        metas = {m.rank: m for m in gathered}
+        self.group = group
+        self.rank = rank
+        self.device = flat.master.device
+        shapes = {s.name: s.shape for s in model_specs(plan.config)}
+        self.terms = hetero_terms(metas, rank, shapes)
+        slots = max((len({p for p, _d, _q in t}) for _n, _o, t in self.terms), default=0)
+        self.scratch = torch.zeros((max(slots, 1), flat.numel), dtype=torch.float32, device=self.device)
+        self.opened = {}
+        with torch.cuda.device(self.device):
+            for r, m in metas.items():
+                if r != rank:
+                    self.opened[r] = k.symm_open(m.export["handle"])
+        self.plan, self.slot_of = hetero_gather(
+            self.terms, metas, rank, flat, lambda r: flat.region_ptr if r == rank else self.opened[r], self.scratch)
+        self.table = None
+        self.closed = False
+
+    def reduce(self, stage) -> None:
+        if stage.flat.parity != 0:
+            raise RuntimeError("the heterogeneous reduction reads gradient buffer 0")
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)              # every holder's gradients are final
+        if self.plan.rows:
+            if self.table is None:
+                self.table = torch.tensor(self.plan.rows, dtype=torch.int64).to(self.device)
+            _ext.require().reshard_gather(self.table, self.plan.items)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)              # nobody reads a gradient any more
+        hetero_sum(self.terms, self.slot_of, self.scratch, stage.flat, stage.flat.grads[0])
+
+    def close(self, *, barrier: bool = True) -> None:
+        if self.closed:
+            return
+        k = _ext.require()
+        torch.cuda.synchronize(self.device)
+        if barrier:
+            dist.barrier(group=self.group)
+        for ptr in self.opened.values():
+            k.symm_close(ptr)
+        self.closed = True

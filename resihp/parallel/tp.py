@@ -209,6 +209,7 @@ class TensorParallelStage:
         self._bind_compute_tensors()
         self.ws = None
         self.dp = None  # peer mappings of the fused DP reduction (set by the gradient reducer)
+        self.hetero = None  # peer mappings of the P2P heterogeneous-replica reduction
         rows = config.micro_batch_size * config.seq_len
         if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= min(8, fused.MAX_DEGREE)
                 and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0):
@@ -316,6 +317,9 @@ class TensorParallelStage:
         if self.dp is not None:
             self.dp.close(barrier=barrier)
             self.dp = None
+        if self.hetero is not None:
+            self.hetero.close(barrier=barrier)
+            self.hetero = None
 
     def _col_linear(self, h, w, g):
         """Column-parallel linear; under SP the token all-gather is fused into the GEMM."""
