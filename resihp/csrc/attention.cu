@@ -1,4 +1,6 @@
-// Causal flash attention (forward and backward) on the sm_100a tensor cores.
+// Causal flash attention (forward and backward) on the sm_100a tensor cores. Replaces the
+// reference's materialised [B, H, S, S] scores, triu mask, softmax and weights @ v
+// (resihp/parallel/tp.py:238-242, resihp/model.py:60-71).
 //
 // Q, K and V are read in place from the fused projection qkv[T, (Hq + 2*Hkv) * D]
 // (row t = batch b, position t % S), GQA maps q head h to kv head h / (Hq / Hkv).

@@ -1,6 +1,9 @@
 // Tensor-parallel GEMMs fused with their sequence-parallel collective over NVLink peer
 // memory (CUDA IPC mappings of each rank's symmetric workspace; plain P2P loads and
-// stores plus flag words -- no multicast of any kind).
+// stores plus flag words -- no multicast of any kind). Reference counterparts: the
+// column/row-parallel ``F.linear`` calls with the Megatron ``f`` / ``g`` all-reduces
+// (resihp/parallel/tp.py:63-89, 235-249); here with sequence parallelism the pair
+// becomes all-gather / reduce-scatter over tokens, fused into the GEMM.
 //
 //   AG->GEMM   y[T, N]      = all_gather_tokens(x_r[T/tp, K]) * op(W)
 //   GEMM->RS   y_r[T/tp, N] = reduce_scatter_tokens(h[T, K] * op(W))

@@ -16,6 +16,9 @@
 //              32*(w%4)..+31 = tile rows), apply the epilogue, store to global memory;
 //              the second accumulator lets the next tile's MMAs overlap this epilogue.
 // Every barrier wait is bounded (common.cuh) and reports into ``err``.
+//
+// Replaces the reference's projections (``F.linear`` in resihp/parallel/tp.py:235-237,
+// 243, 247-248, 272) and their autograd products.
 #include <algorithm>
 #include <cudaTypedefs.h>
 

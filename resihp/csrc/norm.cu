@@ -1,5 +1,6 @@
 // RMSNorm forward/backward (bf16 activations, fp32 statistics), with the residual add of
-// a pre-norm block fused in:
+// a pre-norm block fused in (the Llama counterpart of the reference's ``F.layer_norm``
+// calls, resihp/parallel/tp.py:262,264,268, and their residual adds):
 //
 //   forward   s = x (+ r);   y = s * rstd * w,   rstd = 1 / sqrt(mean(s^2) + eps)
 //   backward  g = dy * w;    ds = rstd * (g - s_hat * mean(g * s_hat)) (+ dres),

@@ -1,4 +1,7 @@
-// Memory-bound kernels of the Llama block and the optimizer:
+// Memory-bound kernels of the Llama block and the optimizer (reference counterparts:
+// ``F.gelu`` MLP activation resihp/parallel/tp.py:247, ``torch.optim.AdamW``
+// resihp/reference.py:29-38 stepped at resihp/parallel/pp.py:451, vocab-parallel
+// embedding resihp/parallel/tp.py:222-228):
 //   * RoPE (rotate-half / GPT-NeoX pairing) applied in place to the Q and K heads of
 //     the fused QKV activation, forward and backward (backward rotates by -theta);
 //   * SwiGLU  h = silu(g) * u  over the fused [g | u] projection, forward and backward;
