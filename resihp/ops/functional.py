@@ -8,6 +8,10 @@ and let autograd fill ``param.grad`` -- the reference-semantics path.
 
 Conventions: activations are 2-D ``[tokens, features]``; token ``t`` of a micro-batch
 is sequence ``t // S`` position ``t % S``.
+
+Reference counterparts: the per-op torch calls of the TP stage
+(``resihp/parallel/tp.py:222-273``: vocab-parallel embedding, projections, attention,
+layer norms, GELU MLP, LM head) and the loss (``resihp/reference.py:41-50``).
 """
 
 from __future__ import annotations

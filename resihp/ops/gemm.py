@@ -1,7 +1,8 @@
 """Linear-layer products on the tcgen05 GEMM (``csrc/gemm.cu``).
 
 All three products of a bias-free linear layer ``y = x w^T`` read their operands in
-place (no transposes): the kernel takes each operand K-major or MN-major.
+place (no transposes): the kernel takes each operand K-major or MN-major. (Reference:
+``F.linear`` at ``resihp/parallel/tp.py:235-248,272`` and its autograd products.)
 
 On CPU tensors the same functions compute in plain torch, which is the FP32 reference
 path; CUDA tensors must be bf16 and always run the hand-written kernel.

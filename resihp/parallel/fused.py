@@ -8,7 +8,8 @@
   gradient, whose gathered copy feeds the weight gradient.
 
 Both replace the NCCL pair ``gather_tokens`` / ``scatter_tokens`` of
-:mod:`resihp.parallel.collectives` (the baseline). They exchange data through a
+:mod:`resihp.parallel.collectives` (the baseline; the reference's counterparts are the
+Megatron ``f`` / ``g`` all-reduce regions, ``resihp/parallel/tp.py:63-89``). They exchange data through a
 :class:`SymmetricWorkspace` per TP group: one CUDA-IPC-shared region per rank holding
 the cross-GPU flag words, two publish slots for the AG input and two partial buffers
 for the RS (alternating by call parity), plus a local receive buffer. Peers only ever
