@@ -218,25 +218,50 @@ class GradientReducer:
                     dist.all_reduce(grad[start: start + self.bucket_elems], group=self.groups[members])
 
     def _reduce_logical(self, stage) -> None:
-        """Heterogeneous plans: full-size logical sums over the executor group."""
+        """Heterogeneous plans: full-size logical sums over the executor group.
+
+        Logical tensors are packed into buckets of about ``bucket_elems`` elements (one
+        all-reduce per bucket, not per tensor); each tensor occupies the same bucket
+        slot on every rank because the packing follows the model's name order.
+        """
         if stage is not None:
             self._sp_partial_replicated(stage)
         config = self.plan.config
         device = stage.device if stage is not None else torch.device("cpu")
         held = {} if stage is None else {s.name: s for s in stage.specs}
-        for spec in model_specs(config):
-            full = torch.zeros(spec.shape, dtype=torch.float32, device=device)
-            s = held.get(spec.name)
-            if s is not None:
-                if spec.shard_dim is None:
-                    # one copy per holder stage: without SP every TP member computed the
-                    # same gradient, with SP the partial sums were just all-reduced over
-                    # the TP group, so either way each member holds the stage's total
-                    if stage.tp_rank == 0:
-                        full += stage.g[spec.name]
-                else:
-                    torch.chunk(full, stage.tp_size, dim=spec.shard_dim)[stage.tp_rank].copy_(stage.g[spec.name])
-            dist.all_reduce(full, group=self.executor_group)
-            if s is not None:
-                mine = full if spec.shard_dim is None else torch.chunk(full, stage.tp_size, dim=spec.shard_dim)[stage.tp_rank]
-                stage.g[spec.name].copy_(mine)
+        specs = model_specs(config)
+        buckets, cur, size = [], [], 0
+        for spec in specs:
+            n = 1
+            for x in spec.shape:
+                n *= x
+            cur.append((spec, n))
+            size += n
+            if size >= self.bucket_elems:
+                buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            buckets.append(cur)
+        for bucket in buckets:
+            flat = torch.zeros(sum(n for _s, n in bucket), dtype=torch.float32, device=device)
+            off = 0
+            for spec, n in bucket:
+                full = flat[off: off + n].view(spec.shape)
+                if spec.name in held:
+                    if spec.shard_dim is None:
+                        # one copy per holder stage: without SP every TP member computed the
+                        # same gradient, with SP the partial sums were just all-reduced over
+                        # the TP group, so either way each member holds the stage's total
+                        if stage.tp_rank == 0:
+                            full += stage.g[spec.name]
+                    else:
+                        torch.chunk(full, stage.tp_size, dim=spec.shard_dim)[stage.tp_rank].copy_(stage.g[spec.name])
+                off += n
+            dist.all_reduce(flat, group=self.executor_group)
+            off = 0
+            for spec, n in bucket:
+                if spec.name in held:
+                    full = flat[off: off + n].view(spec.shape)
+                    mine = full if spec.shard_dim is None else torch.chunk(full, stage.tp_size, dim=spec.shard_dim)[stage.tp_rank]
+                    stage.g[spec.name].copy_(mine)
+                off += n
