@@ -137,3 +137,109 @@ def test_disjoint_layers_partition_groups_in_order():
         seen = [r for grp in layer for r in grp]
         assert len(seen) == len(set(seen))
     assert sorted(g for layer in layers for g in layer) == sorted(groups)
+
+
+def test_dp_peers_step_passes_the_right_buffers(monkeypatch):
+    """The fused DP step's host side: which gradient parity it reads, where the sum goes,
+    the flag arrays, the AdamW step count and the parity swap afterwards."""
+    from resihp.ops import _ext
+    from resihp.parallel import peer
+
+    class Stub:
+        calls = []
+
+        def symm_region(self, total, device):
+            return torch.zeros(total, dtype=torch.uint8), b"h"
+
+        def dp_allreduce_adamw(self, *args):
+            self.calls.append(args)
+
+    stub = Stub()
+    monkeypatch.setattr(_ext, "require", lambda: stub)
+    entries = [(TensorSpec("w", (8, 8), None, "normal"), (8, 8))]
+    flat = FlatState(entries, "cpu", torch.bfloat16, shared=True)
+
+    class Stage:
+        pass
+
+    stage = Stage()
+    stage.flat = flat
+    stage.config = _config(dtype="bf16")
+    stage.use_grad = flat.set_parity
+    dp = peer.DpPeers.__new__(peer.DpPeers)
+    dp.rank, dp.bases, dp.grid, dp.epoch, dp.closed = 1, [1000, flat.region_ptr], 3, 0, False
+    for expected_parity in (0, 1, 0):
+        assert flat.parity == expected_parity
+        dp.step(stage)
+        args = stub.calls[-1]
+        grads, me, sum_out = args[0], args[1], args[2]
+        off = flat.field_offsets[f"grad{expected_parity}"]
+        assert grads == [1000 + off, flat.region_ptr + off] and me == 1
+        assert sum_out is flat.grads[1 - expected_parity]
+        assert args[3] is flat.master and args[4] is flat.exp_avg and args[5] is flat.exp_avg_sq
+        assert args[6] is flat.work
+        assert args[12] == flat.step and args[14] == flat.region_ptr and args[15] == [1000, flat.region_ptr]
+        assert args[16] == dp.epoch and args[17] == 3
+    assert flat.step == 3 and flat.parity == 1
+
+
+def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
+    """The fused TP workspace's host bookkeeping: per call the publish/ready bases grow by
+    the kernel module's own step (variant 0) or the row-block base does (variant 1), and
+    slots / partial buffers alternate by epoch."""
+    import contextlib
+
+    from resihp.ops import _ext
+    from resihp.parallel import fused
+
+    class Stub:
+        def __init__(self):
+            self.ag, self.rs = [], []
+
+        def symm_alloc(self, total):
+            return 1 << 20, b"h"
+
+        def symm_open(self, handle):
+            return 1 << 30
+
+        def fused_grid(self, t, n, tp):
+            return 7
+
+        def fused_counter_step(self, grid, variant):
+            return (4 if variant == 0 else 6) * grid
+
+        def fused_block_step(self, t, n, tp, grid):
+            return 12
+
+        def ag_gemm(self, *args):
+            self.ag.append(args)
+
+        def gemm_rs(self, *args):
+            self.rs.append(args)
+
+    stub = Stub()
+    monkeypatch.setattr(_ext, "require", lambda: stub)
+    monkeypatch.setattr(fused.dist, "get_world_size", lambda group: 4)
+    monkeypatch.setattr(fused.dist, "get_rank", lambda group: 1)
+    monkeypatch.setattr(fused.dist, "all_gather_object", lambda out, obj, group: out.__setitem__(slice(None), [obj] * 4))
+    monkeypatch.setattr(fused.dist, "barrier", lambda group=None: None)
+    monkeypatch.setattr(torch.cuda, "device", lambda d: contextlib.nullcontext())
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda d=None: None)
+    for v3, variant in ((False, 0), (True, 1)):
+        monkeypatch.setattr(fused, "ROW_BLOCK_VARIANT", v3)
+        ws = fused.SymmetricWorkspace(None, 128, 64, "cpu")
+        assert ws.variant == variant
+        x = torch.zeros(128, 64, dtype=torch.bfloat16)
+        w = torch.zeros(32, 64, dtype=torch.bfloat16)
+        for call in range(3):
+            ws.all_gather_gemm(x, w, False, 32)
+            args = stub.ag[-1]
+            assert args[9] == call + 1                                   # epoch
+            assert args[1] == ws._slot(ws.base, call + 1)                # own slot of this parity
+            assert args[13] == (4 if variant == 0 else 6) * 7 * call     # publish base before the call
+            assert args[17] == variant and args[18] == ws.base + 256
+            assert args[19] == (12 * call if variant == 1 else 0)
+        assert ws._slot(ws.base, 1) != ws._slot(ws.base, 2) and ws._slot(ws.base, 1) == ws._slot(ws.base, 3)
+        h = torch.zeros(512, 16, dtype=torch.bfloat16)
+        ws.gemm_reduce_scatter(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
+        assert stub.rs[-1][-1] == variant and stub.rs[-1][7] == ws._part(ws.base, 1)
