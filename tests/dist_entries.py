@@ -229,7 +229,8 @@ def e2e_entry(rank, env, config_dict, failures, out_dir):
     plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
     groups = cp.build_training_groups(plan)
     cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=ck)
-    record = {"rank": rank, "iterations": [], "plans": [plan.digest], "recoveries": [], "stopped": None}
+    record = {"rank": rank, "iterations": [], "plans": [plan.digest], "recoveries": [], "stopped": None,
+              "groups": [len(dist.distributed_c10d._world.pg_map)]}
     failed = ()
     try:
         it = 0
@@ -261,6 +262,7 @@ def e2e_entry(rank, env, config_dict, failures, out_dir):
                 if cp.training_run is not None:
                     a1 = verify.matches_checkpoint(cp.training_run, plan=plan, rank=rank, checkpoint_path=ck)
                 record["plans"].append(plan.digest)
+                record["groups"].append(len(dist.distributed_c10d._world.pg_map))
                 record["recoveries"].append({"after": it, "lost": list(lost), "a1": a1,
                                              "resumed_from": cp.resume_cursor, "version": plan.version})
                 it = cp.resume_cursor

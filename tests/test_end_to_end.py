@@ -17,7 +17,8 @@ event lands on the replica the first left untouched. The reference's end-to-end 
 6. before resuming, every placed rank's state equals the checkpoint (principle A1);
 7. after resuming, each iteration's loss matches the single-process oracle restarted
    from the anchor of the last failure (principle A2), iterations 1-2 the plain oracle;
-8. no process group survives the run.
+8. no process group survives the run, and none leaks across safe points: after each
+   re-formation a rank holds no more groups than the initial plan needed.
 """
 
 import os
@@ -128,6 +129,8 @@ def test_three_d_run_with_two_kills(tmp_path, sp):
         got = loss_at(it)
         assert abs(got - w) <= 1e-4 * abs(w), (it, got, w)
 
-    # 8. nothing left behind
+    # 8. nothing left behind, nothing leaked across epochs
     for r in survivors:
         assert results[r]["initialized"] is False
+        counts = results[r]["groups"]
+        assert len(counts) == 3 and max(counts[1:]) <= counts[0], counts
