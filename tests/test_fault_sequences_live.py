@@ -66,3 +66,31 @@ def test_random_sequence_recovers_consistently(seed, tmp_path):
                     per_replica.setdefault(e["replica"], e["loss"])
         got = sum(per_replica.values())
         assert abs(got - want) <= 1e-4 * abs(want), (after, got, want)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("victim", [0, 1, 2, 3])
+def test_losing_any_single_rank_recovers(victim, tmp_path):
+    """TP2 x DP2 on four ranks, each rank killed in turn after iteration 2 -- including
+    rank 0, the checkpoint writer and lowest rank (reference: the lose-every-rank family of
+    ``tests/test_recovery.py``)."""
+    run_config = dict(CONFIG, tp=2, pp=1, dp=2, num_layers=4, iterations=4)
+    config = TrainConfig(**run_config)
+    codes = run_ranks(dist_entries.e2e_entry, 4, run_config, {"2": victim}, str(tmp_path))
+    assert_killed(codes, [victim], f"victim {victim}")
+    survivors = [r for r in range(4) if r != victim]
+    results = read_results(tmp_path, range(4))
+    for r in survivors:
+        res = results[r]
+        assert res["stopped"] is None and len(res["plans"]) == 2 and res["initialized"] is False
+        assert all(rec["a1"] in (True, None) for rec in res["recoveries"])
+    anchor, completed = load_anchor(os.path.join(tmp_path, "anchor_2.pt"))
+    want = steps_from_anchor(config, anchor, start=completed, count=2)
+    for i, rec in enumerate(want):
+        per_replica = {}
+        for r in survivors:
+            for e in results[r]["iterations"]:
+                if e["iteration"] == 3 + i and e.get("loss") is not None:
+                    per_replica.setdefault(e["replica"], e["loss"])
+        got = sum(per_replica.values())
+        assert abs(got - rec["loss"]) <= 1e-4 * abs(rec["loss"]), (victim, 3 + i, got, rec["loss"])
