@@ -271,3 +271,35 @@ def e2e_entry(rank, env, config_dict, failures, out_dir):
     cp.shutdown()
     record["initialized"] = dist.is_initialized()
     write_result(out_dir, rank, record)
+
+
+def churn_entry(rank, env, config_dict, churn_after, out_dir):
+    """Train; optionally tear every group down after ``churn_after`` iterations and rebuild
+    the world, the groups and the run from its own live state under the same plan."""
+    _setup(env)
+    from harness import write_result
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.plan import build_plan
+    from resihp.recovery import initial_run, recover
+
+    config = TrainConfig(**config_dict)
+    os.chdir(out_dir)
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    ck = Path(out_dir, "checkpoint.pt")
+    cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=ck)
+    losses = []
+    for it in range(1, config.iterations + 1):
+        losses.append(cp.training_step())
+        cp.commit_checkpoint(plan, cursor=it)
+        cp.flush_checkpoint()
+        if it == churn_after:
+            cp.dissolve_world()
+            cp.form_world(cp.members, epoch=cp.epoch + 1)
+            groups = cp.build_training_groups(plan)
+            cp.training_run, _digest, _cursor = recover(cp.training_run, plan=plan, previous=plan, rank=rank,
+                                                        cursor=it, checkpoint_path=ck, groups=groups)
+    write_result(out_dir, rank, {"rank": rank, "losses": losses})
+    cp.shutdown()

@@ -67,3 +67,19 @@ def test_rollback_to_an_older_checkpoint_matches_a_rerun(tmp_path):
         for it, loss in r["losses"].items():
             want.setdefault(int(it), set()).add(loss)
     assert got == {it: sorted(v) for it, v in sorted(want.items())} and sorted(got) == [3, 4, 5, 6]
+
+
+@pytest.mark.slow
+def test_group_churn_without_failure_is_transparent(tmp_path):
+    """Every communicator torn down and rebuilt between iterations, the run rebuilt from
+    its own state under the same plan: the losses equal an uninterrupted run bit for bit
+    (reference: the ``dynamic_groups_pipeline`` gate of ``tests/test_combinations.py``)."""
+    config = dict(BASE, tp=2, pp=2, dp=1, iterations=4)
+    runs = {}
+    for churn in (0, 2):
+        out = tmp_path / f"churn{churn}"
+        out.mkdir()
+        codes = run_ranks(dist_entries.churn_entry, 4, config, churn, str(out))
+        assert set(codes.values()) == {0}, codes
+        runs[churn] = {r: v["losses"] for r, v in read_results(out, range(4)).items()}
+    assert runs[0] == runs[2]
