@@ -26,6 +26,7 @@ CASES = [
     (dict(tp=2, pp=2, dp=2, tied_embeddings=True), (5, 2)),  # two failures, tied pairs at mixed degrees
     (dict(tp=2, pp=1, dp=2, sequence_parallel=True), (1,)),  # SP replica (TP2) next to a TP1 replica
     (dict(tp=2, pp=2, dp=2, sequence_parallel=True, tied_embeddings=True), (5, 2)),  # all of it at once
+    (dict(tp=1, pp=1, dp=4), (0,)),                        # 4 micro-batches over 3 replicas: a 2/1/1 split
 ]
 
 
