@@ -4,6 +4,8 @@
     python -m resihp.utils.kernel_probe attn   # causal attention fwd + bwd, B2 H16 S2048 D128
     python -m resihp.utils.kernel_probe dp     # fused DP all-reduce + AdamW, 2 replicas emulated, 64M elements
     python -m resihp.utils.kernel_probe reshard  # state move TP2 -> TP1 of one 1.3B layer group (3 fields)
+    python -m resihp.utils.kernel_probe gemm_time  # CUDA-event TF/s: forward / dgrad / wgrad / cuBLAS forward
+    python -m resihp.utils.kernel_probe attn_time  # CUDA-event fwd / bwd time of the causal attention
     python -m resihp.utils.kernel_probe fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
     python -m resihp.utils.kernel_probe fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
 
@@ -40,6 +42,56 @@ def attn() -> None:
         qkv = torch.randn(b * seq, 3 * hq * d, device="cuda").bfloat16().requires_grad_()
         out = fn.rope_attention(qkv, cs, seq, hq, hq, d)
         out.backward(torch.randn_like(out))
+
+
+def _time_us(fn_, it: int = 20, warm: int = 5) -> float:
+    """CUDA-event time of one call (``warm`` untimed calls, then ``it`` timed back to back)."""
+    for _ in range(warm):
+        fn_()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(it):
+        fn_()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / it * 1000.0
+
+
+def gemm_time() -> None:
+    """TF/s of the three linear-layer products and of ``torch.matmul`` on the 1.3B shapes."""
+    import json
+
+    out = []
+    for m, n, k in ((4096, 6144, 2048), (4096, 11008, 2048), (4096, 2048, 5504), (8192, 8192, 8192)):
+        x = torch.randn(m, k, device="cuda").bfloat16()
+        w = torch.randn(n, k, device="cuda").bfloat16()
+        dy = torch.randn(m, n, device="cuda").bfloat16()
+        acc = torch.zeros(n, k, device="cuda")
+        flop = 2.0 * m * n * k
+        row = {"m": m, "n": n, "k": k}
+        for name, fn_ in (("forward", lambda: ops.linear(x, w)), ("dgrad", lambda: ops.linear_dgrad(dy, w)),
+                          ("wgrad", lambda: ops.linear_wgrad(dy, x, out=acc, accumulate=True)),
+                          ("cublas_forward", lambda: torch.matmul(x, w.t()))):
+            row[name + "_tflops"] = round(flop / _time_us(fn_) / 1e6, 1)
+        out.append(row)
+    print(json.dumps(out))
+
+
+def attn_time() -> None:
+    """Forward and backward time of the causal attention at B2 H16 S2048 D128."""
+    import json
+
+    seq, hq, d, b = 2048, 16, 128, 2
+    k = ops._ext.require()
+    qkv = torch.randn(b * seq, 3 * hq * d, device="cuda").bfloat16()
+    out, lse = k.attn_fwd(qkv, seq, hq, hq, d, d**-0.5)
+    dout = torch.randn_like(out)
+    fwd = _time_us(lambda: k.attn_fwd(qkv, seq, hq, hq, d, d**-0.5))
+    bwd = _time_us(lambda: k.attn_bwd(qkv, out, dout, lse, seq, hq, hq, d, d**-0.5))
+    flop = 2 * 2 * b * hq * seq * seq * d / 2  # two products, causal half
+    print(json.dumps({"fwd_us": round(fwd, 1), "bwd_us": round(bwd, 1), "fwd_tflops": round(flop / fwd / 1e6, 1),
+                      "bwd_tflops": round(2.5 * flop / bwd / 1e6, 1)}))
 
 
 def dp() -> None:
@@ -114,7 +166,8 @@ def main(argv=None) -> None:
     if what in ("fused_ag", "fused_rs"):
         {"fused_ag": fused_ag, "fused_rs": fused_rs}[what](int(args[1]) if len(args) > 1 else 2)
     else:
-        {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard}[what]()
+        {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard, "gemm_time": gemm_time,
+         "attn_time": attn_time}[what]()
     torch.cuda.synchronize()
     ops.check_device_errors()
     print("ok", what)
