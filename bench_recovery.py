@@ -16,6 +16,10 @@ after each event.
 
     python bench_recovery.py [--gpus 8] [--kills 30:5,60:2] [--iterations 70]
     python bench_recovery.py --config 1     # CPU/Gloo, 4 ranks, kill rank 3 after step 8
+    python bench_recovery.py --config 1 --reference-model [--impl reference]
+        # config 1's topology and kill on the closest model the reference can run (GPT-2
+        # blocks, vocab 1024, seq 128, seed 1), by this framework or by the unmodified
+        # reference timed through baseline/recovery_hook
 """
 
 from __future__ import annotations
@@ -37,6 +41,27 @@ CONFIG1 = dict(model_dim=256, num_layers=4, num_heads=4, ffn_dim=688, vocab_size
                micro_batch_size=2, seed=0, tp=2, pp=2, dp=1, iterations=20, arch="llama", dtype="fp32",
                tied_embeddings=True, norm_eps=1e-5, rope_theta=10000.0, init_std=0.02, lr=1e-3, beta1=0.9,
                beta2=0.95, weight_decay=0.1)
+# The closest run the reference can express: GPT-2 blocks (its only model), FP32, its AdamW
+# settings, seed 1 (it rejects seed 0); vocabulary and sequence set through its run
+# constants by the timing hook.
+REFERENCE_MODEL1 = dict(model_dim=256, num_layers=4, num_heads=4, batch_size=8, micro_batch_size=2, seed=1, tp=2,
+                        pp=2, dp=1, iterations=20, memory_budget_bytes=None)
+
+
+def _json_objects(text):
+    """Every JSON object in ``text`` (the reference's ranks share stdout without
+    line-atomic writes, so objects can run together on one line)."""
+    dec = json.JSONDecoder()
+    out, i = [], 0
+    while True:
+        j = text.find("{", i)
+        if j < 0:
+            return out
+        try:
+            obj, i = dec.raw_decode(text, j)
+            out.append(obj)
+        except json.JSONDecodeError:
+            i = j + 1
 
 
 def parse():
@@ -49,6 +74,10 @@ def parse():
     p.add_argument("--layout", default=None, help="tp,pp,dp (default: config 4's layout for --gpus)")
     p.add_argument("--config", type=int, choices=(1, 4), default=4,
                    help="4: the 1.3B GPU run (default); 1: the CPU/Gloo run of BASELINE config 1")
+    p.add_argument("--reference-model", action="store_true",
+                   help="config 1 only: the GPT-2 config-1-like model the reference can express")
+    p.add_argument("--impl", choices=("resihp", "reference"), default="resihp",
+                   help="config 1 with --reference-model: run the unmodified reference instead")
     p.add_argument("--checkpoint-every", type=int, default=None,
                    help="commit the logical checkpoint every N steps (default: every step without a peer "
                         "replica, never with one)")
@@ -57,8 +86,12 @@ def parse():
 
 def main():
     args = parse()
+    if args.impl == "reference" and not (args.config == 1 and args.reference_model):
+        raise SystemExit("--impl reference runs config 1 with --reference-model only")
     if args.config == 1:
         config = dict(CONFIG1)
+        if args.reference_model:
+            config = dict(REFERENCE_MODEL1)
         tp, pp, dp = config["tp"], config["pp"], config["dp"]
         args.gpus = tp * pp * dp
         args.kills = "8:3"
@@ -87,26 +120,41 @@ def main():
         env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", RESIHP_CHECKPOINT=os.path.join(tmp, "ck.pt"))
         if args.config == 1:
             env.update(CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")  # config 1 is the CPU/Gloo run
+        if args.impl == "reference":
+            ref = os.path.join(ROOT, "baseline", "_ref")
+            if not os.path.isdir(os.path.join(ref, "resihp")):
+                raise SystemExit("reference not installed under baseline/_ref")
+            env.update(PYTHONPATH=os.pathsep.join([os.path.join(ROOT, "baseline", "recovery_hook"), ref]),
+                       RESIHP_REFHOOK="1", RESIHP_REF_VOCAB="1024", RESIHP_REF_SEQ="128")
+        elif args.reference_model:
+            with open(cfg_path, "w") as f:
+                json.dump(dict(config, vocab_size=1024, seq_len=128), f)
         env.setdefault("RESIHP_GROUP_TIMEOUT", "120")
         out = subprocess.run(
             [sys.executable, "-m", "resihp.launch", "--config", cfg_path, "--failures", fail_path,
              "--timeout", str(args.timeout)],
             cwd=tmp, env=env, capture_output=True, text=True, timeout=args.timeout + 120,
         )
-    lines = []
-    for line in out.stdout.splitlines():
-        if line.startswith("{"):
-            try:
-                lines.append(json.loads(line))
-            except json.JSONDecodeError:
-                pass
+    lines = _json_objects(out.stdout)
+    if args.impl == "reference":
+        for l in lines:
+            if "refrecovery" in l:
+                l["recovery"] = dict(l.pop("refrecovery"), after_iteration=kills[0][0], phases={},
+                                     plan_version=1)
+            if "refstep" in l:
+                l["step"], l["step_s"] = -1, l.pop("refstep")["step_s"]
     launch = next((l["launch"] for l in lines if "launch" in l), None)
     steps: dict[int, list] = {}
     for l in lines:
         if "step" in l:
             steps.setdefault(l["step"], []).append(l["step_s"])
-    tokens = config["batch_size"] * config["seq_len"]
-    label = "llama-config1 (CPU/Gloo, FP32)" if args.config == 1 else ("llama-1.3b" if not args.small else "llama-small")
+    seq_len = config.get("seq_len", 128 if args.reference_model else 16)
+    tokens = config["batch_size"] * seq_len
+    if args.config == 1:
+        label = ("gpt2 config-1-like (CPU/Gloo, FP32)" if args.reference_model else "llama-config1 (CPU/Gloo, FP32)")
+    else:
+        label = "llama-1.3b" if not args.small else "llama-small"
+    all_steps = sorted(x for v in steps.values() for x in v)
     step_rate = {it: tokens / max(v) for it, v in steps.items()}
     events = []
     for a, r in kills:
@@ -128,10 +176,11 @@ def main():
         })
     print(json.dumps({
         "metric": "fail-stop recovery seconds (failure -> end of first resumed step, max over survivors)",
+        "impl": args.impl, "median_step_s": round(statistics.median(all_steps), 4) if all_steps else None,
         "n_gpus": 0 if args.config == 1 else args.gpus, "ranks": args.gpus,
         "config": {"model": label, "baseline_config": args.config,
                    "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if config.get("sequence_parallel") else ""),
-                   "dtype": config["dtype"], "global_batch": config["batch_size"], "seq_len": config["seq_len"]},
+                   "dtype": config.get("dtype", "fp32"), "global_batch": config["batch_size"], "seq_len": seq_len},
         "events": events, "launch": launch, "launcher_rc": out.returncode,
         "stopped": [l for l in lines if "stopped" in l],
         "steps_seen": sorted(steps),
