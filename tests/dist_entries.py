@@ -12,9 +12,13 @@ if ROOT not in sys.path:
 
 def _setup(env):
     os.environ.update(env)
+    import faulthandler
+
     import torch
 
     torch.set_num_threads(1)
+    # a rank stuck in a collective prints every thread's stack instead of hanging silently
+    faulthandler.dump_traceback_later(240, repeat=True)
 
 
 def train_entry(rank, env, config_dict, steps, out_dir, dump_state):
