@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--impl", choices=["resihp", "reference"], default="resihp")
     p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
                    help="BASELINE config: 2 (default, 1/2/4/8 GPUs), 3 or 5 (8 GPUs)")
+    p.add_argument("--trace", default=None,
+                   help="after the timed steps, profile one more step per rank and write a Chrome trace "
+                        "plus a kernel summary into this directory (analysis only; not part of the number)")
     return p.parse_args()
 
 
@@ -173,6 +176,30 @@ def _tp_comm(tp):
     return "fused-nvlink" if fused.ENABLED and tp <= fused.MAX_DEGREE else "nccl"
 
 
+def _trace_step(step, directory, rank, barrier):
+    """One profiled step after the measurement: Chrome trace + top kernels by device time."""
+    import json as _json
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    os.makedirs(directory, exist_ok=True)
+    barrier()
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    barrier()
+    prof.export_chrome_trace(os.path.join(directory, f"trace_rank{rank}.json"))
+    rows = []
+    for ev in prof.key_averages():
+        device_us = getattr(ev, "device_time_total", 0.0) or getattr(ev, "cuda_time_total", 0.0)
+        if device_us > 0:
+            rows.append({"name": ev.key[:120], "calls": ev.count, "device_us": round(device_us, 1)})
+    rows.sort(key=lambda r: -r["device_us"])
+    with open(os.path.join(directory, f"kernels_rank{rank}.json"), "w") as f:
+        _json.dump(rows[:60], f, indent=1)
+
+
 def _memory(run, plan, config, device):
     """``(measured peak bytes, the planner's estimate)`` for this rank's stage."""
     import torch
@@ -262,6 +289,8 @@ def run_ours(args):
     counter.enabled = False
     launches = int(reduce_max(counter.launches))
     check_device_errors(local)
+    if args.trace:
+        _trace_step(step, args.trace, rank, barrier)
     try:
         used, estimate = _memory(run, plan, config, device)
     except (ValueError, RuntimeError) as error:  # an auxiliary report must not cost the measurement
