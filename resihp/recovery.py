@@ -466,7 +466,6 @@ def _p2p_recover(run, *, plan, rank, anchor, groups, device, cursor, pin):
             flat = new_run.stage.flat
             shapes = _shape_of(config)
             owned = stage_layout(plan, stage)
-            idx = stage.tp_members.index(rank)
             by_name = {}
             for route in routes_for(plan, rank):
                 for name in route_names(config, route):

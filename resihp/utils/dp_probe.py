@@ -18,7 +18,7 @@ import torch
 import torch.distributed as dist
 
 from resihp.models.layout import TensorSpec
-from resihp.ops import _ext, check_device_errors
+from resihp.ops import check_device_errors
 from resihp.ops import functional as fn
 from resihp.parallel.tp import FlatState
 
@@ -30,7 +30,6 @@ def main():
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl")
     dev = torch.device("cuda", rank)
-    k = _ext.require()
     flat = FlatState([(TensorSpec("w", (n,), None, "normal"), (n,))], dev, torch.bfloat16, shared=True)
     g = torch.Generator(device="cuda").manual_seed(11 + rank)
     flat.grads[0].normal_(generator=g)
