@@ -233,3 +233,68 @@ class Simulation:
                         live[r] = [[a, None] for a in self._call_agents(r, epoch[r])]
             steps += 1
         return steps
+
+
+class DpSimulation:
+    """``dp`` replicas running ``epochs`` training steps, each: backward accumulates into
+    the current gradient buffer, then the fused DP kernel (``peer_state.cu``) -- per CTA:
+    announce the epoch in every peer's flag array, wait for every peer's announcement,
+    read every replica's current buffer for the CTA's slice, write the sum into the other
+    buffer -- after which the buffers swap roles (the next backward zeroes and fills the
+    summed one)."""
+
+    def __init__(self, *, dp, grid, epochs, seed):
+        self.dp, self.grid, self.epochs = dp, grid, epochs
+        self.rng = random.Random(seed)
+        # per replica: flag words [grid][dp], two gradient buffers of per-slice versions
+        self.flags = [[[0] * dp for _ in range(grid)] for _ in range(dp)]
+        self.grads = [[[None] * grid, [None] * grid] for _ in range(dp)]
+        self.parity = [0] * dp
+
+    def _backward(self, r, e):
+        cur = self.parity[r]
+        for b in range(self.grid):
+            self.grads[r][cur][b] = ("acc", e)                          # zeroed, then accumulated
+            yield lambda: True
+
+    def _cta(self, r, b, e):
+        cur = self.parity[r]
+        for q in range(self.dp):
+            if q != r:
+                self.flags[q][b][r] = max(self.flags[q][b][r], e)       # release store of the epoch
+        yield lambda: all(self.flags[r][b][q] >= e for q in range(self.dp) if q != r)
+        for q in range(self.dp):
+            # every replica's buffer of this epoch holds this step's accumulation
+            got = self.grads[q][cur][b]
+            if got != ("acc", e):
+                raise ProtocolError(f"race: replica {q} slice {b} holds {got}, expected the epoch-{e} gradients")
+            yield lambda: True
+        self.grads[r][1 - cur][b] = ("sum", e)
+
+    def run(self) -> int:
+        phase = {r: ("backward", 1) for r in range(self.dp)}
+        live = {r: [[self._backward(r, 1), None]] for r in range(self.dp)}
+        steps = 0
+        while live:
+            ready = [(r, s) for r, agents in live.items() for s in agents if s[1] is None or s[1]()]
+            if not ready:
+                raise ProtocolError(f"deadlock in phases {phase}")
+            r, slot = self.rng.choice(ready)
+            try:
+                slot[1] = next(slot[0])
+            except StopIteration:
+                live[r].remove(slot)
+                if not live[r]:
+                    kind, e = phase[r]
+                    if kind == "backward":
+                        phase[r] = ("kernel", e)
+                        live[r] = [[self._cta(r, b, e), None] for b in range(self.grid)]
+                    else:
+                        self.parity[r] = 1 - self.parity[r]              # the summed buffer is now current
+                        if e == self.epochs:
+                            del live[r]
+                        else:
+                            phase[r] = ("backward", e + 1)
+                            live[r] = [[self._backward(r, e + 1), None]]
+            steps += 1
+        return steps

@@ -28,3 +28,11 @@ def test_a_host_counting_the_wrong_copy_warps_is_caught():
     wrong = lambda grid: 4 * grid  # noqa: E731
     with pytest.raises(ProtocolError, match="race|deadlock"):
         Simulation("ag", tp=2, rows_per_rank=256, n=512, grid=3, variant=1, epochs=6, seed=0, host_step=wrong).run()
+
+
+@pytest.mark.parametrize("dp,grid", [(2, 3), (3, 4), (4, 2), (8, 3)])
+def test_dp_step_protocol_has_no_race_or_deadlock(dp, grid):
+    from fused_protocol import DpSimulation
+
+    for seed in range(8):
+        assert DpSimulation(dp=dp, grid=grid, epochs=5, seed=seed).run() > 0
