@@ -44,12 +44,46 @@ def assert_equals_checkpoint(run, *, plan, rank, checkpoint_path) -> None:
         raise AssertionError(f"rank {rank} does not equal the checkpoint under plan v{plan.version}: {problems}")
 
 
+def checkpoint_mismatches_at(run, *, plan, rank, checkpoint_path) -> list[str]:
+    """Every way this rank's state differs from the checkpoint at ``checkpoint_path``."""
+    anchor, _ = load_anchor(checkpoint_path)
+    return checkpoint_mismatches(run, plan=plan, rank=rank, anchor=anchor)
+
+
 # --- A2 --------------------------------------------------------------------------------
 
 
-def _denominator(config, exp_avg_sq, step):
+def _check_constants(config, vocab_size, sequence_length):
+    """The reference passes its run constants alongside the config; here the config
+    carries them, and any value passed must agree."""
+    for name, given, have in (("vocab_size", vocab_size, config.vocab_size),
+                              ("sequence_length", sequence_length, config.seq_len)):
+        if given is not None and given != have:
+            raise ValueError(f"{name}={given} does not match the config ({have})")
+
+
+def batch(config, index, *, device, vocab_size=None, sequence_length=None):
+    """Iteration ``index``'s fixed token batch -- the same stream a run consumes."""
+    from .reference import token_stream
+
+    _check_constants(config, vocab_size, sequence_length)
+    return token_stream(config)[index].to(device)
+
+
+def denominator(config, exp_avg_sq, step):
+    """AdamW's ``sqrt(v / bias_correction2) + eps`` after its ``step``-th update."""
     bc2 = 1 - config.beta2 ** float(step)
     return exp_avg_sq.sqrt() / math.sqrt(bc2) + config.adam_eps
+
+
+_denominator = denominator
+
+
+def reference_steps(config, *, count, device="cpu", vocab_size=None, sequence_length=None) -> list[dict]:
+    """The no-failure oracle: ``count`` full-batch steps from the seeded initialisation."""
+    _check_constants(config, vocab_size, sequence_length)
+    run = ReferenceRun(config, device=device)
+    return [step_record(run) for _ in range(count)]
 
 
 def step_record(run: ReferenceRun) -> dict:
@@ -112,6 +146,7 @@ def assert_matches_reference(comparison: dict, *, label: str = "") -> None:
 
 
 __all__ = [
-    "RTOL", "ATOL", "matches_checkpoint", "assert_equals_checkpoint", "step_record", "steps_from_anchor",
-    "compare_shards", "assert_matches_reference", "stage_of", "stage_layout",
+    "RTOL", "ATOL", "matches_checkpoint", "assert_equals_checkpoint", "checkpoint_mismatches_at", "batch",
+    "denominator", "step_record", "reference_steps", "steps_from_anchor", "compare_shards",
+    "assert_matches_reference", "stage_of", "stage_layout",
 ]

@@ -26,3 +26,24 @@ def test_a1_and_a2_on_resumed_tp_run(tmp_path):
     for r in read_results(tmp_path, [0, 1]).values():
         assert r["a1"] is True
         verify.assert_matches_reference(r["cmp"], label=f"rank {r['rank']}")
+
+
+def test_reference_style_helpers():
+    """The reference's verify helpers exist here with the same meaning: ``batch`` is the
+    run's token stream, ``reference_steps`` the no-failure oracle from step 0, and the run
+    constants it passes separately must agree with the config."""
+    import pytest
+    import torch
+
+    from resihp import verify
+    from resihp.config import TrainConfig
+    from resihp.reference import ReferenceRun, token_stream
+
+    cfg = TrainConfig(model_dim=32, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=3, tp=1, pp=1,
+                      dp=1, iterations=2, arch="llama", vocab_size=48, seq_len=8, ffn_dim=64)
+    assert torch.equal(verify.batch(cfg, 1, device="cpu"), token_stream(cfg)[1])
+    with pytest.raises(ValueError):
+        verify.batch(cfg, 0, device="cpu", vocab_size=256)
+    recs = verify.reference_steps(cfg, count=2, vocab_size=48, sequence_length=8)
+    run = ReferenceRun(cfg)
+    assert [r["loss"] for r in recs] == [run.step().loss, run.step().loss]
