@@ -76,8 +76,6 @@ def denominator(config, exp_avg_sq, step):
     return exp_avg_sq.sqrt() / math.sqrt(bc2) + config.adam_eps
 
 
-_denominator = denominator
-
 
 def reference_steps(config, *, count, device="cpu", vocab_size=None, sequence_length=None) -> list[dict]:
     """The no-failure oracle: ``count`` full-batch steps from the seeded initialisation."""
@@ -100,7 +98,7 @@ def step_record(run: ReferenceRun) -> dict:
     params, denoms = {}, {}
     for n, (view, _d) in stage.local_shards().items():
         params[n] = view.detach().clone()
-        denoms[n] = _denominator(stage.config, stage.moment_views(n)["exp_avg_sq"], stage.flat.step)
+        denoms[n] = denominator(stage.config, stage.moment_views(n)["exp_avg_sq"], stage.flat.step)
     return {"loss": float(loss.detach()), "grads": grads, "params": params, "denoms": denoms}
 
 
