@@ -118,6 +118,19 @@ class ControlPlane:
     def world_size(self) -> int:
         return len(self.members)
 
+    # the reference's names for this rank's training groups
+    @property
+    def tp_group(self):
+        return self.groups.tp
+
+    @property
+    def executor_group(self):
+        return self.groups.executor
+
+    @property
+    def boundary_groups(self) -> dict:
+        return dict(self.groups.hops)
+
     def torch_rank(self, plan_rank: int) -> int:
         return self.members.index(plan_rank)
 
