@@ -200,6 +200,22 @@ def _trace_step(step, directory, rank, barrier):
         _json.dump(rows[:60], f, indent=1)
 
 
+def bench_config(which: int, world: int, iterations: int):
+    """The training config the bench runs: BASELINE config ``which`` on ``world`` GPUs."""
+    from resihp.config import TrainConfig
+
+    spec = CONFIGS[which]
+    tp, pp, dp = spec["layouts"][world]
+    extra = dict(num_kv_heads=None)
+    extra.update(spec["extra"])
+    return TrainConfig(
+        **spec["model"], **extra, batch_size=spec["global_batch"], micro_batch_size=spec["micro_batch"], seed=1,
+        tp=tp, pp=pp, dp=dp, iterations=iterations, arch="llama", dtype="bf16",
+        sequence_parallel=tp > 1, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95, weight_decay=0.1,
+        memory_budget_bytes=180 * 10**9,
+    )
+
+
 def _memory(run, plan, config, device):
     """``(measured peak bytes, the planner's estimate)`` for this rank's stage."""
     import torch
@@ -231,7 +247,6 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from resihp.config import TrainConfig
     from resihp.control import ControlPlane
     from resihp.ops import _ext, check_device_errors
     from resihp.plan import build_plan
@@ -247,14 +262,7 @@ def run_ours(args):
     global_batch, micro_batch = spec["global_batch"], spec["micro_batch"]
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    extra = dict(num_kv_heads=None)
-    extra.update(spec["extra"])
-    config = TrainConfig(
-        **spec["model"], **extra, batch_size=global_batch, micro_batch_size=micro_batch, seed=1,
-        tp=tp, pp=pp, dp=dp, iterations=args.warmup + args.steps, arch="llama", dtype="bf16",
-        sequence_parallel=tp > 1, init_std=0.02, lr=3e-4, beta1=0.9, beta2=0.95, weight_decay=0.1,
-        memory_budget_bytes=180 * 10**9,
-    )
+    config = bench_config(args.config, world, args.warmup + args.steps)
     cp = ControlPlane(rank, range(world), _store(rank, world), "nccl", device=device)
     cp.form_world(range(world), epoch=0)
     plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
@@ -293,7 +301,7 @@ def run_ours(args):
         _trace_step(step, args.trace, rank, barrier)
     try:
         used, estimate = _memory(run, plan, config, device)
-    except (ValueError, RuntimeError) as error:  # an auxiliary report must not cost the measurement
+    except Exception as error:  # an auxiliary report must not cost the measurement
         print(f"memory report unavailable: {error}", file=sys.stderr)
         used, estimate = 0.0, 0.0
     mem = torch.tensor([used, estimate])

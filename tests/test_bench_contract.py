@@ -1,0 +1,99 @@
+"""The host-side parts of ``bench.py`` that decide what a reported number means.
+
+* Every (config, GPU count) the bench accepts plans to exactly the layout its JSON line
+  names in ``parallelism`` -- a planner change that picked another TP degree or stage
+  count would otherwise silently change the measured configuration.
+* The clock summary keeps only the visible GPUs' samples and names every throttle reason
+  that was active.
+* The memory report reads the attributes it needs from a real run (here a CPU/Gloo TP2
+  run) and matches the planner's estimate for that stage.
+"""
+
+import json
+import os
+from pathlib import Path
+
+import pytest
+
+import bench
+from harness import read_results, run_ranks, write_result
+from resihp.memory import estimate_memory
+from resihp.planner.pp import peak_in_flight
+from resihp.plan import build_plan
+
+
+@pytest.mark.parametrize("which", sorted(bench.CONFIGS))
+def test_every_bench_layout_plans_as_reported(which):
+    for world, (tp, pp, dp) in bench.CONFIGS[which]["layouts"].items():
+        config = bench.bench_config(which, world, 8)
+        plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+        assert tuple(plan.active_ranks) == tuple(range(world))
+        assert {s.tp_degree for s in plan.stages} == {tp}, (which, world)
+        assert len({s.replica_id for s in plan.stages}) == dp
+        assert len(plan.stages) == pp * dp
+        assert config.sequence_parallel == (tp > 1) and config.dtype == "bf16"
+
+
+def test_parse_defaults_fit_the_timing_rules(monkeypatch):
+    monkeypatch.setattr("sys.argv", ["bench.py"])
+    args = bench.parse()
+    assert args.gpus == 1 and args.warmup >= 3 and args.steps >= 1 and args.impl == "resihp" and args.config == 2
+
+
+def test_clock_summary_filters_gpus_and_names_reasons():
+    sampler = bench.ClockSampler()
+    row = lambda gpu, mhz, cap: [gpu, str(mhz), "1965", "900.0", "0x4", "Not Active", "Not Active", "Not Active", cap]
+    sampler.rows = [row("0", 1800, "Active"), row("0", 1900, "Not Active"), row("0", 1700, "Not Active"),
+                    row("1", 500, "Not Active"), row("0", "[N/A]", "Not Active")]
+    out = sampler.stop({"0"})
+    assert out["sm_mhz"] == 1800.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 4
+    assert bench.ClockSampler().stop({"0"})["reasons"] == ["unsampled"]
+
+
+def test_visible_devices(monkeypatch):
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3,5")
+    assert bench._visible(1, 1) == {"5"} and bench._visible(0, 2) == {"3", "5"}
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench._visible(2, 1) == {"2"} and bench._visible(0, 4) == {"0", "1", "2", "3"}
+
+
+CONFIG = dict(model_dim=32, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=2, tp=2, pp=1, dp=1,
+              iterations=2, arch="llama", vocab_size=32, seq_len=8, ffn_dim=64)
+
+
+def _memory_entry(rank, env, out_dir):
+    os.environ.update(env)
+    import torch
+
+    torch.set_num_threads(1)
+    torch.cuda.max_memory_allocated = lambda device=None: 1000  # the caching allocator's peak on a GPU
+    from resihp.config import TrainConfig
+    from resihp.control import ControlPlane
+    from resihp.recovery import initial_run
+
+    config = TrainConfig(**CONFIG)
+    cp = ControlPlane.initialize(training_backend="gloo")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    groups = cp.build_training_groups(plan)
+    run = initial_run(plan, rank=rank, groups=groups)
+    run.step()
+    used, estimate = bench._memory(run, plan, config, "cpu")
+    write_result(out_dir, rank, {"used": used, "estimate": estimate, "micro": len(run.runtime.micro_batches)})
+    cp.shutdown()
+
+
+@pytest.mark.slow
+def test_memory_report_reads_a_real_run(tmp_path):
+    codes = run_ranks(_memory_entry, 2, str(tmp_path))
+    assert set(codes.values()) == {0}, codes
+    results = read_results(tmp_path, [0, 1])
+    from resihp.config import TrainConfig
+
+    config = TrainConfig(**CONFIG)
+    for r in results.values():
+        want = estimate_memory(config, tp_degree=2, stage_layers=2, micro_batches=r["micro"], sequence_length=8,
+                               vocab_size=32, in_flight_micro_batches=peak_in_flight(r["micro"], stage_index=0,
+                                                                                     num_stages=1)).total
+        assert r["estimate"] == float(want) and r["used"] >= 1000
+    assert json.loads(Path(tmp_path, "result_0.json").read_text())["micro"] == 2
