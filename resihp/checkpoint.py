@@ -274,6 +274,35 @@ def load_anchor(path, *, verify: bool = True) -> tuple[dict[str, dict[str, torch
     return anchor, payload["completed_steps"]
 
 
+def install_anchor(model, optimizer, anchor: dict) -> None:
+    """Load a full logical anchor into a module-form model and its ``torch.optim.AdamW``.
+
+    ``model`` exposes ``logical_state_dict()`` (:class:`resihp.model.ReferenceTransformer`);
+    ``anchor`` is :func:`load_anchor`'s ``{name: {param[, exp_avg, exp_avg_sq, step]}}``.
+    Parameters and moments land on the model's device; the step count stays a CPU
+    tensor, as torch's AdamW keeps it. Names the anchor has moments for replace the
+    optimizer's whole state (reference: ``resihp/checkpoint.py:248-269``).
+    """
+    named = model.logical_state_dict()
+    missing = sorted(set(named) - set(anchor))
+    if missing:
+        raise CheckpointError(f"anchor lacks parameters: {missing}")
+    with torch.no_grad():
+        for name, param in named.items():
+            param.copy_(anchor[name]["param"].to(param.device, param.dtype))
+    optimizer.state.clear()
+    for name, param in named.items():
+        fields = anchor[name]
+        if "exp_avg" not in fields:
+            continue
+        step = fields["step"]
+        optimizer.state[param] = {
+            "step": (step.detach().clone() if torch.is_tensor(step) else torch.tensor(float(step))).to("cpu", torch.float32),
+            "exp_avg": fields["exp_avg"].to(param.device, param.dtype).clone(),
+            "exp_avg_sq": fields["exp_avg_sq"].to(param.device, param.dtype).clone(),
+        }
+
+
 def load_checkpoint(path, config: TrainConfig) -> tuple[dict, int, int]:
     """Validated ``(anchor, completed_steps, plan_version)``; restores the CPU/CUDA RNG."""
     from .models.layout import model_specs

@@ -127,6 +127,46 @@ def reduction_topology(plan) -> ReductionTopology:
 
 
 # ---------------------------------------------------------------------------------------
+def dp_combine_gradients(local: dict, *, group=None) -> dict:
+    """Sum each logical gradient over every replica that holds it; return this rank's
+    slices of the sums (reference: ``resihp/parallel/dp.py:98-151``).
+
+    ``local``: ``{name: {"grad", "shard_dim", "shard_index", "old_size", "replica"}}``
+    for the shards this rank owns. Every rank of ``group`` exchanges its shards as
+    objects; per name each replica's full gradient is rebuilt at that replica's own
+    degree, the replicas are added in ascending replica id (so every rank adds the same
+    terms in the same order), and each rank keeps its slice under its own layout. The
+    general form for small states and tools; training reduces with
+    :class:`GradientReducer`.
+    """
+    from .reshard import reconstruct_full
+    from .tp import local_slice
+
+    mine = {
+        name: {"grad": e["grad"].detach().to("cpu"), "shard_dim": e["shard_dim"], "shard_index": int(e["shard_index"]),
+               "old_size": int(e["old_size"]), "replica": int(e["replica"])}
+        for name, e in local.items()
+    }
+    gathered: list = [None] * dist.get_world_size(group)
+    dist.all_gather_object(gathered, mine, group=group)
+    shards: dict = {}  # name -> replica -> (degree, {index: grad})
+    dims: dict = {}
+    for contribution in gathered:
+        for name, e in contribution.items():
+            dims[name] = e["shard_dim"]
+            degree, held = shards.setdefault(name, {}).setdefault(e["replica"], (e["old_size"], {}))
+            held.setdefault(e["shard_index"], e["grad"])
+    out = {}
+    for name, e in local.items():
+        total = None
+        for replica in sorted(shards[name]):
+            degree, held = shards[name][replica]
+            full, _ = reconstruct_full(name, dims[name], degree, held)
+            total = full.clone() if total is None else total + full
+        out[name] = local_slice(total, e["shard_dim"], int(e["shard_index"]), int(e["old_size"])).to(e["grad"].device)
+    return out
+
+
 # the reducer
 # ---------------------------------------------------------------------------------------
 

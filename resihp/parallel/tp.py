@@ -236,9 +236,10 @@ class TensorParallelStage:
                 p = f"layers.{gid}."
                 for key, first, last in (("qkv", "attn.q_proj.weight", "attn.v_proj.weight"),
                                          ("gate_up", "mlp.gate.weight", "mlp.up.weight")):
-                    w = self.flat.span(self.flat.work, p + first, p + last, d)
                     if self.kernel:
-                        w = w.detach().requires_grad_(True)
+                        w = self.flat.span(self.flat.work, p + first, p + last, d).detach().requires_grad_(True)
+                    else:  # a leaf of its own: autograd accumulates into the grad span set in use_grad
+                        w = nn.Parameter(self.flat.span(self.flat.master, p + first, p + last, d))
                     fused_w[p + key] = w
                     spans.append((p + key, p + first, p + last))
         self._grad_sets = []
@@ -255,6 +256,8 @@ class TensorParallelStage:
         if not self.kernel:
             for name, p in self.w.items():
                 p.grad = self.g[name]
+            for w, g in self.fused_w.values():
+                w.grad = g
 
     def parameters(self):
         return list(self.w.values())

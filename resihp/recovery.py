@@ -40,15 +40,12 @@ from .parallel import peer
 from .models.layout import group_specs, model_specs, stage_specs
 from .parallel.dp import GradientReducer
 from .parallel.pp import PipelineRuntime
+from .parallel.reshard import ReshardError
 from .parallel.tp import TensorParallelStage, local_slice
 from .planner.dp import DPAssignment
 from .reference import digest_tensors, token_stream
 
 FIELDS = ("param", "exp_avg", "exp_avg_sq")
-
-
-class ReshardError(RuntimeError):
-    """State could not be recovered intact (stop code ``state_mismatch``)."""
 
 
 @dataclass

@@ -13,14 +13,39 @@ loss plus SHA-256 digests of the parameters and AdamW state after every step.
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 from hashlib import sha256
 
 import torch
+from torch.nn import functional as F
 
 from .config import TrainConfig
 from .models.init import initial_state
 from .parallel.tp import TensorParallelStage
+
+# AdamW and loss of a run whose config leaves them at their defaults (the reference's
+# module constants, ``resihp/reference.py:20-23``); a config's own fields override them.
+_DEFAULTS = {f.name: f.default for f in dataclasses.fields(TrainConfig)}
+LEARNING_RATE = _DEFAULTS["lr"]
+WEIGHT_DECAY = _DEFAULTS["weight_decay"]
+ADAM_BETAS = (_DEFAULTS["beta1"], _DEFAULTS["beta2"])
+ADAM_EPS = _DEFAULTS["adam_eps"]
+
+
+def adamw(params, config: TrainConfig | None = None) -> torch.optim.AdamW:
+    """``torch.optim.AdamW`` over ``params`` with ``config``'s hyper-parameters (default:
+    the module constants) -- the optimizer a module-form model trains with to match a run.
+    """
+    if config is None:
+        return torch.optim.AdamW(params, lr=LEARNING_RATE, betas=ADAM_BETAS, eps=ADAM_EPS, weight_decay=WEIGHT_DECAY)
+    return torch.optim.AdamW(params, lr=config.lr, betas=(config.beta1, config.beta2), eps=config.adam_eps,
+                             weight_decay=config.weight_decay)
+
+
+def next_token_loss(logits: torch.Tensor, tokens: torch.Tensor, vocab_size: int) -> torch.Tensor:
+    """Mean cross-entropy of ``logits [B, S, V]`` against the next token of ``tokens [B, S]``."""
+    return F.cross_entropy(logits[:, :-1].reshape(-1, vocab_size), tokens[:, 1:].reshape(-1))
 
 
 class TokenStream:
@@ -64,6 +89,12 @@ def digest_tensors(items) -> str:
         h.update(repr(arr.shape).encode("utf-8"))
         h.update(arr.tobytes())
     return h.hexdigest()
+
+
+def logical_state_digest(model) -> str:
+    """SHA-256 of a model's full logical parameters, for anything with
+    ``logical_state_dict()`` (a stage at TP degree 1, a module-form model)."""
+    return digest_tensors(sorted(model.logical_state_dict().items()))
 
 
 @dataclass(frozen=True)

@@ -21,9 +21,13 @@ import os
 import time
 from pathlib import Path
 
-from .config import load_config
+from .config import TrainConfig, load_config
 
 CHECKPOINT_PATH = Path(os.environ.get("RESIHP_CHECKPOINT", "checkpoint.pt"))
+#: Token-stream shape of a config that does not set ``vocab_size`` / ``seq_len`` (the
+#: reference's run constants, ``resihp/train.py:37-38``); a config's fields override them.
+VOCAB_SIZE = TrainConfig.__dataclass_fields__["vocab_size"].default
+SEQUENCE_LENGTH = TrainConfig.__dataclass_fields__["seq_len"].default
 
 
 def parse_args(argv=None):
