@@ -1,4 +1,5 @@
-"""The whole bf16 sm_100a model against the FP32 module-form decoder (one GPU).
+"""The whole bf16 sm_100a model against the FP32 module-form decoder (one GPU; runs last
+in the GPU tier, after the per-kernel tests it builds on).
 
 One full-batch forward + backward of the training stage on ``cuda:0`` -- every kernel
 of the flagship path: embedding, RMSNorm (+residual), fused QKV / gate-up GEMMs, RoPE,
