@@ -76,7 +76,12 @@ class ConsistentStop(RuntimeError):
 class ControlPlane:
     """This rank's place in the world; rebuilds it after a real fail-stop."""
 
-    def __init__(self, rank, members, store, training_backend, *, memory_budget=None, device=None):
+    def __init__(self, rank, members, store, training_backend, *, memory_budget=None, device=None,
+                 vocab_size=None, sequence_length=None):
+        # ``vocab_size`` / ``sequence_length``: the reference passes its run constants
+        # here; the config carries them in this package, and any value given must agree
+        self.vocab_size = vocab_size
+        self.sequence_length = sequence_length
         self.rank = int(rank)
         self.members = tuple(sorted(members))
         self.store = store
@@ -366,6 +371,10 @@ class ControlPlane:
         # the checkpoint file must be complete before the first agreement: every rank
         # may read it during recovery
         self.flush_checkpoint()
+        for name, given, have in (("vocab_size", self.vocab_size, config.vocab_size),
+                                  ("sequence_length", self.sequence_length, config.seq_len)):
+            if given is not None and given != have:
+                raise ValueError(f"{name}={given} does not match the config ({have})")
         failed = tuple(sorted(set(failed_ranks) | set(lost)))
         survivors = tuple(r for r in self.members if r not in set(lost))
         new_plan, reason = None, None

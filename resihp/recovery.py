@@ -135,6 +135,15 @@ class PlannedRun:
         self.batches = token_stream(plan.config, pin=pin and self.device.type == "cuda")
         self.cursor = cursor
 
+    # the reference's run constants, carried by the config here
+    @property
+    def vocab_size(self) -> int:
+        return self.plan.config.vocab_size
+
+    @property
+    def sequence_length(self) -> int:
+        return self.plan.config.seq_len
+
     def step(self):
         loss = self.runtime.train_step(self.batches[self.cursor])
         self.cursor += 1

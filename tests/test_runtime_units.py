@@ -243,3 +243,17 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
         h = torch.zeros(512, 16, dtype=torch.bfloat16)
         ws.gemm_reduce_scatter(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
         assert stub.rs[-1][-1] == variant and stub.rs[-1][7] == ws._part(ws.base, 1)
+
+
+def test_control_plane_run_constants_must_match_the_config():
+    """The reference's ``ControlPlane(vocab_size=, sequence_length=)`` is accepted; a value
+    that disagrees with the config stops the safe point before any collective."""
+    from resihp.control import ControlPlane
+
+    config = TrainConfig(model_dim=16, num_layers=2, num_heads=2, batch_size=2, micro_batch_size=1, seed=1, tp=1,
+                         pp=2, dp=1, iterations=2, vocab_size=32, seq_len=8)
+    plan = build_plan(config, step=0, version=0, vocab_size=32, sequence_length=8)
+    cp = ControlPlane(0, range(2), None, "gloo", vocab_size=64, sequence_length=8)
+    assert (cp.vocab_size, cp.sequence_length) == (64, 8)
+    with pytest.raises(ValueError, match="vocab_size=64 does not match the config"):
+        cp.safe_point(config, plan, (), (1,), next_step=1)
