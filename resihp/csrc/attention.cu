@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(192, 1)
       tma_prefetch(&tm);
       mbar_expect_tx(q_full, L::kQ);
       #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0);
+      for (int c = 0; c < D / 64; ++c) tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0, a.err);
       for (int j = 0; j < nblk; ++j) {
         const int st = j % ST;
         const uint32_t n = j / ST;
@@ -154,12 +154,12 @@ __global__ void __launch_bounds__(192, 1)
         mbar_expect_tx(&k_full[st], L::kKV);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(sk + st * L::kKV + c * kBlk * 128, &tm, &k_full[st], (a.hq + kvh) * D + 64 * c, kv_row);
+          tma_load_2d(sk + st * L::kKV + c * kBlk * 128, &tm, &k_full[st], (a.hq + kvh) * D + 64 * c, kv_row, a.err);
         mbar_expect_tx(&v_full[st], L::kKV);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c)
           tma_load_2d(sv + st * L::kKV + c * kBlk * 128, &tm, &v_full[st], (a.hq + a.hkv + kvh) * D + 64 * c,
-                      kv_row);
+                      kv_row, a.err);
       }
     }
   } else if (warp == 1) {
@@ -394,8 +394,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_expect_tx(kv_full, 2 * L::kT);
       #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_2d(sk + c * kBlk * 128, &tm, kv_full, (a.hq + g) * D + 64 * c, kv_row0);
-        tma_load_2d(sv + c * kBlk * 128, &tm, kv_full, (a.hq + a.hkv + g) * D + 64 * c, kv_row0);
+        tma_load_2d(sk + c * kBlk * 128, &tm, kv_full, (a.hq + g) * D + 64 * c, kv_row0, a.err);
+        tma_load_2d(sv + c * kBlk * 128, &tm, kv_full, (a.hq + a.hkv + g) * D + 64 * c, kv_row0, a.err);
       }
       for (int it = 0; it < steps; ++it) {
         const int h = g * group + it / nq;
@@ -405,8 +405,8 @@ __global__ void __launch_bounds__(192, 1)
         mbar_expect_tx(qd_full, 2 * L::kT);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(sq + c * kBlk * 128, &tm, qd_full, h * D + 64 * c, q_row0);
-          tma_load_2d(sdo + c * kBlk * 128, &tm_do, qd_full, h * D + 64 * c, q_row0);
+          tma_load_2d(sq + c * kBlk * 128, &tm, qd_full, h * D + 64 * c, q_row0, a.err);
+          tma_load_2d(sdo + c * kBlk * 128, &tm_do, qd_full, h * D + 64 * c, q_row0, a.err);
         }
       }
     }
@@ -603,8 +603,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_expect_tx(q_full, 2 * L::kT);
       #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0);
-        tma_load_2d(sdo + c * kBlk * 128, &tm_do, q_full, h * D + 64 * c, row0);
+        tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0, a.err);
+        tma_load_2d(sdo + c * kBlk * 128, &tm_do, q_full, h * D + 64 * c, row0, a.err);
       }
       for (int j = 0; j < nblk; ++j) {
         const int st = j % ST;
@@ -613,8 +613,8 @@ __global__ void __launch_bounds__(192, 1)
         mbar_expect_tx(&kv_full[st], 2 * L::kT);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(sk + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + kvh) * D + 64 * c, kv_row);
-          tma_load_2d(sv + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + a.hkv + kvh) * D + 64 * c, kv_row);
+          tma_load_2d(sk + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + kvh) * D + 64 * c, kv_row, a.err);
+          tma_load_2d(sv + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + a.hkv + kvh) * D + 64 * c, kv_row, a.err);
         }
       }
     }

@@ -42,6 +42,39 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }
 
+// ---- bounds-checked build ---------------------------------------------------------------
+// Compiled with -DRESIHP_BOUNDS_CHECK (the separate library ``_C_checked.so``), the
+// kernels test the addresses they compute before they use them: TMA tile coordinates
+// (innermost coordinate on a 16-byte boundary, no negative coordinate, shared-memory
+// destination on the 1024-byte swizzle boundary), TMEM column ranges against the
+// allocation, offsets into shared-memory tiles against the tile, and element offsets
+// into peer buffers against the buffer. A failed test records kErrBounds in the kernel's
+// error word and the access is skipped; a wait that depended on it runs out its budget
+// and the kernel returns. In the default build every test is a compile-time ``true``.
+#ifdef RESIHP_BOUNDS_CHECK
+constexpr bool kBoundsCheck = true;
+#else
+constexpr bool kBoundsCheck = false;
+#endif
+
+__device__ __forceinline__ bool bounds_ok(bool ok, int* err) {
+  if constexpr (kBoundsCheck) {
+    if (!ok) {
+      record_error(err, kErrBounds);
+      return false;
+    }
+  }
+  return true;
+}
+
+// A ``width``-column TMEM access at ``taddr`` stays inside the ``ncols`` columns
+// allocated at ``base`` (and in lanes 0..127).
+__device__ __forceinline__ bool tmem_span_ok(uint32_t taddr, uint32_t base, uint32_t ncols, uint32_t width,
+                                             int* err) {
+  const uint32_t col = (taddr & 0xFFFFu) - (base & 0xFFFFu);
+  return bounds_ok((taddr >> 16) < 128u && col + width <= ncols, err);
+}
+
 // ---- mbarrier ------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -99,7 +132,10 @@ __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
 
 // 2-D tiled load into this CTA's shared memory; completion is counted on ``bar``.
 // ``x`` is the innermost coordinate; callers keep x * sizeof(elem) a multiple of 16.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+// Every tensor map of this package holds bf16, so the checked build tests x % 8.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            int* err = nullptr) {
+  if (!bounds_ok((x & 7) == 0 && x >= 0 && y >= 0 && (smem_u32(dst) & 1023u) == 0, err)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(dst)),
@@ -107,7 +143,9 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int* err = nullptr) {
+  if (!bounds_ok((x & 7) == 0 && x >= 0 && y >= 0 && z >= 0 && (smem_u32(dst) & 1023u) == 0, err)) return;
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
           smem_u32(dst)),

@@ -112,7 +112,13 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 // (thread index `ct`), `kU` loads in flight per thread.
 template <int kT, int kU>
 __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* src, int64_t sld, int rows,
-                                          int cols16, int ct) {
+                                          int cols16, int ct, int* err) {
+  // checked build: both ends of a 16-byte vector copy on 16-byte boundaries, rows no
+  // wider than their strides
+  if (!bounds_ok(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0 &&
+                     cols16 <= dld && cols16 <= sld,
+                 err))
+    return;
   const int64_t total = int64_t(rows) * cols16;
   for (int64_t base = ct; base < total; base += int64_t(kT) * kU) {
     uint4 r[kU];
@@ -240,14 +246,14 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
           uint8_t* sb = sa + S::kABytes;
           mbar_expect_tx(&full[s], S::kStageBytes);
           const int k0 = kb * kFBK;
-          if (MODE == 1 && own) tma_load_2d(sa, &tma_a, &full[s], k0, m0 - cm.rank * cm.rows_per_rank);
-          else if (MODE == 1) tma_load_2d(sa, &tma_a2, &full[s], k0, m0);
-          else tma_load_2d(sa, &tma_a, &full[s], k0, m0);
+          if (MODE == 1 && own) tma_load_2d(sa, &tma_a, &full[s], k0, m0 - cm.rank * cm.rows_per_rank, g.err);
+          else if (MODE == 1) tma_load_2d(sa, &tma_a2, &full[s], k0, m0, g.err);
+          else tma_load_2d(sa, &tma_a, &full[s], k0, m0, g.err);
           if (B_MN) {
             #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tma_b, &full[s], n0 + 64 * c, k0);
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tma_b, &full[s], n0 + 64 * c, k0, g.err);
           } else {
-            tma_load_2d(sb, &tma_b, &full[s], k0, n0);
+            tma_load_2d(sb, &tma_b, &full[s], k0, n0, g.err);
           }
           if (++s == kStages) { s = 0; ph ^= 1; }
         }
@@ -267,6 +273,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
         if (!mbar_wait(&acc_empty[a], accph ^ 1, g.err, kErrMmaWait)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * BN;
+        if (!tmem_span_ok(d, tmem_base, 2 * BN, BN, g.err)) break;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&full[s], ph, g.err, kErrMmaWait)) { ok = false; break; }
           tc_fence_after();
@@ -312,7 +319,9 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
       #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t v[32];
-        tmem_ld32(tmem_base + a * BN + cc * 32 + (uint32_t(q * 32) << 16), v);
+        const uint32_t ta = tmem_base + a * BN + cc * 32 + (uint32_t(q * 32) << 16);
+        if (!tmem_span_ok(ta, tmem_base, 2 * BN, 32, g.err)) continue;
+        tmem_ld32(ta, v);
         tmem_wait_ld();
         const int col0 = tn * BN + cc * 32;
         if (!ok || col0 >= g.n) continue;
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
           copy_rows<kCT, kCU>(
               reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx), cols16,
               reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(lo) * cm.ldx), cols16, hi - lo, cols16,
-              ct);
+              ct, g.err);
           fence_proxy_async_global();
           __threadfence();
           __syncwarp();
@@ -431,7 +440,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
           }
           copy_rows<kCT, kCU>(
               reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + r0) * cm.ldx), cols16,
-              reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(r0) * cm.ldx), cols16, srows, cols16, ct);
+              reinterpret_cast<const uint4*>(cm.peer_slot[chunk] + int64_t(r0) * cm.ldx), cols16, srows, cols16, ct, g.err);
           fence_proxy_async_global();
           __threadfence();
           __syncwarp();
@@ -455,7 +464,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
             if (!ok) break;
             const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[src] + int64_t(m0) * g.n + tn * BN);
             uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(src) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
-            copy_rows<kCT, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, ct);
+            copy_rows<kCT, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, ct, g.err);
           }
         } else {
           // this warp's peers (every kCW-th peer), copied in the order their tiles arrive
@@ -482,7 +491,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
             if (got < 0) continue;
             const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[got] + int64_t(m0) * g.n + tn * BN);
             uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(got) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
-            copy_rows<32, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, lane);
+            copy_rows<32, kCU>(to, g.n / 8, from, g.n / 8, kFBM, ncols16, lane, g.err);
             pending &= ~(1u << got);
           }
         }

@@ -126,16 +126,16 @@ __global__ void __launch_bounds__(192, 1)
           mbar_expect_tx(&full[s], S::kStageBytes);
           const int k0 = kb * kBK;
           if (A_MN) {
-            tma_load_2d(sa, &tma_a, &full[s], m0, k0);
-            tma_load_2d(sa + 8192, &tma_a, &full[s], m0 + 64, k0);
+            tma_load_2d(sa, &tma_a, &full[s], m0, k0, g.err);
+            tma_load_2d(sa + 8192, &tma_a, &full[s], m0 + 64, k0, g.err);
           } else {
-            tma_load_2d(sa, &tma_a, &full[s], k0, m0);
+            tma_load_2d(sa, &tma_a, &full[s], k0, m0, g.err);
           }
           if (B_MN) {
             #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tma_b, &full[s], n0 + 64 * c, k0);
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tma_b, &full[s], n0 + 64 * c, k0, g.err);
           } else {
-            tma_load_2d(sb, &tma_b, &full[s], k0, n0);
+            tma_load_2d(sb, &tma_b, &full[s], k0, n0, g.err);
           }
           if (++s == kStages) { s = 0; ph ^= 1; }
         }
@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&acc_empty[a], accph ^ 1, g.err, kErrMmaWait)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * BN;
+        if (!tmem_span_ok(d, tmem_base, S::kTmemCols, BN, g.err)) break;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&full[s], ph, g.err, kErrMmaWait)) { ok = false; break; }
           tc_fence_after();
@@ -188,7 +189,9 @@ __global__ void __launch_bounds__(192, 1)
       #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem_base + a * BN + c * 32 + (uint32_t(q * 32) << 16), v);
+        const uint32_t ta = tmem_base + a * BN + c * 32 + (uint32_t(q * 32) << 16);
+        if (!tmem_span_ok(ta, tmem_base, S::kTmemCols, 32, g.err)) continue;
+        tmem_ld32(ta, v);
         tmem_wait_ld();
         const int col0 = tn * BN + c * 32;
         if (!row_ok || col0 >= g.n) continue;

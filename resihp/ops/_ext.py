@@ -12,7 +12,10 @@ import importlib.util
 import os
 
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-_LIB = os.path.join(_PKG, "_C.so")
+#: ``RESIHP_CHECKED=1`` loads the bounds-checked build of the same kernels instead.
+CHECKED = os.environ.get("RESIHP_CHECKED", "0") == "1"
+_NAME = "_C_checked" if CHECKED else "_C"
+_LIB = os.path.join(_PKG, _NAME + ".so")
 _module = None
 _error: Exception | None = None
 
@@ -24,9 +27,10 @@ def _load():
     try:
         import torch  # noqa: F401  (libtorch must be loaded before the extension)
 
-        spec = importlib.util.spec_from_file_location("resihp._C", _LIB)
+        spec = importlib.util.spec_from_file_location("resihp." + _NAME, _LIB)
         if spec is None or not os.path.exists(_LIB):
-            raise ImportError(f"extension not built: {_LIB} (run python -m resihp.ops.build)")
+            raise ImportError(f"extension not built: {_LIB} (run python -m resihp.ops.build"
+                              f"{' --checked' if CHECKED else ''})")
         module = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(module)
         _module = module
