@@ -9,6 +9,8 @@ Llama blocks with GQA, and tied embeddings; plus the reference-API helpers
 (``next_token_loss``, ``logical_state_digest``, ``install_anchor``).
 """
 
+import math
+
 import pytest
 import torch
 
@@ -117,3 +119,21 @@ def test_reference_signature_and_constants():
     opt = adamw(model.parameters())
     group = opt.param_groups[0]
     assert group["lr"] == LEARNING_RATE and group["betas"] == ADAM_BETAS
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_parameter_counts_agree_with_the_memory_model(case):
+    """The module, the layout table and the memory model count the same parameters
+    (reference: ``tests/test_reference.py:110``, parameter count = memory model)."""
+    from resihp.memory import layer_parameter_count
+    from resihp.models.layout import layer_specs, parameter_count
+
+    config = TrainConfig(**CASES[case])
+    model = ReferenceTransformer(config)
+    assert parameter_count(config) == sum(p.numel() for p in model.parameters())
+    sharded, replicated = layer_parameter_count(config)
+    block = sum(p.numel() for p in model.layers["0"].parameters())
+    assert block == sharded + replicated == sum(math.prod(s.shape) for s in layer_specs(config, 0))
+    if config.arch == "gpt2":
+        d = config.model_dim
+        assert block == 12 * d * d + 4 * d  # the reference's per-layer figure (FFN = 4d)
