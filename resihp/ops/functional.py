@@ -3,8 +3,9 @@
 CUDA tensors (bf16) run the sm_100a kernels; weight gradients are accumulated straight
 into FP32 *main-grad* buffers passed alongside each weight (gradient-accumulation
 fusion), so the bf16 weights never hold a ``.grad`` and micro-batches accumulate
-without extra passes. CPU tensors run the same math as plain FP32 torch expressions
-and let autograd fill ``param.grad`` -- the reference-semantics path.
+without extra passes. FP32 tensors (CPU, or CUDA for a reference-semantics run on a
+GPU) run the same math as plain torch expressions and let autograd fill
+``param.grad``.
 
 Conventions: activations are 2-D ``[tokens, features]``; token ``t`` of a micro-batch
 is sequence ``t // S`` position ``t % S``.
@@ -32,6 +33,12 @@ def _k():
     return _ext.require()
 
 
+def on_kernels(t: torch.Tensor) -> bool:
+    """bf16 CUDA tensors run the sm_100a kernels; FP32 tensors (CPU or CUDA) take the
+    plain-torch FP32 reference path."""
+    return t.is_cuda and t.dtype == torch.bfloat16
+
+
 # ---------------------------------------------------------------------------------------
 # linear
 # ---------------------------------------------------------------------------------------
@@ -57,7 +64,7 @@ class _Linear(Function):
 
 def linear(x, w, main_grad=None, residual=None):
     """``x @ w.T`` (+ residual). CUDA: tcgen05 GEMM, wgrad accumulated into ``main_grad``."""
-    if not x.is_cuda:
+    if not on_kernels(x):
         y = F.linear(x, w)
         return y if residual is None else y + residual
     return _Linear.apply(x, w, main_grad, residual)
@@ -88,7 +95,7 @@ class _RMSNorm(Function):
 
 def rmsnorm(x, w, eps, main_grad=None, residual=None):
     """``(rmsnorm(x + residual) * w, x + residual)``; without a residual the second output is ``x``."""
-    if not x.is_cuda:
+    if not on_kernels(x):
         s = x if residual is None else x + residual
         rstd = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)
         return s * rstd * w, s
@@ -151,7 +158,7 @@ def rope_attention(qkv, cs, seq, hq, hkv, d):
     CUDA: RoPE is applied to ``qkv`` in place (the projection output is consumed, not
     copied), so callers must not read ``qkv`` afterwards expecting un-rotated values.
     """
-    if qkv.is_cuda:
+    if on_kernels(qkv):
         return _RopeAttention.apply(qkv, cs, seq, hq, hkv, d)
     t = qkv.shape[0]
     b = t // seq
@@ -197,7 +204,7 @@ class _SwiGLU(Function):
 
 def swiglu(gu):
     """``silu(g) * u`` over the fused ``[g | u]`` projection."""
-    if gu.is_cuda:
+    if on_kernels(gu):
         return _SwiGLU.apply(gu)
     g, u = gu.chunk(2, dim=-1)
     return F.silu(g) * u
@@ -227,7 +234,7 @@ class _Embedding(Function):
 
 def embedding(ids, w, main_grad=None, start=0):
     """Rows ``ids - start`` of this rank's vocab shard ``w``; ids outside it give zeros."""
-    if w.is_cuda:
+    if on_kernels(w):
         return _Embedding.apply(ids, w, main_grad, start)
     flat = ids.reshape(-1)
     local = flat - start
@@ -278,7 +285,7 @@ def vocab_parallel_cross_entropy(logits, labels, start=0, group=None, scale=1.0)
     CUDA: the logits buffer is consumed (it is overwritten by its own gradient in
     backward), so callers must not reuse it.
     """
-    if logits.is_cuda:
+    if on_kernels(logits):
         return _VocabParallelXent.apply(logits, labels.contiguous(), start, group, scale)
     lg = logits.float()
     tp = 1 if group is None else dist.get_world_size(group)
@@ -328,10 +335,12 @@ class _TorchVocabParallelXent(Function):
 def adamw_flat(p, g, m, v, step, *, lr, beta1, beta2, eps, weight_decay, p_bf16=None, grad_scale=1.0):
     """One AdamW step over flat FP32 buffers (torch.optim.AdamW's formulation).
 
-    CPU: the exact torch single-tensor op sequence, so results equal ``torch.optim.AdamW``
-    bit for bit. CUDA: one fused kernel that also refreshes the bf16 working copy.
+    FP32 path (no bf16 copy; CPU or CUDA): the exact torch single-tensor op sequence, so
+    results equal ``torch.optim.AdamW``'s single-tensor implementation bit for bit. bf16
+    training path (CUDA, ``p_bf16`` given): one fused kernel that also refreshes the bf16
+    working copy.
     """
-    if p.is_cuda:
+    if p.is_cuda and p_bf16 is not None:  # the bf16 training path: one fused kernel
         _k().adamw(p, g, m, v, p_bf16, lr, beta1, beta2, eps, weight_decay, int(step), grad_scale)
         return
     grad = g if grad_scale == 1.0 else g * grad_scale

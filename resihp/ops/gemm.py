@@ -4,8 +4,8 @@ All three products of a bias-free linear layer ``y = x w^T`` read their operands
 place (no transposes): the kernel takes each operand K-major or MN-major. (Reference:
 ``F.linear`` at ``resihp/parallel/tp.py:235-248,272`` and its autograd products.)
 
-On CPU tensors the same functions compute in plain torch, which is the FP32 reference
-path; CUDA tensors must be bf16 and always run the hand-written kernel.
+bf16 CUDA tensors always run the hand-written kernel; FP32 tensors (CPU or CUDA)
+compute in plain torch, the FP32 reference path.
 """
 
 from __future__ import annotations
@@ -21,7 +21,7 @@ EPI_ADD_BF16 = 3
 
 
 def _cuda(*tensors) -> bool:
-    return tensors[0].is_cuda
+    return tensors[0].is_cuda and tensors[0].dtype == torch.bfloat16
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:

@@ -52,3 +52,17 @@ def test_bf16_model_gradients_match_the_fp32_module(extra):
         cos = torch.nn.functional.cosine_similarity(g.flatten(), ref.flatten(), dim=0).item()
         rel = ((g - ref).norm() / ref.norm().clamp_min(1e-20)).item()
         assert cos >= 0.99 and rel <= 0.1, (name, cos, rel)
+
+
+@pytest.mark.parametrize("arch", ["gpt2", "llama"])
+def test_fp32_reference_runs_on_cuda_like_on_cpu(arch):
+    """A reference-style FP32 config on a GPU takes the plain-torch FP32 path (the
+    kernels are bf16-only) and trains like the CPU oracle (reference:
+    ``tests/test_reference.py:126``, CPU vs CUDA FP32)."""
+    extra = dict(ffn_dim=512, num_heads=2, init_std=0.05) if arch == "llama" else dict(num_heads=4)
+    config = TrainConfig(**dict(SHAPE, **extra, arch=arch, seq_len=64, vocab_size=256, iterations=3))
+    cpu, gpu = ReferenceRun(config), ReferenceRun(config, device="cuda:0")
+    assert not gpu.stage.kernel
+    for _ in range(3):
+        a, b = cpu.step(), gpu.step()
+        assert abs(a.loss - b.loss) <= 1e-4 * abs(a.loss), (a.loss, b.loss)
