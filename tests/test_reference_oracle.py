@@ -6,10 +6,12 @@
   framework's oracle -- which runs the distributed stage code at TP degree 1 -- trains
   like the reference's ``ReferenceTransformer`` + ``torch.optim.AdamW``: same losses to
   reassociation precision, parameters within AdamW's conditioning;
-* two oracle runs are bit-identical (loss and state digests).
+* two oracle runs are bit-identical (loss and state digests);
+* the module-form GPT-2 decoder (``resihp.model``) has the reference model's parameter
+  names in the same order, its initial weights bit for bit, and its logits.
 
 The reference is imported from ``baseline/_ref`` in a subprocess (both packages are
-named ``resihp``); those two tests skip when it is not installed.
+named ``resihp``); those tests skip when it is not installed.
 """
 
 import json
@@ -79,3 +81,27 @@ def test_oracle_is_repeatable():
     for _ in range(3):
         ra, rb = a.step(), b.step()
         assert ra.loss == rb.loss and ra.param_digest == rb.param_digest and ra.optim_digest == rb.optim_digest
+
+
+@needs_ref
+def test_module_form_gpt2_equals_the_reference_transformer():
+    """``resihp.model.ReferenceTransformer`` (GPT-2 blocks) built for the reference's
+    config has the reference model's parameter names, the same initial weights bit for
+    bit, and the same logits to FP32 rounding."""
+    from resihp.model import ReferenceTransformer
+
+    theirs = _in_reference(
+        "import json, torch\nfrom resihp.config import TrainConfig\nfrom resihp.model import ReferenceTransformer\n"
+        f"torch.manual_seed({SHAPE['seed']})\n"
+        f"m = ReferenceTransformer(TrainConfig(**{SHAPE!r}), vocab_size={VOCAB}, sequence_length={SEQ})\n"
+        f"tokens = torch.randint(0, {VOCAB}, (2, {SEQ}), generator=torch.Generator().manual_seed(5))\n"
+        "print(json.dumps({'state': {k: v.tolist() for k, v in m.logical_state_dict().items()},\n"
+        "                  'logits': m(tokens).tolist()}))\n"
+    )
+    ours = ReferenceTransformer(TrainConfig(**SHAPE, vocab_size=VOCAB, seq_len=SEQ))
+    state = ours.logical_state_dict()
+    assert list(state) == list(theirs["state"])
+    for name, values in theirs["state"].items():
+        assert torch.equal(state[name].detach(), torch.tensor(values)), name
+    tokens = torch.randint(0, VOCAB, (2, SEQ), generator=torch.Generator().manual_seed(5))
+    torch.testing.assert_close(ours(tokens).detach(), torch.tensor(theirs["logits"]), rtol=1e-5, atol=1e-5)
