@@ -30,9 +30,18 @@ namespace resihp {
 enum GemmEpilogue : int {
   kEpiStoreBf16 = 0,   // C(bf16) = alpha * acc
   kEpiStoreF32 = 1,    // C(f32)  = alpha * acc
-  kEpiAccumF32 = 2,    // C(f32) += alpha * acc
+  kEpiAccumF32 = 2,    // C(f32) += alpha * acc   (load, add, store)
   kEpiAddBf16 = 3,     // C(bf16) = alpha * acc + R(bf16)
+  kEpiRedF32 = 4,      // C(f32) += alpha * acc   (red.global.add: no load latency in the epilogue)
 };
+
+// Fire-and-forget C[0..3] += v in L2. Every element of C is added to by exactly one
+// thread of one CTA per launch, so the sum is the same single fp32 addition the
+// load-add-store epilogue performs (atomic f32 adds flush subnormals to zero).
+__device__ __forceinline__ void red_add_v4(float* p, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
 
 struct GemmArgs {
   void* c;
@@ -225,6 +234,10 @@ __global__ void __launch_bounds__(192, 1)
             if (col0 + 4 * j >= g.n) break;
             float4 o = make_float4(g.alpha * __uint_as_float(v[4 * j]), g.alpha * __uint_as_float(v[4 * j + 1]),
                                    g.alpha * __uint_as_float(v[4 * j + 2]), g.alpha * __uint_as_float(v[4 * j + 3]));
+            if (EPI == kEpiRedF32) {
+              red_add_v4(out + 4 * j, o);
+              continue;
+            }
             if (EPI == kEpiAccumF32) {
               float4 p = *reinterpret_cast<const float4*>(out + 4 * j);
               o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
@@ -315,7 +328,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
 // The operand-major / epilogue combinations the linear layers use:
 //   forward  (K,K)   store bf16 or add residual
 //   dgrad    (K,MN)  store bf16 or fp32
-//   wgrad    (MN,MN) store or accumulate fp32
+//   wgrad    (MN,MN) store or accumulate fp32 (load-add-store or red.global.add)
 template <int BN>
 static void dispatch(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g,
                      cudaStream_t st, int max_ctas) {
@@ -326,6 +339,7 @@ static void dispatch(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, const
   if (!a_mn && b_mn && epi == kEpiStoreF32) return launch_gemm<BN, false, true, kEpiStoreF32>(ta, tb, g, st, max_ctas);
   if (a_mn && b_mn && epi == kEpiStoreF32) return launch_gemm<BN, true, true, kEpiStoreF32>(ta, tb, g, st, max_ctas);
   if (a_mn && b_mn && epi == kEpiAccumF32) return launch_gemm<BN, true, true, kEpiAccumF32>(ta, tb, g, st, max_ctas);
+  if (a_mn && b_mn && epi == kEpiRedF32) return launch_gemm<BN, true, true, kEpiRedF32>(ta, tb, g, st, max_ctas);
   if (a_mn && b_mn && epi == kEpiStoreBf16) return launch_gemm<BN, true, true, kEpiStoreBf16>(ta, tb, g, st, max_ctas);
   RESIHP_CHECK(false, "unsupported GEMM combination a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
 }

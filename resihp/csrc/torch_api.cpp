@@ -70,7 +70,8 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
   const int64_t kb = b_mn ? b.size(0) : b.size(1);
   TORCH_CHECK(k == kb, "GEMM reduction sizes differ: ", k, " vs ", kb);
   TORCH_CHECK(c.size(0) == m && c.size(1) == n, "GEMM output shape mismatch");
-  const bool want_f32 = epi == 1 || epi == 2;
+  TORCH_CHECK(epi >= 0 && epi <= 4, "unknown GEMM epilogue ", epi);
+  const bool want_f32 = epi == 1 || epi == 2 || epi == 4;
   TORCH_CHECK(c.scalar_type() == (want_f32 ? at::kFloat : at::kBFloat16), "GEMM output dtype does not match epilogue");
   const void* r = nullptr;
   int64_t ldr = 0;

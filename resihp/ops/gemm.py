@@ -10,6 +10,8 @@ compute in plain torch, the FP32 reference path.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _ext
@@ -18,6 +20,11 @@ EPI_BF16 = 0
 EPI_F32 = 1
 EPI_ACC_F32 = 2
 EPI_ADD_BF16 = 3
+EPI_RED_F32 = 4
+
+#: Weight-gradient accumulation through ``red.global.add`` (no load in the epilogue)
+#: instead of load-add-store; same sums except that subnormals flush to zero.
+WGRAD_RED = os.environ.get("RESIHP_WGRAD_RED", "0") == "1"
 
 
 def _cuda(*tensors) -> bool:
@@ -72,7 +79,8 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = N
     if out is None:
         out = torch.empty((d2.shape[1], x2.shape[1]), dtype=torch.float32, device=dy.device)
         accumulate = False
-    _ext.require().gemm(d2, True, x2, True, out, EPI_ACC_F32 if accumulate else EPI_F32)
+    _ext.require().gemm(d2, True, x2, True, out, ((EPI_RED_F32 if WGRAD_RED else EPI_ACC_F32) if accumulate
+                                                 else EPI_F32))
     return out
 
 

@@ -59,7 +59,8 @@ def _time_us(fn_, it: int = 20, warm: int = 5) -> float:
 
 
 def gemm_time() -> None:
-    """TF/s of the three linear-layer products and of ``torch.matmul`` on the 1.3B shapes."""
+    """TF/s of the three linear-layer products (the weight gradient accumulated by
+    load-add-store and by ``red.global.add``) and of ``torch.matmul`` on the 1.3B shapes."""
     import json
 
     out = []
@@ -70,8 +71,10 @@ def gemm_time() -> None:
         acc = torch.zeros(n, k, device="cuda")
         flop = 2.0 * m * n * k
         row = {"m": m, "n": n, "k": k}
+        k_ = ops._ext.require()
         for name, fn_ in (("forward", lambda: ops.linear(x, w)), ("dgrad", lambda: ops.linear_dgrad(dy, w)),
-                          ("wgrad", lambda: ops.linear_wgrad(dy, x, out=acc, accumulate=True)),
+                          ("wgrad", lambda: k_.gemm(dy, True, x, True, acc, 2)),
+                          ("wgrad_red", lambda: k_.gemm(dy, True, x, True, acc, 4)),
                           ("cublas_forward", lambda: torch.matmul(x, w.t()))):
             row[name + "_tflops"] = round(flop / _time_us(fn_) / 1e6, 1)
         out.append(row)
