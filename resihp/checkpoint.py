@@ -12,7 +12,7 @@ either implementation reads the other's files)::
 
 ``identity`` holds the reference's fields for GPT-2 blocks and adds the Llama shape
 fields otherwise; topology (TP/PP/DP, micro-batch size) is deliberately absent.
-Writes go to ``<path>.tmp``, are read back and digest-checked, then ``os.replace``-d
+Writes go to ``<path>.tmp``, are read back and compared with memory, then ``os.replace``-d
 over the single canonical path; any failure removes the temp file and leaves the last
 valid checkpoint untouched. Every problem a load can find is reported as its own
 :class:`CheckpointError` (missing file, unreadable payload, format, identity, names,
@@ -120,6 +120,20 @@ def _torch_load(path: Path, mmap: bool = False) -> dict:
     return torch.load(path, weights_only=False, mmap=mmap)
 
 
+def _same(a, b) -> bool:
+    """Structural equality with tensors compared byte for byte (NaN payloads included)."""
+    if torch.is_tensor(a):
+        if not (torch.is_tensor(b) and a.dtype == b.dtype and a.shape == b.shape):
+            return False
+        return torch.equal(a.detach().contiguous().view(-1).view(torch.uint8),
+                           b.detach().contiguous().view(-1).view(torch.uint8))
+    if isinstance(a, dict):
+        return isinstance(b, dict) and a.keys() == b.keys() and all(_same(a[k], b[k]) for k in a)
+    if isinstance(a, (list, tuple)):
+        return type(a) is type(b) and len(a) == len(b) and all(_same(x, y) for x, y in zip(a, b))
+    return type(a) is type(b) and a == b
+
+
 def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int = 0,
                     rng: tuple | None = None) -> Path:
     """Atomically write the logical checkpoint; returns the canonical path."""
@@ -131,7 +145,9 @@ def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: i
     tmp = path.with_name(path.name + ".tmp")
     try:
         torch.save(payload, tmp)
-        if payload_digest(_torch_load(tmp)) != payload["digest"]:
+        # read back and compare every field byte for byte with what was written (the
+        # digest stored in it included): as strong as re-hashing, without a second SHA-256
+        if not _same(_torch_load(tmp), payload):
             raise CheckpointError("checkpoint write verification failed: temp file differs from memory")
         os.replace(tmp, path)
     except BaseException:

@@ -49,6 +49,35 @@ def test_failed_replace_keeps_previous(tmp_path, monkeypatch):
     assert not (tmp_path / "ck.pt.tmp").exists()
 
 
+def test_write_verification_catches_a_changed_byte_and_accepts_nan(tmp_path, monkeypatch):
+    """The temp file is read back and compared with memory byte for byte: one flipped
+    value aborts the write and keeps the previous file; NaNs (a diverged run) are kept
+    as written and compare equal to themselves."""
+    from resihp import checkpoint as ck
+
+    path, run = _saved(tmp_path)
+    before = path.read_bytes()
+    real_load = ck._torch_load
+
+    def flipped(p, mmap=False):
+        payload = real_load(p, mmap)
+        t = payload["params"]["lm_head.weight"]
+        t.view(-1)[7] = t.view(-1)[7] + 1.0
+        return payload
+
+    monkeypatch.setattr(ck, "_torch_load", flipped)
+    with pytest.raises(CheckpointError, match="write verification failed"):
+        save_checkpoint(path, C, run.full_state(), completed_steps=5, plan_version=3)
+    assert path.read_bytes() == before and not (tmp_path / "ck.pt.tmp").exists()
+    monkeypatch.setattr(ck, "_torch_load", real_load)
+
+    full = run.full_state()
+    full["lm_head.weight"]["param"].view(-1)[3] = float("nan")
+    save_checkpoint(path, C, full, completed_steps=1, plan_version=3)
+    anchor, _ = load_anchor(path)
+    assert torch.isnan(anchor["lm_head.weight"]["param"].view(-1)[3])
+
+
 def test_each_corruption_is_its_own_root_cause(tmp_path):
     path, _ = _saved(tmp_path)
     payload = torch.load(path, weights_only=False)
