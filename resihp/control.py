@@ -265,7 +265,7 @@ class ControlPlane:
             handle = self._new_group(hop)
             if self.rank in hop:
                 g.hops[hop] = handle
-        executors = self._new_group(plan.active_ranks)
+        executors = self._world_or_new_group(plan.active_ranks)
         g.executor = executors if self.is_training_rank(plan) else None
         topo = reduction_topology(plan)
         for members in topo.tied_groups + topo.dp_groups:
@@ -273,9 +273,26 @@ class ControlPlane:
             if self.rank in members:
                 g.reduce[members] = handle
         if self._needs_live_group(plan):
-            g.live = self._new_group(self.members)
+            g.live = self._world_or_new_group(self.members)
         self.groups = g
         return g
+
+    def _world_carries_training(self) -> bool:
+        """The world group can run the training collectives itself: it is Gloo and so is
+        training, or it carries the device-bound NCCL communicator."""
+        import torch
+
+        if self.training_backend == "gloo":
+            return True
+        return (NCCL_SPLIT and self.training_backend == "nccl" and self.device is not None
+                and torch.device(self.device).type == "cuda")
+
+    def _world_or_new_group(self, plan_ranks):
+        """The world group itself when ``plan_ranks`` are all its members (one communicator
+        fewer to create at a safe point), else a new group. Every rank decides alike."""
+        if tuple(sorted(plan_ranks)) == self.members and self._world_carries_training():
+            return self.world_group
+        return self._new_group(plan_ranks)
 
     def _build_training_groups_batched(self, plan: ExecutionPlan) -> TrainingGroups:
         """The same groups as :meth:`build_training_groups`, split family by family."""
@@ -284,12 +301,15 @@ class ControlPlane:
         tp = self._split_family([tuple(s.tp_members) for s in stages if len(s.tp_members) > 1])
         g.tp = next(iter(tp.values()), None)
         g.hops = self._split_family(list(boundary_hops(plan)))
-        executors = self._split_family([tuple(plan.active_ranks)])
+        if tuple(sorted(plan.active_ranks)) == self.members:
+            executors = {tuple(plan.active_ranks): self.world_group}
+        else:
+            executors = self._split_family([tuple(plan.active_ranks)])
         g.executor = executors.get(tuple(plan.active_ranks)) if self.is_training_rank(plan) else None
         topo = reduction_topology(plan)
         g.reduce = self._split_family(list(topo.tied_groups + topo.dp_groups))
         if self._needs_live_group(plan):
-            g.live = self._split_family([tuple(self.members)]).get(tuple(self.members))
+            g.live = self.world_group
         self.groups = g
         return g
 
@@ -305,7 +325,7 @@ class ControlPlane:
 
         g = self.groups
         handles = [g.tp, *g.hops.values(), g.executor, *g.reduce.values(), g.live]
-        seen = set()
+        seen = {id(self.world_group)}  # a training group may be the world itself: dissolve_world ends it
         for h in handles:
             if h is not None and id(h) not in seen:
                 seen.add(id(h))
