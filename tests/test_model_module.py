@@ -28,6 +28,7 @@ CASES = {
     "gpt2": dict(BASE, arch="gpt2"),
     "llama-gqa": dict(BASE, arch="llama", num_kv_heads=2, ffn_dim=48, init_std=0.1),
     "llama-tied": dict(BASE, arch="llama", ffn_dim=48, tied_embeddings=True, init_std=0.1, rope_theta=500.0),
+    "llama-recompute": dict(BASE, arch="llama", num_kv_heads=1, ffn_dim=40, init_std=0.1, recompute=True),
 }
 
 
