@@ -275,6 +275,11 @@ def validate(payload: dict, config: TrainConfig, expected_shapes: dict[str, tupl
     verify_digest(payload)
 
 
+def completed_steps(path) -> int:
+    """The iterations a checkpoint has completed, read without loading its tensors."""
+    return int(read_payload(path, mmap=True)["completed_steps"])
+
+
 def load_anchor(path, *, verify: bool = True) -> tuple[dict[str, dict[str, torch.Tensor]], int]:
     """``({name: {param[, exp_avg, exp_avg_sq, step]}}, completed_steps)`` from a checkpoint."""
     payload = read_payload(path)

@@ -34,6 +34,8 @@ def parse_args(argv=None):
     p = argparse.ArgumentParser(description="resihp training worker")
     p.add_argument("--config", required=True, type=Path)
     p.add_argument("--failures", required=True, type=Path)
+    p.add_argument("--resume", type=Path, default=None,
+                   help="restart a stopped job from this checkpoint (any TP/PP/DP layout)")
     return p.parse_args(argv)
 
 
@@ -68,9 +70,32 @@ def _emit(obj) -> None:
     sys.stdout.flush()
 
 
-def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
+def _resumed_run(path: Path, config, plan, *, rank, groups, device):
+    """``(run, completed steps)`` rebuilt from a checkpoint under ``plan``.
+
+    The checkpoint is topology-free, so the restarted job may run another layout; the
+    installed shards are checked against the checkpoint (principle A1) before training.
+    """
+    from .checkpoint import CheckpointError, load_checkpoint
+    from .recovery import checkpoint_mismatches, run_from_anchor
+
+    anchor, completed, _version = load_checkpoint(path, config)  # validated; restores the RNG
+    if completed >= config.iterations:
+        raise CheckpointError(f"checkpoint {path} already holds {completed} of {config.iterations} iterations")
+    run = run_from_anchor(plan, rank=rank, anchor=anchor, completed=completed, groups=groups, device=device)
+    problems = [] if run is None else checkpoint_mismatches(run, plan=plan, rank=rank, anchor=anchor)
+    if problems:
+        raise CheckpointError(f"rank {rank} state differs from {path} after the restart: {problems[:5]}")
+    return run, completed
+
+
+def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH, resume: Path | None = None):
+    """One rank's whole job. ``resume`` restarts it from a checkpoint: training continues
+    after the checkpoint's completed iterations, and failure events at or before them are
+    in the past."""
     import torch
 
+    from .checkpoint import completed_steps
     from .control import ConsistentStop, ControlPlane
     from .plan import build_plan
     from .recovery import initial_run
@@ -79,13 +104,18 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
     schedule = {e.after_iteration: e.failed_rank for e in loaded.failures}
     device = select_device()
     control = ControlPlane.initialize(memory_budget=config.memory_budget_bytes, device=device)
+    start = 0 if resume is None else completed_steps(resume)
     plan = build_plan(
-        config, step=0, version=0, memory_budget=config.memory_budget_bytes,
+        config, step=start, version=0, memory_budget=config.memory_budget_bytes,
         vocab_size=config.vocab_size, sequence_length=config.seq_len,
     )
     groups = control.build_training_groups(plan)
-    control.attach_run(initial_run(plan, rank=control.rank, groups=groups, device=device),
-                       checkpoint_path=checkpoint_path, device=device)
+    if resume is None:
+        run = initial_run(plan, rank=control.rank, groups=groups, device=device)
+    else:
+        run, start = _resumed_run(resume, config, plan, rank=control.rank, groups=groups, device=device)
+        _emit({"resume": {"rank": control.rank, "checkpoint": str(resume), "completed_steps": start}})
+    control.attach_run(run, checkpoint_path=checkpoint_path, device=device)
     failed: tuple[int, ...] = ()
     pending_recovery = None
     trained: list[int] = []
@@ -93,7 +123,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
     digests = [plan.digest]
     tokens_per_step = config.batch_size * config.seq_len
     try:
-        iteration = 0
+        iteration = start
         while iteration < config.iterations:
             iteration += 1
             if control.training_run is not None:
@@ -155,7 +185,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH):
 def main(argv=None):
     args = parse_args(argv)
     if "RANK" in os.environ:
-        run_distributed(load_config(args.config, args.failures))
+        run_distributed(load_config(args.config, args.failures), resume=args.resume)
         return
     config = json.loads(args.config.read_text(encoding="utf-8"))
     failures = json.loads(args.failures.read_text(encoding="utf-8"))
