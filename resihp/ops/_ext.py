@@ -1,9 +1,9 @@
 """Loader for the in-tree sm_100a extension ``resihp/_C.so``.
 
-The CUDA path has no fallback: on a machine with a GPU, a missing or unloadable
-extension is an error (``require()`` raises), never a silent switch to torch kernels.
-CPU tensors take the plain-torch FP32 path of each op, which is what the CPU test tier
-and the reference-semantics runs use.
+The bf16 CUDA path has no fallback: a missing or unloadable extension is an error
+(``require()`` raises), never a silent switch to torch kernels. FP32 tensors (CPU, or
+CUDA in a reference-semantics run) take the plain-torch FP32 path of each op, which is
+what the CPU test tier and the reference-semantics runs use.
 """
 
 from __future__ import annotations
