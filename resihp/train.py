@@ -40,11 +40,21 @@ def parse_args(argv=None):
 
 
 def select_device():
+    """This rank's GPU (``LOCAL_RANK``), or the CPU where there is none.
+
+    One rank per GPU is a hard rule, not a default: the fused kernels of ranks that wait
+    on one another must run concurrently, which two launches sharing one GPU do not
+    guarantee. A job with more ranks than visible GPUs is refused.
+    """
     import torch
 
     if not torch.cuda.is_available():
         return torch.device("cpu")
-    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if local >= torch.cuda.device_count():
+        raise RuntimeError(f"rank with LOCAL_RANK={local} has no GPU of its own: {torch.cuda.device_count()} visible; "
+                           "run one rank per GPU")
+    torch.cuda.set_device(local)
     return torch.device("cuda", torch.cuda.current_device())
 
 
