@@ -196,8 +196,10 @@ def _trace_step(step, directory, rank, barrier):
         if device_us > 0:
             rows.append({"name": ev.key[:120], "calls": ev.count, "device_us": round(device_us, 1)})
     rows.sort(key=lambda r: -r["device_us"])
+    from resihp.utils.trace import categorize
+
     with open(os.path.join(directory, f"kernels_rank{rank}.json"), "w") as f:
-        _json.dump(rows[:60], f, indent=1)
+        _json.dump({"categories": categorize(rows), "top_kernels": rows[:60]}, f, indent=1)
 
 
 def bench_config(which: int, world: int, iterations: int):

@@ -42,3 +42,43 @@ def _range(name: str):
 def nvtx_range(name: str):
     """A context manager that brackets its body with an NVTX range when tracing is on."""
     return _range(name) if _ON else contextlib.nullcontext()
+
+
+# kernel name pattern -> category, first match wins (names as the torch profiler reports
+# them, demangled or mangled; the GEMM's template arguments say which linear-layer
+# product it is: <BN, A MN-major, B MN-major, epilogue>)
+_CATEGORIES = (
+    (r"fused_gemm_kernel", "fused TP collective GEMM"),
+    (r"gemm_kernel<\d+, false, false|gemm_kernelILi\d+ELb0ELb0E", "GEMM forward"),
+    (r"gemm_kernel<\d+, false, true|gemm_kernelILi\d+ELb0ELb1E", "GEMM dgrad"),
+    (r"gemm_kernel<\d+, true, true|gemm_kernelILi\d+ELb1ELb1E", "GEMM wgrad"),
+    (r"gemm_kernel", "GEMM other"),
+    (r"attn_fwd_kernel", "attention forward"),
+    (r"attn_bwd|attn_delta", "attention backward"),
+    (r"rmsnorm|column_sum", "RMSNorm"),
+    (r"rope_kernel|swiglu|embedding_(fwd|bwd)_kernel", "RoPE / SwiGLU / embedding"),
+    (r"xent_", "cross-entropy"),
+    (r"dp_adamw_kernel", "fused DP all-reduce + AdamW"),
+    (r"adamw_kernel", "AdamW"),
+    (r"reshard_gather", "state move"),
+    (r"(?i)nccl", "NCCL"),
+    (r"(?i)memcpy|memset", "copies"),
+)
+
+
+def categorize(rows) -> dict:
+    """Device time per kernel category from ``[{"name", "calls", "device_us"}]`` rows:
+    ``{category: {"device_us", "calls", "share"}}``, largest first. What matches no
+    pattern (torch's own elementwise kernels, fills) is ``"other"``."""
+    import re
+
+    totals: dict[str, list] = {}
+    for row in rows:
+        name = row["name"]
+        cat = next((c for pattern, c in _CATEGORIES if re.search(pattern, name)), "other")
+        entry = totals.setdefault(cat, [0.0, 0])
+        entry[0] += float(row["device_us"])
+        entry[1] += int(row["calls"])
+    whole = sum(v[0] for v in totals.values()) or 1.0
+    ordered = sorted(totals.items(), key=lambda kv: -kv[1][0])
+    return {c: {"device_us": round(us, 1), "calls": n, "share": round(us / whole, 4)} for c, (us, n) in ordered}

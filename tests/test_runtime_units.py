@@ -257,3 +257,24 @@ def test_control_plane_run_constants_must_match_the_config():
     assert (cp.vocab_size, cp.sequence_length) == (64, 8)
     with pytest.raises(ValueError, match="vocab_size=64 does not match the config"):
         cp.safe_point(config, plan, (), (1,), next_step=1)
+
+
+def test_trace_categories_name_the_linear_layer_products():
+    from resihp.utils.trace import categorize
+
+    rows = [
+        {"name": "void resihp::gemm_kernel<256, false, false, 0>(CUtensorMap_st, CUtensorMap_st, resihp::GemmArgs)",
+         "calls": 10, "device_us": 600.0},
+        {"name": "_ZN6resihp11gemm_kernelILi256ELb1ELb1ELi2EEEv14CUtensorMap_stS1_NS_8GemmArgsE", "calls": 5,
+         "device_us": 300.0},
+        {"name": "void resihp::gemm_kernel<128, false, true, 0>(...)", "calls": 2, "device_us": 50.0},
+        {"name": "void resihp::fused_gemm_kernel<256, false, 1, 0>(...)", "calls": 1, "device_us": 20.0},
+        {"name": "void resihp::(anonymous namespace)::attn_bwd_dq_kernel<128>(...)", "calls": 1, "device_us": 20.0},
+        {"name": "ncclDevKernel_AllReduce_Sum_f32_RING_LL(...)", "calls": 1, "device_us": 5.0},
+        {"name": "void at::native::vectorized_elementwise_kernel<4>(...)", "calls": 1, "device_us": 5.0},
+    ]
+    cats = categorize(rows)
+    assert list(cats)[:2] == ["GEMM forward", "GEMM wgrad"]
+    assert cats["GEMM dgrad"]["calls"] == 2 and cats["fused TP collective GEMM"]["device_us"] == 20.0
+    assert cats["attention backward"]["share"] == 0.02 and cats["NCCL"]["calls"] == 1 and "other" in cats
+    assert abs(sum(c["share"] for c in cats.values()) - 1.0) < 1e-3
