@@ -61,12 +61,15 @@ def select_device():
 def fail_stop(schedule, rank: int, iteration: int, *, before=None) -> None:
     """``SIGKILL`` this process if the schedule fails ``rank`` after ``iteration``.
 
+    ``schedule`` maps an iteration to the rank (or a collection of ranks, for tests of
+    simultaneous failures; failure files name one rank per event) that fails after it.
     ``before`` runs first (the worker passes its checkpoint flush, so a scheduled
     fail-stop happens after its iteration's commit is on disk).
     """
     import signal
 
-    if schedule.get(iteration) == rank:
+    victims = schedule.get(iteration)
+    if victims == rank or (isinstance(victims, (list, tuple, set, frozenset)) and rank in victims):
         if before is not None:
             before()
         os.kill(os.getpid(), signal.SIGKILL)

@@ -94,3 +94,32 @@ def test_losing_any_single_rank_recovers(victim, tmp_path):
                     per_replica.setdefault(e["replica"], e["loss"])
         got = sum(per_replica.values())
         assert abs(got - rec["loss"]) <= 1e-4 * abs(rec["loss"]), (victim, 3 + i, got, rec["loss"])
+
+
+@pytest.mark.slow
+def test_two_ranks_lost_at_one_boundary(tmp_path):
+    """Two ranks of different replicas die after the same iteration: the survivors see
+    both at one boundary, take one safe point for the pair (the plan the planner makes
+    for both failures at once), and train on -- beyond the reference's schedule format,
+    which names one rank per event."""
+    kills = {"2": [2, 5]}
+    config = TrainConfig(**CONFIG)
+    codes = run_ranks(dist_entries.e2e_entry, 8, CONFIG, kills, str(tmp_path))
+    assert_killed(codes, [2, 5], "pair")
+    plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)
+    after = build_plan(config, step=2, version=1, failed_ranks=(2, 5), previous=plan, vocab_size=config.vocab_size,
+                       sequence_length=config.seq_len)
+    results = read_results(tmp_path, [r for r in range(8) if r not in (2, 5)])
+    for res in results.values():
+        assert res["stopped"] is None and res["plans"] == [plan.digest, after.digest]
+        assert all(rec["a1"] in (True, None) for rec in res["recoveries"])
+        trained = [e for e in res["iterations"] if e["trained"]]
+        assert [e["cursor"] for e in trained] == list(range(len(trained)))
+    anchor, completed = load_anchor(os.path.join(tmp_path, "anchor_2.pt"))
+    want = steps_from_anchor(config, anchor, start=completed, count=1)[0]["loss"]
+    per_replica = {}
+    for res in results.values():
+        for e in res["iterations"]:
+            if e["iteration"] == 3 and e.get("loss") is not None:
+                per_replica.setdefault(e["replica"], e["loss"])
+    assert abs(sum(per_replica.values()) - want) <= 1e-4 * abs(want)
