@@ -4,8 +4,8 @@ Put this directory first on ``PYTHONPATH`` of the reference's launcher (with
 ``RESIHP_REFHOOK=1``); every worker then imports it at start-up. It changes no file of
 the reference: when the reference's ``resihp.control`` module loads, it wraps
 ``ControlPlane.observe``, ``safe_point`` and ``training_step`` with timers and prints one
-``{"refrecovery": ...}`` JSON line per fail-stop (failure detected at the boundary ->
-end of the first resumed step, the same interval this framework reports) and a
+``{"refrecovery": ...}`` JSON line per fail-stop (numbered from 1; failure detected at the
+boundary -> end of the first resumed step, the same interval this framework reports) and a
 ``{"refstep": ...}`` line per trained step. ``RESIHP_REF_VOCAB`` / ``RESIHP_REF_SEQ``
 replace the reference's hard-coded run constants (vocabulary 256, sequence 16) so it
 can run the config-1 shape.
@@ -24,7 +24,7 @@ def _patch(control):
     if hasattr(main, "VOCAB_SIZE"):
         main.VOCAB_SIZE = int(os.environ.get("RESIHP_REF_VOCAB", main.VOCAB_SIZE))
         main.SEQUENCE_LENGTH = int(os.environ.get("RESIHP_REF_SEQ", main.SEQUENCE_LENGTH))
-    state = {"t_fail": None, "pending": False, "t_sp": None}
+    state = {"t_fail": None, "pending": False, "t_sp": None, "event": 0}
     cls = control.ControlPlane
     observe, safe_point, training_step = cls.observe, cls.safe_point, cls.training_step
 
@@ -37,6 +37,7 @@ def _patch(control):
 
     def timed_safe_point(self, *args, **kwargs):
         out = safe_point(self, *args, **kwargs)
+        state["event"] += 1
         state["pending"] = True
         state["t_sp"] = time.perf_counter()
         return out
@@ -49,7 +50,8 @@ def _patch(control):
             print(json.dumps({"refstep": {"rank": self.rank, "step_s": t1 - t0}}), flush=True)
         if state["pending"]:
             state["pending"] = False
-            print(json.dumps({"refrecovery": {"rank": self.rank, "seconds": t1 - state["t_fail"],
+            print(json.dumps({"refrecovery": {"rank": self.rank, "event": state["event"],
+                                              "seconds": t1 - state["t_fail"],
                                               "safe_point_s": state["t_sp"] - state["t_fail"],
                                               "first_step_s": t1 - t0}}), flush=True)
         return out

@@ -74,6 +74,9 @@ def parse():
     p.add_argument("--layout", default=None, help="tp,pp,dp (default: config 4's layout for --gpus)")
     p.add_argument("--config", type=int, choices=(1, 4), default=4,
                    help="4: the 1.3B GPU run (default); 1: the CPU/Gloo run of BASELINE config 1")
+    p.add_argument("--shipped", action="store_true",
+                   help="the shipped configs/train.json + configs/failures.json schedule on CPU/Gloo "
+                        "(8 ranks, 5 fail-stops); with --impl reference, the unmodified reference runs it")
     p.add_argument("--reference-model", action="store_true",
                    help="config 1 only: the GPT-2 config-1-like model the reference can express")
     p.add_argument("--impl", choices=("resihp", "reference"), default="resihp",
@@ -86,9 +89,17 @@ def parse():
 
 def main():
     args = parse()
-    if args.impl == "reference" and not (args.config == 1 and args.reference_model):
-        raise SystemExit("--impl reference runs config 1 with --reference-model only")
-    if args.config == 1:
+    if args.impl == "reference" and not (args.shipped or (args.config == 1 and args.reference_model)):
+        raise SystemExit("--impl reference runs --shipped, or config 1 with --reference-model")
+    if args.shipped:
+        with open(os.path.join(ROOT, "configs", "train.json")) as f:
+            config = json.load(f)
+        with open(os.path.join(ROOT, "configs", "failures.json")) as f:
+            shipped = json.load(f)["events"]
+        tp, pp, dp = config["tp"], config["pp"], config["dp"]
+        args.gpus = tp * pp * dp
+        args.kills = ",".join(f"{e['after_iteration']}:{e['failed_rank']}" for e in shipped)
+    elif args.config == 1:
         config = dict(CONFIG1)
         if args.reference_model:
             config = dict(REFERENCE_MODEL1)
@@ -118,14 +129,16 @@ def main():
         with open(fail_path, "w") as f:
             json.dump(failures, f)
         env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", RESIHP_CHECKPOINT=os.path.join(tmp, "ck.pt"))
-        if args.config == 1:
-            env.update(CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")  # config 1 is the CPU/Gloo run
+        if args.config == 1 or args.shipped:
+            env.update(CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="1")  # the CPU/Gloo runs
         if args.impl == "reference":
             ref = os.path.join(ROOT, "baseline", "_ref")
             if not os.path.isdir(os.path.join(ref, "resihp")):
                 raise SystemExit("reference not installed under baseline/_ref")
             env.update(PYTHONPATH=os.pathsep.join([os.path.join(ROOT, "baseline", "recovery_hook"), ref]),
-                       RESIHP_REFHOOK="1", RESIHP_REF_VOCAB="1024", RESIHP_REF_SEQ="128")
+                       RESIHP_REFHOOK="1")
+            if not args.shipped:  # config 1's token-stream shape; the shipped config uses the defaults
+                env.update(RESIHP_REF_VOCAB="1024", RESIHP_REF_SEQ="128")
         elif args.reference_model:
             with open(cfg_path, "w") as f:
                 json.dump(dict(config, vocab_size=1024, seq_len=128), f)
@@ -139,8 +152,9 @@ def main():
     if args.impl == "reference":
         for l in lines:
             if "refrecovery" in l:
-                l["recovery"] = dict(l.pop("refrecovery"), after_iteration=kills[0][0], phases={},
-                                     plan_version=1)
+                rec = l.pop("refrecovery")
+                event = rec.get("event", 1)
+                l["recovery"] = dict(rec, after_iteration=kills[event - 1][0], phases={}, plan_version=event)
             if "refstep" in l:
                 l["step"], l["step_s"] = -1, l.pop("refstep")["step_s"]
     launch = next((l["launch"] for l in lines if "launch" in l), None)
@@ -150,7 +164,9 @@ def main():
             steps.setdefault(l["step"], []).append(l["step_s"])
     seq_len = config.get("seq_len", 128 if args.reference_model else 16)
     tokens = config["batch_size"] * seq_len
-    if args.config == 1:
+    if args.shipped:
+        label = "shipped configs/train.json (gpt2, CPU/Gloo, FP32)"
+    elif args.config == 1:
         label = ("gpt2 config-1-like (CPU/Gloo, FP32)" if args.reference_model else "llama-config1 (CPU/Gloo, FP32)")
     else:
         label = "llama-1.3b" if not args.small else "llama-small"
@@ -177,14 +193,14 @@ def main():
     print(json.dumps({
         "metric": "fail-stop recovery seconds (failure -> end of first resumed step, max over survivors)",
         "impl": args.impl, "median_step_s": round(statistics.median(all_steps), 4) if all_steps else None,
-        "n_gpus": 0 if args.config == 1 else args.gpus, "ranks": args.gpus,
-        "config": {"model": label, "baseline_config": args.config,
+        "n_gpus": 0 if (args.config == 1 or args.shipped) else args.gpus, "ranks": args.gpus,
+        "config": {"model": label, "baseline_config": None if args.shipped else args.config,
                    "parallelism": f"tp{tp}-pp{pp}-dp{dp}" + ("-sp" if config.get("sequence_parallel") else ""),
                    "dtype": config.get("dtype", "fp32"), "global_batch": config["batch_size"], "seq_len": seq_len},
         "events": events, "launch": launch, "launcher_rc": out.returncode,
         "stopped": [l for l in lines if "stopped" in l],
         "steps_seen": sorted(steps),
-        "recovery_lines": [l["recovery"] for l in lines if "recovery" in l][:4],
+        "recovery_lines": [l["recovery"] for l in lines if "recovery" in l][:4 * len(kills)],
         "stderr_tail": out.stderr[-1500:] if out.returncode else "",
     }), flush=True)
 
