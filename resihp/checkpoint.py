@@ -134,9 +134,25 @@ def _same(a, b) -> bool:
     return type(a) is type(b) and a == b
 
 
-def save_checkpoint(path, config: TrainConfig, full: dict, *, completed_steps: int, plan_version: int = 0,
-                    rng: tuple | None = None) -> Path:
-    """Atomically write the logical checkpoint; returns the canonical path."""
+def _is_run(obj) -> bool:
+    """A single-process run (:class:`resihp.reference.ReferenceRun`) rather than a config."""
+    return hasattr(obj, "full_state") and hasattr(obj, "cursor") and hasattr(obj, "config")
+
+
+def save_checkpoint(path, config: TrainConfig, full: dict | None = None, *, completed_steps: int | None = None,
+                    plan_version: int = 0, rng: tuple | None = None) -> Path:
+    """Atomically write the logical checkpoint; returns the canonical path.
+
+    ``config`` + ``full`` (``{name: {param[, exp_avg, exp_avg_sq, step]}}``) +
+    ``completed_steps``; or, as the reference calls it (``resihp/checkpoint.py:133``), a
+    single-process run in place of ``config``, whose state and cursor are written.
+    """
+    if _is_run(config):
+        run = config
+        config, full = run.config, run.full_state()
+        completed_steps = run.cursor if completed_steps is None else completed_steps
+    if full is None or completed_steps is None:
+        raise TypeError("save_checkpoint needs the full state and completed_steps (or a run)")
     if type(plan_version) is not int or plan_version < 0:
         raise CheckpointError("plan_version must be a non-negative integer")
     payload = build_payload(config, full, completed_steps=completed_steps, plan_version=plan_version, rng=rng)
@@ -324,14 +340,25 @@ def install_anchor(model, optimizer, anchor: dict) -> None:
         }
 
 
-def load_checkpoint(path, config: TrainConfig) -> tuple[dict, int, int]:
-    """Validated ``(anchor, completed_steps, plan_version)``; restores the CPU/CUDA RNG."""
+def load_checkpoint(path, config: TrainConfig):
+    """Validated ``(anchor, completed_steps, plan_version)``; restores the CPU/CUDA RNG.
+
+    Given a single-process run instead of a config (the reference's call,
+    ``resihp/checkpoint.py:272``), the state is installed into the run, its cursor set,
+    and ``(completed_steps, plan_version)`` returned.
+    """
     from .models.layout import model_specs
 
+    run = config if _is_run(config) else None
+    if run is not None:
+        config = run.config
     payload = read_payload(path)
     validate(payload, config, {s.name: s.shape for s in model_specs(config)})
     torch.set_rng_state(payload["cpu_rng_state"])
     if payload["cuda_rng_state"] is not None and torch.cuda.is_available():
         torch.cuda.set_rng_state_all(payload["cuda_rng_state"])
     anchor, completed = load_anchor(path, verify=False)
+    if run is not None:
+        run.restore(anchor, completed)
+        return completed, payload["plan_version"]
     return anchor, completed, payload["plan_version"]

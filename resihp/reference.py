@@ -103,15 +103,26 @@ class StepRecord:
     loss: float
     param_digest: str
     optim_digest: str
+    tokens: tuple = ()  # the batch, row by row (the reference records it too)
 
 
 class ReferenceRun:
     """The whole model in one process (see the module docstring)."""
 
-    def __init__(self, config: TrainConfig, *, device="cpu", full_state=None, moments=None, cursor: int = 0):
+    def __init__(self, config: TrainConfig, *, device="cpu", full_state=None, moments=None, cursor: int = 0,
+                 vocab_size: int | None = None, sequence_length: int | None = None):
+        # the reference passes its run constants here; they override the config's
+        changes = {}
+        if vocab_size is not None and vocab_size != config.vocab_size:
+            changes["vocab_size"] = vocab_size
+        if sequence_length is not None and sequence_length != config.seq_len:
+            changes["seq_len"] = sequence_length
+        config = dataclasses.replace(config, **changes) if changes else config
         if config.seq_len < 2:
             raise ValueError("sequence_length must be at least 2 for next-token loss")
         self.config = config
+        self.vocab_size = config.vocab_size
+        self.sequence_length = config.seq_len
         self.device = torch.device(device)
         state = initial_state(config, device=self.device) if full_state is None else full_state
         self.stage = TensorParallelStage(
@@ -131,6 +142,7 @@ class ReferenceRun:
         stage.optimizer_step()
         record = StepRecord(
             step=self.cursor,
+            tokens=tuple(tuple(row) for row in tokens.tolist()),
             loss=float(loss.detach()),
             param_digest=digest_tensors(sorted(stage.logical_state_dict().items())),
             optim_digest=digest_tensors(sorted(
@@ -139,6 +151,20 @@ class ReferenceRun:
         )
         self.cursor += 1
         return record
+
+    def restore(self, anchor: dict, completed: int) -> None:
+        """Install a full logical anchor (``{name: {param[, exp_avg, exp_avg_sq, step]}}``)
+        and continue after ``completed`` steps."""
+        stage = self.stage
+        with torch.no_grad():
+            for name, view in stage.logical_state_dict().items():
+                view.copy_(anchor[name]["param"].to(view.device, torch.float32))
+            stage.flat.exp_avg.zero_()
+            stage.flat.exp_avg_sq.zero_()
+            stage.flat.step = 0
+        stage.install_moments({n: e for n, e in anchor.items() if "exp_avg" in e})
+        stage.flat.refresh_work()
+        self.cursor = int(completed)
 
     def full_state(self) -> dict[str, dict[str, torch.Tensor]]:
         """``{name: {param, exp_avg, exp_avg_sq, step}}`` (the checkpoint's logical form)."""
@@ -154,6 +180,7 @@ class ReferenceRun:
         return out
 
 
-def run_reference(config: TrainConfig, *, device="cpu") -> list[StepRecord]:
-    run = ReferenceRun(config, device=device)
-    return [run.step() for _ in range(config.iterations)]
+def run_reference(config: TrainConfig, *, device="cpu", vocab_size: int | None = None,
+                  sequence_length: int | None = None) -> list[StepRecord]:
+    run = ReferenceRun(config, device=device, vocab_size=vocab_size, sequence_length=sequence_length)
+    return [run.step() for _ in range(run.config.iterations)]

@@ -158,3 +158,20 @@ def test_we_read_the_references_checkpoint(tmp_path):
     for name, values in theirs.items():
         assert torch.equal(anchor[name]["param"], torch.tensor(values)), name
         assert int(anchor[name]["step"]) == 2
+
+
+def test_reference_style_save_and_load_resume_a_run_bit_for_bit(tmp_path):
+    """The reference's calls -- ``ReferenceRun(config, vocab_size=, sequence_length=)``,
+    ``save_checkpoint(path, run, plan_version=)``, ``load_checkpoint(path, run)`` -- work
+    here and a restored run continues exactly like the original."""
+    base = TrainConfig(model_dim=16, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=3, tp=1,
+                       pp=1, dp=1, iterations=4)
+    run = ReferenceRun(base, vocab_size=32, sequence_length=8)
+    first = [run.step() for _ in range(2)]
+    assert run.config.vocab_size == 32 and run.sequence_length == 8
+    assert first[0].tokens == tuple(tuple(r) for r in run.batches[0].tolist())
+    path = save_checkpoint(tmp_path / "ck.pt", run, plan_version=1)
+    other = ReferenceRun(base, vocab_size=32, sequence_length=8)
+    assert load_checkpoint(path, other) == (2, 1) and other.cursor == 2
+    a, b = run.step(), other.step()
+    assert (a.loss, a.param_digest, a.optim_digest) == (b.loss, b.param_digest, b.optim_digest)
