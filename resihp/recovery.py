@@ -163,8 +163,29 @@ class PlannedRun:
         return out
 
 
-def initial_run(plan, *, rank, groups: TrainingGroups, device=None, pin=False):
-    """The run a rank starts with: the seeded initial weights cut to its stage and shard."""
+def _reference_groups(plan, groups, *, vocab_size=None, sequence_length=None, world_group=None, tp_group=None,
+                      executor_group=None, boundary_groups=None) -> TrainingGroups:
+    """``groups``, or the :class:`TrainingGroups` the reference's keyword form names
+    (``tp_group``, ``executor_group``, ``boundary_groups``, ``world_group``); the
+    reference's run constants, when passed, must match the plan's config."""
+    config = plan.config
+    for name, given, have in (("vocab_size", vocab_size, config.vocab_size),
+                              ("sequence_length", sequence_length, config.seq_len)):
+        if given is not None and given != have:
+            raise ValueError(f"{name}={given} does not match the config ({have})")
+    if groups is not None:
+        return groups
+    return TrainingGroups(world=world_group, tp=tp_group, hops=dict(boundary_groups or {}), executor=executor_group)
+
+
+def initial_run(plan, *, rank, groups: TrainingGroups | None = None, device=None, pin=False, **reference_form):
+    """The run a rank starts with: the seeded initial weights cut to its stage and shard.
+
+    ``reference_form``: the reference's keywords (``vocab_size``, ``sequence_length``,
+    ``tp_group``, ``executor_group``, ``boundary_groups``) in place of ``groups``
+    (reference ``resihp/recovery.py:262-305``).
+    """
+    groups = _reference_groups(plan, groups, **reference_form)
     sp = stage_of(plan, rank)
     if sp is None:
         return None
@@ -286,13 +307,18 @@ def gather_full_state(run, plan, *, group, dst: int | None, device, bucket_elems
     return full_state
 
 
-def commit_checkpoint(run, path, *, plan, groups: TrainingGroups, writer: bool, cursor: int, device=None,
-                      background=None):
+def commit_checkpoint(run, path, *, plan, groups: TrainingGroups | None = None, writer: bool,
+                      cursor: int | None = None, device=None, background=None, group=None, **reference_form):
     """Safe-point step 2: gather every shard and atomically write the one checkpoint.
 
     ``background`` (a :class:`~resihp.checkpoint.CheckpointWriter`) moves the writer's
-    file write to its thread; the gather itself is a collective and stays in line.
+    file write to its thread; the gather itself is a collective and stays in line. The
+    reference's form passes the executor group as ``group`` and the run constants, and
+    lets the cursor default to the run's (reference ``resihp/recovery.py:340-370``).
     """
+    groups = _reference_groups(plan, groups, executor_group=group, **reference_form)
+    if cursor is None:
+        cursor = 0 if run is None else run.cursor
     if groups.executor is None:
         return
     dst = plan.active_ranks[0]

@@ -32,7 +32,7 @@ ATOL = 1e-5
 # --- A1 --------------------------------------------------------------------------------
 
 
-def matches_checkpoint(run, *, plan, rank, checkpoint_path) -> bool:
+def matches_checkpoint(run, plan, rank, checkpoint_path) -> bool:
     anchor, _ = load_anchor(checkpoint_path)
     return not checkpoint_mismatches(run, plan=plan, rank=rank, anchor=anchor)
 
@@ -70,10 +70,23 @@ def batch(config, index, *, device, vocab_size=None, sequence_length=None):
     return token_stream(config)[index].to(device)
 
 
-def denominator(config, exp_avg_sq, step):
-    """AdamW's ``sqrt(v / bias_correction2) + eps`` after its ``step``-th update."""
-    bc2 = 1 - config.beta2 ** float(step)
-    return exp_avg_sq.sqrt() / math.sqrt(bc2) + config.adam_eps
+def denominator(config, exp_avg_sq=None, step=None):
+    """AdamW's ``sqrt(v / bias_correction2) + eps`` after its ``step``-th update.
+
+    ``denominator(config, exp_avg_sq, step)``; or, as the reference calls it,
+    ``denominator(state)`` with ``state = {"exp_avg_sq", "step"}`` and the default
+    AdamW hyper-parameters.
+    """
+    if exp_avg_sq is None:
+        from .config import TrainConfig
+
+        state, defaults = config, TrainConfig.__dataclass_fields__
+        exp_avg_sq, step = state["exp_avg_sq"], state["step"]
+        beta2, eps = defaults["beta2"].default, defaults["adam_eps"].default
+    else:
+        beta2, eps = config.beta2, config.adam_eps
+    bc2 = 1 - beta2 ** float(step)
+    return exp_avg_sq.sqrt() / math.sqrt(bc2) + eps
 
 
 
@@ -84,8 +97,16 @@ def reference_steps(config, *, count, device="cpu", vocab_size=None, sequence_le
     return [step_record(run) for _ in range(count)]
 
 
-def step_record(run: ReferenceRun) -> dict:
-    """One full-batch oracle step: its gradients, new parameters, moments and denominators."""
+def step_record(run, optimizer=None, tokens=None, *, vocab_size=None) -> dict:
+    """One full-batch oracle step: its gradients, new parameters, moments and denominators.
+
+    ``step_record(run)`` steps a :class:`~resihp.reference.ReferenceRun`. The reference's
+    form ``step_record(model, optimizer, tokens, vocab_size=V)`` steps a module-form model
+    (:class:`resihp.model.ReferenceTransformer`) with its ``torch.optim.AdamW`` and
+    returns the reference's keys: loss, grads, params, moments.
+    """
+    if optimizer is not None:
+        return _module_step_record(run, optimizer, tokens, vocab_size)
     stage = run.stage
     tokens = run.batches[run.cursor].to(run.device)
     stage.zero_grad()
@@ -102,8 +123,27 @@ def step_record(run: ReferenceRun) -> dict:
     return {"loss": float(loss.detach()), "grads": grads, "params": params, "denoms": denoms}
 
 
-def steps_from_anchor(config, anchor, *, start: int, count: int, device="cpu") -> list[dict]:
+def _module_step_record(model, optimizer, tokens, vocab_size) -> dict:
+    from .reference import next_token_loss
+
+    loss = next_token_loss(model(tokens), tokens, vocab_size)
+    optimizer.zero_grad()
+    loss.backward()
+    named = model.logical_state_dict()
+    grads = {n: p.grad.detach().clone() for n, p in named.items()}
+    optimizer.step()
+    return {
+        "loss": float(loss.detach()), "grads": grads,
+        "params": {n: p.detach().clone() for n, p in named.items()},
+        "moments": {n: {k: optimizer.state[p][k].detach().clone() for k in ("exp_avg", "exp_avg_sq", "step")}
+                    for n, p in named.items()},
+    }
+
+
+def steps_from_anchor(config, anchor, *, start: int, count: int, device="cpu", vocab_size=None,
+                      sequence_length=None) -> list[dict]:
     """A2's oracle: ``count`` full-batch steps from the checkpoint ``anchor`` at cursor ``start``."""
+    _check_constants(config, vocab_size, sequence_length)
     full = {n: e["param"] for n, e in anchor.items()}
     moments = {n: e for n, e in anchor.items() if "exp_avg" in e}
     run = ReferenceRun(config, device=device, full_state=full, moments=moments, cursor=start)
