@@ -138,3 +138,27 @@ def parameter_count(config: TrainConfig) -> int:
             n *= x
         total += n
     return total
+
+
+def kernel_shape_problems(config: TrainConfig, tp_size: int) -> list[str]:
+    """The shape rules of the bf16 sm_100a kernels that a stage at TP degree ``tp_size``
+    would break (empty when the shape runs). The same rules the kernels' host wrappers
+    check before a launch (``csrc/attention.cu``, ``norm.cu``, ``xent.cu``, ``gemm.cu``),
+    gathered so a stage can refuse an unsupported shape with one message at set-up."""
+    out = []
+    d, hd, tp = config.model_dim, config.head_dim, tp_size
+    if hd not in (64, 128):
+        out.append(f"head_dim {hd} (attention: 64 or 128)")
+    if config.seq_len % 128:
+        out.append(f"seq_len {config.seq_len} (attention: a multiple of 128)")
+    w = d // 8
+    if d % 8 or w == 0 or w > 1024 or (w % 32 if w >= 32 else 32 % w):
+        out.append(f"model_dim {d} (RMSNorm: a multiple of 8, at most 8192, d/8 dividing or divisible by 32)")
+    if (config.vocab_size // tp) % 8:
+        out.append(f"vocabulary shard {config.vocab_size // tp} (cross-entropy and LM-head GEMM: a multiple of 8)")
+    hq, hkv = config.num_heads // tp, config.kv_heads // tp
+    for what, n in (("fused QKV width", (hq + 2 * hkv) * hd), ("attention output width", hq * hd),
+                    ("FFN shard", config.ffn // tp)):
+        if n % 8:
+            out.append(f"{what} {n} (GEMM operands: a multiple of 8)")
+    return out

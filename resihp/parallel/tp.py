@@ -35,7 +35,7 @@ import torch.distributed as dist
 from torch.nn import functional as F
 
 from ..config import TrainConfig
-from ..models.layout import TensorSpec, local_shape, stage_specs
+from ..models.layout import TensorSpec, kernel_shape_problems, local_shape, stage_specs
 from ..ops import functional as fn
 from . import collectives as cc
 from . import fused
@@ -192,6 +192,10 @@ class TensorParallelStage:
         self.kernel = self.device.type == "cuda" and config.dtype == "bf16"
         if config.arch == "gpt2" and self.kernel:
             raise ValueError("gpt2 blocks run on the FP32 reference path only (dtype fp32)")
+        if self.kernel:
+            problems = kernel_shape_problems(config, self.tp_size)
+            if problems:
+                raise ValueError(f"the bf16 kernels cannot run this shape at TP {self.tp_size}: " + "; ".join(problems))
         compute = torch.bfloat16 if self.kernel else torch.float32
         self.act_dtype = compute
 

@@ -97,3 +97,30 @@ def test_memory_report_reads_a_real_run(tmp_path):
                                                                                      num_stages=1)).total
         assert r["estimate"] == float(want) and r["used"] >= 1000
     assert json.loads(Path(tmp_path, "result_0.json").read_text())["micro"] == 2
+
+
+def test_every_gpu_shape_we_run_passes_the_kernel_shape_rules():
+    """The set-up check of the bf16 kernels' shape rules accepts every shape the bench,
+    the recovery bench, the smoke run and the GPU tests run (at each TP degree they use
+    or a fail-stop can leave), and names the rule a bad shape breaks."""
+    import bench_recovery
+    from resihp.config import TrainConfig
+    from resihp.models.layout import kernel_shape_problems
+
+    for which, spec in bench.CONFIGS.items():
+        for world, (tp, _pp, _dp) in spec["layouts"].items():
+            config = bench.bench_config(which, world, 8)
+            for degree in sorted({1, tp}):
+                assert kernel_shape_problems(config, degree) == [], (which, world, degree)
+    base = dict(batch_size=64, micro_batch_size=2, seed=1, tp=2, pp=2, dp=2, iterations=1, arch="llama", dtype="bf16")
+    recovery = [dict(bench_recovery.MODEL), dict(bench_recovery.MODEL, num_layers=4, model_dim=1024, num_heads=8,
+                                                  ffn_dim=2752, seq_len=1024)]
+    gpu_tests = [dict(model_dim=256, num_layers=2, num_heads=h, vocab_size=1024, seq_len=256, ffn_dim=512)
+                 for h in (2, 4)]
+    for shape in recovery + gpu_tests:
+        for degree in (1, 2):
+            assert kernel_shape_problems(TrainConfig(**base, **shape), degree) == [], (shape, degree)
+    bad = TrainConfig(**base, num_layers=2, model_dim=96, num_heads=4, vocab_size=1001, seq_len=100, ffn_dim=100)
+    problems = " | ".join(kernel_shape_problems(bad, 2))
+    for rule in ("head_dim 24", "seq_len 100", "model_dim 96", "vocabulary shard 500", "FFN shard 50"):
+        assert rule in problems, (rule, problems)
