@@ -124,3 +124,15 @@ def test_every_gpu_shape_we_run_passes_the_kernel_shape_rules():
     problems = " | ".join(kernel_shape_problems(bad, 2))
     for rule in ("head_dim 24", "seq_len 100", "model_dim 96", "vocabulary shard 500", "FFN shard 50"):
         assert rule in problems, (rule, problems)
+
+
+def test_recovery_bench_reads_interleaved_reference_output():
+    """The reference's ranks share stdout without line-atomic writes: JSON objects can run
+    together or be split by other text; every whole object is still recovered, in order."""
+    import bench_recovery
+
+    text = ('noise {"refstep": {"rank": 0, "step_s": 0.1}}{"refrecovery": {"rank": 2, "event": 2, "seconds": 1.5}}\n'
+            'W1202 warning {"launch": {"killed_ranks": [1]}} {broken\n{"step": 3, "loss": 2.0}')
+    objs = bench_recovery._json_objects(text)
+    assert [list(o)[0] for o in objs] == ["refstep", "refrecovery", "launch", "step"]
+    assert objs[1]["refrecovery"]["event"] == 2
