@@ -4,7 +4,8 @@
 // Every spin-wait here is bounded by the global nanosecond timer. A wait that runs out
 // records a code in the kernel's error word and returns false; the caller then leaves
 // its loop, so a kernel can never hang the GPU on a barrier that is never completed.
-// The host reads the error word after the launch and raises.
+// The host reads the error word after the launch and raises. (No counterpart in the
+// reference, which runs library kernels only.)
 #pragma once
 #include <cstdint>
 #include <cuda.h>

@@ -1,6 +1,7 @@
 // Torch-free host interface of the CUDA kernels. Each launcher validates its arguments,
 // enqueues on ``stream`` and throws std::runtime_error on misuse; the torch-facing
-// wrappers in torch_api.cpp translate tensors into these calls.
+// wrappers in torch_api.cpp translate tensors into these calls. No counterpart in the
+// reference, which has no native code.
 #pragma once
 #include <cstdint>
 #include <stdexcept>

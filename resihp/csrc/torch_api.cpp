@@ -1,6 +1,8 @@
 // Torch-facing wrappers and Python bindings of the sm_100a kernels (module resihp._C).
 // Shapes, dtypes and strides are checked here; the CUDA launchers behind launch.h only
 // see raw pointers, so the kernel translation units stay free of torch headers.
+// (The reference is pure Python and calls torch / NCCL ops directly; this layer has no
+// counterpart there.)
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
