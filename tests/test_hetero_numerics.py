@@ -27,6 +27,8 @@ CASES = [
     (dict(tp=2, pp=1, dp=2, sequence_parallel=True), (1,)),  # SP replica (TP2) next to a TP1 replica
     (dict(tp=2, pp=2, dp=2, sequence_parallel=True, tied_embeddings=True), (5, 2)),  # all of it at once
     (dict(tp=1, pp=1, dp=4), (0,)),                        # 4 micro-batches over 3 replicas: a 2/1/1 split
+    (dict(tp=4, pp=3, dp=1, num_kv_heads=4, num_layers=4), (4, 9, 6)),  # TP4 stages shrink twice, layers move
+    (dict(tp=1, pp=3, dp=3, num_layers=4), (4, 5)),        # a replica loses two stages of three
 ]
 
 
