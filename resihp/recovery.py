@@ -33,7 +33,7 @@ from hashlib import sha256
 import torch
 import torch.distributed as dist
 
-from .checkpoint import CheckpointError, read_payload, save_checkpoint, verify_digest
+from .checkpoint import CheckpointError, identity, read_payload, save_checkpoint, verify_digest
 from .models.init import initial_stage_state
 from .ops import _ext
 from .parallel import peer
@@ -422,6 +422,43 @@ def _load_anchor(checkpoint_path):
     return anchor, payload["completed_steps"], payload["digest"]
 
 
+class InitialAnchor(dict):
+    """The seeded initial state as a checkpoint anchor (``{name: {"param"}}``, no moments,
+    zero completed steps), built name by name as recovery asks for it.
+
+    Every run of a config starts from this state, bit for bit on every rank, so a
+    failure that comes before the first checkpoint commit rolls back to it instead of
+    stopping: the iterations before the failure are re-run under the new plan.
+    """
+
+    def __init__(self, config):
+        super().__init__()
+        self.config = config
+        self.names = {s.name for s in model_specs(config)}
+        self.digest = sha256(("initial-state:" + repr(sorted(identity(config).items()))).encode("utf-8")).hexdigest()
+
+    def _build(self, name: str) -> None:
+        from .models.init import initial_state
+
+        # GPT-2 blocks are drawn from one generator in module order: build them all once
+        wanted = None if self.config.arch == "gpt2" else [name]
+        for n, t in initial_state(self.config, names=wanted).items():
+            dict.setdefault(self, n, {"param": t})
+
+    def get(self, name, default=None):
+        if name not in self.names:
+            return default
+        if not dict.__contains__(self, name):
+            self._build(name)
+        return dict.__getitem__(self, name)
+
+    def __getitem__(self, name):
+        entry = self.get(name)
+        if entry is None:
+            raise KeyError(name)
+        return entry
+
+
 def state_fingerprint(run) -> str:
     """Cheap, deterministic fingerprint of one rank's shards (computed on its device)."""
     if run is None:
@@ -573,7 +610,10 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
     Returns ``(run, state digest, resume cursor)``: the cursor is the number of completed
     iterations training continues from -- ``cursor`` itself, or the checkpoint's count
     when the plan needs a checkpoint route and the checkpoint is older than the live
-    state (every rank then rolls back to it).
+    state (every rank then rolls back to it). A failure before the first commit of a
+    ``checkpoint_every > 1`` run rolls back to the seeded initial state
+    (:class:`InitialAnchor`, cursor 0); a missing file after a commit is
+    ``checkpoint_unusable``.
 
     Every surviving rank calls this (the idle ones too: their shards may be donors).
     The checkpoint is read only when some route needs it or when it is current, in which
@@ -584,7 +624,11 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
     needs_checkpoint = any(r.donor_kind == "checkpoint" for r in plan.state_routes)
     loaded = _load_anchor(checkpoint_path)
     if loaded is None and needs_checkpoint:
-        raise CheckpointError(f"checkpoint missing: {checkpoint_path}")
+        if cursor >= config.checkpoint_every:  # a commit happened, and its file is gone
+            raise CheckpointError(f"checkpoint missing: {checkpoint_path}")
+        # no commit yet (checkpoint_every > 1): the seeded initial state is the checkpoint
+        initial = InitialAnchor(config)
+        loaded = (initial, 0, initial.digest)
     anchor, completed, ck_digest = loaded if loaded is not None else ({}, None, None)
     current = completed == cursor
     rollback = needs_checkpoint and not current

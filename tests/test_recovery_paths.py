@@ -83,3 +83,35 @@ def test_group_churn_without_failure_is_transparent(tmp_path):
         assert set(codes.values()) == {0}, codes
         runs[churn] = {r: v["losses"] for r, v in read_results(out, range(4)).items()}
     assert runs[0] == runs[2]
+
+
+@pytest.mark.slow
+def test_failure_before_the_first_checkpoint_rolls_back_to_the_initial_state(tmp_path):
+    """``checkpoint_every = 3`` and a kill after iteration 2: no checkpoint exists yet and
+    the dead rank's stage has no other holder. Every run of the config starts from the
+    same seeded state, so the survivors roll back to it (cursor 0) instead of stopping,
+    and re-run iterations 1-2 onwards under the new plan exactly like an uninterrupted
+    run of that plan from the initial state."""
+    from resihp.checkpoint import save_checkpoint
+    from resihp.config import TrainConfig
+    from resihp.models.init import initial_state
+
+    config = dict(BASE, tp=1, pp=3, dp=1, checkpoint_every=3, iterations=5)
+    codes = run_ranks(dist_entries.failstop_entry, 3, config, {"2": 2}, str(tmp_path))
+    assert_killed(codes, [2], "early failure")
+    results = read_results(tmp_path, [0, 1])
+    for r in results.values():
+        assert r["stopped"] is None, r
+        assert r["recoveries"][0]["after"] == 2 and r["recoveries"][0]["resumed_from"] == 0
+    anchor = tmp_path / "initial.pt"
+    cfg = TrainConfig(**config)
+    save_checkpoint(anchor, cfg, {n: {"param": t} for n, t in initial_state(cfg).items()}, completed_steps=0)
+    rerun_dir = tmp_path / "rerun"
+    rerun_dir.mkdir()
+    codes = run_ranks(dist_entries.rerun_entry, 2, config, [2], 2, str(anchor), str(rerun_dir))
+    assert set(codes.values()) == {0}
+    want = {}
+    for r in read_results(rerun_dir, [0, 1]).values():
+        for it, loss in r["losses"].items():
+            want.setdefault(int(it), set()).add(loss)
+    assert _losses_after(results, 1) == {it: sorted(v) for it, v in sorted(want.items())}
