@@ -431,9 +431,11 @@ class InitialAnchor(dict):
     stopping: the iterations before the failure are re-run under the new plan.
     """
 
-    def __init__(self, config):
+    def __init__(self, config, device=None):
         super().__init__()
         self.config = config
+        # drawn where the run drew it (a CUDA generator's numbers differ from the CPU's), kept on the host
+        self.device = torch.device("cpu") if device is None else torch.device(device)
         self.names = {s.name for s in model_specs(config)}
         self.digest = sha256(("initial-state:" + repr(sorted(identity(config).items()))).encode("utf-8")).hexdigest()
 
@@ -442,8 +444,8 @@ class InitialAnchor(dict):
 
         # GPT-2 blocks are drawn from one generator in module order: build them all once
         wanted = None if self.config.arch == "gpt2" else [name]
-        for n, t in initial_state(self.config, names=wanted).items():
-            dict.setdefault(self, n, {"param": t})
+        for n, t in initial_state(self.config, names=wanted, device=self.device).items():
+            dict.setdefault(self, n, {"param": t.cpu()})
 
     def get(self, name, default=None):
         if name not in self.names:
@@ -627,7 +629,7 @@ def recover(run, *, plan, previous, rank, cursor, checkpoint_path, groups: Train
         if cursor >= config.checkpoint_every:  # a commit happened, and its file is gone
             raise CheckpointError(f"checkpoint missing: {checkpoint_path}")
         # no commit yet (checkpoint_every > 1): the seeded initial state is the checkpoint
-        initial = InitialAnchor(config)
+        initial = InitialAnchor(config, device)
         loaded = (initial, 0, initial.digest)
     anchor, completed, ck_digest = loaded if loaded is not None else ({}, None, None)
     current = completed == cursor
