@@ -102,6 +102,27 @@ def _resumed_run(path: Path, config, plan, *, rank, groups, device):
     return run, completed
 
 
+def _adopt_checkpoint(resume: Path, checkpoint_path: Path, control) -> None:
+    """Make the restart point this job's checkpoint too, so a failure before the job's own
+    first commit rolls back to it. The lowest rank links (or copies) the file into place
+    atomically; the others wait for it."""
+    import shutil
+
+    import torch.distributed as dist
+
+    src, dst = Path(resume).resolve(), Path(checkpoint_path).resolve()
+    if src != dst and control.rank == min(control.members):
+        tmp = dst.with_name(dst.name + ".adopt")
+        if tmp.exists():
+            tmp.unlink()
+        try:
+            os.link(src, tmp)
+        except OSError:
+            shutil.copyfile(src, tmp)
+        os.replace(tmp, dst)
+    dist.barrier(group=control.world_group)
+
+
 def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH, resume: Path | None = None):
     """One rank's whole job. ``resume`` restarts it from a checkpoint: training continues
     after the checkpoint's completed iterations, and failure events at or before them are
@@ -127,6 +148,7 @@ def run_distributed(loaded, *, checkpoint_path: Path = CHECKPOINT_PATH, resume: 
         run = initial_run(plan, rank=control.rank, groups=groups, device=device)
     else:
         run, start = _resumed_run(resume, config, plan, rank=control.rank, groups=groups, device=device)
+        _adopt_checkpoint(resume, checkpoint_path, control)
         _emit({"resume": {"rank": control.rank, "checkpoint": str(resume), "completed_steps": start}})
     control.attach_run(run, checkpoint_path=checkpoint_path, device=device)
     failed: tuple[int, ...] = ()

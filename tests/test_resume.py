@@ -60,3 +60,17 @@ def test_restart_from_checkpoint_continues_the_run(tmp_path):
     for it in (5, 6, 7):
         got, want = other[it][0], whole[it][0]
         assert abs(got - want) <= 1e-4 * abs(want), (it, got, want)
+
+
+@pytest.mark.slow
+def test_restarted_job_rolls_back_to_its_restart_point(tmp_path):
+    """The restart checkpoint becomes the job's own checkpoint: with ``checkpoint_every =
+    3`` a kill after iteration 5 -- before the restarted job's first commit, with no peer
+    replica -- rolls every survivor back to iteration 4 instead of stopping."""
+    _launch(tmp_path / "first", 4)
+    checkpoint = tmp_path / "first" / "checkpoint.pt"
+    lines, losses = _launch(tmp_path / "again", 7, resume=checkpoint, events=[(5, 3)], checkpoint_every=3)
+    recoveries = [l["recovery"] for l in lines if "recovery" in l]
+    assert recoveries and all(r["resumed_from"] == 4 for r in recoveries)
+    assert not [l for l in lines if "stopped" in l]
+    assert sorted(losses) == [5, 6, 7]
