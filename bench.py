@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--impl", choices=["resihp", "reference"], default="resihp")
     p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
                    help="BASELINE config: 2 (default, 1/2/4/8 GPUs), 3 or 5 (8 GPUs)")
+    p.add_argument("--layout", default=None,
+                   help="tp,pp,dp to run instead of the config's layout for this GPU count (e.g. 1,1,2: pure "
+                        "data parallelism on 2 GPUs); the JSON line's parallelism field names what ran")
     p.add_argument("--trace", default=None,
                    help="after the timed steps, profile one more step per rank and write a Chrome trace "
                         "plus a kernel summary into this directory (analysis only; not part of the number)")
@@ -202,12 +205,15 @@ def _trace_step(step, directory, rank, barrier):
         _json.dump({"categories": categorize(rows), "top_kernels": rows[:60]}, f, indent=1)
 
 
-def bench_config(which: int, world: int, iterations: int):
-    """The training config the bench runs: BASELINE config ``which`` on ``world`` GPUs."""
+def bench_config(which: int, world: int, iterations: int, layout: tuple[int, int, int] | None = None):
+    """The training config the bench runs: BASELINE config ``which`` on ``world`` GPUs
+    (in ``layout`` = ``(tp, pp, dp)`` when given, else the config's layout for them)."""
     from resihp.config import TrainConfig
 
     spec = CONFIGS[which]
-    tp, pp, dp = spec["layouts"][world]
+    tp, pp, dp = layout if layout is not None else spec["layouts"][world]
+    if tp * pp * dp != world:
+        raise SystemExit(f"layout tp{tp} pp{pp} dp{dp} does not use {world} GPUs")
     extra = dict(num_kv_heads=None)
     extra.update(spec["extra"])
     return TrainConfig(
@@ -258,13 +264,14 @@ def run_ours(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     spec = CONFIGS[args.config]
-    if world not in spec["layouts"]:
+    layout = tuple(int(x) for x in args.layout.split(",")) if args.layout else None
+    if layout is None and world not in spec["layouts"]:
         raise SystemExit(f"config {args.config} runs on {sorted(spec['layouts'])} GPUs, not {world}")
-    tp, pp, dp = spec["layouts"][world]
+    tp, pp, dp = layout if layout is not None else spec["layouts"][world]
     global_batch, micro_batch = spec["global_batch"], spec["micro_batch"]
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    config = bench_config(args.config, world, args.warmup + args.steps)
+    config = bench_config(args.config, world, args.warmup + args.steps, layout)
     cp = ControlPlane(rank, range(world), _store(rank, world), "nccl", device=device)
     cp.form_world(range(world), epoch=0)
     plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len)

@@ -136,3 +136,14 @@ def test_recovery_bench_reads_interleaved_reference_output():
     objs = bench_recovery._json_objects(text)
     assert [list(o)[0] for o in objs] == ["refstep", "refrecovery", "launch", "step"]
     assert objs[1]["refrecovery"]["event"] == 2
+
+
+def test_layout_override_plans_as_asked():
+    for world, layout in ((2, (1, 1, 2)), (4, (1, 1, 4)), (4, (2, 1, 2)), (8, (1, 1, 8))):
+        config = bench.bench_config(2, world, 8, layout)
+        plan = build_plan(config, step=0, version=0, vocab_size=config.vocab_size, sequence_length=config.seq_len,
+                          memory_budget=config.memory_budget_bytes)
+        assert {s.tp_degree for s in plan.stages} == {layout[0]} and len(plan.stages) == layout[1] * layout[2]
+        assert config.sequence_parallel == (layout[0] > 1)
+    with pytest.raises(SystemExit, match="does not use 4 GPUs"):
+        bench.bench_config(2, 4, 8, (2, 1, 1))
