@@ -239,6 +239,20 @@ def parse_failures(raw: dict[str, Any], train: TrainConfig) -> tuple[FailureEven
     return tuple(events)
 
 
+def with_run_constants(config: TrainConfig, vocab_size: int | None = None,
+                       sequence_length: int | None = None) -> TrainConfig:
+    """``config`` with the token-stream shape a reference-style caller passes on its own
+    (the reference keeps vocabulary and sequence length as run constants)."""
+    from dataclasses import replace
+
+    changes = {}
+    if vocab_size is not None and vocab_size != config.vocab_size:
+        changes["vocab_size"] = vocab_size
+    if sequence_length is not None and sequence_length != config.seq_len:
+        changes["seq_len"] = sequence_length
+    return replace(config, **changes) if changes else config
+
+
 def load_config(config_path: str | Path, failures_path: str | Path) -> LoadedConfig:
     train = parse_train(_load_json_object(Path(config_path), "training config"))
     failures = parse_failures(_load_json_object(Path(failures_path), "failure config"), train)

@@ -23,13 +23,11 @@ there is no ``lm_head.weight``.
 
 from __future__ import annotations
 
-import dataclasses
-
 import torch
 from torch import nn
 from torch.nn import functional as F
 
-from .config import TrainConfig
+from .config import TrainConfig, with_run_constants
 from .models.init import initial_state
 
 #: GPT-2 blocks: MLP hidden width as a multiple of ``model_dim`` (``ffn_dim`` overrides).
@@ -180,12 +178,7 @@ class ReferenceTransformer(nn.Module):
     def __init__(self, config: TrainConfig, *, vocab_size: int | None = None, sequence_length: int | None = None,
                  init: bool = True):
         super().__init__()
-        changes = {}
-        if vocab_size is not None and vocab_size != config.vocab_size:
-            changes["vocab_size"] = vocab_size
-        if sequence_length is not None and sequence_length != config.seq_len:
-            changes["seq_len"] = sequence_length
-        config = dataclasses.replace(config, **changes) if changes else config
+        config = with_run_constants(config, vocab_size, sequence_length)
         self.config = config
         self.vocab_size = config.vocab_size
         self.sequence_length = config.seq_len

@@ -20,7 +20,7 @@ from hashlib import sha256
 import torch
 from torch.nn import functional as F
 
-from .config import TrainConfig
+from .config import TrainConfig, with_run_constants
 from .models.init import initial_state
 from .parallel.tp import TensorParallelStage
 
@@ -111,13 +111,7 @@ class ReferenceRun:
 
     def __init__(self, config: TrainConfig, *, device="cpu", full_state=None, moments=None, cursor: int = 0,
                  vocab_size: int | None = None, sequence_length: int | None = None):
-        # the reference passes its run constants here; they override the config's
-        changes = {}
-        if vocab_size is not None and vocab_size != config.vocab_size:
-            changes["vocab_size"] = vocab_size
-        if sequence_length is not None and sequence_length != config.seq_len:
-            changes["seq_len"] = sequence_length
-        config = dataclasses.replace(config, **changes) if changes else config
+        config = with_run_constants(config, vocab_size, sequence_length)  # the reference's run constants
         if config.seq_len < 2:
             raise ValueError("sequence_length must be at least 2 for next-token loss")
         self.config = config
