@@ -27,6 +27,7 @@ kept and the digest is agreed over the ranks' local shard digests.
 
 from __future__ import annotations
 
+from collections.abc import Mapping
 from dataclasses import dataclass, field
 from hashlib import sha256
 
@@ -422,7 +423,7 @@ def _load_anchor(checkpoint_path):
     return anchor, payload["completed_steps"], payload["digest"]
 
 
-class InitialAnchor(dict):
+class InitialAnchor(Mapping):
     """The seeded initial state as a checkpoint anchor (``{name: {"param"}}``, no moments,
     zero completed steps), built name by name as recovery asks for it.
 
@@ -432,33 +433,30 @@ class InitialAnchor(dict):
     """
 
     def __init__(self, config, device=None):
-        super().__init__()
         self.config = config
         # drawn where the run drew it (a CUDA generator's numbers differ from the CPU's), kept on the host
         self.device = torch.device("cpu") if device is None else torch.device(device)
-        self.names = {s.name for s in model_specs(config)}
+        self.names = [s.name for s in model_specs(config)]
         self.digest = sha256(("initial-state:" + repr(sorted(identity(config).items()))).encode("utf-8")).hexdigest()
-
-    def _build(self, name: str) -> None:
-        from .models.init import initial_state
-
-        # GPT-2 blocks are drawn from one generator in module order: build them all once
-        wanted = None if self.config.arch == "gpt2" else [name]
-        for n, t in initial_state(self.config, names=wanted, device=self.device).items():
-            dict.setdefault(self, n, {"param": t.cpu()})
-
-    def get(self, name, default=None):
-        if name not in self.names:
-            return default
-        if not dict.__contains__(self, name):
-            self._build(name)
-        return dict.__getitem__(self, name)
+        self._built: dict[str, dict] = {}
 
     def __getitem__(self, name):
-        entry = self.get(name)
-        if entry is None:
-            raise KeyError(name)
-        return entry
+        if name not in self._built:
+            if name not in self.names:
+                raise KeyError(name)
+            from .models.init import initial_state
+
+            # GPT-2 blocks are drawn from one generator in module order: build them all once
+            wanted = None if self.config.arch == "gpt2" else [name]
+            for n, t in initial_state(self.config, names=wanted, device=self.device).items():
+                self._built.setdefault(n, {"param": t.cpu()})
+        return self._built[name]
+
+    def __iter__(self):
+        return iter(self.names)
+
+    def __len__(self):
+        return len(self.names)
 
 
 def state_fingerprint(run) -> str:
