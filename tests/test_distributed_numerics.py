@@ -51,6 +51,7 @@ LAYOUTS = [
     dict(tp=2, pp=2, dp=1, sequence_parallel=True, tied_embeddings=True),
     dict(tp=2, pp=2, dp=2),
     dict(tp=2, pp=2, dp=1, sequence_parallel=True, recompute=True),
+    dict(tp=2, pp=2, dp=2, arch="gpt2", num_kv_heads=None, ffn_dim=None),  # the reference's blocks, distributed
 ]
 
 
