@@ -203,6 +203,9 @@ def check_train(config: TrainConfig) -> None:
         raise ConfigError(f"{what} field num_heads must be divisible by num_kv_heads")
     if config.arch == "gpt2" and config.kv_heads != config.num_heads:
         raise ConfigError(f"{what}: gpt2 blocks have no grouped-query attention")
+    if config.arch == "gpt2" and config.sequence_parallel:
+        raise ConfigError(f"{what}: sequence_parallel needs llama blocks (gpt2 blocks run the reference's "
+                          "all-reduce tensor parallelism)")
     if config.seq_len < 2:
         raise ConfigError(f"{what} field seq_len must be at least 2 for next-token loss")
     if config.beta1 >= 1 or config.beta2 >= 1:

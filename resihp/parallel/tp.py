@@ -185,6 +185,8 @@ class TensorParallelStage:
         self.vocab_per_rank = config.vocab_size // self.tp_size
         self.vocab_start = self.tp_rank * self.vocab_per_rank
         self.sp = bool(config.sequence_parallel) and self.tp_size > 1
+        if self.sp and config.arch == "gpt2":
+            raise ValueError("sequence parallelism needs llama blocks; gpt2 blocks use all-reduce TP")
         if config.vocab_size % self.tp_size:
             raise ValueError("tp_size must divide vocab_size")
         if config.num_heads % self.tp_size or config.kv_heads % self.tp_size:

@@ -26,7 +26,8 @@ def test_reference_files_load_unchanged(tmp_path):
 
 
 @pytest.mark.parametrize("bad", [{"model_dim": 0}, {"tp": True}, {"seed": -1}, {"batch_size": 7}, {"num_heads": 7},
-                                 {"surprise": 1}, {"arch": "bert"}, {"dtype": "fp8"}, {"num_kv_heads": 3, "arch": "llama"}])
+                                 {"surprise": 1}, {"arch": "bert"}, {"dtype": "fp8"}, {"num_kv_heads": 3, "arch": "llama"},
+                                 {"sequence_parallel": True}])
 def test_rejects_invalid_train(bad):
     with pytest.raises(ConfigError):
         parse_train(dict(BASE, **bad))
