@@ -83,6 +83,61 @@ class _ScatterTokens(Function):
         return _all_gather_rows(grad, ctx.group), None
 
 
+class _ColumnParallelLinear(Function):
+    """``gather_tokens(h) @ w.T`` (SP) or ``copy_to_tp(h) @ w.T``, with the backward's
+    input-gradient collective overlapped with the weight-gradient product.
+
+    Megatron's order: the input gradient is computed first and its reduce-scatter (SP)
+    or all-reduce is started asynchronously; the weight gradient -- which needs no
+    communication -- runs while it is in flight; the collective is awaited last. The
+    sums are the same as with the collective after both products.
+    """
+
+    @staticmethod
+    def forward(ctx, h, w, main_grad, group, sp):
+        from ..ops import functional as fn
+
+        x = _all_gather_rows(h, group) if sp else h
+        ctx.save_for_backward(x, w)
+        ctx.main_grad, ctx.group, ctx.sp = main_grad, group, sp
+        ctx.kernel = fn.on_kernels(x)
+        return fn.linear(x, w) if not ctx.kernel else _kernel_linear(x, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops.gemm import linear_dgrad, linear_wgrad
+
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = linear_dgrad(dy, w)
+        n = dist.get_world_size(ctx.group)
+        if ctx.sp:
+            out = torch.empty((dx.shape[0] // n,) + tuple(dx.shape[1:]), dtype=dx.dtype, device=dx.device)
+            work = dist.reduce_scatter_tensor(out, dx.contiguous(), group=ctx.group, async_op=True)
+        else:
+            out = dx.contiguous()
+            work = dist.all_reduce(out, group=ctx.group, async_op=True)
+        dw = None
+        if ctx.kernel:
+            if ctx.main_grad is not None:
+                linear_wgrad(dy, x, out=ctx.main_grad, accumulate=True)
+        elif ctx.needs_input_grad[1]:
+            dw = linear_wgrad(dy, x).to(w.dtype)
+        work.wait()
+        return out, dw, None, None, None
+
+
+def _kernel_linear(x, w):
+    from ..ops.gemm import linear
+
+    return linear(x, w)
+
+
+def column_parallel_linear(h, w, main_grad, group, sp: bool):
+    """The column-parallel linear of a TP group of two or more (see :class:`_ColumnParallelLinear`)."""
+    return _ColumnParallelLinear.apply(h, w, main_grad, group, sp)
+
+
 def copy_to_tp(x, group):
     return x if tp_size(group) == 1 else _Copy.apply(x, group)
 

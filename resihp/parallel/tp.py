@@ -334,16 +334,15 @@ class TensorParallelStage:
         """Column-parallel linear; under SP the token all-gather is fused into the GEMM."""
         if self.ws is not None:
             return fused.ag_linear(h, w, g, self.ws)
-        return fn.linear(self._col_input(h), w, g)
+        if self.tp_size > 1:  # the input-gradient collective overlaps the weight gradient
+            return cc.column_parallel_linear(h, w, g, self.group, self.sp)
+        return fn.linear(h, w, g)
 
     def _row_linear(self, x, w, g):
         """Row-parallel linear; under SP the token reduce-scatter is fused into the GEMM."""
         if self.ws is not None:
             return fused.linear_rs(x, w, g, self.ws)
         return self._row_output(fn.linear(x, w, g))
-
-    def _col_input(self, h):
-        return cc.gather_tokens(h, self.group) if self.sp else cc.copy_to_tp(h, self.group)
 
     def _row_output(self, y):
         return cc.scatter_tokens(y, self.group) if self.sp else cc.reduce_from_tp(y, self.group)
