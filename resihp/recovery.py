@@ -434,23 +434,27 @@ class InitialAnchor(Mapping):
 
     def __init__(self, config, device=None):
         self.config = config
-        # drawn where the run drew it (a CUDA generator's numbers differ from the CPU's), kept on the host
+        # the initial state does not depend on the device it is drawn for; kept on the host
         self.device = torch.device("cpu") if device is None else torch.device(device)
         self.names = [s.name for s in model_specs(config)]
+        self._known = frozenset(self.names)
         self.digest = sha256(("initial-state:" + repr(sorted(identity(config).items()))).encode("utf-8")).hexdigest()
         self._built: dict[str, dict] = {}
 
     def __getitem__(self, name):
         if name not in self._built:
-            if name not in self.names:
+            if name not in self._known:
                 raise KeyError(name)
             from .models.init import initial_state
 
             # GPT-2 blocks are drawn from one generator in module order: build them all once
             wanted = None if self.config.arch == "gpt2" else [name]
-            for n, t in initial_state(self.config, names=wanted, device=self.device).items():
-                self._built.setdefault(n, {"param": t.cpu()})
+            for n, t in initial_state(self.config, names=wanted).items():  # the same values on any device
+                self._built.setdefault(n, {"param": t})
         return self._built[name]
+
+    def __contains__(self, name):
+        return name in self._known  # a membership test draws nothing
 
     def __iter__(self):
         return iter(self.names)

@@ -35,6 +35,7 @@ def test_bf16_model_gradients_match_the_fp32_module(extra):
     assert run.stage.kernel  # the sm_100a path, not the torch fallback
     tokens = run.batches[0]
     stage = run.stage
+    start = {n: v.detach().float().cpu().clone() for n, v in stage.logical_state_dict().items()}
     stage.zero_grad()
     b, s = tokens.shape
     loss = stage.forward(tokens=tokens.cuda(), loss_scale=1.0 / (b * (s - 1)))
@@ -44,6 +45,9 @@ def test_bf16_model_gradients_match_the_fp32_module(extra):
     grads = {n: stage.g[n].detach().float().cpu() for n in stage.logical_state_dict()}
 
     module = ReferenceTransformer(TrainConfig(**SHAPE, **extra))
+    for name, param in module.logical_state_dict().items():
+        assert torch.equal(param.detach(), start[name]), name  # one initial model on both devices
+    module.load_logical_state(start)
     want = module.loss(tokens)
     want.backward()
     assert abs(loss.item() - want.item()) <= 1e-2 * want.item(), (loss.item(), want.item())
@@ -66,3 +70,23 @@ def test_fp32_reference_runs_on_cuda_like_on_cpu(arch):
     for _ in range(3):
         a, b = cpu.step(), gpu.step()
         assert abs(a.loss - b.loss) <= 1e-4 * abs(a.loss), (a.loss, b.loss)
+
+
+@pytest.mark.parametrize("arch", ["gpt2", "llama"])
+def test_initial_state_does_not_depend_on_the_device(arch):
+    """One seed gives one initial model whether a run trains on the CPU or a GPU (the
+    CPU oracle then validates a GPU run of the same config)."""
+    from resihp.models.init import DRAW_PIECE, initial_state
+
+    extra = dict(ffn_dim=512, num_heads=2) if arch == "llama" else dict(num_heads=4)
+    config = TrainConfig(**dict(SHAPE, **extra, arch=arch))
+    cpu, gpu = initial_state(config), initial_state(config, device="cuda:0")
+    assert cpu.keys() == gpu.keys()
+    for name in cpu:
+        assert gpu[name].device.type == "cuda"
+        assert torch.equal(cpu[name], gpu[name].cpu()), name
+    if arch == "llama":  # a tensor larger than one draw piece, drawn in pieces
+        big = TrainConfig(**dict(SHAPE, **extra, arch=arch, vocab_size=DRAW_PIECE // 256 + 64))
+        a = initial_state(big, names=["token_embedding.weight"])["token_embedding.weight"]
+        b = initial_state(big, names=["token_embedding.weight"], device="cuda:0")["token_embedding.weight"]
+        assert a.numel() > DRAW_PIECE and torch.equal(a, b.cpu())
