@@ -98,7 +98,7 @@ def test_each_corruption_is_its_own_root_cause(tmp_path):
         load_anchor(path)
 
 
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+@pytest.mark.reference
 def test_reference_reads_our_checkpoint(tmp_path):
     path, run = _saved(tmp_path, steps=2)
     code = (
@@ -133,7 +133,7 @@ def test_background_writer_orders_writes_and_surfaces_errors(tmp_path):
     writer.flush()  # the error is reported once
 
 
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+@pytest.mark.reference
 def test_we_read_the_references_checkpoint(tmp_path):
     """A checkpoint the reference wrote (after two of its own steps) loads and validates
     here for the same configuration, names, step and values included."""

@@ -2,7 +2,8 @@
 
 The reference installed under ``baseline/_ref`` is run in a subprocess (both packages
 are named ``resihp``), on the same random scenarios, and every plan digest and stop code
-along each failure sequence must agree. Skipped when the reference is not installed.
+along each failure sequence must agree. Skipped when the reference is not installed
+(a failure instead with ``RESIHP_REQUIRE_REFERENCE=1``).
 """
 
 import json
@@ -29,7 +30,7 @@ print(json.dumps([plan_scenarios.replay(config, plan, s) for s in plan_scenarios
 """
 
 
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+@pytest.mark.reference
 def test_digests_match_reference_planner():
     tests_dir = os.path.dirname(os.path.abspath(__file__))
     env = {k: v for k, v in os.environ.items() if k != "PYTHONPATH"}

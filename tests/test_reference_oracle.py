@@ -11,7 +11,8 @@
   names in the same order, its initial weights bit for bit, and its logits.
 
 The reference is imported from ``baseline/_ref`` in a subprocess (both packages are
-named ``resihp``); those tests skip when it is not installed.
+named ``resihp``); those tests skip when it is not installed (fail with
+``RESIHP_REQUIRE_REFERENCE=1``).
 """
 
 import json
@@ -27,7 +28,7 @@ from resihp.reference import ReferenceRun, token_stream
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "baseline", "_ref")
-needs_ref = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "resihp")), reason="reference not installed")
+needs_ref = pytest.mark.reference
 
 SHAPE = dict(model_dim=32, num_layers=2, num_heads=4, batch_size=4, micro_batch_size=2, seed=3, tp=1, pp=1, dp=1,
              iterations=4)
