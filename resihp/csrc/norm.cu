@@ -249,6 +249,12 @@ cudaError_t noalloc_scratch(float** out) {
   return cudaSuccess;
 }
 
+void forget_scratch(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  g_scratch_ptr[dev] = nullptr;
+}
+
 bool width_supported(int d) {
   if (d <= 0 || d % 8 != 0 || d / 8 > 1024) return false;
   const int lanes = d / 8;
@@ -264,6 +270,9 @@ extern "C" __attribute__((visibility("default"))) int resihp_rmsnorm_bwd_noalloc
   if (dy == nullptr || s == nullptr || w == nullptr || rstd == nullptr || ds == nullptr || dw == nullptr || rows < 1 ||
       !width_supported(d))
     return RESIHP_NOALLOC_BAD_ARGUMENT;
+  // An error left by an earlier, unrelated call stays with its owner: report it as such
+  // without reading (and so clearing) it, and launch nothing.
+  if (cudaPeekAtLastError() != cudaSuccess) return RESIHP_NOALLOC_PENDING_ERROR;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
@@ -285,6 +294,10 @@ extern "C" __attribute__((visibility("default"))) int resihp_rmsnorm_bwd_noalloc
   return RESIHP_NOALLOC_OK;
 }
 
+extern "C" __attribute__((visibility("default"))) void resihp_noalloc_forget_device(int device) {
+  forget_scratch(device);
+}
+
 extern "C" __attribute__((visibility("default"))) const char* resihp_noalloc_strerror(int code) {
   switch (code) {
     case RESIHP_NOALLOC_OK: return "ok";
@@ -292,6 +305,8 @@ extern "C" __attribute__((visibility("default"))) const char* resihp_noalloc_str
     case RESIHP_NOALLOC_TOO_LARGE:
       return "scratch need exceeds the built-in 16 MiB (RESIHP_NOALLOC_SCRATCH_FLOATS) scratch array";
     case RESIHP_NOALLOC_CUDA_ERROR: return "a CUDA runtime call or kernel launch failed";
+    case RESIHP_NOALLOC_PENDING_ERROR:
+      return "an earlier CUDA error was pending on this thread; nothing was launched and the error is left in place";
     default: return "unknown error code";
   }
 }

@@ -71,3 +71,27 @@ def test_noalloc_rejects_bad_sizes():
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     code = lib.resihp_rmsnorm_bwd_noalloc(_ptr(dy), _ptr(s), _ptr(w), _ptr(rstd), None, _ptr(ds), _ptr(dw), 0, 8, 100, stream)
     assert code == 1 and b"unsupported width" in lib.resihp_noalloc_strerror(code)
+
+
+def test_noalloc_leaves_an_earlier_error_to_its_owner():
+    """A CUDA error pending from an unrelated earlier call (here a host-side one: an
+    invalid device ordinal) is neither reported as this entry point's failure nor
+    cleared: the call returns the pending-error code and launches nothing."""
+    lib = _lib()
+    cudart = ctypes.CDLL("libcudart.so.12")  # the runtime instance the extension uses
+    cudart.cudaSetDevice.argtypes = [ctypes.c_int]
+    cudart.cudaSetDevice.restype = ctypes.c_int
+    cudart.cudaGetLastError.restype = ctypes.c_int
+    dy, s, w, rstd, _ = _inputs(8, 256, seed=2)
+    ds = torch.zeros_like(dy)
+    dw = torch.zeros(256, device="cuda")
+    torch.cuda.synchronize()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert cudart.cudaSetDevice(1 << 20) != 0  # leaves cudaErrorInvalidDevice pending
+    code = lib.resihp_rmsnorm_bwd_noalloc(_ptr(dy), _ptr(s), _ptr(w), _ptr(rstd), None, _ptr(ds), _ptr(dw), 0, 8, 256,
+                                          stream)
+    pending = cudart.cudaGetLastError()  # still there for its owner, then cleared
+    assert code == 4 and b"pending" in lib.resihp_noalloc_strerror(code)
+    assert pending != 0 and cudart.cudaGetLastError() == 0
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(ds) == 0 and torch.count_nonzero(dw) == 0  # nothing ran
