@@ -17,7 +17,9 @@
 namespace resihp {
 
 // Wait budget for one barrier phase. Generous on purpose: a healthy wait is
-// microseconds; this only has to be short enough to turn a bug into an error.
+// microseconds; this only has to be short enough to turn a bug into an error. Waits on
+// another GPU's flags take their budget from the launch instead (``peer_wait_budget_ns``
+// on the host, default the same 4 s), so a test can make such a wait run out quickly.
 constexpr uint64_t kWaitBudgetNs = 4000000000ull;
 
 enum ErrorCode : int {
@@ -288,12 +290,12 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Wait until *p >= target (wrap-safe); false + error code when the budget runs out.
-__device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int* err, int code) {
+// Wait until *p >= target (wrap-safe); false + error code when ``budget_ns`` runs out.
+__device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int* err, int code, uint64_t budget_ns) {
   const uint64_t start = globaltimer();
   #pragma unroll 1
   while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
-    if (globaltimer() - start > kWaitBudgetNs) {
+    if (globaltimer() - start > budget_ns) {
       record_error(err, code);
       return false;
     }

@@ -92,13 +92,15 @@ struct FusedArgs {
   int64_t ldc;
   int m, n, k;
   int* err;
+  uint64_t wait_ns;  // budget of each wait on a peer's flag or a pull counter
   CommArgs comm;
 };
 
 // One lane waits, the whole warp learns the outcome.
-__device__ __forceinline__ bool warp_wait_geq(const unsigned* p, unsigned target, int* err, int lane) {
+__device__ __forceinline__ bool warp_wait_geq(const unsigned* p, unsigned target, int* err, int lane,
+                                              uint64_t budget_ns) {
   int ok = 1;
-  if (lane == 0) ok = wait_geq(p, target, err, kErrPeerWait) ? 1 : 0;
+  if (lane == 0) ok = wait_geq(p, target, err, kErrPeerWait, budget_ns) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -233,8 +235,8 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
           // V = 0: the whole peer chunk; V = 1: only this tile's 128-row block
           const int key = V == 0 ? chunk : chunk * tiles_m_chunk + (m0 - chunk * cm.rows_per_rank) / kFBM;
           if (key != ready_key) {
-            const bool arrived = V == 0 ? wait_geq(cm.ready + key, cm.ready_target, g.err, kErrPeerWait)
-                                        : wait_geq(cm.rb_ready + key, cm.rb_target, g.err, kErrPeerWait);
+            const bool arrived = V == 0 ? wait_geq(cm.ready + key, cm.ready_target, g.err, kErrPeerWait, g.wait_ns)
+                                        : wait_geq(cm.rb_ready + key, cm.rb_target, g.err, kErrPeerWait, g.wait_ns);
             if (!arrived) { ok = false; break; }
             fence_proxy_async_global();
             ready_key = key;
@@ -410,7 +412,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
         // pull: this CTA's rows of every peer chunk
         for (int p = 1; p < cm.tp && ok; ++p) {
           const int chunk = (cm.rank + p) % cm.tp;
-          ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
+          ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane, g.wait_ns);
           if (!ok) break;
           copy_rows<kCT, kCU>(
               reinterpret_cast<uint4*>(cm.xg + (int64_t(chunk) * cm.rows_per_rank + lo) * cm.ldx), cols16,
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
           const int rb = (u / slices) % blocks;
           const int r0 = rb * kFBM + (u % slices) * srows;
           if (chunk != announced) {
-            ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane);
+            ok = warp_wait_geq(cm.sig_ag + chunk, cm.epoch, g.err, lane, g.wait_ns);
             if (!ok) break;
             announced = chunk;
           }
@@ -460,7 +462,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
         if (V == 0) {
           for (int src = 0; src < cm.tp && ok; ++src) {
             if (src == cm.rank) continue;
-            ok = warp_wait_geq(cm.peer_flag[src] + flag, cm.flag_target, g.err, lane);
+            ok = warp_wait_geq(cm.peer_flag[src] + flag, cm.flag_target, g.err, lane, g.wait_ns);
             if (!ok) break;
             const uint4* from = reinterpret_cast<const uint4*>(cm.peer_part[src] + int64_t(m0) * g.n + tn * BN);
             uint4* to = reinterpret_cast<uint4*>(cm.recv + (int64_t(src) * cm.rows_per_rank + lrow0) * g.n + tn * BN);
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(CopyCfg<V>::kThreads, 1)
               for (int src = 0; src < cm.tp && got < 0; ++src)
                 if ((pending >> src & 1u) && static_cast<int>(ld_acquire_sys(cm.peer_flag[src] + flag) - cm.flag_target) >= 0)
                   got = src;
-              if (got < 0 && globaltimer() - start > kWaitBudgetNs) {
+              if (got < 0 && globaltimer() - start > g.wait_ns) {
                 record_error(g.err, kErrPeerWait);
                 got = -2;
               }
@@ -590,6 +592,7 @@ void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, 
   g.n = n;
   g.k = k;
   g.err = err;
+  g.wait_ns = peer_wait_budget_ns();
   CommArgs& c = g.comm;
   c.rank = rank;
   c.tp = tp;
@@ -633,6 +636,7 @@ void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local
   g.n = n;
   g.k = k;
   g.err = err;
+  g.wait_ns = peer_wait_budget_ns();
   CommArgs& c = g.comm;
   c.rank = rank;
   c.tp = tp;

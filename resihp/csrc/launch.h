@@ -39,6 +39,14 @@ inline void append(std::string& o, const T& v, const R&... r) {
     RESIHP_CHECK(_e == cudaSuccess, #expr, " failed: ", cudaGetErrorString(_e));        \
   } while (0)
 
+// Budget of every wait on another GPU's flag inside a kernel, in nanoseconds (default
+// 4 s). The host reads it at each launch of a kernel that waits on peers and passes it
+// as a launch argument; a wait that runs out records kErrPeerWait in the device's error
+// word and the kernel returns. Tests shorten it to make a wait that nothing completes
+// end quickly.
+uint64_t peer_wait_budget_ns();
+void set_peer_wait_budget_ns(uint64_t ns);
+
 // AdamW coefficients of one step (bias corrections folded in on the host, in double).
 struct AdamWCoef {
   float lr, b1, b2, eps, wd, step_size, bc2_sqrt, grad_scale;

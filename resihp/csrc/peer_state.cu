@@ -16,12 +16,24 @@
 //   of it from the donors' regions with the re-partition (new TP degree, shard dim 0 or 1)
 //   folded into the copy descriptors, and writes the bf16 compute copy of the master
 //   weights in the same pass.
+#include <atomic>
 #include <cuda_bf16.h>
 
 #include "common.cuh"
 #include "launch.h"
 
 namespace resihp {
+
+namespace {
+std::atomic<uint64_t> g_peer_wait_budget_ns{kWaitBudgetNs};
+}  // namespace
+
+uint64_t peer_wait_budget_ns() { return g_peer_wait_budget_ns.load(std::memory_order_relaxed); }
+
+void set_peer_wait_budget_ns(uint64_t ns) {
+  RESIHP_CHECK(ns > 0, "peer wait budget must be positive");
+  g_peer_wait_budget_ns.store(ns, std::memory_order_relaxed);
+}
 
 // ---- fused DP all-reduce + AdamW -----------------------------------------------------
 
@@ -47,6 +59,7 @@ struct DpArgs {
   int64_t n4, per_cta;
   AdamWCoef c;
   int* err;
+  uint64_t wait_ns;            // budget of each wait on a peer's flag
 };
 
 __device__ __forceinline__ float4 ld_cg_f4(const float4* p) { return __ldcg(p); }
@@ -79,7 +92,7 @@ __global__ void __launch_bounds__(kDpThreads) dp_adamw_kernel(const __grid_const
     for (int q = 0; q < a.dp; ++q)
       if (q != a.me) st_release_sys(a.flags_peer[q] + blockIdx.x * kMaxDp + a.me, a.epoch);
     for (int q = 0; q < a.dp && good; ++q)
-      if (q != a.me && !wait_geq(a.flags_local + blockIdx.x * kMaxDp + q, a.epoch, a.err, kErrPeerWait)) good = 0;
+      if (q != a.me && !wait_geq(a.flags_local + blockIdx.x * kMaxDp + q, a.epoch, a.err, kErrPeerWait, a.wait_ns)) good = 0;
     ok = good;
   }
   __syncthreads();
@@ -157,6 +170,7 @@ void dp_allreduce_adamw(const float* const* grads, int dp, int me, float* sum_ou
   a.per_cta = (a.n4 + grid - 1) / grid;
   a.c = coef;
   a.err = err;
+  a.wait_ns = peer_wait_budget_ns();
   if (dp <= 2) dp_adamw_kernel<2><<<grid, kDpThreads, 0, st>>>(a);
   else if (dp <= 4) dp_adamw_kernel<4><<<grid, kDpThreads, 0, st>>>(a);
   else dp_adamw_kernel<8><<<grid, kDpThreads, 0, st>>>(a);

@@ -448,6 +448,10 @@ void reshard_gather_t(torch::Tensor descs, int64_t items) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "resihp sm_100a kernels";
   m.def("read_and_clear_error", &resihp::read_and_clear_error, "synchronising read+reset of the kernel error word");
+  m.def("peer_wait_budget_ns", [] { return int64_t(resihp::peer_wait_budget_ns()); },
+        "budget of each in-kernel wait on another GPU's flag (ns)");
+  m.def("set_peer_wait_budget_ns", [](int64_t ns) { resihp::set_peer_wait_budget_ns(uint64_t(ns)); },
+        "set the budget of each in-kernel wait on another GPU's flag (ns)");
   m.def("gemm", &resihp::gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c"), py::arg("epi"), py::arg("alpha") = 1.0, py::arg("residual") = py::none(),
         py::arg("max_ctas") = 0, py::arg("force_bn") = 0);

@@ -5,4 +5,4 @@ CPU tensors; there is no other path.
 """
 
 from . import _ext  # noqa: F401
-from .gemm import check_device_errors, linear, linear_dgrad, linear_wgrad  # noqa: F401
+from .gemm import KernelError, check_device_errors, linear, linear_dgrad, linear_wgrad  # noqa: F401

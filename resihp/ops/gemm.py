@@ -84,11 +84,34 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = N
     return out
 
 
+#: Codes a kernel records in its device's error word (``ErrorCode`` in csrc/common.cuh).
+ERROR_CODES = {
+    1: "TMA producer waited past its budget for a free shared-memory stage",
+    2: "MMA issuer waited past its budget for a filled stage or a free accumulator",
+    3: "epilogue waited past its budget for a finished accumulator",
+    4: "a wait on another GPU's flag ran out its budget (peer never arrived)",
+    5: "a bounds check of the checked build skipped an access",
+}
+PEER_WAIT = 4
+
+
+class KernelError(RuntimeError):
+    """A kernel reported an error code (a bounded wait that ran out, a failed bounds
+    check) instead of hanging or faulting; ``code`` is the recorded code."""
+
+    def __init__(self, code: int, device_index: int):
+        self.code = int(code)
+        self.device_index = int(device_index)
+        what = ERROR_CODES.get(self.code, "unknown error code")
+        super().__init__(f"resihp kernel reported error code {self.code} on cuda:{self.device_index}: {what}")
+
+
 def check_device_errors(device: torch.device | int | None = None) -> None:
-    """Raise if any kernel on ``device`` reported a timed-out wait or a bounds error."""
+    """Raise :class:`KernelError` if any kernel on ``device`` reported a timed-out wait
+    or a bounds error since the last check (the word is cleared by the read)."""
     if not torch.cuda.is_available():
         return
     index = torch.cuda.current_device() if device is None else torch.device("cuda", device).index if isinstance(device, int) else (device.index or 0)
     code = _ext.require().read_and_clear_error(index)
     if code:
-        raise RuntimeError(f"resihp kernel reported error code {code} on cuda:{index}")
+        raise KernelError(code, index)

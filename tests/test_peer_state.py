@@ -68,6 +68,51 @@ def test_dp_kernel_matches_sum_then_adamw():
     torch.testing.assert_close(a.exp_avg_sq.cpu(), cpu[2], rtol=1e-6, atol=0)
 
 
+def test_dp_kernel_reports_a_peer_that_never_arrives():
+    """Failure detection on the device, with no fault: the emulated DP peer never flags
+    its gradients, the per-launch wait budget is short (50 ms), and the kernel gives up,
+    records the peer-wait code and returns without touching the state; the host turns
+    the code into a :class:`KernelError`, and the same context runs the kernel
+    correctly afterwards."""
+    import time
+
+    from resihp.ops import KernelError, _ext, check_device_errors
+
+    k = _ext.require()
+    dev = torch.device("cuda", 0)
+    a, b = _flat([(4096, 64)], dev), _flat([(4096, 64)], dev)
+    a.grads[0].fill_(1.0)
+    b.grads[0].fill_(2.0)
+    a.master.fill_(0.5)
+    before = a.master.clone()
+    grid = k.dp_grid(a.numel, 0)
+    args = lambda epoch: ([a.grads[0].data_ptr(), b.grads[0].data_ptr()], 0, a.grads[1], a.master, a.exp_avg,  # noqa: E731
+                          a.exp_avg_sq, a.work, 1e-3, 0.9, 0.95, 1e-8, 0.0, 1, 1.0, a.region_ptr,
+                          [a.region_ptr, b.region_ptr], epoch, grid)
+    check_device_errors(0)
+    default = k.peer_wait_budget_ns()
+    k.set_peer_wait_budget_ns(50_000_000)
+    try:
+        t0 = time.perf_counter()
+        k.dp_allreduce_adamw(*args(9))  # nothing ever sets the peer's epoch-9 flag
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+    finally:
+        k.set_peer_wait_budget_ns(default)
+    with pytest.raises(KernelError) as info:
+        check_device_errors(0)
+    assert info.value.code == 4 and "peer" in str(info.value)
+    assert 0.04 <= waited < 3.0, waited  # gave up after its budget, not the 4 s default
+    assert torch.equal(a.master, before)  # the step did not run
+    check_device_errors(0)  # the word was cleared by the read
+
+    a.flags.view(-1, 8)[:grid, 1] = 10  # now the peer has arrived
+    k.dp_allreduce_adamw(*args(10))
+    torch.cuda.synchronize()
+    check_device_errors(0)
+    assert torch.equal(a.grads[1], torch.full_like(a.grads[1], 3.0))
+
+
 def test_reshard_gather_reproduces_local_slices():
     from resihp.ops import check_device_errors
     from resihp.parallel.peer import GatherPlan, shard_pieces
