@@ -1,20 +1,28 @@
 """Deterministic data-parallel micro-batch assignment.
 
-``assign(step, failure_signature, topology)`` is a pure function with the reference's
-semantics (``resihp/planner/dp.py:150-218``):
+``assign(step, failure_signature, topology)`` is pure and keeps the reference's
+semantics (``resihp/planner/dp.py:150-218``; the plan digest depends on them):
 
-* a replica is a candidate only when no stage of its pipeline holds a failed rank;
-* its capacity is the minimum over its stages of the memory gate -- the stage's own
-  micro-batch capacity (default: all of them) or 0 when the memory model rejects the
-  stage at its 1F1B position -- and a zero-capacity replica is dropped;
-* micro-batches are split across candidates in proportion to capacity by largest
-  remainder (ties to the lower candidate index), and numbered contiguously replica by
-  replica, so each micro-batch flows through exactly one replica's whole pipeline.
+* a replica can take work only if no stage of its pipeline holds a failed rank;
+* its capacity is the smallest stage capacity along its pipeline, where a stage's
+  capacity is its own micro-batch bound (default: all of them) or 0 when the memory
+  model rejects the stage at its 1F1B position; a replica of capacity 0 takes nothing;
+* the step's micro-batches are apportioned over the capacity vector by the
+  largest-remainder (Hamilton) method, equal remainders favouring the lower replica;
+* micro-batch ids are consecutive ranges handed out replica by replica in replica
+  order, and each micro-batch runs through every stage of its one replica.
+
+The formulation here is vector-shaped: the topology is folded into one pipeline per
+replica, every pipeline is reduced to one capacity (0 = excluded), and placements are
+generated from the apportioned counts already in ``(micro_batch, stage_id)`` order.
 """
 
 from __future__ import annotations
 
+from collections import Counter
 from dataclasses import dataclass
+from itertools import groupby
+from operator import attrgetter
 from typing import Iterable
 
 from ..config import TrainConfig
@@ -63,17 +71,15 @@ class DPAssignment:
 
     @property
     def by_micro_batch(self) -> dict[int, tuple[DPPlacement, ...]]:
-        out: dict[int, list[DPPlacement]] = {}
-        for p in self.placements:
-            out.setdefault(p.micro_batch, []).append(p)
-        return {k: tuple(v) for k, v in out.items()}
+        """Placements of each micro-batch (ascending ids), in placement order."""
+        ordered = sorted(self.placements, key=attrgetter("micro_batch"))  # stable
+        return {mb: tuple(group) for mb, group in groupby(ordered, key=attrgetter("micro_batch"))}
 
     @property
     def micro_batches_per_replica(self) -> dict[int, int]:
-        seen: dict[int, set[int]] = {}
-        for p in self.placements:
-            seen.setdefault(p.replica_id, set()).add(p.micro_batch)
-        return {r: len(m) for r, m in seen.items()}
+        """Distinct micro-batches each replica runs (ascending replica ids)."""
+        runs = Counter(replica for replica, _ in {(p.replica_id, p.micro_batch) for p in self.placements})
+        return dict(sorted(runs.items()))
 
 
 @dataclass(frozen=True)
@@ -90,34 +96,40 @@ class InfeasibleDP(ValueError):
         self.reason = reason
 
 
-def _check(topology: DPTopology) -> None:
+def _validated(topology) -> DPTopology:
+    """The topology, after every structural rule is checked (first violation raises)."""
     if not isinstance(topology, DPTopology):
-        raise TypeError("active_topology must be a DPTopology")
-    positive_int("micro_batches", topology.micro_batches)
-    positive_int("sequence_length", topology.sequence_length)
-    positive_int("vocab_size", topology.vocab_size)
+        raise TypeError(f"expected a DPTopology, got {type(topology).__name__}")
+    for name in ("micro_batches", "sequence_length", "vocab_size"):
+        positive_int(name, getattr(topology, name))
     if topology.memory_budget is not None:
         positive_int("memory_budget", topology.memory_budget)
-    if not topology.stages:
-        raise ValueError("active_topology must contain at least one stage")
-    keys: set[tuple[int, int]] = set()
-    for s in topology.stages:
-        non_negative_int("replica_id", s.replica_id)
-        non_negative_int("stage_id", s.stage_id)
-        positive_int("stage_layers", s.stage_layers)
-        positive_int("tp_degree", s.tp_degree)
-        if len(unique_ranks("stage ranks", s.ranks)) != s.tp_degree:
-            raise ValueError("stage ranks length must equal tp_degree")
-        if (s.replica_id, s.stage_id) in keys:
-            raise ValueError("active_topology contains duplicate replica/stage")
-        keys.add((s.replica_id, s.stage_id))
-        if s.capacity is not None:
-            positive_int("capacity", s.capacity)
+    if len(topology.stages) == 0:
+        raise ValueError("a DP topology needs at least one stage")
+    keys = [(s.replica_id, s.stage_id) for s in topology.stages]
+    for stage in topology.stages:
+        non_negative_int("replica_id", stage.replica_id)
+        non_negative_int("stage_id", stage.stage_id)
+        positive_int("stage_layers", stage.stage_layers)
+        positive_int("tp_degree", stage.tp_degree)
+        held = unique_ranks("stage ranks", stage.ranks)
+        if len(held) != stage.tp_degree:
+            raise ValueError(f"stage {stage.stage_id} of replica {stage.replica_id} lists {len(held)} ranks "
+                             f"for TP degree {stage.tp_degree}")
+        if keys.count((stage.replica_id, stage.stage_id)) > 1:
+            raise ValueError(f"stage {stage.stage_id} of replica {stage.replica_id} appears more than once")
+        if stage.capacity is not None:
+            positive_int("capacity", stage.capacity)
+    return topology
 
 
 def stage_capacity(topology: DPTopology, stage: DPStage, *, index: int, num_stages: int) -> int:
-    """Micro-batches ``stage`` can take at pipeline position ``index`` (0 = rejected)."""
-    if topology.memory_budget is not None and not memory_feasible(
+    """Micro-batches ``stage`` can take at pipeline position ``index`` (0 = rejected by
+    the memory model, replaying its 1F1B in-flight peak at that position)."""
+    bound = topology.micro_batches if stage.capacity is None else stage.capacity
+    if topology.memory_budget is None:
+        return bound
+    fits = memory_feasible(
         topology.config,
         tp_degree=stage.tp_degree,
         stage_layers=stage.stage_layers,
@@ -126,57 +138,59 @@ def stage_capacity(topology: DPTopology, stage: DPStage, *, index: int, num_stag
         vocab_size=topology.vocab_size,
         memory_budget=topology.memory_budget,
         in_flight_micro_batches=peak_in_flight(topology.micro_batches, stage_index=index, num_stages=num_stages),
-    ):
+    )
+    return bound if fits else 0
+
+
+def _pipelines(topology: DPTopology) -> list[tuple[DPStage, ...]]:
+    """One stage tuple per replica, replicas ascending, stages ascending within each."""
+    ordered = sorted(topology.stages, key=lambda s: (s.replica_id, s.stage_id))
+    replicas = sorted({s.replica_id for s in ordered})
+    return [tuple(s for s in ordered if s.replica_id == r) for r in replicas]
+
+
+def _pipeline_capacity(topology: DPTopology, pipeline: tuple[DPStage, ...], dead: frozenset[int]) -> int:
+    if not dead.isdisjoint(r for s in pipeline for r in s.ranks):
         return 0
-    return topology.micro_batches if stage.capacity is None else stage.capacity
+    depth = len(pipeline)
+    return min(stage_capacity(topology, s, index=i, num_stages=depth) for i, s in enumerate(pipeline))
 
 
 def split_by_capacity(total: int, capacities: tuple[int, ...]) -> tuple[int, ...]:
-    """Largest-remainder split of ``total`` proportional to ``capacities``."""
-    whole = sum(capacities)
-    if whole <= 0:
-        return tuple(0 for _ in capacities)
-    shares = [total * c // whole for c in capacities]
-    left = total - sum(shares)
-    order = sorted(range(len(capacities)), key=lambda i: (-(total * capacities[i] % whole), i))
-    for i in order[:left]:
-        shares[i] += 1
-    return tuple(shares)
+    """Hamilton apportionment of ``total`` over ``capacities``: each entry gets the floor
+    of its exact share, and the units left over go to the largest fractional parts
+    (equal parts: lower index first). All-zero capacities get nothing."""
+    weight = sum(capacities)
+    if weight <= 0:
+        return (0,) * len(capacities)
+    exact = [divmod(total * c, weight) for c in capacities]  # (floor, remainder * weight)
+    spare = total - sum(q for q, _ in exact)
+    favoured = sorted(range(len(capacities)), key=lambda i: (-exact[i][1], i))[:spare]
+    return tuple(q + (1 if i in favoured else 0) for i, (q, _) in enumerate(exact))
 
 
 def assign(step: int, failure_signature: Iterable[int], active_topology: DPTopology) -> DPAssignment:
     """Place every micro-batch on exactly one healthy replica's whole pipeline."""
     step = non_negative_int("step", step)
-    _check(active_topology)
+    topology = _validated(active_topology)
     failures = unique_ranks("failure_signature", failure_signature)
-    dead = set(failures)
+    dead = frozenset(failures)
 
-    replicas: dict[int, dict[int, DPStage]] = {}
-    for s in active_topology.stages:
-        replicas.setdefault(s.replica_id, {})[s.stage_id] = s
+    pipelines = _pipelines(topology)
+    capacity = [_pipeline_capacity(topology, p, dead) for p in pipelines]
+    if max(capacity) <= 0:
+        raise InfeasibleDP(DPInfeasibleReason(
+            "no_feasible_dp_target",
+            f"none of the {len(pipelines)} DP replicas can take micro-batches after failures {list(failures)}"))
+    usable = [i for i, c in enumerate(capacity) if c > 0]
+    counts = split_by_capacity(topology.micro_batches, tuple(capacity[i] for i in usable))
 
-    candidates: list[tuple[tuple[DPStage, ...], int]] = []
-    for replica in sorted(replicas):
-        pipeline = tuple(replicas[replica][sid] for sid in sorted(replicas[replica]))
-        if any(dead.intersection(s.ranks) for s in pipeline):
-            continue
-        capacity = min(
-            stage_capacity(active_topology, s, index=i, num_stages=len(pipeline))
-            for i, s in enumerate(pipeline)
-        )
-        if capacity > 0:
-            candidates.append((pipeline, capacity))
-    if not candidates:
-        raise InfeasibleDP(
-            DPInfeasibleReason("no_feasible_dp_target", "no healthy DP replica can accept the micro-batches")
-        )
-
-    counts = split_by_capacity(active_topology.micro_batches, tuple(c for _, c in candidates))
-    placements = []
-    mb = 0
-    for (pipeline, _), count in zip(candidates, counts):
-        for _ in range(count):
-            placements.extend(DPPlacement(mb, s.stage_id, s.replica_id, s.ranks) for s in pipeline)
-            mb += 1
-    placements.sort(key=lambda p: (p.micro_batch, p.stage_id))
+    placements: list[DPPlacement] = []
+    next_id = 0
+    for i, count in zip(usable, counts):
+        for micro_batch in range(next_id, next_id + count):
+            placements += [DPPlacement(micro_batch, s.stage_id, s.replica_id, s.ranks) for s in pipelines[i]]
+        next_id += count
+    # ids grow replica by replica and stages ascend inside each pipeline, so the list is
+    # already in (micro_batch, stage_id) order
     return DPAssignment(step=step, failure_signature=failures, placements=tuple(placements))
