@@ -1,7 +1,7 @@
 """Fused DP all-reduce + AdamW against NCCL all-reduce + the AdamW kernel, on 2+ GPUs.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 \\
-        --master-port 29583 -m resihp.utils.dp_probe [elements]
+        --master-port 29583 bench_dp_step.py [elements]
 
 Every rank holds one flat state of ``elements`` FP32 values (default 325,000,000: one
 TP2 x PP2 stage of the 1.3B model) in a shared region. CUDA-event timing (3 warm-up,
@@ -75,7 +75,7 @@ def main():
     adam_us = t_ev(lambda: fn.adamw_flat(flat.master, flat.grad, flat.exp_avg, flat.exp_avg_sq, 5, lr=1e-4,
                                          beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, p_bf16=flat.work))
     check_device_errors(rank)
-    peaks_path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+    peaks_path = os.path.join(os.path.dirname(os.path.abspath(__file__)),
                               "MEASURED_PEAKS.json")
     hbm = 6650.0
     if os.path.exists(peaks_path):

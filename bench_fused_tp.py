@@ -1,9 +1,9 @@
 """Fused AG->GEMM / GEMM->RS against NCCL + GEMM, on 2-8 GPUs.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
-        --master-port 29581 -m resihp.utils.fused_probe            # 1.3B layer shapes (T=4096, d=2048)
-    ... -m resihp.utils.fused_probe --sweep                         # BASELINE config-5 sweep
-    ... -m resihp.utils.fused_probe --config3                       # Llama-3-8B layer shapes
+        --master-port 29581 bench_fused_tp.py            # 1.3B layer shapes (T=4096, d=2048)
+    ... bench_fused_tp.py --sweep                         # BASELINE config-5 sweep
+    ... bench_fused_tp.py --config3                       # Llama-3-8B layer shapes
 
 The sweep covers M = 4096..32768 tokens with K, N in {5120, 13824}: column-parallel
 AG->GEMM ``[M, 5120] x [5120, N/tp]`` (N = 5120, 13824) and row-parallel GEMM->RS
@@ -28,7 +28,7 @@ LINK_GBS = 770.0
 
 
 def _peaks():
-    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)),
                         "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:

@@ -1,13 +1,13 @@
 """Small single-GPU workloads of the hot kernels, sized for profiler captures.
 
-    python -m resihp.utils.kernel_probe gemm   # forward + wgrad GEMM, 4096 x 6144 x 2048
-    python -m resihp.utils.kernel_probe attn   # causal attention fwd + bwd, B2 H16 S2048 D128
-    python -m resihp.utils.kernel_probe dp     # fused DP all-reduce + AdamW, 2 replicas emulated, 64M elements
-    python -m resihp.utils.kernel_probe reshard  # state move TP2 -> TP1 of one 1.3B layer group (3 fields)
-    python -m resihp.utils.kernel_probe gemm_time  # CUDA-event TF/s: forward / dgrad / wgrad / cuBLAS forward
-    python -m resihp.utils.kernel_probe attn_time  # CUDA-event fwd / bwd time of the causal attention
-    python -m resihp.utils.kernel_probe fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
-    python -m resihp.utils.kernel_probe fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
+    python bench_kernels.py gemm   # forward + wgrad GEMM, 4096 x 6144 x 2048
+    python bench_kernels.py attn   # causal attention fwd + bwd, B2 H16 S2048 D128
+    python bench_kernels.py dp     # fused DP all-reduce + AdamW, 2 replicas emulated, 64M elements
+    python bench_kernels.py reshard  # state move TP2 -> TP1 of one 1.3B layer group (3 fields)
+    python bench_kernels.py gemm_time  # CUDA-event TF/s: forward / dgrad / wgrad / cuBLAS forward
+    python bench_kernels.py attn_time  # CUDA-event fwd / bwd time of the causal attention
+    python bench_kernels.py fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
+    python bench_kernels.py fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
 and launches every kernel a handful of times, so a capture of one or two launches ends
