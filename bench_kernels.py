@@ -8,6 +8,7 @@
     python bench_kernels.py attn_time  # CUDA-event fwd / bwd time of the causal attention
     python bench_kernels.py fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
     python bench_kernels.py fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
+    python bench_kernels.py fused_time  # CUDA-event time of the emulated fused kernels vs the GEMM alone
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
 and launches every kernel a handful of times, so a capture of one or two launches ends
@@ -149,17 +150,44 @@ def reshard() -> None:
 
 
 def fused_ag(tp: int = 2) -> None:
-    from resihp.utils.fused_emulation import emulate_ag
+    from resihp.utils.fused_emulation import AgSession
 
-    for epoch in range(1, 4):
-        emulate_ag(4096, 2048, 3 * 2048 // tp, tp=tp, epoch=epoch)
+    s = AgSession(4096, 2048, 3 * 2048 // tp, tp=tp)
+    for _ in range(3):
+        s.launch()
 
 
 def fused_rs(tp: int = 2) -> None:
-    from resihp.utils.fused_emulation import emulate_rs
+    from resihp.utils.fused_emulation import RsSession
 
-    for epoch in range(1, 4):
-        emulate_rs(4096, 5504 // tp, 2048, tp=tp, epoch=epoch)
+    s = RsSession(4096, 5504 // tp, 2048, tp=tp)
+    for _ in range(3):
+        s.launch()
+
+
+def fused_time() -> None:
+    """CUDA-event time of the fused TP kernels with the peers emulated by local buffers
+    (the kernel's structure without NVLink latency) against this package's GEMM alone
+    on the gathered shape, at TP 2, 4 and 8 (1.3B shapes; both kernel variants)."""
+    import json
+
+    from resihp.utils.fused_emulation import AgSession, RsSession
+
+    out = []
+    for tp in (2, 4, 8):
+        n_ag, k_rs = 3 * 2048 // tp, 5504 // tp
+        x = torch.randn(4096, 2048, device="cuda").bfloat16()
+        w = torch.randn(n_ag, 2048, device="cuda").bfloat16()
+        h = torch.randn(4096, k_rs, device="cuda").bfloat16()
+        w2 = torch.randn(2048, k_rs, device="cuda").bfloat16()
+        row = {"tp": tp, "ag_gemm_alone_us": round(_time_us(lambda: ops.linear(x, w)), 1),
+               "rs_gemm_alone_us": round(_time_us(lambda: ops.linear(h, w2)), 1)}
+        for v in (0, 1):
+            ag, rs = AgSession(4096, 2048, n_ag, tp=tp, variant=v), RsSession(4096, k_rs, 2048, tp=tp, variant=v)
+            row[f"ag_v{v}_us"] = round(_time_us(ag.launch), 1)
+            row[f"rs_v{v}_us"] = round(_time_us(rs.launch), 1)
+        out.append(row)
+    print(json.dumps(out))
 
 
 def main(argv=None) -> None:
@@ -170,7 +198,7 @@ def main(argv=None) -> None:
         {"fused_ag": fused_ag, "fused_rs": fused_rs}[what](int(args[1]) if len(args) > 1 else 2)
     else:
         {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard, "gemm_time": gemm_time,
-         "attn_time": attn_time}[what]()
+         "attn_time": attn_time, "fused_time": fused_time}[what]()
     torch.cuda.synchronize()
     ops.check_device_errors()
     print("ok", what)

@@ -120,9 +120,14 @@ namespace resihp {
 // Peer-memory kernels over a stage's flat training state (peer_state.cu).
 constexpr int kMaxDp = 8;
 int dp_grid(int64_t n, int num_sms);
+// One-phase (sums_peer == nullptr): every rank reads every peer's whole accumulated
+// gradient. Two-phase push variant (sums_peer, flags2_*): rank q reduces part q of each
+// CTA slice, pushes the sum into every rank's receiving buffer, then steps locally.
 void dp_allreduce_adamw(const float* const* grads, int dp, int me, float* sum_out, float* p, float* m, float* v,
                         void* p_bf16, int64_t n, const AdamWCoef& coef, unsigned* flags_local,
-                        unsigned* const* flags_peer, unsigned epoch, int grid, int* err, cudaStream_t st);
+                        unsigned* const* flags_peer, unsigned epoch, int grid, int* err, cudaStream_t st,
+                        float* const* sums_peer = nullptr, unsigned* flags2_local = nullptr,
+                        unsigned* const* flags2_peer = nullptr);
 
 // One strided block copy of the state move: rows x cols fp32 elements.
 struct CopyDesc {

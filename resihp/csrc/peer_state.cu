@@ -60,6 +60,10 @@ struct DpArgs {
   AdamWCoef c;
   int* err;
   uint64_t wait_ns;            // budget of each wait on a peer's flag
+  // two-phase variant only (reduce-scatter, push, local AdamW):
+  float4* sum_peer[kMaxDp];    // group rank q's receiving buffer (its sum_out); [me] is local
+  unsigned* flags2_local;      // [grid][kMaxDp]: "my part's sums are in your buffer", written by peers
+  unsigned* flags2_peer[kMaxDp];
 };
 
 __device__ __forceinline__ float4 ld_cg_f4(const float4* p) { return __ldcg(p); }
@@ -138,6 +142,108 @@ __global__ void __launch_bounds__(kDpThreads) dp_adamw_kernel(const __grid_const
   }
 }
 
+// Two-phase variant for larger groups: CTA b of every rank still owns the same slice of
+// the flat buffers, but the slice is cut into `dp` parts and group rank q reduces only
+// part q. Phase 1: rank q sums part q of every rank's accumulated gradient (rank order,
+// so the bits are the same as the one-phase kernel's) and *pushes* the sum into part q
+// of every rank's receiving buffer (its own with a local store). Phase 2: once every
+// peer has flagged its part as pushed, each rank applies AdamW to the whole slice from
+// its now complete local receiving buffer. NVLink carries 2 (dp-1)/dp of the gradient
+// bytes into each GPU instead of (dp-1) times them.
+//
+// Buffer safety: the pushes of step t land in each rank's receiving buffer for step t,
+// which nobody reads or writes in step t before the pushes (its owner accumulates into
+// the other buffer, and the previous step's readers of it -- phase 1 of step t-1 --
+// finished before their step-t announcement, which the pusher waited for in phase 0).
+// A rank leaves the kernel only after every push into it is flagged, so its next step
+// can zero and reuse the buffer freely.
+template <int Q>
+__global__ void __launch_bounds__(kDpThreads) dp_adamw_push_kernel(const __grid_constant__ DpArgs a) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    int good = 1;
+    __threadfence_system();
+    for (int q = 0; q < a.dp; ++q)
+      if (q != a.me) st_release_sys(a.flags_peer[q] + blockIdx.x * kMaxDp + a.me, a.epoch);
+    for (int q = 0; q < a.dp && good; ++q)
+      if (q != a.me && !wait_geq(a.flags_local + blockIdx.x * kMaxDp + q, a.epoch, a.err, kErrPeerWait, a.wait_ns))
+        good = 0;
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int64_t lo = int64_t(blockIdx.x) * a.per_cta;
+  const int64_t hi = lo + a.per_cta < a.n4 ? lo + a.per_cta : a.n4;
+  const int64_t part = (hi - lo + a.dp - 1) / a.dp;
+  const int64_t mlo = lo + a.me * part < hi ? lo + a.me * part : hi;
+  const int64_t mhi = mlo + part < hi ? mlo + part : hi;
+  constexpr int kU = dp_unroll<Q>();
+  constexpr int64_t kStep = int64_t(kDpThreads) * kU;
+  // phase 1: reduce my part, push it to every rank
+  for (int64_t base = mlo + threadIdx.x; base < mhi; base += kStep) {
+    float4 g[Q][kU];
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * kDpThreads;
+      if (i >= mhi) continue;
+      #pragma unroll
+      for (int q = 0; q < Q; ++q)
+        if (q < a.dp) g[q][u] = ld_cg_f4(a.grad[q] + i);
+    }
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * kDpThreads;
+      if (i >= mhi) continue;
+      float4 s = g[0][u];
+      #pragma unroll
+      for (int q = 1; q < Q; ++q)
+        if (q < a.dp) add4(s, g[q][u]);
+      #pragma unroll
+      for (int q = 0; q < Q; ++q)
+        if (q < a.dp) __stcg(a.sum_peer[q] + i, s);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int good = 1;
+    for (int q = 0; q < a.dp; ++q)
+      if (q != a.me) st_release_sys(a.flags2_peer[q] + blockIdx.x * kMaxDp + a.me, a.epoch);
+    for (int q = 0; q < a.dp && good; ++q)
+      if (q != a.me && !wait_geq(a.flags2_local + blockIdx.x * kMaxDp + q, a.epoch, a.err, kErrPeerWait, a.wait_ns))
+        good = 0;
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  // phase 2: AdamW over the whole slice from the local receiving buffer
+  for (int64_t base = lo + threadIdx.x; base < hi; base += kStep) {
+    float4 s[kU], p[kU], m[kU], v[kU];
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * kDpThreads;
+      if (i >= hi) continue;
+      s[u] = __ldcg(a.sum_out + i);
+      p[u] = __ldcs(a.p + i);
+      m[u] = __ldcs(a.m + i);
+      v[u] = __ldcs(a.v + i);
+    }
+    #pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * kDpThreads;
+      if (i >= hi) continue;
+      adamw_elem(p[u].x, m[u].x, v[u].x, s[u].x, a.c);
+      adamw_elem(p[u].y, m[u].y, v[u].y, s[u].y, a.c);
+      adamw_elem(p[u].z, m[u].z, v[u].z, s[u].z, a.c);
+      adamw_elem(p[u].w, m[u].w, v[u].w, s[u].w, a.c);
+      __stcs(a.p + i, p[u]);
+      __stcs(a.m + i, m[u]);
+      __stcs(a.v + i, v[u]);
+      if (a.p_bf16 != nullptr) a.p_bf16[i] = pack4_bf16(p[u]);
+    }
+  }
+}
+
 int dp_grid(int64_t n, int num_sms) {
   const int64_t n4 = n / 4;
   const int64_t want = 2 * int64_t(num_sms);
@@ -147,7 +253,8 @@ int dp_grid(int64_t n, int num_sms) {
 
 void dp_allreduce_adamw(const float* const* grads, int dp, int me, float* sum_out, float* p, float* m, float* v,
                         void* p_bf16, int64_t n, const AdamWCoef& coef, unsigned* flags_local,
-                        unsigned* const* flags_peer, unsigned epoch, int grid, int* err, cudaStream_t st) {
+                        unsigned* const* flags_peer, unsigned epoch, int grid, int* err, cudaStream_t st,
+                        float* const* sums_peer, unsigned* flags2_local, unsigned* const* flags2_peer) {
   RESIHP_CHECK(dp >= 1 && dp <= kMaxDp && me >= 0 && me < dp, "dp_allreduce_adamw: bad group size / rank");
   RESIHP_CHECK(n % 4 == 0 && n > 0, "dp_allreduce_adamw: buffer length must be a positive multiple of 4");
   RESIHP_CHECK(grid >= 1, "dp_allreduce_adamw: empty grid");
@@ -171,9 +278,25 @@ void dp_allreduce_adamw(const float* const* grads, int dp, int me, float* sum_ou
   a.c = coef;
   a.err = err;
   a.wait_ns = peer_wait_budget_ns();
-  if (dp <= 2) dp_adamw_kernel<2><<<grid, kDpThreads, 0, st>>>(a);
-  else if (dp <= 4) dp_adamw_kernel<4><<<grid, kDpThreads, 0, st>>>(a);
-  else dp_adamw_kernel<8><<<grid, kDpThreads, 0, st>>>(a);
+  if (sums_peer != nullptr) {
+    RESIHP_CHECK(flags2_local != nullptr && flags2_peer != nullptr, "dp_allreduce_adamw: push variant needs flags");
+    for (int q = 0; q < dp; ++q) {
+      RESIHP_CHECK(reinterpret_cast<uintptr_t>(sums_peer[q]) % 16 == 0, "dp_allreduce_adamw: unaligned sum buffer");
+      a.sum_peer[q] = reinterpret_cast<float4*>(sums_peer[q]);
+      a.flags2_peer[q] = flags2_peer[q];
+    }
+    RESIHP_CHECK(a.sum_peer[me] == a.sum_out, "dp_allreduce_adamw: sums_peer[me] must be the local sum buffer");
+    a.flags2_local = flags2_local;
+    if (dp <= 2) dp_adamw_push_kernel<2><<<grid, kDpThreads, 0, st>>>(a);
+    else if (dp <= 4) dp_adamw_push_kernel<4><<<grid, kDpThreads, 0, st>>>(a);
+    else dp_adamw_push_kernel<8><<<grid, kDpThreads, 0, st>>>(a);
+  } else if (dp <= 2) {
+    dp_adamw_kernel<2><<<grid, kDpThreads, 0, st>>>(a);
+  } else if (dp <= 4) {
+    dp_adamw_kernel<4><<<grid, kDpThreads, 0, st>>>(a);
+  } else {
+    dp_adamw_kernel<8><<<grid, kDpThreads, 0, st>>>(a);
+  }
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 

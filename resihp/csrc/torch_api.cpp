@@ -408,7 +408,8 @@ int64_t dp_grid_t(int64_t n, int64_t device) {
 void dp_allreduce_adamw_t(std::vector<int64_t> grads, int64_t me, torch::Tensor sum_out, torch::Tensor p,
                           torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p_bf16, double lr, double b1,
                           double b2, double eps, double wd, int64_t step, double grad_scale, int64_t flags_local,
-                          std::vector<int64_t> flags_peer, int64_t epoch, int64_t grid) {
+                          std::vector<int64_t> flags_peer, int64_t epoch, int64_t grid,
+                          std::vector<int64_t> sums_peer, int64_t flags2_local, std::vector<int64_t> flags2_peer) {
   for (auto* t : {&sum_out, &p, &m, &v})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat && t->is_contiguous() && t->numel() == p.numel(),
                 "DP AdamW buffers must be contiguous fp32 of equal size");
@@ -427,9 +428,17 @@ void dp_allreduce_adamw_t(std::vector<int64_t> grads, int64_t me, torch::Tensor 
   for (auto x : grads) g.push_back(as_ptr<const float>(x));
   for (auto x : flags_peer) f.push_back(as_ptr<unsigned>(x));
   const AdamWCoef c = adamw_coef(float(lr), float(b1), float(b2), float(eps), float(wd), step, float(grad_scale));
+  const bool push = !sums_peer.empty();
+  TORCH_CHECK(!push || (int64_t(sums_peer.size()) == dp && int64_t(flags2_peer.size()) == dp && flags2_local != 0),
+              "the push variant needs one receiving buffer and one second flag array per DP rank");
+  std::vector<float*> sp;
+  std::vector<unsigned*> f2;
+  for (auto x : sums_peer) sp.push_back(as_ptr<float>(x));
+  for (auto x : flags2_peer) f2.push_back(as_ptr<unsigned>(x));
   dp_allreduce_adamw(g.data(), int(dp), int(me), sum_out.data_ptr<float>(), p.data_ptr<float>(), m.data_ptr<float>(),
                      v.data_ptr<float>(), pb, p.numel(), c, as_ptr<unsigned>(flags_local), f.data(), unsigned(epoch),
-                     int(grid), error_word(p.device()), cur_stream());
+                     int(grid), error_word(p.device()), cur_stream(), push ? sp.data() : nullptr,
+                     push ? as_ptr<unsigned>(flags2_local) : nullptr, push ? f2.data() : nullptr);
 }
 
 // descs: int64 [n, 9] on the device, one CopyDesc per row (see launch.h for the fields).
@@ -487,6 +496,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("flag_local"), py::arg("peer_flag"), py::arg("recv"), py::arg("grid"), py::arg("variant") = 0);
   m.def("symm_region", &resihp::symm_region_t);
   m.def("dp_grid", &resihp::dp_grid_t);
-  m.def("dp_allreduce_adamw", &resihp::dp_allreduce_adamw_t);
+  m.def("dp_allreduce_adamw", &resihp::dp_allreduce_adamw_t, py::arg("grads"), py::arg("me"), py::arg("sum_out"),
+        py::arg("p"), py::arg("m"), py::arg("v"), py::arg("p_bf16"), py::arg("lr"), py::arg("b1"), py::arg("b2"),
+        py::arg("eps"), py::arg("wd"), py::arg("step"), py::arg("grad_scale"), py::arg("flags_local"),
+        py::arg("flags_peer"), py::arg("epoch"), py::arg("grid"), py::arg("sums_peer") = std::vector<int64_t>{},
+        py::arg("flags2_local") = 0, py::arg("flags2_peer") = std::vector<int64_t>{});
   m.def("reshard_gather", &resihp::reshard_gather_t);
 }

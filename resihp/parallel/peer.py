@@ -33,6 +33,10 @@ import torch.distributed as dist
 from ..ops import _ext
 
 ENABLED = os.environ.get("RESIHP_FUSED_DP", "1") != "0"
+# Groups of at least this many replicas take the two-phase kernel (each rank reduces one
+# part of every slice and pushes the sum to all ranks): 2 (dp-1)/dp of the gradient
+# bytes cross NVLink into each GPU instead of (dp-1) times them.
+PUSH_MIN_DP = int(os.environ.get("RESIHP_DP_PUSH_MIN", "3"))
 MAX_DP = 8
 DP_FLAG_OFFSET = 0          # byte offset of the DP flag words inside the region's flag area
 COPY_ROW = 32 * 1024        # longest row (elements) one copy work item moves
@@ -73,7 +77,8 @@ class DpPeers:
             for r, other in enumerate(gathered):
                 self.bases.append(flat.region_ptr if r == self.rank else k.symm_open(other["handle"]))
         self.grid = k.dp_grid(flat.numel, self.device.index or 0)
-        if DP_FLAG_OFFSET + 4 * MAX_DP * self.grid > flat.flags.numel() * 4:
+        self.push = self.size >= PUSH_MIN_DP
+        if DP_FLAG_OFFSET + 2 * 4 * MAX_DP * self.grid > flat.flags.numel() * 4:
             raise ValueError("DP flag area too small for the launch grid")
         self.epoch = 0
         self.closed = False
@@ -88,11 +93,17 @@ class DpPeers:
         cur = flat.parity
         goff = flat.field_offsets[f"grad{cur}"]
         foff = DP_FLAG_OFFSET  # the flag area starts the region
+        extra = {}
+        if self.push:
+            soff = flat.field_offsets[f"grad{1 - cur}"]
+            f2 = foff + 4 * MAX_DP * self.grid  # the second flag array follows the first
+            extra = dict(sums_peer=[b + soff for b in self.bases], flags2_local=flat.region_ptr + f2,
+                         flags2_peer=[b + f2 for b in self.bases])
         k.dp_allreduce_adamw(
             [b + goff for b in self.bases], self.rank, flat.grads[1 - cur], flat.master, flat.exp_avg,
             flat.exp_avg_sq, None if flat.work is flat.master else flat.work, c.lr, c.beta1, c.beta2, c.adam_eps,
             c.weight_decay, flat.step, 1.0, flat.region_ptr + foff, [b + foff for b in self.bases], self.epoch,
-            self.grid,
+            self.grid, **extra,
         )
         stage.use_grad(1 - cur)
 

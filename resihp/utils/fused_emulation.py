@@ -72,3 +72,69 @@ def emulate_rs(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed
     own = hs[0][:rows].float() @ ws[0].float().t()
     ref = own + sum(p[:rows].float() for p in partials[1:])
     return y, ref
+
+
+class AgSession:
+    """Repeated emulated AG->GEMM launches of rank 0 on one set of buffers, with the
+    epoch and the counter bases advanced per launch as the real workspace advances them
+    (so every launch waits for its own pulls); the peers' announcements are preset far
+    ahead. For timing and profiler captures."""
+
+    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, variant: int = 0, device="cuda"):
+        self.kx = _ext.require()
+        dev = torch.device(device)
+        rows = tokens // tp
+        self.tp, self.n, self.t, self.variant = tp, n, tokens, variant
+        self.chunks = [torch.randn(rows, k, device=dev).bfloat16() for _ in range(tp)]
+        self.w = (torch.randn(n, k, device=dev) / k**0.5).bfloat16()
+        self.slots = [torch.empty_like(self.chunks[0])] + [c.clone() for c in self.chunks[1:]]
+        self.xg = torch.empty(tokens, k, device=dev, dtype=torch.bfloat16)
+        self.y = torch.empty(tokens, n, device=dev, dtype=torch.bfloat16)
+        self.sig = _u32(8, dev)
+        self.sig[1:tp] = 1 << 30
+        self.peer_sig = [_u32(8, dev) for _ in range(tp)]
+        self.pub, self.ready, self.rb_ready = _u32(1, dev), _u32(tp, dev), _u32(tokens // 128, dev)
+        self.grid = self.kx.fused_grid(tokens, n, tp)
+        self.epoch = self.pub_base = self.ready_base = self.rb_base = 0
+
+    def launch(self):
+        kx = self.kx
+        self.epoch += 1
+        kx.ag_gemm(self.chunks[0], self.slots[0].data_ptr(), [s.data_ptr() for s in self.slots], self.xg, self.w,
+                   False, self.y, 0, self.tp, self.epoch, self.sig.data_ptr(), [p.data_ptr() for p in self.peer_sig],
+                   self.pub.data_ptr(), self.pub_base, self.ready.data_ptr(), self.ready_base, self.grid,
+                   self.variant, self.rb_ready.data_ptr(), self.rb_base)
+        step = kx.fused_counter_step(self.grid, self.variant)
+        self.pub_base += step
+        if self.variant == 0:
+            self.ready_base += step
+        else:
+            self.rb_base += kx.fused_block_step(self.t, self.n, self.tp, self.grid)
+        return self.y
+
+
+class RsSession:
+    """Repeated emulated GEMM->RS launches of rank 0 (peer tile flags preset far ahead)."""
+
+    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, variant: int = 0, device="cuda"):
+        self.kx = _ext.require()
+        dev = torch.device(device)
+        rows = tokens // tp
+        self.tp, self.variant = tp, variant
+        self.h = torch.randn(tokens, k, device=dev).bfloat16()
+        self.w = (torch.randn(n, k, device=dev) / k**0.5).bfloat16()
+        self.parts = [torch.empty(tokens, n, device=dev, dtype=torch.bfloat16) for _ in range(tp)]
+        tiles = (tokens // 128) * ((n + 255) // 256)
+        self.own_flags = _u32(tiles, dev)
+        self.peer_flags = [self.own_flags] + [_u32(tiles, dev, 1 << 30) for _ in range(1, tp)]
+        self.recv = torch.empty(tp, rows, n, device=dev, dtype=torch.bfloat16)
+        self.y = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
+        self.grid = self.kx.fused_grid(tokens, n, tp)
+        self.epoch = 0
+
+    def launch(self):
+        self.epoch += 1
+        self.kx.gemm_rs(self.h, self.w, False, self.y, 0, self.tp, self.epoch, self.parts[0].data_ptr(),
+                        [p.data_ptr() for p in self.parts], self.own_flags.data_ptr(),
+                        [f.data_ptr() for f in self.peer_flags], self.recv.data_ptr(), self.grid, self.variant)
+        return self.y

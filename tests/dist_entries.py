@@ -48,8 +48,23 @@ def train_entry(rank, env, config_dict, steps, out_dir, dump_state):
     cp.shutdown()
 
 
-def failstop_entry(rank, env, config_dict, failures, out_dir):
-    """The worker loop with a failure schedule; records per-iteration losses and plans."""
+def _device(gpu):
+    """This rank's GPU (``LOCAL_RANK``) for the GPU variants of the gates, else the CPU."""
+    import torch
+
+    if not gpu:
+        return None, "gloo"
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    return torch.device("cuda", torch.cuda.current_device()), "nccl"
+
+
+def failstop_entry(rank, env, config_dict, failures, out_dir, gpu=False):
+    """The worker loop with a failure schedule; records per-iteration losses and plans.
+
+    ``gpu``: one GPU per rank, NCCL training groups, the bf16 kernels; every rank
+    finishes its GPU work before the kill point (nothing is in flight when a rank dies),
+    and after each recovery the rank checks its installed state against the checkpoint
+    the recovery resumed from (principle A1) and records the mismatches."""
     _setup(env)
     import torch
 
@@ -63,11 +78,13 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
     config = TrainConfig(**config_dict)
     schedule = {int(k): v for k, v in failures.items()}
     os.chdir(out_dir)
-    cp = ControlPlane.initialize(training_backend="gloo", memory_budget=config.memory_budget_bytes)
+    device, backend = _device(gpu)
+    cp = ControlPlane.initialize(training_backend=backend, memory_budget=config.memory_budget_bytes, device=device)
     plan = build_plan(config, step=0, version=0, memory_budget=config.memory_budget_bytes,
                       vocab_size=config.vocab_size, sequence_length=config.seq_len)
     groups = cp.build_training_groups(plan)
-    cp.attach_run(initial_run(plan, rank=rank, groups=groups), checkpoint_path=Path(out_dir, "checkpoint.pt"))
+    cp.attach_run(initial_run(plan, rank=rank, groups=groups, device=device),
+                  checkpoint_path=Path(out_dir, "checkpoint.pt"), device=device)
     record = {"rank": rank, "losses": {}, "plans": [plan.digest], "stopped": None, "recoveries": []}
     failed = ()
     try:
@@ -79,6 +96,7 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
                 record["losses"][str(it)] = loss
             if it % config.checkpoint_every == 0:
                 cp.commit_checkpoint(plan, cursor=it)
+            cp.quiesce()
             write_result(out_dir, rank, record)
             fail_stop(schedule, rank, it, before=cp.flush_checkpoint)
             lost = cp.observe()
@@ -90,9 +108,17 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
                 ck = Path(out_dir, "checkpoint.pt")
                 if rank == min(cp.members) and ck.exists():
                     shutil.copy(ck, Path(out_dir, f"anchor_{it}.pt"))
+                entry = {"after": it, "lost": list(lost), "phases": cp.last_recovery, "resumed_from": cp.resume_cursor}
+                if gpu and ck.exists():
+                    from resihp.checkpoint import load_anchor
+                    from resihp.recovery import checkpoint_mismatches
+
+                    anchor, completed = load_anchor(ck)
+                    entry["a1_completed"] = completed
+                    entry["a1_mismatches"] = ([] if cp.training_run is None else
+                                              checkpoint_mismatches(cp.training_run, plan=plan, rank=rank, anchor=anchor))
                 record["plans"].append(plan.digest)
-                record["recoveries"].append({"after": it, "lost": list(lost), "phases": cp.last_recovery,
-                                             "resumed_from": cp.resume_cursor})
+                record["recoveries"].append(entry)
                 it = cp.resume_cursor
     except ConsistentStop as stop:
         record["stopped"] = stop.reason.code
@@ -103,7 +129,7 @@ def failstop_entry(rank, env, config_dict, failures, out_dir):
     cp.shutdown()
 
 
-def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir):
+def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir, gpu=False):
     """Uninterrupted re-run of the post-failure plan from the anchor the failure resumed from."""
     _setup(env)
     from harness import write_result
@@ -124,11 +150,12 @@ def rerun_entry(rank, env, config_dict, failed, after, anchor_path, out_dir):
     from resihp import membership
 
     store = membership.connect(os.environ[membership.HOST_ENV], os.environ[membership.PORT_ENV])
-    cp = ControlPlane(plan_rank, survivors, store, "gloo")
+    device, backend = _device(gpu)
+    cp = ControlPlane(plan_rank, survivors, store, backend, device=device)
     cp.form_world(survivors, epoch=0)
     groups = cp.build_training_groups(plan)
     anchor, completed = load_anchor(anchor_path)
-    run = run_from_anchor(plan, rank=plan_rank, anchor=anchor, completed=completed, groups=groups)
+    run = run_from_anchor(plan, rank=plan_rank, anchor=anchor, completed=completed, groups=groups, device=device)
     losses = {}
     for it in range(completed + 1, config.iterations + 1):
         loss = run.step() if run is not None else None

@@ -68,6 +68,67 @@ def test_dp_kernel_matches_sum_then_adamw():
     torch.testing.assert_close(a.exp_avg_sq.cpu(), cpu[2], rtol=1e-6, atol=0)
 
 
+def test_dp_push_kernel_matches_sum_then_adamw():
+    """The two-phase variant (groups of three and more), run as group rank 0 of three
+    with the peers emulated by local regions: every flag a peer would set is preset, and
+    the parts the peers would push are preset in this rank's receiving buffer. Rank 0
+    must reduce exactly its part of every CTA slice (in rank order), push it into every
+    peer's receiving buffer and nowhere else, and step like sum-then-AdamW bit for bit."""
+    from resihp.ops import _ext, check_device_errors
+    from resihp.ops import functional as fn
+
+    k = _ext.require()
+    dev = torch.device("cuda", 0)
+    shapes = [(1000, 3), (257,), (4096, 64)]
+    regions = [_flat(shapes, dev) for _ in range(3)]
+    a = regions[0]
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for f in regions:
+        f.grads[0].copy_(torch.randn(f.numel, device=dev, generator=g))
+        f.grads[1].zero_()
+    a.master.copy_(torch.randn(a.numel, device=dev, generator=g))
+    a.exp_avg.copy_(torch.randn(a.numel, device=dev, generator=g))
+    a.exp_avg_sq.copy_(torch.rand(a.numel, device=dev, generator=g))
+    total = regions[0].grads[0] + regions[1].grads[0] + regions[2].grads[0]
+    a.grads[1].copy_(total)  # the parts the peers push
+    hp = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+    ref_p, ref_m, ref_v = a.master.clone(), a.exp_avg.clone(), a.exp_avg_sq.clone()
+    ref_bf = torch.empty_like(a.work)
+    step, epoch = 2, 7
+    fn.adamw_flat(ref_p, total, ref_m, ref_v, step, lr=hp["lr"], beta1=hp["beta1"], beta2=hp["beta2"], eps=hp["eps"],
+                  weight_decay=hp["weight_decay"], p_bf16=ref_bf)
+    grid = k.dp_grid(a.numel, 0)
+    a.flags.view(-1, 8)[:grid, 1:3] = epoch             # phase 0: both peers' gradients are final
+    a.flags.view(-1, 8)[grid:2 * grid, 1:3] = epoch     # phase 1: both peers have pushed their parts
+    f2 = 4 * 8 * grid
+    k.dp_allreduce_adamw([r.grads[0].data_ptr() for r in regions], 0, a.grads[1], a.master, a.exp_avg, a.exp_avg_sq,
+                         a.work, hp["lr"], hp["beta1"], hp["beta2"], hp["eps"], hp["weight_decay"], step, 1.0,
+                         a.region_ptr, [r.region_ptr for r in regions], epoch, grid,
+                         sums_peer=[r.grads[1].data_ptr() for r in regions], flags2_local=a.region_ptr + f2,
+                         flags2_peer=[r.region_ptr + f2 for r in regions])
+    torch.cuda.synchronize()
+    check_device_errors(0)
+    assert torch.equal(a.grads[1], total)
+    assert torch.equal(a.master, ref_p) and torch.equal(a.exp_avg, ref_m) and torch.equal(a.exp_avg_sq, ref_v)
+    assert torch.equal(a.work, ref_bf)
+    # rank 0's part of each CTA slice (float4 units), pushed to both peers and only there
+    n4 = a.numel // 4
+    per = (n4 + grid - 1) // grid
+    mine = torch.zeros(n4, dtype=torch.bool)
+    for b in range(grid):
+        lo, hi = b * per, min(b * per + per, n4)
+        if lo >= hi:
+            continue
+        part = (hi - lo + 2) // 3
+        mine[lo:min(lo + part, hi)] = True
+    mine = mine.repeat_interleave(4).to(dev)
+    for r in regions[1:]:
+        assert torch.equal(r.grads[1][mine], total[mine])
+        assert torch.count_nonzero(r.grads[1][~mine]) == 0
+        assert torch.equal(r.flags.view(-1, 8)[:grid, 0].cpu(), torch.full((grid,), epoch, dtype=torch.int32))
+        assert torch.equal(r.flags.view(-1, 8)[grid:2 * grid, 0].cpu(), torch.full((grid,), epoch, dtype=torch.int32))
+
+
 def test_dp_kernel_reports_a_peer_that_never_arrives():
     """Failure detection on the device, with no fault: the emulated DP peer never flags
     its gradients, the per-launch wait budget is short (50 ms), and the kernel gives up,

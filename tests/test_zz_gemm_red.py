@@ -1,4 +1,4 @@
-"""The weight-gradient GEMM's ``red.global.add`` epilogue (``RESIHP_WGRAD_RED=1``).
+"""The weight-gradient GEMM's ``red.global.add`` epilogue (the default; ``RESIHP_WGRAD_RED=0`` turns it off).
 
 Accumulating ``dy^T x`` into an FP32 buffer through fire-and-forget L2 reductions must
 give exactly the sums of the load-add-store epilogue (each element receives one
