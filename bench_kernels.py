@@ -8,6 +8,7 @@
     python bench_kernels.py attn_time  # CUDA-event fwd / bwd time of the causal attention
     python bench_kernels.py fused_ag [tp]  # fused AG->GEMM, 1.3B QKV shape, peers emulated locally
     python bench_kernels.py fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
+    python bench_kernels.py fused_ar [tp]  # fused GEMM->AR (no sequence parallelism), same shape
     python bench_kernels.py fused_time  # CUDA-event time of the emulated fused kernels vs the GEMM alone
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
@@ -150,6 +151,7 @@ def reshard() -> None:
 
 
 def fused_ag(tp: int = 2) -> None:
+    """Three emulated AG->GEMM launches at the 1.3B QKV shape (T 4096, K 2048, N 6144/tp)."""
     from resihp.utils.fused_emulation import AgSession
 
     s = AgSession(4096, 2048, 3 * 2048 // tp, tp=tp)
@@ -157,10 +159,11 @@ def fused_ag(tp: int = 2) -> None:
         s.launch()
 
 
-def fused_rs(tp: int = 2) -> None:
+def fused_rs(tp: int = 2, all_reduce: bool = False) -> None:
+    """Three emulated GEMM->RS (or GEMM->AR) launches at the 1.3B down-projection shape."""
     from resihp.utils.fused_emulation import RsSession
 
-    s = RsSession(4096, 5504 // tp, 2048, tp=tp)
+    s = RsSession(4096, 5504 // tp, 2048, tp=tp, all_reduce=all_reduce)
     for _ in range(3):
         s.launch()
 
@@ -168,7 +171,7 @@ def fused_rs(tp: int = 2) -> None:
 def fused_time() -> None:
     """CUDA-event time of the fused TP kernels with the peers emulated by local buffers
     (the kernel's structure without NVLink latency) against this package's GEMM alone
-    on the gathered shape, at TP 2, 4 and 8 (1.3B shapes; both kernel variants)."""
+    on the same shape, at TP 2, 4 and 8 (1.3B shapes)."""
     import json
 
     from resihp.utils.fused_emulation import AgSession, RsSession
@@ -180,13 +183,12 @@ def fused_time() -> None:
         w = torch.randn(n_ag, 2048, device="cuda").bfloat16()
         h = torch.randn(4096, k_rs, device="cuda").bfloat16()
         w2 = torch.randn(2048, k_rs, device="cuda").bfloat16()
-        row = {"tp": tp, "ag_gemm_alone_us": round(_time_us(lambda: ops.linear(x, w)), 1),
-               "rs_gemm_alone_us": round(_time_us(lambda: ops.linear(h, w2)), 1)}
-        for v in (0, 1):
-            ag, rs = AgSession(4096, 2048, n_ag, tp=tp, variant=v), RsSession(4096, k_rs, 2048, tp=tp, variant=v)
-            row[f"ag_v{v}_us"] = round(_time_us(ag.launch), 1)
-            row[f"rs_v{v}_us"] = round(_time_us(rs.launch), 1)
-        out.append(row)
+        ag, rs = AgSession(4096, 2048, n_ag, tp=tp), RsSession(4096, k_rs, 2048, tp=tp)
+        ar = RsSession(4096, k_rs, 2048, tp=tp, all_reduce=True)
+        out.append({"tp": tp, "ag_gemm_alone_us": round(_time_us(lambda: ops.linear(x, w)), 1),
+                    "ag_us": round(_time_us(ag.launch), 1),
+                    "rs_gemm_alone_us": round(_time_us(lambda: ops.linear(h, w2)), 1),
+                    "rs_us": round(_time_us(rs.launch), 1), "ar_us": round(_time_us(ar.launch), 1)})
     print(json.dumps(out))
 
 
@@ -194,8 +196,12 @@ def main(argv=None) -> None:
     args = argv or sys.argv[1:]
     what = args[0]
     torch.manual_seed(0)
-    if what in ("fused_ag", "fused_rs"):
-        {"fused_ag": fused_ag, "fused_rs": fused_rs}[what](int(args[1]) if len(args) > 1 else 2)
+    if what in ("fused_ag", "fused_rs", "fused_ar"):
+        tp = int(args[1]) if len(args) > 1 else 2
+        if what == "fused_ag":
+            fused_ag(tp)
+        else:
+            fused_rs(tp, all_reduce=what == "fused_ar")
     else:
         {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard, "gemm_time": gemm_time,
          "attn_time": attn_time, "fused_time": fused_time}[what]()

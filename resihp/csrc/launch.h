@@ -9,6 +9,7 @@
 #include <type_traits>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 
 namespace resihp {
 
@@ -96,18 +97,36 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
 
 namespace resihp {
 
+// Fused TP collectives (fused_gemm.cu). Every rank of a TP group maps every other
+// rank's symmetric workspace; these are this call's pointers into all of them.
+constexpr int kFusedMaxTp = 8;
+constexpr int kFusedMaxRb = 256;      // 128-row blocks per rank's chunk
+constexpr int kFusedMaxTiles = 8192;  // output tiles (128 x 256) per call
+struct FusedPeers {
+  int rank, tp, rows_per_rank;
+  int slices;              // AG push units per 128-row block (a power of two up to 32)
+  unsigned epoch;          // AG: AG calls so far (this one included); RS, AR: RS + AR calls
+  unsigned ar_epoch;       // AR calls so far
+  unsigned* tile_ctr;      // local work-claim counters and the values they had before this call
+  unsigned tile_base;
+  unsigned* copy_ctr;
+  unsigned copy_base;
+  __nv_bfloat16* land[kFusedMaxTp];      // AG landing zone [T, K] of each rank (this call's parity)
+  unsigned* ag_cnt[kFusedMaxTp];         // AG counters [kFusedMaxTp][kFusedMaxRb] of each rank
+  __nv_bfloat16* recv[kFusedMaxTp];      // RS receive buffer [tp][T/tp, N] of each rank (parity)
+  unsigned* rs_cnt[kFusedMaxTp];         // RS per-own-tile counters [2 parities][kFusedMaxTiles] of each rank
+  __nv_bfloat16* out_land[kFusedMaxTp];  // AR reduced-output landing zone [T, N] of each rank (parity)
+  unsigned* ar_cnt[kFusedMaxTp];         // AR per-tile counters of each rank
+};
 int fused_grid(int m, int n, int tp);
-int fused_counter_step(int grid, int variant);
-int fused_block_step(int t_rows, int n, int tp, int grid);
-void ag_gemm(const void* x_local, void* own_slot, const void* const* peer_slot, void* xg, const void* w,
-             int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n, int k, int rank, int tp,
-             unsigned epoch, unsigned* sig_ag, unsigned* const* peer_sig_ag, unsigned* pub, unsigned pub_base,
-             unsigned* ready, unsigned ready_base, unsigned* rb_ready, unsigned rb_base, int variant, int grid,
-             int* err, cudaStream_t st);
-void gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y_local, int64_t ldy, int t_rows, int n,
-             int k, int rank, int tp, unsigned epoch, void* part_local, const void* const* peer_part,
-             unsigned* flag_local, const unsigned* const* peer_flag, void* recv, int variant, int grid, int* err,
-             cudaStream_t st);
+int fused_slices(int rows_per_rank);
+// Claims a launch makes on its counters (the host adds them to its bases after the call).
+int fused_tile_claims(int t_rows, int n, int grid);
+int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, bool xg, int grid);
+void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,
+                   int t_rows, int n, int k, const FusedPeers& peers, int grid, int* err, cudaStream_t st);
+void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n,
+                   int k, bool all_reduce, const FusedPeers& peers, int grid, int* err, cudaStream_t st);
 void* symm_alloc(int64_t bytes, void* handle_out);
 void* symm_open(const void* handle);
 void symm_close(void* p);

@@ -323,58 +323,80 @@ py::bytes debug_read_bytes_t(int64_t p, int64_t bytes) {
 void symm_free_t(int64_t p) { symm_free(as_ptr<void>(p)); }
 
 int64_t fused_grid_t(int64_t m, int64_t n, int64_t tp) { return fused_grid(int(m), int(n), int(tp)); }
-int64_t fused_counter_step_t(int64_t grid, int64_t variant) { return fused_counter_step(int(grid), int(variant)); }
-int64_t fused_block_step_t(int64_t t_rows, int64_t n, int64_t tp, int64_t grid) {
-  return fused_block_step(int(t_rows), int(n), int(tp), int(grid));
+int64_t fused_slices_t(int64_t rows_per_rank) { return fused_slices(int(rows_per_rank)); }
+int64_t fused_tile_claims_t(int64_t t_rows, int64_t n, int64_t grid) {
+  return fused_tile_claims(int(t_rows), int(n), int(grid));
+}
+int64_t fused_copy_claims_t(int64_t mode, int64_t t_rows, int64_t n, int64_t tp, int64_t slices, bool xg,
+                            int64_t grid) {
+  return fused_copy_claims(int(mode), int(t_rows), int(n), int(tp), int(slices), xg, int(grid));
 }
 
-void ag_gemm_t(torch::Tensor x_local, int64_t own_slot, std::vector<int64_t> peer_slot, torch::Tensor xg,
-               torch::Tensor w, bool w_mn, torch::Tensor y, int64_t rank, int64_t tp, int64_t epoch, int64_t sig_ag,
-               std::vector<int64_t> peer_sig_ag, int64_t pub, int64_t pub_base, int64_t ready, int64_t ready_base,
-               int64_t grid, int64_t variant, int64_t rb_ready, int64_t rb_base) {
+// The peers of one fused call as a flat int64 list: rank, tp, rows_per_rank, slices, epoch,
+// ar_epoch, tile_ctr, tile_base, copy_ctr, copy_base, then tp addresses each of land,
+// ag_cnt, recv, rs_cnt, out_land, ar_cnt (0 where a call does not use them).
+static FusedPeers decode_peers(const std::vector<int64_t>& v) {
+  TORCH_CHECK(v.size() >= 10, "fused peers: header missing");
+  FusedPeers p{};
+  p.rank = int(v[0]);
+  p.tp = int(v[1]);
+  p.rows_per_rank = int(v[2]);
+  p.slices = int(v[3]);
+  p.epoch = unsigned(v[4]);
+  p.ar_epoch = unsigned(v[5]);
+  p.tile_ctr = as_ptr<unsigned>(v[6]);
+  p.tile_base = unsigned(v[7]);
+  p.copy_ctr = as_ptr<unsigned>(v[8]);
+  p.copy_base = unsigned(v[9]);
+  TORCH_CHECK(p.tp >= 2 && p.tp <= kFusedMaxTp && v.size() == size_t(10 + 6 * p.tp), "fused peers: bad length");
+  for (int r = 0; r < p.tp; ++r) {
+    p.land[r] = as_ptr<__nv_bfloat16>(v[10 + r]);
+    p.ag_cnt[r] = as_ptr<unsigned>(v[10 + p.tp + r]);
+    p.recv[r] = as_ptr<__nv_bfloat16>(v[10 + 2 * p.tp + r]);
+    p.rs_cnt[r] = as_ptr<unsigned>(v[10 + 3 * p.tp + r]);
+    p.out_land[r] = as_ptr<__nv_bfloat16>(v[10 + 4 * p.tp + r]);
+    p.ar_cnt[r] = as_ptr<unsigned>(v[10 + 5 * p.tp + r]);
+  }
+  return p;
+}
+
+void ag_gemm_t(torch::Tensor x_local, c10::optional<torch::Tensor> xg, torch::Tensor w, bool w_mn, torch::Tensor y,
+               std::vector<int64_t> peers, int64_t grid) {
   check_cuda_bf16(x_local, "x_local");
-  check_cuda_bf16(xg, "xg");
   check_cuda_bf16(w, "w");
   check_cuda_bf16(y, "y");
-  TORCH_CHECK(x_local.is_contiguous() && xg.is_contiguous() && y.is_contiguous() && w.stride(1) == 1,
-              "fused AG-GEMM tensors must be contiguous");
-  TORCH_CHECK(int64_t(peer_slot.size()) == tp && int64_t(peer_sig_ag.size()) == tp, "one entry per rank");
+  const FusedPeers p = decode_peers(peers);
+  TORCH_CHECK(x_local.is_contiguous() && y.is_contiguous() && w.stride(1) == 1, "fused AG-GEMM tensors must be contiguous");
   const int64_t k = x_local.size(1);
-  const int64_t t = xg.size(0);
+  const int64_t t = x_local.size(0) * p.tp;
   const int64_t n = y.size(1);
-  TORCH_CHECK(xg.size(1) == k && y.size(0) == t && x_local.size(0) * tp == t, "fused AG-GEMM shapes");
+  TORCH_CHECK(y.size(0) == t, "fused AG-GEMM shapes");
+  void* xg_ptr = nullptr;
+  if (xg.has_value()) {
+    check_cuda_bf16(*xg, "xg");
+    TORCH_CHECK(xg->is_contiguous() && xg->size(0) == t && xg->size(1) == k, "fused AG-GEMM gathered-copy shape");
+    xg_ptr = xg->data_ptr();
+  }
   TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused AG-GEMM weight");
   c10::cuda::CUDAGuard guard(x_local.device());
-  std::vector<const void*> slots;
-  std::vector<unsigned*> sigs;
-  for (auto v : peer_slot) slots.push_back(as_ptr<const void>(v));
-  for (auto v : peer_sig_ag) sigs.push_back(as_ptr<unsigned>(v));
-  ag_gemm(x_local.data_ptr(), as_ptr<void>(own_slot), slots.data(), xg.data_ptr(), w.data_ptr(), w.stride(0), w_mn,
-          y.data_ptr(), y.stride(0), int(t), int(n), int(k), int(rank), int(tp), unsigned(epoch),
-          as_ptr<unsigned>(sig_ag), sigs.data(), as_ptr<unsigned>(pub), unsigned(pub_base), as_ptr<unsigned>(ready),
-          unsigned(ready_base), as_ptr<unsigned>(rb_ready), unsigned(rb_base), int(variant), int(grid),
-          error_word(x_local.device()), cur_stream());
+  fused_ag_gemm(x_local.data_ptr(), xg_ptr, w.data_ptr(), w.stride(0), w_mn, y.data_ptr(), y.stride(0), int(t),
+                int(n), int(k), p, int(grid), error_word(x_local.device()), cur_stream());
 }
 
-void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y_local, int64_t rank, int64_t tp,
-               int64_t epoch, int64_t part_local, std::vector<int64_t> peer_part, int64_t flag_local,
-               std::vector<int64_t> peer_flag, int64_t recv, int64_t grid, int64_t variant) {
+// RS (all_reduce false): y is this rank's [T/tp, N] rows; AR: y is the full [T, N].
+void gemm_rs_t(torch::Tensor h, torch::Tensor w, bool w_mn, torch::Tensor y, bool all_reduce,
+               std::vector<int64_t> peers, int64_t grid) {
   check_cuda_bf16(h, "h");
   check_cuda_bf16(w, "w");
-  check_cuda_bf16(y_local, "y_local");
-  TORCH_CHECK(h.is_contiguous() && y_local.is_contiguous() && w.stride(1) == 1, "fused GEMM-RS tensors must be contiguous");
-  TORCH_CHECK(int64_t(peer_part.size()) == tp && int64_t(peer_flag.size()) == tp, "one entry per rank");
-  const int64_t t = h.size(0), k = h.size(1), n = y_local.size(1);
-  TORCH_CHECK(y_local.size(0) * tp == t, "fused GEMM-RS shapes");
+  check_cuda_bf16(y, "y");
+  const FusedPeers p = decode_peers(peers);
+  TORCH_CHECK(h.is_contiguous() && y.is_contiguous() && w.stride(1) == 1, "fused GEMM-RS tensors must be contiguous");
+  const int64_t t = h.size(0), k = h.size(1), n = y.size(1);
+  TORCH_CHECK(all_reduce ? y.size(0) == t : y.size(0) * p.tp == t, "fused GEMM-RS/AR shapes");
   TORCH_CHECK(w_mn ? (w.size(0) == k && w.size(1) == n) : (w.size(0) == n && w.size(1) == k), "fused GEMM-RS weight");
   c10::cuda::CUDAGuard guard(h.device());
-  std::vector<const void*> parts;
-  std::vector<const unsigned*> flags;
-  for (auto v : peer_part) parts.push_back(as_ptr<const void>(v));
-  for (auto v : peer_flag) flags.push_back(as_ptr<const unsigned>(v));
-  gemm_rs(h.data_ptr(), w.data_ptr(), w.stride(0), w_mn, y_local.data_ptr(), y_local.stride(0), int(t), int(n), int(k),
-          int(rank), int(tp), unsigned(epoch), as_ptr<void>(part_local), parts.data(), as_ptr<unsigned>(flag_local),
-          flags.data(), as_ptr<void>(recv), int(variant), int(grid), error_word(h.device()), cur_stream());
+  fused_gemm_rs(h.data_ptr(), w.data_ptr(), w.stride(0), w_mn, y.data_ptr(), y.stride(0), int(t), int(n), int(k),
+                all_reduce, p, int(grid), error_word(h.device()), cur_stream());
 }
 
 // ---- flat-state regions and the peer-state kernels ----------------------------------------
@@ -484,16 +506,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("debug_fill_bytes", &resihp::debug_fill_bytes_t);
   m.def("debug_read_bytes", &resihp::debug_read_bytes_t);
   m.def("fused_grid", &resihp::fused_grid_t);
-  m.def("fused_counter_step", &resihp::fused_counter_step_t);
-  m.def("fused_block_step", &resihp::fused_block_step_t);
-  m.def("ag_gemm", &resihp::ag_gemm_t, py::arg("x_local"), py::arg("own_slot"), py::arg("peer_slot"), py::arg("xg"),
-        py::arg("w"), py::arg("w_mn"), py::arg("y"), py::arg("rank"), py::arg("tp"), py::arg("epoch"),
-        py::arg("sig_ag"), py::arg("peer_sig_ag"), py::arg("pub"), py::arg("pub_base"), py::arg("ready"),
-        py::arg("ready_base"), py::arg("grid"), py::arg("variant") = 0, py::arg("rb_ready") = 0,
-        py::arg("rb_base") = 0);
-  m.def("gemm_rs", &resihp::gemm_rs_t, py::arg("h"), py::arg("w"), py::arg("w_mn"), py::arg("y_local"),
-        py::arg("rank"), py::arg("tp"), py::arg("epoch"), py::arg("part_local"), py::arg("peer_part"),
-        py::arg("flag_local"), py::arg("peer_flag"), py::arg("recv"), py::arg("grid"), py::arg("variant") = 0);
+  m.def("fused_slices", &resihp::fused_slices_t);
+  m.def("fused_tile_claims", &resihp::fused_tile_claims_t);
+  m.def("fused_copy_claims", &resihp::fused_copy_claims_t);
+  m.def("ag_gemm", &resihp::ag_gemm_t, py::arg("x_local"), py::arg("xg"), py::arg("w"), py::arg("w_mn"), py::arg("y"),
+        py::arg("peers"), py::arg("grid"));
+  m.def("gemm_rs", &resihp::gemm_rs_t, py::arg("h"), py::arg("w"), py::arg("w_mn"), py::arg("y"),
+        py::arg("all_reduce"), py::arg("peers"), py::arg("grid"));
   m.def("symm_region", &resihp::symm_region_t);
   m.def("dp_grid", &resihp::dp_grid_t);
   m.def("dp_allreduce_adamw", &resihp::dp_allreduce_adamw_t, py::arg("grads"), py::arg("me"), py::arg("sum_out"),

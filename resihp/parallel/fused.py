@@ -1,20 +1,28 @@
-"""Fused sequence-parallel TP linears over NVLink peer memory (csrc/fused_gemm.cu).
+"""Fused TP linears over NVLink peer memory (csrc/fused_gemm.cu).
+
+With sequence parallelism (tokens sharded between the TP ranks):
 
 * :func:`ag_linear`  -- column-parallel: ``y = all_gather_tokens(x_r) @ w.T`` as one
   AG->GEMM kernel; backward: the input gradient is one GEMM->RS kernel and the weight
-  gradient reuses the gathered input the forward kernel left in its gather buffer.
+  gradient reuses the gathered input the forward kernel assembled.
 * :func:`linear_rs`  -- row-parallel: ``y_r = reduce_scatter_tokens(h @ w.T)`` as one
   GEMM->RS kernel; backward: the input gradient is one AG->GEMM kernel over the output
   gradient, whose gathered copy feeds the weight gradient.
 
-Both replace the NCCL pair ``gather_tokens`` / ``scatter_tokens`` of
-:mod:`resihp.parallel.collectives` (the baseline; the reference's counterparts are the
-Megatron ``f`` / ``g`` all-reduce regions, ``resihp/parallel/tp.py:63-89``). They exchange data through a
+Without it (every rank holds every token, the reference's own layout):
+
+* :func:`col_linear_ar` -- column-parallel: a local GEMM forward; backward: the input
+  gradient's all-reduce fused into its GEMM (GEMM->AR).
+* :func:`row_linear_ar` -- row-parallel: ``y = all_reduce(x @ w.T)`` as one GEMM->AR
+  kernel; backward: local GEMMs.
+
+These replace the NCCL collectives of :mod:`resihp.parallel.collectives` (the
+baseline; the reference's counterparts are the Megatron ``f`` / ``g`` all-reduce
+regions, ``resihp/parallel/tp.py:63-89``). They exchange data through a
 :class:`SymmetricWorkspace` per TP group: one CUDA-IPC-shared region per rank holding
-the cross-GPU flag words, two publish slots for the AG input and two partial buffers
-for the RS (alternating by call parity), plus a local receive buffer. Peers only ever
-read each other's regions (P2P loads) and write each other's flag words; nothing in the
-workspace is multicast.
+the counter words, two AG landing zones, two RS receive buffers and two AR output
+landing zones (alternating by call parity). Peers write into each other's regions
+(posted P2P stores and release reductions on counters); nothing is multicast.
 
 All ranks of a TP group issue their fused calls in the same order (they follow the same
 model code), which is what the epoch counters rely on.
@@ -29,19 +37,23 @@ import torch.distributed as dist
 from torch.autograd import Function
 
 from ..ops import _ext
-from ..ops.gemm import linear_wgrad
+from ..ops.gemm import linear, linear_dgrad, linear_wgrad
 
 ENABLED = os.environ.get("RESIHP_FUSED_TP", "1") != "0"
-# Largest TP degree that takes the fused kernels. Above it the NCCL collectives + this
-# package's GEMM are used: in these kernels every CTA pulls a slice of every peer chunk
-# with register-staged loads, which keeps too few bytes in flight once the per-rank
-# chunk is small and the peers many (measured slower than NCCL at TP8).
-MAX_DEGREE = int(os.environ.get("RESIHP_FUSED_TP_MAX_DEGREE", "2"))
-# Kernel variant for TP > 2 (six copy warps with sixteen loads in flight each, per-row-block
-# readiness in the AG, first-ready peer order in the RS). Off until measured on GPUs.
-ROW_BLOCK_VARIANT = os.environ.get("RESIHP_FUSED_TP_V3", "0") == "1"
-_RB_READY = 256  # byte offset of the per-row-block ready counters in the flag area
+# Largest TP degree that takes the fused kernels; above it NCCL + this package's GEMM.
+MAX_DEGREE = int(os.environ.get("RESIHP_FUSED_TP_MAX_DEGREE", "8"))
 DEBUG = os.environ.get("RESIHP_FUSED_DEBUG", "0") == "1"
+
+MODE_AG, MODE_RS, MODE_AR = 1, 2, 3
+MAX_TP, MAX_RB, MAX_TILES = 8, 256, 8192     # launch.h: kFusedMaxTp, kFusedMaxRb, kFusedMaxTiles
+_AG_CNT = 0                                   # byte offsets of the counter words in the flag area
+_RS_CNT = _AG_CNT + 4 * MAX_TP * MAX_RB       # two banks by call parity
+_AR_CNT = _RS_CNT + 2 * 4 * MAX_TILES
+_CTRS = _AR_CNT + 4 * MAX_TILES               # local claim counters: AG tile, AG copy, RS tile, RS copy
+_FLAG_BYTES = 112 * 1024
+_GUARD_BYTES = 256                            # debug layout: guard bytes after every buffer
+_GUARD_VALUE = 0xA5
+_U32 = 0xFFFFFFFF
 
 
 def _debug_check(what: str, device) -> None:
@@ -58,19 +70,13 @@ def _debug_check(what: str, device) -> None:
         raise RuntimeError(f"fused {what} reported error code {code}")
 
 
-_MAX_TILES = 8192             # per-tile flags of the RS partial buffer
-_FLAG_BYTES = 4096 + 4 * _MAX_TILES
-_GUARD_BYTES = 256            # debug layout: guard bytes after every buffer
-_GUARD_VALUE = 0xA5
-
-
 class SymmetricWorkspace:
     """This rank's IPC-shared region and its mappings of every peer's region.
 
-    Layout (bytes): flag words | two AG publish slots ``[T/tp, width]`` | two RS partial
-    buffers ``[T, width]`` | one RS receive buffer ``[tp, T/tp, width]``. The AG input and
-    the RS output of every fused call have the model width, so one region serves all four
-    projections of a layer and their backward passes.
+    Layout (bytes): counter words (112 KB) | two AG landing zones ``[T, width]`` | two RS
+    receive buffers ``[tp, T/tp, width]`` | two AR output landing zones ``[T, width]``.
+    Every fused call's gathered input, reduced output and all-reduced output has the
+    model width, so one region serves all projections of a layer and their backward.
     """
 
     def __init__(self, group, rows_per_rank: int, width: int, device):
@@ -78,30 +84,27 @@ class SymmetricWorkspace:
         self.group = group
         self.tp = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        if self.tp > 8:
-            raise ValueError("fused TP collectives support up to 8 ranks")
+        if self.tp > MAX_TP:
+            raise ValueError(f"fused TP collectives support up to {MAX_TP} ranks")
         t = rows_per_rank * self.tp
-        if (t // 128) * ((width + 255) // 256) > _MAX_TILES:
+        if rows_per_rank % 128 or rows_per_rank // 128 > MAX_RB:
+            raise ValueError("fused TP workspace: rows per rank must be a multiple of 128 (at most 32768)")
+        if (t // 128) * ((width + 255) // 256) > MAX_TILES:
             raise ValueError("fused TP workspace: too many output tiles")
-        if _RB_READY + 4 * (t // 128) > 4096:
-            raise ValueError("fused TP workspace: too many row blocks for the flag area")
-        self.variant = 1 if (self.tp > 2 and ROW_BLOCK_VARIANT) else 0
         self.rows_per_rank = rows_per_rank
         self.width = width
+        self.t = t
         self.device = torch.device(device)
-        self.slot_bytes = rows_per_rank * width * 2
-        self.part_bytes = t * width * 2
-        # debug builds of the layout put a guard after every buffer (none otherwise, so
-        # the production layout is unchanged)
+        with torch.cuda.device(self.device):
+            self.slices = k.fused_slices(rows_per_rank)
+        self.buf_bytes = t * width * 2
         g = _GUARD_BYTES if DEBUG else 0
-        self.slot_off = _FLAG_BYTES + g
-        self.slot_stride = self.slot_bytes + g
-        self.part_off = self.slot_off + 2 * self.slot_stride
-        self.part_stride = self.part_bytes + g
-        self.recv_off = self.part_off + 2 * self.part_stride
-        self.total = self.recv_off + self.tp * self.slot_bytes + g
-        self.guards = [_FLAG_BYTES] + [self.slot_off + i * self.slot_stride + self.slot_bytes for i in range(2)] + [
-            self.part_off + i * self.part_stride + self.part_bytes for i in range(2)] + [self.total - g] if g else []
+        self.stride = self.buf_bytes + g
+        self.land_off = _FLAG_BYTES + g
+        self.recv_off = self.land_off + 2 * self.stride
+        self.out_off = self.recv_off + 2 * self.stride
+        self.total = self.out_off + 2 * self.stride
+        self.guards = ([_FLAG_BYTES] + [self.land_off + i * self.stride + self.buf_bytes for i in range(6)]) if g else []
         with torch.cuda.device(self.device):
             self.base, handle = k.symm_alloc(self.total)
             for off in self.guards:
@@ -115,30 +118,23 @@ class SymmetricWorkspace:
                 self.peers.append(self.base if r == self.rank else k.symm_open(h))
         dist.barrier(group=group)
         self.ag_epoch = 0
-        self.rs_epoch = 0
-        self.pub_base = 0
-        self.ready_base = 0
-        self.rb_base = 0
+        self.rs_epoch = 0   # RS and AR calls (they share the receive buffers and counters)
+        self.ar_epoch = 0
+        self.bases = [0, 0, 0, 0]  # claims so far on the AG tile, AG copy, RS tile, RS copy counters
         self.closed = False
 
-    # flag words (u32) inside a region
-    def _sig_ag(self, base):
-        return base
+    def _buf(self, base, off, epoch):
+        return base + off + (epoch % 2) * self.stride
 
-    def _pub(self, base):
-        return base + 64
-
-    def _ready(self, base):
-        return base + 128
-
-    def _tile_flags(self, base):
-        return base + 4096
-
-    def _slot(self, base, epoch):
-        return base + self.slot_off + (epoch % 2) * self.slot_stride
-
-    def _part(self, base, epoch):
-        return base + self.part_off + (epoch % 2) * self.part_stride
+    def _peers(self, tile_ctr: int, copy_ctr: int) -> list[int]:
+        """The flat peer description of the next call (see ``decode_peers`` in torch_api.cpp)."""
+        head = [self.rank, self.tp, self.rows_per_rank, self.slices, self.ag_epoch if tile_ctr == 0 else self.rs_epoch,
+                self.ar_epoch, self.base + _CTRS + 4 * tile_ctr, self.bases[tile_ctr] & _U32,
+                self.base + _CTRS + 4 * copy_ctr, self.bases[copy_ctr] & _U32]
+        ps = self.peers
+        return (head + [self._buf(p, self.land_off, self.ag_epoch) for p in ps] + [p + _AG_CNT for p in ps]
+                + [self._buf(p, self.recv_off, self.rs_epoch) for p in ps] + [p + _RS_CNT for p in ps]
+                + [self._buf(p, self.out_off, self.ar_epoch) for p in ps] + [p + _AR_CNT for p in ps])
 
     def check_guards(self, what: str) -> None:
         """Debug layout: raise if a kernel wrote past any buffer of this region."""
@@ -149,59 +145,62 @@ class SymmetricWorkspace:
                 raise RuntimeError(f"fused {what}: workspace guard at byte {off} was overwritten")
 
     def fits(self, rows: int, width: int) -> bool:
-        return rows == self.rows_per_rank * self.tp and width == self.width
+        return rows == self.t and width == self.width
 
-    # --- the two collectives --------------------------------------------------------
+    def _after(self, what: str, device, tile_ctr: int, copy_ctr: int, mode: int, n: int, grid: int,
+               xg: bool = False) -> None:
+        k = _ext.require()
+        self.bases[tile_ctr] += k.fused_tile_claims(self.t, n, grid)
+        self.bases[copy_ctr] += k.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg, grid)
+        _debug_check(what, device)
+        if DEBUG:
+            self.check_guards(what)
 
-    def all_gather_gemm(self, x_local, w, w_mn: bool, n: int):
-        """``(all_gather(x_local) @ op(w), gathered x)``; ``op(w)`` is ``w.T`` or ``w`` (``w_mn``)."""
+    # --- the three collectives ------------------------------------------------------
+
+    def all_gather_gemm(self, x_local, w, w_mn: bool, n: int, *, keep_gathered: bool = True):
+        """``(all_gather(x_local) @ op(w), gathered x or None)``; ``op(w)`` is ``w.T`` or ``w`` (``w_mn``)."""
         k = _ext.require()
         self.ag_epoch += 1
-        e = self.ag_epoch
         x_local = x_local.contiguous()
-        t = x_local.shape[0] * self.tp
-        xg = torch.empty((t, x_local.shape[1]), dtype=x_local.dtype, device=x_local.device)
-        y = torch.empty((t, n), dtype=x_local.dtype, device=x_local.device)
-        grid = k.fused_grid(t, n, self.tp)
-        k.ag_gemm(x_local, self._slot(self.base, e), [self._slot(p, e) for p in self.peers], xg, w, w_mn, y,
-                  self.rank, self.tp, e, self._sig_ag(self.base), [self._sig_ag(p) for p in self.peers],
-                  self._pub(self.base), self.pub_base, self._ready(self.base), self.ready_base, grid,
-                  self.variant, self.base + _RB_READY, self.rb_base)
-        step = k.fused_counter_step(grid, self.variant)  # the kernel's own per-launch counter increments
-        self.pub_base += step
-        if self.variant == 0:
-            self.ready_base += step
-        else:
-            self.rb_base += k.fused_block_step(t, n, self.tp, grid)
-        _debug_check(f"ag_gemm epoch {e}", x_local.device)
-        if DEBUG:
-            self.check_guards(f"ag_gemm epoch {e}")
+        xg = torch.empty((self.t, x_local.shape[1]), dtype=x_local.dtype, device=x_local.device) if keep_gathered else None
+        y = torch.empty((self.t, n), dtype=x_local.dtype, device=x_local.device)
+        grid = k.fused_grid(self.t, n, self.tp)
+        k.ag_gemm(x_local, xg, w, w_mn, y, self._peers(0, 1), grid)
+        self._after(f"ag_gemm epoch {self.ag_epoch}", x_local.device, 0, 1, MODE_AG, n, grid, xg is not None)
         return y, xg
 
     def gemm_reduce_scatter(self, h, w, w_mn: bool, n: int):
         """``reduce_scatter_tokens(h @ op(w))`` -> this rank's ``[T/tp, n]`` rows."""
         k = _ext.require()
         self.rs_epoch += 1
-        e = self.rs_epoch
         h = h.contiguous()
-        t = h.shape[0]
-        y = torch.empty((t // self.tp, n), dtype=h.dtype, device=h.device)
-        grid = k.fused_grid(t, n, self.tp)
-        k.gemm_rs(h, w, w_mn, y, self.rank, self.tp, e, self._part(self.base, e),
-                  [self._part(p, e) for p in self.peers], self._tile_flags(self.base),
-                  [self._tile_flags(p) for p in self.peers], self.base + self.recv_off, grid, self.variant)
-        _debug_check(f"gemm_rs epoch {e}", h.device)
-        if DEBUG:
-            self.check_guards(f"gemm_rs epoch {e}")
+        y = torch.empty((self.rows_per_rank, n), dtype=h.dtype, device=h.device)
+        grid = k.fused_grid(self.t, n, self.tp)
+        k.gemm_rs(h, w, w_mn, y, False, self._peers(2, 3), grid)
+        self._after(f"gemm_rs epoch {self.rs_epoch}", h.device, 2, 3, MODE_RS, n, grid)
+        return y
+
+    def gemm_all_reduce(self, h, w, w_mn: bool, n: int):
+        """``all_reduce(h @ op(w))`` -> the full ``[T, n]`` on every rank."""
+        k = _ext.require()
+        self.rs_epoch += 1
+        self.ar_epoch += 1
+        h = h.contiguous()
+        y = torch.empty((self.t, n), dtype=h.dtype, device=h.device)
+        grid = k.fused_grid(self.t, n, self.tp)
+        k.gemm_rs(h, w, w_mn, y, True, self._peers(2, 3), grid)
+        self._after(f"gemm_ar epoch {self.ar_epoch}", h.device, 2, 3, MODE_AR, n, grid)
         return y
 
     def close(self, *, barrier: bool = True):
         """Unmap the peers' regions and free this one.
 
         Every rank of the group must have finished its fused kernels first -- a peer may
-        still be reading this rank's buffers -- so by default the group synchronises
-        before anything is unmapped. At a fail-stop safe point (``barrier=False``) no
-        kernel is in flight anywhere and the dead peer cannot take part in a barrier.
+        still be writing into this rank's buffers -- so by default the group
+        synchronises before anything is unmapped. At a fail-stop safe point
+        (``barrier=False``) no kernel is in flight anywhere and the dead peer cannot
+        take part in a barrier.
         """
         if self.closed:
             return
@@ -253,6 +252,42 @@ class _LinearRS(Function):
         return dh, None, None, None
 
 
+class _ColLinearAR(Function):
+    @staticmethod
+    def forward(ctx, h, w, main_grad, ws):
+        ctx.save_for_backward(h, w)
+        ctx.main_grad = main_grad
+        ctx.ws = ws
+        return linear(h, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        h, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dh = ctx.ws.gemm_all_reduce(dy, w, True, w.shape[1])
+        if ctx.main_grad is not None:
+            linear_wgrad(dy, h, out=ctx.main_grad, accumulate=True)
+        return dh, None, None, None
+
+
+class _RowLinearAR(Function):
+    @staticmethod
+    def forward(ctx, x, w, main_grad, ws):
+        ctx.save_for_backward(x, w)
+        ctx.main_grad = main_grad
+        ctx.ws = ws
+        return ws.gemm_all_reduce(x, w, False, w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = linear_dgrad(dy, w)
+        if ctx.main_grad is not None:
+            linear_wgrad(dy, x, out=ctx.main_grad, accumulate=True)
+        return dx, None, None, None
+
+
 def ag_linear(x_local, w, main_grad, ws):
     """Column-parallel SP linear: all-gather over tokens fused into the GEMM."""
     return _AGLinear.apply(x_local, w, main_grad, ws)
@@ -261,3 +296,13 @@ def ag_linear(x_local, w, main_grad, ws):
 def linear_rs(h, w, main_grad, ws):
     """Row-parallel SP linear: reduce-scatter over tokens fused into the GEMM."""
     return _LinearRS.apply(h, w, main_grad, ws)
+
+
+def col_linear_ar(h, w, main_grad, ws):
+    """Column-parallel linear without SP: the input gradient's all-reduce fused into its GEMM."""
+    return _ColLinearAR.apply(h, w, main_grad, ws)
+
+
+def row_linear_ar(x, w, main_grad, ws):
+    """Row-parallel linear without SP: the output all-reduce fused into the GEMM."""
+    return _RowLinearAR.apply(x, w, main_grad, ws)

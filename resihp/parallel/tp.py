@@ -217,8 +217,8 @@ class TensorParallelStage:
         self.dp = None  # peer mappings of the fused DP reduction (set by the gradient reducer)
         self.hetero = None  # peer mappings of the P2P heterogeneous-replica reduction
         rows = config.micro_batch_size * config.seq_len
-        if (self.kernel and self.sp and fused.ENABLED and self.tp_size <= min(8, fused.MAX_DEGREE)
-                and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0):
+        if (self.kernel and fused.ENABLED and 1 < self.tp_size <= min(8, fused.MAX_DEGREE)
+                and rows % self.tp_size == 0 and (rows // self.tp_size) % 128 == 0 and self.dim % 32 == 0):
             self.ws = fused.SymmetricWorkspace(group, rows // self.tp_size, self.dim, self.device)
         self.rope = None
         if config.arch == "llama":
@@ -331,17 +331,19 @@ class TensorParallelStage:
             self.hetero = None
 
     def _col_linear(self, h, w, g):
-        """Column-parallel linear; under SP the token all-gather is fused into the GEMM."""
+        """Column-parallel linear; its collective (SP: the token all-gather; otherwise the
+        input gradient's all-reduce) is fused into the GEMM on the kernel path."""
         if self.ws is not None:
-            return fused.ag_linear(h, w, g, self.ws)
+            return fused.ag_linear(h, w, g, self.ws) if self.sp else fused.col_linear_ar(h, w, g, self.ws)
         if self.tp_size > 1:  # the input-gradient collective overlaps the weight gradient
             return cc.column_parallel_linear(h, w, g, self.group, self.sp)
         return fn.linear(h, w, g)
 
     def _row_linear(self, x, w, g):
-        """Row-parallel linear; under SP the token reduce-scatter is fused into the GEMM."""
+        """Row-parallel linear; its collective (SP: the token reduce-scatter; otherwise the
+        output all-reduce) is fused into the GEMM on the kernel path."""
         if self.ws is not None:
-            return fused.linear_rs(x, w, g, self.ws)
+            return fused.linear_rs(x, w, g, self.ws) if self.sp else fused.row_linear_ar(x, w, g, self.ws)
         return self._row_output(fn.linear(x, w, g))
 
     def _row_output(self, y):

@@ -1,15 +1,18 @@
 """The fused TP kernels on one GPU, with the peers emulated by local buffers.
 
-A fused AG->GEMM or GEMM->RS launch of group rank 0 out of ``tp`` normally reads its
-peers' symmetric buffers over NVLink and waits for their flag words. Here every peer
-buffer is a second buffer on the same device, filled with what that peer would have
-published, and every flag word the kernel waits on is set before the launch -- so the
-launch runs alone, waits for nothing, and can be checked against torch or captured by
-a profiler on a single GPU. (Two kernels that wait on each other never run as separate
-launches on one GPU; here nothing is waited on.)
+A fused launch of group rank 0 out of ``tp`` normally pushes into its peers' workspaces
+over NVLink and waits on counters the peers raise in its own workspace. Here every
+"peer" workspace is a second region on the same device with the same layout, the data
+each peer would have pushed into rank 0 is written there beforehand and every counter
+rank 0 waits on is preset far ahead -- so the launch runs alone, waits for nothing and
+can be checked against torch, timed, or captured by a profiler on a single GPU. (Two
+kernels that wait on each other never run as separate launches on one GPU; here
+nothing is waited on.) Rank 0's own pushes land in the emulated peers' regions, where a
+test can check them.
 
-    from resihp.utils.fused_emulation import emulate_ag, emulate_rs
-    y, want = emulate_ag(tokens=4096, k=2048, n=3072, tp=2)
+    from resihp.utils.fused_emulation import Emulation
+    em = Emulation(tokens=4096, width=2048, tp=2)
+    y = em.all_gather_gemm(w)          # y = gather(x) @ w.T, rank 0's view
 """
 
 from __future__ import annotations
@@ -17,124 +20,143 @@ from __future__ import annotations
 import torch
 
 from ..ops import _ext
+from ..parallel import fused
+
+_FAR = 1 << 30  # a counter value no launch of a test reaches
 
 
-def _u32(count, device, fill=0):
-    return torch.full((count,), fill, dtype=torch.int32, device=device)
+class Emulation:
+    """``tp`` workspaces on one device laid out like :class:`~resihp.parallel.fused.
+    SymmetricWorkspace`; launches run as group rank 0."""
 
+    def __init__(self, tokens: int, width: int, *, tp: int = 2, seed: int = 0, device="cuda"):
+        self.kx = _ext.require()
+        self.dev = torch.device(device)
+        self.tp, self.t, self.width = tp, tokens, width
+        self.rpr = tokens // tp
+        g = torch.Generator(device=self.dev).manual_seed(seed)
+        self.gen = g
+        with torch.cuda.device(self.dev):
+            self.slices = self.kx.fused_slices(self.rpr)
+        self.buf_bytes = tokens * width * 2
+        self.land_off = fused._FLAG_BYTES
+        self.recv_off = self.land_off + 2 * self.buf_bytes
+        self.out_off = self.recv_off + 2 * self.buf_bytes
+        total = self.out_off + 2 * self.buf_bytes
+        self.regions = [torch.zeros(total, dtype=torch.uint8, device=self.dev) for _ in range(tp)]
+        self.bases = [r.data_ptr() for r in self.regions]
+        self.epochs = {"ag": 0, "rs": 0, "ar": 0}
+        self.claims = [0, 0, 0, 0]
+        self.x = torch.randn(tokens, width, device=self.dev, generator=g).bfloat16()  # every rank's chunk, stacked
+        # rank 0's waits pass at once; the peers' counters start at zero (rank 0 raises them)
+        self.u32(0, fused._AG_CNT, fused.MAX_TP * fused.MAX_RB).view(fused.MAX_TP, fused.MAX_RB)[1:].fill_(_FAR)
+        self.u32(0, fused._RS_CNT, 2 * fused.MAX_TILES).fill_(_FAR)
+        self.u32(0, fused._AR_CNT, fused.MAX_TILES).fill_(_FAR)
+        for parity in range(2):  # the peers' chunks already in rank 0's landing zones
+            self.buf(0, self.land_off, parity, (tokens, width))[self.rpr:].copy_(self.x[self.rpr:])
 
-def emulate_ag(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda",
-               variant: int = 0):
-    """``(y, reference)`` of one emulated AG->GEMM launch of rank 0: ``y = gather(x) @ w.T``."""
-    kx = _ext.require()
-    dev = torch.device(device)
-    g = torch.Generator(device=dev).manual_seed(seed)
-    rows = tokens // tp
-    chunks = [torch.randn(rows, k, device=dev, generator=g).bfloat16() for _ in range(tp)]
-    w = (torch.randn(n, k, device=dev, generator=g) / k**0.5).bfloat16()
-    slots = [torch.empty_like(chunks[0])] + [c.clone() for c in chunks[1:]]  # peers already published
-    xg = torch.empty(tokens, k, device=dev, dtype=torch.bfloat16)
-    y = torch.empty(tokens, n, device=dev, dtype=torch.bfloat16)
-    sig = _u32(8, dev)
-    sig[1:tp] = epoch                      # every peer announced this epoch
-    peer_sig = [_u32(8, dev) for _ in range(tp)]  # where this rank's announcement lands
-    pub = _u32(1, dev)
-    ready = _u32(tp, dev)
-    rb_ready = _u32(tokens // 128, dev)
-    grid = kx.fused_grid(tokens, n, tp)
-    kx.ag_gemm(chunks[0], slots[0].data_ptr(), [s.data_ptr() for s in slots], xg, w, False, y, 0, tp, epoch,
-               sig.data_ptr(), [p.data_ptr() for p in peer_sig], pub.data_ptr(), 0, ready.data_ptr(), 0, grid,
-               variant, rb_ready.data_ptr(), 0)
-    ref = torch.cat(chunks).float() @ w.float().t()
-    return y, ref, xg, torch.cat(chunks)
+    # --- views into the emulated workspaces ---------------------------------------------
+    def u32(self, rank, off, count):
+        return self.regions[rank][off:off + 4 * count].view(torch.int32)
 
+    def buf(self, rank, off, parity, shape):
+        start = off + parity * self.buf_bytes
+        n = shape[0] * shape[1]
+        return self.regions[rank][start:start + 2 * n].view(torch.bfloat16).view(shape)
 
-def emulate_rs(tokens: int, k: int, n: int, *, tp: int = 2, epoch: int = 1, seed: int = 0, device="cuda",
-               variant: int = 0):
-    """``(y_r, reference)`` of one emulated GEMM->RS launch of rank 0: rows ``[0, T/tp)`` of
-    ``sum over ranks of h_rank @ w_rank.T``, the peers' partials preset in local buffers."""
-    kx = _ext.require()
-    dev = torch.device(device)
-    g = torch.Generator(device=dev).manual_seed(seed)
-    rows = tokens // tp
-    hs = [torch.randn(tokens, k, device=dev, generator=g).bfloat16() for _ in range(tp)]
-    ws = [(torch.randn(n, k, device=dev, generator=g) / k**0.5).bfloat16() for _ in range(tp)]
-    partials = [(h.float() @ w.float().t()).bfloat16() for h, w in zip(hs, ws)]  # what each peer publishes
-    parts = [torch.empty(tokens, n, device=dev, dtype=torch.bfloat16)] + partials[1:]
-    tiles = (tokens // 128) * ((n + 255) // 256)
-    own_flags = _u32(tiles, dev)
-    peer_flags = [own_flags] + [_u32(tiles, dev, 4 * epoch) for _ in range(1, tp)]  # every peer tile is final
-    recv = torch.empty(tp, rows, n, device=dev, dtype=torch.bfloat16)
-    y = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
-    grid = kx.fused_grid(tokens, n, tp)
-    kx.gemm_rs(hs[0], ws[0], False, y, 0, tp, epoch, parts[0].data_ptr(), [p.data_ptr() for p in parts],
-               own_flags.data_ptr(), [f.data_ptr() for f in peer_flags], recv.data_ptr(), grid, variant)
-    own = hs[0][:rows].float() @ ws[0].float().t()
-    ref = own + sum(p[:rows].float() for p in partials[1:])
-    return y, ref
+    def _peers(self, tile_ctr, copy_ctr, epoch):
+        head = [0, self.tp, self.rpr, self.slices, epoch, self.epochs["ar"], self.bases[0] + fused._CTRS + 4 * tile_ctr,
+                self.claims[tile_ctr] & fused._U32, self.bases[0] + fused._CTRS + 4 * copy_ctr,
+                self.claims[copy_ctr] & fused._U32]
+        bs = self.bases
+        return (head + [b + self.land_off + (self.epochs["ag"] % 2) * self.buf_bytes for b in bs]
+                + [b + fused._AG_CNT for b in bs]
+                + [b + self.recv_off + (self.epochs["rs"] % 2) * self.buf_bytes for b in bs]
+                + [b + fused._RS_CNT for b in bs]
+                + [b + self.out_off + (self.epochs["ar"] % 2) * self.buf_bytes for b in bs]
+                + [b + fused._AR_CNT for b in bs])
+
+    def _advance(self, tile_ctr, copy_ctr, mode, n, grid, xg):
+        self.claims[tile_ctr] += self.kx.fused_tile_claims(self.t, n, grid)
+        self.claims[copy_ctr] += self.kx.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg, grid)
+
+    # --- the three launches (rank 0) ------------------------------------------------------
+    def all_gather_gemm(self, w, *, w_mn=False, keep_gathered=True):
+        """``(y, xg)`` of rank 0's AG->GEMM: ``y = gather(x) @ op(w)``."""
+        self.epochs["ag"] += 1
+        n = w.shape[1] if w_mn else w.shape[0]
+        xg = torch.empty(self.t, self.width, device=self.dev, dtype=torch.bfloat16) if keep_gathered else None
+        y = torch.empty(self.t, n, device=self.dev, dtype=torch.bfloat16)
+        grid = self.kx.fused_grid(self.t, n, self.tp)
+        self.kx.ag_gemm(self.x[:self.rpr], xg, w, w_mn, y, self._peers(0, 1, self.epochs["ag"]), grid)
+        self._advance(0, 1, fused.MODE_AG, n, grid, xg is not None)
+        return y, xg
+
+    def preset_partials(self, h_peers, w_peers, *, w_mn=False, all_reduce=False):
+        """Write what every peer would push into rank 0 for an RS (or AR) launch: each
+        peer's bf16 partial of rank 0's rows, in both parities (and, for an AR, every
+        other owner's reduced rows in rank 0's output landing zone). Returns the FP32
+        reference of the launch's output."""
+        n = w_peers[0].shape[1] if w_mn else w_peers[0].shape[0]
+        op = (lambda w: w.float()) if w_mn else (lambda w: w.float().t())
+        parts = [h.float() @ op(w) for h, w in zip(h_peers, w_peers)]
+        for parity in range(2):
+            recv = self.buf(0, self.recv_off, parity, (self.tp, self.rpr * n)).view(self.tp, self.rpr, n)
+            for src in range(1, self.tp):
+                recv[src].copy_(parts[src][:self.rpr].bfloat16())
+        if not all_reduce:
+            own = parts[0][:self.rpr]
+            return own + sum(parts[src][:self.rpr].bfloat16().float() for src in range(1, self.tp))
+        full = parts[0].clone()
+        for src in range(1, self.tp):
+            full += parts[src].bfloat16().float()
+        for parity in range(2):
+            out = self.buf(0, self.out_off, parity, (self.t, n))
+            out[self.rpr:].copy_(full[self.rpr:].bfloat16())
+        return full
+
+    def gemm_reduce_scatter(self, h, w, *, w_mn=False):
+        self.epochs["rs"] += 1
+        n = w.shape[1] if w_mn else w.shape[0]
+        y = torch.empty(self.rpr, n, device=self.dev, dtype=torch.bfloat16)
+        grid = self.kx.fused_grid(self.t, n, self.tp)
+        self.kx.gemm_rs(h, w, w_mn, y, False, self._peers(2, 3, self.epochs["rs"]), grid)
+        self._advance(2, 3, fused.MODE_RS, n, grid, False)
+        return y
+
+    def gemm_all_reduce(self, h, w, *, w_mn=False):
+        self.epochs["rs"] += 1
+        self.epochs["ar"] += 1
+        n = w.shape[1] if w_mn else w.shape[0]
+        y = torch.empty(self.t, n, device=self.dev, dtype=torch.bfloat16)
+        grid = self.kx.fused_grid(self.t, n, self.tp)
+        self.kx.gemm_rs(h, w, w_mn, y, True, self._peers(2, 3, self.epochs["rs"]), grid)
+        self._advance(2, 3, fused.MODE_AR, n, grid, False)
+        return y
 
 
 class AgSession:
-    """Repeated emulated AG->GEMM launches of rank 0 on one set of buffers, with the
-    epoch and the counter bases advanced per launch as the real workspace advances them
-    (so every launch waits for its own pulls); the peers' announcements are preset far
-    ahead. For timing and profiler captures."""
+    """Repeated emulated AG->GEMM launches (one set of buffers), for timing and captures."""
 
-    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, variant: int = 0, device="cuda"):
-        self.kx = _ext.require()
-        dev = torch.device(device)
-        rows = tokens // tp
-        self.tp, self.n, self.t, self.variant = tp, n, tokens, variant
-        self.chunks = [torch.randn(rows, k, device=dev).bfloat16() for _ in range(tp)]
-        self.w = (torch.randn(n, k, device=dev) / k**0.5).bfloat16()
-        self.slots = [torch.empty_like(self.chunks[0])] + [c.clone() for c in self.chunks[1:]]
-        self.xg = torch.empty(tokens, k, device=dev, dtype=torch.bfloat16)
-        self.y = torch.empty(tokens, n, device=dev, dtype=torch.bfloat16)
-        self.sig = _u32(8, dev)
-        self.sig[1:tp] = 1 << 30
-        self.peer_sig = [_u32(8, dev) for _ in range(tp)]
-        self.pub, self.ready, self.rb_ready = _u32(1, dev), _u32(tp, dev), _u32(tokens // 128, dev)
-        self.grid = self.kx.fused_grid(tokens, n, tp)
-        self.epoch = self.pub_base = self.ready_base = self.rb_base = 0
+    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, keep_gathered: bool = True, device="cuda"):
+        self.em = Emulation(tokens, k, tp=tp, device=device)
+        self.w = (torch.randn(n, k, device=device) / k**0.5).bfloat16()
+        self.keep = keep_gathered
 
     def launch(self):
-        kx = self.kx
-        self.epoch += 1
-        kx.ag_gemm(self.chunks[0], self.slots[0].data_ptr(), [s.data_ptr() for s in self.slots], self.xg, self.w,
-                   False, self.y, 0, self.tp, self.epoch, self.sig.data_ptr(), [p.data_ptr() for p in self.peer_sig],
-                   self.pub.data_ptr(), self.pub_base, self.ready.data_ptr(), self.ready_base, self.grid,
-                   self.variant, self.rb_ready.data_ptr(), self.rb_base)
-        step = kx.fused_counter_step(self.grid, self.variant)
-        self.pub_base += step
-        if self.variant == 0:
-            self.ready_base += step
-        else:
-            self.rb_base += kx.fused_block_step(self.t, self.n, self.tp, self.grid)
-        return self.y
+        return self.em.all_gather_gemm(self.w, keep_gathered=self.keep)[0]
 
 
 class RsSession:
-    """Repeated emulated GEMM->RS launches of rank 0 (peer tile flags preset far ahead)."""
+    """Repeated emulated GEMM->RS (or GEMM->AR) launches of rank 0, for timing and captures."""
 
-    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, variant: int = 0, device="cuda"):
-        self.kx = _ext.require()
-        dev = torch.device(device)
-        rows = tokens // tp
-        self.tp, self.variant = tp, variant
-        self.h = torch.randn(tokens, k, device=dev).bfloat16()
-        self.w = (torch.randn(n, k, device=dev) / k**0.5).bfloat16()
-        self.parts = [torch.empty(tokens, n, device=dev, dtype=torch.bfloat16) for _ in range(tp)]
-        tiles = (tokens // 128) * ((n + 255) // 256)
-        self.own_flags = _u32(tiles, dev)
-        self.peer_flags = [self.own_flags] + [_u32(tiles, dev, 1 << 30) for _ in range(1, tp)]
-        self.recv = torch.empty(tp, rows, n, device=dev, dtype=torch.bfloat16)
-        self.y = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
-        self.grid = self.kx.fused_grid(tokens, n, tp)
-        self.epoch = 0
+    def __init__(self, tokens: int, k: int, n: int, *, tp: int = 2, all_reduce: bool = False, device="cuda"):
+        self.em = Emulation(tokens, n, tp=tp, device=device)
+        self.h = torch.randn(tokens, k, device=device).bfloat16()
+        self.w = (torch.randn(n, k, device=device) / k**0.5).bfloat16()
+        self.all_reduce = all_reduce
 
     def launch(self):
-        self.epoch += 1
-        self.kx.gemm_rs(self.h, self.w, False, self.y, 0, self.tp, self.epoch, self.parts[0].data_ptr(),
-                        [p.data_ptr() for p in self.parts], self.own_flags.data_ptr(),
-                        [f.data_ptr() for f in self.peer_flags], self.recv.data_ptr(), self.grid, self.variant)
-        return self.y
+        if self.all_reduce:
+            return self.em.gemm_all_reduce(self.h, self.w)
+        return self.em.gemm_reduce_scatter(self.h, self.w)

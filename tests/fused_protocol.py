@@ -1,16 +1,18 @@
-"""A model of the fused TP kernels' cross-GPU protocol, for race and deadlock checks.
+"""A model of the fused kernels' cross-GPU protocols, for race and deadlock checks.
 
-Mirrors ``resihp/csrc/fused_gemm.cu`` at the level of what synchronises: every copy
-warp, TMA producer and epilogue of every CTA of every rank is an agent; flag words and
-counters are shared integers; data buffers hold, per row or tile, the epoch whose values
-they contain. A random scheduler interleaves the agents (each rank's calls run in stream
-order), every wait blocks until its condition holds, and every read of data checks that
-the data is the epoch being computed -- a stale or overwritten row is a race. If no agent
-can move while some are unfinished, the protocol deadlocked (the kernels' bounded waits
-would report error code 4). The host side -- the counter bases advanced per call and
-the per-call targets -- comes from the extension's own host functions, so a mismatch
-between what the host expects and what the kernel's warps add (the bug class met on a
-GPU once) shows up here as a deadlock.
+Mirrors ``resihp/csrc/fused_gemm.cu`` (and the DP step of ``peer_state.cu``) at the level
+of what synchronises. Every tile producer, epilogue and copy-warp group of every CTA of
+every rank is an agent; counter words and claim counters are shared integers; data
+buffers hold, per row block or tile, the epoch whose values they contain. A random
+scheduler interleaves the agents (each rank's calls run in stream order; a rank starts
+call e+1 once every agent of call e finished), every wait blocks until its condition
+holds, and every read checks that the data is the epoch being computed -- a stale or
+already overwritten block is a race. If no agent can move while some are unfinished,
+the protocol deadlocked (the kernels' bounded waits would report error code 4). Work is
+claimed from per-rank counters as in the kernels, and the host side -- the bases
+advanced per call -- comes from the extension's own host functions, so a host that
+advances by a different count than the kernel claims shows up here (as a missed or
+repeated tile, a race or a deadlock).
 """
 
 from __future__ import annotations
@@ -20,6 +22,8 @@ import random
 from resihp.ops import _ext
 
 FBM = 128
+RING = 4  # tile ring depth between a CTA's producer and its epilogue
+MODES = {"ag": 1, "rs": 2, "ar": 3}
 
 
 class ProtocolError(AssertionError):
@@ -41,170 +45,176 @@ def fused_tile(t, tiles_m_chunk, tiles_n, rank, tp, first, rows_per_rank):
 
 
 class _Rank:
-    def __init__(self, tp, rows_per_rank, tiles):
-        t = rows_per_rank * tp
-        self.sig = [0] * 8
-        self.pub = 0
-        self.ready = [0] * tp
-        self.rb_ready = [0] * (t // FBM)
-        self.slot = [[None] * rows_per_rank, [None] * rows_per_rank]
-        self.xg = [None] * t
-        self.part = [dict(), dict()]
-        self.flags = [0] * tiles
-        self.recv = {}
-        self.pulled = {}
-        # host bookkeeping of the workspace
-        self.pub_base = self.ready_base = self.rb_base = 0
+    def __init__(self, tp, blocks, per_chunk):
+        self.ag_cnt = [[0] * blocks for _ in range(tp)]         # [src][row block] push units landed
+        self.land = [dict(), dict()]                            # parity -> {(chunk, row block): epoch}
+        self.rs_cnt = [[0] * per_chunk, [0] * per_chunk]        # [call parity][own tile] -> partial warps landed
+        self.recv = [dict(), dict()]                            # parity -> {(src, tile): epoch}
+        self.ar_cnt = [0] * (per_chunk * tp)                    # global tile -> reduced warps landed
+        self.out = [dict(), dict()]                             # parity -> {global tile: ar epoch}
+        self.ctr = {"tile": 0, "copy": 0}                       # claim counters (device)
+        self.base = {"tile": 0, "copy": 0}                      # what the host believes they hold
+        self.seen_tiles: list[int] = []
+        self.seen_items: list[int] = []
 
 
 class Simulation:
-    """``tp`` ranks running ``epochs`` calls of one op (``"ag"`` or ``"rs"``)."""
+    """``tp`` ranks running ``epochs`` calls of one op (``"ag"``, ``"rs"`` or ``"ar"``)."""
 
-    def __init__(self, op, *, tp, rows_per_rank, n, grid, variant, epochs, seed, host_step=None):
+    def __init__(self, op, *, tp, rows_per_rank, n, grid, epochs, seed, slices=4, keep_gathered=True,
+                 copy_claims=None):
         self.k = _ext.require()
-        self.op, self.tp, self.rows, self.n, self.grid, self.variant = op, tp, rows_per_rank, n, grid, variant
-        self.epochs = epochs
+        self.op, self.mode = op, MODES[op]
+        self.tp, self.rows, self.n, self.grid, self.epochs = tp, rows_per_rank, n, grid, epochs
+        self.slices, self.keep = slices, keep_gathered
         self.rng = random.Random(seed)
-        self.cw = self.k.fused_counter_step(1, variant)            # copy warps per CTA
-        self.host_step = host_step or (lambda g: self.k.fused_counter_step(g, variant))
-        self.tiles_m_chunk = rows_per_rank // FBM
+        self.blocks = rows_per_rank // FBM
         self.tiles_n = (n + 255) // 256
-        self.tiles = self.tiles_m_chunk * self.tiles_n * tp
-        self.ranks = [_Rank(tp, rows_per_rank, self.tiles) for _ in range(tp)]
-        t_rows = rows_per_rank * tp
-        self.slices = self.k.fused_block_step(t_rows, n, tp, grid) // self.k.fused_counter_step(1, 1)
-
-    # --- agents (generators yielding wait predicates) ----------------------------------
-
-    def _rows_of(self, b, w):
-        lo = self.rows * b // self.grid
-        hi = self.rows * (b + 1) // self.grid
-        return list(range(lo + w, hi, self.cw))
-
-    def _ag_copy(self, r, b, w, e, pub_target):
-        me = self.ranks[r]
-        par = e % 2
-        for row in self._rows_of(b, w):                                 # publish
-            me.slot[par][row] = e
-            me.xg[r * self.rows + row] = e
-        yield lambda: True
-        me.pub += 1
-        if me.pub == pub_target:
-            for p in range(self.tp):
-                if p != r:
-                    self.ranks[p].sig[r] = e                            # announce to every peer
-        if self.variant == 0:
-            for step in range(1, self.tp):
-                c = (r + step) % self.tp
-                yield lambda c=c: me.sig[c] >= e
-                for row in self._rows_of(b, w):
-                    self._read(self.ranks[c].slot[par][row], e, f"AG slot of rank {c} row {row}")
-                    me.xg[c * self.rows + row] = e
-                yield lambda: True
-                me.ready[c] += 1
-        else:
-            blocks, s = self.tiles_m_chunk, self.slices
-            srows = FBM // s
-            units = (self.tp - 1) * blocks * s
-            for u in range(b, units, self.grid):
-                c = (r + 1 + u // (blocks * s)) % self.tp
-                rb = (u // s) % blocks
-                r0 = rb * FBM + (u % s) * srows
-                yield lambda c=c: me.sig[c] >= e
-                for row in range(r0 + w, r0 + srows, self.cw):
-                    self._read(self.ranks[c].slot[par][row], e, f"AG slot of rank {c} row {row}")
-                    me.xg[c * self.rows + row] = e
-                me.rb_ready[c * blocks + rb] += 1
-
-    def _ag_producer(self, r, b, e, ready_target, rb_target):
-        me = self.ranks[r]
-        for t in range(b, self.tiles, self.grid):
-            c, m0, _tn = fused_tile(t, self.tiles_m_chunk, self.tiles_n, r, self.tp, 0, self.rows)
-            if c == r:
-                continue
-            if self.variant == 0:
-                yield lambda c=c: me.ready[c] >= ready_target
-            else:
-                key = c * self.tiles_m_chunk + (m0 - c * self.rows) // FBM
-                yield lambda key=key: me.rb_ready[key] >= rb_target
-            for row in range(m0, m0 + FBM):
-                self._read(me.xg[row], e, f"AG gathered row {row} on rank {r}")
-
-    def _rs_tiles(self, r, b):
-        out = []
-        for t in range(b, self.tiles, self.grid):
-            c, m0, tn = fused_tile(t, self.tiles_m_chunk, self.tiles_n, r, self.tp, 1, self.rows)
-            out.append((c, (m0 // FBM) * self.tiles_n + tn))
-        return out
-
-    def _rs_epilogue(self, r, b, e):
-        me = self.ranks[r]
-        par = e % 2
-        j = 0
-        for c, flag in self._rs_tiles(r, b):
-            if c != r:
-                me.part[par][flag] = e                                  # partial tile of a peer's rows
-                me.flags[flag] += 4                                     # four epilogue warps
-                yield lambda: True
-            else:
-                yield lambda j=j: me.pulled.get((e, b, j), 0) >= self.cw
-                for src in range(self.tp):
-                    if src != r:
-                        self._read(me.recv.get((src, flag)), e, f"RS receive of tile {flag} from {src}")
-                j += 1
-
-    def _rs_copy(self, r, b, w, e):
-        me = self.ranks[r]
-        par = e % 2
-        j = 0
-        for c, flag in self._rs_tiles(r, b):
-            if c != r:
-                continue
-            peers = [s for s in range(self.tp) if s != r]
-            mine = peers if self.variant == 0 else [s for i, s in enumerate(peers) if i % self.cw == w]
-            pending = list(mine)
-            while pending:
-                if self.variant == 0:
-                    src = pending[0]
-                    yield lambda src=src: self.ranks[src].flags[flag] >= 4 * e
-                else:
-                    yield lambda: any(self.ranks[s].flags[flag] >= 4 * e for s in pending)
-                    src = next(s for s in pending if self.ranks[s].flags[flag] >= 4 * e)
-                self._read(self.ranks[src].part[par].get(flag), e, f"RS partial tile {flag} of rank {src}")
-                me.recv[(src, flag)] = e
-                pending.remove(src)
-            me.pulled[(e, b, j)] = me.pulled.get((e, b, j), 0) + 1
-            j += 1
+        self.per_chunk = self.blocks * self.tiles_n
+        self.tiles = self.per_chunk * tp
+        self.t_rows = rows_per_rank * tp
+        self.copy_claims = copy_claims or (lambda: self.k.fused_copy_claims(self.mode, self.t_rows, self.n, self.tp,
+                                                                           self.slices, self.keep, self.grid))
+        self.ranks = [_Rank(tp, self.blocks, self.per_chunk) for _ in range(tp)]
 
     def _read(self, version, e, what):
         if version != e:
             raise ProtocolError(f"race: {what} holds epoch {version}, expected {e}")
 
+    def _claim(self, me, kind, limit):
+        got = me.ctr[kind] - me.base[kind]
+        me.ctr[kind] += 1
+        return got if 0 <= got < limit else -1
+
+    # --- agents (generators yielding wait predicates) ----------------------------------
+
+    def _producer(self, r, e, queue):
+        """Claims tiles (at most RING ahead of the epilogue) and loads their inputs."""
+        me = self.ranks[r]
+        par = e % 2
+        first = 0 if self.op == "ag" else 1
+        while True:
+            yield lambda: queue["claimed"] - queue["done"] < RING
+            t = self._claim(me, "tile", self.tiles)
+            if t < 0:
+                queue["items"].append(None)
+                queue["claimed"] += 1
+                return
+            me.seen_tiles.append(t)
+            c, m0, tn = fused_tile(t, self.blocks, self.tiles_n, r, self.tp, first, self.rows)
+            rb = (m0 - c * self.rows) // FBM
+            if self.op == "ag" and c != r:
+                yield lambda c=c, rb=rb: me.ag_cnt[c][rb] >= self.slices * e
+                self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} on rank {r}")
+            queue["items"].append((c, rb, tn))
+            queue["claimed"] += 1
+
+    def _epilogue(self, r, e, queue, ar_e):
+        me = self.ranks[r]
+        par = e % 2
+        i = 0
+        while True:
+            yield lambda i=i: len(queue["items"]) > i
+            item = queue["items"][i]
+            i += 1
+            queue["done"] += 1
+            if item is None:
+                return
+            c, rb, tn = item
+            local = rb * self.tiles_n + tn
+            if self.op == "ag":
+                continue
+            if c != r:
+                owner = self.ranks[c]
+                owner.recv[par][(r, local)] = e                     # partial pushed into the owner
+                yield lambda: True
+                owner.rs_cnt[par][local] += 4                       # four epilogue warps count it
+                continue
+            yield lambda local=local: me.rs_cnt[par][local] >= 4 * (self.tp - 1) * ((e + 1) // 2)
+            for src in range(self.tp):
+                if src != r:
+                    self._read(me.recv[par].get((src, local)), e, f"RS receive of tile {local} from {src} on {r}")
+            if self.op == "ar":
+                gtile = (c * self.blocks + rb) * self.tiles_n + tn
+                for p in range(self.tp):
+                    if p != r:
+                        self.ranks[p].out[ar_e % 2][gtile] = ar_e
+                yield lambda: True
+                for p in range(self.tp):
+                    if p != r:
+                        self.ranks[p].ar_cnt[gtile] += 4
+
+    def _copy(self, r, e, ar_e, xg):
+        me = self.ranks[r]
+        par = e % 2
+        units = self.blocks * self.slices
+        n_push = (self.tp - 1) * units if self.op == "ag" else 0
+        n_xg = self.tp * units if (self.op == "ag" and self.keep) else 0
+        n_ar = (self.tp - 1) * self.per_chunk if self.op == "ar" else 0
+        items = n_push + n_xg + n_ar
+        if items == 0:
+            return
+        while True:
+            it = self._claim(me, "copy", items)
+            yield lambda: True
+            if it < 0:
+                return
+            me.seen_items.append(it)
+            if it < n_push:
+                j, u = divmod(it, units)
+                dest = (r - j - 1) % self.tp
+                rb = u // self.slices
+                peer = self.ranks[dest]
+                key = (r, rb)
+                # one unit's rows; the block's value is that of the last unit written
+                peer.land[par][key] = e
+                yield lambda: True
+                peer.ag_cnt[r][rb] += 1
+            elif it < n_push + n_xg:
+                i2 = it - n_push
+                c = (r + i2 // units) % self.tp
+                rb = (i2 % units) // self.slices
+                if c != r:
+                    yield lambda c=c, rb=rb: me.ag_cnt[c][rb] >= self.slices * e
+                    self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} (xg) on {r}")
+                xg[(c, rb)] = xg.get((c, rb), 0) + 1
+            else:
+                i3 = it - n_push - n_xg
+                c = (r + 1 + i3 // self.per_chunk) % self.tp
+                lt = i3 % self.per_chunk
+                gtile = (c * self.blocks + lt // self.tiles_n) * self.tiles_n + lt % self.tiles_n
+                yield lambda g=gtile: me.ar_cnt[g] >= 4 * ar_e
+                self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
+
     # --- the scheduler -------------------------------------------------------------------
 
     def _call_agents(self, r, e):
         me = self.ranks[r]
-        step = self.host_step(self.grid)
+        me.seen_tiles, me.seen_items = [], []
+        self._xg = getattr(self, "_xg", {})
+        self._xg[r] = {}
         agents = []
-        if self.op == "ag":
-            pub_target = me.pub_base + step
-            ready_target = me.ready_base + step
-            rb_target = me.rb_base + self.k.fused_block_step(self.rows * self.tp, self.n, self.tp, self.grid)
-            for b in range(self.grid):
-                agents.append(self._ag_producer(r, b, e, ready_target, rb_target))
-                for w in range(self.cw):
-                    agents.append(self._ag_copy(r, b, w, e, pub_target))
-            me.pub_base += step
-            if self.variant == 0:
-                me.ready_base += step
-            else:
-                me.rb_base += self.k.fused_block_step(self.rows * self.tp, self.n, self.tp, self.grid)
-        else:
-            for b in range(self.grid):
-                agents.append(self._rs_epilogue(r, b, e))
-                for w in range(self.cw):
-                    agents.append(self._rs_copy(r, b, w, e))
+        for _ in range(self.grid):
+            queue = {"items": [], "claimed": 0, "done": 0}
+            agents.append(self._producer(r, e, queue))
+            agents.append(self._epilogue(r, e, queue, e))
+            agents.append(self._copy(r, e, e, self._xg[r]))
         return agents
+
+    def _finish_call(self, r, e):
+        me = self.ranks[r]
+        if sorted(me.seen_tiles) != list(range(self.tiles)):
+            raise ProtocolError(f"call {e} on rank {r} computed tiles {sorted(me.seen_tiles)}, not each tile once")
+        if self.op == "ag" and self.keep:
+            units = self.blocks * self.slices
+            full = {(c, rb): self.slices for c in range(self.tp) for rb in range(self.blocks)}
+            if self._xg[r] != full or len(me.seen_items) != (2 * self.tp - 1) * units:
+                raise ProtocolError(f"call {e} on rank {r}: gathered copy incomplete")
+        # the host advances its bases by what the extension says a launch claims
+        me.base["tile"] += self.k.fused_tile_claims(self.t_rows, self.n, self.grid)
+        me.base["copy"] += self.copy_claims()
+        if me.base["tile"] != me.ctr["tile"] or me.base["copy"] != me.ctr["copy"]:
+            raise ProtocolError(f"race: host bases {me.base} disagree with the claim counters {me.ctr} on rank {r}")
 
     def run(self) -> int:
         """Interleave every call of every rank; return the number of scheduling steps."""
@@ -226,6 +236,7 @@ class Simulation:
             except StopIteration:
                 live[r].remove(slot)
                 if not live[r]:
+                    self._finish_call(r, epoch[r])
                     epoch[r] += 1
                     if epoch[r] > self.epochs:
                         del live[r]
@@ -238,24 +249,34 @@ class Simulation:
 class DpSimulation:
     """``dp`` replicas running ``epochs`` training steps, each: backward accumulates into
     the current gradient buffer, then the fused DP kernel (``peer_state.cu``) -- per CTA:
-    announce the epoch in every peer's flag array, wait for every peer's announcement,
-    read every replica's current buffer for the CTA's slice, write the sum into the other
-    buffer -- after which the buffers swap roles (the next backward zeroes and fills the
-    summed one)."""
+    announce the epoch in every peer's flag array and wait for every peer's; then either
+    (one-phase) read every replica's current buffer for the CTA's slice and write the sum
+    into the local other buffer, or (``push``) reduce this replica's part of the slice
+    from every replica's current buffer, push the sum into every replica's other buffer,
+    flag it in a second flag array, wait for every peer's part, and read the whole slice
+    from the local other buffer -- after which the buffers swap roles (the next backward
+    zeroes and fills the summed one)."""
 
-    def __init__(self, *, dp, grid, epochs, seed):
-        self.dp, self.grid, self.epochs = dp, grid, epochs
+    def __init__(self, *, dp, grid, epochs, seed, push=False):
+        self.dp, self.grid, self.epochs, self.push = dp, grid, epochs, push
         self.rng = random.Random(seed)
-        # per replica: flag words [grid][dp], two gradient buffers of per-slice versions
+        # per replica: flag words [grid][dp] (two arrays), two gradient buffers of
+        # per-(slice, part) versions
         self.flags = [[[0] * dp for _ in range(grid)] for _ in range(dp)]
-        self.grads = [[[None] * grid, [None] * grid] for _ in range(dp)]
+        self.flags2 = [[[0] * dp for _ in range(grid)] for _ in range(dp)]
+        self.grads = [[dict(), dict()] for _ in range(dp)]
         self.parity = [0] * dp
 
     def _backward(self, r, e):
         cur = self.parity[r]
         for b in range(self.grid):
-            self.grads[r][cur][b] = ("acc", e)                          # zeroed, then accumulated
+            for q in range(self.dp):
+                self.grads[r][cur][(b, q)] = ("acc", e)                 # zeroed, then accumulated
             yield lambda: True
+
+    def _check(self, got, want, what):
+        if got != want:
+            raise ProtocolError(f"race: {what} holds {got}, expected {want}")
 
     def _cta(self, r, b, e):
         cur = self.parity[r]
@@ -263,13 +284,27 @@ class DpSimulation:
             if q != r:
                 self.flags[q][b][r] = max(self.flags[q][b][r], e)       # release store of the epoch
         yield lambda: all(self.flags[r][b][q] >= e for q in range(self.dp) if q != r)
+        if not self.push:
+            for q in range(self.dp):
+                for part in range(self.dp):
+                    self._check(self.grads[q][cur].get((b, part)), ("acc", e), f"replica {q} slice {b}")
+                yield lambda: True
+            for part in range(self.dp):
+                self.grads[r][1 - cur][(b, part)] = ("sum", e)
+            return
         for q in range(self.dp):
-            # every replica's buffer of this epoch holds this step's accumulation
-            got = self.grads[q][cur][b]
-            if got != ("acc", e):
-                raise ProtocolError(f"race: replica {q} slice {b} holds {got}, expected the epoch-{e} gradients")
+            self._check(self.grads[q][cur].get((b, r)), ("acc", e), f"replica {q} slice {b} part {r}")
             yield lambda: True
-        self.grads[r][1 - cur][b] = ("sum", e)
+        for q in range(self.dp):
+            # the same buffer index in every replica's region (the layouts are identical)
+            self.grads[q][1 - cur][(b, r)] = ("sum", e)
+            yield lambda: True
+        for q in range(self.dp):
+            if q != r:
+                self.flags2[q][b][r] = max(self.flags2[q][b][r], e)
+        yield lambda: all(self.flags2[r][b][q] >= e for q in range(self.dp) if q != r)
+        for part in range(self.dp):
+            self._check(self.grads[r][1 - cur].get((b, part)), ("sum", e), f"replica {r} sum slice {b} part {part}")
 
     def run(self) -> int:
         phase = {r: ("backward", 1) for r in range(self.dp)}

@@ -1,49 +1,97 @@
-"""Fused AG->GEMM / GEMM->RS kernels on ONE GPU, peers emulated by local buffers.
+"""Fused AG->GEMM / GEMM->RS / GEMM->AR kernels on ONE GPU, peers emulated by local buffers.
 
-The launch of group rank 0 reads "peer" chunks / partials from second buffers on the
-same device whose flag words are set beforehand, so no launch waits on another (see
-``resihp.utils.fused_emulation``). Results are compared with an FP32 torch product for
-TP degrees 2, 4 and 8 -- the kernels' gather, tile order, per-chunk readiness and
-rank-ordered reduction are all exercised without a second GPU.
+Group rank 0 launches; the "peers" are second workspaces on the same device whose data
+and counters are preset as if the peers had already pushed (see
+``resihp.utils.fused_emulation``), so no launch waits on another. Checked for TP degrees
+2, 4 and 8 against an FP32 torch product: the output, the gathered input kept for the
+backward pass, and what rank 0 itself pushed into the peers' workspaces -- its chunk in
+every peer's landing zone (AG), its partial tiles in each owner's receive buffer (RS),
+its reduced tiles in every peer's output landing zone (AR) -- with the counter
+increments the peers would wait on.
 """
-
-import os
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-# The row-block variant (TP > 2) joins these tests once it has been measured on GPUs.
-VARIANTS = [0, 1] if os.environ.get("RESIHP_FUSED_TP_V3", "0") == "1" else [0]
+T, K, N = 1024, 512, 768
 
 
 def _rel(a, b):
     return ((a.float() - b).norm() / b.norm()).item()
 
 
-@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("tp", [2, 4, 8])
-def test_emulated_ag_gemm(tp, variant):
+def test_emulated_ag_gemm(tp):
     from resihp.ops import check_device_errors
-    from resihp.utils.fused_emulation import emulate_ag
+    from resihp.parallel import fused
+    from resihp.utils.fused_emulation import Emulation
 
-    for epoch in (1, 2):
-        y, ref, xg, x_full = emulate_ag(1024, 512, 768, tp=tp, epoch=epoch, seed=tp + epoch, variant=variant)
+    em = Emulation(T, K, tp=tp, seed=tp)
+    w = (torch.randn(N, K, device="cuda") / K**0.5).bfloat16()
+    for call in (1, 2, 3):
+        y, xg = em.all_gather_gemm(w)
         torch.cuda.synchronize()
         check_device_errors(0)
-        assert torch.equal(xg, x_full)  # the gather buffer holds the whole gathered input
-        assert _rel(y, ref) < 1e-2
+        assert torch.equal(xg, em.x)  # the whole gathered input, for the weight gradient
+        assert _rel(y, em.x.float() @ w.float().t()) < 1e-2
+        parity = call % 2
+        blocks = em.rpr // 128
+        for peer in range(1, tp):
+            land = em.buf(peer, em.land_off, parity, (T, K))
+            assert torch.equal(land[:em.rpr], em.x[:em.rpr])  # rank 0's chunk, rows 0..T/tp
+            cnt = em.u32(peer, fused._AG_CNT, fused.MAX_TP * fused.MAX_RB).view(fused.MAX_TP, fused.MAX_RB)
+            assert torch.equal(cnt[0, :blocks].cpu(), torch.full((blocks,), em.slices * call, dtype=torch.int32))
+            assert int(cnt[0, blocks:].abs().sum()) == 0
 
 
-@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("tp", [2, 4, 8])
-def test_emulated_gemm_rs(tp, variant):
+def test_emulated_ag_gemm_mn_weight(tp):
+    """The backward form (``w`` read N-major: ``dy_gathered @ w``) without a gathered copy."""
     from resihp.ops import check_device_errors
-    from resihp.utils.fused_emulation import emulate_rs
+    from resihp.utils.fused_emulation import Emulation
 
-    for epoch in (1, 2):
-        y, ref = emulate_rs(1024, 512, 768, tp=tp, epoch=epoch, seed=10 * tp + epoch, variant=variant)
+    em = Emulation(T, K, tp=tp, seed=3 * tp)
+    w = (torch.randn(K, N, device="cuda") / K**0.5).bfloat16()
+    y, xg = em.all_gather_gemm(w, w_mn=True, keep_gathered=False)
+    torch.cuda.synchronize()
+    check_device_errors(0)
+    assert xg is None and _rel(y, em.x.float() @ w.float()) < 1e-2
+
+
+@pytest.mark.parametrize("all_reduce", [False, True], ids=["rs", "ar"])
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_emulated_gemm_rs_ar(tp, all_reduce):
+    from resihp.ops import check_device_errors
+    from resihp.parallel import fused
+    from resihp.utils.fused_emulation import Emulation
+
+    em = Emulation(T, N, tp=tp, seed=10 * tp)
+    g = torch.Generator(device="cuda").manual_seed(5 + tp)
+    hs = [torch.randn(T, K, device="cuda", generator=g).bfloat16() for _ in range(tp)]
+    ws = [(torch.randn(N, K, device="cuda", generator=g) / K**0.5).bfloat16() for _ in range(tp)]
+    ref = em.preset_partials(hs, ws, all_reduce=all_reduce)
+    tiles_n = (N + 255) // 256
+    per_chunk = (em.rpr // 128) * tiles_n
+    from resihp.ops import linear
+
+    mine = linear(hs[0], ws[0])  # this package's GEMM: the same accumulation order as the fused kernel
+    for call in (1, 2):
+        y = em.gemm_all_reduce(hs[0], ws[0]) if all_reduce else em.gemm_reduce_scatter(hs[0], ws[0])
         torch.cuda.synchronize()
         check_device_errors(0)
+        assert y.shape[0] == (T if all_reduce else em.rpr)
         assert _rel(y, ref) < 1e-2
+        parity = call % 2
+        for owner in range(1, tp):
+            # rank 0's partial of the owner's rows, in the owner's receive buffer slot 0
+            recv = em.buf(owner, em.recv_off, parity, (tp, em.rpr * N)).view(tp, em.rpr, N)
+            assert torch.equal(recv[0], mine[owner * em.rpr:(owner + 1) * em.rpr])
+            bank = em.u32(owner, fused._RS_CNT, 2 * fused.MAX_TILES).view(2, fused.MAX_TILES)[call % 2]
+            assert torch.equal(bank[:per_chunk].cpu(), torch.full((per_chunk,), 4, dtype=torch.int32))
+            if all_reduce:
+                out = em.buf(owner, em.out_off, parity, (T, N))
+                assert torch.equal(out[:em.rpr], y[:em.rpr])  # rank 0's reduced rows pushed to every peer
+                arc = em.u32(owner, fused._AR_CNT, fused.MAX_TILES)
+                assert torch.equal(arc[:per_chunk].cpu(), torch.full((per_chunk,), 4 * call, dtype=torch.int32))

@@ -1,8 +1,10 @@
-"""Fused AG->GEMM and GEMM->RS kernels against NCCL + FP32 torch, on 2+ GPUs.
+"""Fused AG->GEMM, GEMM->RS and GEMM->AR kernels against NCCL + FP32 torch, on 2+ GPUs.
 
-Spawns one process per GPU (up to 8); each compares the fused forward and backward
-against all-gather / reduce-scatter on NCCL followed by an FP32 torch product.
-Skipped with fewer than two GPUs.
+Spawns one process per GPU (up to 8); each compares the fused forward and backward --
+the sequence-parallel pair and the all-reduce forms used without sequence parallelism
+-- against all-gather / reduce-scatter / all-reduce on NCCL followed by an FP32 torch
+product, and checks that every rank holds the same all-reduced bits. Skipped with
+fewer than two GPUs.
 """
 
 import os
@@ -25,7 +27,7 @@ def _worker(rank, world, port, out):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
     from resihp.ops import check_device_errors
-    from resihp.parallel.fused import SymmetricWorkspace, ag_linear, linear_rs
+    from resihp.parallel.fused import SymmetricWorkspace, ag_linear, col_linear_ar, linear_rs, row_linear_ar
 
     g = torch.Generator(device="cuda").manual_seed(1234)
     d, n, t = 512, 768, 256 * world
@@ -70,6 +72,30 @@ def _worker(rank, world, port, out):
         errs[f"rs_dh{it}"] = ((h.grad.float() - ref_dh).norm() / ref_dh.norm()).item()
         ref_dw2 = dyg.t() @ h.detach().float()
         errs[f"rs_dw{it}"] = ((mg2 - ref_dw2).norm() / ref_dw2.norm()).item()
+        # without sequence parallelism: every rank holds all tokens; the row linear's output
+        # and the column linear's input gradient are all-reduced inside their GEMMs
+        xr = x_full.detach().clone().requires_grad_()
+        mg3 = torch.zeros(n, d, device="cuda")
+        yc = col_linear_ar(xr, w1, mg3, ws)
+        errs[f"cl_fwd{it}"] = ((yc.float() - ref).norm() / ref.norm()).item()
+        yc.backward(dy_full)
+        ref_dx_full = sum(parts)
+        errs[f"cl_dx{it}"] = ((xr.grad.float() - ref_dx_full).norm() / ref_dx_full.norm()).item()
+        errs[f"cl_dw{it}"] = ((mg3 - ref_dw).norm() / ref_dw.norm()).item()
+        hr = h.detach().clone().requires_grad_()
+        mg4 = torch.zeros(d, n, device="cuda")
+        ya = row_linear_ar(hr, w2, mg4, ws)
+        ref_ya = sum(allp)
+        errs[f"ar_fwd{it}"] = ((ya.float() - ref_ya).norm() / ref_ya.norm()).item()
+        same = [torch.empty_like(ya) for _ in range(world)]
+        dist.all_gather(same, ya.detach().contiguous())
+        errs[f"ar_same{it}"] = float(max((t.float() - ya.float()).abs().max().item() for t in same))
+        dya = dyg.bfloat16()  # replicated output gradient
+        ya.backward(dya)
+        ref_dha = dya.float() @ w2.float()
+        errs[f"ar_dh{it}"] = ((hr.grad.float() - ref_dha).norm() / ref_dha.norm()).item()
+        ref_dw4 = dya.float().t() @ h.detach().float()
+        errs[f"ar_dw{it}"] = ((mg4 - ref_dw4).norm() / ref_dw4.norm()).item()
     torch.cuda.synchronize()
     check_device_errors(rank)
     ws.close()
@@ -93,5 +119,5 @@ def test_fused_ag_gemm_and_gemm_rs(tmp_path):
     for r in range(world):
         errs = torch.load(tmp_path / f"errs_{r}.pt")
         for k, v in errs.items():
-            limit = 1e-3 if "dw" in k else 1.5e-2
-            assert v < limit, (r, k, v, errs)
+            limit = 0.0 if "same" in k else (1e-3 if "dw" in k else 1.5e-2)
+            assert v <= limit, (r, k, v, errs)

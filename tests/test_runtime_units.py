@@ -151,8 +151,8 @@ def test_dp_peers_step_passes_the_right_buffers(monkeypatch):
         def symm_region(self, total, device):
             return torch.zeros(total, dtype=torch.uint8), b"h"
 
-        def dp_allreduce_adamw(self, *args):
-            self.calls.append(args)
+        def dp_allreduce_adamw(self, *args, **kwargs):
+            self.calls.append(args + (kwargs,))
 
     stub = Stub()
     monkeypatch.setattr(_ext, "require", lambda: stub)
@@ -167,7 +167,7 @@ def test_dp_peers_step_passes_the_right_buffers(monkeypatch):
     stage.config = _config(dtype="bf16")
     stage.use_grad = flat.set_parity
     dp = peer.DpPeers.__new__(peer.DpPeers)
-    dp.rank, dp.bases, dp.grid, dp.epoch, dp.closed = 1, [1000, flat.region_ptr], 3, 0, False
+    dp.rank, dp.bases, dp.grid, dp.epoch, dp.closed, dp.push = 1, [1000, flat.region_ptr], 3, 0, False, False
     for expected_parity in (0, 1, 0):
         assert flat.parity == expected_parity
         dp.step(stage)
@@ -179,14 +179,23 @@ def test_dp_peers_step_passes_the_right_buffers(monkeypatch):
         assert args[3] is flat.master and args[4] is flat.exp_avg and args[5] is flat.exp_avg_sq
         assert args[6] is flat.work
         assert args[12] == flat.step and args[14] == flat.region_ptr and args[15] == [1000, flat.region_ptr]
-        assert args[16] == dp.epoch and args[17] == 3
+        assert args[16] == dp.epoch and args[17] == 3 and args[18] == {}
     assert flat.step == 3 and flat.parity == 1
+    # groups of three and more take the two-phase kernel: the peers' receiving buffers
+    # (the sum parity) and the second flag array, right after the first
+    dp.push = True
+    dp.step(stage)
+    extra = stub.calls[-1][18]  # the step read grad1 (parity 1) and sums into grad0
+    assert extra["sums_peer"] == [1000 + flat.field_offsets["grad0"], flat.region_ptr + flat.field_offsets["grad0"]]
+    assert extra["flags2_local"] == flat.region_ptr + 4 * peer.MAX_DP * 3
+    assert extra["flags2_peer"] == [1000 + 4 * peer.MAX_DP * 3, flat.region_ptr + 4 * peer.MAX_DP * 3]
 
 
 def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
-    """The fused TP workspace's host bookkeeping: per call the publish/ready bases grow by
-    the kernel module's own step (variant 0) or the row-block base does (variant 1), and
-    slots / partial buffers alternate by epoch."""
+    """The fused TP workspace's host bookkeeping: each call passes its epoch, the
+    buffers of this epoch's parity on every rank, and the claim counters' bases as they
+    stood before the call; the bases then grow by the kernel module's own claim counts
+    (AG on its pair of counters, RS and AR on theirs)."""
     import contextlib
 
     from resihp.ops import _ext
@@ -205,17 +214,20 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
         def fused_grid(self, t, n, tp):
             return 7
 
-        def fused_counter_step(self, grid, variant):
-            return (4 if variant == 0 else 6) * grid
+        def fused_slices(self, rows_per_rank):
+            return 16
 
-        def fused_block_step(self, t, n, tp, grid):
-            return 12
+        def fused_tile_claims(self, t, n, grid):
+            return 100 + grid
 
-        def ag_gemm(self, *args):
-            self.ag.append(args)
+        def fused_copy_claims(self, mode, t, n, tp, slices, xg, grid):
+            return {1: 50 if xg else 20, 2: 0, 3: 30}[mode] + (grid if mode != 2 else 0)
 
-        def gemm_rs(self, *args):
-            self.rs.append(args)
+        def ag_gemm(self, x_local, xg, w, w_mn, y, peers, grid):
+            self.ag.append((xg, peers, grid))
+
+        def gemm_rs(self, h, w, w_mn, y, all_reduce, peers, grid):
+            self.rs.append((y.shape, all_reduce, peers))
 
     stub = Stub()
     monkeypatch.setattr(_ext, "require", lambda: stub)
@@ -225,24 +237,38 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
     monkeypatch.setattr(fused.dist, "barrier", lambda group=None: None)
     monkeypatch.setattr(torch.cuda, "device", lambda d: contextlib.nullcontext())
     monkeypatch.setattr(torch.cuda, "synchronize", lambda d=None: None)
-    for v3, variant in ((False, 0), (True, 1)):
-        monkeypatch.setattr(fused, "ROW_BLOCK_VARIANT", v3)
-        ws = fused.SymmetricWorkspace(None, 128, 64, "cpu")
-        assert ws.variant == variant
-        x = torch.zeros(128, 64, dtype=torch.bfloat16)
-        w = torch.zeros(32, 64, dtype=torch.bfloat16)
-        for call in range(3):
-            ws.all_gather_gemm(x, w, False, 32)
-            args = stub.ag[-1]
-            assert args[9] == call + 1                                   # epoch
-            assert args[1] == ws._slot(ws.base, call + 1)                # own slot of this parity
-            assert args[13] == (4 if variant == 0 else 6) * 7 * call     # publish base before the call
-            assert args[17] == variant and args[18] == ws.base + 256
-            assert args[19] == (12 * call if variant == 1 else 0)
-        assert ws._slot(ws.base, 1) != ws._slot(ws.base, 2) and ws._slot(ws.base, 1) == ws._slot(ws.base, 3)
-        h = torch.zeros(512, 16, dtype=torch.bfloat16)
-        ws.gemm_reduce_scatter(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
-        assert stub.rs[-1][-1] == variant and stub.rs[-1][7] == ws._part(ws.base, 1)
+    ws = fused.SymmetricWorkspace(None, 128, 64, "cpu")
+    tp = 4
+    peers_of = [1 << 30, ws.base, 1 << 30, 1 << 30]  # this rank is group rank 1
+    assert ws.slices == 16 and ws.t == 512
+    x = torch.zeros(128, 64, dtype=torch.bfloat16)
+    w = torch.zeros(32, 64, dtype=torch.bfloat16)
+    for call in range(1, 4):
+        ws.all_gather_gemm(x, w, False, 32)
+        xg, peers, grid = stub.ag[-1]
+        assert xg is not None and tuple(xg.shape) == (512, 64) and grid == 7
+        assert peers[:6] == [1, tp, 128, 16, call, 0]                      # rank, tp, rows, slices, epoch, ar epoch
+        assert peers[6] == ws.base + fused._CTRS and peers[7] == (107 * (call - 1))      # AG tile counter, base
+        assert peers[8] == ws.base + fused._CTRS + 4 and peers[9] == (57 * (call - 1))   # AG copy counter, base
+        land = peers[10:10 + tp]
+        assert land == [b + ws.land_off + (call % 2) * ws.stride for b in peers_of]
+        assert peers[10 + tp:10 + 2 * tp] == [b + fused._AG_CNT for b in peers_of]
+    ws.all_gather_gemm(x, w, False, 32, keep_gathered=False)
+    assert stub.ag[-1][0] is None and stub.ag[-1][1][9] == 57 * 3
+    assert ws.bases[1] == 57 * 3 + 27                                         # no gathered copy: fewer items
+    h = torch.zeros(512, 16, dtype=torch.bfloat16)
+    ws.gemm_reduce_scatter(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
+    shape, ar, peers = stub.rs[-1]
+    assert tuple(shape) == (128, 64) and not ar and peers[4] == 1 and peers[5] == 0
+    assert peers[7] == 0 and peers[9] == 0                                    # RS counters start fresh
+    assert peers[10 + 2 * tp:10 + 3 * tp] == [b + ws.recv_off + ws.stride for b in peers_of]
+    ws.gemm_all_reduce(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
+    shape, ar, peers = stub.rs[-1]
+    assert tuple(shape) == (512, 64) and ar and peers[4] == 2 and peers[5] == 1
+    assert peers[7] == 107 and peers[9] == 0                                  # after one RS: tile claims only
+    assert peers[10 + 4 * tp:10 + 5 * tp] == [b + ws.out_off + ws.stride for b in peers_of]
+    assert peers[10 + 5 * tp:10 + 6 * tp] == [b + fused._AR_CNT for b in peers_of]
+    assert ws.bases == [107 * 4, 57 * 3 + 27, 107 * 2, 37]
 
 
 def test_control_plane_run_constants_must_match_the_config():
