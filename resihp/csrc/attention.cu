@@ -23,6 +23,8 @@
 //                  P^T = exp(S^T - lse), dS^T = P^T (dP^T - Delta), then
 //                  dV += P^T dO and dK += dS^T Q accumulated in TMEM.
 //   attn_bwd_dq    one CTA per (q block, q head, batch): S, dP recomputed, dQ += dS K.
+//   Both run the kv (dK/dV) or q (dQ) side in sub-blocks of 64 rows with double-buffered
+//   TMEM scores and eight elementwise warps (see the kernels).
 //   The same smem tile of dS^T serves as K-major A (for dK) -- and the dQ kernel writes
 //   its own dS tile K-major for dQ += dS K.
 // All waits are bounded (common.cuh) and report into the error word.
@@ -103,16 +105,20 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + ST;
-  uint64_t* kv_empty = v_full + ST;
-  uint64_t* s_full = kv_empty + ST;
+  uint64_t* k_empty = v_full + ST;   // K of a stage read by its S MMAs (refilled a step before V)
+  uint64_t* v_empty = k_empty + ST;  // V of a stage read by its PV MMAs
+  uint64_t* s_full = v_empty + ST;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* pv_done = p_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
 
-  const int qblk = (a.seq / kBlk) - 1 - blockIdx.x;   // heaviest causal rows first
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  // CTAs are dispatched in linear order with x fastest: the causal block is the slowest
+  // grid dimension, so every (head, batch) pair's longest block goes first (longest
+  // processing time first keeps the last wave short)
+  const int qblk = (a.seq / kBlk) - 1 - blockIdx.z;
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
   const int kvh = h / (a.hq / a.hkv);
   const int nblk = qblk + 1;
   const int row0 = b * a.seq + qblk * kBlk;
@@ -123,7 +129,8 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
@@ -146,20 +153,28 @@ __global__ void __launch_bounds__(192, 1)
       mbar_expect_tx(q_full, L::kQ);
       #pragma unroll
       for (int c = 0; c < D / 64; ++c) tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0, a.err);
-      for (int j = 0; j < nblk; ++j) {
-        const int st = j % ST;
-        const uint32_t n = j / ST;
-        if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, a.err, kErrTmaWait)) break;
-        const int kv_row = b * a.seq + j * kBlk;
-        mbar_expect_tx(&k_full[st], L::kKV);
-        #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(sk + st * L::kKV + c * kBlk * 128, &tm, &k_full[st], (a.hq + kvh) * D + 64 * c, kv_row, a.err);
-        mbar_expect_tx(&v_full[st], L::kKV);
-        #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(sv + st * L::kKV + c * kBlk * 128, &tm, &v_full[st], (a.hq + a.hkv + kvh) * D + 64 * c,
-                      kv_row, a.err);
+      // K runs one block ahead of V: K_j as soon as S_{j-ST} has read its stage, then
+      // V_{j-1} once PV_{j-1-ST} has read its stage
+      for (int j = 0; j <= nblk; ++j) {
+        if (j < nblk) {
+          const int st = j % ST;
+          if (!mbar_wait(&k_empty[st], ((j / ST) & 1) ^ 1, a.err, kErrTmaWait)) break;
+          mbar_expect_tx(&k_full[st], L::kKV);
+          #pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_2d(sk + st * L::kKV + c * kBlk * 128, &tm, &k_full[st], (a.hq + kvh) * D + 64 * c,
+                        b * a.seq + j * kBlk, a.err);
+        }
+        if (j >= 1) {
+          const int jv = j - 1;
+          const int st = jv % ST;
+          if (!mbar_wait(&v_empty[st], ((jv / ST) & 1) ^ 1, a.err, kErrTmaWait)) break;
+          mbar_expect_tx(&v_full[st], L::kKV);
+          #pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_2d(sv + st * L::kKV + c * kBlk * 128, &tm, &v_full[st], (a.hq + a.hkv + kvh) * D + 64 * c,
+                        b * a.seq + jv * kBlk, a.err);
+        }
       }
     }
   } else if (warp == 1) {
@@ -182,7 +197,7 @@ __global__ void __launch_bounds__(192, 1)
           umma_bf16(t_o, da, db, id_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
         return true;
       };
       for (int j = 0; j < nblk && ok; ++j) {
@@ -199,6 +214,7 @@ __global__ void __launch_bounds__(192, 1)
                     smem_desc_sw128(k_addr + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
         if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok) issue_pv(nblk - 1);
@@ -329,56 +345,89 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t o
 }
 
 // ---- backward: dK, dV ----------------------------------------------------------------
+//
+// One CTA per (kv block of 128 rows, kv head, batch), looping over every q head of the
+// group and every causal q sub-block of 64 rows. Sixty-four q rows per step keep
+// S^T / dP^T small enough (2 x 64 TMEM columns each) to double-buffer next to the dV and
+// dK accumulators; Q / dO / lse / delta come through a three-stage ring (their loads run
+// two steps ahead, off the critical path) and the P^T / dS^T tiles are double-buffered in
+// shared memory, so step i+1's S^T and dP^T MMAs run while the elementwise warps turn
+// step i into P^T and dS^T, and step i's dV / dK MMAs run while they do step i+1:
+//   warp 0      TMA: K, V once; then Q_i, dO_i (64 rows) and their lse / delta rows
+//   warp 1      MMA: S^T_i = K Q_i^T, dP^T_i = V dO_i^T (128 x 64), then dV += P^T_{i-1} dO_{i-1},
+//               dK += dS^T_{i-1} Q_{i-1} (128 x D)
+//   warps 2-9   elementwise, two warps per TMEM lane quadrant (32 q columns each):
+//               P^T = exp2(S^T * scale*log2e - lse*log2e) (causal mask on the diagonal),
+//               dS^T = P^T (dP^T - Delta), both as bf16 into 128B-swizzled K-major tiles.
+constexpr int kQs = 64;             // q rows per dK/dV step
+constexpr int kQdStages = 3;        // Q / dO / lse / delta ring: loads run two steps ahead
+constexpr int kEwWarps = 8;         // elementwise warps
+constexpr int kDkdvThreads = 64 + 32 * kEwWarps;
 
 template <int D>
 struct DkdvSmem {
-  static constexpr int kT = kBlk * D * 2;   // one 128 x D bf16 tile
-  static constexpr int kP = kBlk * kBlk * 2;
-  static constexpr int kBytes = 4 * kT + 2 * kP + 2 * kBlk * 4 + 1024 + 256;
+  static constexpr int kKV = kBlk * D * 2;   // K or V tile
+  static constexpr int kQ = kQs * D * 2;     // one Q or dO tile of 64 rows
+  static constexpr int kP = kBlk * kQs * 2;  // one P^T or dS^T tile [128 kv, 64 q]
+  static constexpr int kBytes = 2 * kKV + 2 * kQdStages * kQ + 4 * kP + 2 * kQdStages * kQs * 4 + 1024 + 256;
 };
 
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
-    attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
-                         AttnArgs a) {
+__global__ void __launch_bounds__(kDkdvThreads, 1)
+    attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
   using L = DkdvSmem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
   uint8_t* sk = smem;
-  uint8_t* sv = sk + L::kT;
-  uint8_t* sq = sv + L::kT;
-  uint8_t* sdo = sq + L::kT;
-  uint8_t* spt = sdo + L::kT;   // P^T  [kv, q] K-major
-  uint8_t* sdst = spt + L::kP;  // dS^T [kv, q] K-major
-  float* s_lse = reinterpret_cast<float*>(sdst + L::kP);   // per q row: lse * log2e
-  float* s_delta = s_lse + kBlk;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + kBlk);
+  uint8_t* sv = sk + L::kKV;
+  constexpr int QS = kQdStages;
+  uint8_t* sq = sv + L::kKV;          // QS stages
+  uint8_t* sdo = sq + QS * L::kQ;     // QS stages
+  uint8_t* spt = sdo + QS * L::kQ;    // 2 stages of P^T  [kv, q] K-major
+  uint8_t* sdst = spt + 2 * L::kP;    // 2 stages of dS^T [kv, q] K-major
+  float* s_lse = reinterpret_cast<float*>(sdst + 2 * L::kP);   // [QS][kQs]
+  float* s_delta = s_lse + QS * kQs;                            // [QS][kQs]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + QS * kQs);
   uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;     // Q_i, dO_i (and lse/delta) landed
-  uint64_t* qd_empty = bars + 2;    // the MMAs reading Q_i, dO_i are done
-  uint64_t* sp_full = bars + 3;     // S^T and dP^T ready in TMEM
-  uint64_t* sp_empty = bars + 4;    // softmax finished reading S^T / dP^T
-  uint64_t* ds_full = bars + 5;     // P^T and dS^T written to smem
-  uint64_t* acc_done = bars + 6;    // dV/dK MMAs of this step done (smem P^T/dS^T free)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint64_t* qd_full = bars + 1;          // [QS] Q, dO, lse, delta of a step landed
+  uint64_t* qd_empty = qd_full + QS;     // [QS] the dV/dK MMAs reading that step's Q, dO are done
+  uint64_t* st_full = qd_empty + QS;     // [2] S^T, dP^T of a step in TMEM
+  uint64_t* st_empty = st_full + 2;      // [2] the elementwise warps read them
+  uint64_t* ds_full = st_empty + 2;      // [2] P^T, dS^T of a step in smem
+  uint64_t* ds_empty = ds_full + 2;      // [2] the dV/dK MMAs reading them are done
+  uint64_t* acc_done = ds_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
 
-  const int kvblk = blockIdx.x;
-  const int g = blockIdx.y;
-  const int b = blockIdx.z;
+  const int kvblk = blockIdx.z;  // slowest grid dimension: the longest causal ranges go first
+  const int g = blockIdx.x;
+  const int b = blockIdx.y;
   const int group = a.hq / a.hkv;
-  const int nq = a.seq / kBlk - kvblk;          // causal: q blocks kvblk .. end
+  const int nq = a.seq / kQs - 2 * kvblk;  // causal: q sub-blocks 2*kvblk .. end
   const int steps = nq * group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_row0 = b * a.seq + kvblk * kBlk;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qd_full, 1);
-    mbar_init(qd_empty, 1);
-    mbar_init(sp_full, 1);
-    mbar_init(sp_empty, 4);
-    mbar_init(ds_full, 4);
+    for (int s = 0; s < QS; ++s) {
+      mbar_init(&qd_full[s], 1);
+      mbar_init(&qd_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&st_full[s], 1);
+      mbar_init(&st_empty[s], kEwWarps);
+      mbar_init(&ds_full[s], kEwWarps);
+      mbar_init(&ds_empty[s], 1);
+    }
     mbar_init(acc_done, 1);
     fence_barrier_init();
   }
@@ -387,128 +436,136 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_st = tmem, t_dpt = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + D;
+  // TMEM columns: S^T[2] 0 / 64, dP^T[2] 128 / 192, dV 256.., dK 256+D..
+  const uint32_t t_dv = tmem + 256, t_dk = tmem + 256 + D;
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(kv_full, 2 * L::kT);
+      mbar_expect_tx(kv_full, 2 * L::kKV);
       #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_2d(sk + c * kBlk * 128, &tm, kv_full, (a.hq + g) * D + 64 * c, kv_row0, a.err);
-        tma_load_2d(sv + c * kBlk * 128, &tm, kv_full, (a.hq + a.hkv + g) * D + 64 * c, kv_row0, a.err);
+        tma_load_2d(sk + c * kBlk * 128, &tm_kv, kv_full, (a.hq + g) * D + 64 * c, kv_row0, a.err);
+        tma_load_2d(sv + c * kBlk * 128, &tm_kv, kv_full, (a.hq + a.hkv + g) * D + 64 * c, kv_row0, a.err);
       }
       for (int it = 0; it < steps; ++it) {
+        const int s = it % QS;
+        if (!mbar_wait(&qd_empty[s], ((it / QS) & 1) ^ 1, a.err, kErrTmaWait)) break;
         const int h = g * group + it / nq;
-        const int qb = kvblk + it % nq;
-        if (!mbar_wait(qd_empty, (it & 1) ^ 1, a.err, kErrTmaWait)) break;
-        const int q_row0 = b * a.seq + qb * kBlk;
-        mbar_expect_tx(qd_full, 2 * L::kT);
+        const int qs = 2 * kvblk + it % nq;
+        const int q_row0 = b * a.seq + qs * kQs;
+        const int64_t stat = (int64_t(b) * a.hq + h) * a.seq + qs * kQs;
+        mbar_expect_tx(&qd_full[s], 2 * L::kQ + 2 * kQs * 4);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(sq + c * kBlk * 128, &tm, qd_full, h * D + 64 * c, q_row0, a.err);
-          tma_load_2d(sdo + c * kBlk * 128, &tm_do, qd_full, h * D + 64 * c, q_row0, a.err);
+          tma_load_2d(sq + s * L::kQ + c * kQs * 128, &tm_q, &qd_full[s], h * D + 64 * c, q_row0, a.err);
+          tma_load_2d(sdo + s * L::kQ + c * kQs * 128, &tm_do, &qd_full[s], h * D + 64 * c, q_row0, a.err);
         }
+        bulk_load(s_lse + s * kQs, a.lse + stat, kQs * 4, &qd_full[s]);
+        bulk_load(s_delta + s * kQs, a.delta + stat, kQs * 4, &qd_full[s]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
+      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kQs, 0, 0);
       constexpr uint32_t id_acc = idesc_bf16_f32(kBlk, D, 0, 1);
-      const uint32_t k_addr = smem_u32(sk), v_addr = smem_u32(sv), q_addr = smem_u32(sq), do_addr = smem_u32(sdo);
-      const uint32_t pt_addr = smem_u32(spt), dst_addr = smem_u32(sdst);
+      const uint32_t k_addr = smem_u32(sk), v_addr = smem_u32(sv);
       bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
-      for (int it = 0; it < steps && ok; ++it) {
-        if (!mbar_wait(qd_full, it & 1, a.err, kErrMmaWait)) { ok = false; break; }
-        if (!mbar_wait(sp_empty, (it & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
-        tc_fence_after();
-        #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
-          umma_bf16(t_st, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024), id_s,
-                    kk > 0);
-          umma_bf16(t_dpt, smem_desc_sw128(v_addr + off, 16, 1024), smem_desc_sw128(do_addr + off, 16, 1024), id_s,
-                    kk > 0);
+      for (int it = 0; it <= steps && ok; ++it) {
+        if (it < steps) {
+          const int s = it & 1;
+          const int s3 = it % QS;
+          if (!mbar_wait(&qd_full[s3], (it / QS) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+          if (!mbar_wait(&st_empty[s], ((it >> 1) & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sq + s3 * L::kQ), do_addr = smem_u32(sdo + s3 * L::kQ);
+          #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t okv = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+            const uint32_t oq = (kk >> 2) * kQs * 128 + (kk & 3) * 32;
+            umma_bf16(tmem + s * kQs, smem_desc_sw128(k_addr + okv, 16, 1024), smem_desc_sw128(q_addr + oq, 16, 1024),
+                      id_s, kk > 0);
+            umma_bf16(tmem + 128 + s * kQs, smem_desc_sw128(v_addr + okv, 16, 1024),
+                      smem_desc_sw128(do_addr + oq, 16, 1024), id_s, kk > 0);
+          }
+          umma_commit(&st_full[s]);
         }
-        umma_commit(sp_full);
-        if (!mbar_wait(ds_full, it & 1, a.err, kErrMmaWait)) { ok = false; break; }
-        tc_fence_after();
-        #pragma unroll
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
-          umma_bf16(t_dv, smem_desc_sw128(pt_addr + aoff, 16, 1024), smem_desc_sw128(do_addr + kk * 2048, kBlk * 128, 1024),
-                    id_acc, (it > 0 || kk > 0));
-          umma_bf16(t_dk, smem_desc_sw128(dst_addr + aoff, 16, 1024), smem_desc_sw128(q_addr + kk * 2048, kBlk * 128, 1024),
-                    id_acc, (it > 0 || kk > 0));
+        if (it >= 1) {
+          const int p = it - 1;
+          const int sp = p & 1;
+          if (!mbar_wait(&ds_full[sp], (p >> 1) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+          const int sp3 = p % QS;
+          const uint32_t pt_addr = smem_u32(spt + sp * L::kP), dst_addr = smem_u32(sdst + sp * L::kP);
+          const uint32_t q_addr = smem_u32(sq + sp3 * L::kQ), do_addr = smem_u32(sdo + sp3 * L::kQ);
+          #pragma unroll
+          for (int kk = 0; kk < kQs / 16; ++kk) {
+            umma_bf16(t_dv, smem_desc_sw128(pt_addr + kk * 32, 16, 1024),
+                      smem_desc_sw128(do_addr + kk * 2048, kQs * 128, 1024), id_acc, (p > 0 || kk > 0));
+            umma_bf16(t_dk, smem_desc_sw128(dst_addr + kk * 32, 16, 1024),
+                      smem_desc_sw128(q_addr + kk * 2048, kQs * 128, 1024), id_acc, (p > 0 || kk > 0));
+          }
+          umma_commit(&qd_empty[sp3]);
+          umma_commit(&ds_empty[sp]);
         }
-        umma_commit(qd_empty);
-        umma_commit(acc_done);
       }
+      if (ok) umma_commit(acc_done);
     }
   } else {
-    const int q4 = warp & 3;
-    const int c_row = q4 * 32 + lane;      // kv row within the tile
-    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const int quad = warp & 3;                 // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;          // which 32 of the 64 q columns
+    const int c_row = quad * 32 + lane;        // kv row within the tile
+    const int k_pos = kvblk * kBlk + c_row;    // its position in the sequence
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
     const float sl2 = a.scale * kLog2e;
-    const int et = threadIdx.x - 64;       // 0..127
     bool ok = true;
     for (int it = 0; it < steps; ++it) {
-      const int h = g * group + it / nq;
-      const int qb = kvblk + it % nq;
-      const bool diag = qb == kvblk;
-      // lse / delta of this q block into smem (read by every kv row)
-      {
-        const int64_t base = (int64_t(b) * a.hq + h) * a.seq + qb * kBlk;
-        // previous step's readers are done once ds_full of that step was arrived; the
-        // named barrier below orders the overwrite after all 128 threads passed it.
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        s_lse[et] = a.lse[base + et] * kLog2e;
-        s_delta[et] = a.delta[base + et];
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
-      if (!mbar_wait(sp_full, it & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      const int s = it & 1;
+      const uint32_t n = (it >> 1) & 1;
+      const int qs = 2 * kvblk + it % nq;
+      const bool diag = qs < 2 * kvblk + 2;   // q sub-block overlaps the kv block: causal mask
+      if (!mbar_wait(&st_full[s], n, a.err, kErrEpiWait)) { ok = false; break; }
       tc_fence_after();
-      if (it > 0) {
-        // smem P^T / dS^T of the previous step are read by its dV/dK MMAs
-        if (!mbar_wait(acc_done, (it - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
-      }
-      #pragma unroll 1
-      for (int c = 0; c < kBlk; c += 32) {
-        uint32_t sv32[32], dv32[32];
-        tmem_ld32(t_st + lane_off + c, sv32);
-        tmem_ld32(t_dpt + lane_off + c, dv32);
-        tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+      uint32_t sv32[32], dv32[32];
+      tmem_ld32(tmem + s * kQs + lane_off + half * 32, sv32);
+      tmem_ld32(tmem + 128 + s * kQs + lane_off + half * 32, dv32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st_empty[s]);
+      // lse / delta of this step landed with Q (the MMA that filled S^T waited for them)
+      const int s3 = it % QS;
+      if (!mbar_wait(&qd_full[s3], (it / QS) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      if (!mbar_wait(&ds_empty[s], n ^ 1, a.err, kErrEpiWait)) { ok = false; break; }
+      const float* lse = s_lse + s3 * kQs + half * 32;
+      const float* dlt = s_delta + s3 * kQs + half * 32;
+      const int q_pos0 = qs * kQs + half * 32;
+      uint32_t pk[16], dk[16];
+      #pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float p[2], ds[2];
         #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p[2], ds[2];
-          #pragma unroll
-          for (int z = 0; z < 2; ++z) {
-            const int qr = c + e + z;      // q row within the q tile
-            float pv = fast_exp2(fmaf(__uint_as_float(sv32[e + z]), sl2, -s_lse[qr]));
-            if (diag && qr < c_row) pv = 0.f;
-            p[z] = pv;
-            ds[z] = pv * (__uint_as_float(dv32[e + z]) - s_delta[qr]);
-          }
-          pk[e / 2] = pack_bf16(p[0], p[1]);
-          dk[e / 2] = pack_bf16(ds[0], ds[1]);
+        for (int z = 0; z < 2; ++z) {
+          float pv = fast_exp2(fmaf(__uint_as_float(sv32[e + z]), sl2, -lse[e + z] * kLog2e));
+          if (diag && q_pos0 + e + z < k_pos) pv = 0.f;
+          p[z] = pv;
+          ds[z] = pv * (__uint_as_float(dv32[e + z]) - dlt[e + z]);
         }
-        store_row32(spt, c_row, c, pk, kBlk);
-        store_row32(sdst, c_row, c, dk, kBlk);
+        pk[e / 2] = pack_bf16(p[0], p[1]);
+        dk[e / 2] = pack_bf16(ds[0], ds[1]);
       }
+      store_row32(spt + s * L::kP, c_row, half * 32, pk, kBlk);
+      store_row32(sdst + s * L::kP, c_row, half * 32, dk, kBlk);
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(sp_empty);
-        mbar_arrive(ds_full);
-      }
+      if (lane == 0) mbar_arrive(&ds_full[s]);
     }
-    if (ok && steps > 0 && mbar_wait(acc_done, (steps - 1) & 1, a.err, kErrEpiWait)) {
+    if (ok && steps > 0 && mbar_wait(acc_done, 0, a.err, kErrEpiWait)) {
       tc_fence_after();
       __nv_bfloat16* dk_dst = a.out + int64_t(kv_row0 + c_row) * a.out_ld + int64_t(a.hq + g) * D;
       __nv_bfloat16* dv_dst = a.out + int64_t(kv_row0 + c_row) * a.out_ld + int64_t(a.hq + a.hkv + g) * D;
       #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
+      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
         uint32_t v1[32], v2[32];
         tmem_ld32(t_dv + lane_off + c, v1);
         tmem_ld32(t_dk + lane_off + c, v2);
@@ -539,43 +596,57 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---- backward: dQ --------------------------------------------------------------------
+//
+// One CTA per (q block of 128 rows, q head, batch), looping over the causal kv range in
+// sub-blocks of 64 rows, mirroring the dK/dV kernel: S_j / dP_j (128 x 64) double-buffered
+// in TMEM next to the dQ accumulator, K_j / V_j in a three-stage ring and the dS tiles
+// double-buffered in shared memory, so the MMAs of one sub-block overlap the elementwise
+// work of the previous one:
+//   warp 0      TMA: Q, dO once; K_j, V_j (64 rows) into the ring
+//   warp 1      MMA: S_j = Q K_j^T, dP_j = dO V_j^T, then dQ += dS_{j-1} K_{j-1}
+//   warps 2-9   elementwise, two warps per TMEM lane quadrant (32 kv columns each):
+//               dS = P (dP - Delta), P = exp2(S * scale*log2e - lse*log2e), causal mask.
+constexpr int kKs = 64;   // kv rows per dQ step
+constexpr int kDqStages = 3;
 
 template <int D>
 struct DqSmem {
-  static constexpr int kT = kBlk * D * 2;
-  static constexpr int kStages = 2;
-  static constexpr int kP = kBlk * kBlk * 2;
-  static constexpr int kBytes = 2 * kT + 2 * kStages * kT + kP + 1024 + 256;
+  static constexpr int kT = kBlk * D * 2;    // Q or dO tile
+  static constexpr int kKV = kKs * D * 2;    // one K or V tile of 64 rows
+  static constexpr int kDs = kBlk * kKs * 2; // one dS tile [128 q, 64 kv]
+  static constexpr int kBytes = 2 * kT + 2 * kDqStages * kKV + 2 * kDs + 1024 + 256;
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
-    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
+__global__ void __launch_bounds__(kDkdvThreads, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_kv64, AttnArgs a) {
   using L = DqSmem<D>;
-  constexpr int ST = L::kStages;
+  constexpr int ST = kDqStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
   uint8_t* sq = smem;
   uint8_t* sdo = sq + L::kT;
   uint8_t* sk = sdo + L::kT;           // ST stages
-  uint8_t* sv = sk + ST * L::kT;       // ST stages
-  uint8_t* sds = sv + ST * L::kT;      // dS [q, kv] K-major
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + L::kP);
+  uint8_t* sv = sk + ST * L::kKV;      // ST stages
+  uint8_t* sds = sv + ST * L::kKV;     // 2 stages of dS [q, kv] K-major
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + 2 * L::kDs);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;        // ST
-  uint64_t* kv_empty = kv_full + ST;   // ST
-  uint64_t* sp_full = kv_empty + ST;
-  uint64_t* sp_empty = sp_full + 1;
-  uint64_t* ds_full = sp_empty + 1;
-  uint64_t* dq_done = ds_full + 1;
+  uint64_t* kv_full = bars + 1;              // [ST]
+  uint64_t* kv_empty = kv_full + ST;         // [ST]
+  uint64_t* s_full = kv_empty + ST;          // [2] S, dP of a sub-block in TMEM
+  uint64_t* s_empty = s_full + 2;            // [2] the elementwise warps read them
+  uint64_t* ds_full = s_empty + 2;           // [2] dS of a sub-block in smem
+  uint64_t* ds_empty = ds_full + 2;          // [2] the dQ MMA reading it is done
+  uint64_t* dq_done = ds_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_done + 1);
 
-  const int qblk = (a.seq / kBlk) - 1 - blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  const int qblk = (a.seq / kBlk) - 1 - blockIdx.z;   // slowest grid dimension: heaviest first
+  const int h = blockIdx.x;
+  const int b = blockIdx.y;
   const int kvh = h / (a.hq / a.hkv);
-  const int nblk = qblk + 1;
+  const int nkv = 2 * qblk + 2;                       // kv sub-blocks 0 .. 2*qblk+1
   const int row0 = b * a.seq + qblk * kBlk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -585,9 +656,12 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(sp_full, 1);
-    mbar_init(sp_empty, 4);
-    mbar_init(ds_full, 4);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], kEwWarps);
+      mbar_init(&ds_full[s], kEwWarps);
+      mbar_init(&ds_empty[s], 1);
+    }
     mbar_init(dq_done, 1);
     fence_barrier_init();
   }
@@ -596,7 +670,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256;
+  // TMEM columns: S[2] 0 / 64, dP[2] 128 / 192, dQ 256..
+  const uint32_t t_dq = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -606,98 +681,111 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_2d(sq + c * kBlk * 128, &tm, q_full, h * D + 64 * c, row0, a.err);
         tma_load_2d(sdo + c * kBlk * 128, &tm_do, q_full, h * D + 64 * c, row0, a.err);
       }
-      for (int j = 0; j < nblk; ++j) {
+      for (int j = 0; j < nkv; ++j) {
         const int st = j % ST;
         if (!mbar_wait(&kv_empty[st], ((j / ST) & 1) ^ 1, a.err, kErrTmaWait)) break;
-        const int kv_row = b * a.seq + j * kBlk;
-        mbar_expect_tx(&kv_full[st], 2 * L::kT);
+        const int kv_row = b * a.seq + j * kKs;
+        mbar_expect_tx(&kv_full[st], 2 * L::kKV);
         #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(sk + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + kvh) * D + 64 * c, kv_row, a.err);
-          tma_load_2d(sv + st * L::kT + c * kBlk * 128, &tm, &kv_full[st], (a.hq + a.hkv + kvh) * D + 64 * c, kv_row, a.err);
+          tma_load_2d(sk + st * L::kKV + c * kKs * 128, &tm_kv64, &kv_full[st], (a.hq + kvh) * D + 64 * c, kv_row,
+                      a.err);
+          tma_load_2d(sv + st * L::kKV + c * kKs * 128, &tm_kv64, &kv_full[st], (a.hq + a.hkv + kvh) * D + 64 * c,
+                      kv_row, a.err);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
+      constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kKs, 0, 0);
       constexpr uint32_t id_dq = idesc_bf16_f32(kBlk, D, 0, 1);
-      const uint32_t q_addr = smem_u32(sq), do_addr = smem_u32(sdo), ds_addr = smem_u32(sds);
+      const uint32_t q_addr = smem_u32(sq), do_addr = smem_u32(sdo);
       bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
-      for (int j = 0; j < nblk && ok; ++j) {
-        const int st = j % ST;
-        if (!mbar_wait(&kv_full[st], (j / ST) & 1, a.err, kErrMmaWait)) { ok = false; break; }
-        if (!mbar_wait(sp_empty, (j & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sk + st * L::kT), v_addr = smem_u32(sv + st * L::kT);
-        #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
-          umma_bf16(t_s, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024), id_s,
-                    kk > 0);
-          umma_bf16(t_dp, smem_desc_sw128(do_addr + off, 16, 1024), smem_desc_sw128(v_addr + off, 16, 1024), id_s,
-                    kk > 0);
+      for (int j = 0; j <= nkv && ok; ++j) {
+        if (j < nkv) {
+          const int st = j % ST;
+          const int s = j & 1;
+          if (!mbar_wait(&kv_full[st], (j / ST) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+          if (!mbar_wait(&s_empty[s], ((j >> 1) & 1) ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sk + st * L::kKV), v_addr = smem_u32(sv + st * L::kKV);
+          #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oq = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
+            const uint32_t okv = (kk >> 2) * kKs * 128 + (kk & 3) * 32;
+            umma_bf16(tmem + s * kKs, smem_desc_sw128(q_addr + oq, 16, 1024), smem_desc_sw128(k_addr + okv, 16, 1024),
+                      id_s, kk > 0);
+            umma_bf16(tmem + 128 + s * kKs, smem_desc_sw128(do_addr + oq, 16, 1024),
+                      smem_desc_sw128(v_addr + okv, 16, 1024), id_s, kk > 0);
+          }
+          umma_commit(&s_full[s]);
         }
-        umma_commit(sp_full);
-        if (!mbar_wait(ds_full, j & 1, a.err, kErrMmaWait)) { ok = false; break; }
-        tc_fence_after();
-        #pragma unroll
-        for (int kk = 0; kk < kBlk / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
-          umma_bf16(t_dq, smem_desc_sw128(ds_addr + aoff, 16, 1024), smem_desc_sw128(k_addr + kk * 2048, kBlk * 128, 1024),
-                    id_dq, (j > 0 || kk > 0));
+        if (j >= 1) {
+          const int p = j - 1;
+          const int sp = p & 1;
+          const int stp = p % ST;
+          if (!mbar_wait(&ds_full[sp], (p >> 1) & 1, a.err, kErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ds_addr = smem_u32(sds + sp * L::kDs), k_addr = smem_u32(sk + stp * L::kKV);
+          #pragma unroll
+          for (int kk = 0; kk < kKs / 16; ++kk)
+            umma_bf16(t_dq, smem_desc_sw128(ds_addr + kk * 32, 16, 1024),
+                      smem_desc_sw128(k_addr + kk * 2048, kKs * 128, 1024), id_dq, (p > 0 || kk > 0));
+          umma_commit(&kv_empty[stp]);
+          umma_commit(&ds_empty[sp]);
         }
-        umma_commit(&kv_empty[st]);
-        umma_commit(dq_done);
       }
+      if (ok) umma_commit(dq_done);
     }
   } else {
-    const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;
-    const uint32_t lane_off = uint32_t(q4 * 32) << 16;
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;                 // q row within the tile
+    const int q_pos = qblk * kBlk + r;
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
     const float sl2 = a.scale * kLog2e;
-    const int64_t stat = (int64_t(b) * a.hq + h) * a.seq + qblk * kBlk + r;
+    const int64_t stat = (int64_t(b) * a.hq + h) * a.seq + q_pos;
     const float lse2 = a.lse[stat] * kLog2e;
     const float dlt = a.delta[stat];
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const bool diag = j == qblk;
-      if (!mbar_wait(sp_full, j & 1, a.err, kErrEpiWait)) { ok = false; break; }
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      const uint32_t n = (j >> 1) & 1;
+      const bool diag = j >= 2 * qblk;              // the sub-block reaches the q block's rows
+      const int k_pos0 = j * kKs + half * 32;
+      if (!mbar_wait(&s_full[s], n, a.err, kErrEpiWait)) { ok = false; break; }
       tc_fence_after();
-      if (j > 0 && !mbar_wait(dq_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
-      #pragma unroll 1
-      for (int c = 0; c < kBlk; c += 32) {
-        uint32_t s32[32], p32[32];
-        tmem_ld32(t_s + lane_off + c, s32);
-        tmem_ld32(t_dp + lane_off + c, p32);
-        tmem_wait_ld();
-        uint32_t pk[16];
+      uint32_t s32[32], p32[32];
+      tmem_ld32(tmem + s * kKs + lane_off + half * 32, s32);
+      tmem_ld32(tmem + 128 + s * kKs + lane_off + half * 32, p32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[s]);
+      if (!mbar_wait(&ds_empty[s], n ^ 1, a.err, kErrEpiWait)) { ok = false; break; }
+      uint32_t pk[16];
+      #pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float ds[2];
         #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float ds[2];
-          #pragma unroll
-          for (int z = 0; z < 2; ++z) {
-            float pv = fast_exp2(fmaf(__uint_as_float(s32[e + z]), sl2, -lse2));
-            if (diag && c + e + z > r) pv = 0.f;
-            ds[z] = pv * (__uint_as_float(p32[e + z]) - dlt);
-          }
-          pk[e / 2] = pack_bf16(ds[0], ds[1]);
+        for (int z = 0; z < 2; ++z) {
+          float pv = fast_exp2(fmaf(__uint_as_float(s32[e + z]), sl2, -lse2));
+          if (diag && k_pos0 + e + z > q_pos) pv = 0.f;
+          ds[z] = pv * (__uint_as_float(p32[e + z]) - dlt);
         }
-        store_row32(sds, r, c, pk, kBlk);
+        pk[e / 2] = pack_bf16(ds[0], ds[1]);
       }
+      store_row32(sds + s * L::kDs, r, half * 32, pk, kBlk);
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(sp_empty);
-        mbar_arrive(ds_full);
-      }
+      if (lane == 0) mbar_arrive(&ds_full[s]);
     }
-    if (ok && mbar_wait(dq_done, (nblk - 1) & 1, a.err, kErrEpiWait)) {
+    if (ok && mbar_wait(dq_done, 0, a.err, kErrEpiWait)) {
       tc_fence_after();
       __nv_bfloat16* dst = a.out + int64_t(row0 + r) * a.out_ld + int64_t(h) * D;
       #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
+      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
         uint32_t v[32];
         tmem_ld32(t_dq + lane_off + c, v);
         tmem_wait_ld();
@@ -739,7 +827,7 @@ void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float*
   check_shapes(rows, seq, hq, hkv, d);
   const CUtensorMap tm = make_tma_2d_bf16(qkv, rows, int64_t(hq + 2 * hkv) * d, qkv_ld, 64, kBlk);
   AttnArgs a{static_cast<__nv_bfloat16*>(out), lse, nullptr, nullptr, seq, hq, hkv, d, out_ld, 0, scale, err};
-  dim3 grid(seq / kBlk, hq, rows / seq);
+  dim3 grid(hq, rows / seq, seq / kBlk);
   if (d == 128) {
     set_smem(attn_fwd_kernel<128>, FwdSmem<128>::kBytes);
     attn_fwd_kernel<128><<<grid, 192, FwdSmem<128>::kBytes, st>>>(tm, a);
@@ -764,22 +852,26 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
   }
   const CUtensorMap tm = make_tma_2d_bf16(qkv, rows, int64_t(hq + 2 * hkv) * d, qkv_ld, 64, kBlk);
   const CUtensorMap tm_do = make_tma_2d_bf16(dout, rows, int64_t(hq) * d, dout_ld, 64, kBlk);
+  const CUtensorMap tm_q64 = make_tma_2d_bf16(qkv, rows, int64_t(hq + 2 * hkv) * d, qkv_ld, 64, kQs);  // also K, V rows
+  const CUtensorMap tm_do64 = make_tma_2d_bf16(dout, rows, int64_t(hq) * d, dout_ld, 64, kQs);
+  RESIHP_CHECK(reinterpret_cast<uintptr_t>(lse) % 16 == 0 && reinterpret_cast<uintptr_t>(delta) % 16 == 0,
+               "attention statistics must be 16-byte aligned");
   AttnArgs a{static_cast<__nv_bfloat16*>(dqkv), const_cast<float*>(lse), static_cast<const __nv_bfloat16*>(dout),
              delta, seq, hq, hkv, d, dqkv_ld, dout_ld, scale, err};
-  dim3 grid_kv(seq / kBlk, hkv, rows / seq);
-  dim3 grid_q(seq / kBlk, hq, rows / seq);
+  dim3 grid_kv(hkv, rows / seq, seq / kBlk);
+  dim3 grid_q(hq, rows / seq, seq / kBlk);
   if (d == 128) {
     set_smem(attn_bwd_dkdv_kernel<128>, DkdvSmem<128>::kBytes);
-    attn_bwd_dkdv_kernel<128><<<grid_kv, 192, DkdvSmem<128>::kBytes, st>>>(tm, tm_do, a);
+    attn_bwd_dkdv_kernel<128><<<grid_kv, kDkdvThreads, DkdvSmem<128>::kBytes, st>>>(tm, tm_q64, tm_do64, a);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     set_smem(attn_bwd_dq_kernel<128>, DqSmem<128>::kBytes);
-    attn_bwd_dq_kernel<128><<<grid_q, 192, DqSmem<128>::kBytes, st>>>(tm, tm_do, a);
+    attn_bwd_dq_kernel<128><<<grid_q, kDkdvThreads, DqSmem<128>::kBytes, st>>>(tm, tm_do, tm_q64, a);
   } else {
     set_smem(attn_bwd_dkdv_kernel<64>, DkdvSmem<64>::kBytes);
-    attn_bwd_dkdv_kernel<64><<<grid_kv, 192, DkdvSmem<64>::kBytes, st>>>(tm, tm_do, a);
+    attn_bwd_dkdv_kernel<64><<<grid_kv, kDkdvThreads, DkdvSmem<64>::kBytes, st>>>(tm, tm_q64, tm_do64, a);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     set_smem(attn_bwd_dq_kernel<64>, DqSmem<64>::kBytes);
-    attn_bwd_dq_kernel<64><<<grid_q, 192, DqSmem<64>::kBytes, st>>>(tm, tm_do, a);
+    attn_bwd_dq_kernel<64><<<grid_q, kDkdvThreads, DqSmem<64>::kBytes, st>>>(tm, tm_do, tm_q64, a);
   }
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }

@@ -111,23 +111,65 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv
   for (int c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = mine ? src[c] : make_uint4(0, 0, 0, 0);
 }
 
-// One block per run of equal ids in ``order`` (token indices sorted by id, stable):
-// dW[id - start] += sum of dy rows of the run, in sorted (= token) order.
-__global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ order,
-                                     const __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int rows, int d,
-                                     int64_t start, int64_t count) {
+// Deterministic embedding backward without a library sort. For each segment of up to
+// kSortMax tokens (in token order): one CTA sorts the packed keys (local vocabulary row
+// << 32 | token index) ascending in shared memory with a bitonic network -- equal rows
+// keep token order, as the token index is the low word -- then one block per run of
+// equal rows sums that run's dy rows in token order into dW. Tokens outside this rank's
+// vocabulary shard get the largest key and are skipped. Segments are processed in
+// token order, so every dW element is accumulated in the same order on every run.
+constexpr int kSortMax = 16384;        // keys per segment (128 KB of shared memory)
+constexpr int kSortThreads = 1024;
+
+__global__ void __launch_bounds__(kSortThreads) embedding_sort_kernel(const int64_t* __restrict__ ids, int rows,
+                                                                        int64_t start, int64_t count,
+                                                                        uint64_t* __restrict__ keys_out) {
+  extern __shared__ uint64_t key[];
+  int n = 1;
+  while (n < rows) n <<= 1;
+  for (int i = threadIdx.x; i < n; i += kSortThreads) {
+    uint64_t k = ~uint64_t(0);
+    if (i < rows) {
+      const int64_t local = ids[i] - start;
+      if (local >= 0 && local < count) k = (uint64_t(local) << 32) | uint64_t(i);
+    }
+    key[i] = k;
+  }
+  __syncthreads();
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n / 2; i += kSortThreads) {
+        // the i-th compare-exchange pair of this pass
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const uint64_t a = key[lo], b = key[hi];
+        if ((a > b) == ascending) {
+          key[lo] = b;
+          key[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < rows; i += kSortThreads) keys_out[i] = key[i];
+}
+
+// One block per run of equal rows in the sorted keys: dW[row] += sum of the run's dy rows.
+__global__ void embedding_bwd_kernel(const uint64_t* __restrict__ keys, const __nv_bfloat16* __restrict__ dy,
+                                     float* __restrict__ dw, int rows, int d) {
   const int head = blockIdx.x;
   if (head >= rows) return;
-  const int64_t id = sorted_ids[head];
-  if (head > 0 && sorted_ids[head - 1] == id) return;  // not the first of its run
-  const int64_t local = id - start;
-  if (local < 0 || local >= count) return;
+  const uint64_t k = keys[head];
+  if (k == ~uint64_t(0)) return;                                 // outside this shard
+  const uint32_t row = uint32_t(k >> 32);
+  if (head > 0 && uint32_t(keys[head - 1] >> 32) == row) return;  // not the first of its run
   int end = head + 1;
-  while (end < rows && sorted_ids[end] == id) ++end;
+  while (end < rows && keys[end] != ~uint64_t(0) && uint32_t(keys[end] >> 32) == row) ++end;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float acc = 0.f;
-    for (int j = head; j < end; ++j) acc += bf(dy[order[j] * d + c]);
-    dw[local * d + c] += acc;
+    for (int j = head; j < end; ++j) acc += bf(dy[int64_t(uint32_t(keys[j])) * d + c]);
+    dw[int64_t(row) * d + c] += acc;
   }
 }
 
@@ -194,11 +236,23 @@ void embedding_fwd(const int64_t* ids, const void* w, void* out, int rows, int d
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
-void embedding_bwd(const int64_t* sorted_ids, const int64_t* order, const void* dy, float* dw, int rows, int d,
-                   int64_t start, int64_t count, cudaStream_t st) {
-  embedding_bwd_kernel<<<rows, 256, 0, st>>>(sorted_ids, order, static_cast<const __nv_bfloat16*>(dy), dw, rows, d,
-                                             start, count);
-  RESIHP_CUDA_CHECK(cudaGetLastError());
+int embedding_sort_segment() { return kSortMax; }
+
+void embedding_bwd(const int64_t* ids, const void* dy, float* dw, uint64_t* keys, int rows, int d, int64_t start,
+                   int64_t count, cudaStream_t st) {
+  RESIHP_CHECK(count < (int64_t(1) << 32) - 1, "embedding shard too large for 32-bit row keys");
+  const auto* dyb = static_cast<const __nv_bfloat16*>(dy);
+  const int smem = kSortMax * int(sizeof(uint64_t));
+  RESIHP_CUDA_CHECK(cudaFuncSetAttribute(embedding_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  for (int off = 0; off < rows; off += kSortMax) {
+    const int seg = std::min(kSortMax, rows - off);
+    int n = 1;
+    while (n < seg) n <<= 1;
+    embedding_sort_kernel<<<1, kSortThreads, n * int(sizeof(uint64_t)), st>>>(ids + off, seg, start, count, keys);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    embedding_bwd_kernel<<<seg, 256, 0, st>>>(keys, dyb + int64_t(off) * d, dw, seg, d);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+  }
 }
 
 }  // namespace resihp

@@ -42,7 +42,7 @@ def _load():
 # Kernels each extension entry point launches (for the benchmark's launch count).
 KERNELS_PER_CALL = {
     "gemm": 1, "rmsnorm_fwd": 1, "rmsnorm_bwd": 2, "rope": 1, "swiglu_fwd": 1, "swiglu_bwd": 1,
-    "adamw": 1, "embedding_fwd": 1, "embedding_bwd": 1, "xent_stats": 1, "xent_grad": 1,
+    "adamw": 1, "embedding_fwd": 1, "embedding_bwd": 2, "xent_stats": 1, "xent_grad": 1,
     "attn_fwd": 1, "attn_bwd": 3, "ag_gemm": 1, "gemm_rs": 1, "dp_allreduce_adamw": 1, "reshard_gather": 1,
 }
 
