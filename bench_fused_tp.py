@@ -1,4 +1,4 @@
-"""Fused AG->GEMM / GEMM->RS against NCCL + GEMM, on 2-8 GPUs.
+"""Fused AG->GEMM / GEMM->RS / GEMM->AR against NCCL + GEMM, on 2-8 GPUs.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         --master-port 29581 bench_fused_tp.py            # 1.3B layer shapes (T=4096, d=2048)
@@ -124,6 +124,20 @@ def main():
                        nccl_cublas_us=t_ev(nccl_cublas), nccl_ours_us=t_ev(nccl_ours),
                        gemm_only_us=t_ev(lambda: ops.linear(h, w)))
             row["roofline_us"] = roofline(2.0 * m * k * width, (world - 1) / world * m * width * 2)
+            out.append(row)
+            if sweep:
+                continue
+
+            def nccl_cublas_ar():
+                y = torch.matmul(h, w.t())
+                dist.all_reduce(y)
+                return y
+
+            # without sequence parallelism: the row-parallel output all-reduce
+            row = dict(op="gemm_ar", m=m, k=k_full, k_per_rank=k, n=width, tp=world,
+                       fused_us=t_ev(lambda: ws.gemm_all_reduce(h, w, False, width)),
+                       nccl_cublas_us=t_ev(nccl_cublas_ar), gemm_only_us=t_ev(lambda: ops.linear(h, w)))
+            row["roofline_us"] = roofline(2.0 * m * k * width, 2 * (world - 1) / world * m * width * 2)
             out.append(row)
         ws.close()
         del x

@@ -61,6 +61,7 @@ constexpr int kCopyThreads = 32 * kCopyWarps;
 constexpr int kFusedThreads = 192 + kCopyThreads;
 constexpr int kTileRing = 4;
 constexpr int kCopyUnroll = 8;
+constexpr int kCopyBatch = 8;  // copy items per claim
 
 enum FusedMode : int { kModeAG = 1, kModeRS = 2, kModeAR = 3 };
 
@@ -345,31 +346,39 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         #pragma unroll
         for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
         if (reduce_here) {
-          // every rank's partial, summed in rank order (this rank's own in fp32)
-          float tot[32];
+          // every rank's partial, summed in rank order (this rank's own in fp32); each
+          // 8-column quarter issues every source's load before the first addition, so the
+          // tp-1 receive-buffer reads overlap instead of running one after another
           #pragma unroll
-          for (int e = 0; e < 32; ++e) tot[e] = 0.f;
-          for (int src = 0; src < p.tp; ++src) {
-            if (src == p.rank) {
-              #pragma unroll
-              for (int e = 0; e < 32; ++e) tot[e] += f[e];
-              continue;
-            }
-            const __nv_bfloat16* pp = p.recv[p.rank] + (int64_t(src) * rpr + lrow) * g.n + col0;
+          for (int qq = 0; qq < 4; ++qq) {
+            uint4 raw[kFusedMaxTp];
             #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 raw4 = *reinterpret_cast<const uint4*>(pp + 8 * u);
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw4);
+            for (int src = 0; src < kFusedMaxTp; ++src)
+              if (src < p.tp && src != p.rank)
+                raw[src] = *reinterpret_cast<const uint4*>(p.recv[p.rank] + (int64_t(src) * rpr + lrow) * g.n + col0 +
+                                                           8 * qq);
+            float tot[8];
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) tot[e] = 0.f;
+            #pragma unroll
+            for (int src = 0; src < kFusedMaxTp; ++src) {
+              if (src >= p.tp) continue;
+              if (src == p.rank) {
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) tot[e] += f[8 * qq + e];
+                continue;
+              }
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[src]);
               #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 x = __bfloat1622float2(h[e]);
-                tot[8 * u + 2 * e] += x.x;
-                tot[8 * u + 2 * e + 1] += x.y;
+                tot[2 * e] += x.x;
+                tot[2 * e + 1] += x.y;
               }
             }
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) f[8 * qq + e] = tot[e];
           }
-          #pragma unroll
-          for (int e = 0; e < 32; ++e) f[e] = tot[e];
         }
         uint4 o[4];
         #pragma unroll
@@ -411,59 +420,80 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
   } else {
     // ---------------- copy warps ----------------
+    // Items are claimed kCopyBatch at a time; consecutive push units of one destination
+    // (and consecutive gathered-copy units of one chunk) are contiguous rows, so each
+    // run of a batch is one span copy, and a batch's pushes share one system fence.
     const int ct = threadIdx.x - 192;  // 0 .. kCopyThreads-1
     const int k16 = g.k / 8;           // 16-byte vectors per row of the AG input
     const int srows = kFBM / max(p.slices, 1);
-    const int units = tiles_m_chunk * p.slices;  // push units of this rank's chunk
+    const int units = tiles_m_chunk * p.slices;  // push units of this rank's chunk (unit u = rows u*srows..)
     const int n_push = MODE == kModeAG ? (p.tp - 1) * units : 0;
-    const int n_xg = (MODE == kModeAG && g.xg != nullptr) ? p.tp * units : 0;
+    // gathered copy: every chunk into xg, or (xg is this rank's landing zone, which the
+    // peers already fill) only the own chunk
+    const int n_xg = MODE != kModeAG || g.xg == nullptr ? 0 : (g.xg == p.land[p.rank] ? units : p.tp * units);
     const int n_ar = MODE == kModeAR ? (p.tp - 1) * per_chunk : 0;
     const int items = n_push + n_xg + n_ar;
+    const int batch = MODE == kModeAR ? 1 : kCopyBatch;  // an AR item is a whole 128 x 256 tile
     while (items > 0) {
-      if (ct == 0) {
-        const unsigned c = atomicAdd(p.copy_ctr, 1u) - p.copy_base;
-        claim[0] = c < unsigned(items) ? int(c) : -1;
-      }
+      if (ct == 0) claim[0] = int(atomicAdd(p.copy_ctr, unsigned(batch)) - p.copy_base);
       copy_bar();
-      const int it = claim[0];
+      const int first_item = claim[0];
       copy_bar();
-      if (it < 0) break;
-      if (it < n_push) {
-        // push unit u of this rank's chunk to peer (rank - j): rows r0 .. r0+srows
-        const int j = it / units + 1;
-        const int u = it % units;
-        const int dest = (p.rank - j + p.tp) % p.tp;
-        const int rb = u / p.slices;
-        const int r0 = rb * kFBM + (u % p.slices) * srows;
-        copy_span(reinterpret_cast<uint4*>(p.land[dest] + (int64_t(p.rank) * rpr + r0) * g.k),
-                  reinterpret_cast<const uint4*>(g.x_local + int64_t(r0) * g.k), int64_t(srows) * k16, ct, g.err);
+      if (first_item < 0 || first_item >= items) break;
+      const int last_item = min(first_item + batch, items);
+      bool ok = true;
+      // pushes: runs of one destination, then one fence, then one count per unit
+      const int pe = min(last_item, n_push);
+      if (first_item < pe) {
+        for (int i = first_item; i < pe;) {
+          const int j = i / units;
+          const int run_end = min(pe, (j + 1) * units);
+          const int dest = (p.rank - j - 1 + p.tp) % p.tp;
+          const int r0 = (i % units) * srows;
+          copy_span(reinterpret_cast<uint4*>(p.land[dest] + (int64_t(p.rank) * rpr + r0) * g.k),
+                    reinterpret_cast<const uint4*>(g.x_local + int64_t(r0) * g.k), int64_t(run_end - i) * srows * k16,
+                    ct, g.err);
+          i = run_end;
+        }
         __threadfence_system();
         copy_bar();
-        if (ct == 0) red_release_add(p.ag_cnt[dest] + p.rank * kFusedMaxRb + rb, 1u);
-      } else if (it < n_push + n_xg) {
-        // unit u of chunk c into the gathered copy (own chunk first, then in arrival order)
-        const int i2 = it - n_push;
+        if (ct == 0)
+          for (int i = first_item; i < pe; ++i) {
+            const int dest = (p.rank - i / units - 1 + p.tp) % p.tp;
+            red_release_add(p.ag_cnt[dest] + p.rank * kFusedMaxRb + (i % units) / p.slices, 1u);
+          }
+      }
+      // gathered copy: runs of one chunk (own chunk first, then in arrival order)
+      const int xb = max(first_item, n_push), xe = min(last_item, n_push + n_xg);
+      for (int i = xb; i < xe && ok;) {
+        const int i2 = i - n_push;
         const int c = (p.rank + i2 / units) % p.tp;
-        const int u = i2 % units;
-        const int rb = u / p.slices;
-        const int r0 = rb * kFBM + (u % p.slices) * srows;
+        const int run_end = min(xe, n_push + (i2 / units + 1) * units);
+        const int u0 = i2 % units, u1 = u0 + (run_end - i);
         const __nv_bfloat16* src;
         if (c == p.rank) {
-          src = g.x_local + int64_t(r0) * g.k;
+          src = g.x_local;
         } else {
-          if (ct == 0)
-            claim[1] = wait_geq(p.ag_cnt[p.rank] + c * kFusedMaxRb + rb, unsigned(p.slices) * p.epoch, g.err,
-                                kErrPeerWait, g.wait_ns);
+          if (ct == 0) {
+            int arrived = 1;
+            for (int rb = u0 / p.slices; rb <= (u1 - 1) / p.slices && arrived; ++rb)
+              arrived = wait_geq(p.ag_cnt[p.rank] + c * kFusedMaxRb + rb, unsigned(p.slices) * p.epoch, g.err,
+                                 kErrPeerWait, g.wait_ns);
+            claim[1] = arrived;
+          }
           copy_bar();
-          const int arrived = claim[1];
+          ok = claim[1] != 0;
           copy_bar();
-          if (!arrived) break;
-          src = p.land[p.rank] + (int64_t(c) * rpr + r0) * g.k;
+          src = p.land[p.rank] + int64_t(c) * rpr * g.k;
         }
-        copy_span(reinterpret_cast<uint4*>(g.xg + (int64_t(c) * rpr + r0) * g.k), reinterpret_cast<const uint4*>(src),
-                  int64_t(srows) * k16, ct, g.err);
-      } else {
-        // AR: another owner's reduced tile, from the output landing zone into y
+        if (ok)
+          copy_span(reinterpret_cast<uint4*>(g.xg + (int64_t(c) * rpr + int64_t(u0) * srows) * g.k),
+                    reinterpret_cast<const uint4*>(src + int64_t(u0) * srows * g.k), int64_t(u1 - u0) * srows * k16,
+                    ct, g.err);
+        i = run_end;
+      }
+      // AR: other owners' reduced tiles, from the output landing zone into y
+      for (int it = max(first_item, n_push + n_xg); it < last_item && ok; ++it) {
         const int i3 = it - n_push - n_xg;
         const int c = (p.rank + 1 + i3 / per_chunk) % p.tp;
         const int lt = i3 % per_chunk;
@@ -473,14 +503,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         if (ct == 0)
           claim[1] = wait_geq(p.ar_cnt[p.rank] + global_tile, 4u * p.ar_epoch, g.err, kErrPeerWait, g.wait_ns);
         copy_bar();
-        const int arrived = claim[1];
+        ok = claim[1] != 0;
         copy_bar();
-        if (!arrived) break;
+        if (!ok) break;
         const int ncols16 = min(BN, g.n - tn * BN) / 8;
         copy_rows(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN), g.ldc / 8,
                   reinterpret_cast<const uint4*>(p.out_land[p.rank] + int64_t(m0) * g.n + tn * BN), g.n / 8, kFBM,
                   ncols16, ct, g.err);
       }
+      if (!ok) break;
     }
   }
 
@@ -521,10 +552,13 @@ void check_peers(const FusedPeers& p, int t_rows, int n, int k, const char* what
 
 }  // namespace
 
+// One CTA per SM whatever the tile count: CTAs without a tile still run copy warps, and
+// the bytes in flight of the pushes and copies scale with the CTAs that issue them.
 int fused_grid(int m, int n, int tp) {
+  (void)m;
+  (void)n;
   (void)tp;
-  const int tiles = (m / kFBM) * ((n + 255) / 256);
-  return std::min(tiles, sm_count());
+  return sm_count();
 }
 
 int fused_slices(int rows_per_rank) {
@@ -536,14 +570,16 @@ int fused_slices(int rows_per_rank) {
 
 int fused_tile_claims(int t_rows, int n, int grid) { return (t_rows / kFBM) * ((n + 255) / 256) + grid; }
 
-int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, bool xg, int grid) {
+int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_chunks, int grid) {
   const int rpr = t_rows / tp;
   const int units = (rpr / kFBM) * slices;
   const int per_chunk = (rpr / kFBM) * ((n + 255) / 256);
   int items = 0;
-  if (mode == kModeAG) items = (tp - 1) * units + (xg ? tp * units : 0);
+  if (mode == kModeAG) items = (tp - 1) * units + xg_chunks * units;
   if (mode == kModeAR) items = (tp - 1) * per_chunk;
-  return items > 0 ? items + grid : 0;
+  // every batch claimed, plus one failing claim per CTA, a batch of items each
+  const int batch = mode == kModeAR ? 1 : kCopyBatch;
+  return items > 0 ? ((items + batch - 1) / batch + grid) * batch : 0;
 }
 
 void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,

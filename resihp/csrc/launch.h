@@ -79,8 +79,10 @@ void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n
            float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st);
 void embedding_fwd(const int64_t* ids, const void* w, void* out, int rows, int d, int64_t start, int64_t count,
                    cudaStream_t st);
-void embedding_bwd(const int64_t* sorted_ids, const int64_t* order, const void* dy, float* dw, int rows, int d,
-                   int64_t start, int64_t count, cudaStream_t st);
+// keys: device scratch of min(rows, embedding_sort_segment()) uint64 values.
+int embedding_sort_segment();
+void embedding_bwd(const int64_t* ids, const void* dy, float* dw, uint64_t* keys, int rows, int d, int64_t start,
+                   int64_t count, cudaStream_t st);
 
 void xent_stats(const void* logits, int64_t ld, const int64_t* labels, float* stats, int rows, int v, int64_t start,
                 cudaStream_t st);
@@ -122,7 +124,9 @@ int fused_grid(int m, int n, int tp);
 int fused_slices(int rows_per_rank);
 // Claims a launch makes on its counters (the host adds them to its bases after the call).
 int fused_tile_claims(int t_rows, int n, int grid);
-int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, bool xg, int grid);
+// xg_chunks: chunks copied into the gathered input (0: none, 1: only the own chunk into
+// this rank's landing zone, tp: every chunk into a separate buffer).
+int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_chunks, int grid);
 void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,
                    int t_rows, int n, int k, const FusedPeers& peers, int grid, int* err, cudaStream_t st);
 void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n,

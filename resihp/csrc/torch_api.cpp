@@ -215,12 +215,13 @@ void embedding_bwd_t(torch::Tensor ids, torch::Tensor dy, torch::Tensor dw, int6
   check_cuda_bf16(dy, "dy");
   TORCH_CHECK(dw.scalar_type() == torch::kFloat && dw.dim() == 2 && dw.is_contiguous(), "dw must be fp32 [V, d]");
   c10::cuda::CUDAGuard guard(dy.device());
-  auto flat = ids.reshape({-1});
-  auto sorted = std::get<0>(torch::sort(flat, /*stable=*/true, /*dim=*/0, /*descending=*/false));
-  auto order = std::get<1>(torch::sort(flat, true, 0, false)).contiguous();
+  auto flat = ids.reshape({-1}).contiguous();
   auto dy2 = dy.reshape({flat.numel(), dw.size(1)}).contiguous();
-  embedding_bwd(sorted.contiguous().data_ptr<int64_t>(), order.data_ptr<int64_t>(), dy2.data_ptr(),
-                dw.data_ptr<float>(), int(flat.numel()), int(dw.size(1)), start, dw.size(0), cur_stream());
+  const int64_t seg = std::min<int64_t>(flat.numel(), embedding_sort_segment());
+  auto keys = torch::empty({std::max<int64_t>(seg, 1)}, flat.options());  // uint64 keys in int64 storage
+  embedding_bwd(flat.data_ptr<int64_t>(), dy2.data_ptr(), dw.data_ptr<float>(),
+                reinterpret_cast<uint64_t*>(keys.data_ptr<int64_t>()), int(flat.numel()), int(dw.size(1)), start,
+                dw.size(0), cur_stream());
 }
 
 // ---- cross-entropy --------------------------------------------------------------------
@@ -327,9 +328,9 @@ int64_t fused_slices_t(int64_t rows_per_rank) { return fused_slices(int(rows_per
 int64_t fused_tile_claims_t(int64_t t_rows, int64_t n, int64_t grid) {
   return fused_tile_claims(int(t_rows), int(n), int(grid));
 }
-int64_t fused_copy_claims_t(int64_t mode, int64_t t_rows, int64_t n, int64_t tp, int64_t slices, bool xg,
+int64_t fused_copy_claims_t(int64_t mode, int64_t t_rows, int64_t n, int64_t tp, int64_t slices, int64_t xg_chunks,
                             int64_t grid) {
-  return fused_copy_claims(int(mode), int(t_rows), int(n), int(tp), int(slices), xg, int(grid));
+  return fused_copy_claims(int(mode), int(t_rows), int(n), int(tp), int(slices), int(xg_chunks), int(grid));
 }
 
 // The peers of one fused call as a flat int64 list: rank, tp, rows_per_rank, slices, epoch,

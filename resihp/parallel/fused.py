@@ -106,7 +106,10 @@ class SymmetricWorkspace:
         self.total = self.out_off + 2 * self.stride
         self.guards = ([_FLAG_BYTES] + [self.land_off + i * self.stride + self.buf_bytes for i in range(6)]) if g else []
         with torch.cuda.device(self.device):
-            self.base, handle = k.symm_alloc(self.total)
+            # a tensor owns the region (freed when the last view of it dies: a caller may
+            # still hold the landing-zone view an AG returned)
+            self.region, handle = k.symm_region(self.total, self.device.index or 0)
+            self.base = self.region.data_ptr()
             for off in self.guards:
                 k.debug_fill_bytes(self.base + off, _GUARD_BYTES, _GUARD_VALUE)
             torch.cuda.synchronize()
@@ -148,26 +151,41 @@ class SymmetricWorkspace:
         return rows == self.t and width == self.width
 
     def _after(self, what: str, device, tile_ctr: int, copy_ctr: int, mode: int, n: int, grid: int,
-               xg: bool = False) -> None:
+               xg_chunks: int = 0) -> None:
         k = _ext.require()
         self.bases[tile_ctr] += k.fused_tile_claims(self.t, n, grid)
-        self.bases[copy_ctr] += k.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg, grid)
+        self.bases[copy_ctr] += k.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg_chunks, grid)
         _debug_check(what, device)
         if DEBUG:
             self.check_guards(what)
 
     # --- the three collectives ------------------------------------------------------
 
-    def all_gather_gemm(self, x_local, w, w_mn: bool, n: int, *, keep_gathered: bool = True):
-        """``(all_gather(x_local) @ op(w), gathered x or None)``; ``op(w)`` is ``w.T`` or ``w`` (``w_mn``)."""
+    def landing(self, epoch: int, width: int) -> torch.Tensor:
+        """This rank's AG landing zone of ``epoch``'s parity as a ``[T, width]`` view."""
+        start = self.land_off + (epoch % 2) * self.stride
+        return self.region[start:start + self.t * width * 2].view(torch.bfloat16).view(self.t, width)
+
+    def all_gather_gemm(self, x_local, w, w_mn: bool, n: int, *, keep_gathered=True):
+        """``(all_gather(x_local) @ op(w), gathered x or None)``; ``op(w)`` is ``w.T`` or ``w`` (``w_mn``).
+
+        ``keep_gathered``: ``True`` copies the gathered input into a new tensor (kept as
+        long as the caller wants); ``"landing"`` returns this rank's landing zone itself
+        (the kernel adds only the own chunk; valid until the AG call after next, so for
+        use right away); ``False`` returns none."""
         k = _ext.require()
         self.ag_epoch += 1
         x_local = x_local.contiguous()
-        xg = torch.empty((self.t, x_local.shape[1]), dtype=x_local.dtype, device=x_local.device) if keep_gathered else None
+        if keep_gathered == "landing":
+            xg, chunks = self.landing(self.ag_epoch, x_local.shape[1]), 1
+        elif keep_gathered:
+            xg, chunks = torch.empty((self.t, x_local.shape[1]), dtype=x_local.dtype, device=x_local.device), self.tp
+        else:
+            xg, chunks = None, 0
         y = torch.empty((self.t, n), dtype=x_local.dtype, device=x_local.device)
         grid = k.fused_grid(self.t, n, self.tp)
         k.ag_gemm(x_local, xg, w, w_mn, y, self._peers(0, 1), grid)
-        self._after(f"ag_gemm epoch {self.ag_epoch}", x_local.device, 0, 1, MODE_AG, n, grid, xg is not None)
+        self._after(f"ag_gemm epoch {self.ag_epoch}", x_local.device, 0, 1, MODE_AG, n, grid, chunks)
         return y, xg
 
     def gemm_reduce_scatter(self, h, w, w_mn: bool, n: int):
@@ -211,7 +229,7 @@ class SymmetricWorkspace:
         for r, p in enumerate(self.peers):
             if r != self.rank:
                 k.symm_close(p)
-        k.symm_free(self.base)
+        self.region = None  # freed with its last view
         self.closed = True
 
 
@@ -246,7 +264,9 @@ class _LinearRS(Function):
     @staticmethod
     def backward(ctx, dy_local):
         h, w = ctx.saved_tensors
-        dh, dyg = ctx.ws.all_gather_gemm(dy_local.contiguous(), w, True, w.shape[1])
+        # the gathered output gradient feeds the weight gradient right away: read it in place
+        dh, dyg = ctx.ws.all_gather_gemm(dy_local.contiguous(), w, True, w.shape[1],
+                                         keep_gathered="landing" if ctx.main_grad is not None else False)
         if ctx.main_grad is not None:
             linear_wgrad(dyg, h, out=ctx.main_grad, accumulate=True)
         return dh, None, None, None

@@ -76,20 +76,26 @@ class Emulation:
                 + [b + self.out_off + (self.epochs["ar"] % 2) * self.buf_bytes for b in bs]
                 + [b + fused._AR_CNT for b in bs])
 
-    def _advance(self, tile_ctr, copy_ctr, mode, n, grid, xg):
+    def _advance(self, tile_ctr, copy_ctr, mode, n, grid, xg_chunks):
         self.claims[tile_ctr] += self.kx.fused_tile_claims(self.t, n, grid)
-        self.claims[copy_ctr] += self.kx.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg, grid)
+        self.claims[copy_ctr] += self.kx.fused_copy_claims(mode, self.t, n, self.tp, self.slices, xg_chunks, grid)
 
     # --- the three launches (rank 0) ------------------------------------------------------
     def all_gather_gemm(self, w, *, w_mn=False, keep_gathered=True):
-        """``(y, xg)`` of rank 0's AG->GEMM: ``y = gather(x) @ op(w)``."""
+        """``(y, xg)`` of rank 0's AG->GEMM: ``y = gather(x) @ op(w)`` (``keep_gathered`` as
+        in :meth:`~resihp.parallel.fused.SymmetricWorkspace.all_gather_gemm`)."""
         self.epochs["ag"] += 1
         n = w.shape[1] if w_mn else w.shape[0]
-        xg = torch.empty(self.t, self.width, device=self.dev, dtype=torch.bfloat16) if keep_gathered else None
+        if keep_gathered == "landing":
+            xg, chunks = self.buf(0, self.land_off, self.epochs["ag"] % 2, (self.t, self.width)), 1
+        elif keep_gathered:
+            xg, chunks = torch.empty(self.t, self.width, device=self.dev, dtype=torch.bfloat16), self.tp
+        else:
+            xg, chunks = None, 0
         y = torch.empty(self.t, n, device=self.dev, dtype=torch.bfloat16)
         grid = self.kx.fused_grid(self.t, n, self.tp)
         self.kx.ag_gemm(self.x[:self.rpr], xg, w, w_mn, y, self._peers(0, 1, self.epochs["ag"]), grid)
-        self._advance(0, 1, fused.MODE_AG, n, grid, xg is not None)
+        self._advance(0, 1, fused.MODE_AG, n, grid, chunks)
         return y, xg
 
     def preset_partials(self, h_peers, w_peers, *, w_mn=False, all_reduce=False):
@@ -121,7 +127,7 @@ class Emulation:
         y = torch.empty(self.rpr, n, device=self.dev, dtype=torch.bfloat16)
         grid = self.kx.fused_grid(self.t, n, self.tp)
         self.kx.gemm_rs(h, w, w_mn, y, False, self._peers(2, 3, self.epochs["rs"]), grid)
-        self._advance(2, 3, fused.MODE_RS, n, grid, False)
+        self._advance(2, 3, fused.MODE_RS, n, grid, 0)
         return y
 
     def gemm_all_reduce(self, h, w, *, w_mn=False):
@@ -131,7 +137,7 @@ class Emulation:
         y = torch.empty(self.t, n, device=self.dev, dtype=torch.bfloat16)
         grid = self.kx.fused_grid(self.t, n, self.tp)
         self.kx.gemm_rs(h, w, w_mn, y, True, self._peers(2, 3, self.epochs["rs"]), grid)
-        self._advance(2, 3, fused.MODE_AR, n, grid, False)
+        self._advance(2, 3, fused.MODE_AR, n, grid, 0)
         return y
 
 

@@ -23,6 +23,7 @@ from resihp.ops import _ext
 
 FBM = 128
 RING = 4  # tile ring depth between a CTA's producer and its epilogue
+COPY_BATCH = 8  # copy items claimed at once (fused_gemm.cu: kCopyBatch)
 MODES = {"ag": 1, "rs": 2, "ar": 3}
 
 
@@ -73,17 +74,17 @@ class Simulation:
         self.per_chunk = self.blocks * self.tiles_n
         self.tiles = self.per_chunk * tp
         self.t_rows = rows_per_rank * tp
-        self.copy_claims = copy_claims or (lambda: self.k.fused_copy_claims(self.mode, self.t_rows, self.n, self.tp,
-                                                                           self.slices, self.keep, self.grid))
+        self.copy_claims = copy_claims or (lambda: self.k.fused_copy_claims(
+            self.mode, self.t_rows, self.n, self.tp, self.slices, self.tp if self.keep else 0, self.grid))
         self.ranks = [_Rank(tp, self.blocks, self.per_chunk) for _ in range(tp)]
 
     def _read(self, version, e, what):
         if version != e:
             raise ProtocolError(f"race: {what} holds epoch {version}, expected {e}")
 
-    def _claim(self, me, kind, limit):
+    def _claim(self, me, kind, limit, batch=1):
         got = me.ctr[kind] - me.base[kind]
-        me.ctr[kind] += 1
+        me.ctr[kind] += batch
         return got if 0 <= got < limit else -1
 
     # --- agents (generators yielding wait predicates) ----------------------------------
@@ -145,6 +146,8 @@ class Simulation:
                         self.ranks[p].ar_cnt[gtile] += 4
 
     def _copy(self, r, e, ar_e, xg):
+        """One CTA's copy warps: claim COPY_BATCH items at a time; a batch's pushes land,
+        then (one fence) their counts; then its gathered-copy and AR items."""
         me = self.ranks[r]
         par = e % 2
         units = self.blocks * self.slices
@@ -154,37 +157,43 @@ class Simulation:
         items = n_push + n_xg + n_ar
         if items == 0:
             return
+        size = 1 if self.op == "ar" else COPY_BATCH  # an AR item is a whole tile
         while True:
-            it = self._claim(me, "copy", items)
+            first = self._claim(me, "copy", items, size)
             yield lambda: True
-            if it < 0:
+            if first < 0:
                 return
-            me.seen_items.append(it)
-            if it < n_push:
-                j, u = divmod(it, units)
-                dest = (r - j - 1) % self.tp
-                rb = u // self.slices
-                peer = self.ranks[dest]
-                key = (r, rb)
-                # one unit's rows; the block's value is that of the last unit written
-                peer.land[par][key] = e
+            batch = range(first, min(first + size, items))
+            me.seen_items.extend(batch)
+            pushed = []
+            for it in batch:
+                if it < n_push:
+                    j, u = divmod(it, units)
+                    dest = (r - j - 1) % self.tp
+                    self.ranks[dest].land[par][(r, u // self.slices)] = e
+                    pushed.append((dest, u // self.slices))
+            if pushed:
                 yield lambda: True
-                peer.ag_cnt[r][rb] += 1
-            elif it < n_push + n_xg:
-                i2 = it - n_push
-                c = (r + i2 // units) % self.tp
-                rb = (i2 % units) // self.slices
-                if c != r:
-                    yield lambda c=c, rb=rb: me.ag_cnt[c][rb] >= self.slices * e
-                    self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} (xg) on {r}")
-                xg[(c, rb)] = xg.get((c, rb), 0) + 1
-            else:
-                i3 = it - n_push - n_xg
-                c = (r + 1 + i3 // self.per_chunk) % self.tp
-                lt = i3 % self.per_chunk
-                gtile = (c * self.blocks + lt // self.tiles_n) * self.tiles_n + lt % self.tiles_n
-                yield lambda g=gtile: me.ar_cnt[g] >= 4 * ar_e
-                self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
+                for dest, rb in pushed:
+                    self.ranks[dest].ag_cnt[r][rb] += 1
+            for it in batch:
+                if it < n_push:
+                    continue
+                if it < n_push + n_xg:
+                    i2 = it - n_push
+                    c = (r + i2 // units) % self.tp
+                    rb = (i2 % units) // self.slices
+                    if c != r:
+                        yield lambda c=c, rb=rb: me.ag_cnt[c][rb] >= self.slices * e
+                        self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} (xg) on {r}")
+                    xg[(c, rb)] = xg.get((c, rb), 0) + 1
+                else:
+                    i3 = it - n_push - n_xg
+                    c = (r + 1 + i3 // self.per_chunk) % self.tp
+                    lt = i3 % self.per_chunk
+                    gtile = (c * self.blocks + lt // self.tiles_n) * self.tiles_n + lt % self.tiles_n
+                    yield lambda g=gtile: me.ar_cnt[g] >= 4 * ar_e
+                    self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
 
     # --- the scheduler -------------------------------------------------------------------
 

@@ -48,7 +48,8 @@ def test_emulated_ag_gemm(tp):
 
 @pytest.mark.parametrize("tp", [2, 4, 8])
 def test_emulated_ag_gemm_mn_weight(tp):
-    """The backward form (``w`` read N-major: ``dy_gathered @ w``) without a gathered copy."""
+    """The backward form (``w`` read N-major: ``dy_gathered @ w``), without a gathered copy
+    and with the landing zone itself as the gathered input (only the own chunk added)."""
     from resihp.ops import check_device_errors
     from resihp.utils.fused_emulation import Emulation
 
@@ -58,6 +59,10 @@ def test_emulated_ag_gemm_mn_weight(tp):
     torch.cuda.synchronize()
     check_device_errors(0)
     assert xg is None and _rel(y, em.x.float() @ w.float()) < 1e-2
+    y, land = em.all_gather_gemm(w, w_mn=True, keep_gathered="landing")
+    torch.cuda.synchronize()
+    check_device_errors(0)
+    assert torch.equal(land, em.x) and _rel(y, em.x.float() @ w.float()) < 1e-2
 
 
 @pytest.mark.parametrize("all_reduce", [False, True], ids=["rs", "ar"])

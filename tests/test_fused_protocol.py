@@ -31,7 +31,7 @@ def test_a_host_counting_the_wrong_claims_is_caught():
     # a host that forgets the copy warps' one failing claim per CTA starts the next call's
     # claims in the middle of the items: units are skipped or repeated
     k = __import__("resihp.ops._ext", fromlist=["require"]).require()
-    wrong = lambda: k.fused_copy_claims(1, 512, 512, 2, 4, True, 3) - 3  # noqa: E731
+    wrong = lambda: k.fused_copy_claims(1, 512, 512, 2, 4, 2, 3) - 8 * 3  # noqa: E731
     with pytest.raises(ProtocolError, match="race|deadlock|incomplete"):
         Simulation("ag", tp=2, rows_per_rank=256, n=512, grid=3, epochs=4, seed=0, copy_claims=wrong).run()
 

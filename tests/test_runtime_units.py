@@ -205,8 +205,8 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
         def __init__(self):
             self.ag, self.rs = [], []
 
-        def symm_alloc(self, total):
-            return 1 << 20, b"h"
+        def symm_region(self, total, device):
+            return torch.zeros(total, dtype=torch.uint8), b"h"
 
         def symm_open(self, handle):
             return 1 << 30
