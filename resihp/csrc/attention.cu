@@ -13,10 +13,12 @@
 //   warp 1      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers,
 //               O += P_j V_j into the TMEM O accumulator (S_{j+1} is issued before
 //               PV_j so the tensor core works while softmax runs)
-//   warps 2-5   softmax, one thread per query row: row max over the S row in TMEM,
-//               P = exp2(S * scale*log2e - m), P written as bf16 into a 128B-swizzled
-//               smem tile (the A operand of PV), O rescaled in TMEM when the max grows,
-//               finally O / l stored as bf16 and the log-sum-exp kept for backward.
+//   warps 2-9   softmax, two threads per query row (the two warps of a TMEM lane
+//               quadrant take 64 columns each and exchange the row maximum through
+//               shared memory): P = exp2(S * scale*log2e - m), P written as bf16 into a
+//               128B-swizzled smem tile (the A operand of PV), each half of O rescaled
+//               in TMEM when the max grows, finally O / l stored as bf16 and the
+//               log-sum-exp kept for backward.
 // Backward (deterministic, no atomics):
 //   attn_bwd_dkdv  one CTA per (kv block, kv head, batch), looping over every q head of
 //                  the group and every causal q block: S^T = K Q^T, dP^T = V dO^T,
@@ -80,17 +82,20 @@ __device__ __forceinline__ void store_row32(uint8_t* tile, int r, int c0, const 
   }
 }
 
+constexpr int kFwdThreads = 64 + 8 * 32;  // producer, MMA issuer, eight softmax warps
+
 template <int D>
 struct FwdSmem {
   static constexpr int kQ = kBlk * D * 2;
   static constexpr int kKV = kBlk * D * 2;
   static constexpr int kStages = 2;
   static constexpr int kP = kBlk * kBlk * 2;
-  static constexpr int kBytes = kQ + 2 * kStages * kKV + kP + 1024 + 256;
+  static constexpr int kMx = 6 * kBlk * 4;   // row-max exchange [2 blocks][2 halves][128], row-sum [2][128]
+  static constexpr int kBytes = kQ + 2 * kStages * kKV + kP + kMx + 1024 + 256;
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
   using L = FwdSmem<D>;
   constexpr int ST = L::kStages;
@@ -101,7 +106,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sk = sq + L::kQ;                 // ST stages of K
   uint8_t* sv = sk + ST * L::kKV;           // ST stages of V
   uint8_t* sp = sv + ST * L::kKV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + L::kP);
+  float* s_mx = reinterpret_cast<float*>(sp + L::kP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + L::kP + L::kMx);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + ST;
@@ -134,9 +140,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);
+      mbar_init(&s_empty[s], 8);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     fence_barrier_init();
   }
@@ -220,69 +226,82 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) issue_pv(nblk - 1);
     }
   } else {
+    // eight softmax warps: the two warps of a TMEM lane quadrant split each row's 128
+    // columns (and O's D columns); only the row maximum is exchanged per block
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;           // query row within the tile
     const uint32_t lane_off = uint32_t(q4 * 32) << 16;
     const float sl2 = a.scale * kLog2e;
-    float m = -INFINITY, l = 0.f;
+    constexpr int kHalf = kBlk / 2;
+    float m = -INFINITY, l = 0.f;           // l: this half's share of the row sum
     bool ok = true;
+    // Every softmax thread passes named barrier 2 exactly once per block and once after
+    // the loop, also after a wait ran out (it then only keeps the barrier count), so the
+    // two warps of a pair can never wait at different barrier instances.
     for (int j = 0; j < nblk; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
-      tc_fence_after();
+      if (ok && !mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrEpiWait)) ok = false;
       const bool diag = j == qblk;
-      const uint32_t t_s = tmem + sb * kBlk + lane_off;
-      // the whole S row in registers: four 32-column loads, one wait
-      uint32_t v[kBlk];
-      #pragma unroll
-      for (int c = 0; c < kBlk; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
-      tmem_wait_ld();
-      float mx = m;
-      if (diag) {
+      uint32_t v[kHalf];
+      float mloc = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        const uint32_t t_s = tmem + sb * kBlk + lane_off + half * kHalf;
         #pragma unroll
-        for (int e = 0; e < kBlk; ++e)
-          if (e <= r) mx = fmaxf(mx, __uint_as_float(v[e]));
-      } else {
-        #pragma unroll
-        for (int e = 0; e < kBlk; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+        for (int c = 0; c < kHalf; c += 32) tmem_ld32(t_s + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+        tmem_wait_ld();
+        if (diag) {
+          #pragma unroll
+          for (int e = 0; e < kHalf; ++e)
+            if (half * kHalf + e <= r) mloc = fmaxf(mloc, __uint_as_float(v[e]));
+        } else {
+          #pragma unroll
+          for (int e = 0; e < kHalf; ++e) mloc = fmaxf(mloc, __uint_as_float(v[e]));
+        }
       }
+      s_mx[(sb * 2 + half) * kBlk + r] = mloc;
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (!ok) continue;
+      const float mx = fmaxf(m, fmaxf(mloc, s_mx[(sb * 2 + (half ^ 1)) * kBlk + r]));
       const float alpha = fast_exp2((m - mx) * sl2);   // 0 on the first block (m = -inf)
       const float neg = mx * sl2;
       // P smem is still being read by PV_{j-1}: wait for it before overwriting
       if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+        if (!mbar_wait(pv_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; continue; }
         tc_fence_after();
       }
       float rowsum = 0.f;
       #pragma unroll
-      for (int c = 0; c < kBlk; c += 32) {
+      for (int c = 0; c < kHalf; c += 32) {
         uint32_t pk[16];
         #pragma unroll
         for (int e = 0; e < 32; e += 2) {
+          const int col = half * kHalf + c + e;
           float p0 = fast_exp2(fmaf(__uint_as_float(v[c + e]), sl2, -neg));
           float p1 = fast_exp2(fmaf(__uint_as_float(v[c + e + 1]), sl2, -neg));
-          if (diag && c + e > r) p0 = 0.f;
-          if (diag && c + e + 1 > r) p1 = 0.f;
+          if (diag && col > r) p0 = 0.f;
+          if (diag && col + 1 > r) p1 = 0.f;
           rowsum += p0 + p1;
           pk[e / 2] = pack_bf16(p0, p1);
         }
-        store_row32(sp, r, c, pk, kBlk);
+        store_row32(sp, r, half * kHalf + c, pk, kBlk);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
       l = l * alpha + rowsum;
       m = mx;
-      // rescale the running O when this warp saw the max grow
+      // rescale this half's columns of the running O when this warp saw the max grow
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         #pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(t_o + lane_off + c, v);
+        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 16) {
+          uint32_t w16[16];
+          tmem_ld16(t_o + lane_off + c, w16);
           tmem_wait_ld();
           #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-          tmem_st16(t_o + lane_off + c, v);
+          for (int e = 0; e < 16; ++e) w16[e] = __float_as_uint(__uint_as_float(w16[e]) * alpha);
+          tmem_st16(t_o + lane_off + c, w16);
         }
         tmem_wait_st();
       }
@@ -291,26 +310,31 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
+    // the row sum: both halves' shares, added in half order (own slots: the partner may
+    // still be reading the last block's maximum)
+    s_mx[(4 + half) * kBlk + r] = l;
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    const float lsum = s_mx[4 * kBlk + r] + s_mx[5 * kBlk + r];
     if (ok && mbar_wait(pv_done, (nblk - 1) & 1, a.err, kErrEpiWait)) {
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / lsum;
       __nv_bfloat16* dst = a.out + int64_t(row0 + r) * a.out_ld + int64_t(h) * D;
       #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_o + lane_off + c, v);
+      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
+        uint32_t w32[32];
+        tmem_ld32(t_o + lane_off + c, w32);
         tmem_wait_ld();
         #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint4 o;
-          o.x = pack_bf16(__uint_as_float(v[8 * u + 0]) * inv, __uint_as_float(v[8 * u + 1]) * inv);
-          o.y = pack_bf16(__uint_as_float(v[8 * u + 2]) * inv, __uint_as_float(v[8 * u + 3]) * inv);
-          o.z = pack_bf16(__uint_as_float(v[8 * u + 4]) * inv, __uint_as_float(v[8 * u + 5]) * inv);
-          o.w = pack_bf16(__uint_as_float(v[8 * u + 6]) * inv, __uint_as_float(v[8 * u + 7]) * inv);
+          o.x = pack_bf16(__uint_as_float(w32[8 * u + 0]) * inv, __uint_as_float(w32[8 * u + 1]) * inv);
+          o.y = pack_bf16(__uint_as_float(w32[8 * u + 2]) * inv, __uint_as_float(w32[8 * u + 3]) * inv);
+          o.z = pack_bf16(__uint_as_float(w32[8 * u + 4]) * inv, __uint_as_float(w32[8 * u + 5]) * inv);
+          o.w = pack_bf16(__uint_as_float(w32[8 * u + 6]) * inv, __uint_as_float(w32[8 * u + 7]) * inv);
           *reinterpret_cast<uint4*>(dst + c + 8 * u) = o;
         }
       }
-      a.lse[(int64_t(b) * a.hq + h) * a.seq + qblk * kBlk + r] = m * a.scale + logf(l);
+      if (half == 0) a.lse[(int64_t(b) * a.hq + h) * a.seq + qblk * kBlk + r] = m * a.scale + logf(lsum);
     }
   }
   tc_fence_before();
@@ -830,10 +854,10 @@ void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float*
   dim3 grid(hq, rows / seq, seq / kBlk);
   if (d == 128) {
     set_smem(attn_fwd_kernel<128>, FwdSmem<128>::kBytes);
-    attn_fwd_kernel<128><<<grid, 192, FwdSmem<128>::kBytes, st>>>(tm, a);
+    attn_fwd_kernel<128><<<grid, kFwdThreads, FwdSmem<128>::kBytes, st>>>(tm, a);
   } else {
     set_smem(attn_fwd_kernel<64>, FwdSmem<64>::kBytes);
-    attn_fwd_kernel<64><<<grid, 192, FwdSmem<64>::kBytes, st>>>(tm, a);
+    attn_fwd_kernel<64><<<grid, kFwdThreads, FwdSmem<64>::kBytes, st>>>(tm, a);
   }
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
