@@ -23,14 +23,16 @@
 //     (source, block). The producer loads own-chunk tiles from x_local and a peer chunk's
 //     tiles from the local landing zone once that block's counter is complete. The copy
 //     warps then also assemble the gathered input in ``xg`` for the backward pass.
-// RS: tiles of the peers' token chunks run first; their epilogue stores the bf16
-//     partial straight into the owning peer's receive buffer and counts the tile there.
+// RS: tiles of the peers' token chunks run first; their epilogue stores the bf16 partial
+//     in a local send buffer and flags it, and the copy warps push each finished partial
+//     tile, row by row (one warp store per 512-byte row), into the owning peer's receive
+//     buffer and count it there.
 //     Own-chunk tiles run last: their epilogue waits for the tp-1 contributions and sums
 //     every rank's partial in rank order (this rank's own in fp32), deterministically.
 //     (The tile counters come in two banks by call parity: a fast source may already be
 //     contributing to the next call.)
-// AR: RS, then each owner pushes its reduced tile into every peer's output landing zone
-//     and counts it; the copy warps copy the other owners' tiles from there into y.
+// AR: RS, then the copy warps push each own reduced tile into every peer's output
+//     landing zone and count it, and copy the other owners' tiles from there into y.
 //
 // Work is claimed dynamically -- output tiles by the producer, copy items by the copy
 // warps -- from per-call counters in the same global order on every rank (peer data
@@ -116,25 +118,28 @@ __device__ __forceinline__ void copy_span(uint4* dst, const uint4* src, int64_t 
   }
 }
 
-// ``rows`` rows of ``cols16`` 16-byte vectors with their own row strides (in vectors).
+// ``rows`` rows of ``cols16`` (at most 32) 16-byte vectors with their own row strides (in
+// vectors): one warp per row, each lane one vector, kCopyUnroll rows in flight per warp
+// before their stores (a 256-column bf16 tile row is one 512-byte warp access).
 __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* src, int64_t sld, int rows, int cols16,
                                           int ct, int* err) {
   if (!bounds_ok(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0 &&
-                     cols16 <= dld && cols16 <= sld,
+                     cols16 <= dld && cols16 <= sld && cols16 <= 32,
                  err))
     return;
-  const int64_t total = int64_t(rows) * cols16;
-  for (int64_t base = ct; base < total; base += int64_t(kCopyThreads) * kCopyUnroll) {
-    uint4 r[kCopyUnroll];
+  const int w = ct >> 5, lane = ct & 31;
+  if (lane >= cols16) return;
+  for (int r0 = w; r0 < rows; r0 += kCopyWarps * kCopyUnroll) {
+    uint4 v[kCopyUnroll];
     #pragma unroll
     for (int u = 0; u < kCopyUnroll; ++u) {
-      const int64_t i = base + int64_t(u) * kCopyThreads;
-      if (i < total) r[u] = ld_cg_v4(src + (i / cols16) * sld + (i % cols16));
+      const int r = r0 + u * kCopyWarps;
+      if (r < rows) v[u] = ld_cg_v4(src + int64_t(r) * sld + lane);
     }
     #pragma unroll
     for (int u = 0; u < kCopyUnroll; ++u) {
-      const int64_t i = base + int64_t(u) * kCopyThreads;
-      if (i < total) dst[(i / cols16) * dld + (i % cols16)] = r[u];
+      const int r = r0 + u * kCopyWarps;
+      if (r < rows) dst[int64_t(r) * dld + lane] = v[u];
     }
   }
 }
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   // RS counters come in two banks by call parity: contributions to one tile come from
   // tp-1 sources, and a source can be one call ahead (never two), so counting a call's
   // parity only is what keeps a fast source's next-call contributions out of this count.
-  const unsigned rs_target = 4u * unsigned(p.tp - 1) * ((p.epoch + 1u) / 2u);
+  const unsigned rs_target = unsigned(p.tp - 1) * ((p.epoch + 1u) / 2u);
   unsigned* const rs_bank_local = p.rs_cnt[p.rank] + (p.epoch & 1u) * kFusedMaxTiles;
 
   if (threadIdx.x == 0) {
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       bool ok = true;
       __nv_bfloat16* dst;
       if (MODE == kModeAG) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
-      else if (!own) dst = p.recv[chunk] + (int64_t(p.rank) * rpr + lrow) * g.n;  // the owner's receive buffer
+      else if (!own) dst = p.send + int64_t(row) * g.n;  // local; the copy warps push it to the owner
       else if (MODE == kModeRS) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(lrow) * g.ldc;
       else dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
       if (reduce_here) {
@@ -389,30 +394,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           o[u].w = pack_bf16(f[8 * u + 6], f[8 * u + 7]);
           *reinterpret_cast<uint4*>(dst + col0 + 8 * u) = o[u];
         }
-        if (MODE == kModeAR && own) {
-          // the reduced rows, pushed into every peer's output landing zone
-          for (int r = 0; r < p.tp; ++r) {
-            if (r == p.rank) continue;
-            __nv_bfloat16* pd = p.out_land[r] + int64_t(row) * g.n + col0;
-            #pragma unroll
-            for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(pd + 8 * u) = o[u];
-          }
-        }
       }
       if (MODE != kModeAG && !own) {
-        // this warp's 32 rows of the partial tile are in the owner's buffer: count them there
-        __threadfence_system();
+        // this warp's 32 rows of the partial tile are in the local send buffer
+        __threadfence();
         __syncwarp();
-        if (lane == 0) red_release_add(p.rs_cnt[chunk] + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+        if (lane == 0) atomicAdd(p.send_cnt + (m0 / kFBM) * tiles_n + tn, 1u);
       }
       if (MODE == kModeAR && own && ok) {
-        __threadfence_system();
+        // this warp's 32 reduced rows are in y: the copy warps push them to every peer
+        __threadfence();
         __syncwarp();
-        if (lane == 0) {
-          const int global_tile = (m0 / kFBM) * tiles_n + tn;
-          for (int r = 0; r < p.tp; ++r)
-            if (r != p.rank) red_release_add(p.ar_cnt[r] + global_tile, 1u);
-        }
+        if (lane == 0) atomicAdd(p.own_cnt + local_tile, 1u);
       }
       tc_fence_before();
       __syncwarp();
@@ -431,9 +424,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // gathered copy: every chunk into xg, or (xg is this rank's landing zone, which the
     // peers already fill) only the own chunk
     const int n_xg = MODE != kModeAG || g.xg == nullptr ? 0 : (g.xg == p.land[p.rank] ? units : p.tp * units);
+    // RS / AR: push each peer-chunk partial tile to its owner (in the order the tiles are
+    // claimed); AR also: push each own reduced tile to every peer, then copy the other
+    // owners' reduced tiles from the output landing zone into y
+    const int n_rsp = MODE != kModeAG ? (p.tp - 1) * per_chunk : 0;
+    const int n_own = MODE == kModeAR ? per_chunk : 0;
     const int n_ar = MODE == kModeAR ? (p.tp - 1) * per_chunk : 0;
-    const int items = n_push + n_xg + n_ar;
-    const int batch = MODE == kModeAR ? 1 : kCopyBatch;  // an AR item is a whole 128 x 256 tile
+    const int items = MODE == kModeAG ? n_push + n_xg : n_rsp + n_own + n_ar;
+    const int batch = MODE == kModeAG ? kCopyBatch : 1;  // an RS / AR item is a whole 128 x 256 tile
     while (items > 0) {
       if (ct == 0) claim[0] = int(atomicAdd(p.copy_ctr, unsigned(batch)) - p.copy_base);
       copy_bar();
@@ -492,24 +490,60 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                     ct, g.err);
         i = run_end;
       }
-      // AR: other owners' reduced tiles, from the output landing zone into y
-      for (int it = max(first_item, n_push + n_xg); it < last_item && ok; ++it) {
-        const int i3 = it - n_push - n_xg;
-        const int c = (p.rank + 1 + i3 / per_chunk) % p.tp;
-        const int lt = i3 % per_chunk;
-        const int m0 = c * rpr + (lt / tiles_n) * kFBM;
-        const int tn = lt % tiles_n;
-        const int global_tile = (m0 / kFBM) * tiles_n + tn;
-        if (ct == 0)
-          claim[1] = wait_geq(p.ar_cnt[p.rank] + global_tile, 4u * p.ar_epoch, g.err, kErrPeerWait, g.wait_ns);
+      // RS / AR items (one tile each)
+      for (int it = first_item; MODE != kModeAG && it < last_item && ok; ++it) {
+        int chunk, m0, tn;
+        if (it < n_rsp + n_own) {
+          fused_tile(it, tiles_m_chunk, tiles_n, p, 1, chunk, m0, tn);  // push items follow the claim order
+        } else {
+          const int i3 = it - n_rsp - n_own;  // gather: another owner's reduced tile
+          chunk = (p.rank + 1 + i3 / per_chunk) % p.tp;
+          const int lt = i3 % per_chunk;
+          m0 = chunk * rpr + (lt / tiles_n) * kFBM;
+          tn = lt % tiles_n;
+        }
+        const int gtile = (m0 / kFBM) * tiles_n + tn;
+        const int local_tile = ((m0 - chunk * rpr) / kFBM) * tiles_n + tn;
+        const int ncols16 = min(BN, g.n - tn * BN) / 8;
+        if (ct == 0) {
+          if (it < n_rsp)
+            claim[1] = wait_geq(p.send_cnt + gtile, 4u * p.epoch, g.err, kErrEpiWait, kWaitBudgetNs);
+          else if (it < n_rsp + n_own)
+            claim[1] = wait_geq(p.own_cnt + local_tile, 4u * p.ar_epoch, g.err, kErrEpiWait, kWaitBudgetNs);
+          else
+            claim[1] = wait_geq(p.ar_cnt[p.rank] + gtile, p.ar_epoch, g.err, kErrPeerWait, g.wait_ns);
+        }
         copy_bar();
         ok = claim[1] != 0;
         copy_bar();
         if (!ok) break;
-        const int ncols16 = min(BN, g.n - tn * BN) / 8;
-        copy_rows(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN), g.ldc / 8,
-                  reinterpret_cast<const uint4*>(p.out_land[p.rank] + int64_t(m0) * g.n + tn * BN), g.n / 8, kFBM,
-                  ncols16, ct, g.err);
+        if (it < n_rsp) {
+          // the partial tile -> the owner's receive buffer, slot of this rank
+          copy_rows(reinterpret_cast<uint4*>(p.recv[chunk] + (int64_t(p.rank) * rpr + (m0 - chunk * rpr)) * g.n +
+                                             tn * BN),
+                    g.n / 8, reinterpret_cast<const uint4*>(p.send + int64_t(m0) * g.n + tn * BN), g.n / 8, kFBM,
+                    ncols16, ct, g.err);
+          __threadfence_system();
+          copy_bar();
+          if (ct == 0) red_release_add(p.rs_cnt[chunk] + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+        } else if (it < n_rsp + n_own) {
+          // the reduced tile -> every peer's output landing zone
+          const uint4* src =
+              reinterpret_cast<const uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN);
+          for (int r = 0; r < p.tp; ++r)
+            if (r != p.rank)
+              copy_rows(reinterpret_cast<uint4*>(p.out_land[r] + int64_t(m0) * g.n + tn * BN), g.n / 8, src,
+                        g.ldc / 8, kFBM, ncols16, ct, g.err);
+          __threadfence_system();
+          copy_bar();
+          if (ct == 0)
+            for (int r = 0; r < p.tp; ++r)
+              if (r != p.rank) red_release_add(p.ar_cnt[r] + gtile, 1u);
+        } else {
+          copy_rows(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN),
+                    g.ldc / 8, reinterpret_cast<const uint4*>(p.out_land[p.rank] + int64_t(m0) * g.n + tn * BN),
+                    g.n / 8, kFBM, ncols16, ct, g.err);
+        }
       }
       if (!ok) break;
     }
@@ -576,9 +610,10 @@ int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_ch
   const int per_chunk = (rpr / kFBM) * ((n + 255) / 256);
   int items = 0;
   if (mode == kModeAG) items = (tp - 1) * units + xg_chunks * units;
-  if (mode == kModeAR) items = (tp - 1) * per_chunk;
+  if (mode == kModeRS) items = (tp - 1) * per_chunk;
+  if (mode == kModeAR) items = (tp - 1) * per_chunk + per_chunk + (tp - 1) * per_chunk;
   // every batch claimed, plus one failing claim per CTA, a batch of items each
-  const int batch = mode == kModeAR ? 1 : kCopyBatch;
+  const int batch = mode == kModeAG ? kCopyBatch : 1;
   return items > 0 ? ((items + batch - 1) / batch + grid) * batch : 0;
 }
 

@@ -119,6 +119,9 @@ struct FusedPeers {
   unsigned* rs_cnt[kFusedMaxTp];         // RS per-own-tile counters [2 parities][kFusedMaxTiles] of each rank
   __nv_bfloat16* out_land[kFusedMaxTp];  // AR reduced-output landing zone [T, N] of each rank (parity)
   unsigned* ar_cnt[kFusedMaxTp];         // AR per-tile counters of each rank
+  __nv_bfloat16* send;                   // local: RS partial tiles [T, N] before the push
+  unsigned* send_cnt;                    // local: per-tile count of finished partial rows (4 warps per call)
+  unsigned* own_cnt;                     // local: per-own-tile count of finished reduced rows (AR)
 };
 int fused_grid(int m, int n, int tp);
 int fused_slices(int rows_per_rank);

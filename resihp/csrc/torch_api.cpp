@@ -349,7 +349,7 @@ static FusedPeers decode_peers(const std::vector<int64_t>& v) {
   p.tile_base = unsigned(v[7]);
   p.copy_ctr = as_ptr<unsigned>(v[8]);
   p.copy_base = unsigned(v[9]);
-  TORCH_CHECK(p.tp >= 2 && p.tp <= kFusedMaxTp && v.size() == size_t(10 + 6 * p.tp), "fused peers: bad length");
+  TORCH_CHECK(p.tp >= 2 && p.tp <= kFusedMaxTp && v.size() == size_t(10 + 6 * p.tp + 3), "fused peers: bad length");
   for (int r = 0; r < p.tp; ++r) {
     p.land[r] = as_ptr<__nv_bfloat16>(v[10 + r]);
     p.ag_cnt[r] = as_ptr<unsigned>(v[10 + p.tp + r]);
@@ -358,6 +358,9 @@ static FusedPeers decode_peers(const std::vector<int64_t>& v) {
     p.out_land[r] = as_ptr<__nv_bfloat16>(v[10 + 4 * p.tp + r]);
     p.ar_cnt[r] = as_ptr<unsigned>(v[10 + 5 * p.tp + r]);
   }
+  p.send = as_ptr<__nv_bfloat16>(v[10 + 6 * p.tp]);
+  p.send_cnt = as_ptr<unsigned>(v[11 + 6 * p.tp]);
+  p.own_cnt = as_ptr<unsigned>(v[12 + 6 * p.tp]);
   return p;
 }
 

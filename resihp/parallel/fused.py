@@ -49,8 +49,10 @@ MAX_TP, MAX_RB, MAX_TILES = 8, 256, 8192     # launch.h: kFusedMaxTp, kFusedMaxR
 _AG_CNT = 0                                   # byte offsets of the counter words in the flag area
 _RS_CNT = _AG_CNT + 4 * MAX_TP * MAX_RB       # two banks by call parity
 _AR_CNT = _RS_CNT + 2 * 4 * MAX_TILES
-_CTRS = _AR_CNT + 4 * MAX_TILES               # local claim counters: AG tile, AG copy, RS tile, RS copy
-_FLAG_BYTES = 112 * 1024
+_SEND_CNT = _AR_CNT + 4 * MAX_TILES           # local: finished partial rows per tile (RS, AR)
+_OWN_CNT = _SEND_CNT + 4 * MAX_TILES          # local: finished reduced rows per own tile (AR)
+_CTRS = _OWN_CNT + 4 * MAX_TILES              # local claim counters: AG tile, AG copy, RS tile, RS copy
+_FLAG_BYTES = 176 * 1024
 _GUARD_BYTES = 256                            # debug layout: guard bytes after every buffer
 _GUARD_VALUE = 0xA5
 _U32 = 0xFFFFFFFF
@@ -73,8 +75,9 @@ def _debug_check(what: str, device) -> None:
 class SymmetricWorkspace:
     """This rank's IPC-shared region and its mappings of every peer's region.
 
-    Layout (bytes): counter words (112 KB) | two AG landing zones ``[T, width]`` | two RS
-    receive buffers ``[tp, T/tp, width]`` | two AR output landing zones ``[T, width]``.
+    Layout (bytes): counter words (176 KB) | two AG landing zones ``[T, width]`` | two RS
+    receive buffers ``[tp, T/tp, width]`` | two AR output landing zones ``[T, width]`` |
+    the RS send buffer ``[T, width]`` (local: partial tiles before the copy warps push them).
     Every fused call's gathered input, reduced output and all-reduced output has the
     model width, so one region serves all projections of a layer and their backward.
     """
@@ -103,8 +106,9 @@ class SymmetricWorkspace:
         self.land_off = _FLAG_BYTES + g
         self.recv_off = self.land_off + 2 * self.stride
         self.out_off = self.recv_off + 2 * self.stride
-        self.total = self.out_off + 2 * self.stride
-        self.guards = ([_FLAG_BYTES] + [self.land_off + i * self.stride + self.buf_bytes for i in range(6)]) if g else []
+        self.send_off = self.out_off + 2 * self.stride
+        self.total = self.send_off + self.stride
+        self.guards = ([_FLAG_BYTES] + [self.land_off + i * self.stride + self.buf_bytes for i in range(7)]) if g else []
         with torch.cuda.device(self.device):
             # a tensor owns the region (freed when the last view of it dies: a caller may
             # still hold the landing-zone view an AG returned)
@@ -137,7 +141,8 @@ class SymmetricWorkspace:
         ps = self.peers
         return (head + [self._buf(p, self.land_off, self.ag_epoch) for p in ps] + [p + _AG_CNT for p in ps]
                 + [self._buf(p, self.recv_off, self.rs_epoch) for p in ps] + [p + _RS_CNT for p in ps]
-                + [self._buf(p, self.out_off, self.ar_epoch) for p in ps] + [p + _AR_CNT for p in ps])
+                + [self._buf(p, self.out_off, self.ar_epoch) for p in ps] + [p + _AR_CNT for p in ps]
+                + [self.base + self.send_off, self.base + _SEND_CNT, self.base + _OWN_CNT])
 
     def check_guards(self, what: str) -> None:
         """Debug layout: raise if a kernel wrote past any buffer of this region."""

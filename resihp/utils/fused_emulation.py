@@ -42,7 +42,8 @@ class Emulation:
         self.land_off = fused._FLAG_BYTES
         self.recv_off = self.land_off + 2 * self.buf_bytes
         self.out_off = self.recv_off + 2 * self.buf_bytes
-        total = self.out_off + 2 * self.buf_bytes
+        self.send_off = self.out_off + 2 * self.buf_bytes
+        total = self.send_off + self.buf_bytes
         self.regions = [torch.zeros(total, dtype=torch.uint8, device=self.dev) for _ in range(tp)]
         self.bases = [r.data_ptr() for r in self.regions]
         self.epochs = {"ag": 0, "rs": 0, "ar": 0}
@@ -74,7 +75,8 @@ class Emulation:
                 + [b + self.recv_off + (self.epochs["rs"] % 2) * self.buf_bytes for b in bs]
                 + [b + fused._RS_CNT for b in bs]
                 + [b + self.out_off + (self.epochs["ar"] % 2) * self.buf_bytes for b in bs]
-                + [b + fused._AR_CNT for b in bs])
+                + [b + fused._AR_CNT for b in bs]
+                + [bs[0] + self.send_off, bs[0] + fused._SEND_CNT, bs[0] + fused._OWN_CNT])
 
     def _advance(self, tile_ctr, copy_ctr, mode, n, grid, xg_chunks):
         self.claims[tile_ctr] += self.kx.fused_tile_claims(self.t, n, grid)

@@ -49,9 +49,12 @@ class _Rank:
     def __init__(self, tp, blocks, per_chunk):
         self.ag_cnt = [[0] * blocks for _ in range(tp)]         # [src][row block] push units landed
         self.land = [dict(), dict()]                            # parity -> {(chunk, row block): epoch}
-        self.rs_cnt = [[0] * per_chunk, [0] * per_chunk]        # [call parity][own tile] -> partial warps landed
+        self.rs_cnt = [[0] * per_chunk, [0] * per_chunk]        # [call parity][own tile] -> partial tiles landed
         self.recv = [dict(), dict()]                            # parity -> {(src, tile): epoch}
-        self.ar_cnt = [0] * (per_chunk * tp)                    # global tile -> reduced warps landed
+        self.send = dict()                                      # local send buffer: {global tile: epoch}
+        self.send_cnt = [0] * (per_chunk * tp)                  # global tile -> partial warps in the send buffer
+        self.own_cnt = [0] * per_chunk                          # own tile -> reduced warps in y (AR)
+        self.ar_cnt = [0] * (per_chunk * tp)                    # global tile -> reduced tiles landed
         self.out = [dict(), dict()]                             # parity -> {global tile: ar epoch}
         self.ctr = {"tile": 0, "copy": 0}                       # claim counters (device)
         self.base = {"tile": 0, "copy": 0}                      # what the host believes they hold
@@ -125,25 +128,19 @@ class Simulation:
             local = rb * self.tiles_n + tn
             if self.op == "ag":
                 continue
+            gtile = (c * self.blocks + rb) * self.tiles_n + tn
             if c != r:
-                owner = self.ranks[c]
-                owner.recv[par][(r, local)] = e                     # partial pushed into the owner
+                me.send[gtile] = e                                  # partial into the local send buffer
                 yield lambda: True
-                owner.rs_cnt[par][local] += 4                       # four epilogue warps count it
+                me.send_cnt[gtile] += 4                             # four epilogue warps count it
                 continue
-            yield lambda local=local: me.rs_cnt[par][local] >= 4 * (self.tp - 1) * ((e + 1) // 2)
+            yield lambda local=local: me.rs_cnt[par][local] >= (self.tp - 1) * ((e + 1) // 2)
             for src in range(self.tp):
                 if src != r:
                     self._read(me.recv[par].get((src, local)), e, f"RS receive of tile {local} from {src} on {r}")
             if self.op == "ar":
-                gtile = (c * self.blocks + rb) * self.tiles_n + tn
-                for p in range(self.tp):
-                    if p != r:
-                        self.ranks[p].out[ar_e % 2][gtile] = ar_e
                 yield lambda: True
-                for p in range(self.tp):
-                    if p != r:
-                        self.ranks[p].ar_cnt[gtile] += 4
+                me.own_cnt[local] += 4                              # reduced rows in y, for the copy warps
 
     def _copy(self, r, e, ar_e, xg):
         """One CTA's copy warps: claim COPY_BATCH items at a time; a batch's pushes land,
@@ -153,11 +150,13 @@ class Simulation:
         units = self.blocks * self.slices
         n_push = (self.tp - 1) * units if self.op == "ag" else 0
         n_xg = self.tp * units if (self.op == "ag" and self.keep) else 0
+        n_rsp = (self.tp - 1) * self.per_chunk if self.op != "ag" else 0
+        n_own = self.per_chunk if self.op == "ar" else 0
         n_ar = (self.tp - 1) * self.per_chunk if self.op == "ar" else 0
-        items = n_push + n_xg + n_ar
+        items = n_push + n_xg if self.op == "ag" else n_rsp + n_own + n_ar
         if items == 0:
             return
-        size = 1 if self.op == "ar" else COPY_BATCH  # an AR item is a whole tile
+        size = 1 if self.op != "ag" else COPY_BATCH  # an RS / AR item is a whole tile
         while True:
             first = self._claim(me, "copy", items, size)
             yield lambda: True
@@ -177,6 +176,9 @@ class Simulation:
                 for dest, rb in pushed:
                     self.ranks[dest].ag_cnt[r][rb] += 1
             for it in batch:
+                if self.op != "ag":
+                    yield from self._rs_item(r, e, ar_e, it, n_rsp, n_own)
+                    continue
                 if it < n_push:
                     continue
                 if it < n_push + n_xg:
@@ -187,13 +189,41 @@ class Simulation:
                         yield lambda c=c, rb=rb: me.ag_cnt[c][rb] >= self.slices * e
                         self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} (xg) on {r}")
                     xg[(c, rb)] = xg.get((c, rb), 0) + 1
-                else:
-                    i3 = it - n_push - n_xg
-                    c = (r + 1 + i3 // self.per_chunk) % self.tp
-                    lt = i3 % self.per_chunk
-                    gtile = (c * self.blocks + lt // self.tiles_n) * self.tiles_n + lt % self.tiles_n
-                    yield lambda g=gtile: me.ar_cnt[g] >= 4 * ar_e
-                    self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
+
+    def _rs_item(self, r, e, ar_e, it, n_rsp, n_own):
+        """One RS / AR copy item: push a peer-chunk partial tile to its owner, push an own
+        reduced tile to every peer (AR), or take another owner's reduced tile (AR)."""
+        me = self.ranks[r]
+        par = e % 2
+        if it < n_rsp + n_own:
+            c, m0, tn = fused_tile(it, self.blocks, self.tiles_n, r, self.tp, 1, self.rows)
+            rb = (m0 - c * self.rows) // FBM
+        else:
+            i3 = it - n_rsp - n_own
+            c = (r + 1 + i3 // self.per_chunk) % self.tp
+            rb, tn = divmod(i3 % self.per_chunk, self.tiles_n)
+        local = rb * self.tiles_n + tn
+        gtile = (c * self.blocks + rb) * self.tiles_n + tn
+        if it < n_rsp:
+            yield lambda: me.send_cnt[gtile] >= 4 * e
+            self._read(me.send.get(gtile), e, f"send buffer tile {gtile} on {r}")
+            self.ranks[c].recv[par][(r, local)] = e                 # the partial into the owner
+            yield lambda: True
+            self.ranks[c].rs_cnt[par][local] += 1
+        elif it < n_rsp + n_own:
+            if c != r:
+                raise ProtocolError(f"own push item {it} on rank {r} maps to chunk {c}")
+            yield lambda: me.own_cnt[local] >= 4 * ar_e
+            for p in range(self.tp):
+                if p != r:
+                    self.ranks[p].out[ar_e % 2][gtile] = ar_e
+            yield lambda: True
+            for p in range(self.tp):
+                if p != r:
+                    self.ranks[p].ar_cnt[gtile] += 1
+        else:
+            yield lambda: me.ar_cnt[gtile] >= ar_e
+            self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
 
     # --- the scheduler -------------------------------------------------------------------
 

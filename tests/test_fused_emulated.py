@@ -94,9 +94,9 @@ def test_emulated_gemm_rs_ar(tp, all_reduce):
             recv = em.buf(owner, em.recv_off, parity, (tp, em.rpr * N)).view(tp, em.rpr, N)
             assert torch.equal(recv[0], mine[owner * em.rpr:(owner + 1) * em.rpr])
             bank = em.u32(owner, fused._RS_CNT, 2 * fused.MAX_TILES).view(2, fused.MAX_TILES)[call % 2]
-            assert torch.equal(bank[:per_chunk].cpu(), torch.full((per_chunk,), 4, dtype=torch.int32))
+            assert torch.equal(bank[:per_chunk].cpu(), torch.full((per_chunk,), 1, dtype=torch.int32))
             if all_reduce:
                 out = em.buf(owner, em.out_off, parity, (T, N))
                 assert torch.equal(out[:em.rpr], y[:em.rpr])  # rank 0's reduced rows pushed to every peer
                 arc = em.u32(owner, fused._AR_CNT, fused.MAX_TILES)
-                assert torch.equal(arc[:per_chunk].cpu(), torch.full((per_chunk,), 4 * call, dtype=torch.int32))
+                assert torch.equal(arc[:per_chunk].cpu(), torch.full((per_chunk,), call, dtype=torch.int32))

@@ -221,7 +221,7 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
             return 100 + grid
 
         def fused_copy_claims(self, mode, t, n, tp, slices, xg, grid):
-            return {1: 50 if xg else 20, 2: 0, 3: 30}[mode] + (grid if mode != 2 else 0)
+            return {1: 50 if xg else 20, 2: 15, 3: 30}[mode] + grid
 
         def ag_gemm(self, x_local, xg, w, w_mn, y, peers, grid):
             self.ag.append((xg, peers, grid))
@@ -265,10 +265,11 @@ def test_symmetric_workspace_counter_bases_follow_the_kernel(monkeypatch):
     ws.gemm_all_reduce(h, torch.zeros(64, 16, dtype=torch.bfloat16), False, 64)
     shape, ar, peers = stub.rs[-1]
     assert tuple(shape) == (512, 64) and ar and peers[4] == 2 and peers[5] == 1
-    assert peers[7] == 107 and peers[9] == 0                                  # after one RS: tile claims only
+    assert peers[7] == 107 and peers[9] == 22                                 # after one RS
     assert peers[10 + 4 * tp:10 + 5 * tp] == [b + ws.out_off + ws.stride for b in peers_of]
     assert peers[10 + 5 * tp:10 + 6 * tp] == [b + fused._AR_CNT for b in peers_of]
-    assert ws.bases == [107 * 4, 57 * 3 + 27, 107 * 2, 37]
+    assert peers[10 + 6 * tp:] == [ws.base + ws.send_off, ws.base + fused._SEND_CNT, ws.base + fused._OWN_CNT]
+    assert ws.bases == [107 * 4, 57 * 3 + 27, 107 * 2, 22 + 37]
 
 
 def test_control_plane_run_constants_must_match_the_config():
