@@ -265,6 +265,102 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- CTA pairs (tcgen05 cta_group::2) ----------------------------------------------
+// Two CTAs of a 2-CTA cluster share one MMA: the even CTA (the leader) issues
+// tcgen05.mma.cta_group::2, which reads the A and B halves from both CTAs' shared memory
+// at the same offsets and writes each CTA's half of the accumulator into its own TMEM.
+// All tcgen05 allocation / MMA / commit instructions of such a kernel use cta_group::2.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs: release this CTA's prior writes, acquire the peer's.
+// (Per-thread form: callable where a warp's lanes arrive at different times.)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// shared::cluster address of this CTA's shared-memory object ``p`` as seen in CTA ``rank``.
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// mbar_wait with acquire at cluster scope, for a barrier that CTAs of the cluster arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+  const uint32_t b = smem_u32(bar);
+  const uint64_t start = globaltimer();
+  #pragma unroll 1
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(b), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (globaltimer() - start > kWaitBudgetNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted on an
+// mbarrier of either CTA of the pair (``bar_cluster``: a shared::cluster address).
+// No multicast: each CTA loads its own half.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
+                                                 int* err = nullptr) {
+  if (!bounds_ok((x & 7) == 0 && x >= 0 && y >= 0 && (smem_u32(dst) & 1023u) == 0, err)) return;
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Called by the same warp of both CTAs: ``ncols`` TMEM columns in each, at one address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Leader only: D[tmem of both CTAs] (+)= A * B^T over the pair (M = 256 split by CTA,
+// N split by CTA for the operand, whole N in each CTA's accumulator).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Leader only: arrive once on the mbarrier at ``bar_cluster`` (either CTA) when every
+// pair MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -290,16 +386,28 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Wait until *p >= target (wrap-safe); false + error code when ``budget_ns`` runs out.
+// The counter is polled with relaxed loads (a short sleep between polls once the first
+// few miss, so a waiting thread does not crowd the memory system its SM's other warps
+// use) and the acquire is one fence after the condition holds.
 __device__ __forceinline__ bool wait_geq(const unsigned* p, unsigned target, int* err, int code, uint64_t budget_ns) {
+  if (static_cast<int>(ld_acquire_sys(p) - target) >= 0) return true;
   const uint64_t start = globaltimer();
   #pragma unroll 1
-  while (static_cast<int>(ld_acquire_sys(p) - target) < 0) {
+  for (int i = 0; static_cast<int>(ld_relaxed_sys(p) - target) < 0; ++i) {
+    if (i >= 8) __nanosleep(128);
     if (globaltimer() - start > budget_ns) {
       record_error(err, code);
       return false;
     }
   }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   return true;
 }
 

@@ -10,6 +10,7 @@
 // rows share a block so that a block has >= 256 threads. The weight gradient is
 // reduced deterministically: every block of a fixed-size persistent grid writes one
 // fp32 partial row, and a second kernel sums the partials in block order.
+#include <algorithm>
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -166,6 +167,172 @@ __global__ void column_sum_kernel(const float* __restrict__ partial, int parts, 
   dw[c] = accumulate ? dw[c] + acc : acc;
 }
 
+// ---- warp-per-row variants for d = 256 * VPL (VPL = 1, 2, 4, 8) ------------------------
+// A warp owns a whole row: lane l holds the 16-byte vectors at columns (32 j + l) * 8,
+// j < VPL (each j one coalesced 512-byte warp access), the row statistics are warp
+// shuffles (no block barrier per row), and every lane has 2 VPL loads in flight. The
+// weight-gradient partials of a block's eight warps are added in warp order in shared
+// memory, one fp32 partial row per block.
+
+__device__ __forceinline__ float warp_sum(float v) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kNormWarps = 8;
+
+
+template <int VPL>
+__global__ void __launch_bounds__(32 * kNormWarps)
+    rmsnorm_fwd_warp_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
+                            const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                            __nv_bfloat16* __restrict__ s_out, float* __restrict__ rstd_out, int rows, float eps) {
+  constexpr int D = 256 * VPL;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kNormWarps) {
+    const int64_t base = int64_t(row) * D;
+    Vec8 sv[VPL];
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j) sv[j] = load8(x + base + (32 * j + lane) * 8);
+    if (r != nullptr) {
+      #pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const Vec8 rv = load8(r + base + (32 * j + lane) * 8);
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) sv[j].v[i] = __bfloat162float(__float2bfloat16(sv[j].v[i] + rv.v[i]));
+        store8(s_out + base + (32 * j + lane) * 8, sv[j]);
+      }
+    }
+    float sq = 0.f;
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) sq += sv[j].v[i] * sv[j].v[i];
+    const float rstd = rsqrtf(warp_sum(sq) / float(D) + eps);
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const Vec8 wv = load8(w + (32 * j + lane) * 8);
+      Vec8 o;
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) o.v[i] = sv[j].v[i] * rstd * wv.v[i];
+      store8(y + base + (32 * j + lane) * 8, o);
+    }
+    if (lane == 0) rstd_out[row] = rstd;
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(32 * kNormWarps)
+    rmsnorm_bwd_warp_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ s,
+                            const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                            const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ ds,
+                            float* __restrict__ dw_partial, int rows) {
+  constexpr int D = 256 * VPL;
+  extern __shared__ float4 dw_smem4[];  // [kNormWarps][D / 4]: each warp's running dw row
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4* mine = dw_smem4 + warp * (D / 4);
+  #pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    mine[(32 * j + lane) * 2] = make_float4(0.f, 0.f, 0.f, 0.f);
+    mine[(32 * j + lane) * 2 + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  uint4 wr[VPL];  // this lane's weights, packed, for every row
+  #pragma unroll
+  for (int j = 0; j < VPL; ++j) wr[j] = *reinterpret_cast<const uint4*>(w + (32 * j + lane) * 8);
+  for (int row = blockIdx.x * kNormWarps + warp; row < rows; row += gridDim.x * kNormWarps) {
+    const int64_t base = int64_t(row) * D;
+    const float rs = rstd[row];
+    // every load of the row in flight at once, kept packed (bf16) through the reduction
+    uint4 dyr[VPL], sr[VPL], rr[VPL];
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      dyr[j] = *reinterpret_cast<const uint4*>(dy + base + (32 * j + lane) * 8);
+      sr[j] = *reinterpret_cast<const uint4*>(s + base + (32 * j + lane) * 8);
+      if (dres != nullptr) rr[j] = *reinterpret_cast<const uint4*>(dres + base + (32 * j + lane) * 8);
+    }
+    float dot = 0.f;
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      asm volatile("" : "+r"(wr[j].x), "+r"(wr[j].y), "+r"(wr[j].z), "+r"(wr[j].w));
+      const Vec8 dyv = load8(reinterpret_cast<const __nv_bfloat16*>(&dyr[j]));
+      const Vec8 svv = load8(reinterpret_cast<const __nv_bfloat16*>(&sr[j]));
+      const Vec8 wv = load8(reinterpret_cast<const __nv_bfloat16*>(&wr[j]));
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) dot += dyv.v[i] * wv.v[i] * (svv.v[i] * rs);
+    }
+    const float mean = warp_sum(dot) / float(D);
+    #pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      // unpack again rather than keep the unpacked floats of the first loop alive
+      // (register pressure): the empty asm hides that the values are unchanged
+      asm volatile("" : "+r"(dyr[j].x), "+r"(dyr[j].y), "+r"(dyr[j].z), "+r"(dyr[j].w));
+      asm volatile("" : "+r"(sr[j].x), "+r"(sr[j].y), "+r"(sr[j].z), "+r"(sr[j].w));
+      asm volatile("" : "+r"(wr[j].x), "+r"(wr[j].y), "+r"(wr[j].z), "+r"(wr[j].w));
+      const Vec8 dyv = load8(reinterpret_cast<const __nv_bfloat16*>(&dyr[j]));
+      const Vec8 svv = load8(reinterpret_cast<const __nv_bfloat16*>(&sr[j]));
+      const Vec8 wv = load8(reinterpret_cast<const __nv_bfloat16*>(&wr[j]));
+      Vec8 o;
+      float sh[8];
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sh[i] = svv.v[i] * rs;
+        o.v[i] = rs * (dyv.v[i] * wv.v[i] - sh[i] * mean);
+      }
+      if (dres != nullptr) {
+        const Vec8 rv = load8(reinterpret_cast<const __nv_bfloat16*>(&rr[j]));
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) o.v[i] += rv.v[i];
+      }
+      store8(ds + base + (32 * j + lane) * 8, o);
+      float4 a = mine[(32 * j + lane) * 2], b = mine[(32 * j + lane) * 2 + 1];
+      a.x += dyv.v[0] * sh[0]; a.y += dyv.v[1] * sh[1]; a.z += dyv.v[2] * sh[2]; a.w += dyv.v[3] * sh[3];
+      b.x += dyv.v[4] * sh[4]; b.y += dyv.v[5] * sh[5]; b.z += dyv.v[6] * sh[6]; b.w += dyv.v[7] * sh[7];
+      mine[(32 * j + lane) * 2] = a;
+      mine[(32 * j + lane) * 2 + 1] = b;
+    }
+  }
+  __syncthreads();
+  const float* dw_smem = reinterpret_cast<const float*>(dw_smem4);
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    #pragma unroll
+    for (int q = 0; q < kNormWarps; ++q) acc += dw_smem[q * D + c];
+    dw_partial[int64_t(blockIdx.x) * D + c] = acc;
+  }
+}
+
+// dw[c] (+)= sum over partial rows of partial[p, c] in a fixed order: block (32 columns
+// x 8 groups); group g sums rows g, g+8, g+16, ... in turn, then the 8 group sums are
+// added in group order. Used with the warp-per-row backward (fewer, wider blocks than
+// column_sum_kernel's one thread per column would keep busy).
+__global__ void column_sum_wide_kernel(const float* __restrict__ partial, int parts, int d, float* __restrict__ dw,
+                                       int accumulate) {
+  __shared__ float sums[8][33];
+  const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cl;
+  float acc = 0.f;
+  if (c < d)
+    for (int p = grp; p < parts; p += 8) acc += partial[int64_t(p) * d + c];
+  sums[grp][cl] = acc;
+  __syncthreads();
+  if (grp == 0 && c < d) {
+    float tot = 0.f;
+    #pragma unroll
+    for (int q = 0; q < 8; ++q) tot += sums[q][cl];
+    dw[c] = accumulate ? dw[c] + tot : tot;
+  }
+}
+
+// VPL of the warp-per-row kernels for width d, or 0 for the general kernels.
+int norm_vpl(int d) {
+  return (d == 256 || d == 512 || d == 1024 || d == 2048) ? d / 256 : 0;
+}
+
+int warp_norm_grid(int rows, int num_sms) {
+  return std::max(1, std::min((rows + kNormWarps - 1) / kNormWarps, num_sms));
+}
+
 int norm_block(int d) {
   const int lanes = d / 8;
   int rows = lanes >= 256 ? 1 : 256 / lanes;
@@ -175,10 +342,59 @@ int norm_block(int d) {
 }  // namespace
 
 int rmsnorm_partial_rows(int rows, int d, int num_sms) {
+  if (norm_vpl(d) != 0) return warp_norm_grid(rows, num_sms);
   const int block = norm_block(d);
   const int rows_per_block = block / (d / 8);
   int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * num_sms);
   return grid * rows_per_block;
+}
+
+namespace {
+
+template <int VPL>
+void launch_bwd_warp(const void* dy, const void* s, const void* w, const float* rstd, const void* dres, void* ds,
+                     float* partial, int rows, int grid, cudaStream_t st) {
+  constexpr int smem = kNormWarps * 256 * VPL * int(sizeof(float));
+  auto kernel = rmsnorm_bwd_warp_kernel<VPL>;
+  if (smem > 48 * 1024) (void)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  kernel<<<grid, 32 * kNormWarps, smem, st>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
+      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
+      static_cast<__nv_bfloat16*>(ds), partial, rows);
+}
+
+}  // namespace
+
+// The backward's two launches into a caller-provided ``partial`` buffer of
+// rmsnorm_partial_rows(rows, d, num_sms) x d floats (shared by both entry points).
+cudaError_t rmsnorm_bwd_launch(const void* dy, const void* s, const void* w, const float* rstd, const void* dres,
+                               void* ds, float* partial, float* dw, int accumulate, int rows, int d, int num_sms,
+                               cudaStream_t st) {
+  const int vpl = norm_vpl(d);
+  if (vpl != 0) {
+    const int grid = warp_norm_grid(rows, num_sms);
+    switch (vpl) {
+      case 1: launch_bwd_warp<1>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;
+      case 2: launch_bwd_warp<2>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;
+      case 4: launch_bwd_warp<4>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;
+      default: launch_bwd_warp<8>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    column_sum_wide_kernel<<<(d + 31) / 32, 256, 0, st>>>(partial, grid, d, dw, accumulate);
+    return cudaGetLastError();
+  }
+  const int block = norm_block(d);
+  const int rows_per_block = block / (d / 8);
+  const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * num_sms);
+  rmsnorm_bwd_kernel<<<grid, block, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
+      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
+      static_cast<__nv_bfloat16*>(ds), partial, rows, d);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  column_sum_kernel<<<(d + 255) / 256, 256, 0, st>>>(partial, grid * rows_per_block, d, dw, accumulate);
+  return cudaGetLastError();
 }
 
 static void check_d(int d) {
@@ -189,6 +405,23 @@ static void check_d(int d) {
 void rmsnorm_fwd(const void* x, const void* r, const void* w, void* y, void* s_out, float* rstd, int rows, int d,
                  float eps, int num_sms, cudaStream_t st) {
   check_d(d);
+  const int vpl = norm_vpl(d);
+  if (vpl != 0) {
+    const int grid = std::max(1, std::min((rows + kNormWarps - 1) / kNormWarps, 8 * num_sms));
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    const auto* rb = static_cast<const __nv_bfloat16*>(r);
+    const auto* wb = static_cast<const __nv_bfloat16*>(w);
+    auto* yb = static_cast<__nv_bfloat16*>(y);
+    auto* sb = static_cast<__nv_bfloat16*>(s_out);
+    switch (vpl) {
+      case 1: rmsnorm_fwd_warp_kernel<1><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      case 2: rmsnorm_fwd_warp_kernel<2><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      case 4: rmsnorm_fwd_warp_kernel<4><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      default: rmsnorm_fwd_warp_kernel<8><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
+    }
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int block = norm_block(d);
   const int rows_per_block = block / (d / 8);
   const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 8 * num_sms);
@@ -202,16 +435,7 @@ void rmsnorm_fwd(const void* x, const void* r, const void* w, void* y, void* s_o
 void rmsnorm_bwd(const void* dy, const void* s, const void* w, const float* rstd, const void* dres, void* ds,
                  float* partial, float* dw, int accumulate, int rows, int d, int num_sms, cudaStream_t st) {
   check_d(d);
-  const int block = norm_block(d);
-  const int rows_per_block = block / (d / 8);
-  const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * num_sms);
-  rmsnorm_bwd_kernel<<<grid, block, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
-      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
-      static_cast<__nv_bfloat16*>(ds), partial, rows, d);
-  RESIHP_CUDA_CHECK(cudaGetLastError());
-  column_sum_kernel<<<(d + 255) / 256, 256, 0, st>>>(partial, grid * rows_per_block, d, dw, accumulate);
-  RESIHP_CUDA_CHECK(cudaGetLastError());
+  RESIHP_CUDA_CHECK(rmsnorm_bwd_launch(dy, s, w, rstd, dres, ds, partial, dw, accumulate, rows, d, num_sms, st));
 }
 
 }  // namespace resihp
@@ -276,21 +500,13 @@ extern "C" __attribute__((visibility("default"))) int resihp_rmsnorm_bwd_noalloc
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
-  // Same launch shape as the allocating entry point (rmsnorm_bwd), so results agree.
-  const int block = norm_block(d);
-  const int rows_per_block = block / (d / 8);
-  const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * sms);
-  const long long need = static_cast<long long>(grid) * rows_per_block * d;
+  // The same launches as the allocating entry point (rmsnorm_bwd), so results agree.
+  const long long need = static_cast<long long>(rmsnorm_partial_rows(rows, d, sms)) * d;
   if (need > RESIHP_NOALLOC_SCRATCH_FLOATS) return RESIHP_NOALLOC_TOO_LARGE;
   float* partial = nullptr;
   if (noalloc_scratch(&partial) != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
-  rmsnorm_bwd_kernel<<<grid, block, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
-      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
-      static_cast<__nv_bfloat16*>(ds), partial, rows, d);
-  if (cudaGetLastError() != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
-  column_sum_kernel<<<(d + 255) / 256, 256, 0, stream>>>(partial, grid * rows_per_block, d, dw, accumulate);
-  if (cudaGetLastError() != cudaSuccess) return RESIHP_NOALLOC_CUDA_ERROR;
+  if (rmsnorm_bwd_launch(dy, s, w, rstd, dres, ds, partial, dw, accumulate, rows, d, sms, stream) != cudaSuccess)
+    return RESIHP_NOALLOC_CUDA_ERROR;
   return RESIHP_NOALLOC_OK;
 }
 

@@ -42,6 +42,40 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __res
   }
 }
 
+// Vector form (hd % 16 == 0, 16-byte aligned rows): one thread rotates eight pairs
+// (p..p+7, p+hd/2..p+hd/2+7) with two 16-byte loads and stores; a block walks rows
+// (grid-stride) and its threads the rows' Q/K head vectors, so no 64-bit division per
+// element.
+__global__ void rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs, int rows, int seq,
+                                int heads_qk, int hd, int64_t row_stride, int pos_offset, float sign) {
+  const int half = hd / 2, vph = half / 8;
+  const int per_row = heads_qk * vph;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int pos = (row + pos_offset) % seq;
+    const float4* c4 = reinterpret_cast<const float4*>(cs + int64_t(pos) * half);
+    __nv_bfloat16* rb = qkv + int64_t(row) * row_stride;
+    for (int j = threadIdx.x; j < per_row; j += blockDim.x) {
+      const int h = j / vph, v = j - h * vph;
+      __nv_bfloat16* b = rb + h * hd + v * 8;
+      const uint4 r1 = *reinterpret_cast<const uint4*>(b);
+      const uint4 r2 = *reinterpret_cast<const uint4*>(b + half);
+      const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&r1);
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&r2);
+      uint32_t o1[4], o2[4];
+      #pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 c = c4[v * 4 + q];  // (cos, sin) of pairs 2q, 2q+1
+        const float2 a = __bfloat1622float2(x1[q]), bb = __bfloat1622float2(x2[q]);
+        const float s0 = sign * c.y, s1 = sign * c.w;
+        o1[q] = pack_bf16(a.x * c.x - bb.x * s0, a.y * c.z - bb.y * s1);
+        o2[q] = pack_bf16(bb.x * c.x + a.x * s0, bb.y * c.z + a.y * s1);
+      }
+      *reinterpret_cast<uint4*>(b) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+      *reinterpret_cast<uint4*>(b + half) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+    }
+  }
+}
+
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + __expf(-x)); }
 
 // gu: [rows, 2F] = [g | u];  h: [rows, F]
@@ -80,6 +114,55 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __
     }
     *reinterpret_cast<uint32_t*>(dgu + row * 2 * f + col) = pack_bf16(dg[0], dg[1]);
     *reinterpret_cast<uint32_t*>(dgu + row * 2 * f + f + col) = pack_bf16(du[0], du[1]);
+  }
+}
+
+// Vector forms (f % 8 == 0): one thread per 8 columns of a row, 16-byte accesses, and
+// the row / column split is one 32-bit division per 8 elements.
+__global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int rows,
+                                      int f) {
+  const unsigned vpr = unsigned(f) / 8u;
+  const unsigned total = unsigned(rows) * vpr;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned row = i / vpr, col = (i - row * vpr) * 8u;
+    const __nv_bfloat16* g = gu + int64_t(row) * 2 * f + col;
+    const uint4 gr = *reinterpret_cast<const uint4*>(g);
+    const uint4 ur = *reinterpret_cast<const uint4*>(g + f);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gr);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&ur);
+    uint32_t o[4];
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 gf = __bfloat1622float2(g2[q]), uf = __bfloat1622float2(u2[q]);
+      o[q] = pack_bf16(gf.x * sigmoid(gf.x) * uf.x, gf.y * sigmoid(gf.y) * uf.y);
+    }
+    *reinterpret_cast<uint4*>(h + int64_t(row) * f + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void swiglu_bwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
+                                      __nv_bfloat16* __restrict__ dgu, int rows, int f) {
+  const unsigned vpr = unsigned(f) / 8u;
+  const unsigned total = unsigned(rows) * vpr;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned row = i / vpr, col = (i - row * vpr) * 8u;
+    const int64_t gbase = int64_t(row) * 2 * f + col;
+    const uint4 gr = *reinterpret_cast<const uint4*>(gu + gbase);
+    const uint4 ur = *reinterpret_cast<const uint4*>(gu + gbase + f);
+    const uint4 dr = *reinterpret_cast<const uint4*>(dh + int64_t(row) * f + col);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gr);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&ur);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dr);
+    uint32_t og[4], ou[4];
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 gf = __bfloat1622float2(g2[q]), uf = __bfloat1622float2(u2[q]), df = __bfloat1622float2(d2[q]);
+      const float sx = sigmoid(gf.x), sy = sigmoid(gf.y);
+      og[q] = pack_bf16(df.x * uf.x * sx * (1.f + gf.x * (1.f - sx)), df.y * uf.y * sy * (1.f + gf.y * (1.f - sy)));
+      ou[q] = pack_bf16(df.x * gf.x * sx, df.y * gf.y * sy);
+    }
+    *reinterpret_cast<uint4*>(dgu + gbase) = make_uint4(og[0], og[1], og[2], og[3]);
+    *reinterpret_cast<uint4*>(dgu + gbase + f) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
   }
 }
 
@@ -183,6 +266,16 @@ int grid_for(int64_t work, int block, int num_sms) {
 void rope(void* qkv, const float* cs, int rows, int seq, int heads_qk, int hd, int64_t row_stride, int pos_offset,
           bool inverse, int num_sms, cudaStream_t st) {
   RESIHP_CHECK(hd % 2 == 0, "rope head_dim must be even");
+  if (hd % 16 == 0 && row_stride % 8 == 0 && reinterpret_cast<uintptr_t>(qkv) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(cs) % 16 == 0 && pos_offset >= 0) {
+    const int per_row = heads_qk * (hd / 16);
+    const int block = per_row >= 256 ? 256 : ((per_row + 31) / 32) * 32;
+    const int grid = std::max(1, std::min(rows, num_sms * (2048 / block)));
+    rope_vec_kernel<<<grid, block, 0, st>>>(static_cast<__nv_bfloat16*>(qkv), reinterpret_cast<const float2*>(cs),
+                                            rows, seq, heads_qk, hd, row_stride, pos_offset, inverse ? -1.f : 1.f);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int64_t work = int64_t(rows) * heads_qk * (hd / 2);
   rope_kernel<<<grid_for(work, 256, num_sms), 256, 0, st>>>(static_cast<__nv_bfloat16*>(qkv),
                                                              reinterpret_cast<const float2*>(cs), rows, seq, heads_qk,
@@ -192,6 +285,13 @@ void rope(void* qkv, const float* cs, int rows, int seq, int heads_qk, int hd, i
 
 void swiglu_fwd(const void* gu, void* h, int rows, int f, int num_sms, cudaStream_t st) {
   RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
+  if (f % 8 == 0 && int64_t(rows) * (f / 8) < (int64_t(1) << 31) &&
+      (reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(h)) % 16 == 0) {
+    swiglu_fwd_vec_kernel<<<grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(h), rows, f);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   swiglu_fwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(h), rows, f);
   RESIHP_CUDA_CHECK(cudaGetLastError());
@@ -199,6 +299,14 @@ void swiglu_fwd(const void* gu, void* h, int rows, int f, int num_sms, cudaStrea
 
 void swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, int num_sms, cudaStream_t st) {
   RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
+  if (f % 8 == 0 && int64_t(rows) * (f / 8) < (int64_t(1) << 31) &&
+      (reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dh) | reinterpret_cast<uintptr_t>(dgu)) % 16 == 0) {
+    swiglu_bwd_vec_kernel<<<grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
+        rows, f);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   swiglu_bwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
       rows, f);

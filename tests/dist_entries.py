@@ -117,6 +117,10 @@ def failstop_entry(rank, env, config_dict, failures, out_dir, gpu=False):
                     entry["a1_completed"] = completed
                     entry["a1_mismatches"] = ([] if cp.training_run is None else
                                               checkpoint_mismatches(cp.training_run, plan=plan, rank=rank, anchor=anchor))
+                if gpu and cp.training_run is not None:
+                    red = cp.training_run.runtime.reducer
+                    entry["reduction"] = ("none" if red is None else "p2p-hetero" if red.hetero is not None
+                                          else "fused-dp" if red.fused_dp is not None else "nccl")
                 record["plans"].append(plan.digest)
                 record["recoveries"].append(entry)
                 it = cp.resume_cursor

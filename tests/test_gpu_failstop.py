@@ -57,16 +57,21 @@ GPU_CONFIG = dict(
 )
 
 
-def test_failstop_resumes_bitwise_like_a_rerun_on_four_gpus(tmp_path, monkeypatch):
+@pytest.mark.parametrize("hetero", ["nccl", "p2p"])
+def test_failstop_resumes_bitwise_like_a_rerun_on_four_gpus(tmp_path, monkeypatch, hetero):
     """TP2 x DP2 with sequence parallelism on four GPUs: the fused TP kernels (AG->GEMM,
     GEMM->RS over peer memory) and the fused DP all-reduce + AdamW run every step. Rank 3
     is SIGKILLed after step 3 (between steps, its GPU idle); the survivors replan onto
     three GPUs (replica 0 keeps TP2, replica 1 continues at TP1), move the lost state and
     resume. Checked: every survivor's installed state equals the checkpoint it resumed
     from, bit for bit (principle A1), and the losses of steps 4-7 equal, bit for bit, an
-    uninterrupted run of the new plan started from that checkpoint on three GPUs."""
+    uninterrupted run of the new plan started from that checkpoint on three GPUs. The
+    replicas' gradients after the failure meet through the logical reduction: bucketed
+    NCCL all-reduces (``nccl``) or the peer-memory gather and ordered sum (``p2p``,
+    ``RESIHP_P2P_HETERO=1``), in both the failing run and the re-run."""
     if torch.cuda.device_count() < 4:
         pytest.skip("needs four GPUs")
+    monkeypatch.setenv("RESIHP_P2P_HETERO", "1" if hetero == "p2p" else "0")
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     import dist_entries
     from harness import assert_killed, read_results, run_ranks
@@ -86,6 +91,8 @@ def test_failstop_resumes_bitwise_like_a_rerun_on_four_gpus(tmp_path, monkeypatc
         (event,) = r["recoveries"]
         assert event["resumed_from"] == kill_after and event["a1_completed"] == kill_after
         assert event["a1_mismatches"] == [], (r["rank"], event["a1_mismatches"])
+        if hetero == "p2p":  # the replicas now differ in layout: the peer-memory gather ran
+            assert event["reduction"] == "p2p-hetero", (r["rank"], event["reduction"])
     after = {rank: {int(k): v for k, v in r["losses"].items() if int(k) > kill_after} for rank, r in survivors.items()}
     for rank, losses in after.items():  # every survivor reports its replica's loss of every resumed step
         assert sorted(losses) == list(range(kill_after + 1, GPU_CONFIG["iterations"] + 1)), (rank, losses)

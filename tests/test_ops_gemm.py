@@ -56,3 +56,38 @@ def test_residual_epilogue_and_both_tiles():
     _ext.require().gemm(x, False, w, False, out, 0, 1.0, None, 3, 128)
     assert _rel(out, x.float() @ w.float().t()) < 1e-2
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (300, 520, 136), (1024, 2048, 512), (4096, 2048, 5504)])
+def test_cta_pair_tiles(m, n, k):
+    """The 256 x 256 CTA-pair kernel (force_bn=512) against FP32 torch, for the forward,
+    dgrad and wgrad operand layouts and every epilogue the linear layers use, next to the
+    single-CTA kernel (force_bn=256); a one-pair grid pushes many tiles through both
+    TMEM accumulators."""
+    torch.manual_seed(2)
+    lib = _ext.require()
+    x = torch.randn(m, k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") / k**0.5).bfloat16()
+    dy = torch.randn(m, n, device="cuda").bfloat16()
+    r = torch.randn(m, n, device="cuda").bfloat16()
+    fwd = x.float() @ w.float().t()
+    cases = [
+        # (A, a_mn, B, b_mn, epilogue, out dtype, out shape, residual, reference)
+        (x, False, w, False, 0, torch.bfloat16, (m, n), None, fwd),
+        (x, False, w, False, 3, torch.bfloat16, (m, n), r, fwd + r.float()),
+        (dy, False, w, True, 0, torch.bfloat16, (m, k), None, dy.float() @ w.float()),
+        (dy, False, w, True, 1, torch.float32, (m, k), None, dy.float() @ w.float()),
+        (dy, True, x, True, 1, torch.float32, (n, k), None, dy.float().t() @ x.float()),
+    ]
+    for a, a_mn, b, b_mn, epi, dtype, shape, res, ref in cases:
+        for bn, max_ctas in ((256, 0), (512, 0), (512, 2)):
+            out = torch.empty(shape, device="cuda", dtype=dtype)
+            lib.gemm(a, a_mn, b, b_mn, out, epi, 1.0, res, max_ctas, bn)
+            assert _rel(out, ref) < 1e-2, (epi, bn, max_ctas)
+    # accumulating wgrad epilogues (load-add-store and red.global.add)
+    ref_dw = dy.float().t() @ x.float()
+    for epi in (2, 4):
+        acc = torch.ones(n, k, device="cuda")
+        lib.gemm(dy, True, x, True, acc, epi, 1.0, None, 0, 512)
+        assert _rel(acc, ref_dw + 1) < 1e-3
+    ops.check_device_errors()

@@ -14,7 +14,7 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-@pytest.mark.parametrize("d", [256, 2048, 5120])
+@pytest.mark.parametrize("d", [128, 256, 1024, 2048, 5120])
 @pytest.mark.parametrize("with_residual", [False, True])
 def test_rmsnorm(d, with_residual):
     torch.manual_seed(0)
@@ -43,9 +43,10 @@ def test_rmsnorm(d, with_residual):
     assert _rel(mg, wf.grad) < 1e-2
 
 
-def test_swiglu():
+@pytest.mark.parametrize("f", [704, 6])  # 16-byte vector kernels; scalar kernels (f % 8 != 0)
+def test_swiglu(f):
     torch.manual_seed(0)
-    gu = torch.randn(300, 2 * 704, device="cuda").bfloat16().requires_grad_()
+    gu = torch.randn(300, 2 * f, device="cuda").bfloat16().requires_grad_()
     h = fn.swiglu(gu)
     gf = gu.detach().float().requires_grad_()
     g, u = gf.chunk(2, -1)
