@@ -4,6 +4,8 @@
         --master-port 29581 bench_fused_tp.py            # 1.3B layer shapes (T=4096, d=2048)
     ... bench_fused_tp.py --sweep                         # BASELINE config-5 sweep
     ... bench_fused_tp.py --config3                       # Llama-3-8B layer shapes
+    ... bench_fused_tp.py --trace DIR                     # also: per-CTA timelines of one
+                                                          # fused call per op (JSON per rank)
 
 The sweep covers M = 4096..32768 tokens with K, N in {5120, 13824}: column-parallel
 AG->GEMM ``[M, 5120] x [5120, N/tp]`` (N = 5120, 13824) and row-parallel GEMM->RS
@@ -13,6 +15,7 @@ package's GEMM. The roofline of a fused op is the slower of its FLOPs at the mea
 bf16 peak and the bytes that must cross NVLink at 770 GB/s per direction.
 
 CUDA-event timing (3 warm-up, 10 launches, max over ranks); rank 0 prints JSON.
+``host_us`` is the host time to issue one fused call (the launch path, no sync).
 """
 
 from __future__ import annotations
@@ -48,6 +51,36 @@ def main():
     sweep = "--sweep" in sys.argv
     config3 = "--config3" in sys.argv
     peak = _peaks()
+    trace_dir = sys.argv[sys.argv.index("--trace") + 1] if "--trace" in sys.argv else None
+    kx = ops._ext.require()
+
+    def host_us(fn, it=20):
+        import time
+
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(it):
+            fn()
+        t1 = time.perf_counter()
+        torch.cuda.synchronize()
+        return (t1 - t0) / it * 1e6
+
+    def trace(name, fn):
+        """One call with the per-CTA stamps on; rank r writes DIR/<name>_rank<r>.json."""
+        if trace_dir is None:
+            return
+        slots = kx.fused_trace_slots()
+        buf = torch.zeros(1024 * slots, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        kx.set_fused_trace(buf.data_ptr())
+        fn()
+        torch.cuda.synchronize()
+        kx.set_fused_trace(0)
+        rows = buf.view(1024, slots).cpu().tolist()
+        os.makedirs(trace_dir, exist_ok=True)
+        with open(os.path.join(trace_dir, f"{name}_rank{rank}.json"), "w") as f:
+            json.dump([r for r in rows if r[0] > 0], f)
 
     def t_ev(fn, it=10, warm=3):
         for _ in range(warm):
@@ -100,7 +133,9 @@ def main():
             row = dict(op="ag_gemm", m=m, k=width, n=n_full, n_per_rank=n, tp=world,
                        fused_us=t_ev(lambda: ws.all_gather_gemm(x, w, False, n)),
                        nccl_cublas_us=t_ev(nccl_cublas), nccl_ours_us=t_ev(nccl_ours),
-                       gemm_only_us=t_ev(lambda: ops.linear(xg_buf, w)))
+                       gemm_only_us=t_ev(lambda: ops.linear(xg_buf, w)),
+                       host_us=host_us(lambda: ws.all_gather_gemm(x, w, False, n)))
+            trace(f"ag_{m}_{n_full}", lambda: ws.all_gather_gemm(x, w, False, n))
             row["roofline_us"] = roofline(2.0 * m * width * n, (world - 1) / world * m * width * 2)
             out.append(row)
         for k_full in rs_ks:
@@ -122,7 +157,9 @@ def main():
             row = dict(op="gemm_rs", m=m, k=k_full, k_per_rank=k, n=width, tp=world,
                        fused_us=t_ev(lambda: ws.gemm_reduce_scatter(h, w, False, width)),
                        nccl_cublas_us=t_ev(nccl_cublas), nccl_ours_us=t_ev(nccl_ours),
-                       gemm_only_us=t_ev(lambda: ops.linear(h, w)))
+                       gemm_only_us=t_ev(lambda: ops.linear(h, w)),
+                       host_us=host_us(lambda: ws.gemm_reduce_scatter(h, w, False, width)))
+            trace(f"rs_{m}_{k_full}", lambda: ws.gemm_reduce_scatter(h, w, False, width))
             row["roofline_us"] = roofline(2.0 * m * k * width, (world - 1) / world * m * width * 2)
             out.append(row)
             if sweep:
@@ -136,7 +173,9 @@ def main():
             # without sequence parallelism: the row-parallel output all-reduce
             row = dict(op="gemm_ar", m=m, k=k_full, k_per_rank=k, n=width, tp=world,
                        fused_us=t_ev(lambda: ws.gemm_all_reduce(h, w, False, width)),
-                       nccl_cublas_us=t_ev(nccl_cublas_ar), gemm_only_us=t_ev(lambda: ops.linear(h, w)))
+                       nccl_cublas_us=t_ev(nccl_cublas_ar), gemm_only_us=t_ev(lambda: ops.linear(h, w)),
+                       host_us=host_us(lambda: ws.gemm_all_reduce(h, w, False, width)))
+            trace(f"ar_{m}_{k_full}", lambda: ws.gemm_all_reduce(h, w, False, width))
             row["roofline_us"] = roofline(2.0 * m * k * width, 2 * (world - 1) / world * m * width * 2)
             out.append(row)
         ws.close()

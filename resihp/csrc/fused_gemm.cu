@@ -27,12 +27,14 @@
 //     in a local send buffer and flags it, and the copy warps push each finished partial
 //     tile, row by row (one warp store per 512-byte row), into the owning peer's receive
 //     buffer and count it there.
-//     Own-chunk tiles run last: their epilogue waits for the tp-1 contributions and sums
-//     every rank's partial in rank order (this rank's own in fp32), deterministically.
+//     Own-chunk tiles run last: their epilogue stores this rank's partial in y, and once
+//     the tp-1 contributions have arrived the copy warps add them (own partial first,
+//     then the peers' in rank order, in fp32, deterministically), many rows in flight.
 //     (The tile counters come in two banks by call parity: a fast source may already be
 //     contributing to the next call.)
-// AR: RS, then the copy warps push each own reduced tile into every peer's output
-//     landing zone and count it, and copy the other owners' tiles from there into y.
+// AR: RS, where the copy warps also store each reduced own row into every peer's output
+//     landing zone and count it there (per row slice), then copy the other owners'
+//     tiles from there into y.
 //
 // Work is claimed dynamically -- output tiles by the producer, copy items by the copy
 // warps -- from per-call counters in the same global order on every rank (peer data
@@ -64,6 +66,13 @@ constexpr int kFusedThreads = 192 + kCopyThreads;
 constexpr int kTileRing = 4;
 constexpr int kCopyUnroll = 8;
 constexpr int kCopyBatch = 8;  // copy items per claim
+// An own tile's reduction is split into this many copy items (row slices): enough items
+// to give every CTA's copy warps one (at least 1, at most 8 slices of 16 rows).
+__host__ __device__ inline int red_slices(int per_chunk, int grid) {
+  int s = 1;
+  while (s < 8 && per_chunk * s < grid) s *= 2;
+  return s;
+}
 
 enum FusedMode : int { kModeAG = 1, kModeRS = 2, kModeAR = 3 };
 
@@ -75,8 +84,19 @@ struct FusedArgs {
   uint64_t wait_ns;  // budget of each wait on a peer's counter
   const __nv_bfloat16* x_local;  // AG: this rank's chunk [T/tp, K], row stride K
   __nv_bfloat16* xg;             // AG: gathered copy [T, K] for the backward (nullptr: none)
+  uint64_t* trace;               // profiling aid: [grid][kTraceSlots] timer stamps, or null
   FusedPeers p;
 };
+
+// Profiling aid (off unless a trace buffer is set with set_fused_trace): every CTA
+// records global-timer stamps at fixed points: 0 start, 1 producer done claiming,
+// 2-9 epilogue end of its first 8 tiles, 10-25 (start, end) of its first 8 copy claims,
+// 26-33 the claimed item of each, 34 end.
+constexpr int kTraceSlots = 40;
+#define FUSED_STAMP(slot, value)                                              \
+  do {                                                                        \
+    if (g.trace != nullptr) g.trace[blockIdx.x * kTraceSlots + (slot)] = (value); \
+  } while (0)
 
 template <int BN>
 struct FusedShape {
@@ -97,6 +117,28 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
+}
+
+// Eight bf16 (a 16-byte vector, low half first) to fp32, exactly, without taking the
+// vector's address (which would keep a register array in local memory).
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  #pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// arr[i] by a select over every slot: a runtime index into a kernel-parameter array
+// would make the compiler copy the array to local memory.
+template <class T>
+__device__ __forceinline__ T pick(const T (&arr)[kFusedMaxTp], int i) {
+  T r = arr[0];
+  #pragma unroll
+  for (int q = 1; q < kFusedMaxTp; ++q)
+    if (q == i) r = arr[q];
+  return r;
 }
 
 // ``count`` contiguous 16-byte vectors, copy-warp thread ``ct`` of kCopyThreads, eight
@@ -142,6 +184,84 @@ __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* 
       if (r < rows) dst[int64_t(r) * dld + lane] = v[u];
     }
   }
+}
+
+// Copy warps: one own output tile (rows lrow0.. of this rank's chunk, global row m0..,
+// columns c0..c0 + 8 ncols16) becomes y = own partial (already in y, bf16) + the peers'
+// bf16 partials in ascending rank order, summed in fp32. One warp per row, one 16-byte
+// vector per lane; 16 / tp rows (all their sources) loaded before the first sum, so the
+// receive-buffer reads overlap. AR: each reduced row is also stored into every peer's
+// output landing zone.
+template <int MODE, int TP>
+__device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers& p, int lrow0, int m0, int c0, int w,
+                                            int lane, int rbeg, int rend) {
+  // TP: the group size, or 0 for any size up to kFusedMaxTp (one row at a time)
+  constexpr int kSrc = TP > 0 ? TP : kFusedMaxTp;
+  constexpr int kRows = TP > 0 && 8 / TP > 0 ? 8 / TP : 1;  // rows whose sources load at once
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(g.c);
+  const __nv_bfloat16* recv = pick(p.recv, p.rank);
+  for (int r0 = rbeg + w * kRows; r0 < rend; r0 += kCopyWarps * kRows) {
+    uint4 v[kRows][kSrc];
+    #pragma unroll
+    for (int rr = 0; rr < kRows; ++rr) {
+      if (r0 + rr >= rend) continue;
+      const int lrow = lrow0 + r0 + rr;
+      const int64_t yrow = MODE == kModeRS ? lrow : int64_t(m0 + r0 + rr);
+      #pragma unroll
+      for (int src = 0; src < kSrc; ++src) {
+        if (TP == 0 && src >= p.tp) continue;
+        const uint4* a = src == p.rank
+                             ? reinterpret_cast<const uint4*>(y + yrow * g.ldc + c0) + lane
+                             : reinterpret_cast<const uint4*>(recv + (int64_t(src) * p.rows_per_rank + lrow) * g.n +
+                                                              c0) +
+                                   lane;
+        v[rr][src] = ld_cg_v4(a);
+      }
+    }
+    #pragma unroll
+    for (int rr = 0; rr < kRows; ++rr) {
+      if (r0 + rr >= rend) continue;
+      // the own partial first, then the peers' in ascending rank order
+      uint4 own = v[rr][0];
+      #pragma unroll
+      for (int q = 1; q < kSrc; ++q)
+        if (q == p.rank) own = v[rr][q];
+      float tot[8];
+      bf16x8_to_f32(own, tot);
+      #pragma unroll
+      for (int src = 0; src < kSrc; ++src) {
+        if (src == p.rank || (TP == 0 && src >= p.tp)) continue;
+        float x[8];
+        bf16x8_to_f32(v[rr][src], x);
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) tot[e] += x[e];
+      }
+      uint4 o;
+      o.x = pack_bf16(tot[0], tot[1]);
+      o.y = pack_bf16(tot[2], tot[3]);
+      o.z = pack_bf16(tot[4], tot[5]);
+      o.w = pack_bf16(tot[6], tot[7]);
+      const int lrow = lrow0 + r0 + rr;
+      const int64_t yrow = MODE == kModeRS ? lrow : int64_t(m0 + r0 + rr);
+      reinterpret_cast<uint4*>(y + yrow * g.ldc + c0)[lane] = o;
+      if (MODE == kModeAR) {
+        #pragma unroll
+        for (int r = 0; r < kFusedMaxTp; ++r)
+          if (r < p.tp && r != p.rank)
+            reinterpret_cast<uint4*>(p.out_land[r] + int64_t(m0 + r0 + rr) * g.n + c0)[lane] = o;
+      }
+    }
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ void reduce_own_tile(const FusedArgs& g, const FusedPeers& p, int lrow0, int m0, int c0,
+                                                int ncols16, int ct, int rbeg, int rend) {
+  const int w = ct >> 5, lane = ct & 31;
+  if (lane >= ncols16) return;
+  if (p.tp == 2) reduce_rows<MODE, 2>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
+  else if (p.tp == 4) reduce_rows<MODE, 4>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
+  else reduce_rows<MODE, 0>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
 }
 
 // Tile t -> (chunk, m0, tn). Chunks are visited starting at (rank + first) % tp; inside a
@@ -195,7 +315,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   // tp-1 sources, and a source can be one call ahead (never two), so counting a call's
   // parity only is what keeps a fast source's next-call contributions out of this count.
   const unsigned rs_target = unsigned(p.tp - 1) * ((p.epoch + 1u) / 2u);
-  unsigned* const rs_bank_local = p.rs_cnt[p.rank] + (p.epoch & 1u) * kFusedMaxTiles;
+  unsigned* const rs_bank_local = pick(p.rs_cnt, p.rank) + (p.epoch & 1u) * kFusedMaxTiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -217,6 +337,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) FUSED_STAMP(0, globaltimer());
 
   if (warp == 0) {
     // ---------------- tile claims + TMA producer ----------------
@@ -268,6 +389,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         }
         if (!ok) break;
       }
+      FUSED_STAMP(1, globaltimer());
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -326,18 +448,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const int lrow = row - chunk * rpr;
       const bool own = chunk == p.rank;
       const int local_tile = ((m0 - chunk * rpr) / kFBM) * tiles_n + tn;  // tile index inside its chunk
-      const bool reduce_here = MODE != kModeAG && own;
       bool ok = true;
       __nv_bfloat16* dst;
       if (MODE == kModeAG) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
       else if (!own) dst = p.send + int64_t(row) * g.n;  // local; the copy warps push it to the owner
       else if (MODE == kModeRS) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(lrow) * g.ldc;
       else dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
-      if (reduce_here) {
-        int arrived = 1;
-        if (lane == 0) arrived = wait_geq(rs_bank_local + local_tile, rs_target, g.err, kErrPeerWait, g.wait_ns);
-        ok = __shfl_sync(0xffffffffu, arrived, 0) != 0;
-      }
+      // own tiles: this rank's partial goes to y as is; the copy warps add the peers'
+      // partials once they have arrived (off the MMA / epilogue critical path)
       #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t v[32];
@@ -346,45 +464,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         tmem_ld32(ta, v);
         tmem_wait_ld();
         const int col0 = tn * BN + cc * 32;
-        if (!ok || col0 >= g.n) continue;
+        if (col0 >= g.n) continue;
         float f[32];
         #pragma unroll
         for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
-        if (reduce_here) {
-          // every rank's partial, summed in rank order (this rank's own in fp32); each
-          // 8-column quarter issues every source's load before the first addition, so the
-          // tp-1 receive-buffer reads overlap instead of running one after another
-          #pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            uint4 raw[kFusedMaxTp];
-            #pragma unroll
-            for (int src = 0; src < kFusedMaxTp; ++src)
-              if (src < p.tp && src != p.rank)
-                raw[src] = *reinterpret_cast<const uint4*>(p.recv[p.rank] + (int64_t(src) * rpr + lrow) * g.n + col0 +
-                                                           8 * qq);
-            float tot[8];
-            #pragma unroll
-            for (int e = 0; e < 8; ++e) tot[e] = 0.f;
-            #pragma unroll
-            for (int src = 0; src < kFusedMaxTp; ++src) {
-              if (src >= p.tp) continue;
-              if (src == p.rank) {
-                #pragma unroll
-                for (int e = 0; e < 8; ++e) tot[e] += f[8 * qq + e];
-                continue;
-              }
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[src]);
-              #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 x = __bfloat1622float2(h[e]);
-                tot[2 * e] += x.x;
-                tot[2 * e + 1] += x.y;
-              }
-            }
-            #pragma unroll
-            for (int e = 0; e < 8; ++e) f[8 * qq + e] = tot[e];
-          }
-        }
         uint4 o[4];
         #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -401,8 +484,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         __syncwarp();
         if (lane == 0) atomicAdd(p.send_cnt + (m0 / kFBM) * tiles_n + tn, 1u);
       }
-      if (MODE == kModeAR && own && ok) {
-        // this warp's 32 reduced rows are in y: the copy warps push them to every peer
+      if (MODE != kModeAG && own && ok) {
+        // this warp's 32 rows of the own partial are in y: the copy warps reduce them
         __threadfence();
         __syncwarp();
         if (lane == 0) atomicAdd(p.own_cnt + local_tile, 1u);
@@ -410,6 +493,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (warp == 2 && lane == 0 && i < 8) FUSED_STAMP(2 + i, globaltimer());
     }
   } else {
     // ---------------- copy warps ----------------
@@ -428,16 +512,23 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // claimed); AR also: push each own reduced tile to every peer, then copy the other
     // owners' reduced tiles from the output landing zone into y
     const int n_rsp = MODE != kModeAG ? (p.tp - 1) * per_chunk : 0;
-    const int n_own = MODE == kModeAR ? per_chunk : 0;
+    // reduce (and, AR, push) row slices of the own tiles, so the reduction spreads
+    // over every CTA's copy warps
+    const int red = red_slices(per_chunk, int(gridDim.x));
+    const int n_own = MODE != kModeAG ? per_chunk * red : 0;
     const int n_ar = MODE == kModeAR ? (p.tp - 1) * per_chunk : 0;
     const int items = MODE == kModeAG ? n_push + n_xg : n_rsp + n_own + n_ar;
     const int batch = MODE == kModeAG ? kCopyBatch : 1;  // an RS / AR item is a whole 128 x 256 tile
-    while (items > 0) {
+    for (int nclaim = 0; items > 0; ++nclaim) {
       if (ct == 0) claim[0] = int(atomicAdd(p.copy_ctr, unsigned(batch)) - p.copy_base);
       copy_bar();
       const int first_item = claim[0];
       copy_bar();
       if (first_item < 0 || first_item >= items) break;
+      if (ct == 0 && nclaim < 8) {
+        FUSED_STAMP(10 + 2 * nclaim, globaltimer());
+        FUSED_STAMP(26 + nclaim, uint64_t(first_item));
+      }
       const int last_item = min(first_item + batch, items);
       bool ok = true;
       // pushes: runs of one destination, then one fence, then one count per unit
@@ -490,11 +581,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                     ct, g.err);
         i = run_end;
       }
-      // RS / AR items (one tile each)
+      // RS / AR items (a tile, or a 16-row slice of an own tile)
       for (int it = first_item; MODE != kModeAG && it < last_item && ok; ++it) {
-        int chunk, m0, tn;
-        if (it < n_rsp + n_own) {
+        int chunk, m0, tn, slice = 0;
+        if (it < n_rsp) {
           fused_tile(it, tiles_m_chunk, tiles_n, p, 1, chunk, m0, tn);  // push items follow the claim order
+        } else if (it < n_rsp + n_own) {
+          // own tiles in their claim order (they follow the peers' tiles: t >= n_rsp)
+          fused_tile(n_rsp + (it - n_rsp) / red, tiles_m_chunk, tiles_n, p, 1, chunk, m0, tn);
+          slice = (it - n_rsp) % red;
         } else {
           const int i3 = it - n_rsp - n_own;  // gather: another owner's reduced tile
           chunk = (p.rank + 1 + i3 / per_chunk) % p.tp;
@@ -509,9 +604,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           if (it < n_rsp)
             claim[1] = wait_geq(p.send_cnt + gtile, 4u * p.epoch, g.err, kErrEpiWait, kWaitBudgetNs);
           else if (it < n_rsp + n_own)
-            claim[1] = wait_geq(p.own_cnt + local_tile, 4u * p.ar_epoch, g.err, kErrEpiWait, kWaitBudgetNs);
+            claim[1] = wait_geq(p.own_cnt + local_tile, 4u * p.epoch, g.err, kErrEpiWait, kWaitBudgetNs) &&
+                       wait_geq(rs_bank_local + local_tile, rs_target, g.err, kErrPeerWait, g.wait_ns);
           else
-            claim[1] = wait_geq(p.ar_cnt[p.rank] + gtile, p.ar_epoch, g.err, kErrPeerWait, g.wait_ns);
+            claim[1] = wait_geq(pick(p.ar_cnt, p.rank) + gtile, unsigned(red) * p.ar_epoch, g.err, kErrPeerWait,
+                                g.wait_ns);
         }
         copy_bar();
         ok = claim[1] != 0;
@@ -519,43 +616,49 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         if (!ok) break;
         if (it < n_rsp) {
           // the partial tile -> the owner's receive buffer, slot of this rank
-          copy_rows(reinterpret_cast<uint4*>(p.recv[chunk] + (int64_t(p.rank) * rpr + (m0 - chunk * rpr)) * g.n +
+          copy_rows(reinterpret_cast<uint4*>(pick(p.recv, chunk) + (int64_t(p.rank) * rpr + (m0 - chunk * rpr)) * g.n +
                                              tn * BN),
                     g.n / 8, reinterpret_cast<const uint4*>(p.send + int64_t(m0) * g.n + tn * BN), g.n / 8, kFBM,
                     ncols16, ct, g.err);
           __threadfence_system();
           copy_bar();
-          if (ct == 0) red_release_add(p.rs_cnt[chunk] + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+          if (ct == 0) red_release_add(pick(p.rs_cnt, chunk) + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
         } else if (it < n_rsp + n_own) {
-          // the reduced tile -> every peer's output landing zone
-          const uint4* src =
-              reinterpret_cast<const uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN);
-          for (int r = 0; r < p.tp; ++r)
-            if (r != p.rank)
-              copy_rows(reinterpret_cast<uint4*>(p.out_land[r] + int64_t(m0) * g.n + tn * BN), g.n / 8, src,
-                        g.ldc / 8, kFBM, ncols16, ct, g.err);
-          __threadfence_system();
-          copy_bar();
-          if (ct == 0)
-            for (int r = 0; r < p.tp; ++r)
-              if (r != p.rank) red_release_add(p.ar_cnt[r] + gtile, 1u);
+          // y (own partial) + every peer's partial, in rank order after the own one; AR:
+          // the sum also goes to every peer's output landing zone
+          const int slice_rows = kFBM / red;
+          reduce_own_tile<MODE>(g, p, m0 - chunk * rpr, m0, tn * BN, ncols16, ct, slice * slice_rows,
+                                (slice + 1) * slice_rows);
+          if (MODE == kModeAR) {
+            __threadfence_system();
+            copy_bar();
+            if (ct == 0) {
+              #pragma unroll
+              for (int r = 0; r < kFusedMaxTp; ++r)
+                if (r < p.tp && r != p.rank) red_release_add(p.ar_cnt[r] + gtile, 1u);
+            }
+          }
         } else {
           copy_rows(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN),
-                    g.ldc / 8, reinterpret_cast<const uint4*>(p.out_land[p.rank] + int64_t(m0) * g.n + tn * BN),
+                    g.ldc / 8, reinterpret_cast<const uint4*>(pick(p.out_land, p.rank) + int64_t(m0) * g.n + tn * BN),
                     g.n / 8, kFBM, ncols16, ct, g.err);
         }
       }
+      if (ct == 0 && nclaim < 8) FUSED_STAMP(11 + 2 * nclaim, globaltimer());
       if (!ok) break;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FUSED_STAMP(34, globaltimer());
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
 }
+
+uint64_t* g_fused_trace = nullptr;
 
 int sm_count() {
   int dev = 0, n = 0;
@@ -610,12 +713,21 @@ int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_ch
   const int per_chunk = (rpr / kFBM) * ((n + 255) / 256);
   int items = 0;
   if (mode == kModeAG) items = (tp - 1) * units + xg_chunks * units;
-  if (mode == kModeRS) items = (tp - 1) * per_chunk;
-  if (mode == kModeAR) items = (tp - 1) * per_chunk + per_chunk + (tp - 1) * per_chunk;
+  const int red = red_slices(per_chunk, grid);
+  if (mode == kModeRS) items = (tp - 1) * per_chunk + per_chunk * red;
+  if (mode == kModeAR) items = (tp - 1) * per_chunk + per_chunk * red + (tp - 1) * per_chunk;
   // every batch claimed, plus one failing claim per CTA, a batch of items each
   const int batch = mode == kModeAG ? kCopyBatch : 1;
   return items > 0 ? ((items + batch - 1) / batch + grid) * batch : 0;
 }
+
+int fused_red_slices(int t_rows, int n, int tp, int grid) {
+  return red_slices((t_rows / tp / kFBM) * ((n + 255) / 256), grid);
+}
+
+void set_fused_trace(uint64_t* buffer) { g_fused_trace = buffer; }
+
+int fused_trace_slots() { return kTraceSlots; }
 
 void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,
                    int t_rows, int n, int k, const FusedPeers& peers, int grid, int* err, cudaStream_t st) {
@@ -636,6 +748,7 @@ void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bo
   g.k = k;
   g.err = err;
   g.wait_ns = peer_wait_budget_ns();
+  g.trace = g_fused_trace;
   g.x_local = static_cast<const __nv_bfloat16*>(x_local);
   g.xg = static_cast<__nv_bfloat16*>(xg);
   g.p = peers;
@@ -661,6 +774,7 @@ void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y
   g.k = k;
   g.err = err;
   g.wait_ns = peer_wait_budget_ns();
+  g.trace = g_fused_trace;
   g.p = peers;
   if (all_reduce) {
     if (w_mn) launch_fused<256, true, kModeAR>(ta, ta, tb, g, grid, st);

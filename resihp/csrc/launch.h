@@ -130,6 +130,12 @@ int fused_tile_claims(int t_rows, int n, int grid);
 // xg_chunks: chunks copied into the gathered input (0: none, 1: only the own chunk into
 // this rank's landing zone, tp: every chunk into a separate buffer).
 int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_chunks, int grid);
+// Row slices per own tile in the RS / AR reduction (the AR counts each slice).
+int fused_red_slices(int t_rows, int n, int tp, int grid);
+// Profiling aid: stamp per-CTA timelines of the fused kernels into ``buffer``
+// ([grid][fused_trace_slots()] uint64 device memory), or stop (nullptr).
+void set_fused_trace(uint64_t* buffer);
+int fused_trace_slots();
 void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,
                    int t_rows, int n, int k, const FusedPeers& peers, int grid, int* err, cudaStream_t st);
 void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n,

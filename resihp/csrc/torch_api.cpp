@@ -487,6 +487,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "budget of each in-kernel wait on another GPU's flag (ns)");
   m.def("set_peer_wait_budget_ns", [](int64_t ns) { resihp::set_peer_wait_budget_ns(uint64_t(ns)); },
         "set the budget of each in-kernel wait on another GPU's flag (ns)");
+  m.def("fused_red_slices", &resihp::fused_red_slices, "row slices per own tile of the fused RS / AR reduction");
+  m.def("set_fused_trace", [](int64_t ptr) { resihp::set_fused_trace(reinterpret_cast<uint64_t*>(ptr)); },
+        "profiling aid: per-CTA timer stamps of the fused TP kernels into a device buffer (0: off)");
+  m.def("fused_trace_slots", &resihp::fused_trace_slots, "stamps per CTA of the fused-kernel trace");
   m.def("gemm", &resihp::gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c"), py::arg("epi"), py::arg("alpha") = 1.0, py::arg("residual") = py::none(),
         py::arg("max_ctas") = 0, py::arg("force_bn") = 0);

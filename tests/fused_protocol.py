@@ -53,7 +53,8 @@ class _Rank:
         self.recv = [dict(), dict()]                            # parity -> {(src, tile): epoch}
         self.send = dict()                                      # local send buffer: {global tile: epoch}
         self.send_cnt = [0] * (per_chunk * tp)                  # global tile -> partial warps in the send buffer
-        self.own_cnt = [0] * per_chunk                          # own tile -> reduced warps in y (AR)
+        self.own_cnt = [0] * per_chunk                          # own tile -> own-partial warps in y
+        self.own_y = dict()                                     # own tile -> epoch of the own partial in y
         self.ar_cnt = [0] * (per_chunk * tp)                    # global tile -> reduced tiles landed
         self.out = [dict(), dict()]                             # parity -> {global tile: ar epoch}
         self.ctr = {"tile": 0, "copy": 0}                       # claim counters (device)
@@ -80,6 +81,7 @@ class Simulation:
         self.copy_claims = copy_claims or (lambda: self.k.fused_copy_claims(
             self.mode, self.t_rows, self.n, self.tp, self.slices, self.tp if self.keep else 0, self.grid))
         self.ranks = [_Rank(tp, self.blocks, self.per_chunk) for _ in range(tp)]
+        self.slices_red = self.k.fused_red_slices(self.t_rows, n, tp, grid)  # row slices per own-tile reduction
 
     def _read(self, version, e, what):
         if version != e:
@@ -134,13 +136,9 @@ class Simulation:
                 yield lambda: True
                 me.send_cnt[gtile] += 4                             # four epilogue warps count it
                 continue
-            yield lambda local=local: me.rs_cnt[par][local] >= (self.tp - 1) * ((e + 1) // 2)
-            for src in range(self.tp):
-                if src != r:
-                    self._read(me.recv[par].get((src, local)), e, f"RS receive of tile {local} from {src} on {r}")
-            if self.op == "ar":
-                yield lambda: True
-                me.own_cnt[local] += 4                              # reduced rows in y, for the copy warps
+            me.own_y[local] = e                                     # the own partial into y
+            yield lambda: True
+            me.own_cnt[local] += 4                                  # for the copy warps' reduction
 
     def _copy(self, r, e, ar_e, xg):
         """One CTA's copy warps: claim COPY_BATCH items at a time; a batch's pushes land,
@@ -151,7 +149,7 @@ class Simulation:
         n_push = (self.tp - 1) * units if self.op == "ag" else 0
         n_xg = self.tp * units if (self.op == "ag" and self.keep) else 0
         n_rsp = (self.tp - 1) * self.per_chunk if self.op != "ag" else 0
-        n_own = self.per_chunk if self.op == "ar" else 0
+        n_own = self.per_chunk * self.slices_red if self.op != "ag" else 0
         n_ar = (self.tp - 1) * self.per_chunk if self.op == "ar" else 0
         items = n_push + n_xg if self.op == "ag" else n_rsp + n_own + n_ar
         if items == 0:
@@ -191,12 +189,17 @@ class Simulation:
                     xg[(c, rb)] = xg.get((c, rb), 0) + 1
 
     def _rs_item(self, r, e, ar_e, it, n_rsp, n_own):
-        """One RS / AR copy item: push a peer-chunk partial tile to its owner, push an own
-        reduced tile to every peer (AR), or take another owner's reduced tile (AR)."""
+        """One RS / AR copy item: push a peer-chunk partial tile to its owner, reduce a
+        16-row slice of an own tile (and, AR, push it to every peer), or take another
+        owner's reduced tile (AR)."""
         me = self.ranks[r]
         par = e % 2
-        if it < n_rsp + n_own:
+        if it < n_rsp:
             c, m0, tn = fused_tile(it, self.blocks, self.tiles_n, r, self.tp, 1, self.rows)
+            rb = (m0 - c * self.rows) // FBM
+        elif it < n_rsp + n_own:
+            t = n_rsp + (it - n_rsp) // self.slices_red
+            c, m0, tn = fused_tile(t, self.blocks, self.tiles_n, r, self.tp, 1, self.rows)
             rb = (m0 - c * self.rows) // FBM
         else:
             i3 = it - n_rsp - n_own
@@ -212,17 +215,23 @@ class Simulation:
             self.ranks[c].rs_cnt[par][local] += 1
         elif it < n_rsp + n_own:
             if c != r:
-                raise ProtocolError(f"own push item {it} on rank {r} maps to chunk {c}")
-            yield lambda: me.own_cnt[local] >= 4 * ar_e
-            for p in range(self.tp):
-                if p != r:
-                    self.ranks[p].out[ar_e % 2][gtile] = ar_e
-            yield lambda: True
-            for p in range(self.tp):
-                if p != r:
-                    self.ranks[p].ar_cnt[gtile] += 1
+                raise ProtocolError(f"own reduction item {it} on rank {r} maps to chunk {c}")
+            yield lambda: me.own_cnt[local] >= 4 * e
+            yield lambda: me.rs_cnt[par][local] >= (self.tp - 1) * ((e + 1) // 2)
+            self._read(me.own_y.get(local), e, f"own partial of tile {local} on {r}")
+            for src in range(self.tp):
+                if src != r:
+                    self._read(me.recv[par].get((src, local)), e, f"RS receive of tile {local} from {src} on {r}")
+            if self.op == "ar":
+                for p in range(self.tp):
+                    if p != r:
+                        self.ranks[p].out[ar_e % 2][gtile] = ar_e
+                yield lambda: True
+                for p in range(self.tp):
+                    if p != r:
+                        self.ranks[p].ar_cnt[gtile] += 1
         else:
-            yield lambda: me.ar_cnt[gtile] >= ar_e
+            yield lambda: me.ar_cnt[gtile] >= self.slices_red * ar_e
             self._read(me.out[ar_e % 2].get(gtile), ar_e, f"AR output tile {gtile} on {r}")
 
     # --- the scheduler -------------------------------------------------------------------

@@ -99,4 +99,6 @@ def test_emulated_gemm_rs_ar(tp, all_reduce):
                 out = em.buf(owner, em.out_off, parity, (T, N))
                 assert torch.equal(out[:em.rpr], y[:em.rpr])  # rank 0's reduced rows pushed to every peer
                 arc = em.u32(owner, fused._AR_CNT, fused.MAX_TILES)
-                assert torch.equal(arc[:per_chunk].cpu(), torch.full((per_chunk,), call, dtype=torch.int32))
+                grid = em.kx.fused_grid(T, N, tp)
+                slices = em.kx.fused_red_slices(T, N, tp, grid)  # each reduced row slice is counted
+                assert torch.equal(arc[:per_chunk].cpu(), torch.full((per_chunk,), slices * call, dtype=torch.int32))

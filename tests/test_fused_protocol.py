@@ -14,7 +14,7 @@ from fused_protocol import ProtocolError, Simulation
 
 
 @pytest.mark.parametrize("op", ["ag", "rs", "ar"])
-@pytest.mark.parametrize("tp,grid", [(2, 3), (2, 8), (4, 5), (8, 7)])
+@pytest.mark.parametrize("tp,grid", [(2, 3), (2, 8), (4, 5), (8, 7), (2, 20)])
 def test_protocol_has_no_race_or_deadlock(op, tp, grid):
     for seed in range(5):
         sim = Simulation(op, tp=tp, rows_per_rank=256, n=512, grid=grid, epochs=4, seed=seed)
