@@ -4,10 +4,10 @@
 Model: Llama-style 1.3B (24 layers, hidden 2048, 16 heads MHA, SwiGLU 5504, vocab 32000),
 bf16 compute with FP32 master weights and AdamW; sequence 2048, micro-batch 2, global
 batch 64 sequences of synthetic seeded tokens, random normal(0, 0.02) init. Layout per
-N (sub-layouts of config 2's TP2 x PP2 x DP2, the fastest first: data parallelism, then
-the pipeline, then tensor parallelism; total work fixed, so scaling is strong):
-1 -> one GPU, 2 -> DP2, 4 -> PP2 x DP2, 8 -> TP2 x PP2 x DP2 (sequence parallel when
-TP > 1). Both arms run the same layout for each N.
+N (total work fixed, so scaling is strong): below eight GPUs the fastest measured
+layout, pure data parallelism (1 -> one GPU, 2 -> DP2, 4 -> DP4: 381.9k tokens/s
+against 365.2k for PP2 x DP2); at eight GPUs config 2's own TP2 x PP2 x DP2 (sequence
+parallel). Both arms run the same layout for each N.
 
 ``value`` is device-timed: CUDA events around exactly K steps, barrier + synchronize on
 both sides, max over ranks. ``e2e`` is the same K steps through the public API
@@ -39,7 +39,7 @@ METRIC = "tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; fail-stop r
 MODEL = dict(model_dim=2048, num_layers=24, num_heads=16, ffn_dim=5504, vocab_size=32000, seq_len=2048)
 GLOBAL_BATCH = 64
 MICRO_BATCH = 2
-LAYOUTS = {1: (1, 1, 1), 2: (1, 1, 2), 4: (1, 2, 2), 8: (2, 2, 2)}  # (tp, pp, dp)
+LAYOUTS = {1: (1, 1, 1), 2: (1, 1, 2), 4: (1, 1, 4), 8: (2, 2, 2)}  # (tp, pp, dp)
 
 # BASELINE configs 3 and 5 (8 GPUs only; --config 3 / --config 5).
 CONFIGS = {

@@ -348,21 +348,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // Delta[b, h, s] = sum_d dO * O  (fp32)
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_ld, const __nv_bfloat16* __restrict__ dout,
                                   int64_t do_ld, float* __restrict__ delta, int rows, int seq, int hq, int d) {
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  // eight lanes per (token, head): 16-byte loads, a three-step shuffle reduction
   const int lane = threadIdx.x & 31;
-  if (warp_global >= rows * hq) return;
-  const int t = warp_global / hq, h = warp_global % hq;
-  const __nv_bfloat16* po = o + int64_t(t) * o_ld + int64_t(h) * d;
-  const __nv_bfloat16* pd = dout + int64_t(t) * do_ld + int64_t(h) * d;
+  const int idx = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + (lane >> 3);
+  const int gl = lane & 7;
+  const bool live = idx < rows * hq;
   float acc = 0.f;
-  for (int c = lane * 2; c < d; c += 64) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(po + c));
-    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(pd + c));
-    acc += x.x * y.x + x.y * y.y;
+  int t = 0, h = 0;
+  if (live) {
+    t = idx / hq;
+    h = idx % hq;
+    const __nv_bfloat16* po = o + int64_t(t) * o_ld + int64_t(h) * d;
+    const __nv_bfloat16* pd = dout + int64_t(t) * do_ld + int64_t(h) * d;
+    for (int c = gl * 8; c < d; c += 64) {
+      const uint4 xr = *reinterpret_cast<const uint4*>(po + c);
+      const uint4 yr = *reinterpret_cast<const uint4*>(pd + c);
+      const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&xr);
+      const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&yr);
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = __bfloat1622float2(x[e]), b = __bfloat1622float2(y[e]);
+        acc += a.x * b.x + a.y * b.y;
+      }
+    }
   }
   #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
+  for (int off = 4; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (live && gl == 0) {
     const int b = t / seq, s = t % seq;
     delta[(int64_t(b) * hq + h) * seq + s] = acc;
   }
@@ -869,7 +881,7 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
   RESIHP_CHECK(dqkv_ld == int64_t(hq + 2 * hkv) * d, "dqkv must be dense");
   {
     const int warps = rows * hq;
-    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(out), out_ld,
+    attn_delta_kernel<<<((warps + 3) / 4 * 32 + 255) / 256, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(out), out_ld,
                                                                 static_cast<const __nv_bfloat16*>(dout), dout_ld,
                                                                 delta, rows, seq, hq, d);
     RESIHP_CUDA_CHECK(cudaGetLastError());

@@ -64,8 +64,18 @@ constexpr int kCopyWarps = 4;
 constexpr int kCopyThreads = 32 * kCopyWarps;
 constexpr int kFusedThreads = 192 + kCopyThreads;
 constexpr int kTileRing = 4;
-constexpr int kCopyUnroll = 8;
-constexpr int kCopyBatch = 8;  // copy items per claim
+constexpr int kCopyUnroll = 8;  // 16-byte vectors in flight per thread in copy_rows
+constexpr int kSpanUnroll = 16; // ... in copy_span (AG pushes: more bytes in flight per SM over NVLink)
+constexpr int kCopyBatch = 8;   // most AG copy items per claim
+
+// AG copy items per claim: up to kCopyBatch (fewer claims and system fences), but small
+// enough that the items spread over every CTA's copy warps -- a push's rate over NVLink
+// is set by the bytes each SM keeps in flight, so concentrating the pushes on a few CTAs
+// would starve the link.
+__host__ __device__ inline int ag_copy_batch(int items, int grid) {
+  const int b = items / (2 * grid);
+  return b < 1 ? 1 : (b > kCopyBatch ? kCopyBatch : b);
+}
 // An own tile's reduction is split into this many copy items (row slices): enough items
 // to give every CTA's copy warps one (at least 1, at most 8 slices of 16 rows).
 __host__ __device__ inline int red_slices(int per_chunk, int grid) {
@@ -141,19 +151,19 @@ __device__ __forceinline__ T pick(const T (&arr)[kFusedMaxTp], int i) {
   return r;
 }
 
-// ``count`` contiguous 16-byte vectors, copy-warp thread ``ct`` of kCopyThreads, eight
-// loads in flight per thread before their stores.
+// ``count`` contiguous 16-byte vectors, copy-warp thread ``ct`` of kCopyThreads,
+// kSpanUnroll loads in flight per thread before their stores.
 __device__ __forceinline__ void copy_span(uint4* dst, const uint4* src, int64_t count, int ct, int* err) {
   if (!bounds_ok(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0, err)) return;
-  for (int64_t base = ct; base < count; base += int64_t(kCopyThreads) * kCopyUnroll) {
-    uint4 r[kCopyUnroll];
+  for (int64_t base = ct; base < count; base += int64_t(kCopyThreads) * kSpanUnroll) {
+    uint4 r[kSpanUnroll];
     #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) {
+    for (int u = 0; u < kSpanUnroll; ++u) {
       const int64_t i = base + int64_t(u) * kCopyThreads;
       if (i < count) r[u] = ld_cg_v4(src + i);
     }
     #pragma unroll
-    for (int u = 0; u < kCopyUnroll; ++u) {
+    for (int u = 0; u < kSpanUnroll; ++u) {
       const int64_t i = base + int64_t(u) * kCopyThreads;
       if (i < count) dst[i] = r[u];
     }
@@ -497,7 +507,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     }
   } else {
     // ---------------- copy warps ----------------
-    // Items are claimed kCopyBatch at a time; consecutive push units of one destination
+    // AG items are claimed ag_copy_batch at a time; consecutive push units of one destination
     // (and consecutive gathered-copy units of one chunk) are contiguous rows, so each
     // run of a batch is one span copy, and a batch's pushes share one system fence.
     const int ct = threadIdx.x - 192;  // 0 .. kCopyThreads-1
@@ -518,7 +528,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int n_own = MODE != kModeAG ? per_chunk * red : 0;
     const int n_ar = MODE == kModeAR ? (p.tp - 1) * per_chunk : 0;
     const int items = MODE == kModeAG ? n_push + n_xg : n_rsp + n_own + n_ar;
-    const int batch = MODE == kModeAG ? kCopyBatch : 1;  // an RS / AR item is a whole 128 x 256 tile
+    // an RS / AR item is a whole 128 x 256 tile (or a slice of one)
+    const int batch = MODE == kModeAG ? ag_copy_batch(items, int(gridDim.x)) : 1;
     for (int nclaim = 0; items > 0; ++nclaim) {
       if (ct == 0) claim[0] = int(atomicAdd(p.copy_ctr, unsigned(batch)) - p.copy_base);
       copy_bar();
@@ -717,7 +728,7 @@ int fused_copy_claims(int mode, int t_rows, int n, int tp, int slices, int xg_ch
   if (mode == kModeRS) items = (tp - 1) * per_chunk + per_chunk * red;
   if (mode == kModeAR) items = (tp - 1) * per_chunk + per_chunk * red + (tp - 1) * per_chunk;
   // every batch claimed, plus one failing claim per CTA, a batch of items each
-  const int batch = mode == kModeAG ? kCopyBatch : 1;
+  const int batch = mode == kModeAG ? ag_copy_batch(items, grid) : 1;
   return items > 0 ? ((items + batch - 1) / batch + grid) * batch : 0;
 }
 

@@ -16,7 +16,7 @@ regions of other ranks and read them with P2P loads inside their own kernels:
   reshard of ``resihp/parallel/reshard.py:187-243``).
 * :class:`HeteroPeers` -- the logical gradient sum for replicas with different layouts
   (reference: ``resihp/parallel/dp.py:140-151``) as P2P pulls of the other holders'
-  pieces plus an ordered sum; off unless ``RESIHP_P2P_HETERO=1``.
+  pieces plus an ordered sum (``RESIHP_P2P_HETERO=0``: bucketed NCCL all-reduces instead).
 
 Mappings are opened after a fail-stop's world re-formation and closed at the next safe
 point, when no kernel is in flight; a dead rank's region is never mapped again.
@@ -261,7 +261,7 @@ class GatherPlan:
 # heterogeneous replicas: the logical gradient sum by P2P pulls
 # ---------------------------------------------------------------------------------------
 
-HETERO_ENABLED = os.environ.get("RESIHP_P2P_HETERO", "0") == "1"
+HETERO_ENABLED = os.environ.get("RESIHP_P2P_HETERO", "1") == "1"
 
 
 @dataclass(frozen=True)

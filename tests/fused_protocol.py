@@ -154,7 +154,9 @@ class Simulation:
         items = n_push + n_xg if self.op == "ag" else n_rsp + n_own + n_ar
         if items == 0:
             return
-        size = 1 if self.op != "ag" else COPY_BATCH  # an RS / AR item is a whole tile
+        # an RS / AR item is a whole tile (or a slice); AG items come in batches small
+        # enough to spread over the grid (fused_gemm.cu ag_copy_batch)
+        size = 1 if self.op != "ag" else max(1, min(COPY_BATCH, items // (2 * self.grid)))
         while True:
             first = self._claim(me, "copy", items, size)
             yield lambda: True
