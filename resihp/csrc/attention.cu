@@ -408,12 +408,6 @@ struct DkdvSmem {
   static constexpr int kBytes = 2 * kKV + 2 * kQdStages * kQ + 4 * kP + 2 * kQdStages * kQs * 4 + 1024 + 256;
 };
 
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 
 template <int D>
 __global__ void __launch_bounds__(kDkdvThreads, 1)

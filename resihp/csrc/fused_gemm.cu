@@ -20,13 +20,15 @@
 // AG: the copy warps push this rank's chunk, in units of a few rows, into every peer's
 //     landing zone, destination-major in the order the peers consume it (peer r-1
 //     first: it computes chunk r right after its own), and count each 128-row block per
-//     (source, block). The producer loads own-chunk tiles from x_local and a peer chunk's
+//     (source, block). Pushes are bulk asynchronous copies driven by one thread (TMA
+//     engine: global -> shared staging -> peer global, two 16 KB buffers), so the bytes
+//     in flight do not cost registers. The producer loads own-chunk tiles from x_local and a peer chunk's
 //     tiles from the local landing zone once that block's counter is complete. The copy
 //     warps then also assemble the gathered input in ``xg`` for the backward pass.
 // RS: tiles of the peers' token chunks run first; their epilogue stores the bf16 partial
-//     in a local send buffer and flags it, and the copy warps push each finished partial
-//     tile, row by row (one warp store per 512-byte row), into the owning peer's receive
-//     buffer and count it there.
+//     in a local, tile-contiguous send buffer and flags it, and the copy warps push each
+//     finished 64 KB tile as one bulk copy into the owning peer's (tile-contiguous)
+//     receive buffer and count it there.
 //     Own-chunk tiles run last: their epilogue stores this rank's partial in y, and once
 //     the tp-1 contributions have arrived the copy warps add them (own partial first,
 //     then the peers' in rank order, in fp32, deterministically), many rows in flight.
@@ -67,6 +69,7 @@ constexpr int kTileRing = 4;
 constexpr int kCopyUnroll = 8;  // 16-byte vectors in flight per thread in copy_rows
 constexpr int kSpanUnroll = 16; // ... in copy_span (AG pushes: more bytes in flight per SM over NVLink)
 constexpr int kCopyBatch = 8;   // most AG copy items per claim
+constexpr int kChunk = 16384;   // bytes per bulk-push chunk (two shared-memory buffers of it)
 
 // AG copy items per claim: up to kCopyBatch (fewer claims and system fences), but small
 // enough that the items spread over every CTA's copy warps -- a push's rate over NVLink
@@ -114,7 +117,8 @@ struct FusedShape {
   static constexpr int kABytes = kFBM * kFBK * 2;
   static constexpr int kBBytes = BN * kFBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 512;
+  static constexpr int kSmem = kStages * kStageBytes + 2 * kChunk + 1024 + 512;
+  static constexpr int kTileElems = kFBM * BN;  // one tile in the RS send / receive buffers
 };
 
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
@@ -203,13 +207,14 @@ __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* 
 // receive-buffer reads overlap. AR: each reduced row is also stored into every peer's
 // output landing zone.
 template <int MODE, int TP>
-__device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers& p, int lrow0, int m0, int c0, int w,
-                                            int lane, int rbeg, int rend) {
+__device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers& p, const __nv_bfloat16* recv_tile,
+                                            int64_t src_stride, int tile_ld, int lrow0, int m0, int c0, int w, int lane,
+                                            int rbeg, int rend) {
   // TP: the group size, or 0 for any size up to kFusedMaxTp (one row at a time)
   constexpr int kSrc = TP > 0 ? TP : kFusedMaxTp;
-  constexpr int kRows = TP > 0 && 8 / TP > 0 ? 8 / TP : 1;  // rows whose sources load at once
+  constexpr int kTpDiv = TP > 0 ? TP : 8;
+  constexpr int kRows = 8 / kTpDiv > 0 ? 8 / kTpDiv : 1;  // rows whose sources load at once
   __nv_bfloat16* y = static_cast<__nv_bfloat16*>(g.c);
-  const __nv_bfloat16* recv = pick(p.recv, p.rank);
   for (int r0 = rbeg + w * kRows; r0 < rend; r0 += kCopyWarps * kRows) {
     uint4 v[kRows][kSrc];
     #pragma unroll
@@ -222,8 +227,8 @@ __device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers
         if (TP == 0 && src >= p.tp) continue;
         const uint4* a = src == p.rank
                              ? reinterpret_cast<const uint4*>(y + yrow * g.ldc + c0) + lane
-                             : reinterpret_cast<const uint4*>(recv + (int64_t(src) * p.rows_per_rank + lrow) * g.n +
-                                                              c0) +
+                             : reinterpret_cast<const uint4*>(recv_tile + src * src_stride +
+                                                              int64_t(r0 + rr) * tile_ld) +
                                    lane;
         v[rr][src] = ld_cg_v4(a);
       }
@@ -265,13 +270,62 @@ __device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers
 }
 
 template <int MODE>
-__device__ __forceinline__ void reduce_own_tile(const FusedArgs& g, const FusedPeers& p, int lrow0, int m0, int c0,
-                                                int ncols16, int ct, int rbeg, int rend) {
+// The receive buffer is tile-contiguous: source src's partial of own tile lt starts at
+// recv + (src * per_chunk + lt) * tile_elems, rows tile_ld apart.
+__device__ __forceinline__ void reduce_own_tile(const FusedArgs& g, const FusedPeers& p, int lt, int per_chunk,
+                                                int tile_elems, int tile_ld, int lrow0, int m0, int c0, int ncols16,
+                                                int ct, int rbeg, int rend) {
   const int w = ct >> 5, lane = ct & 31;
   if (lane >= ncols16) return;
-  if (p.tp == 2) reduce_rows<MODE, 2>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
-  else if (p.tp == 4) reduce_rows<MODE, 4>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
-  else reduce_rows<MODE, 0>(g, p, lrow0, m0, c0, w, lane, rbeg, rend);
+  const __nv_bfloat16* recv_tile = pick(p.recv, p.rank) + int64_t(lt) * tile_elems;
+  const int64_t stride = int64_t(per_chunk) * tile_elems;
+  if (p.tp == 2) reduce_rows<MODE, 2>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
+  else if (p.tp == 4) reduce_rows<MODE, 4>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
+  else reduce_rows<MODE, 0>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
+}
+
+// One thread: ``bytes`` (a multiple of 16) from this GPU's memory at ``src`` to ``dst`` (a
+// peer's memory) through the TMA engine, staged in two kChunk shared-memory buffers: the
+// load of chunk c+1 overlaps the store of chunk c, and no register holds a byte in
+// flight. On return every store is complete and ordered before the caller's next
+// generic-proxy operations (a release on a peer's counter follows). ``phase`` carries
+// the buffers' barrier phases from call to call. False if a wait ran out its budget.
+__device__ __forceinline__ bool bulk_push(uint8_t* stage, uint64_t* bar, uint32_t& phase, uint8_t* dst,
+                                          const uint8_t* src, int64_t bytes, int* err) {
+  if (!bounds_ok(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | uintptr_t(bytes)) & 15u) == 0,
+                 err))
+    return false;
+  const int nch = int((bytes + kChunk - 1) / kChunk);
+  bulk_wait_read_all();  // an earlier push may still be reading the buffers
+  #pragma unroll 1
+  for (int c = 0; c < 2 && c < nch; ++c) {
+    const uint32_t len = uint32_t(min(int64_t(kChunk), bytes - int64_t(c) * kChunk));
+    mbar_expect_tx(&bar[c], len);
+    bulk_load(stage + c * kChunk, src + int64_t(c) * kChunk, len, &bar[c]);
+  }
+  bool ok = true;
+  #pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    const int b = c & 1;
+    if (!mbar_wait(&bar[b], (phase >> b) & 1u, err, kErrEpiWait)) {
+      ok = false;
+      break;
+    }
+    phase ^= 1u << b;
+    const uint32_t len = uint32_t(min(int64_t(kChunk), bytes - int64_t(c) * kChunk));
+    bulk_store(dst + int64_t(c) * kChunk, stage + b * kChunk, len);
+    bulk_commit();
+    if (c + 2 < nch) {
+      bulk_wait_read_all();  // this store has read buffer b: refill it
+      const uint32_t len2 = uint32_t(min(int64_t(kChunk), bytes - int64_t(c + 2) * kChunk));
+      mbar_expect_tx(&bar[b], len2);
+      bulk_load(stage + b * kChunk, src + int64_t(c + 2) * kChunk, len2, &bar[b]);
+    }
+  }
+  bulk_wait_all();
+  fence_proxy_async_global();  // the async-proxy writes before the generic release that follows
+  __threadfence_system();
+  return ok;
 }
 
 // Tile t -> (chunk, m0, tn). Chunks are visited starting at (rank + first) % tp; inside a
@@ -301,7 +355,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * S::kStageBytes);
+  uint8_t* bstage = smem + kStages * S::kStageBytes;  // bulk-push buffers [2][kChunk]
+  uint64_t* full = reinterpret_cast<uint64_t*>(bstage + 2 * kChunk);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -310,6 +365,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   int* ring = reinterpret_cast<int*>(ring_empty + kTileRing);
   int* claim = ring + kTileRing;  // copy warps: claimed item, wait outcome
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(claim + 4);
+  uint64_t* bbar = reinterpret_cast<uint64_t*>(tmem_slot + 2);  // [2] bulk-push loads landed
 
   const FusedPeers& p = g.p;
   const int warp = threadIdx.x >> 5;
@@ -340,6 +396,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       mbar_init(&ring_full[r], 1);
       mbar_init(&ring_empty[r], 5);  // the MMA thread and the four epilogue warps
     }
+    mbar_init(&bbar[0], 1);
+    mbar_init(&bbar[1], 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
@@ -461,7 +519,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       bool ok = true;
       __nv_bfloat16* dst;
       if (MODE == kModeAG) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
-      else if (!own) dst = p.send + int64_t(row) * g.n;  // local; the copy warps push it to the owner
+      else if (!own) dst = p.send + int64_t((m0 / kFBM) * tiles_n + tn) * S::kTileElems + (row - m0) * BN - tn * BN;
+      // (a peer tile's partial: local, tile-contiguous, so the copy warps push it whole)
       else if (MODE == kModeRS) dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(lrow) * g.ldc;
       else dst = static_cast<__nv_bfloat16*>(g.c) + int64_t(row) * g.ldc;
       // own tiles: this rank's partial goes to y as is; the copy warps add the peers'
@@ -511,6 +570,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // (and consecutive gathered-copy units of one chunk) are contiguous rows, so each
     // run of a batch is one span copy, and a batch's pushes share one system fence.
     const int ct = threadIdx.x - 192;  // 0 .. kCopyThreads-1
+    uint32_t bphase = 0;               // ct 0: phase bits of the two bulk-push buffers
     const int k16 = g.k / 8;           // 16-byte vectors per row of the AG input
     const int srows = kFBM / max(p.slices, 1);
     const int units = tiles_m_chunk * p.slices;  // push units of this rank's chunk (unit u = rows u*srows..)
@@ -545,23 +605,30 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       // pushes: runs of one destination, then one fence, then one count per unit
       const int pe = min(last_item, n_push);
       if (first_item < pe) {
-        for (int i = first_item; i < pe;) {
-          const int j = i / units;
-          const int run_end = min(pe, (j + 1) * units);
-          const int dest = (p.rank - j - 1 + p.tp) % p.tp;
-          const int r0 = (i % units) * srows;
-          copy_span(reinterpret_cast<uint4*>(p.land[dest] + (int64_t(p.rank) * rpr + r0) * g.k),
-                    reinterpret_cast<const uint4*>(g.x_local + int64_t(r0) * g.k), int64_t(run_end - i) * srows * k16,
-                    ct, g.err);
-          i = run_end;
-        }
-        __threadfence_system();
-        copy_bar();
-        if (ct == 0)
-          for (int i = first_item; i < pe; ++i) {
-            const int dest = (p.rank - i / units - 1 + p.tp) % p.tp;
-            red_release_add(p.ag_cnt[dest] + p.rank * kFusedMaxRb + (i % units) / p.slices, 1u);
+        // one thread drives the TMA engine: each run is one contiguous span of rows
+        if (ct == 0) {
+          bool pushed = true;
+          for (int i = first_item; i < pe && pushed;) {
+            const int j = i / units;
+            const int run_end = min(pe, (j + 1) * units);
+            const int dest = (p.rank - j - 1 + p.tp) % p.tp;
+            const int r0 = (i % units) * srows;
+            pushed = bulk_push(bstage, bbar, bphase,
+                               reinterpret_cast<uint8_t*>(pick(p.land, dest) + (int64_t(p.rank) * rpr + r0) * g.k),
+                               reinterpret_cast<const uint8_t*>(g.x_local + int64_t(r0) * g.k),
+                               int64_t(run_end - i) * srows * g.k * 2, g.err);
+            i = run_end;
           }
+          if (pushed)
+            for (int i = first_item; i < pe; ++i) {
+              const int dest = (p.rank - i / units - 1 + p.tp) % p.tp;
+              red_release_add(pick(p.ag_cnt, dest) + p.rank * kFusedMaxRb + (i % units) / p.slices, 1u);
+            }
+          claim[1] = pushed;
+        }
+        copy_bar();
+        ok = claim[1] != 0;
+        copy_bar();
       }
       // gathered copy: runs of one chunk (own chunk first, then in arrival order)
       const int xb = max(first_item, n_push), xe = min(last_item, n_push + n_xg);
@@ -626,20 +693,26 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         copy_bar();
         if (!ok) break;
         if (it < n_rsp) {
-          // the partial tile -> the owner's receive buffer, slot of this rank
-          copy_rows(reinterpret_cast<uint4*>(pick(p.recv, chunk) + (int64_t(p.rank) * rpr + (m0 - chunk * rpr)) * g.n +
-                                             tn * BN),
-                    g.n / 8, reinterpret_cast<const uint4*>(p.send + int64_t(m0) * g.n + tn * BN), g.n / 8, kFBM,
-                    ncols16, ct, g.err);
-          __threadfence_system();
+          // the partial tile -> the owner's receive buffer (slot of this rank): the whole
+          // tile, contiguous in both buffers, through the TMA engine, then counted there
+          if (ct == 0) {
+            const bool pushed = bulk_push(
+                bstage, bbar, bphase,
+                reinterpret_cast<uint8_t*>(pick(p.recv, chunk) + (int64_t(p.rank) * per_chunk + local_tile) * S::kTileElems),
+                reinterpret_cast<const uint8_t*>(p.send + int64_t(gtile) * S::kTileElems), int64_t(S::kTileElems) * 2,
+                g.err);
+            if (pushed) red_release_add(pick(p.rs_cnt, chunk) + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+            claim[1] = pushed;
+          }
           copy_bar();
-          if (ct == 0) red_release_add(pick(p.rs_cnt, chunk) + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+          ok = claim[1] != 0;
+          copy_bar();
         } else if (it < n_rsp + n_own) {
           // y (own partial) + every peer's partial, in rank order after the own one; AR:
           // the sum also goes to every peer's output landing zone
           const int slice_rows = kFBM / red;
-          reduce_own_tile<MODE>(g, p, m0 - chunk * rpr, m0, tn * BN, ncols16, ct, slice * slice_rows,
-                                (slice + 1) * slice_rows);
+          reduce_own_tile<MODE>(g, p, local_tile, per_chunk, S::kTileElems, BN, m0 - chunk * rpr, m0, tn * BN, ncols16,
+                                ct, slice * slice_rows, (slice + 1) * slice_rows);
           if (MODE == kModeAR) {
             __threadfence_system();
             copy_bar();

@@ -76,8 +76,9 @@ class SymmetricWorkspace:
     """This rank's IPC-shared region and its mappings of every peer's region.
 
     Layout (bytes): counter words (176 KB) | two AG landing zones ``[T, width]`` | two RS
-    receive buffers ``[tp, T/tp, width]`` | two AR output landing zones ``[T, width]`` |
-    the RS send buffer ``[T, width]`` (local: partial tiles before the copy warps push them).
+    receive buffers (``[tp][T/128 tiles of this rank's chunk][128 x 256]``, tile-contiguous)
+    | two AR output landing zones ``[T, width]`` | the RS send buffer (``[T/128 x
+    tiles_n][128 x 256]``, local: partial tiles before the copy warps push them whole).
     Every fused call's gathered input, reduced output and all-reduced output has the
     model width, so one region serves all projections of a layer and their backward.
     """
@@ -100,7 +101,9 @@ class SymmetricWorkspace:
         self.device = torch.device(device)
         with torch.cuda.device(self.device):
             self.slices = k.fused_slices(rows_per_rank)
-        self.buf_bytes = t * width * 2
+        # every buffer holds [T, width] rows, or (RS send / receive) the same data as whole
+        # 128 x 256 tiles, so its size rounds the width up to 256 columns
+        self.buf_bytes = t * (-(-width // 256) * 256) * 2
         g = _GUARD_BYTES if DEBUG else 0
         self.stride = self.buf_bytes + g
         self.land_off = _FLAG_BYTES + g

@@ -38,7 +38,7 @@ class Emulation:
         self.gen = g
         with torch.cuda.device(self.dev):
             self.slices = self.kx.fused_slices(self.rpr)
-        self.buf_bytes = tokens * width * 2
+        self.buf_bytes = tokens * (-(-width // 256) * 256) * 2  # as SymmetricWorkspace
         self.land_off = fused._FLAG_BYTES
         self.recv_off = self.land_off + 2 * self.buf_bytes
         self.out_off = self.recv_off + 2 * self.buf_bytes
@@ -59,6 +59,26 @@ class Emulation:
     # --- views into the emulated workspaces ---------------------------------------------
     def u32(self, rank, off, count):
         return self.regions[rank][off:off + 4 * count].view(torch.int32)
+
+    def recv_tiles(self, rank, parity, n):
+        """Rank ``rank``'s receive buffer as ``[tp, tiles of a chunk, 128, 256]``."""
+        tiles = (self.rpr // 128) * (-(-n // 256))
+        return self.buf(rank, self.recv_off, parity, (self.tp * tiles * 128, 256)).view(self.tp, tiles, 128, 256)
+
+    def to_tiles(self, rows_x_n):
+        """``[rpr, n]`` rows as the kernels' tile-contiguous ``[tiles, 128, 256]`` (tile =
+        128-row block major, then 256-column block; columns past n zero)."""
+        r, n = rows_x_n.shape
+        tn = -(-n // 256)
+        padded = torch.zeros(r, tn * 256, dtype=rows_x_n.dtype, device=rows_x_n.device)
+        padded[:, :n] = rows_x_n
+        return padded.view(r // 128, 128, tn, 256).permute(0, 2, 1, 3).reshape(-1, 128, 256)
+
+    def from_tiles(self, tiles, n):
+        """Inverse of :meth:`to_tiles` (``[tiles, 128, 256]`` -> ``[rpr, n]``)."""
+        tn = -(-n // 256)
+        t = tiles.view(-1, tn, 128, 256).permute(0, 2, 1, 3).reshape(-1, tn * 256)
+        return t[:, :n]
 
     def buf(self, rank, off, parity, shape):
         start = off + parity * self.buf_bytes
@@ -109,9 +129,9 @@ class Emulation:
         op = (lambda w: w.float()) if w_mn else (lambda w: w.float().t())
         parts = [h.float() @ op(w) for h, w in zip(h_peers, w_peers)]
         for parity in range(2):
-            recv = self.buf(0, self.recv_off, parity, (self.tp, self.rpr * n)).view(self.tp, self.rpr, n)
+            recv = self.recv_tiles(0, parity, n)
             for src in range(1, self.tp):
-                recv[src].copy_(parts[src][:self.rpr].bfloat16())
+                recv[src].copy_(self.to_tiles(parts[src][:self.rpr].bfloat16()))
         if not all_reduce:
             own = parts[0][:self.rpr]
             return own + sum(parts[src][:self.rpr].bfloat16().float() for src in range(1, self.tp))

@@ -91,8 +91,9 @@ def test_emulated_gemm_rs_ar(tp, all_reduce):
         parity = call % 2
         for owner in range(1, tp):
             # rank 0's partial of the owner's rows, in the owner's receive buffer slot 0
-            recv = em.buf(owner, em.recv_off, parity, (tp, em.rpr * N)).view(tp, em.rpr, N)
-            assert torch.equal(recv[0], mine[owner * em.rpr:(owner + 1) * em.rpr])
+            # (tile-contiguous: 128 x 256 tiles)
+            recv = em.recv_tiles(owner, parity, N)
+            assert torch.equal(em.from_tiles(recv[0], N), mine[owner * em.rpr:(owner + 1) * em.rpr])
             bank = em.u32(owner, fused._RS_CNT, 2 * fused.MAX_TILES).view(2, fused.MAX_TILES)[call % 2]
             assert torch.equal(bank[:per_chunk].cpu(), torch.full((per_chunk,), 1, dtype=torch.int32))
             if all_reduce:
