@@ -58,12 +58,13 @@ def test_residual_epilogue_and_both_tiles():
     ops.check_device_errors()
 
 
-@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (300, 520, 136), (1024, 2048, 512), (4096, 2048, 5504)])
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (300, 520, 136), (1024, 2048, 512), (4096, 2048, 5504),
+                                   (512, 512, 8192)])
 def test_cta_pair_tiles(m, n, k):
     """The 256 x 256 CTA-pair kernel (force_bn=512) against FP32 torch, for the forward,
     dgrad and wgrad operand layouts and every epilogue the linear layers use, next to the
     single-CTA kernel (force_bn=256); a one-pair grid pushes many tiles through both
-    TMEM accumulators."""
+    TMEM accumulators; 512 x 512 x 8192 is four tiles of 128 K blocks each."""
     torch.manual_seed(2)
     lib = _ext.require()
     x = torch.randn(m, k, device="cuda").bfloat16()
