@@ -525,14 +525,16 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           if (!mbar_wait(&ds_full[sp], (p >> 1) & 1, a.err, kErrMmaWait)) { ok = false; break; }
           tc_fence_after();
           const int sp3 = p % QS;
-          const uint32_t pt_addr = smem_u32(spt + sp * L::kP), dst_addr = smem_u32(sdst + sp * L::kP);
           const uint32_t q_addr = smem_u32(sq + sp3 * L::kQ), do_addr = smem_u32(sdo + sp3 * L::kQ);
           #pragma unroll
           for (int kk = 0; kk < kQs / 16; ++kk) {
-            umma_bf16(t_dv, smem_desc_sw128(pt_addr + kk * 32, 16, 1024),
-                      smem_desc_sw128(do_addr + kk * 2048, kQs * 128, 1024), id_acc, (p > 0 || kk > 0));
-            umma_bf16(t_dk, smem_desc_sw128(dst_addr + kk * 32, 16, 1024),
-                      smem_desc_sw128(q_addr + kk * 2048, kQs * 128, 1024), id_acc, (p > 0 || kk > 0));
+            // A from TMEM: P^T / dS^T as packed bf16 pairs, 16 q columns = 8 TMEM columns
+            // per K step; the two 32-column halves sit at the start of each half's region
+            const uint32_t acol = uint32_t(sp * kQs + (kk >> 1) * 32 + (kk & 1) * 8);
+            umma_bf16_ts(t_dv, tmem + acol, smem_desc_sw128(do_addr + kk * 2048, kQs * 128, 1024), id_acc,
+                         (p > 0 || kk > 0));
+            umma_bf16_ts(t_dk, tmem + 128 + acol, smem_desc_sw128(q_addr + kk * 2048, kQs * 128, 1024), id_acc,
+                         (p > 0 || kk > 0));
           }
           umma_commit(&qd_empty[sp3]);
           umma_commit(&ds_empty[sp]);
@@ -565,7 +567,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       // lse / delta of this step landed with Q (the MMA that filled S^T waited for them)
       const int s3 = it % QS;
       if (!mbar_wait(&qd_full[s3], (it / QS) & 1, a.err, kErrEpiWait)) { ok = false; break; }
-      if (!mbar_wait(&ds_empty[s], n ^ 1, a.err, kErrEpiWait)) { ok = false; break; }
       const float* lse = s_lse + s3 * kQs + half * 32;
       const float* dlt = s_delta + s3 * kQs + half * 32;
       const int q_pos0 = qs * kQs + half * 32;
@@ -583,9 +584,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         pk[e / 2] = pack_bf16(p[0], p[1]);
         dk[e / 2] = pack_bf16(ds[0], ds[1]);
       }
-      store_row32(spt + s * L::kP, c_row, half * 32, pk, kBlk);
-      store_row32(sdst + s * L::kP, c_row, half * 32, dk, kBlk);
-      fence_proxy_async();
+      // P^T and dS^T back into this step's S^T / dP^T TMEM buffers (the first 16 columns
+      // of this warp's 32): the A operands of the dV / dK MMAs. The buffers are free: the
+      // MMAs that read the previous step of this parity were issued (in order) before the
+      // ones that filled S^T here, and the next MMAs that write them are issued after
+      // this step's dV / dK MMAs.
+      tmem_st16(tmem + s * kQs + lane_off + half * 32, pk);
+      tmem_st16(tmem + 128 + s * kQs + lane_off + half * 32, dk);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[s]);
@@ -756,11 +762,11 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           const int stp = p % ST;
           if (!mbar_wait(&ds_full[sp], (p >> 1) & 1, a.err, kErrMmaWait)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t ds_addr = smem_u32(sds + sp * L::kDs), k_addr = smem_u32(sk + stp * L::kKV);
+          const uint32_t k_addr = smem_u32(sk + stp * L::kKV);
           #pragma unroll
-          for (int kk = 0; kk < kKs / 16; ++kk)
-            umma_bf16(t_dq, smem_desc_sw128(ds_addr + kk * 32, 16, 1024),
-                      smem_desc_sw128(k_addr + kk * 2048, kKs * 128, 1024), id_dq, (p > 0 || kk > 0));
+          for (int kk = 0; kk < kKs / 16; ++kk)  // A = dS from TMEM (packed bf16, see below)
+            umma_bf16_ts(t_dq, tmem + uint32_t(sp * kKs + (kk >> 1) * 32 + (kk & 1) * 8),
+                         smem_desc_sw128(k_addr + kk * 2048, kKs * 128, 1024), id_dq, (p > 0 || kk > 0));
           umma_commit(&kv_empty[stp]);
           umma_commit(&ds_empty[sp]);
         }
@@ -792,7 +798,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
-      if (!mbar_wait(&ds_empty[s], n ^ 1, a.err, kErrEpiWait)) { ok = false; break; }
       uint32_t pk[16];
       #pragma unroll
       for (int e = 0; e < 32; e += 2) {
@@ -805,8 +810,11 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         }
         pk[e / 2] = pack_bf16(ds[0], ds[1]);
       }
-      store_row32(sds + s * L::kDs, r, half * 32, pk, kBlk);
-      fence_proxy_async();
+      // dS back into this sub-block's S TMEM buffer (the first 16 columns of this warp's
+      // 32), the A operand of the dQ MMA; buffer reuse is ordered by the MMA issue order
+      // as in the dK / dV kernel
+      tmem_st16(tmem + s * kKs + lane_off + half * 32, pk);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[s]);
