@@ -63,25 +63,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Byte offset of bf16 element (r, c) in a K-major 128B-swizzled tile made of 64-column
-// chunks of `rows` rows each.
-__device__ __forceinline__ uint32_t sw128_offset(int r, int c, int rows) {
-  const int chunk = c >> 6;
-  const int cc = c & 63;
-  const int unit = (cc >> 3) ^ (r & 7);
-  return uint32_t(chunk * rows * 128 + r * 128 + unit * 16 + (cc & 7) * 2);
-}
-
-// Write 32 consecutive columns (c0 .. c0+31, c0 % 32 == 0) of row r, given as 16 packed
-// bf16 pairs, into a swizzled K-major tile.
-__device__ __forceinline__ void store_row32(uint8_t* tile, int r, int c0, const uint32_t (&pk)[16], int rows) {
-  #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    uint4 v = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-    *reinterpret_cast<uint4*>(tile + sw128_offset(r, c0 + 8 * u, rows)) = v;
-  }
-}
-
 constexpr int kFwdThreads = 64 + 8 * 32;  // producer, MMA issuer, eight softmax warps
 
 template <int D>
@@ -188,7 +169,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kBlk, 0, 0);
       constexpr uint32_t id_o = idesc_bf16_f32(kBlk, D, 0, 1);
       const uint32_t q_addr = smem_u32(sq);
-      const uint32_t p_addr = smem_u32(sp);
       bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
       auto issue_pv = [&](int j) -> bool {
         const int st = j % ST;
@@ -198,9 +178,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t v_addr = smem_u32(sv + st * L::kKV);
         #pragma unroll
         for (int kk = 0; kk < kBlk / 16; ++kk) {
-          const uint64_t da = smem_desc_sw128(p_addr + (kk >> 2) * kBlk * 128 + (kk & 3) * 32, 16, 1024);
+          // A = P of block j from TMEM: packed bf16 in the first 32 columns of each
+          // 64-column half of S buffer j & 1 (8 columns per 16 kv)
+          const uint32_t pa = tmem + uint32_t((j & 1) * kBlk + (kk >> 2) * (kBlk / 2) + (kk & 3) * 8);
           const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, kBlk * 128, 1024);
-          umma_bf16(t_o, da, db, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(t_o, pa, db, id_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
         umma_commit(&v_empty[st]);
@@ -266,11 +248,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float mx = fmaxf(m, fmaxf(mloc, s_mx[(sb * 2 + (half ^ 1)) * kBlk + r]));
       const float alpha = fast_exp2((m - mx) * sl2);   // 0 on the first block (m = -inf)
       const float neg = mx * sl2;
-      // P smem is still being read by PV_{j-1}: wait for it before overwriting
-      if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; continue; }
-        tc_fence_after();
-      }
+      // P goes into this block's own S buffer in TMEM, so it does not wait for PV_{j-1}
       float rowsum = 0.f;
       #pragma unroll
       for (int c = 0; c < kHalf; c += 32) {
@@ -285,15 +263,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           rowsum += p0 + p1;
           pk[e / 2] = pack_bf16(p0, p1);
         }
-        store_row32(sp, r, half * kHalf + c, pk, kBlk);
+        // packed P over the S values this warp already holds in registers: the first 32
+        // columns of its 64-column half, the A operand of PV_j
+        tmem_st16(tmem + sb * kBlk + lane_off + half * kHalf + c / 2, pk);
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
       l = l * alpha + rowsum;
       m = mx;
       // rescale this half's columns of the running O when this warp saw the max grow
+      // (after PV_{j-1}, which accumulates into O, has completed)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; continue; }
+        tc_fence_after();
         #pragma unroll 1
         for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 16) {
           uint32_t w16[16];
@@ -305,7 +289,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         tmem_wait_st();
       }
-      fence_proxy_async();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
