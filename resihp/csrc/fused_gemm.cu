@@ -34,9 +34,9 @@
 //     then the peers' in rank order, in fp32, deterministically), many rows in flight.
 //     (The tile counters come in two banks by call parity: a fast source may already be
 //     contributing to the next call.)
-// AR: RS, where the copy warps also store each reduced own row into every peer's output
-//     landing zone and count it there (per row slice), then copy the other owners'
-//     tiles from there into y.
+// AR: RS, where the copy warps also stage each reduced slice of an own tile and bulk-push
+//     it into every peer's (tile-contiguous) output landing zone and count it there, then
+//     copy the other owners' tiles from there into y.
 //
 // Work is claimed dynamically -- output tiles by the producer, copy items by the copy
 // warps -- from per-call counters in the same global order on every rank (peer data
@@ -209,7 +209,7 @@ __device__ __forceinline__ void copy_rows(uint4* dst, int64_t dld, const uint4* 
 template <int MODE, int TP>
 __device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers& p, const __nv_bfloat16* recv_tile,
                                             int64_t src_stride, int tile_ld, int lrow0, int m0, int c0, int w, int lane,
-                                            int rbeg, int rend) {
+                                            int rbeg, int rend, __nv_bfloat16* ar_stage) {
   // TP: the group size, or 0 for any size up to kFusedMaxTp (one row at a time)
   constexpr int kSrc = TP > 0 ? TP : kFusedMaxTp;
   constexpr int kTpDiv = TP > 0 ? TP : 8;
@@ -259,12 +259,9 @@ __device__ __forceinline__ void reduce_rows(const FusedArgs& g, const FusedPeers
       const int lrow = lrow0 + r0 + rr;
       const int64_t yrow = MODE == kModeRS ? lrow : int64_t(m0 + r0 + rr);
       reinterpret_cast<uint4*>(y + yrow * g.ldc + c0)[lane] = o;
-      if (MODE == kModeAR) {
-        #pragma unroll
-        for (int r = 0; r < kFusedMaxTp; ++r)
-          if (r < p.tp && r != p.rank)
-            reinterpret_cast<uint4*>(p.out_land[r] + int64_t(m0 + r0 + rr) * g.n + c0)[lane] = o;
-      }
+      // AR: also into the own tile's (otherwise unused) slot of the send buffer, tile-
+      // contiguous, from where the slice is bulk-pushed to every peer
+      if (MODE == kModeAR) reinterpret_cast<uint4*>(ar_stage + int64_t(r0 + rr) * tile_ld)[lane] = o;
     }
   }
 }
@@ -274,14 +271,14 @@ template <int MODE>
 // recv + (src * per_chunk + lt) * tile_elems, rows tile_ld apart.
 __device__ __forceinline__ void reduce_own_tile(const FusedArgs& g, const FusedPeers& p, int lt, int per_chunk,
                                                 int tile_elems, int tile_ld, int lrow0, int m0, int c0, int ncols16,
-                                                int ct, int rbeg, int rend) {
+                                                int ct, int rbeg, int rend, __nv_bfloat16* ar_stage) {
   const int w = ct >> 5, lane = ct & 31;
   if (lane >= ncols16) return;
   const __nv_bfloat16* recv_tile = pick(p.recv, p.rank) + int64_t(lt) * tile_elems;
   const int64_t stride = int64_t(per_chunk) * tile_elems;
-  if (p.tp == 2) reduce_rows<MODE, 2>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
-  else if (p.tp == 4) reduce_rows<MODE, 4>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
-  else reduce_rows<MODE, 0>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend);
+  if (p.tp == 2) reduce_rows<MODE, 2>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend, ar_stage);
+  else if (p.tp == 4) reduce_rows<MODE, 4>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend, ar_stage);
+  else reduce_rows<MODE, 0>(g, p, recv_tile, stride, tile_ld, lrow0, m0, c0, w, lane, rbeg, rend, ar_stage);
 }
 
 // One thread: ``bytes`` (a multiple of 16) from this GPU's memory at ``src`` to ``dst`` (a
@@ -711,21 +708,39 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           // y (own partial) + every peer's partial, in rank order after the own one; AR:
           // the sum also goes to every peer's output landing zone
           const int slice_rows = kFBM / red;
+          __nv_bfloat16* ar_stage = p.send + int64_t(gtile) * S::kTileElems;  // the own tile's send slot
           reduce_own_tile<MODE>(g, p, local_tile, per_chunk, S::kTileElems, BN, m0 - chunk * rpr, m0, tn * BN, ncols16,
-                                ct, slice * slice_rows, (slice + 1) * slice_rows);
+                                ct, slice * slice_rows, (slice + 1) * slice_rows, ar_stage);
           if (MODE == kModeAR) {
-            __threadfence_system();
+            // the reduced slice (contiguous rows of the tile-contiguous stage) to every
+            // peer's output landing zone (same layout) by bulk copies, then counted there
+            fence_proxy_async_global();  // this thread's stage writes, before the TMA reads them
             copy_bar();
             if (ct == 0) {
-              #pragma unroll
-              for (int r = 0; r < kFusedMaxTp; ++r)
-                if (r < p.tp && r != p.rank) red_release_add(p.ar_cnt[r] + gtile, 1u);
+              bool pushed = true;
+              const int64_t off = int64_t(gtile) * S::kTileElems + int64_t(slice) * slice_rows * BN;
+              #pragma unroll 1
+              for (int r = 0; r < p.tp && pushed; ++r)
+                if (r != p.rank)
+                  pushed = bulk_push(bstage, bbar, bphase, reinterpret_cast<uint8_t*>(pick(p.out_land, r) + off),
+                                     reinterpret_cast<const uint8_t*>(p.send + off), int64_t(slice_rows) * BN * 2,
+                                     g.err);
+              if (pushed) {
+                #pragma unroll
+                for (int r = 0; r < kFusedMaxTp; ++r)
+                  if (r < p.tp && r != p.rank) red_release_add(p.ar_cnt[r] + gtile, 1u);
+              }
+              claim[1] = pushed;
             }
+            copy_bar();
+            ok = claim[1] != 0;
+            copy_bar();
           }
         } else {
+          // another owner's reduced tile: tile-contiguous landing zone -> rows of y
           copy_rows(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(g.c) + int64_t(m0) * g.ldc + tn * BN),
-                    g.ldc / 8, reinterpret_cast<const uint4*>(pick(p.out_land, p.rank) + int64_t(m0) * g.n + tn * BN),
-                    g.n / 8, kFBM, ncols16, ct, g.err);
+                    g.ldc / 8, reinterpret_cast<const uint4*>(pick(p.out_land, p.rank) + int64_t(gtile) * S::kTileElems),
+                    BN / 8, kFBM, ncols16, ct, g.err);
         }
       }
       if (ct == 0 && nclaim < 8) FUSED_STAMP(11 + 2 * nclaim, globaltimer());

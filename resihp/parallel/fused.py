@@ -77,8 +77,9 @@ class SymmetricWorkspace:
 
     Layout (bytes): counter words (176 KB) | two AG landing zones ``[T, width]`` | two RS
     receive buffers (``[tp][T/128 tiles of this rank's chunk][128 x 256]``, tile-contiguous)
-    | two AR output landing zones ``[T, width]`` | the RS send buffer (``[T/128 x
-    tiles_n][128 x 256]``, local: partial tiles before the copy warps push them whole).
+    | two AR output landing zones (``[T/128 x tiles_n][128 x 256]``, tile-contiguous) |
+    the RS send buffer (same tiles, local: partial tiles before the copy warps push them
+    whole; the AR stages its reduced own tiles there).
     Every fused call's gathered input, reduced output and all-reduced output has the
     model width, so one region serves all projections of a layer and their backward.
     """

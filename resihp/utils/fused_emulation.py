@@ -65,8 +65,13 @@ class Emulation:
         tiles = (self.rpr // 128) * (-(-n // 256))
         return self.buf(rank, self.recv_off, parity, (self.tp * tiles * 128, 256)).view(self.tp, tiles, 128, 256)
 
+    def out_tiles(self, rank, parity, n):
+        """Rank ``rank``'s AR output landing zone as ``[T/128 x tiles_n, 128, 256]`` tiles."""
+        tiles = (self.t // 128) * (-(-n // 256))
+        return self.buf(rank, self.out_off, parity, (tiles * 128, 256)).view(tiles, 128, 256)
+
     def to_tiles(self, rows_x_n):
-        """``[rpr, n]`` rows as the kernels' tile-contiguous ``[tiles, 128, 256]`` (tile =
+        """``[rows, n]`` rows as the kernels' tile-contiguous ``[tiles, 128, 256]`` (tile =
         128-row block major, then 256-column block; columns past n zero)."""
         r, n = rows_x_n.shape
         tn = -(-n // 256)
@@ -138,9 +143,9 @@ class Emulation:
         full = parts[0].clone()
         for src in range(1, self.tp):
             full += parts[src].bfloat16().float()
-        for parity in range(2):
-            out = self.buf(0, self.out_off, parity, (self.t, n))
-            out[self.rpr:].copy_(full[self.rpr:].bfloat16())
+        per_chunk = (self.rpr // 128) * (-(-n // 256))
+        for parity in range(2):  # every other owner's reduced tiles, tile-contiguous
+            self.out_tiles(0, parity, n)[per_chunk:].copy_(self.to_tiles(full.bfloat16())[per_chunk:])
         return full
 
     def gemm_reduce_scatter(self, h, w, *, w_mn=False):

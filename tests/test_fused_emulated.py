@@ -97,7 +97,7 @@ def test_emulated_gemm_rs_ar(tp, all_reduce):
             bank = em.u32(owner, fused._RS_CNT, 2 * fused.MAX_TILES).view(2, fused.MAX_TILES)[call % 2]
             assert torch.equal(bank[:per_chunk].cpu(), torch.full((per_chunk,), 1, dtype=torch.int32))
             if all_reduce:
-                out = em.buf(owner, em.out_off, parity, (T, N))
+                out = em.from_tiles(em.out_tiles(owner, parity, N), N)  # tile-contiguous landing zone
                 assert torch.equal(out[:em.rpr], y[:em.rpr])  # rank 0's reduced rows pushed to every peer
                 arc = em.u32(owner, fused._AR_CNT, fused.MAX_TILES)
                 grid = em.kx.fused_grid(T, N, tp)
