@@ -339,12 +339,17 @@ class TensorParallelStage:
             return cc.column_parallel_linear(h, w, g, self.group, self.sp)
         return fn.linear(h, w, g)
 
-    def _row_linear(self, x, w, g):
-        """Row-parallel linear; its collective (SP: the token reduce-scatter; otherwise the
-        output all-reduce) is fused into the GEMM on the kernel path."""
+    def _row_linear(self, x, w, g, residual=None):
+        """Row-parallel linear (+ ``residual``); its collective (SP: the token
+        reduce-scatter; otherwise the output all-reduce) is fused into the GEMM on the
+        kernel path. Without TP the residual add is the GEMM's epilogue."""
         if self.ws is not None:
-            return fused.linear_rs(x, w, g, self.ws) if self.sp else fused.row_linear_ar(x, w, g, self.ws)
-        return self._row_output(fn.linear(x, w, g))
+            y = fused.linear_rs(x, w, g, self.ws) if self.sp else fused.row_linear_ar(x, w, g, self.ws)
+        elif self.tp_size == 1:
+            return fn.linear(x, w, g, residual=residual)
+        else:
+            y = self._row_output(fn.linear(x, w, g))
+        return y if residual is None else residual + y
 
     def _row_output(self, y):
         return cc.scatter_tokens(y, self.group) if self.sp else cc.reduce_from_tp(y, self.group)
@@ -371,7 +376,7 @@ class TensorParallelStage:
         h, x = fn.rmsnorm(a, self.w[p + "mlp_norm.weight"], c.norm_eps, self.g[p + "mlp_norm.weight"], residual=x)
         wgu, ggu = self.fused_w[p + "gate_up"]
         gu = self._col_linear(h, wgu, ggu)
-        return x + self._row_linear(fn.swiglu(gu), self.w[p + "mlp.down.weight"], self.g[p + "mlp.down.weight"])
+        return self._row_linear(fn.swiglu(gu), self.w[p + "mlp.down.weight"], self.g[p + "mlp.down.weight"], residual=x)
 
     def _gpt2_layer(self, x, gid):
         p = f"layers.{gid}."
