@@ -63,6 +63,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Row ``r`` of 64-column chunk ``chunk`` of a K-major 128B-swizzled bf16 tile with
+// ``rows`` rows (TMA layout: 16-byte unit u of row r sits at unit u ^ (r & 7)) into 32
+// TMEM columns at ``taddr`` (this warp's lanes), as packed bf16 pairs in column order:
+// the layout of an MMA A operand read from tensor memory.
+__device__ __forceinline__ void sw128_row_to_tmem(const uint8_t* tile, int rows, int chunk, int r, uint32_t taddr) {
+  const uint8_t* row = tile + (chunk * rows + r) * 128;
+  uint32_t w[32];
+  #pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const uint4 v = *reinterpret_cast<const uint4*>(row + ((u ^ (r & 7)) * 16));
+    w[4 * u] = v.x;
+    w[4 * u + 1] = v.y;
+    w[4 * u + 2] = v.z;
+    w[4 * u + 3] = v.w;
+  }
+  tmem_st16(taddr, *reinterpret_cast<const uint32_t(*)[16]>(w));
+  tmem_st16(taddr + 16, *reinterpret_cast<const uint32_t(*)[16]>(w + 16));
+}
+
 constexpr int kFwdThreads = 64 + 8 * 32;  // producer, MMA issuer, eight softmax warps
 
 template <int D>
@@ -659,7 +678,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   uint64_t* ds_full = s_empty + 2;           // [2] dS of a sub-block in smem
   uint64_t* ds_empty = ds_full + 2;          // [2] the dQ MMA reading it is done
   uint64_t* dq_done = ds_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_done + 1);
+  uint64_t* qo_tmem = dq_done + 1;           // Q and dO copied into TMEM (the S / dP A operands)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qo_tmem + 1);
 
   const int qblk = (a.seq / kBlk) - 1 - blockIdx.z;   // slowest grid dimension: heaviest first
   const int h = blockIdx.x;
@@ -682,6 +702,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       mbar_init(&ds_empty[s], 1);
     }
     mbar_init(dq_done, 1);
+    mbar_init(qo_tmem, kEwWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -689,8 +710,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S[2] 0 / 64, dP[2] 128 / 192, dQ 256..
-  const uint32_t t_dq = tmem + 256;
+  // TMEM columns: S[2] 0 / 64, dP[2] 128 / 192, dQ 256..383, Q 384..447, dO 448..511
+  // (Q and dO as packed bf16: the A operands of every S and dP MMA, read from TMEM
+  // instead of shared memory)
+  const uint32_t t_dq = tmem + 256, t_q = tmem + 384, t_do = tmem + 448;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -718,8 +741,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_bf16_f32(kBlk, kKs, 0, 0);
       constexpr uint32_t id_dq = idesc_bf16_f32(kBlk, D, 0, 1);
-      const uint32_t q_addr = smem_u32(sq), do_addr = smem_u32(sdo);
-      bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
+      bool ok = mbar_wait(qo_tmem, 0, a.err, kErrMmaWait);  // Q, dO landed and copied into TMEM
       for (int j = 0; j <= nkv && ok; ++j) {
         if (j < nkv) {
           const int st = j % ST;
@@ -730,12 +752,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           const uint32_t k_addr = smem_u32(sk + st * L::kKV), v_addr = smem_u32(sv + st * L::kKV);
           #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t oq = (kk >> 2) * kBlk * 128 + (kk & 3) * 32;
             const uint32_t okv = (kk >> 2) * kKs * 128 + (kk & 3) * 32;
-            umma_bf16(tmem + s * kKs, smem_desc_sw128(q_addr + oq, 16, 1024), smem_desc_sw128(k_addr + okv, 16, 1024),
-                      id_s, kk > 0);
-            umma_bf16(tmem + 128 + s * kKs, smem_desc_sw128(do_addr + oq, 16, 1024),
-                      smem_desc_sw128(v_addr + okv, 16, 1024), id_s, kk > 0);
+            umma_bf16_ts(tmem + s * kKs, t_q + kk * 8, smem_desc_sw128(k_addr + okv, 16, 1024), id_s, kk > 0);
+            umma_bf16_ts(tmem + 128 + s * kKs, t_do + kk * 8, smem_desc_sw128(v_addr + okv, 16, 1024), id_s,
+                         kk > 0);
           }
           umma_commit(&s_full[s]);
         }
@@ -766,7 +786,16 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     const int64_t stat = (int64_t(b) * a.hq + h) * a.seq + q_pos;
     const float lse2 = a.lse[stat] * kLog2e;
     const float dlt = a.delta[stat];
-    bool ok = true;
+    bool ok = mbar_wait(q_full, 0, a.err, kErrEpiWait);
+    if (ok) {
+      // this warp's half of its rows of Q and dO, from the swizzled tiles into TMEM
+      sw128_row_to_tmem(sq, kBlk, half, r, t_q + lane_off + half * 32);
+      sw128_row_to_tmem(sdo, kBlk, half, r, t_do + lane_off + half * 32);
+      tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(qo_tmem);
     for (int j = 0; j < nkv; ++j) {
       const int s = j & 1;
       const uint32_t n = (j >> 1) & 1;
