@@ -15,10 +15,10 @@
 //               PV_j so the tensor core works while softmax runs)
 //   warps 2-9   softmax, two threads per query row (the two warps of a TMEM lane
 //               quadrant take 64 columns each and exchange the row maximum through
-//               shared memory): P = exp2(S * scale*log2e - m), P written as bf16 into a
-//               128B-swizzled smem tile (the A operand of PV), each half of O rescaled
-//               in TMEM when the max grows, finally O / l stored as bf16 and the
-//               log-sum-exp kept for backward.
+//               shared memory): P = exp2(S * scale*log2e - m), P written back as packed
+//               bf16 into its own S buffer in TMEM (the A operand of PV, read from
+//               TMEM), each half of O rescaled in TMEM when the max grows (after the
+//               previous PV), finally O / l stored as bf16 and the log-sum-exp kept.
 // Backward (deterministic, no atomics):
 //   attn_bwd_dkdv  one CTA per (kv block, kv head, batch), looping over every q head of
 //                  the group and every causal q block: S^T = K Q^T, dP^T = V dO^T,
@@ -27,8 +27,8 @@
 //   attn_bwd_dq    one CTA per (q block, q head, batch): S, dP recomputed, dQ += dS K.
 //   Both run the kv (dK/dV) or q (dQ) side in sub-blocks of 64 rows with double-buffered
 //   TMEM scores and eight elementwise warps (see the kernels).
-//   The same smem tile of dS^T serves as K-major A (for dK) -- and the dQ kernel writes
-//   its own dS tile K-major for dQ += dS K.
+//   P^T / dS^T (and dS in the dQ kernel) go back into their score buffers in TMEM as
+//   packed bf16 and are the A operands of the dV / dK (dQ) MMAs, read from TMEM.
 // All waits are bounded (common.cuh) and report into the error word.
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -89,9 +89,8 @@ struct FwdSmem {
   static constexpr int kQ = kBlk * D * 2;
   static constexpr int kKV = kBlk * D * 2;
   static constexpr int kStages = 2;
-  static constexpr int kP = kBlk * kBlk * 2;
   static constexpr int kMx = 6 * kBlk * 4;   // row-max exchange [2 blocks][2 halves][128], row-sum [2][128]
-  static constexpr int kBytes = kQ + 2 * kStages * kKV + kP + kMx + 1024 + 256;
+  static constexpr int kBytes = kQ + 2 * kStages * kKV + kMx + 1024 + 256;
 };
 
 template <int D>
@@ -105,9 +104,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* sq = smem;
   uint8_t* sk = sq + L::kQ;                 // ST stages of K
   uint8_t* sv = sk + ST * L::kKV;           // ST stages of V
-  uint8_t* sp = sv + ST * L::kKV;
-  float* s_mx = reinterpret_cast<float*>(sp + L::kP);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + L::kP + L::kMx);
+  float* s_mx = reinterpret_cast<float*>(sv + ST * L::kKV);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + ST * L::kKV + L::kMx);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + ST;
@@ -388,15 +386,15 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t o
 // group and every causal q sub-block of 64 rows. Sixty-four q rows per step keep
 // S^T / dP^T small enough (2 x 64 TMEM columns each) to double-buffer next to the dV and
 // dK accumulators; Q / dO / lse / delta come through a three-stage ring (their loads run
-// two steps ahead, off the critical path) and the P^T / dS^T tiles are double-buffered in
-// shared memory, so step i+1's S^T and dP^T MMAs run while the elementwise warps turn
+// two steps ahead, off the critical path) and P^T / dS^T go back into the step's TMEM
+// score buffers, so step i+1's S^T and dP^T MMAs run while the elementwise warps turn
 // step i into P^T and dS^T, and step i's dV / dK MMAs run while they do step i+1:
 //   warp 0      TMA: K, V once; then Q_i, dO_i (64 rows) and their lse / delta rows
 //   warp 1      MMA: S^T_i = K Q_i^T, dP^T_i = V dO_i^T (128 x 64), then dV += P^T_{i-1} dO_{i-1},
 //               dK += dS^T_{i-1} Q_{i-1} (128 x D)
 //   warps 2-9   elementwise, two warps per TMEM lane quadrant (32 q columns each):
 //               P^T = exp2(S^T * scale*log2e - lse*log2e) (causal mask on the diagonal),
-//               dS^T = P^T (dP^T - Delta), both as bf16 into 128B-swizzled K-major tiles.
+//               dS^T = P^T (dP^T - Delta), both as packed bf16 into TMEM.
 constexpr int kQs = 64;             // q rows per dK/dV step
 constexpr int kQdStages = 3;        // Q / dO / lse / delta ring: loads run two steps ahead
 constexpr int kEwWarps = 8;         // elementwise warps
@@ -406,8 +404,7 @@ template <int D>
 struct DkdvSmem {
   static constexpr int kKV = kBlk * D * 2;   // K or V tile
   static constexpr int kQ = kQs * D * 2;     // one Q or dO tile of 64 rows
-  static constexpr int kP = kBlk * kQs * 2;  // one P^T or dS^T tile [128 kv, 64 q]
-  static constexpr int kBytes = 2 * kKV + 2 * kQdStages * kQ + 4 * kP + 2 * kQdStages * kQs * 4 + 1024 + 256;
+  static constexpr int kBytes = 2 * kKV + 2 * kQdStages * kQ + 2 * kQdStages * kQs * 4 + 1024 + 256;
 };
 
 
@@ -424,9 +421,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   constexpr int QS = kQdStages;
   uint8_t* sq = sv + L::kKV;          // QS stages
   uint8_t* sdo = sq + QS * L::kQ;     // QS stages
-  uint8_t* spt = sdo + QS * L::kQ;    // 2 stages of P^T  [kv, q] K-major
-  uint8_t* sdst = spt + 2 * L::kP;    // 2 stages of dS^T [kv, q] K-major
-  float* s_lse = reinterpret_cast<float*>(sdst + 2 * L::kP);   // [QS][kQs]
+  float* s_lse = reinterpret_cast<float*>(sdo + QS * L::kQ);  // [QS][kQs]
   float* s_delta = s_lse + QS * kQs;                            // [QS][kQs]
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + QS * kQs);
   uint64_t* kv_full = bars;
@@ -434,9 +429,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   uint64_t* qd_empty = qd_full + QS;     // [QS] the dV/dK MMAs reading that step's Q, dO are done
   uint64_t* st_full = qd_empty + QS;     // [2] S^T, dP^T of a step in TMEM
   uint64_t* st_empty = st_full + 2;      // [2] the elementwise warps read them
-  uint64_t* ds_full = st_empty + 2;      // [2] P^T, dS^T of a step in smem
-  uint64_t* ds_empty = ds_full + 2;      // [2] the dV/dK MMAs reading them are done
-  uint64_t* acc_done = ds_empty + 2;
+  uint64_t* ds_full = st_empty + 2;      // [2] P^T, dS^T of a step back in TMEM
+  uint64_t* acc_done = ds_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
 
   const int kvblk = blockIdx.z;  // slowest grid dimension: the longest causal ranges go first
@@ -458,7 +452,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       mbar_init(&st_full[s], 1);
       mbar_init(&st_empty[s], kEwWarps);
       mbar_init(&ds_full[s], kEwWarps);
-      mbar_init(&ds_empty[s], 1);
     }
     mbar_init(acc_done, 1);
     fence_barrier_init();
@@ -539,7 +532,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
                          (p > 0 || kk > 0));
           }
           umma_commit(&qd_empty[sp3]);
-          umma_commit(&ds_empty[sp]);
         }
       }
       if (ok) umma_commit(acc_done);
@@ -637,8 +629,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 //
 // One CTA per (q block of 128 rows, q head, batch), looping over the causal kv range in
 // sub-blocks of 64 rows, mirroring the dK/dV kernel: S_j / dP_j (128 x 64) double-buffered
-// in TMEM next to the dQ accumulator, K_j / V_j in a three-stage ring and the dS tiles
-// double-buffered in shared memory, so the MMAs of one sub-block overlap the elementwise
+// in TMEM next to the dQ accumulator, K_j / V_j in a three-stage ring and dS written back
+// into the sub-block's S buffer, so the MMAs of one sub-block overlap the elementwise
 // work of the previous one:
 //   warp 0      TMA: Q, dO once; K_j, V_j (64 rows) into the ring
 //   warp 1      MMA: S_j = Q K_j^T, dP_j = dO V_j^T, then dQ += dS_{j-1} K_{j-1}
@@ -651,8 +643,7 @@ template <int D>
 struct DqSmem {
   static constexpr int kT = kBlk * D * 2;    // Q or dO tile
   static constexpr int kKV = kKs * D * 2;    // one K or V tile of 64 rows
-  static constexpr int kDs = kBlk * kKs * 2; // one dS tile [128 q, 64 kv]
-  static constexpr int kBytes = 2 * kT + 2 * kDqStages * kKV + 2 * kDs + 1024 + 256;
+  static constexpr int kBytes = 2 * kT + 2 * kDqStages * kKV + 1024 + 256;
 };
 
 template <int D>
@@ -668,16 +659,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   uint8_t* sdo = sq + L::kT;
   uint8_t* sk = sdo + L::kT;           // ST stages
   uint8_t* sv = sk + ST * L::kKV;      // ST stages
-  uint8_t* sds = sv + ST * L::kKV;     // 2 stages of dS [q, kv] K-major
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sds + 2 * L::kDs);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + ST * L::kKV);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;              // [ST]
   uint64_t* kv_empty = kv_full + ST;         // [ST]
   uint64_t* s_full = kv_empty + ST;          // [2] S, dP of a sub-block in TMEM
   uint64_t* s_empty = s_full + 2;            // [2] the elementwise warps read them
-  uint64_t* ds_full = s_empty + 2;           // [2] dS of a sub-block in smem
-  uint64_t* ds_empty = ds_full + 2;          // [2] the dQ MMA reading it is done
-  uint64_t* dq_done = ds_empty + 2;
+  uint64_t* ds_full = s_empty + 2;           // [2] dS of a sub-block back in TMEM
+  uint64_t* dq_done = ds_full + 2;
   uint64_t* qo_tmem = dq_done + 1;           // Q and dO copied into TMEM (the S / dP A operands)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qo_tmem + 1);
 
@@ -699,7 +688,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], kEwWarps);
       mbar_init(&ds_full[s], kEwWarps);
-      mbar_init(&ds_empty[s], 1);
     }
     mbar_init(dq_done, 1);
     mbar_init(qo_tmem, kEwWarps);
@@ -771,7 +759,6 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
             umma_bf16_ts(t_dq, tmem + uint32_t(sp * kKs + (kk >> 1) * 32 + (kk & 1) * 8),
                          smem_desc_sw128(k_addr + kk * 2048, kKs * 128, 1024), id_dq, (p > 0 || kk > 0));
           umma_commit(&kv_empty[stp]);
-          umma_commit(&ds_empty[sp]);
         }
       }
       if (ok) umma_commit(dq_done);
