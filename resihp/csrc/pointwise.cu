@@ -182,6 +182,24 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// AdamW four elements per thread (16-byte fp32 accesses, 8-byte bf16 store): the same
+// per-element arithmetic as adamw_kernel.
+__global__ void adamw_vec_kernel(float4* __restrict__ p, const float4* __restrict__ g, float4* __restrict__ m,
+                                 float4* __restrict__ v, uint2* __restrict__ p_bf16, int64_t n4, AdamWCoef c) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+    float4 pi = p[i], mi = m[i], vi = v[i];
+    const float4 gi = g[i];
+    adamw_elem(pi.x, mi.x, vi.x, gi.x, c);
+    adamw_elem(pi.y, mi.y, vi.y, gi.y, c);
+    adamw_elem(pi.z, mi.z, vi.z, gi.z, c);
+    adamw_elem(pi.w, mi.w, vi.w, gi.w, c);
+    p[i] = pi;
+    m[i] = mi;
+    v[i] = vi;
+    if (p_bf16 != nullptr) p_bf16[i] = make_uint2(pack_bf16(pi.x, pi.y), pack_bf16(pi.z, pi.w));
+  }
+}
+
 // out[t, :] = W[id_t - start, :] if the id falls in this rank's vocab shard, else 0.
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
                                      __nv_bfloat16* __restrict__ out, int rows, int d, int64_t start, int64_t count) {
@@ -332,6 +350,15 @@ AdamWCoef adamw_coef(float lr, float b1, float b2, float eps, float wd, int64_t 
 void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n, float lr, float b1, float b2,
            float eps, float wd, int64_t step, float grad_scale, int num_sms, cudaStream_t st) {
   const AdamWCoef c = adamw_coef(lr, b1, b2, eps, wd, step, grad_scale);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
+                       reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v);
+  if (n % 4 == 0 && al % 16 == 0 && reinterpret_cast<uintptr_t>(p_bf16) % 8 == 0) {
+    adamw_vec_kernel<<<grid_for(n / 4, 256, num_sms), 256, 0, st>>>(
+        reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
+        reinterpret_cast<float4*>(v), static_cast<uint2*>(p_bf16), n / 4, c);
+    RESIHP_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   adamw_kernel<<<grid_for(n, 256, num_sms), 256, 0, st>>>(p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, c);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }

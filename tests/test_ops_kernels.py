@@ -109,9 +109,9 @@ def test_cross_entropy():
     assert _rel(lg.grad.cpu(), ref_l.grad) < 2e-2
 
 
-def test_adamw_flat_matches_cpu():
+@pytest.mark.parametrize("n", [100_003, 100_000])  # scalar kernel; four-wide kernel
+def test_adamw_flat_matches_cpu(n):
     torch.manual_seed(0)
-    n = 100_003
     p = torch.randn(n)
     g = torch.randn(n)
     m = torch.zeros(n)
