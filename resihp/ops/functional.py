@@ -79,6 +79,8 @@ class _RMSNorm(Function):
     @staticmethod
     def forward(ctx, x, residual, w, main_grad, eps):
         y, s, rstd = _k().rmsnorm_fwd(x, residual, w, eps)
+        # An unused second output gets no gradient (None), not a materialised zero tensor.
+        ctx.set_materialize_grads(False)
         ctx.save_for_backward(s, w, rstd)
         ctx.main_grad = main_grad
         ctx.has_residual = residual is not None
@@ -89,12 +91,19 @@ class _RMSNorm(Function):
         s, w, rstd = ctx.saved_tensors
         dw = ctx.main_grad if ctx.main_grad is not None else torch.zeros(w.shape, dtype=torch.float32, device=w.device)
         dres = None if ds_out is None else ds_out.contiguous()
+        if dy is None:  # only the sum output was used
+            return dres, (dres if ctx.has_residual else None), None, None, None
         ds = _k().rmsnorm_bwd(dy.contiguous(), s, w, rstd, dres, dw, True)
         return ds, (ds if ctx.has_residual else None), None, None, None
 
 
 def rmsnorm(x, w, eps, main_grad=None, residual=None):
-    """``(rmsnorm(x + residual) * w, x + residual)``; without a residual the second output is ``x``."""
+    """``(rmsnorm(x + residual) * w, x + residual)``; without a residual the second output is ``x``.
+
+    On the kernels the gradient arriving at the second output is added inside the
+    backward kernel, so a stream that feeds both this norm and a later residual add
+    should take the second output as that residual (one gradient sum, no extra pass).
+    """
     if not on_kernels(x):
         s = x if residual is None else x + residual
         rstd = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)

@@ -368,7 +368,9 @@ class TensorParallelStage:
         c = self.config
         p = f"layers.{gid}."
         hq, hkv = c.num_heads // self.tp_size, c.kv_heads // self.tp_size
-        h, _ = fn.rmsnorm(x, self.w[p + "attn_norm.weight"], c.norm_eps, self.g[p + "attn_norm.weight"])
+        # The residual stream leaves through the norm's second output, so its gradient
+        # from the MLP-norm residual is summed inside the norm's backward kernel.
+        h, x = fn.rmsnorm(x, self.w[p + "attn_norm.weight"], c.norm_eps, self.g[p + "attn_norm.weight"])
         wqkv, gqkv = self.fused_w[p + "qkv"]
         qkv = self._col_linear(h, wqkv, gqkv)
         o = fn.rope_attention(qkv, self.rope, c.seq_len, hq, hkv, c.head_dim)
