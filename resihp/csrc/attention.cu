@@ -96,6 +96,7 @@ struct FwdSmem {
 template <int D>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  pdl_enter();
   using L = FwdSmem<D>;
   constexpr int ST = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -348,6 +349,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // Delta[b, h, s] = sum_d dO * O  (fp32)
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t o_ld, const __nv_bfloat16* __restrict__ dout,
                                   int64_t do_ld, float* __restrict__ delta, int rows, int seq, int hq, int d) {
+  pdl_enter();
   // eight lanes per (token, head): 16-byte loads, a three-step shuffle reduction
   const int lane = threadIdx.x & 31;
   const int idx = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 4 + (lane >> 3);
@@ -412,6 +414,7 @@ template <int D>
 __global__ void __launch_bounds__(kDkdvThreads, 1)
     attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
+  pdl_enter();
   using L = DkdvSmem<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -650,6 +653,7 @@ template <int D>
 __global__ void __launch_bounds__(kDkdvThreads, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_kv64, AttnArgs a) {
+  pdl_enter();
   using L = DqSmem<D>;
   constexpr int ST = kDqStages;
   extern __shared__ uint8_t smem_raw[];
@@ -867,10 +871,10 @@ void attn_fwd(const void* qkv, int64_t qkv_ld, void* out, int64_t out_ld, float*
   dim3 grid(hq, rows / seq, seq / kBlk);
   if (d == 128) {
     set_smem(attn_fwd_kernel<128>, FwdSmem<128>::kBytes);
-    attn_fwd_kernel<128><<<grid, kFwdThreads, FwdSmem<128>::kBytes, st>>>(tm, a);
+    launch_pdl(attn_fwd_kernel<128>, grid, kFwdThreads, FwdSmem<128>::kBytes, st, tm, a);
   } else {
     set_smem(attn_fwd_kernel<64>, FwdSmem<64>::kBytes);
-    attn_fwd_kernel<64><<<grid, kFwdThreads, FwdSmem<64>::kBytes, st>>>(tm, a);
+    launch_pdl(attn_fwd_kernel<64>, grid, kFwdThreads, FwdSmem<64>::kBytes, st, tm, a);
   }
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
@@ -882,7 +886,7 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
   RESIHP_CHECK(dqkv_ld == int64_t(hq + 2 * hkv) * d, "dqkv must be dense");
   {
     const int warps = rows * hq;
-    attn_delta_kernel<<<((warps + 3) / 4 * 32 + 255) / 256, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(out), out_ld,
+    launch_pdl(attn_delta_kernel, ((warps + 3) / 4 * 32 + 255) / 256, 256, 0, st, static_cast<const __nv_bfloat16*>(out), out_ld,
                                                                 static_cast<const __nv_bfloat16*>(dout), dout_ld,
                                                                 delta, rows, seq, hq, d);
     RESIHP_CUDA_CHECK(cudaGetLastError());
@@ -899,16 +903,16 @@ void attn_bwd(const void* qkv, int64_t qkv_ld, const void* out, int64_t out_ld, 
   dim3 grid_q(hq, rows / seq, seq / kBlk);
   if (d == 128) {
     set_smem(attn_bwd_dkdv_kernel<128>, DkdvSmem<128>::kBytes);
-    attn_bwd_dkdv_kernel<128><<<grid_kv, kDkdvThreads, DkdvSmem<128>::kBytes, st>>>(tm, tm_q64, tm_do64, a);
+    launch_pdl(attn_bwd_dkdv_kernel<128>, grid_kv, kDkdvThreads, DkdvSmem<128>::kBytes, st, tm, tm_q64, tm_do64, a);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     set_smem(attn_bwd_dq_kernel<128>, DqSmem<128>::kBytes);
-    attn_bwd_dq_kernel<128><<<grid_q, kDkdvThreads, DqSmem<128>::kBytes, st>>>(tm, tm_do, tm_q64, a);
+    launch_pdl(attn_bwd_dq_kernel<128>, grid_q, kDkdvThreads, DqSmem<128>::kBytes, st, tm, tm_do, tm_q64, a);
   } else {
     set_smem(attn_bwd_dkdv_kernel<64>, DkdvSmem<64>::kBytes);
-    attn_bwd_dkdv_kernel<64><<<grid_kv, kDkdvThreads, DkdvSmem<64>::kBytes, st>>>(tm, tm_q64, tm_do64, a);
+    launch_pdl(attn_bwd_dkdv_kernel<64>, grid_kv, kDkdvThreads, DkdvSmem<64>::kBytes, st, tm, tm_q64, tm_do64, a);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     set_smem(attn_bwd_dq_kernel<64>, DqSmem<64>::kBytes);
-    attn_bwd_dq_kernel<64><<<grid_q, kDkdvThreads, DqSmem<64>::kBytes, st>>>(tm, tm_do, tm_q64, a);
+    launch_pdl(attn_bwd_dq_kernel<64>, grid_q, kDkdvThreads, DqSmem<64>::kBytes, st, tm, tm_do, tm_q64, a);
   }
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }

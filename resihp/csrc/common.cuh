@@ -8,6 +8,7 @@
 // reference, which runs library kernels only.)
 #pragma once
 #include <cstdint>
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -76,6 +77,45 @@ __device__ __forceinline__ bool tmem_span_ok(uint32_t taddr, uint32_t base, uint
                                              int* err) {
   const uint32_t col = (taddr & 0xFFFFu) - (base & 0xFFFFu);
   return bounds_ok((taddr >> 16) < 128u && col + width <= ncols, err);
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------
+// A kernel launched by launch_pdl may be scheduled while the previous kernel of its stream
+// is still finishing (its launch and CTA placement overlap that kernel's tail), so every
+// such kernel begins with pdl_enter(): griddepcontrol.wait blocks until the previous
+// kernel has completed and its memory operations are visible (before this kernel touches
+// global memory), then griddepcontrol.launch_dependents lets the next kernel of the
+// stream be scheduled the same way. Launched normally, both instructions do nothing.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// RESIHP_PDL=0 launches every kernel with full stream serialisation instead.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("RESIHP_PDL");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
+// <<<grid, block, smem, st>>> with programmatic stream serialisation allowed (the kernel
+// must start with pdl_enter()); the launch error is returned, not raised.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // ---- mbarrier ------------------------------------------------------------------------

@@ -129,6 +129,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& g, int row, int col0
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
+  pdl_enter();
   using S = GemmShape<BN>;
   constexpr int kStages = S::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -301,6 +302,7 @@ struct PairShape {
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
+  pdl_enter();
   using S = PairShape;
   constexpr int kStages = kPairStages;
   extern __shared__ uint8_t smem_raw[];
@@ -516,7 +518,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   }
   const int tiles = ((g.m + kBM - 1) / kBM) * ((g.n + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kernel<<<grid, 192, S::kSmem, stream>>>(ta, tb, g);
+  launch_pdl(kernel, grid, 192, S::kSmem, stream, ta, tb, g);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -530,11 +532,13 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   using S = PairShape;
   auto kernel = gemm_pair_kernel<A_MN, B_MN, EPI>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel starts with pdl_enter()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = S::kSmem;
   cfg.stream = stream;
@@ -558,6 +562,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   int pairs = std::min(tiles, max_pairs[dev]);
   if (max_ctas > 0) pairs = std::min(pairs, std::max(1, max_ctas / 2));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   RESIHP_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, ta, tb, g));
 }
 

@@ -70,6 +70,7 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ s_out, float* __restrict__ rstd_out, int rows, int d,
                                    float eps) {
+  pdl_enter();
   __shared__ float scratch[32];
   const int lanes = d / 8;
   const int rows_per_block = blockDim.x / lanes;
@@ -112,6 +113,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                    const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ ds,
                                    float* __restrict__ dw_partial, int rows, int d) {
+  pdl_enter();
   __shared__ float scratch[32];
   const int lanes = d / 8;
   const int rows_per_block = blockDim.x / lanes;
@@ -160,6 +162,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
 // dw[c] (+)= sum over partial rows p of partial[p, c], in fixed order.
 __global__ void column_sum_kernel(const float* __restrict__ partial, int parts, int d, float* __restrict__ dw,
                                   int accumulate) {
+  pdl_enter();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
   float acc = 0.f;
@@ -188,6 +191,7 @@ __global__ void __launch_bounds__(32 * kNormWarps)
     rmsnorm_fwd_warp_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ r,
                             const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                             __nv_bfloat16* __restrict__ s_out, float* __restrict__ rstd_out, int rows, float eps) {
+  pdl_enter();
   constexpr int D = 256 * VPL;
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kNormWarps) {
@@ -228,6 +232,7 @@ __global__ void __launch_bounds__(32 * kNormWarps)
                             const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                             const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ ds,
                             float* __restrict__ dw_partial, int rows) {
+  pdl_enter();
   constexpr int D = 256 * VPL;
   extern __shared__ float4 dw_smem4[];  // [kNormWarps][D / 4]: each warp's running dw row
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -308,6 +313,7 @@ __global__ void __launch_bounds__(32 * kNormWarps)
 // column_sum_kernel's one thread per column would keep busy).
 __global__ void column_sum_wide_kernel(const float* __restrict__ partial, int parts, int d, float* __restrict__ dw,
                                        int accumulate) {
+  pdl_enter();
   __shared__ float sums[8][33];
   const int cl = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + cl;
@@ -357,7 +363,7 @@ void launch_bwd_warp(const void* dy, const void* s, const void* w, const float* 
   constexpr int smem = kNormWarps * 256 * VPL * int(sizeof(float));
   auto kernel = rmsnorm_bwd_warp_kernel<VPL>;
   if (smem > 48 * 1024) (void)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kernel<<<grid, 32 * kNormWarps, smem, st>>>(
+  launch_pdl(kernel, grid, 32 * kNormWarps, smem, st,
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
       static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
       static_cast<__nv_bfloat16*>(ds), partial, rows);
@@ -381,19 +387,19 @@ cudaError_t rmsnorm_bwd_launch(const void* dy, const void* s, const void* w, con
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    column_sum_wide_kernel<<<(d + 31) / 32, 256, 0, st>>>(partial, grid, d, dw, accumulate);
+    launch_pdl(column_sum_wide_kernel, (d + 31) / 32, 256, 0, st, partial, grid, d, dw, accumulate);
     return cudaGetLastError();
   }
   const int block = norm_block(d);
   const int rows_per_block = block / (d / 8);
   const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * num_sms);
-  rmsnorm_bwd_kernel<<<grid, block, 0, st>>>(
+  launch_pdl(rmsnorm_bwd_kernel, grid, block, 0, st,
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
       static_cast<const __nv_bfloat16*>(w), rstd, static_cast<const __nv_bfloat16*>(dres),
       static_cast<__nv_bfloat16*>(ds), partial, rows, d);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  column_sum_kernel<<<(d + 255) / 256, 256, 0, st>>>(partial, grid * rows_per_block, d, dw, accumulate);
+  launch_pdl(column_sum_kernel, (d + 255) / 256, 256, 0, st, partial, grid * rows_per_block, d, dw, accumulate);
   return cudaGetLastError();
 }
 
@@ -414,10 +420,10 @@ void rmsnorm_fwd(const void* x, const void* r, const void* w, void* y, void* s_o
     auto* yb = static_cast<__nv_bfloat16*>(y);
     auto* sb = static_cast<__nv_bfloat16*>(s_out);
     switch (vpl) {
-      case 1: rmsnorm_fwd_warp_kernel<1><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
-      case 2: rmsnorm_fwd_warp_kernel<2><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
-      case 4: rmsnorm_fwd_warp_kernel<4><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
-      default: rmsnorm_fwd_warp_kernel<8><<<grid, 32 * kNormWarps, 0, st>>>(xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      case 1: launch_pdl(rmsnorm_fwd_warp_kernel<1>, grid, 32 * kNormWarps, 0, st, xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      case 2: launch_pdl(rmsnorm_fwd_warp_kernel<2>, grid, 32 * kNormWarps, 0, st, xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      case 4: launch_pdl(rmsnorm_fwd_warp_kernel<4>, grid, 32 * kNormWarps, 0, st, xb, rb, wb, yb, sb, rstd, rows, eps); break;
+      default: launch_pdl(rmsnorm_fwd_warp_kernel<8>, grid, 32 * kNormWarps, 0, st, xb, rb, wb, yb, sb, rstd, rows, eps); break;
     }
     RESIHP_CUDA_CHECK(cudaGetLastError());
     return;
@@ -425,7 +431,7 @@ void rmsnorm_fwd(const void* x, const void* r, const void* w, void* y, void* s_o
   const int block = norm_block(d);
   const int rows_per_block = block / (d / 8);
   const int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 8 * num_sms);
-  rmsnorm_fwd_kernel<<<grid, block, 0, st>>>(
+  launch_pdl(rmsnorm_fwd_kernel, grid, block, 0, st,
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r),
       static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(s_out), rstd,
       rows, d, eps);

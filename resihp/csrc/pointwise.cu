@@ -24,6 +24,7 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 // Each thread rotates one (i, i + hd/2) pair of one Q or K head.
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs, int rows, int seq,
                             int heads_qk, int hd, int64_t row_stride, int pos_offset, float sign) {
+  pdl_enter();
   const int half = hd / 2;
   const int64_t total = int64_t(rows) * heads_qk * half;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -48,6 +49,7 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __res
 // element.
 __global__ void rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs, int rows, int seq,
                                 int heads_qk, int hd, int64_t row_stride, int pos_offset, float sign) {
+  pdl_enter();
   const int half = hd / 2, vph = half / 8;
   const int per_row = heads_qk * vph;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -81,6 +83,7 @@ __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + __expf(-
 // gu: [rows, 2F] = [g | u];  h: [rows, F]
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int rows,
                                   int f) {
+  pdl_enter();
   const int64_t total = int64_t(rows) * f / 2;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t row = (2 * i) / f;
@@ -96,6 +99,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
 
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
                                   __nv_bfloat16* __restrict__ dgu, int rows, int f) {
+  pdl_enter();
   const int64_t total = int64_t(rows) * f / 2;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t row = (2 * i) / f;
@@ -121,6 +125,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __
 // the row / column split is one 32-bit division per 8 elements.
 __global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int rows,
                                       int f) {
+  pdl_enter();
   const unsigned vpr = unsigned(f) / 8u;
   const unsigned total = unsigned(rows) * vpr;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -142,6 +147,7 @@ __global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, __nv
 
 __global__ void swiglu_bwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
                                       __nv_bfloat16* __restrict__ dgu, int rows, int f) {
+  pdl_enter();
   const unsigned vpr = unsigned(f) / 8u;
   const unsigned total = unsigned(rows) * vpr;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -172,6 +178,7 @@ __global__ void swiglu_bwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, cons
 // and the bf16 working copy of p is refreshed in the same pass.
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ p_bf16, int64_t n, AdamWCoef c) {
+  pdl_enter();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     float pi = p[i], mi = m[i], vi = v[i];
     adamw_elem(pi, mi, vi, g[i], c);
@@ -186,6 +193,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 // per-element arithmetic as adamw_kernel.
 __global__ void adamw_vec_kernel(float4* __restrict__ p, const float4* __restrict__ g, float4* __restrict__ m,
                                  float4* __restrict__ v, uint2* __restrict__ p_bf16, int64_t n4, AdamWCoef c) {
+  pdl_enter();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
     float4 pi = p[i], mi = m[i], vi = v[i];
     const float4 gi = g[i];
@@ -203,6 +211,7 @@ __global__ void adamw_vec_kernel(float4* __restrict__ p, const float4* __restric
 // out[t, :] = W[id_t - start, :] if the id falls in this rank's vocab shard, else 0.
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
                                      __nv_bfloat16* __restrict__ out, int rows, int d, int64_t start, int64_t count) {
+  pdl_enter();
   const int t = blockIdx.x;
   if (t >= rows) return;
   const int64_t id = ids[t] - start;
@@ -225,6 +234,7 @@ constexpr int kSortThreads = 1024;
 __global__ void __launch_bounds__(kSortThreads) embedding_sort_kernel(const int64_t* __restrict__ ids, int rows,
                                                                         int64_t start, int64_t count,
                                                                         uint64_t* __restrict__ keys_out) {
+  pdl_enter();
   extern __shared__ uint64_t key[];
   int n = 1;
   while (n < rows) n <<= 1;
@@ -259,6 +269,7 @@ __global__ void __launch_bounds__(kSortThreads) embedding_sort_kernel(const int6
 // One block per run of equal rows in the sorted keys: dW[row] += sum of the run's dy rows.
 __global__ void embedding_bwd_kernel(const uint64_t* __restrict__ keys, const __nv_bfloat16* __restrict__ dy,
                                      float* __restrict__ dw, int rows, int d) {
+  pdl_enter();
   const int head = blockIdx.x;
   if (head >= rows) return;
   const uint64_t k = keys[head];
@@ -289,13 +300,13 @@ void rope(void* qkv, const float* cs, int rows, int seq, int heads_qk, int hd, i
     const int per_row = heads_qk * (hd / 16);
     const int block = per_row >= 256 ? 256 : ((per_row + 31) / 32) * 32;
     const int grid = std::max(1, std::min(rows, num_sms * (2048 / block)));
-    rope_vec_kernel<<<grid, block, 0, st>>>(static_cast<__nv_bfloat16*>(qkv), reinterpret_cast<const float2*>(cs),
+    launch_pdl(rope_vec_kernel, grid, block, 0, st, static_cast<__nv_bfloat16*>(qkv), reinterpret_cast<const float2*>(cs),
                                             rows, seq, heads_qk, hd, row_stride, pos_offset, inverse ? -1.f : 1.f);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     return;
   }
   const int64_t work = int64_t(rows) * heads_qk * (hd / 2);
-  rope_kernel<<<grid_for(work, 256, num_sms), 256, 0, st>>>(static_cast<__nv_bfloat16*>(qkv),
+  launch_pdl(rope_kernel, grid_for(work, 256, num_sms), 256, 0, st, static_cast<__nv_bfloat16*>(qkv),
                                                              reinterpret_cast<const float2*>(cs), rows, seq, heads_qk,
                                                              hd, row_stride, pos_offset, inverse ? -1.f : 1.f);
   RESIHP_CUDA_CHECK(cudaGetLastError());
@@ -305,12 +316,12 @@ void swiglu_fwd(const void* gu, void* h, int rows, int f, int num_sms, cudaStrea
   RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
   if (f % 8 == 0 && int64_t(rows) * (f / 8) < (int64_t(1) << 31) &&
       (reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(h)) % 16 == 0) {
-    swiglu_fwd_vec_kernel<<<grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st>>>(
+    launch_pdl(swiglu_fwd_vec_kernel, grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st,
         static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(h), rows, f);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  swiglu_fwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
+  launch_pdl(swiglu_fwd_kernel, grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st,
       static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(h), rows, f);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
@@ -319,13 +330,13 @@ void swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, int 
   RESIHP_CHECK(f % 2 == 0, "swiglu width must be even");
   if (f % 8 == 0 && int64_t(rows) * (f / 8) < (int64_t(1) << 31) &&
       (reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dh) | reinterpret_cast<uintptr_t>(dgu)) % 16 == 0) {
-    swiglu_bwd_vec_kernel<<<grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st>>>(
+    launch_pdl(swiglu_bwd_vec_kernel, grid_for(int64_t(rows) * f / 8, 256, num_sms), 256, 0, st,
         static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
         rows, f);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  swiglu_bwd_kernel<<<grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st>>>(
+  launch_pdl(swiglu_bwd_kernel, grid_for(int64_t(rows) * f / 2, 256, num_sms), 256, 0, st,
       static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
       rows, f);
   RESIHP_CUDA_CHECK(cudaGetLastError());
@@ -353,20 +364,20 @@ void adamw(float* p, const float* g, float* m, float* v, void* p_bf16, int64_t n
   const uintptr_t al = reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) |
                        reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v);
   if (n % 4 == 0 && al % 16 == 0 && reinterpret_cast<uintptr_t>(p_bf16) % 8 == 0) {
-    adamw_vec_kernel<<<grid_for(n / 4, 256, num_sms), 256, 0, st>>>(
+    launch_pdl(adamw_vec_kernel, grid_for(n / 4, 256, num_sms), 256, 0, st,
         reinterpret_cast<float4*>(p), reinterpret_cast<const float4*>(g), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), static_cast<uint2*>(p_bf16), n / 4, c);
     RESIHP_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  adamw_kernel<<<grid_for(n, 256, num_sms), 256, 0, st>>>(p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, c);
+  launch_pdl(adamw_kernel, grid_for(n, 256, num_sms), 256, 0, st, p, g, m, v, static_cast<__nv_bfloat16*>(p_bf16), n, c);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
 void embedding_fwd(const int64_t* ids, const void* w, void* out, int rows, int d, int64_t start, int64_t count,
                    cudaStream_t st) {
   RESIHP_CHECK(d % 8 == 0, "embedding width must be a multiple of 8");
-  embedding_fwd_kernel<<<rows, 128, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(w),
+  launch_pdl(embedding_fwd_kernel, rows, 128, 0, st, ids, static_cast<const __nv_bfloat16*>(w),
                                              static_cast<__nv_bfloat16*>(out), rows, d, start, count);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
@@ -383,9 +394,9 @@ void embedding_bwd(const int64_t* ids, const void* dy, float* dw, uint64_t* keys
     const int seg = std::min(kSortMax, rows - off);
     int n = 1;
     while (n < seg) n <<= 1;
-    embedding_sort_kernel<<<1, kSortThreads, n * int(sizeof(uint64_t)), st>>>(ids + off, seg, start, count, keys);
+    launch_pdl(embedding_sort_kernel, 1, kSortThreads, n * int(sizeof(uint64_t)), st, ids + off, seg, start, count, keys);
     RESIHP_CUDA_CHECK(cudaGetLastError());
-    embedding_bwd_kernel<<<seg, 256, 0, st>>>(keys, dyb + int64_t(off) * d, dw, seg, d);
+    launch_pdl(embedding_bwd_kernel, seg, 256, 0, st, keys, dyb + int64_t(off) * d, dw, seg, d);
     RESIHP_CUDA_CHECK(cudaGetLastError());
   }
 }

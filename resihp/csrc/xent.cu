@@ -31,6 +31,7 @@ __device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
 __global__ void xent_stats_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld,
                                   const int64_t* __restrict__ labels, float* __restrict__ stats, int rows, int v,
                                   int64_t start) {
+  pdl_enter();
   __shared__ float sm_m[kXentThreads / 32], sm_s[kXentThreads / 32];
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + int64_t(row) * ld;
@@ -80,6 +81,7 @@ __global__ void xent_stats_kernel(const __nv_bfloat16* __restrict__ logits, int6
 __global__ void xent_grad_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, const int64_t* __restrict__ labels,
                                  const float* __restrict__ lse, const float* __restrict__ scale, int rows, int v,
                                  int64_t start) {
+  pdl_enter();
   const int row = blockIdx.x;
   __nv_bfloat16* x = logits + int64_t(row) * ld;
   const int64_t label = labels[row];
@@ -107,7 +109,7 @@ __global__ void xent_grad_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld,
 void xent_stats(const void* logits, int64_t ld, const int64_t* labels, float* stats, int rows, int v, int64_t start,
                 cudaStream_t st) {
   RESIHP_CHECK(v % 8 == 0 && ld % 8 == 0, "cross-entropy vocab shard must be a multiple of 8");
-  xent_stats_kernel<<<rows, kXentThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), ld, labels, stats, rows,
+  launch_pdl(xent_stats_kernel, rows, kXentThreads, 0, st, static_cast<const __nv_bfloat16*>(logits), ld, labels, stats, rows,
                                                    v, start);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
@@ -115,7 +117,7 @@ void xent_stats(const void* logits, int64_t ld, const int64_t* labels, float* st
 void xent_grad(void* logits, int64_t ld, const int64_t* labels, const float* lse, const float* scale, int rows, int v,
                int64_t start, cudaStream_t st) {
   RESIHP_CHECK(v % 8 == 0 && ld % 8 == 0, "cross-entropy vocab shard must be a multiple of 8");
-  xent_grad_kernel<<<rows, 256, 0, st>>>(static_cast<__nv_bfloat16*>(logits), ld, labels, lse, scale, rows, v, start);
+  launch_pdl(xent_grad_kernel, rows, 256, 0, st, static_cast<__nv_bfloat16*>(logits), ld, labels, lse, scale, rows, v, start);
   RESIHP_CUDA_CHECK(cudaGetLastError());
 }
 
