@@ -67,7 +67,9 @@ def parse():
                         "data parallelism on 2 GPUs); the JSON line's parallelism field names what ran")
     p.add_argument("--trace", default=None,
                    help="after the timed steps, profile one more step per rank and write a Chrome trace "
-                        "plus a kernel summary into this directory (analysis only; not part of the number)")
+                        "plus a kernel summary into this directory (analysis only; not part of the number). "
+                        "With programmatic dependent launch on, a kernel's traced time includes its wait for "
+                        "the previous kernel: set RESIHP_PDL=0 for per-kernel times")
     return p.parse_args()
 
 

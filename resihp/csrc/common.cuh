@@ -324,6 +324,12 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                : "memory");
 }
 
+// Start bringing ``bytes`` (a multiple of 16, 16-byte aligned) of this GPU's global memory
+// into L2; nothing waits for it, and no shared memory or barrier is involved.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Every committed bulk group of this thread has finished reading its shared memory.

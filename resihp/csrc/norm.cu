@@ -245,8 +245,16 @@ __global__ void __launch_bounds__(32 * kNormWarps)
   uint4 wr[VPL];  // this lane's weights, packed, for every row
   #pragma unroll
   for (int j = 0; j < VPL; ++j) wr[j] = *reinterpret_cast<const uint4*>(w + (32 * j + lane) * 8);
-  for (int row = blockIdx.x * kNormWarps + warp; row < rows; row += gridDim.x * kNormWarps) {
+  const int step = gridDim.x * kNormWarps;
+  for (int row = blockIdx.x * kNormWarps + warp; row < rows; row += step) {
     const int64_t base = int64_t(row) * D;
+    // the warp's next row heads for L2 while this one is loaded and reduced
+    if (lane == 0 && row + step < rows) {
+      const int64_t nb = base + int64_t(step) * D;
+      l2_prefetch_bulk(dy + nb, D * 2);
+      l2_prefetch_bulk(s + nb, D * 2);
+      if (dres != nullptr) l2_prefetch_bulk(dres + nb, D * 2);
+    }
     const float rs = rstd[row];
     // every load of the row in flight at once, kept packed (bf16) through the reduction
     uint4 dyr[VPL], sr[VPL], rr[VPL];

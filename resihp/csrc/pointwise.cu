@@ -43,37 +43,58 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __res
   }
 }
 
+// Rotates eight (x1, x2) pairs held as two 16-byte vectors; c4 points at the pairs'
+// (cos, sin) values, two pairs per float4.
+__device__ __forceinline__ void rope8(uint4& r1, uint4& r2, const float4* __restrict__ c4, float sign) {
+  const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&r1);
+  const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&r2);
+  uint32_t o1[4], o2[4];
+  #pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 c = c4[q];  // (cos, sin) of pairs 2q, 2q+1
+    const float2 a = __bfloat1622float2(x1[q]), bb = __bfloat1622float2(x2[q]);
+    const float s0 = sign * c.y, s1 = sign * c.w;
+    o1[q] = pack_bf16(a.x * c.x - bb.x * s0, a.y * c.z - bb.y * s1);
+    o2[q] = pack_bf16(bb.x * c.x + a.x * s0, bb.y * c.z + a.y * s1);
+  }
+  r1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  r2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+}
+
 // Vector form (hd % 16 == 0, 16-byte aligned rows): one thread rotates eight pairs
 // (p..p+7, p+hd/2..p+hd/2+7) with two 16-byte loads and stores; a block walks rows
-// (grid-stride) and its threads the rows' Q/K head vectors, so no 64-bit division per
-// element.
+// (grid-stride) two at a time, so each thread has both rows' loads in flight before it
+// computes, and its threads the rows' Q/K head vectors (no 64-bit division per element).
 __global__ void rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float2* __restrict__ cs, int rows, int seq,
                                 int heads_qk, int hd, int64_t row_stride, int pos_offset, float sign) {
   pdl_enter();
   const int half = hd / 2, vph = half / 8;
   const int per_row = heads_qk * vph;
-  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
-    const int pos = (row + pos_offset) % seq;
-    const float4* c4 = reinterpret_cast<const float4*>(cs + int64_t(pos) * half);
-    __nv_bfloat16* rb = qkv + int64_t(row) * row_stride;
+  for (int row = blockIdx.x; row < rows; row += 2 * gridDim.x) {
+    const int row2 = row + gridDim.x;
+    const bool two = row2 < rows;
+    const float4* c4a = reinterpret_cast<const float4*>(cs + int64_t((row + pos_offset) % seq) * half);
+    const float4* c4b = reinterpret_cast<const float4*>(cs + int64_t((row2 + pos_offset) % seq) * half);
+    __nv_bfloat16* ra = qkv + int64_t(row) * row_stride;
+    __nv_bfloat16* rb = qkv + int64_t(row2) * row_stride;
     for (int j = threadIdx.x; j < per_row; j += blockDim.x) {
       const int h = j / vph, v = j - h * vph;
-      __nv_bfloat16* b = rb + h * hd + v * 8;
-      const uint4 r1 = *reinterpret_cast<const uint4*>(b);
-      const uint4 r2 = *reinterpret_cast<const uint4*>(b + half);
-      const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&r1);
-      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&r2);
-      uint32_t o1[4], o2[4];
-      #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 c = c4[v * 4 + q];  // (cos, sin) of pairs 2q, 2q+1
-        const float2 a = __bfloat1622float2(x1[q]), bb = __bfloat1622float2(x2[q]);
-        const float s0 = sign * c.y, s1 = sign * c.w;
-        o1[q] = pack_bf16(a.x * c.x - bb.x * s0, a.y * c.z - bb.y * s1);
-        o2[q] = pack_bf16(bb.x * c.x + a.x * s0, bb.y * c.z + a.y * s1);
+      const int off = h * hd + v * 8;
+      uint4 a1 = *reinterpret_cast<const uint4*>(ra + off);
+      uint4 a2 = *reinterpret_cast<const uint4*>(ra + off + half);
+      uint4 b1, b2;
+      if (two) {
+        b1 = *reinterpret_cast<const uint4*>(rb + off);
+        b2 = *reinterpret_cast<const uint4*>(rb + off + half);
       }
-      *reinterpret_cast<uint4*>(b) = make_uint4(o1[0], o1[1], o1[2], o1[3]);
-      *reinterpret_cast<uint4*>(b + half) = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+      rope8(a1, a2, c4a + v * 4, sign);
+      *reinterpret_cast<uint4*>(ra + off) = a1;
+      *reinterpret_cast<uint4*>(ra + off + half) = a2;
+      if (two) {
+        rope8(b1, b2, c4b + v * 4, sign);
+        *reinterpret_cast<uint4*>(rb + off) = b1;
+        *reinterpret_cast<uint4*>(rb + off + half) = b2;
+      }
     }
   }
 }
@@ -128,20 +149,35 @@ __global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, __nv
   pdl_enter();
   const unsigned vpr = unsigned(f) / 8u;
   const unsigned total = unsigned(rows) * vpr;
-  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const unsigned row = i / vpr, col = (i - row * vpr) * 8u;
-    const __nv_bfloat16* g = gu + int64_t(row) * 2 * f + col;
-    const uint4 gr = *reinterpret_cast<const uint4*>(g);
-    const uint4 ur = *reinterpret_cast<const uint4*>(g + f);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gr);
-    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&ur);
-    uint32_t o[4];
+  const unsigned stride = gridDim.x * blockDim.x;
+  // two items per thread and iteration: all four loads are issued before any compute
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    uint4 gr[2], ur[2];
+    int64_t out[2];
     #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 gf = __bfloat1622float2(g2[q]), uf = __bfloat1622float2(u2[q]);
-      o[q] = pack_bf16(gf.x * sigmoid(gf.x) * uf.x, gf.y * sigmoid(gf.y) * uf.y);
+    for (int t = 0; t < 2; ++t) {
+      const unsigned it = i + t * stride;
+      if (t == 0 || it < total) {
+        const unsigned row = it / vpr, col = (it - row * vpr) * 8u;
+        const __nv_bfloat16* g = gu + int64_t(row) * 2 * f + col;
+        gr[t] = *reinterpret_cast<const uint4*>(g);
+        ur[t] = *reinterpret_cast<const uint4*>(g + f);
+        out[t] = int64_t(row) * f + col;
+      }
     }
-    *reinterpret_cast<uint4*>(h + int64_t(row) * f + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    #pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t == 1 && i + stride >= total) break;
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gr[t]);
+      const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&ur[t]);
+      uint32_t o[4];
+      #pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 gf = __bfloat1622float2(g2[q]), uf = __bfloat1622float2(u2[q]);
+        o[q] = pack_bf16(gf.x * sigmoid(gf.x) * uf.x, gf.y * sigmoid(gf.y) * uf.y);
+      }
+      *reinterpret_cast<uint4*>(h + out[t]) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
