@@ -53,10 +53,6 @@ GROUP_TIMEOUT = timedelta(seconds=int(os.environ.get("RESIHP_GROUP_TIMEOUT", "30
 # (ncclCommSplit) inside the safe point instead of being initialised from scratch on its
 # first collective.
 NCCL_SPLIT = os.environ.get("RESIHP_NCCL_SPLIT", "1") != "0"
-# Create the NCCL training groups with one ncclCommSplit per family of disjoint groups
-# (all TP groups at once, all DP groups at once, ...) instead of one split per group.
-# Off until measured on GPUs.
-BATCHED_SPLIT = os.environ.get("RESIHP_BATCHED_SPLIT", "0") == "1"
 # The checkpoint writer rank serialises and writes the file on a background thread.
 ASYNC_CHECKPOINT = os.environ.get("RESIHP_ASYNC_CHECKPOINT", "1") != "0"
 
@@ -215,45 +211,8 @@ class ControlPlane:
             ranks=[self.torch_rank(r) for r in plan_ranks], backend=self.training_backend, timeout=GROUP_TIMEOUT
         )
 
-    @staticmethod
-    def disjoint_layers(groups) -> list[list[tuple[int, ...]]]:
-        """Greedy partition of ``groups`` (in order) into layers of pairwise-disjoint groups."""
-        layers: list[list[tuple[int, ...]]] = []
-        used: list[set] = []
-        for grp in groups:
-            for layer, seen in zip(layers, used):
-                if not seen & set(grp):
-                    layer.append(grp)
-                    seen.update(grp)
-                    break
-            else:
-                layers.append([grp])
-                used.append(set(grp))
-        return layers
-
-    def _split_family(self, groups) -> dict:
-        """One ``ncclCommSplit`` per layer of disjoint groups; ``{group: handle}`` for this rank."""
-        import torch.distributed as dist
-
-        handles = {}
-        for layer in self.disjoint_layers(groups):
-            handle = dist.split_group(split_ranks=[[self.torch_rank(r) for r in grp] for grp in layer],
-                                      timeout=GROUP_TIMEOUT)
-            for grp in layer:
-                if self.rank in grp:
-                    handles[grp] = handle
-        return handles
-
-    def _batched_split_ready(self) -> bool:
-        import torch
-
-        return (BATCHED_SPLIT and NCCL_SPLIT and self.training_backend == "nccl" and self.device is not None
-                and torch.device(self.device).type == "cuda")
-
     def build_training_groups(self, plan: ExecutionPlan) -> TrainingGroups:
         """Safe-point step 6c: every rank creates every group in the same plan order."""
-        if self._batched_split_ready():
-            return self._build_training_groups_batched(plan)
         g = TrainingGroups(world=self.world_group)
         for stage in sorted(plan.stages, key=lambda s: (s.replica_id, s.stage_id)):
             if len(stage.tp_members) == 1:
@@ -293,25 +252,6 @@ class ControlPlane:
         if tuple(sorted(plan_ranks)) == self.members and self._world_carries_training():
             return self.world_group
         return self._new_group(plan_ranks)
-
-    def _build_training_groups_batched(self, plan: ExecutionPlan) -> TrainingGroups:
-        """The same groups as :meth:`build_training_groups`, split family by family."""
-        g = TrainingGroups(world=self.world_group)
-        stages = sorted(plan.stages, key=lambda s: (s.replica_id, s.stage_id))
-        tp = self._split_family([tuple(s.tp_members) for s in stages if len(s.tp_members) > 1])
-        g.tp = next(iter(tp.values()), None)
-        g.hops = self._split_family(list(boundary_hops(plan)))
-        if tuple(sorted(plan.active_ranks)) == self.members:
-            executors = {tuple(plan.active_ranks): self.world_group}
-        else:
-            executors = self._split_family([tuple(plan.active_ranks)])
-        g.executor = executors.get(tuple(plan.active_ranks)) if self.is_training_rank(plan) else None
-        topo = reduction_topology(plan)
-        g.reduce = self._split_family(list(topo.tied_groups + topo.dp_groups))
-        if self._needs_live_group(plan):
-            g.live = self.world_group
-        self.groups = g
-        return g
 
     def _needs_live_group(self, plan: ExecutionPlan) -> bool:
         """The live group carries collective state moves; the CUDA bf16 path moves state

@@ -30,8 +30,10 @@
 //     finished 64 KB tile as one bulk copy into the owning peer's (tile-contiguous)
 //     receive buffer and count it there.
 //     Own-chunk tiles run last: their epilogue stores this rank's partial in y, and once
-//     the tp-1 contributions have arrived the copy warps add them (own partial first,
-//     then the peers' in rank order, in fp32, deterministically), many rows in flight.
+//     the tp-1 contributions have arrived the copy warps add them, many rows in flight.
+//     The peers' partials travel as bf16 (as in a bf16 reduce-scatter); the sum is taken
+//     in fp32 in a fixed order (own partial first, then the peers' in rank order), so it
+//     is deterministic.
 //     (The tile counters come in two banks by call parity: a fast source may already be
 //     contributing to the next call.)
 // AR: RS, where the copy warps also stage each reduced slice of an own tile and bulk-push

@@ -127,18 +127,6 @@ def test_trace_ranges_are_free_when_off():
     assert not trace._ON or torch.cuda.is_available()
 
 
-def test_disjoint_layers_partition_groups_in_order():
-    from resihp.control import ControlPlane
-
-    groups = [(0, 1), (2, 3), (1, 2), (4,), (0, 4), (3, 5)]
-    layers = ControlPlane.disjoint_layers(groups)
-    assert layers == [[(0, 1), (2, 3), (4,)], [(1, 2), (0, 4), (3, 5)]]
-    for layer in layers:
-        seen = [r for grp in layer for r in grp]
-        assert len(seen) == len(set(seen))
-    assert sorted(g for layer in layers for g in layer) == sorted(groups)
-
-
 def test_dp_peers_step_passes_the_right_buffers(monkeypatch):
     """The fused DP step's host side: which gradient parity it reads, where the sum goes,
     the flag arrays, the AdamW step count and the parity swap afterwards."""
