@@ -10,6 +10,7 @@
     python bench_kernels.py fused_rs [tp]  # fused GEMM->RS, 1.3B down-proj shape, peers emulated
     python bench_kernels.py fused_ar [tp]  # fused GEMM->AR (no sequence parallelism), same shape
     python bench_kernels.py fused_time  # CUDA-event time of the emulated fused kernels vs the GEMM alone
+    python bench_kernels.py mem_time  # achieved GB/s of RMSNorm, RoPE, SwiGLU and AdamW
 
 Each workload touches a few hundred MB (more than the 126 MB L2, far below the device)
 and launches every kernel a handful of times, so a capture of one or two launches ends
@@ -168,6 +169,65 @@ def fused_rs(tp: int = 2, all_reduce: bool = False) -> None:
         s.launch()
 
 
+def mem_time() -> None:
+    """Achieved bandwidth of the memory-bound step kernels at the 1.3B micro-batch shapes
+    (4096 tokens, d 2048, FFN 5504, 32 rotated Q/K heads of 128): algorithmic bytes (each
+    input read once, each output written once) over the CUDA-event time, and the fraction
+    of the measured copy bandwidth. Three sets of buffers are used in turn, so consecutive
+    calls never find their inputs in the 126 MB L2."""
+    import json
+    import os
+
+    peaks = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    hbm = json.load(open(peaks))["hbm_gbs"] if os.path.exists(peaks) else None
+    t, d, f, heads, hd, seq = 4096, 2048, 5504, 32, 128, 2048
+    k = ops._ext.require()
+    w = (1 + 0.1 * torch.randn(d, device="cuda")).bfloat16()
+    dw = torch.zeros(d, device="cuda")
+    cs = fn.rope_table(seq, hd, 10000.0, device="cuda")
+    sets = []
+    for _ in range(3):
+        x, r = (torch.randn(t, d, device="cuda").bfloat16() for _ in range(2))
+        y, s, rstd = k.rmsnorm_fwd(x, r, w, 1e-5)
+        sets.append({"x": x, "r": r, "s": s, "rstd": rstd, "dy": torch.randn_like(x), "dres": torch.randn_like(x),
+                     "qkv": torch.randn(t, 3 * d, device="cuda").bfloat16(),
+                     "gu": torch.randn(t, 2 * f, device="cuda").bfloat16(),
+                     "dh": torch.randn(t, f, device="cuda").bfloat16()})
+    n = 64 * 2**20
+    flat = [torch.randn(n, device="cuda") for _ in range(4)]
+    pb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    act = t * d * 2
+    cases = {
+        "rmsnorm_fwd_residual": (lambda b: k.rmsnorm_fwd(b["x"], b["r"], w, 1e-5), 4 * act),
+        "rmsnorm_bwd_residual": (lambda b: k.rmsnorm_bwd(b["dy"], b["s"], w, b["rstd"], b["dres"], dw, True), 4 * act),
+        "rope_qk": (lambda b: k.rope(b["qkv"], cs, seq, heads, hd, 0, False), 2 * t * heads * hd * 2),
+        "swiglu_fwd": (lambda b: k.swiglu_fwd(b["gu"]), 3 * t * f * 2),
+        "swiglu_bwd": (lambda b: k.swiglu_bwd(b["gu"], b["dh"]), 5 * t * f * 2),
+    }
+    out = []
+    for name, (call, nbytes) in cases.items():
+        i = [0]
+
+        def rotate():
+            call(sets[i[0] % 3])
+            i[0] += 1
+
+        us = _time_us(rotate, it=30, warm=6)
+        row = {"kernel": name, "us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1)}
+        if hbm:
+            row["of_measured_hbm"] = round(nbytes / us / 1e3 / hbm, 3)
+        out.append(row)
+    # AdamW over 64 Mi fp32 elements: p, g, m, v read, p, m, v written, bf16 copy written
+    us = _time_us(lambda: k.adamw(flat[0], flat[1], flat[2], flat[3], pb, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, 1.0),
+                  it=10, warm=3)
+    nbytes = n * (7 * 4 + 2)
+    row = {"kernel": "adamw_64Mi", "us": round(us, 1), "gbs": round(nbytes / us / 1e3, 1)}
+    if hbm:
+        row["of_measured_hbm"] = round(nbytes / us / 1e3 / hbm, 3)
+    out.append(row)
+    print(json.dumps(out))
+
+
 def fused_time() -> None:
     """CUDA-event time of the fused TP kernels with the peers emulated by local buffers
     (the kernel's structure without NVLink latency) against this package's GEMM alone
@@ -204,7 +264,7 @@ def main(argv=None) -> None:
             fused_rs(tp, all_reduce=what == "fused_ar")
     else:
         {"gemm": gemm, "attn": attn, "dp": dp, "reshard": reshard, "gemm_time": gemm_time,
-         "attn_time": attn_time, "fused_time": fused_time}[what]()
+         "attn_time": attn_time, "fused_time": fused_time, "mem_time": mem_time}[what]()
     torch.cuda.synchronize()
     ops.check_device_errors()
     print("ok", what)
