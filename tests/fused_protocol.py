@@ -67,11 +67,16 @@ class Simulation:
     """``tp`` ranks running ``epochs`` calls of one op (``"ag"``, ``"rs"`` or ``"ar"``)."""
 
     def __init__(self, op, *, tp, rows_per_rank, n, grid, epochs, seed, slices=4, keep_gathered=True,
-                 copy_claims=None):
+                 copy_claims=None, push_depth=1, flush_before_wait=True):
         self.k = _ext.require()
         self.op, self.mode = op, MODES[op]
         self.tp, self.rows, self.n, self.grid, self.epochs = tp, rows_per_rank, n, grid, epochs
         self.slices, self.keep = slices, keep_gathered
+        # RS / AR partial-tile pushes whose counter release a copy agent may still owe
+        # (1: each push is released as soon as its data is complete, as the kernels do;
+        # 2+: the release of push i waits until push i+depth-1 is issued). With
+        # ``flush_before_wait`` every owed release is paid before the agent waits on a peer.
+        self.push_depth, self.flush_before_wait = push_depth, flush_before_wait
         self.rng = random.Random(seed)
         self.blocks = rows_per_rank // FBM
         self.tiles_n = (n + 255) // 256
@@ -157,10 +162,12 @@ class Simulation:
         # an RS / AR item is a whole tile (or a slice); AG items come in batches small
         # enough to spread over the grid (fused_gemm.cu ag_copy_batch)
         size = 1 if self.op != "ag" else max(1, min(COPY_BATCH, items // (2 * self.grid)))
+        owed = []  # (owner, own tile, parity) of pushed partials whose count is not yet released
         while True:
             first = self._claim(me, "copy", items, size)
             yield lambda: True
             if first < 0:
+                self._release(owed, 0)  # a CTA leaves only after every push is counted
                 return
             batch = range(first, min(first + size, items))
             me.seen_items.extend(batch)
@@ -177,7 +184,7 @@ class Simulation:
                     self.ranks[dest].ag_cnt[r][rb] += 1
             for it in batch:
                 if self.op != "ag":
-                    yield from self._rs_item(r, e, ar_e, it, n_rsp, n_own)
+                    yield from self._rs_item(r, e, ar_e, it, n_rsp, n_own, owed)
                     continue
                 if it < n_push:
                     continue
@@ -190,7 +197,13 @@ class Simulation:
                         self._read(me.land[par].get((c, rb)), e, f"AG landing of rank {c} block {rb} (xg) on {r}")
                     xg[(c, rb)] = xg.get((c, rb), 0) + 1
 
-    def _rs_item(self, r, e, ar_e, it, n_rsp, n_own):
+    def _release(self, owed, keep):
+        """Count the oldest owed pushes in their owners' tile counters until ``keep`` remain."""
+        while len(owed) > keep:
+            owner, local, par = owed.pop(0)
+            self.ranks[owner].rs_cnt[par][local] += 1
+
+    def _rs_item(self, r, e, ar_e, it, n_rsp, n_own, owed):
         """One RS / AR copy item: push a peer-chunk partial tile to its owner, reduce a
         16-row slice of an own tile (and, AR, push it to every peer), or take another
         owner's reduced tile (AR)."""
@@ -214,8 +227,12 @@ class Simulation:
             self._read(me.send.get(gtile), e, f"send buffer tile {gtile} on {r}")
             self.ranks[c].recv[par][(r, local)] = e                 # the partial into the owner
             yield lambda: True
-            self.ranks[c].rs_cnt[par][local] += 1
-        elif it < n_rsp + n_own:
+            owed.append((c, local, par))
+            self._release(owed, self.push_depth - 1)
+            return
+        if self.flush_before_wait:
+            self._release(owed, 0)  # the items below wait on peers
+        if it < n_rsp + n_own:
             if c != r:
                 raise ProtocolError(f"own reduction item {it} on rank {r} maps to chunk {c}")
             yield lambda: me.own_cnt[local] >= 4 * e

@@ -6,6 +6,11 @@ rank reading a block or tile of the wrong epoch, without deadlock, with every ti
 computed exactly once per call, and with the host's claim bases (from the extension's
 own host functions) equal to what the kernels claimed. A host whose per-call claim count
 disagrees with the kernel's must be caught. The DP step is checked in both forms.
+
+Deferred push releases (a copy agent keeping two or three partial-tile pushes in flight
+and counting each one only after a later push is issued) are checked too: safe when the
+agent pays every owed count before it waits on a peer, a deadlock when it carries them
+into that wait.
 """
 
 import pytest
@@ -19,6 +24,23 @@ def test_protocol_has_no_race_or_deadlock(op, tp, grid):
     for seed in range(5):
         sim = Simulation(op, tp=tp, rows_per_rank=256, n=512, grid=grid, epochs=4, seed=seed)
         assert sim.run() > 0
+
+
+@pytest.mark.parametrize("op", ["rs", "ar"])
+@pytest.mark.parametrize("tp,grid", [(2, 3), (4, 5), (8, 7)])
+@pytest.mark.parametrize("depth", [2, 3])
+def test_deferred_push_releases_paid_before_peer_waits(op, tp, grid, depth):
+    for seed in range(3):
+        assert Simulation(op, tp=tp, rows_per_rank=256, n=512, grid=grid, epochs=4, seed=seed,
+                          push_depth=depth).run() > 0
+
+
+def test_deferred_push_releases_carried_into_a_peer_wait_deadlock():
+    # every copy agent ends its pushes still owing one count and then waits for the
+    # peers' partials of its own tiles, which the peers' agents owe in the same way
+    with pytest.raises(ProtocolError, match="deadlock"):
+        Simulation("rs", tp=2, rows_per_rank=256, n=512, grid=3, epochs=4, seed=0, push_depth=2,
+                   flush_before_wait=False).run()
 
 
 def test_ag_without_the_gathered_copy():
