@@ -52,6 +52,7 @@
 // call e-1, which needed data the peer produced in its call e-1 -- after it had
 // finished call e-2, the last reader of that parity. (No counterpart in the reference.)
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <cudaTypedefs.h>
 
@@ -100,6 +101,7 @@ struct FusedArgs {
   const __nv_bfloat16* x_local;  // AG: this rank's chunk [T/tp, K], row stride K
   __nv_bfloat16* xg;             // AG: gathered copy [T, K] for the backward (nullptr: none)
   uint64_t* trace;               // profiling aid: [grid][kTraceSlots] timer stamps, or null
+  int push_depth;                // RS / AR partial-tile pushes a copy thread keeps in flight (1 or 2)
   FusedPeers p;
 };
 
@@ -326,6 +328,50 @@ __device__ __forceinline__ bool bulk_push(uint8_t* stage, uint64_t* bar, uint32_
   __threadfence_system();
   return ok;
 }
+
+// bulk_push without its completion wait: every chunk's store is committed as its own
+// bulk group and the staging buffers are free again for the next push (the reads of all
+// but the last chunk are complete; the next push waits for that one), while the writes
+// may still be on their way to the peer. Used where a copy thread keeps a second push in
+// flight and counts the first one only once it is complete (wait_group_keep_tile).
+__device__ __forceinline__ bool bulk_push_issue(uint8_t* stage, uint64_t* bar, uint32_t& phase, uint8_t* dst,
+                                                const uint8_t* src, int64_t bytes, int* err) {
+  if (!bounds_ok(((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | uintptr_t(bytes)) & 15u) == 0,
+                 err))
+    return false;
+  const int nch = int((bytes + kChunk - 1) / kChunk);
+  bulk_wait_read_all();  // an earlier push may still be reading the buffers
+  #pragma unroll 1
+  for (int c = 0; c < 2 && c < nch; ++c) {
+    const uint32_t len = uint32_t(min(int64_t(kChunk), bytes - int64_t(c) * kChunk));
+    mbar_expect_tx(&bar[c], len);
+    bulk_load(stage + c * kChunk, src + int64_t(c) * kChunk, len, &bar[c]);
+  }
+  #pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    const int b = c & 1;
+    if (!mbar_wait(&bar[b], (phase >> b) & 1u, err, kErrEpiWait)) return false;
+    phase ^= 1u << b;
+    const uint32_t len = uint32_t(min(int64_t(kChunk), bytes - int64_t(c) * kChunk));
+    bulk_store(dst + int64_t(c) * kChunk, stage + b * kChunk, len);
+    bulk_commit();
+    if (c + 2 < nch) {
+      bulk_wait_read_all();  // this store has read buffer b: refill it
+      const uint32_t len2 = uint32_t(min(int64_t(kChunk), bytes - int64_t(c + 2) * kChunk));
+      mbar_expect_tx(&bar[b], len2);
+      bulk_load(stage + b * kChunk, src + int64_t(c + 2) * kChunk, len2, &bar[b]);
+    }
+  }
+  return true;
+}
+
+// A whole 128 x 256 bf16 tile is four bulk groups (kChunk bytes each).
+constexpr int kTileGroups = 4;
+static_assert(kFBM * 256 * 2 == kTileGroups * kChunk, "an RS tile push must be kTileGroups chunks");
+
+// Every bulk group of this thread except the kTileGroups most recent (one tile push) is
+// complete: the tile pushed before the latest one has landed.
+__device__ __forceinline__ void bulk_wait_keep_tile() { asm volatile("cp.async.bulk.wait_group 4;" ::: "memory"); }
 
 // Tile t -> (chunk, m0, tn). Chunks are visited starting at (rank + first) % tp; inside a
 // chunk, tiles are grouped along M (eight row blocks at a time) for L2 reuse of B.
@@ -589,6 +635,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int items = MODE == kModeAG ? n_push + n_xg : n_rsp + n_own + n_ar;
     // an RS / AR item is a whole 128 x 256 tile (or a slice of one)
     const int batch = MODE == kModeAG ? ag_copy_batch(items, int(gridDim.x)) : 1;
+    // ct 0, push_depth 2: the tile counter of the last RS / AR partial push, counted
+    // once the push after it is issued, or before this thread waits on a peer (a count
+    // carried into such a wait can deadlock two ranks), or when the copy warps finish
+    unsigned* owed = nullptr;
+    auto pay_owed = [&]() {
+      if (owed == nullptr) return;
+      bulk_wait_all();
+      fence_proxy_async_global();
+      __threadfence_system();
+      red_release_add(owed, 1u);
+      owed = nullptr;
+    };
     for (int nclaim = 0; items > 0; ++nclaim) {
       if (ct == 0) claim[0] = int(atomicAdd(p.copy_ctr, unsigned(batch)) - p.copy_base);
       copy_bar();
@@ -678,6 +736,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const int local_tile = ((m0 - chunk * rpr) / kFBM) * tiles_n + tn;
         const int ncols16 = min(BN, g.n - tn * BN) / 8;
         if (ct == 0) {
+          if (it >= n_rsp) pay_owed();  // the waits below are on peers
           if (it < n_rsp)
             claim[1] = wait_geq(p.send_cnt + gtile, 4u * p.epoch, g.err, kErrEpiWait, kWaitBudgetNs);
           else if (it < n_rsp + n_own)
@@ -695,12 +754,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           // the partial tile -> the owner's receive buffer (slot of this rank): the whole
           // tile, contiguous in both buffers, through the TMA engine, then counted there
           if (ct == 0) {
-            const bool pushed = bulk_push(
-                bstage, bbar, bphase,
-                reinterpret_cast<uint8_t*>(pick(p.recv, chunk) + (int64_t(p.rank) * per_chunk + local_tile) * S::kTileElems),
-                reinterpret_cast<const uint8_t*>(p.send + int64_t(gtile) * S::kTileElems), int64_t(S::kTileElems) * 2,
-                g.err);
-            if (pushed) red_release_add(pick(p.rs_cnt, chunk) + (p.epoch & 1u) * kFusedMaxTiles + local_tile, 1u);
+            uint8_t* dst =
+                reinterpret_cast<uint8_t*>(pick(p.recv, chunk) + (int64_t(p.rank) * per_chunk + local_tile) * S::kTileElems);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.send + int64_t(gtile) * S::kTileElems);
+            unsigned* cnt = pick(p.rs_cnt, chunk) + (p.epoch & 1u) * kFusedMaxTiles + local_tile;
+            bool pushed;
+            if (g.push_depth >= 2) {
+              // issue this tile, then count the previous one once it has landed
+              pushed = bulk_push_issue(bstage, bbar, bphase, dst, src, int64_t(S::kTileElems) * 2, g.err);
+              if (owed != nullptr) {
+                if (pushed) bulk_wait_keep_tile();
+                else bulk_wait_all();
+                fence_proxy_async_global();
+                __threadfence_system();
+                red_release_add(owed, 1u);
+                owed = nullptr;
+              }
+              if (pushed) owed = cnt;
+            } else {
+              pushed = bulk_push(bstage, bbar, bphase, dst, src, int64_t(S::kTileElems) * 2, g.err);
+              if (pushed) red_release_add(cnt, 1u);
+            }
             claim[1] = pushed;
           }
           copy_bar();
@@ -748,6 +822,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       if (ct == 0 && nclaim < 8) FUSED_STAMP(11 + 2 * nclaim, globaltimer());
       if (!ok) break;
     }
+    if (ct == 0) pay_owed();
   }
 
   tc_fence_before();
@@ -857,6 +932,15 @@ void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bo
   else launch_fused<256, false, kModeAG>(ta, tland, tb, g, grid, st);
 }
 
+// RESIHP_PUSH_DEPTH=2: RS / AR partial-tile pushes pipelined two deep per copy thread
+// (each counted once the next is issued); default 1, one push completed at a time.
+static int g_push_depth = [] {
+  const char* e = std::getenv("RESIHP_PUSH_DEPTH");
+  return e != nullptr && e[0] == '2' ? 2 : 1;
+}();
+
+void set_fused_push_depth(int depth) { g_push_depth = depth >= 2 ? 2 : 1; }
+
 void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n,
                    int k, bool all_reduce, const FusedPeers& peers, int grid, int* err, cudaStream_t st) {
   check_peers(peers, t_rows, n, k, all_reduce ? "gemm_ar" : "gemm_rs");
@@ -876,6 +960,7 @@ void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y
   g.err = err;
   g.wait_ns = peer_wait_budget_ns();
   g.trace = g_fused_trace;
+  g.push_depth = g_push_depth;
   g.p = peers;
   if (all_reduce) {
     if (w_mn) launch_fused<256, true, kModeAR>(ta, ta, tb, g, grid, st);

@@ -136,6 +136,8 @@ int fused_red_slices(int t_rows, int n, int tp, int grid);
 // ([grid][fused_trace_slots()] uint64 device memory), or stop (nullptr).
 void set_fused_trace(uint64_t* buffer);
 int fused_trace_slots();
+// RS / AR partial-tile pushes pipelined two deep per copy thread (2) or one at a time (1).
+void set_fused_push_depth(int depth);
 void fused_ag_gemm(const void* x_local, void* xg, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy,
                    int t_rows, int n, int k, const FusedPeers& peers, int grid, int* err, cudaStream_t st);
 void fused_gemm_rs(const void* h, const void* w, int64_t ldw, bool w_mn, void* y, int64_t ldy, int t_rows, int n,

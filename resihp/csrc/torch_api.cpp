@@ -491,6 +491,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_fused_trace", [](int64_t ptr) { resihp::set_fused_trace(reinterpret_cast<uint64_t*>(ptr)); },
         "profiling aid: per-CTA timer stamps of the fused TP kernels into a device buffer (0: off)");
   m.def("fused_trace_slots", &resihp::fused_trace_slots, "stamps per CTA of the fused-kernel trace");
+  m.def("set_fused_push_depth", &resihp::set_fused_push_depth,
+        "RS / AR partial-tile pushes in flight per copy thread: 2 pipelined, 1 one at a time (default)");
   m.def("gemm", &resihp::gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c"), py::arg("epi"), py::arg("alpha") = 1.0, py::arg("residual") = py::none(),
         py::arg("max_ctas") = 0, py::arg("force_bn") = 0);
