@@ -6,6 +6,8 @@
     ... bench_fused_tp.py --config3                       # Llama-3-8B layer shapes
     ... bench_fused_tp.py --trace DIR                     # also: per-CTA timelines of one
                                                           # fused call per op (JSON per rank)
+    RESIHP_PUSH_DEPTH=2 python -m torch.distributed.run ... bench_fused_tp.py
+                                                          # RS / AR pushes pipelined two deep
 
 The sweep covers M = 4096..32768 tokens with K, N in {5120, 13824}: column-parallel
 AG->GEMM ``[M, 5120] x [5120, N/tp]`` (N = 5120, 13824) and row-parallel GEMM->RS
