@@ -289,22 +289,28 @@ __global__ void __launch_bounds__(192, 1)
 //                         on the leader's ``acc_empty`` (8 warp arrivals)
 // No load is multicast: each CTA reads its own operand halves from this GPU's memory.
 
+// Six 32 KB operand stages by default; seven still fit (7 x 32 KB + alignment slack and
+// barriers = 230,656 of the 232,448 bytes a CTA may have), selected with
+// RESIHP_GEMM_STAGES=7 (experimental: the extra stage covers more TMA latency).
 constexpr int kPairStages = 6;
 
+template <int STAGES>
 struct PairShape {
   static constexpr int kABytes = 128 * kBK * 2;   // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * kBK * 2;   // this CTA's 128 rows (N) of B
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kSmem = kPairStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 256;
   static constexpr int kTmemCols = 512;           // two 256-column accumulators
+  static_assert(kSmem <= 232448, "pair GEMM stages exceed the shared memory of a CTA");
+  static_assert((2 * STAGES + 4) * 8 + 4 <= 256, "pair GEMM barriers exceed their area");
 };
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, GemmArgs g) {
   pdl_enter();
-  using S = PairShape;
-  constexpr int kStages = kPairStages;
+  using S = PairShape<STAGES>;
+  constexpr int kStages = STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
@@ -526,11 +532,11 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
 //   forward  (K,K)   store bf16 or add residual
 //   dgrad    (K,MN)  store bf16 or fp32
 //   wgrad    (MN,MN) store or accumulate fp32 (load-add-store or red.global.add)
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int STAGES>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t stream,
                         int max_ctas) {
-  using S = PairShape;
-  auto kernel = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  using S = PairShape<STAGES>;
+  auto kernel = gemm_pair_kernel<A_MN, B_MN, EPI, STAGES>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -567,18 +573,33 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
 }
 
 // The same combinations on CTA pairs.
+template <int ST>
+static void dispatch_pair_stages(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                                 const GemmArgs& g, cudaStream_t st, int max_ctas) {
+  if (!a_mn && !b_mn && epi == kEpiStoreBf16) return launch_pair<false, false, kEpiStoreBf16, ST>(ta, tb, g, st, max_ctas);
+  if (!a_mn && !b_mn && epi == kEpiAddBf16) return launch_pair<false, false, kEpiAddBf16, ST>(ta, tb, g, st, max_ctas);
+  if (!a_mn && !b_mn && epi == kEpiStoreF32) return launch_pair<false, false, kEpiStoreF32, ST>(ta, tb, g, st, max_ctas);
+  if (!a_mn && b_mn && epi == kEpiStoreBf16) return launch_pair<false, true, kEpiStoreBf16, ST>(ta, tb, g, st, max_ctas);
+  if (!a_mn && b_mn && epi == kEpiStoreF32) return launch_pair<false, true, kEpiStoreF32, ST>(ta, tb, g, st, max_ctas);
+  if (a_mn && b_mn && epi == kEpiStoreF32) return launch_pair<true, true, kEpiStoreF32, ST>(ta, tb, g, st, max_ctas);
+  if (a_mn && b_mn && epi == kEpiAccumF32) return launch_pair<true, true, kEpiAccumF32, ST>(ta, tb, g, st, max_ctas);
+  if (a_mn && b_mn && epi == kEpiRedF32) return launch_pair<true, true, kEpiRedF32, ST>(ta, tb, g, st, max_ctas);
+  if (a_mn && b_mn && epi == kEpiStoreBf16) return launch_pair<true, true, kEpiStoreBf16, ST>(ta, tb, g, st, max_ctas);
+  RESIHP_CHECK(false, "unsupported GEMM combination a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+static int pair_stages() {
+  static const int stages = [] {
+    const char* v = std::getenv("RESIHP_GEMM_STAGES");
+    return v != nullptr && std::strcmp(v, "7") == 0 ? 7 : kPairStages;
+  }();
+  return stages;
+}
+
 static void dispatch_pair(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                           const GemmArgs& g, cudaStream_t st, int max_ctas) {
-  if (!a_mn && !b_mn && epi == kEpiStoreBf16) return launch_pair<false, false, kEpiStoreBf16>(ta, tb, g, st, max_ctas);
-  if (!a_mn && !b_mn && epi == kEpiAddBf16) return launch_pair<false, false, kEpiAddBf16>(ta, tb, g, st, max_ctas);
-  if (!a_mn && !b_mn && epi == kEpiStoreF32) return launch_pair<false, false, kEpiStoreF32>(ta, tb, g, st, max_ctas);
-  if (!a_mn && b_mn && epi == kEpiStoreBf16) return launch_pair<false, true, kEpiStoreBf16>(ta, tb, g, st, max_ctas);
-  if (!a_mn && b_mn && epi == kEpiStoreF32) return launch_pair<false, true, kEpiStoreF32>(ta, tb, g, st, max_ctas);
-  if (a_mn && b_mn && epi == kEpiStoreF32) return launch_pair<true, true, kEpiStoreF32>(ta, tb, g, st, max_ctas);
-  if (a_mn && b_mn && epi == kEpiAccumF32) return launch_pair<true, true, kEpiAccumF32>(ta, tb, g, st, max_ctas);
-  if (a_mn && b_mn && epi == kEpiRedF32) return launch_pair<true, true, kEpiRedF32>(ta, tb, g, st, max_ctas);
-  if (a_mn && b_mn && epi == kEpiStoreBf16) return launch_pair<true, true, kEpiStoreBf16>(ta, tb, g, st, max_ctas);
-  RESIHP_CHECK(false, "unsupported GEMM combination a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+  if (pair_stages() == 7) return dispatch_pair_stages<7>(epi, a_mn, b_mn, ta, tb, g, st, max_ctas);
+  return dispatch_pair_stages<kPairStages>(epi, a_mn, b_mn, ta, tb, g, st, max_ctas);
 }
 
 // CTA pairs for every GEMM that takes 256-column tiles (RESIHP_GEMM_PAIR=0: single CTAs).
