@@ -11,6 +11,7 @@
 // reduced deterministically: every block of a fixed-size persistent grid writes one
 // fp32 partial row, and a second kernel sums the partials in block order.
 #include <algorithm>
+#include <cstdlib>
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -315,6 +316,81 @@ __global__ void __launch_bounds__(32 * kNormWarps)
   }
 }
 
+// The same backward in a streaming form (RESIHP_NORM_STREAM=1, experimental): no row
+// stays in registers between the two passes -- the second pass reads dy and s again (L2
+// hits: the row was just read) -- so a thread needs ~80 registers instead of ~250 and
+// three CTAs share an SM: 24 warps, about one row each at the 1.3B shapes, all in flight
+// at once instead of a third of them. Same per-element arithmetic and the same order of
+// the row reduction as the register kernel (ds is identical); dw goes through per-warp
+// shared-memory rows as there, over this kernel's grid.
+constexpr int kStreamCtasPerSm = 3;
+
+template <int VPL>
+__global__ void __launch_bounds__(32 * kNormWarps, kStreamCtasPerSm)
+    rmsnorm_bwd_stream_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ s,
+                              const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                              const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ ds,
+                              float* __restrict__ dw_partial, int rows) {
+  pdl_enter();
+  constexpr int D = 256 * VPL;
+  extern __shared__ float4 dw_smem4[];  // [kNormWarps][D / 4]: each warp's running dw row
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4* mine = dw_smem4 + warp * (D / 4);
+  #pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    mine[(32 * j + lane) * 2] = make_float4(0.f, 0.f, 0.f, 0.f);
+    mine[(32 * j + lane) * 2 + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = blockIdx.x * kNormWarps + warp; row < rows; row += gridDim.x * kNormWarps) {
+    const int64_t base = int64_t(row) * D;
+    const float rs = rstd[row];
+    float dot = 0.f;
+    #pragma unroll 2
+    for (int j = 0; j < VPL; ++j) {
+      const int col = (32 * j + lane) * 8;
+      const Vec8 dyv = load8(dy + base + col);
+      const Vec8 svv = load8(s + base + col);
+      const Vec8 wv = load8(w + col);
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) dot += dyv.v[i] * wv.v[i] * (svv.v[i] * rs);
+    }
+    const float mean = warp_sum(dot) / float(D);
+    #pragma unroll 2
+    for (int j = 0; j < VPL; ++j) {
+      const int col = (32 * j + lane) * 8;
+      const Vec8 dyv = load8(dy + base + col);
+      const Vec8 svv = load8(s + base + col);
+      const Vec8 wv = load8(w + col);
+      Vec8 o;
+      float sh[8];
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        sh[i] = svv.v[i] * rs;
+        o.v[i] = rs * (dyv.v[i] * wv.v[i] - sh[i] * mean);
+      }
+      if (dres != nullptr) {
+        const Vec8 rv = load8(dres + base + col);
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) o.v[i] += rv.v[i];
+      }
+      store8(ds + base + col, o);
+      float4 a = mine[(32 * j + lane) * 2], b = mine[(32 * j + lane) * 2 + 1];
+      a.x += dyv.v[0] * sh[0]; a.y += dyv.v[1] * sh[1]; a.z += dyv.v[2] * sh[2]; a.w += dyv.v[3] * sh[3];
+      b.x += dyv.v[4] * sh[4]; b.y += dyv.v[5] * sh[5]; b.z += dyv.v[6] * sh[6]; b.w += dyv.v[7] * sh[7];
+      mine[(32 * j + lane) * 2] = a;
+      mine[(32 * j + lane) * 2 + 1] = b;
+    }
+  }
+  __syncthreads();
+  const float* dw_smem = reinterpret_cast<const float*>(dw_smem4);
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    #pragma unroll
+    for (int q = 0; q < kNormWarps; ++q) acc += dw_smem[q * D + c];
+    dw_partial[int64_t(blockIdx.x) * D + c] = acc;
+  }
+}
+
 // dw[c] (+)= sum over partial rows of partial[p, c] in a fixed order: block (32 columns
 // x 8 groups); group g sums rows g, g+8, g+16, ... in turn, then the 8 group sums are
 // added in group order. Used with the warp-per-row backward (fewer, wider blocks than
@@ -343,8 +419,23 @@ int norm_vpl(int d) {
   return (d == 256 || d == 512 || d == 1024 || d == 2048) ? d / 256 : 0;
 }
 
+// RESIHP_NORM_STREAM=1 selects the streaming backward (experimental).
+bool norm_stream() {
+  static const bool on = [] {
+    const char* e = std::getenv("RESIHP_NORM_STREAM");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
 int warp_norm_grid(int rows, int num_sms) {
   return std::max(1, std::min((rows + kNormWarps - 1) / kNormWarps, num_sms));
+}
+
+// Grid of the warp-per-row backward: one CTA per SM, or (streaming) kStreamCtasPerSm.
+int bwd_norm_grid(int rows, int num_sms) {
+  return norm_stream() ? std::max(1, std::min((rows + kNormWarps - 1) / kNormWarps, kStreamCtasPerSm * num_sms))
+                       : warp_norm_grid(rows, num_sms);
 }
 
 int norm_block(int d) {
@@ -356,7 +447,7 @@ int norm_block(int d) {
 }  // namespace
 
 int rmsnorm_partial_rows(int rows, int d, int num_sms) {
-  if (norm_vpl(d) != 0) return warp_norm_grid(rows, num_sms);
+  if (norm_vpl(d) != 0) return bwd_norm_grid(rows, num_sms);
   const int block = norm_block(d);
   const int rows_per_block = block / (d / 8);
   int grid = std::min((rows + rows_per_block - 1) / rows_per_block, 2 * num_sms);
@@ -369,7 +460,7 @@ template <int VPL>
 void launch_bwd_warp(const void* dy, const void* s, const void* w, const float* rstd, const void* dres, void* ds,
                      float* partial, int rows, int grid, cudaStream_t st) {
   constexpr int smem = kNormWarps * 256 * VPL * int(sizeof(float));
-  auto kernel = rmsnorm_bwd_warp_kernel<VPL>;
+  auto kernel = norm_stream() ? rmsnorm_bwd_stream_kernel<VPL> : rmsnorm_bwd_warp_kernel<VPL>;
   if (smem > 48 * 1024) (void)cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   launch_pdl(kernel, grid, 32 * kNormWarps, smem, st,
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(s),
@@ -386,7 +477,7 @@ cudaError_t rmsnorm_bwd_launch(const void* dy, const void* s, const void* w, con
                                cudaStream_t st) {
   const int vpl = norm_vpl(d);
   if (vpl != 0) {
-    const int grid = warp_norm_grid(rows, num_sms);
+    const int grid = bwd_norm_grid(rows, num_sms);
     switch (vpl) {
       case 1: launch_bwd_warp<1>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;
       case 2: launch_bwd_warp<2>(dy, s, w, rstd, dres, ds, partial, rows, grid, st); break;

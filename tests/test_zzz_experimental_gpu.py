@@ -10,7 +10,9 @@ Opt-in (``RESIHP_TEST_EXPERIMENTAL=1``) until each has run on a GPU:
   must be incremented exactly once per call;
 * the seven-stage CTA-pair GEMM (``RESIHP_GEMM_STAGES=7``, read once per process, so it
   runs in a child process): forward, dgrad and wgrad products against FP32 torch, and
-  bit for bit against the six-stage kernel (the stage count changes no arithmetic).
+  bit for bit against the six-stage kernel (the stage count changes no arithmetic);
+* the streaming RMSNorm backward (``RESIHP_NORM_STREAM=1``, child process): ds bit for
+  bit equal to the register kernel's, dw equal up to the order of its fp32 row sums.
 """
 
 import json
@@ -106,3 +108,40 @@ def test_seven_stage_pair_gemm_matches_six_stages():
     for shape, got in seven.items():
         assert all(r < 1e-2 for r in got["rel"]), (shape, got["rel"])
         assert got["sha"] == six[shape]["sha"], shape
+
+
+_NORM_CHILD = r"""
+import hashlib, json, torch
+from resihp.ops import _ext
+k = _ext.require()
+torch.manual_seed(0)
+out = {}
+for rows, d in ((4096, 2048), (333, 1024), (1000, 256)):
+    x = torch.randn(rows, d, device="cuda").bfloat16()
+    r = torch.randn(rows, d, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(d, device="cuda")).bfloat16()
+    y, s, rstd = k.rmsnorm_fwd(x, r, w, 1e-5)
+    dy, dres = torch.randn_like(x), torch.randn_like(x)
+    dw = torch.zeros(d, device="cuda")
+    ds = k.rmsnorm_bwd(dy, s, w, rstd, dres, dw, True)
+    torch.cuda.synchronize()
+    out[f"{rows}x{d}"] = {"ds": hashlib.sha256(ds.view(torch.int16).cpu().numpy().tobytes()).hexdigest(),
+                          "dw": dw.cpu().tolist()}
+print(json.dumps(out))
+"""
+
+
+def _norm_child(stream):
+    env = dict(os.environ, PYTHONPATH=ROOT, RESIHP_NORM_STREAM="1" if stream else "0")
+    out = subprocess.run([sys.executable, "-c", _NORM_CHILD], cwd=ROOT, env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert out.returncode == 0, out.stderr[-3000:]
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def test_streaming_norm_backward_matches_the_register_kernel():
+    base, stream = _norm_child(False), _norm_child(True)
+    for shape, got in stream.items():
+        assert got["ds"] == base[shape]["ds"], shape
+        a, b = torch.tensor(got["dw"]), torch.tensor(base[shape]["dw"])
+        assert ((a - b).norm() / b.norm()).item() < 1e-5, shape
