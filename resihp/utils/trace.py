@@ -46,20 +46,24 @@ def nvtx_range(name: str):
 
 # kernel name pattern -> category, first match wins (names as the torch profiler reports
 # them, demangled or mangled; the GEMM's template arguments say which linear-layer
-# product it is: <BN, A MN-major, B MN-major, epilogue>)
+# product it is: <BN, A MN-major, B MN-major, epilogue> for the single-CTA kernel,
+# <A MN-major, B MN-major, epilogue, stages> for the CTA-pair kernel)
 _CATEGORIES = (
     (r"fused_gemm_kernel", "fused TP collective GEMM"),
-    (r"gemm_kernel<\d+, false, false|gemm_kernelILi\d+ELb0ELb0E", "GEMM forward"),
-    (r"gemm_kernel<\d+, false, true|gemm_kernelILi\d+ELb0ELb1E", "GEMM dgrad"),
-    (r"gemm_kernel<\d+, true, true|gemm_kernelILi\d+ELb1ELb1E", "GEMM wgrad"),
-    (r"gemm_kernel", "GEMM other"),
+    (r"gemm_kernel<\d+, false, false|gemm_kernelILi\d+ELb0ELb0E"
+     r"|gemm_pair_kernel<false, false|gemm_pair_kernelILb0ELb0E", "GEMM forward"),
+    (r"gemm_kernel<\d+, false, true|gemm_kernelILi\d+ELb0ELb1E"
+     r"|gemm_pair_kernel<false, true|gemm_pair_kernelILb0ELb1E", "GEMM dgrad"),
+    (r"gemm_kernel<\d+, true, true|gemm_kernelILi\d+ELb1ELb1E"
+     r"|gemm_pair_kernel<true, true|gemm_pair_kernelILb1ELb1E", "GEMM wgrad"),
+    (r"gemm_(pair_)?kernel", "GEMM other"),
     (r"attn_fwd_kernel", "attention forward"),
     (r"attn_bwd|attn_delta", "attention backward"),
     (r"rmsnorm|column_sum", "RMSNorm"),
-    (r"rope_kernel|swiglu|embedding_(fwd|bwd)_kernel", "RoPE / SwiGLU / embedding"),
+    (r"rope(_vec)?_kernel|swiglu|embedding_(fwd|bwd|sort)_kernel", "RoPE / SwiGLU / embedding"),
     (r"xent_", "cross-entropy"),
-    (r"dp_adamw_kernel", "fused DP all-reduce + AdamW"),
-    (r"adamw_kernel", "AdamW"),
+    (r"dp_adamw(_push)?_kernel", "fused DP all-reduce + AdamW"),
+    (r"adamw(_vec)?_kernel", "AdamW"),
     (r"reshard_gather", "state move"),
     (r"(?i)nccl", "NCCL"),
     (r"(?i)memcpy|memset", "copies"),

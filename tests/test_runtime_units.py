@@ -290,6 +290,21 @@ def test_trace_categories_name_the_linear_layer_products():
     ]
     cats = categorize(rows)
     assert list(cats)[:2] == ["GEMM forward", "GEMM wgrad"]
+    # the CTA-pair GEMM, the vector elementwise kernels and the two-phase DP step
+    more = categorize([
+        {"name": "void resihp::gemm_pair_kernel<false, true, 0, 6>(CUtensorMap_st, CUtensorMap_st, resihp::GemmArgs)",
+         "calls": 3, "device_us": 30.0},
+        {"name": "_ZN6resihp16gemm_pair_kernelILb1ELb1ELi4ELi6EEEv14CUtensorMap_stS1_NS_8GemmArgsE", "calls": 2,
+         "device_us": 20.0},
+        {"name": "resihp::(anonymous namespace)::rope_vec_kernel(__nv_bfloat16*, ...)", "calls": 1, "device_us": 4.0},
+        {"name": "resihp::(anonymous namespace)::adamw_vec_kernel(float4*, ...)", "calls": 1, "device_us": 3.0},
+        {"name": "void resihp::dp_adamw_push_kernel<2>(...)", "calls": 1, "device_us": 2.0},
+        {"name": "resihp::(anonymous namespace)::embedding_sort_kernel(long const*, ...)", "calls": 1,
+         "device_us": 1.0},
+    ])
+    assert more["GEMM dgrad"]["calls"] == 3 and more["GEMM wgrad"]["calls"] == 2
+    assert more["RoPE / SwiGLU / embedding"]["calls"] == 2 and more["AdamW"]["calls"] == 1
+    assert more["fused DP all-reduce + AdamW"]["calls"] == 1 and "other" not in more
     assert cats["GEMM dgrad"]["calls"] == 2 and cats["fused TP collective GEMM"]["device_us"] == 20.0
     assert cats["attention backward"]["share"] == 0.02 and cats["NCCL"]["calls"] == 1 and "other" in cats
     assert abs(sum(c["share"] for c in cats.values()) - 1.0) < 1e-3
