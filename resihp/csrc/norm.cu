@@ -6,10 +6,13 @@
 //   backward  g = dy * w;    ds = rstd * (g - s_hat * mean(g * s_hat)) (+ dres),
 //             dw += sum_rows dy * s_hat                  (s_hat = s * rstd)
 //
-// One row is spread over d/8 threads, each holding one 16-byte vector (8 bf16); several
-// rows share a block so that a block has >= 256 threads. The weight gradient is
-// reduced deterministically: every block of a fixed-size persistent grid writes one
-// fp32 partial row, and a second kernel sums the partials in block order.
+// Widths 256-2048 run warp-per-row kernels: a warp owns a row, each lane 8-column
+// vectors of it (the backward keeps the row in packed registers between its two passes;
+// the optional streaming backward reads it again instead). Other widths run the general
+// kernels, where one row is spread over d/8 threads, each holding one 16-byte vector (8
+// bf16), and several rows share a block so that a block has >= 256 threads. The weight
+// gradient is reduced deterministically: every block of a fixed-size persistent grid
+// writes one fp32 partial row, and a second kernel sums the partials in block order.
 #include <algorithm>
 #include <cstdlib>
 #include <cuda_bf16.h>
