@@ -1,5 +1,6 @@
-// Shared sm_100a device helpers: mbarriers with bounded waits, TMA tile loads, and the
-// tcgen05 (5th-generation tensor core + tensor memory) instructions the kernels use.
+// Shared sm_100a device helpers: mbarriers with bounded waits, TMA tile loads and bulk
+// copies, the tcgen05 (5th-generation tensor core + tensor memory) instructions the
+// kernels use, and programmatic dependent launch (launch_pdl / pdl_enter).
 //
 // Every spin-wait here is bounded by the global nanosecond timer. A wait that runs out
 // records a code in the kernel's error word and returns false; the caller then leaves
